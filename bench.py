@@ -1,0 +1,364 @@
+"""Benchmark of the Qwen3-MoE feed-forward hot path on B200 (libqms_cuda through its C ABI).
+
+Workload: the Qwen3-235B-A22B MoE layer operator at decode batch 1 —
+hidden 4096, 128 experts, top-8, moe_intermediate 1536, Q4_0 experts, F32 router — on 1000
+seeded tokens, each an independent T=1 call. Calls cycle through 8 resident layers with
+independent seeded weights (8 x 1.36 GB), so consecutive calls share no weights and every
+step's inputs are far larger than L2. A step is the 1000 calls; the metric is the MoE layer's
+algorithmic HBM bytes (8 experts x 10,616,832 B + 2,097,152 B router = 87,031,808 B per
+token-layer) divided by time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 runs N independent replicas (one per GPU, launched by torch.distributed.run): batch-1
+decode does not shard, so there is no collective on the data path (scaling "weak").
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SHAPE = "235b"
+TOKENS = 1000
+LAYERS = 8
+METRIC = "Qwen3-235B Q4_0 MoE-layer HBM GB/s (decode bs1)"
+WORKLOAD = ("Qwen3-235B-A22B MoE layer operator, decode bs1 (config 2): 1000 seeded tokens per step, "
+            "each an independent T=1 call, cycling 8 resident layers of independent seeded weights")
+
+
+def bytes_per_token_layer(E=4096, X=128, K=8, F=1536) -> int:
+    expert = 3 * F * (E // 32) * 18          # gate + up + down, Q4_0 (18 bytes per 32 weights)
+    return K * expert + X * E * 4            # + F32 router
+
+
+def gate_up_bytes_per_launch(E=4096, K=8, F=1536) -> int:
+    return K * 2 * F * (E // 32) * 18
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic() -> float | None:
+    """DRAM bytes per k_moe_gate_up launch from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "k_moe_gate_up_235b_bs1.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1].strip())
+    return None
+
+
+# ---- clocks ------------------------------------------------------------------------------------
+
+class ClockSampler:
+    def __init__(self, gpu_index: int):
+        self.path = Path(f"/tmp/qms_clocks_{os.getpid()}.csv")
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-i", str(gpu_index), "-lms", "100"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.close()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        self.path.unlink(missing_ok=True)
+        load = [s for s in sm if s > 0.5 * max(sm)] if sm else []
+        return {"sm_mhz": statistics.median(load) if load else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---- CPU: the reference's own moe() ------------------------------------------------------------
+
+def cpu_reference_rate(seconds: float = 8.0, max_calls: int = 2000, layers: int = 2):
+    """Time the reference build's moe() (oracle/_ref, compiled from its sources) on T=1 calls of
+    the same workload, all host threads, `layers` resident 235B-shape layers in host RAM."""
+    from oracle import Reference, host_threads
+    from large_model_b200 import synth
+    ref = Reference()
+    threads = host_threads()
+    ref.set_threads(threads)
+    ls = [synth.make_moe_layer(SHAPE, seed=1000 + i) for i in range(layers)]
+    xn = synth.make_hidden(ls[0].n_embd, 64, seed=2000)
+    for t in range(4):                                    # warm-up (page in, thread pool)
+        ref.moe(ls[t % layers], xn[t])
+    n, t0 = 0, time.perf_counter()
+    while n < max_calls and (time.perf_counter() - t0 < seconds or n < 8):
+        ref.moe(ls[n % layers], xn[n % len(xn)])
+        n += 1
+    dt = time.perf_counter() - t0
+    gbs = n * bytes_per_token_layer() / dt / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+            "sample": f"{n} T=1 moe() calls over {layers} seeded 235B-shape layers in host RAM "
+                      f"({dt:.1f} s, reference build {ref.variant}, {threads} OpenMP threads)"}, n, dt
+
+
+def run_reference_arm(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import Reference, host_threads
+    from large_model_b200 import synth
+    ref = Reference()
+    threads = host_threads()
+    ref.set_threads(threads)
+    ls = [synth.make_moe_layer(SHAPE, seed=1000 + i) for i in range(2)]
+    xn = synth.make_hidden(ls[0].n_embd, 64, seed=2000)
+    calls_per_step = 16
+    k = 0
+    for _ in range(a.warmup):
+        for _ in range(calls_per_step):
+            ref.moe(ls[k % 2], xn[k % 64])
+            k += 1
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        for _ in range(calls_per_step):
+            ref.moe(ls[k % 2], xn[k % 64])
+            k += 1
+    dt = time.perf_counter() - t0
+    value = a.steps * calls_per_step * bytes_per_token_layer() / dt / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": a.gpus,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt / a.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp32",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD + f"; reference CPU arm: each step {calls_per_step} T=1 calls "
+                                              f"over 2 resident layers", "tokens_per_step": calls_per_step},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                             "sample": f"{calls_per_step} T=1 moe() calls per step, reference build {ref.variant}"},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---- GPU ---------------------------------------------------------------------------------------
+
+def device_layer(q, torch, seed: int, device):
+    """A 235B-shape layer drawn on the device with the config's distributions, then uploaded
+    through qms_cuda_moe_create from device memory (GGUF layout, repacked by the library)."""
+    from large_model_b200 import synth
+    E, X, K, F = synth.MOE_SHAPES[SHAPE]
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    router = torch.randn((X, E), generator=g, device=device, dtype=torch.float32) * 0.02
+
+    def q4_0(nblocks):
+        blk = torch.empty((nblocks, 18), dtype=torch.uint8, device=device)
+        d = (torch.rand(nblocks, generator=g, device=device) * 0.004 + 0.002).to(torch.float16)
+        blk[:, 0:2] = d.view(torch.uint8).view(nblocks, 2)
+        nib = torch.randint(-2 ** 31, 2 ** 31 - 1, (nblocks, 4), generator=g, device=device, dtype=torch.int32)
+        blk[:, 2:] = nib.view(torch.uint8).view(nblocks, 16)
+        return blk.view(-1)
+
+    gate, up, down = q4_0(X * F * E // 32), q4_0(X * F * E // 32), q4_0(X * E * F // 32)
+    m = q.MoeLayer(E, X, K, F, router, gate, up, down)
+    del router, gate, up, down
+    return m
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=60)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+    if a.impl == "reference":
+        return run_reference_arm(a)
+
+    import torch
+    import large_model_b200 as q
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    q.init(local)
+    dev = torch.device("cuda", local)
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        cpu, _, _ = cpu_reference_rate()
+
+    layers = [device_layer(q, torch, 100 + 17 * i, dev) for i in range(a.layers)]
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    E = layers[0].n_embd
+    xn = torch.randn((a.tokens, E), generator=g, device=dev, dtype=torch.float32)
+    out = torch.empty_like(xn)
+    for m in layers:
+        m.reserve(1)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        for t in range(a.tokens):
+            layers[t % a.layers].forward(xn[t:t + 1], out=out[t:t + 1], stream=stream)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    graph = None
+    if not a.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        torch.cuda.synchronize()
+    run = graph.replay if graph is not None else step
+
+    with torch.cuda.stream(stream):
+        for _ in range(a.warmup):
+            run()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    time.sleep(0.6)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(a.steps):
+            run()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tokens_total = a.steps * a.tokens * world
+    value = tokens_total * bytes_per_token_layer() / (ms / 1e3) / 1e9
+
+    # per-kernel timing pass (CUDA events around each kernel on the launch stream)
+    kev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    ksum = [0.0, 0.0, 0.0]
+    nk = min(200, a.tokens)
+    for t in range(nk):
+        m = layers[t % a.layers]
+        m.set_kernel_events(kev)
+        with torch.cuda.stream(stream):
+            m.forward(xn[t:t + 1], out=out[t:t + 1], stream=stream)
+        m.set_kernel_events(None)
+        stream.synchronize()
+        for i in range(3):
+            ksum[i] += kev[2 * i].elapsed_time(kev[2 * i + 1])
+    kms = [s / nk for s in ksum]
+    peak, peak_kind = peaks()
+    gu_gbs = gate_up_bytes_per_launch() / (kms[1] / 1e3) / 1e9
+
+    # end to end through the host-buffer entry point (pinned host memory, copies in the timed region)
+    xh = torch.empty((a.tokens, E), dtype=torch.float32, pin_memory=True)
+    xh.copy_(xn.cpu())
+    oh = torch.empty_like(xh, pin_memory=True)
+    xh_np, oh_np = xh.numpy(), oh.numpy()
+    e2e_steps = max(1, min(a.steps, 3))
+    for t in range(min(50, a.tokens)):
+        layers[t % a.layers].forward_host(xh_np[t:t + 1], out=oh_np[t:t + 1])
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        for t in range(a.tokens):
+            layers[t % a.layers].forward_host(xh_np[t:t + 1], out=oh_np[t:t + 1])
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = e2e_steps * a.tokens * world * bytes_per_token_layer() / e2e_s / 1e9
+
+    if rank == 0:
+        traffic = profile_traffic()
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens_per_step": a.tokens, "layers": a.layers,
+                       "bytes_per_token_layer": bytes_per_token_layer(),
+                       "token_layers_per_s": round(tokens_total / (ms / 1e3), 1),
+                       "moe_only_decode_tok_s_94_layers": round(tokens_total / (ms / 1e3) / 94, 2),
+                       "us_per_token_layer": round(ms * 1e3 / (a.steps * a.tokens), 3),
+                       "l2": f"inputs larger than L2 ({a.layers} layers x 1.36 GB resident)",
+                       "graph": graph is not None, "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "kernel": "k_moe_gate_up", "achieved": round(gu_gbs, 1), "peak": peak,
+                         "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback", "unit": "GB/s", "frac": round(gu_gbs / peak, 4),
+                         "traffic": traffic, "bytes_per_launch": gate_up_bytes_per_launch(),
+                         "kernel_us": {"router_topk": round(kms[0] * 1e3, 2), "gate_up": round(kms[1] * 1e3, 2),
+                                       "down_combine": round(kms[2] * 1e3, 2)},
+                         "op_frac": round(value / world / peak, 4)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": a.tokens * E * 4,
+                    "d2h_bytes_per_step": a.tokens * E * 4,
+                    "note": "qms_cuda_moe_forward_host per token: copy in, 3 kernels, copy out, wait"},
+            "gpu_launches": 3 * a.tokens * a.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    for m in layers:
+        m.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

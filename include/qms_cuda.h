@@ -1,0 +1,123 @@
+/* qms_cuda.h - C ABI of libqms_cuda: the B200 (sm_100a) Qwen3-MoE feed-forward path.
+ *
+ * Plain C types only (pointers, sizes, ints); streams are passed as `void *` (a cudaStream_t,
+ * NULL = the legacy default stream). Every function returns an int status (QMS_CUDA_OK = 0,
+ * negative on failure) and records a one-line reason readable with qms_cuda_last_error(),
+ * like the reference's 0 / -1 returns with the reason printed to stderr (src/model.h:135-141).
+ * There is no CPU fallback: without a usable sm_100 device every compute call fails.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   qms_quantize_q8            src/kernels.h:15   (src/kernels.c:34-53)
+ *   qms_vec_dot_q8/qms_matmul  src/kernels.h:19, src/quant.h:23-26 (src/quant.c:128-170)
+ *   qms_vec_dot_f32            src/kernels.h:21   (src/kernels.c:202-221)
+ *   moe()                      src/model.c:1032-1167, called from qms_forward (src/model.c:1284)
+ */
+#ifndef QMS_CUDA_H
+#define QMS_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml tensor type ids, GGUF numbering (src/gguf.h:8-10). */
+enum { QMS_T_F32 = 0, QMS_T_F16 = 1, QMS_T_Q4_0 = 2, QMS_T_Q4_1 = 3, QMS_T_Q8_0 = 8, QMS_T_Q6_K = 14 };
+
+/* Status codes. */
+enum {
+    QMS_CUDA_OK = 0,
+    QMS_CUDA_EINVAL = -1,       /* bad argument or shape */
+    QMS_CUDA_ECUDA = -2,        /* a CUDA runtime call failed */
+    QMS_CUDA_ENOMEM = -3,       /* device allocation failed */
+    QMS_CUDA_EUNSUPPORTED = -4, /* type/shape outside what the kernels implement */
+    QMS_CUDA_ENODEV = -5        /* no sm_100 device */
+};
+
+/* Activation block: 32 int8 values with one fp32 scale; same 44-byte layout as the
+ * reference's QmsQ8 (src/kernels.h:7-12). */
+typedef struct {
+    float d;         /* scale: x ~= q * d */
+    float ds;        /* d * sum(q[0..31]) */
+    int16_t s16[2];  /* sum(q[0..15]), sum(q[16..31]) */
+    int8_t q[32];
+} QmsQ8;
+
+/* ---- library ---------------------------------------------------------------------------- */
+
+/* Reason for the last failure on the calling thread ("" when none). */
+const char *qms_cuda_last_error(void);
+/* Select and check `device` (must be sm_100). Replaces nothing in the reference (CPU only). */
+int qms_cuda_init(int device);
+/* Number of visible CUDA devices, or a negative status. */
+int qms_cuda_device_count(void);
+/* Wait for all work queued on `stream`. */
+int qms_cuda_stream_sync(void *stream);
+
+/* ---- kernel-level mirrors (device pointers) ------------------------------------------------ */
+
+/* Quantise `rows` rows of n floats (n % 32 == 0) to n/32 QmsQ8 blocks each, bit-identical to
+ * qms_quantize_q8 (src/kernels.h:15, src/kernels.c:34-53). */
+int qms_cuda_quantize_q8(const float *x, int64_t n, int64_t rows, QmsQ8 *out, void *stream);
+
+/* y[t][r] = dot(W row r, xq[t]) for a GGUF-layout weight matrix (rows x cols, type Q4_0, Q4_1
+ * or Q6_K) and T quantised activation rows: the integer fast path of qms_matmul / qms_vec_dot_q8
+ * (src/quant.h:23, src/kernels.h:19, src/quant.c:128-170). */
+int qms_cuda_matvec_q8(int type, const void *w, int64_t rows, int64_t cols, const QmsQ8 *xq,
+                       int T, float *y, void *stream);
+
+/* y[t][r] = dot(W row r, x[t]) for an F32 matrix, in qms_vec_dot_f32's exact AVX2 summation
+ * order (src/kernels.h:21, src/kernels.c:202-221), so router logits are bit-identical. */
+int qms_cuda_matvec_f32(const float *w, int64_t rows, int64_t cols, const float *x, int T,
+                        float *y, void *stream);
+
+/* ---- MoE feed-forward block (src/model.c:1032-1167) ---------------------------------------- */
+
+/* One MoE layer as the reference loads it (src/model.c:359-362, model.h:229-243):
+ * router F32 [n_expert][n_embd]; gate/up stacked [n_expert][n_ff] rows of n_embd;
+ * down stacked [n_expert][n_embd] rows of n_ff; ggml block layouts. */
+typedef struct {
+    int n_embd, n_expert, n_used, n_ff;
+    int gate_type, up_type, down_type;
+    const float *router;
+    const void *gate, *up, *down;
+    int src_on_device;          /* 1: the five pointers are device memory; 0: host memory */
+} QmsCudaMoeDesc;
+
+typedef struct QmsCudaMoe QmsCudaMoe;
+
+/* Upload (or copy from device) and repack one layer into HBM on the current device. The
+ * source buffers are not retained. Replaces load_experts / load_mat for one layer
+ * (src/model.c:133-157, 359-362). */
+int qms_cuda_moe_create(const QmsCudaMoeDesc *desc, QmsCudaMoe **out);
+void qms_cuda_moe_destroy(QmsCudaMoe *m);
+/* Bytes of device memory held by the layer (weights + scratch). */
+int64_t qms_cuda_moe_device_bytes(const QmsCudaMoe *m);
+/* Make sure scratch for T tokens exists. Forward calls do this themselves; call it before
+ * capturing forward calls into a CUDA graph (no allocation may happen during capture). */
+int qms_cuda_moe_reserve(QmsCudaMoe *m, int T);
+
+/* out[t] = sum_j w[t][j] * FFN_{sel[t][j]}(xn[t]) for T tokens: moe(m, l, xn, h, T, out)
+ * (src/model.c:1032). xn, out: device fp32 [T][n_embd]. Optional device outputs (NULL to skip):
+ * sel [T][n_used] selected experts in selection order, wts [T][n_used] renormalised weights,
+ * logits [T][n_expert] router logits. resid (optional, device [T][n_embd]): when non-NULL
+ * out = resid + moe(xn), the residual add of qms_forward (src/model.c:1285). */
+int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int *sel,
+                         float *wts, float *logits, const float *resid, void *stream);
+
+/* Kernel timing hook: with events non-NULL (an array of 6 cudaEvent_t), every following forward
+ * records events[2i] before and events[2i+1] after its kernel i (0 router+top-k, 1 gate/up,
+ * 2 down+combine) on the launch stream; this serialises the three kernels (no programmatic
+ * overlap). NULL turns the hook off. */
+int qms_cuda_moe_set_kernel_events(QmsCudaMoe *m, void **events);
+
+/* Same through host buffers (xn, out and the optional outputs in host memory): copies in,
+ * runs, copies out and waits; the drop-in for the reference's host-memory moe() call. */
+int qms_cuda_moe_forward_host(QmsCudaMoe *m, const float *xn, int T, float *out, int *sel,
+                              float *wts, float *logits);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QMS_CUDA_H */

@@ -1,0 +1,220 @@
+"""large_model_b200 - B200-native (sm_100a) Qwen3-MoE feed-forward path of qms.
+
+The product is the C-ABI library `libqms_cuda.so` (include/qms_cuda.h). This module binds it
+with ctypes and mirrors the reference's operator interface for tests and benchmarks:
+
+    quantize_q8(x)               qms_quantize_q8   (src/kernels.h:15)
+    matvec_q8(type, W, xq, ...)  qms_matmul fast path / qms_vec_dot_q8 (src/quant.h:23)
+    matvec_f32(W, x)             qms_vec_dot_f32   (src/kernels.h:21)
+    MoeLayer(...).forward(xn)    moe()             (src/model.c:1032)
+
+Device buffers are torch CUDA tensors (plumbing only); every computation runs in
+libqms_cuda's kernels. There is no CPU fallback: if the library is missing or no sm_100 GPU is
+present, the calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libqms_cuda.so"
+HEADER = PKG.parent / "include" / "qms_cuda.h"
+
+T_F32, T_F16, T_Q4_0, T_Q4_1, T_Q8_0, T_Q6_K = 0, 1, 2, 3, 8, 14
+OK, EINVAL, ECUDA, ENOMEM, EUNSUPPORTED, ENODEV = 0, -1, -2, -3, -4, -5
+
+Q8_DTYPE = np.dtype([("d", "<f4"), ("ds", "<f4"), ("s16", "<i2", (2,)), ("q", "i1", (32,))])
+
+
+class QmsCudaError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"libqms_cuda error {code}: {msg}")
+        self.code = code
+
+
+class MoeDesc(C.Structure):
+    _fields_ = [("n_embd", C.c_int), ("n_expert", C.c_int), ("n_used", C.c_int), ("n_ff", C.c_int),
+                ("gate_type", C.c_int), ("up_type", C.c_int), ("down_type", C.c_int),
+                ("router", C.c_void_p), ("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p),
+                ("src_on_device", C.c_int)]
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load libqms_cuda.so (built by large_model_b200.build); raises when it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise FileNotFoundError(f"{LIB_PATH} is missing: build it with `python -m large_model_b200.build`")
+    L = C.CDLL(str(LIB_PATH))
+    vp, i32, i64 = C.c_void_p, C.c_int, C.c_int64
+    L.qms_cuda_last_error.restype = C.c_char_p
+    L.qms_cuda_init.argtypes = [i32]
+    L.qms_cuda_stream_sync.argtypes = [vp]
+    L.qms_cuda_quantize_q8.argtypes = [vp, i64, i64, vp, vp]
+    L.qms_cuda_matvec_q8.argtypes = [i32, vp, i64, i64, vp, i32, vp, vp]
+    L.qms_cuda_matvec_f32.argtypes = [vp, i64, i64, vp, i32, vp, vp]
+    L.qms_cuda_moe_create.argtypes = [C.POINTER(MoeDesc), C.POINTER(vp)]
+    L.qms_cuda_moe_destroy.argtypes = [vp]
+    L.qms_cuda_moe_destroy.restype = None
+    L.qms_cuda_moe_device_bytes.argtypes = [vp]
+    L.qms_cuda_moe_device_bytes.restype = i64
+    L.qms_cuda_moe_reserve.argtypes = [vp, i32]
+    L.qms_cuda_moe_forward.argtypes = [vp, vp, i32, vp, vp, vp, vp, vp, vp]
+    L.qms_cuda_moe_forward_host.argtypes = [vp, vp, i32, vp, vp, vp, vp]
+    L.qms_cuda_moe_set_kernel_events.argtypes = [vp, C.POINTER(vp)]
+    _lib = L
+    return L
+
+
+def check(rc: int):
+    if rc != OK:
+        raise QmsCudaError(rc, lib().qms_cuda_last_error().decode())
+
+
+def declared_functions() -> list[str]:
+    """Function names declared in include/*.h (the exported C ABI)."""
+    import re
+    names = []
+    for h in sorted((PKG.parent / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names += re.findall(r"\b(qms_cuda_\w+)\s*\(", text)
+    return sorted(set(names))
+
+
+# ---- torch plumbing ----------------------------------------------------------------------------
+
+def _torch():
+    import torch
+    return torch
+
+
+def _ptr(t) -> C.c_void_p | None:
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None) -> C.c_void_p:
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def init(device: int = 0):
+    check(lib().qms_cuda_init(device))
+
+
+def quantize_q8(x):
+    """x: CUDA float32 [rows][n] -> uint8 [rows][n/32*44] holding QmsQ8 blocks."""
+    torch = _torch()
+    x = x.contiguous()
+    n = x.shape[-1]
+    rows = x.numel() // n
+    out = torch.empty((rows, n // 32 * 44), dtype=torch.uint8, device=x.device)
+    check(lib().qms_cuda_quantize_q8(_ptr(x), n, rows, _ptr(out), _stream()))
+    return out
+
+
+def matvec_q8(typ: int, w, rows: int, cols: int, xq, T: int):
+    torch = _torch()
+    y = torch.empty((T, rows), dtype=torch.float32, device=w.device)
+    check(lib().qms_cuda_matvec_q8(typ, _ptr(w), rows, cols, _ptr(xq), T, _ptr(y), _stream()))
+    return y
+
+
+def matvec_f32(w, x):
+    torch = _torch()
+    rows, cols = w.shape
+    x = x.reshape(-1, cols).contiguous()
+    y = torch.empty((x.shape[0], rows), dtype=torch.float32, device=w.device)
+    check(lib().qms_cuda_matvec_f32(_ptr(w), rows, cols, _ptr(x), x.shape[0], _ptr(y), _stream()))
+    return y
+
+
+class MoeLayer:
+    """One resident MoE layer (the reference's moe(), src/model.c:1032)."""
+
+    def __init__(self, n_embd: int, n_expert: int, n_used: int, n_ff: int, router, gate, up, down,
+                 gate_type: int = T_Q4_0, up_type: int = T_Q4_0, down_type: int = T_Q4_0):
+        on_dev = not isinstance(router, np.ndarray)
+        self._keep = (router, gate, up, down)
+        ptr = (lambda a: a.ctypes.data) if not on_dev else (lambda t: t.data_ptr())
+        d = MoeDesc(n_embd, n_expert, n_used, n_ff, gate_type, up_type, down_type,
+                    ptr(router), ptr(gate), ptr(up), ptr(down), int(on_dev))
+        h = C.c_void_p()
+        check(lib().qms_cuda_moe_create(C.byref(d), C.byref(h)))
+        self._keep = None
+        self.h = h
+        self.n_embd, self.n_expert, self.n_used, self.n_ff = n_embd, n_expert, n_used, n_ff
+
+    @classmethod
+    def from_synth(cls, layer) -> "MoeLayer":
+        return cls(layer.n_embd, layer.n_expert, layer.n_used, layer.n_ff, layer.router, layer.gate,
+                   layer.up, layer.down, layer.gate_type, layer.up_type, layer.down_type)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().qms_cuda_moe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def device_bytes(self) -> int:
+        return lib().qms_cuda_moe_device_bytes(self.h)
+
+    def reserve(self, T: int):
+        check(lib().qms_cuda_moe_reserve(self.h, T))
+
+    def set_kernel_events(self, events):
+        """events: 6 torch.cuda.Event(enable_timing=True) recorded around the three kernels of
+        every following forward (or None to stop)."""
+        if events is None:
+            check(lib().qms_cuda_moe_set_kernel_events(self.h, None))
+            return
+        arr = (C.c_void_p * 6)(*[C.c_void_p(e.cuda_event) for e in events])
+        self._events = events
+        check(lib().qms_cuda_moe_set_kernel_events(self.h, arr))
+
+    def forward(self, xn, out=None, sel=None, wts=None, logits=None, resid=None, stream=None):
+        """xn: CUDA float32 [T][n_embd]. Returns out (CUDA float32 [T][n_embd])."""
+        torch = _torch()
+        xn = xn.reshape(-1, self.n_embd)
+        T = xn.shape[0]
+        if out is None:
+            out = torch.empty_like(xn)
+        check(lib().qms_cuda_moe_forward(self.h, _ptr(xn), T, _ptr(out), _ptr(sel), _ptr(wts), _ptr(logits),
+                                          _ptr(resid), _stream(stream)))
+        return out
+
+    def route(self, xn):
+        """Forward that also returns (out, sel, wts, logits) as CUDA tensors."""
+        torch = _torch()
+        xn = xn.reshape(-1, self.n_embd)
+        T = xn.shape[0]
+        sel = torch.empty((T, self.n_used), dtype=torch.int32, device=xn.device)
+        wts = torch.empty((T, self.n_used), dtype=torch.float32, device=xn.device)
+        logits = torch.empty((T, self.n_expert), dtype=torch.float32, device=xn.device)
+        out = self.forward(xn, sel=sel, wts=wts, logits=logits)
+        return out, sel, wts, logits
+
+    def forward_host(self, xn: np.ndarray, out: np.ndarray | None = None, with_routing: bool = False):
+        """Host-buffer entry point (copies in, runs, copies out, waits)."""
+        xn = np.ascontiguousarray(xn, np.float32).reshape(-1, self.n_embd)
+        T = xn.shape[0]
+        if out is None:
+            out = np.empty_like(xn)
+        sel = np.empty((T, self.n_used), np.int32) if with_routing else None
+        wts = np.empty((T, self.n_used), np.float32) if with_routing else None
+        p = lambda a: None if a is None else C.c_void_p(a.ctypes.data)
+        check(lib().qms_cuda_moe_forward_host(self.h, p(xn), T, p(out), p(sel), p(wts), None))
+        return (out, sel, wts) if with_routing else out

@@ -1,0 +1,596 @@
+// qms_moe.cu - the Qwen3-MoE feed-forward block on B200 (sm_100a).
+//
+// Reference: moe() in src/model.c:1032-1167 with moe_group_fast (src/model.c:969-1007).
+// One forward call is three kernels chained with programmatic dependent launch:
+//   k_moe_router   X CTAs: Q8 quantisation of xn (src/kernels.c:34-53), router logits in the
+//                  reference's exact F32 order (src/kernels.c:202-219); the last CTA to finish
+//                  does softmax / top-k / renormalisation (src/model.c:1045-1064) for T <= 4,
+//                  k_moe_topk does it with one CTA per token for larger T.
+//   k_moe_gate_up  one warp per (slot, f): gate row f and up row f of the slot's expert against
+//                  the token's Q8 row (phase 1, :979-988), a = silu(g) * u (:994); the CTA that
+//                  completes a 32-row group re-quantises it to Q8 (phase 2, :995).
+//   k_moe_down     one CTA per (token, 8 output rows): down rows of all n_used experts
+//                  (phase 3, :998-1005), then the weighted sum in selection order with one
+//                  fused multiply-add per expert (:1152-1162), plus the optional residual.
+// Expert weights are repacked at load into 16-byte-aligned rows (qms_common.cuh) so each
+// Q4_0 block is one 128-bit load; gate row f and up row f of an expert are stored adjacently.
+#include <string.h>
+
+#include <algorithm>
+
+#include "qms_common.cuh"
+#include "qms_router.cuh"
+
+using namespace qms;
+
+struct QmsCudaMoe {
+    int device;
+    int E, X, K, F, nbE, nbF;
+    int gate_type, up_type, down_type;
+    float *router;       // [X][E] F32
+    uint8_t *gu;         // [X][F][2] repacked rows of E (gate, up)
+    uint8_t *dn;         // [X][E] repacked rows of F
+    size_t gu_row, gu_expert, dn_row, dn_expert, weight_bytes;
+    // scratch, sized for cap_T tokens
+    int cap_T;
+    void *scratch;
+    size_t scratch_bytes;
+    int8_t *xq_q;
+    float *xq_d;
+    int *xq_s;
+    float *logits;
+    int *sel;
+    float *wts;
+    float *act;
+    int8_t *aq_q;
+    float *aq_d;
+    int *aq_s;
+    int *cnt;            // [0]: router arrivals; [1 + slot*nbF + g]: gate/up group arrivals
+    // host-buffer entry point
+    cudaStream_t hstream;
+    float *d_in, *d_out;
+    int io_cap_T;
+    // optional per-kernel timing events (qms_cuda_moe_set_kernel_events)
+    cudaEvent_t ev[6];
+    int timing;
+};
+
+namespace qms {
+
+constexpr int kTopkInRouterMaxT = 4;   // above this, k_moe_topk runs one CTA per token
+constexpr int kGateUpRows = 8;         // f values per gate/up CTA (one per warp)
+constexpr int kDownRows = 8;           // output rows per down CTA
+
+// ---- load-time repack (GGUF Q4_0 rows -> nibble plane + scale plane) -----------------------
+__global__ void k_repack_q4_0(const uint8_t *__restrict__ src, int64_t nrows, int nb, uint8_t *__restrict__ dst,
+                              size_t dst_stride, int row_mul, int row_add) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= nrows * nb) return;
+    const int64_t r = idx / nb;
+    const int b = (int)(idx % nb);
+    const uint16_t *s = reinterpret_cast<const uint16_t *>(src + idx * 18);
+    uint8_t *row = dst + (size_t)(r * row_mul + row_add) * dst_stride;
+    uint4 v;
+    v.x = (uint32_t)s[1] | ((uint32_t)s[2] << 16);
+    v.y = (uint32_t)s[3] | ((uint32_t)s[4] << 16);
+    v.z = (uint32_t)s[5] | ((uint32_t)s[6] << 16);
+    v.w = (uint32_t)s[7] | ((uint32_t)s[8] << 16);
+    *reinterpret_cast<uint4 *>(row + (size_t)b * 16) = v;
+    *reinterpret_cast<uint16_t *>(row + (size_t)nb * 16 + (size_t)b * 2) = s[0];
+}
+
+// ---- top-k of one token by a whole CTA (blockDim.x >= X, X <= 256) --------------------------
+// Selection order = rank of the logit, ties to the lower expert index: the reference's repeated
+// strict-'>' argmax over probabilities (src/model.c:1053-1062). exp(l - max) is strictly
+// increasing, so ranking the float logits gives the same order and the same tie-breaks.
+// prob = exp((double)l - max) / z as in src/model.c:1047-1050, with z summed as a tree (the
+// reference sums sequentially; the difference is ~1e-16 relative, below float resolution of
+// the final weights). Weights (float)(p_j / sum_j p_j), the sum taken in selection order.
+__device__ void topk_token(const float *__restrict__ lg, int X, int K, int *__restrict__ sel, float *__restrict__ wts,
+                           float *sv, double *sred, double *spj) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const float v = tid < X ? __ldcg(lg + tid) : -INFINITY;
+    if (tid < X) sv[tid] = v;
+    float mx = warp_max(v);
+    if (lane == 0) sred[warp] = mx;
+    __syncthreads();
+    mx = (float)sred[0];
+    for (int i = 1; i < nw; i++) mx = fmaxf(mx, (float)sred[i]);
+    const double ex = tid < X ? exp((double)v - (double)mx) : 0.0;
+    double z = ex;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+    __syncthreads();
+    if (lane == 0) sred[warp] = z;
+    __syncthreads();
+    z = 0.0;
+    for (int i = 0; i < nw; i++) z += sred[i];
+    if (tid < X) {
+        int rank = 0;
+        for (int j = 0; j < tid; j++) rank += sv[j] >= v;
+        for (int j = tid + 1; j < X; j++) rank += sv[j] > v;
+        if (rank < K) {
+            sel[rank] = tid;
+            spj[rank] = ex / z;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        double ws = 0.0;
+        for (int j = 0; j < K; j++) ws += spj[j];
+        for (int j = 0; j < K; j++) wts[j] = (float)(spj[j] / ws);
+    }
+    __syncthreads();
+}
+
+// ---- router: quantise xn, logits, (last CTA) top-k --------------------------------------------
+__global__ void __launch_bounds__(256) k_moe_router(const float *__restrict__ W, int X, int E, const float *__restrict__ xn,
+                                                    int T, int K, int8_t *__restrict__ xq_q, float *__restrict__ xq_d,
+                                                    int *__restrict__ xq_s, float *__restrict__ logits,
+                                                    int *__restrict__ sel, float *__restrict__ wts,
+                                                    int *__restrict__ cnt, int do_topk) {
+    extern __shared__ float4 smem4[];
+    float *srow = reinterpret_cast<float *>(smem4);
+    __shared__ double sred[8];
+    __shared__ double spj[64];
+    __shared__ int s_last;
+    pdl_trigger();
+    const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nbE = E / 32;
+    // (0) Q8 rows of xn: block b = e + X*m, one warp per block
+    for (int64_t b = e + (int64_t)X * warp; b < (int64_t)T * nbE; b += (int64_t)X * 8) {
+        const Q8Lane r = quantize_lane(xn[b * 32 + lane]);
+        xq_q[b * 32 + lane] = (int8_t)r.q;
+        if (lane == 0) {
+            xq_d[b] = r.d;
+            xq_s[b] = r.sum;
+        }
+    }
+    // (1) router row e into shared memory
+    const float4 *src = reinterpret_cast<const float4 *>(W + (size_t)e * E);
+    for (int i = tid; i < E / 4; i += blockDim.x) smem4[i] = __ldg(src + i);
+    __syncthreads();
+    // (2) logits[t][e], 16 threads per token
+    const int grp = tid >> 4, k = tid & 15;
+    for (int t0 = 0; t0 < T; t0 += 16) {
+        const int t = t0 + grp;
+        const bool valid = t < T;
+        const float v = dot_f32_exact16(srow, xn + (size_t)(valid ? t : 0) * E, E, k);
+        if (valid && k == 0) {
+            logits[(size_t)t * X + e] = v;
+            __threadfence();
+        }
+    }
+    if (!do_topk) return;
+    // (3) the last CTA to finish ranks the experts of every token
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        s_last = atomicAdd(cnt, 1) == X - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int t = 0; t < T; t++) topk_token(logits + (size_t)t * X, X, K, sel + t * K, wts + t * K, srow, sred, spj);
+    if (tid == 0) *cnt = 0;
+}
+
+__global__ void __launch_bounds__(256) k_moe_topk(const float *__restrict__ logits, int X, int K, int *__restrict__ sel,
+                                                  float *__restrict__ wts) {
+    __shared__ float sv[256];
+    __shared__ double sred[8];
+    __shared__ double spj[64];
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x;
+    topk_token(logits + (size_t)t * X, X, K, sel + t * K, wts + t * K, sv, sred, spj);
+}
+
+// ---- gate/up + SwiGLU + Q8 re-quantisation ---------------------------------------------------
+template <int NBL>
+__global__ void __launch_bounds__(256) k_moe_gate_up(const uint8_t *__restrict__ gu, size_t gu_expert, size_t gu_row,
+                                                     int nbE, int F, int K, const int8_t *__restrict__ xq_q,
+                                                     const float *__restrict__ xq_d, const int *__restrict__ xq_s,
+                                                     const int *__restrict__ sel, float *__restrict__ act,
+                                                     int8_t *__restrict__ aq_q, float *__restrict__ aq_d,
+                                                     int *__restrict__ aq_s, int *__restrict__ gcnt) {
+    __shared__ int s_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int f = blockIdx.x * kGateUpRows + warp;
+    const int slot = blockIdx.y, t = slot / K;
+    pdl_wait();
+    const int e = __ldcg(sel + slot);
+    const uint8_t *rg = gu + (size_t)e * gu_expert + (size_t)(2 * f) * gu_row;
+    const uint8_t *ru = rg + gu_row;
+    uint4 ng[NBL], nu[NBL];
+    uint16_t sg[NBL], su[NBL];
+#pragma unroll
+    for (int i = 0; i < NBL; i++) {
+        const int b = lane + 32 * i;
+        if (b < nbE) {
+            ng[i] = ld_stream16(rg + (size_t)b * 16);
+            nu[i] = ld_stream16(ru + (size_t)b * 16);
+            sg[i] = ld_stream2(rg + (size_t)nbE * 16 + b * 2);
+            su[i] = ld_stream2(ru + (size_t)nbE * 16 + b * 2);
+        }
+    }
+    const int8_t *xq = xq_q + (size_t)t * nbE * 32;
+    float g = 0.0f, u = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NBL; i++) {
+        const int b = lane + 32 * i;
+        if (b < nbE) {
+            const int4 xa0 = __ldcg(reinterpret_cast<const int4 *>(xq + b * 32));
+            const int4 xa1 = __ldcg(reinterpret_cast<const int4 *>(xq + b * 32 + 16));
+            const float xd = __ldcg(xq_d + (size_t)t * nbE + b);
+            const int xs8 = 8 * __ldcg(xq_s + (size_t)t * nbE + b);
+            g = fmaf((float)(q4_block_isum(ng[i], xa0, xa1) - xs8), h2f(sg[i]) * xd, g);
+            u = fmaf((float)(q4_block_isum(nu[i], xa0, xa1) - xs8), h2f(su[i]) * xd, u);
+        }
+    }
+    g = warp_sum(g);
+    u = warp_sum(u);
+    if (lane == 0) {
+        const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+        act[(size_t)slot * F + f] = __fmul_rn(s, u);
+        __threadfence();
+    }
+    __syncthreads();
+    pdl_trigger();
+    const int nbF = F / 32, grp = f / 32;
+    int *c = gcnt + (size_t)slot * nbF + grp;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(c, kGateUpRows) == 32 - kGateUpRows;
+    }
+    __syncthreads();
+    if (s_last && warp == 0) {
+        __threadfence();
+        const size_t base = (size_t)slot * F + (size_t)grp * 32;
+        const Q8Lane r = quantize_lane(__ldcg(act + base + lane));
+        aq_q[base + lane] = (int8_t)r.q;
+        if (lane == 0) {
+            aq_d[(size_t)slot * nbF + grp] = r.d;
+            aq_s[(size_t)slot * nbF + grp] = r.sum;
+            *c = 0;
+        }
+    }
+}
+
+// ---- down + weighted combine (+ residual) ----------------------------------------------------
+template <int NBL>
+__global__ void __launch_bounds__(256) k_moe_down(const uint8_t *__restrict__ dn, size_t dn_expert, size_t dn_row,
+                                                  int nbF, int E, int K, const int8_t *__restrict__ aq_q,
+                                                  const float *__restrict__ aq_d, const int *__restrict__ aq_s,
+                                                  const int *__restrict__ sel, const float *__restrict__ wts,
+                                                  const float *resid, float *out) {
+    extern __shared__ float sdn[];   // [K][kDownRows]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i0 = blockIdx.x * kDownRows, t = blockIdx.y;
+    const int F = nbF * 32;
+    pdl_wait();
+    int cur = -1;
+    int4 xa0[NBL], xa1[NBL];
+    float xd[NBL];
+    int xs8[NBL];
+    for (int p = warp; p < K * kDownRows; p += 8) {
+        const int k = p % K, r = p / K;
+        const int slot = t * K + k;
+        if (k != cur) {
+            cur = k;
+#pragma unroll
+            for (int i = 0; i < NBL; i++) {
+                const int b = lane + 32 * i;
+                if (b < nbF) {
+                    const int8_t *a = aq_q + (size_t)slot * F + b * 32;
+                    xa0[i] = __ldcg(reinterpret_cast<const int4 *>(a));
+                    xa1[i] = __ldcg(reinterpret_cast<const int4 *>(a + 16));
+                    xd[i] = __ldcg(aq_d + (size_t)slot * nbF + b);
+                    xs8[i] = 8 * __ldcg(aq_s + (size_t)slot * nbF + b);
+                }
+            }
+        }
+        const int e = __ldcg(sel + slot);
+        const uint8_t *row = dn + (size_t)e * dn_expert + (size_t)(i0 + r) * dn_row;
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NBL; i++) {
+            const int b = lane + 32 * i;
+            if (b < nbF) {
+                const uint4 nib = ld_stream16(row + (size_t)b * 16);
+                const float dw = h2f(ld_stream2(row + (size_t)nbF * 16 + b * 2));
+                acc = fmaf((float)(q4_block_isum(nib, xa0[i], xa1[i]) - xs8[i]), dw * xd[i], acc);
+            }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) sdn[k * kDownRows + r] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x < kDownRows) {
+        const int i = i0 + threadIdx.x;
+        float o = 0.0f;
+        for (int j = 0; j < K; j++) o = __fmaf_rn(__ldcg(wts + t * K + j), sdn[j * kDownRows + threadIdx.x], o);
+        if (resid) o = __fadd_rn(resid[(size_t)t * E + i], o);
+        out[(size_t)t * E + i] = o;
+    }
+}
+
+template <typename... P, typename... A>
+static cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A... args) {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, ((P)args)...);
+}
+
+static size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static int ensure_device(int dev) {
+    int cur = -1;
+    QMS_CK(cudaGetDevice(&cur));
+    if (cur != dev) QMS_CK(cudaSetDevice(dev));
+    return QMS_CUDA_OK;
+}
+
+static int upload_q4_0(const void *src, int on_device, int64_t nrows, int nb, uint8_t *dst, size_t stride, int mul,
+                       int add) {
+    const size_t bytes = (size_t)nrows * nb * 18;
+    const uint8_t *dsrc = (const uint8_t *)src;
+    uint8_t *tmp = nullptr;
+    if (!on_device) {
+        if (cudaMalloc(&tmp, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            set_error("moe_create: cannot allocate %zu bytes of staging", bytes);
+            return QMS_CUDA_ENOMEM;
+        }
+        const cudaError_t e = cudaMemcpy(tmp, src, bytes, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(tmp);
+            set_error("moe_create: upload failed: %s", cudaGetErrorString(e));
+            return QMS_CUDA_ECUDA;
+        }
+        dsrc = tmp;
+    }
+    const int64_t n = nrows * nb;
+    k_repack_q4_0<<<(unsigned)((n + 255) / 256), 256>>>(dsrc, nrows, nb, dst, stride, mul, add);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (tmp) cudaFree(tmp);
+    if (e != cudaSuccess) {
+        set_error("moe_create: repack failed: %s", cudaGetErrorString(e));
+        return QMS_CUDA_ECUDA;
+    }
+    return QMS_CUDA_OK;
+}
+
+}  // namespace qms
+
+extern "C" {
+
+void qms_cuda_moe_destroy(QmsCudaMoe *m) {
+    if (!m) return;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    cudaSetDevice(m->device);
+    cudaFree(m->router);
+    cudaFree(m->gu);
+    cudaFree(m->dn);
+    cudaFree(m->scratch);
+    cudaFree(m->d_in);
+    cudaFree(m->d_out);
+    if (m->hstream) cudaStreamDestroy(m->hstream);
+    if (cur >= 0) cudaSetDevice(cur);
+    free(m);
+}
+
+int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
+    clear_error();
+    QMS_REQUIRE(d && out, QMS_CUDA_EINVAL, "moe_create: NULL argument");
+    *out = nullptr;
+    const int E = d->n_embd, X = d->n_expert, K = d->n_used, F = d->n_ff;
+    QMS_REQUIRE(d->router && d->gate && d->up && d->down, QMS_CUDA_EINVAL, "moe_create: NULL tensor");
+    QMS_REQUIRE(E > 0 && X > 0 && K > 0 && F > 0 && K <= X, QMS_CUDA_EINVAL, "moe_create: bad dimensions");
+    // the reference's integer fast path condition (src/model.c:1090-1093)
+    QMS_REQUIRE(E % 256 == 0 && F % 32 == 0, QMS_CUDA_EUNSUPPORTED,
+                "moe_create: n_embd %% 256 and n_ff %% 32 must be 0 (integer fast path)");
+    QMS_REQUIRE(d->gate_type == QMS_T_Q4_0 && d->up_type == QMS_T_Q4_0 && d->down_type == QMS_T_Q4_0,
+                QMS_CUDA_EUNSUPPORTED, "moe_create: expert types %d/%d/%d not supported (Q4_0)", d->gate_type,
+                d->up_type, d->down_type);
+    QMS_REQUIRE(E <= 4096 && F <= 2048 && X <= 256 && K <= 64, QMS_CUDA_EUNSUPPORTED,
+                "moe_create: n_embd <= 4096, n_ff <= 2048, n_expert <= 256, n_used <= 64 required");
+    int dev = 0;
+    QMS_CK(cudaGetDevice(&dev));
+    QmsCudaMoe *m = (QmsCudaMoe *)calloc(1, sizeof(QmsCudaMoe));
+    QMS_REQUIRE(m, QMS_CUDA_ENOMEM, "moe_create: out of host memory");
+    m->device = dev;
+    m->E = E; m->X = X; m->K = K; m->F = F;
+    m->nbE = E / 32; m->nbF = F / 32;
+    m->gate_type = d->gate_type; m->up_type = d->up_type; m->down_type = d->down_type;
+    m->gu_row = q4_row_stride(m->nbE);
+    m->gu_expert = m->gu_row * 2 * (size_t)F;
+    m->dn_row = q4_row_stride(m->nbF);
+    m->dn_expert = m->dn_row * (size_t)E;
+    const size_t rb = (size_t)X * E * 4, gb = m->gu_expert * X, db = m->dn_expert * X;
+    m->weight_bytes = rb + gb + db;
+    if (cudaMalloc(&m->router, rb) != cudaSuccess || cudaMalloc(&m->gu, gb) != cudaSuccess ||
+        cudaMalloc(&m->dn, db) != cudaSuccess) {
+        cudaGetLastError();
+        qms_cuda_moe_destroy(m);
+        set_error("moe_create: cannot allocate %.2f GB of weights", (rb + gb + db) / 1e9);
+        return QMS_CUDA_ENOMEM;
+    }
+    int rc = QMS_CUDA_OK;
+    if (cudaMemset(m->gu, 0, gb) != cudaSuccess || cudaMemset(m->dn, 0, db) != cudaSuccess ||
+        cudaMemcpy(m->router, d->router, rb, d->src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice) !=
+            cudaSuccess) {
+        set_error("moe_create: %s", cudaGetErrorString(cudaGetLastError()));
+        rc = QMS_CUDA_ECUDA;
+    }
+    if (rc == QMS_CUDA_OK)
+        rc = upload_q4_0(d->gate, d->src_on_device, (int64_t)X * F, m->nbE, m->gu, m->gu_row, 2, 0);
+    if (rc == QMS_CUDA_OK)
+        rc = upload_q4_0(d->up, d->src_on_device, (int64_t)X * F, m->nbE, m->gu, m->gu_row, 2, 1);
+    if (rc == QMS_CUDA_OK)
+        rc = upload_q4_0(d->down, d->src_on_device, (int64_t)X * E, m->nbF, m->dn, m->dn_row, 1, 0);
+    if (rc != QMS_CUDA_OK) {
+        qms_cuda_moe_destroy(m);
+        return rc;
+    }
+    *out = m;
+    return QMS_CUDA_OK;
+}
+
+int64_t qms_cuda_moe_device_bytes(const QmsCudaMoe *m) {
+    if (!m) return 0;
+    return (int64_t)(m->weight_bytes + m->scratch_bytes) + (int64_t)m->io_cap_T * m->E * 8;
+}
+
+int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
+    QMS_REQUIRE(m && T >= 0, QMS_CUDA_EINVAL, "moe_reserve: bad arguments");
+    QMS_REQUIRE((int64_t)T * m->K <= 65535, QMS_CUDA_EINVAL, "moe: T * n_used must be <= 65535");
+    if (T <= m->cap_T) return QMS_CUDA_OK;
+    int rc = ensure_device(m->device);
+    if (rc) return rc;
+    const size_t TK = (size_t)T * m->K;
+    size_t off = 0;
+    const size_t o_xq_q = off; off += al256((size_t)T * m->E);
+    const size_t o_xq_d = off; off += al256((size_t)T * m->nbE * 4);
+    const size_t o_xq_s = off; off += al256((size_t)T * m->nbE * 4);
+    const size_t o_log = off; off += al256((size_t)T * m->X * 4);
+    const size_t o_sel = off; off += al256(TK * 4);
+    const size_t o_wts = off; off += al256(TK * 4);
+    const size_t o_act = off; off += al256(TK * m->F * 4);
+    const size_t o_aq_q = off; off += al256(TK * m->F);
+    const size_t o_aq_d = off; off += al256(TK * m->nbF * 4);
+    const size_t o_aq_s = off; off += al256(TK * m->nbF * 4);
+    const size_t o_cnt = off; off += al256((1 + TK * m->nbF) * 4);
+    void *p = nullptr;
+    if (cudaMalloc(&p, off) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("moe_reserve: cannot allocate %zu bytes of scratch for T=%d", off, T);
+        return QMS_CUDA_ENOMEM;
+    }
+    if (cudaMemset(p, 0, off) != cudaSuccess) {
+        cudaFree(p);
+        set_error("moe_reserve: memset failed");
+        return QMS_CUDA_ECUDA;
+    }
+    cudaFree(m->scratch);
+    char *b = (char *)p;
+    m->scratch = p;
+    m->scratch_bytes = off;
+    m->xq_q = (int8_t *)(b + o_xq_q);
+    m->xq_d = (float *)(b + o_xq_d);
+    m->xq_s = (int *)(b + o_xq_s);
+    m->logits = (float *)(b + o_log);
+    m->sel = (int *)(b + o_sel);
+    m->wts = (float *)(b + o_wts);
+    m->act = (float *)(b + o_act);
+    m->aq_q = (int8_t *)(b + o_aq_q);
+    m->aq_d = (float *)(b + o_aq_d);
+    m->aq_s = (int *)(b + o_aq_s);
+    m->cnt = (int *)(b + o_cnt);
+    m->cap_T = T;
+    return QMS_CUDA_OK;
+}
+
+int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int *sel, float *wts, float *logits,
+                         const float *resid, void *stream) {
+    QMS_REQUIRE(m && T >= 0, QMS_CUDA_EINVAL, "moe_forward: bad arguments");
+    if (T == 0) return QMS_CUDA_OK;
+    QMS_REQUIRE(xn && out, QMS_CUDA_EINVAL, "moe_forward: NULL xn or out");
+    int rc = ensure_device(m->device);
+    if (rc) return rc;
+    if (T > m->cap_T) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        QMS_CK(cudaStreamIsCapturing((cudaStream_t)stream, &cs));
+        QMS_REQUIRE(cs == cudaStreamCaptureStatusNone, QMS_CUDA_EINVAL,
+                    "moe_forward: scratch for T=%d must be reserved before graph capture", T);
+        if ((rc = qms_cuda_moe_reserve(m, T))) return rc;
+    }
+    const cudaStream_t s = (cudaStream_t)stream;
+    const int topk_in_router = T <= kTopkInRouterMaxT;
+    const size_t rsmem = (size_t)m->E * 4;
+    if (m->timing) QMS_CK(cudaEventRecord(m->ev[0], s));
+    k_moe_router<<<m->X, 256, rsmem, s>>>(m->router, m->X, m->E, xn, T, m->K, m->xq_q, m->xq_d, m->xq_s, m->logits,
+                                         m->sel, m->wts, m->cnt, topk_in_router);
+    QMS_CK(cudaGetLastError());
+    if (!topk_in_router)
+        QMS_CK(launch_pdl(k_moe_topk, dim3(T), dim3(256), 0, s, (const float *)m->logits, m->X, m->K, m->sel, m->wts));
+    if (m->timing) {
+        QMS_CK(cudaEventRecord(m->ev[1], s));
+        QMS_CK(cudaEventRecord(m->ev[2], s));
+    }
+    const dim3 ggrid(m->F / kGateUpRows, T * m->K);
+    const int nbl = (m->nbE + 31) / 32;
+    auto gk = nbl == 1 ? k_moe_gate_up<1> : nbl == 2 ? k_moe_gate_up<2> : nbl == 3 ? k_moe_gate_up<3> : k_moe_gate_up<4>;
+    QMS_CK(launch_pdl(gk, ggrid, dim3(256), 0, s, (const uint8_t *)m->gu, m->gu_expert, m->gu_row, m->nbE, m->F, m->K,
+                      (const int8_t *)m->xq_q, (const float *)m->xq_d, (const int *)m->xq_s, (const int *)m->sel,
+                      m->act, m->aq_q, m->aq_d, m->aq_s, m->cnt + 1));
+    if (m->timing) {
+        QMS_CK(cudaEventRecord(m->ev[3], s));
+        QMS_CK(cudaEventRecord(m->ev[4], s));
+    }
+    const dim3 dgrid(m->E / kDownRows, T);
+    auto dk = m->nbF <= 32 ? k_moe_down<1> : k_moe_down<2>;
+    QMS_CK(launch_pdl(dk, dgrid, dim3(256), (size_t)m->K * kDownRows * 4, s, (const uint8_t *)m->dn, m->dn_expert,
+                      m->dn_row, m->nbF, m->E, m->K, (const int8_t *)m->aq_q, (const float *)m->aq_d,
+                      (const int *)m->aq_s, (const int *)m->sel, (const float *)m->wts, resid, out));
+    if (m->timing) QMS_CK(cudaEventRecord(m->ev[5], s));
+    const size_t TK = (size_t)T * m->K;
+    if (sel) QMS_CK(cudaMemcpyAsync(sel, m->sel, TK * 4, cudaMemcpyDeviceToDevice, s));
+    if (wts) QMS_CK(cudaMemcpyAsync(wts, m->wts, TK * 4, cudaMemcpyDeviceToDevice, s));
+    if (logits) QMS_CK(cudaMemcpyAsync(logits, m->logits, (size_t)T * m->X * 4, cudaMemcpyDeviceToDevice, s));
+    return QMS_CUDA_OK;
+}
+
+int qms_cuda_moe_set_kernel_events(QmsCudaMoe *m, void **events) {
+    QMS_REQUIRE(m, QMS_CUDA_EINVAL, "moe_set_kernel_events: NULL layer");
+    m->timing = events != nullptr;
+    for (int i = 0; i < 6; i++) m->ev[i] = events ? (cudaEvent_t)events[i] : nullptr;
+    return QMS_CUDA_OK;
+}
+
+int qms_cuda_moe_forward_host(QmsCudaMoe *m, const float *xn, int T, float *out, int *sel, float *wts, float *logits) {
+    QMS_REQUIRE(m && T >= 0, QMS_CUDA_EINVAL, "moe_forward_host: bad arguments");
+    if (T == 0) return QMS_CUDA_OK;
+    QMS_REQUIRE(xn && out, QMS_CUDA_EINVAL, "moe_forward_host: NULL xn or out");
+    int rc = ensure_device(m->device);
+    if (rc) return rc;
+    if (!m->hstream) QMS_CK(cudaStreamCreateWithFlags(&m->hstream, cudaStreamNonBlocking));
+    if ((rc = qms_cuda_moe_reserve(m, T))) return rc;
+    if (T > m->io_cap_T) {
+        cudaFree(m->d_in);
+        cudaFree(m->d_out);
+        m->d_in = m->d_out = nullptr;
+        m->io_cap_T = 0;
+        if (cudaMalloc(&m->d_in, (size_t)T * m->E * 4) != cudaSuccess ||
+            cudaMalloc(&m->d_out, (size_t)T * m->E * 4) != cudaSuccess) {
+            cudaGetLastError();
+            set_error("moe_forward_host: cannot allocate I/O buffers for T=%d", T);
+            return QMS_CUDA_ENOMEM;
+        }
+        m->io_cap_T = T;
+    }
+    const cudaStream_t s = m->hstream;
+    const size_t xb = (size_t)T * m->E * 4;
+    QMS_CK(cudaMemcpyAsync(m->d_in, xn, xb, cudaMemcpyHostToDevice, s));
+    if ((rc = qms_cuda_moe_forward(m, m->d_in, T, m->d_out, nullptr, nullptr, nullptr, nullptr, s))) return rc;
+    QMS_CK(cudaMemcpyAsync(out, m->d_out, xb, cudaMemcpyDeviceToHost, s));
+    const size_t TK = (size_t)T * m->K;
+    if (sel) QMS_CK(cudaMemcpyAsync(sel, m->sel, TK * 4, cudaMemcpyDeviceToHost, s));
+    if (wts) QMS_CK(cudaMemcpyAsync(wts, m->wts, TK * 4, cudaMemcpyDeviceToHost, s));
+    if (logits) QMS_CK(cudaMemcpyAsync(logits, m->logits, (size_t)T * m->X * 4, cudaMemcpyDeviceToHost, s));
+    QMS_CK(cudaStreamSynchronize(s));
+    return QMS_CUDA_OK;
+}
+
+}  // extern "C"

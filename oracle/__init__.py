@@ -1,0 +1,232 @@
+"""ctypes loaders for the CPU checkers (test infrastructure only).
+
+`Oracle` wraps oracle/_build/libqms_oracle.so, the C restatement of qms's MoE path.
+`Reference` wraps oracle/_ref/libqms_ref_*.so, the reference compiled from its own sources
+(oracle/Makefile, target `ref`). Only tests/, __graft_entry__.smoke() and bench.py's
+cpu_baseline / reference arm import this package; the product path never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "_build" / "libqms_oracle.so"
+REF_DIR = HERE / "_ref"
+
+T_F32, T_F16, T_Q4_0, T_Q4_1, T_Q8_0, T_Q6_K = 0, 1, 2, 3, 8, 14
+
+# OrcQ8 / QmsQ8: float d; float ds; int16 s16[2]; int8 q[32]  (44 bytes, src/kernels.h:7-12)
+Q8_DTYPE = np.dtype([("d", "<f4"), ("ds", "<f4"), ("s16", "<i2", (2,)), ("q", "i1", (32,))])
+assert Q8_DTYPE.itemsize == 44
+
+
+def row_bytes(typ: int, ne0: int) -> int:
+    """Bytes per row of ne0 elements (src/gguf.c:85-96)."""
+    return {T_F32: ne0 * 4, T_F16: ne0 * 2,
+            T_Q4_0: ne0 // 32 * 18 if ne0 % 32 == 0 else 0,
+            T_Q4_1: ne0 // 32 * 20 if ne0 % 32 == 0 else 0,
+            T_Q8_0: ne0 // 32 * 34 if ne0 % 32 == 0 else 0,
+            T_Q6_K: ne0 // 256 * 210 if ne0 % 256 == 0 else 0}.get(typ, 0)
+
+
+def _p(a: np.ndarray):
+    return C.c_void_p(a.ctypes.data) if a is not None else None
+
+
+def _build_oracle():
+    if not ORACLE_SO.exists():
+        import subprocess
+        subprocess.run(["make", "-C", str(HERE), "all"], check=True, capture_output=True)
+
+
+class Oracle:
+    """The C restatement (kind "port")."""
+
+    def __init__(self):
+        _build_oracle()
+        self.lib = L = C.CDLL(str(ORACLE_SO))
+        vp, i64, i32 = C.c_void_p, C.c_int64, C.c_int
+        L.orc_f16_to_f32.argtypes = [C.c_uint16]
+        L.orc_f16_to_f32.restype = C.c_float
+        L.orc_dequant_row.argtypes = [i32, vp, vp, i64]
+        L.orc_dequant_row.restype = i32
+        L.orc_quantize_q8.argtypes = [vp, i64, vp]
+        L.orc_vec_dot_q8.argtypes = [i32, vp, vp, i64]
+        L.orc_vec_dot_q8.restype = C.c_float
+        L.orc_vec_dot_f32.argtypes = [vp, vp, i64]
+        L.orc_vec_dot_f32.restype = C.c_float
+        L.orc_matmul.argtypes = [i32, i64, i64, vp, vp, i32, vp]
+        L.orc_route.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp]
+        L.orc_moe.argtypes = [vp, vp, i32, vp, vp, vp, vp]
+        L.orc_moe.restype = i32
+        L.orc_swiglu.argtypes = [vp, vp, i64, vp]
+        L.orc_set_threads.argtypes = [i32]
+
+    def set_threads(self, n: int):
+        self.lib.orc_set_threads(int(n))
+
+    def f16_to_f32(self, h: int) -> float:
+        return self.lib.orc_f16_to_f32(h)
+
+    def dequant_row(self, typ: int, src: np.ndarray, n: int) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        if self.lib.orc_dequant_row(typ, _p(np.ascontiguousarray(src)), _p(out), n) != 0:
+            raise ValueError("unsupported type or size")
+        return out
+
+    def quantize_q8(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty(x.size // 32, Q8_DTYPE)
+        self.lib.orc_quantize_q8(_p(x), x.size, _p(out))
+        return out
+
+    def vec_dot_q8(self, typ: int, w: np.ndarray, xq: np.ndarray, n: int) -> float:
+        return self.lib.orc_vec_dot_q8(typ, _p(np.ascontiguousarray(w)), _p(xq), n)
+
+    def vec_dot_f32(self, w: np.ndarray, x: np.ndarray) -> float:
+        w = np.ascontiguousarray(w, np.float32)
+        x = np.ascontiguousarray(x, np.float32)
+        return self.lib.orc_vec_dot_f32(_p(w), _p(x), x.size)
+
+    def matmul(self, typ: int, rows: int, cols: int, w: np.ndarray, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, cols)
+        y = np.empty((x.shape[0], rows), np.float32)
+        self.lib.orc_matmul(typ, rows, cols, _p(np.ascontiguousarray(w)), _p(x), x.shape[0], _p(y))
+        return y
+
+    def route(self, router: np.ndarray, K: int, xn: np.ndarray):
+        X, E = router.shape
+        xn = np.ascontiguousarray(xn, np.float32).reshape(-1, E)
+        T = xn.shape[0]
+        logits = np.empty((T, X), np.float32)
+        sel = np.empty((T, K), np.int32)
+        w = np.empty((T, K), np.float32)
+        self.lib.orc_route(_p(np.ascontiguousarray(router, np.float32)), X, E, K, _p(xn), T,
+                           _p(logits), _p(sel), _p(w))
+        return logits, sel, w
+
+    def swiglu(self, g: np.ndarray, u: np.ndarray) -> np.ndarray:
+        g = np.ascontiguousarray(g, np.float32)
+        u = np.ascontiguousarray(u, np.float32)
+        a = np.empty_like(g)
+        self.lib.orc_swiglu(_p(g), _p(u), g.size, _p(a))
+        return a
+
+    def moe(self, layer, xn: np.ndarray):
+        """layer: synth.MoeLayer-like object. Returns (out, sel, w, logits)."""
+        E, X, K = layer.n_embd, layer.n_expert, layer.n_used
+        xn = np.ascontiguousarray(xn, np.float32).reshape(-1, E)
+        T = xn.shape[0]
+        out = np.empty((T, E), np.float32)
+        sel = np.empty((T, K), np.int32)
+        w = np.empty((T, K), np.float32)
+        logits = np.empty((T, X), np.float32)
+
+        class Desc(C.Structure):
+            _fields_ = [("n_embd", C.c_int), ("n_expert", C.c_int), ("n_used", C.c_int),
+                        ("n_ff", C.c_int), ("gate_type", C.c_int), ("up_type", C.c_int),
+                        ("down_type", C.c_int), ("router", C.c_void_p), ("gate", C.c_void_p),
+                        ("up", C.c_void_p), ("down", C.c_void_p)]
+        d = Desc(E, X, K, layer.n_ff, layer.gate_type, layer.up_type, layer.down_type,
+                 layer.router.ctypes.data, layer.gate.ctypes.data, layer.up.ctypes.data,
+                 layer.down.ctypes.data)
+        if self.lib.orc_moe(C.byref(d), _p(xn), T, _p(out), _p(sel), _p(w), _p(logits)) != 0:
+            raise ValueError("layer does not take the integer fast path")
+        return out, sel, w, logits
+
+
+def ref_variant() -> str | None:
+    """Pick the reference build this host can run: v4 (AVX-512 VNNI) when the CPU has it."""
+    flags = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    flags = line
+                    break
+    except OSError:
+        pass
+    need_v4 = ("avx512f", "avx512bw", "avx512dq", "avx512vl", "avx512cd", "avx512_vnni")
+    for v in (["v4", "v3"] if all(n in flags.split() for n in need_v4) else ["v3"]):
+        if (REF_DIR / f"libqms_ref_{v}.so").exists():
+            return v
+    return None
+
+
+def reference_available() -> bool:
+    return ref_variant() is not None
+
+
+class Reference:
+    """The reference's own code (kind "reference"), built from its sources by oracle/Makefile."""
+
+    def __init__(self, variant: str | None = None):
+        v = variant or ref_variant()
+        if v is None:
+            raise FileNotFoundError("oracle/_ref was not built (make -C oracle ref)")
+        self.variant = v
+        self.lib = L = C.CDLL(str(REF_DIR / f"libqms_ref_{v}.so"))
+        vp, i64, i32 = C.c_void_p, C.c_int64, C.c_int
+        L.ref_set_threads.argtypes = [i32]
+        L.ref_get_threads.restype = i32
+        L.ref_set_exact.argtypes = [i32]
+        L.ref_moe.argtypes = [i32] * 7 + [vp] * 5 + [i32, vp, vp, vp]
+        L.ref_moe.restype = i32
+        L.qms_quantize_q8.argtypes = [vp, i64, vp]
+        L.qms_vec_dot_q8.argtypes = [i32, vp, vp, i64]
+        L.qms_vec_dot_q8.restype = C.c_float
+        L.qms_vec_dot_f32.argtypes = [vp, vp, i64]
+        L.qms_vec_dot_f32.restype = C.c_float
+        L.qms_dequant_row.argtypes = [i32, vp, vp, i64]
+        L.qms_dequant_row.restype = i32
+        L.qms_matmul.argtypes = [vp, vp, i32, vp]
+
+    def set_threads(self, n: int):
+        self.lib.ref_set_threads(int(n))
+
+    def threads(self) -> int:
+        return self.lib.ref_get_threads()
+
+    def quantize_q8(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty(x.size // 32, Q8_DTYPE)
+        self.lib.qms_quantize_q8(_p(x), x.size, _p(out))
+        return out
+
+    def vec_dot_q8(self, typ: int, w: np.ndarray, xq: np.ndarray, n: int) -> float:
+        return self.lib.qms_vec_dot_q8(typ, _p(np.ascontiguousarray(w)), _p(xq), n)
+
+    def vec_dot_f32(self, w: np.ndarray, x: np.ndarray) -> float:
+        w = np.ascontiguousarray(w, np.float32)
+        x = np.ascontiguousarray(x, np.float32)
+        return self.lib.qms_vec_dot_f32(_p(w), _p(x), x.size)
+
+    def dequant_row(self, typ: int, src: np.ndarray, n: int) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        if self.lib.qms_dequant_row(typ, _p(np.ascontiguousarray(src)), _p(out), n) != 0:
+            raise ValueError("unsupported type or size")
+        return out
+
+    def moe(self, layer, xn: np.ndarray, trace: bool = False):
+        """Returns out [T][E] (and the --trace expert list when trace=True)."""
+        E, X = layer.n_embd, layer.n_expert
+        xn = np.ascontiguousarray(xn, np.float32).reshape(-1, E)
+        T = xn.shape[0]
+        out = np.empty((T, E), np.float32)
+        tr = np.zeros(X, np.int32) if trace else None
+        ntr = C.c_int(0)
+        rc = self.lib.ref_moe(E, X, layer.n_used, layer.n_ff, layer.gate_type, layer.up_type,
+                              layer.down_type, layer.router.ctypes.data, layer.gate.ctypes.data,
+                              layer.up.ctypes.data, layer.down.ctypes.data, _p(xn), T, _p(out),
+                              _p(tr), C.byref(ntr) if trace else None)
+        if rc != 0:
+            raise RuntimeError(f"reference moe() returned {rc}")
+        return (out, tr[: ntr.value].copy()) if trace else out
+
+
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()

@@ -1,0 +1,73 @@
+"""The C-ABI library: it loads, exports every function include/*.h declares, and validates its
+arguments on the host before touching a device. CPU only (no compute calls)."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+import large_model_b200 as q
+
+
+def test_library_exports_every_declared_symbol():
+    L = q.lib()
+    names = q.declared_functions()
+    assert len(names) >= 12
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_q8_block_layout_matches_reference():
+    # QmsQ8 is 44 bytes: float d, float ds, int16 s16[2], int8 q[32] (src/kernels.h:7-12)
+    assert q.Q8_DTYPE.itemsize == 44
+    assert [q.Q8_DTYPE.fields[f][1] for f in ("d", "ds", "s16", "q")] == [0, 4, 8, 12]
+
+
+def _desc(**kw):
+    base = dict(n_embd=512, n_expert=32, n_used=4, n_ff=256, gate_type=q.T_Q4_0, up_type=q.T_Q4_0,
+                down_type=q.T_Q4_0, router=1, gate=1, up=1, down=1, src_on_device=0)
+    base.update(kw)
+    return q.MoeDesc(**base)
+
+
+def _create(d):
+    h = C.c_void_p()
+    rc = q.lib().qms_cuda_moe_create(C.byref(d), C.byref(h))
+    return rc, q.lib().qms_cuda_last_error().decode()
+
+
+def test_create_validates_shapes_before_any_device_call():
+    rc, msg = _create(_desc(n_embd=288))                 # not the integer fast path
+    assert rc == q.EUNSUPPORTED and "256" in msg
+    rc, msg = _create(_desc(n_ff=100))
+    assert rc == q.EUNSUPPORTED
+    rc, msg = _create(_desc(down_type=q.T_Q6_K))
+    assert rc == q.EUNSUPPORTED and "types" in msg
+    rc, msg = _create(_desc(n_used=40, n_expert=32))     # k > n_expert
+    assert rc == q.EINVAL
+    rc, msg = _create(_desc(router=None))
+    assert rc == q.EINVAL
+
+
+def test_kernel_calls_validate_arguments():
+    L = q.lib()
+    assert L.qms_cuda_quantize_q8(None, 32, 1, None, None) == q.EINVAL
+    assert L.qms_cuda_quantize_q8(C.c_void_p(16), 33, 1, C.c_void_p(16), None) == q.EINVAL
+    assert L.qms_cuda_matvec_q8(q.T_Q8_0, C.c_void_p(16), 4, 32, C.c_void_p(16), 1, C.c_void_p(16), None) == q.EUNSUPPORTED
+    assert L.qms_cuda_matvec_q8(q.T_Q6_K, C.c_void_p(16), 4, 32, C.c_void_p(16), 1, C.c_void_p(16), None) == q.EINVAL
+    assert L.qms_cuda_moe_forward(None, None, 1, None, None, None, None, None, None) == q.EINVAL
+
+
+def test_init_without_gpu_fails_loudly():
+    import torch
+    if torch.cuda.is_available():
+        return
+    rc = q.lib().qms_cuda_init(0)
+    assert rc == q.ENODEV
+    assert q.lib().qms_cuda_last_error()
+
+
+def test_declared_functions_cite_reference():
+    text = (q.HEADER).read_text()
+    for cite in ("src/kernels.h:15", "src/kernels.h:19", "src/kernels.h:21", "src/model.c:1032"):
+        assert cite in text

@@ -1,0 +1,173 @@
+"""MoE block parity on a B200: qms_cuda_moe_forward (C ABI) against the oracle / reference.
+
+Bars: identical selected expert ids in identical selection order, router
+logits bit-identical, renormalised weights within 2 float ulps, and the block output within
+1e-3 relative L2 of the reference's integer path (observed ~1e-6: only float summation order of
+the int8 dots differs). Shapes: the tiny config's block, Qwen3-30B-A3B and Qwen3-235B-A22B.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import cases
+from conftest import rel_l2
+from large_model_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+OUT_TOL = 1e-3          # relative L2 of the block output
+ULP_TOL = 2             # renormalised routing weights
+
+
+def _ulps(a, b):
+    a = np.asarray(a, np.float32).view(np.int32).astype(np.int64)
+    b = np.asarray(b, np.float32).view(np.int32).astype(np.int64)
+    return int(np.abs(a - b).max())
+
+
+def _run(cuda, layer, xn):
+    import torch
+    m = cuda.MoeLayer.from_synth(layer)
+    out, sel, w, logits = m.route(torch.from_numpy(xn).cuda())
+    torch.cuda.synchronize()
+    return m, out.cpu().numpy(), sel.cpu().numpy(), w.cpu().numpy(), logits.cpu().numpy()
+
+
+def _check(oracle, layer, xn, out, sel, w, logits, tag=""):
+    o_out, o_sel, o_w, o_logits = oracle.moe(layer, xn)
+    assert np.array_equal(logits.view(np.uint32), o_logits.view(np.uint32)), f"{tag} router logits differ"
+    assert np.array_equal(sel, o_sel), f"{tag} selected experts differ"
+    assert _ulps(w, o_w) <= ULP_TOL, f"{tag} weights differ by {_ulps(w, o_w)} ulps"
+    err = rel_l2(out, o_out)
+    assert err < OUT_TOL, f"{tag} rel L2 {err:.3e}"
+    return err
+
+
+@pytest.mark.parametrize("shape,T", [("tiny", 1), ("tiny", 4), ("tiny", 13), ("30b", 1), ("30b", 5),
+                                     ("235b", 1), ("235b", 3), ("235b", 9)])
+def test_moe_matches_oracle(cuda, oracle, shape, T):
+    layer = synth.make_moe_layer(shape, seed=31 + T)
+    xn = synth.make_hidden(layer.n_embd, T, seed=41 + T)
+    m, out, sel, w, logits = _run(cuda, layer, xn)
+    err = _check(oracle, layer, xn, out, sel, w, logits, f"{shape} T={T}")
+    assert err < 1e-5            # only summation order differs
+    m.close()
+
+
+def test_moe_golden_reference(cuda, golden):
+    """Against outputs produced by the reference's own moe() (tests/golden)."""
+    for name, (layer, xn) in cases.moe_cases().items():
+        m, out, sel, w, logits = _run(cuda, layer, xn)
+        assert rel_l2(out, golden[f"moe/{name}/out"]) < 1e-5, name
+        assert sorted(set(sel.ravel().tolist())) == golden[f"moe/{name}/trace"].tolist(), name
+        m.close()
+
+
+def test_moe_decode_sequence_235b(cuda, oracle):
+    """64 consecutive bs1 calls on one layer (scratch reuse, self-resetting counters)."""
+    import torch
+    layer = synth.make_moe_layer("235b", seed=5)
+    xn = synth.make_hidden(layer.n_embd, 64, seed=6)
+    m = cuda.MoeLayer.from_synth(layer)
+    xd = torch.from_numpy(xn).cuda()
+    outs, sels = [], []
+    for t in range(64):
+        o, s, _, _ = m.route(xd[t:t + 1])
+        outs.append(o)
+        sels.append(s)
+    out = torch.cat(outs).cpu().numpy()
+    sel = torch.cat(sels).cpu().numpy()
+    o_out, o_sel, _, _ = oracle.moe(layer, xn)
+    assert np.array_equal(sel, o_sel)
+    assert rel_l2(out, o_out) < 1e-5
+    m.close()
+
+
+def test_moe_edge_cases(cuda, oracle):
+    import torch
+    layer = synth.make_moe_layer("tiny", seed=3)
+    E = layer.n_embd
+    # all-zero input: every logit 0 -> ties -> experts 0..k-1, equal weights, zero output
+    xn = np.zeros((2, E), np.float32)
+    m, out, sel, w, logits = _run(cuda, layer, xn)
+    _check(oracle, layer, xn, out, sel, w, logits, "zeros")
+    assert sel.tolist() == [[0, 1, 2, 3]] * 2 and np.all(out == 0)
+    # zero 32-blocks inside a token (d == 0 blocks) and huge / tiny magnitudes
+    xn = synth.make_hidden(E, 3, seed=4)
+    xn[0, :64] = 0.0
+    xn[1] *= 1e4
+    xn[2] *= 1e-4
+    out, sel, w, logits = [a.cpu().numpy() for a in m.route(torch.from_numpy(xn).cuda())]
+    _check(oracle, layer, xn, out, sel, w, logits, "magnitudes")
+    # tied router rows: experts 5 and 2 identical -> lower index first
+    tied = synth.make_moe_layer("tiny", seed=3)
+    tied.router[5] = tied.router[2]
+    xt = synth.make_hidden(E, 16, seed=5)
+    m2, out, sel, w, logits = _run(cuda, tied, xt)
+    _check(oracle, tied, xt, out, sel, w, logits, "ties")
+    # empty batch
+    empty = torch.empty((0, E), dtype=torch.float32, device="cuda")
+    assert m.forward(empty).shape == (0, E)
+    m.close()
+    m2.close()
+
+
+def test_moe_host_entry_and_residual(cuda, oracle):
+    import torch
+    layer = synth.make_moe_layer("30b", seed=8)
+    xn = synth.make_hidden(layer.n_embd, 2, seed=9)
+    m = cuda.MoeLayer.from_synth(layer)
+    out_h, sel_h, w_h = m.forward_host(xn, with_routing=True)
+    o_out, o_sel, o_w, _ = oracle.moe(layer, xn)
+    assert np.array_equal(sel_h, o_sel)
+    assert rel_l2(out_h, o_out) < 1e-5
+    resid = torch.from_numpy(synth.make_hidden(layer.n_embd, 2, seed=10)).cuda()
+    xd = torch.from_numpy(xn).cuda()
+    plain = m.forward(xd)
+    fused = m.forward(xd, resid=resid)
+    torch.cuda.synchronize()
+    assert torch.equal(fused, resid + plain)           # h += moe(xn), src/model.c:1285
+    # in place: out aliases the residual
+    h = resid.clone()
+    m.forward(xd, out=h, resid=h)
+    assert torch.equal(h, fused)
+    m.close()
+
+
+def test_moe_deterministic_and_expert_permutation(cuda):
+    """Size-independent properties at the 235B shape: repeated calls are bit-identical, and
+    storing the experts in a different order (router rows permuted alike) changes only the
+    reported ids, not one bit of the output."""
+    import torch
+    layer = synth.make_moe_layer("235b", seed=12)
+    xn = torch.from_numpy(synth.make_hidden(layer.n_embd, 4, seed=13)).cuda()
+    m = cuda.MoeLayer.from_synth(layer)
+    a, sa, _, _ = m.route(xn)
+    b, sb, _, _ = m.route(xn)
+    assert torch.equal(a, b) and torch.equal(sa, sb)
+    X = layer.n_expert
+    perm = np.random.default_rng(1).permutation(X)
+    inv = np.argsort(perm)
+    per = lambda t: np.ascontiguousarray(t.reshape(X, -1)[perm]).reshape(-1)
+    pl = synth.MoeLayer(layer.n_embd, X, layer.n_used, layer.n_ff, np.ascontiguousarray(layer.router[perm]),
+                        per(layer.gate), per(layer.up), per(layer.down))
+    mp = cuda.MoeLayer.from_synth(pl)
+    c, sc, _, _ = mp.route(xn)
+    assert torch.equal(a, c)
+    assert np.array_equal(inv[sc.cpu().numpy()], sa.cpu().numpy())
+    m.close()
+    mp.close()
+
+
+def test_moe_device_source_matches_host_source(cuda):
+    """Creating from device-resident GGUF bytes gives the same layer as from host bytes."""
+    import torch
+    layer = synth.make_moe_layer("30b", seed=14)
+    dev = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (layer.router, layer.gate, layer.up, layer.down)]
+    md = cuda.MoeLayer(layer.n_embd, layer.n_expert, layer.n_used, layer.n_ff, *dev)
+    mh = cuda.MoeLayer.from_synth(layer)
+    xn = torch.from_numpy(synth.make_hidden(layer.n_embd, 3, seed=15)).cuda()
+    assert torch.equal(md.forward(xn), mh.forward(xn))
+    md.close()
+    mh.close()

@@ -181,6 +181,11 @@ class MoeLayer:
         if events is None:
             check(lib().qms_cuda_moe_set_kernel_events(self.h, None))
             return
+        torch = _torch()
+        for e in events:                      # torch creates the CUDA event on its first record
+            if not e.cuda_event:
+                e.record(torch.cuda.current_stream())
+        torch.cuda.current_stream().synchronize()
         arr = (C.c_void_p * 6)(*[C.c_void_p(e.cuda_event) for e in events])
         self._events = events
         check(lib().qms_cuda_moe_set_kernel_events(self.h, arr))

@@ -80,17 +80,17 @@ __global__ void k_repack_q4_0(const uint8_t *__restrict__ src, int64_t nrows, in
 }
 
 // ---- top-k of one token by a whole CTA (blockDim.x >= X, X <= 256) --------------------------
-// Selection order = rank of the logit, ties to the lower expert index: the reference's repeated
-// strict-'>' argmax over probabilities (src/model.c:1053-1062). exp(l - max) is strictly
-// increasing, so ranking the float logits gives the same order and the same tie-breaks.
-// prob = exp((double)l - max) / z as in src/model.c:1047-1050, with z summed as a tree (the
-// reference sums sequentially; the difference is ~1e-16 relative, below float resolution of
-// the final weights). Weights (float)(p_j / sum_j p_j), the sum taken in selection order.
+// The reference (src/model.c:1045-1064): prob[e] = exp((double)l_e - max) / z in double, then
+// top-k by repeated strict-'>' argmax over prob, so ties (including probabilities that
+// underflow to exactly 0) go to the lower expert index; weights (float)(p_j / sum_j p_j) with
+// the sum taken in selection order. Here each thread owns one expert: its rank (the number of
+// experts with a larger p, or an equal p and a lower index) is its position in the selection
+// order. z is summed as a tree (the reference sums sequentially); the difference is ~1e-16
+// relative, below the float resolution of the weights.
 __device__ void topk_token(const float *__restrict__ lg, int X, int K, int *__restrict__ sel, float *__restrict__ wts,
-                           float *sv, double *sred, double *spj) {
+                           double *sp, double *sred, double *spj) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const float v = tid < X ? __ldcg(lg + tid) : -INFINITY;
-    if (tid < X) sv[tid] = v;
     float mx = warp_max(v);
     if (lane == 0) sred[warp] = mx;
     __syncthreads();
@@ -105,13 +105,16 @@ __device__ void topk_token(const float *__restrict__ lg, int X, int K, int *__re
     __syncthreads();
     z = 0.0;
     for (int i = 0; i < nw; i++) z += sred[i];
+    const double p = ex / z;
+    if (tid < X) sp[tid] = p;
+    __syncthreads();
     if (tid < X) {
         int rank = 0;
-        for (int j = 0; j < tid; j++) rank += sv[j] >= v;
-        for (int j = tid + 1; j < X; j++) rank += sv[j] > v;
+        for (int j = 0; j < tid; j++) rank += sp[j] >= p;
+        for (int j = tid + 1; j < X; j++) rank += sp[j] > p;
         if (rank < K) {
             sel[rank] = tid;
-            spj[rank] = ex / z;
+            spj[rank] = p;
         }
     }
     __syncthreads();
@@ -171,19 +174,20 @@ __global__ void __launch_bounds__(256) k_moe_router(const float *__restrict__ W,
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int t = 0; t < T; t++) topk_token(logits + (size_t)t * X, X, K, sel + t * K, wts + t * K, srow, sred, spj);
+    double *sp = reinterpret_cast<double *>(smem4);   // X doubles; X <= E / 2 (checked at create)
+    for (int t = 0; t < T; t++) topk_token(logits + (size_t)t * X, X, K, sel + t * K, wts + t * K, sp, sred, spj);
     if (tid == 0) *cnt = 0;
 }
 
 __global__ void __launch_bounds__(256) k_moe_topk(const float *__restrict__ logits, int X, int K, int *__restrict__ sel,
                                                   float *__restrict__ wts) {
-    __shared__ float sv[256];
+    __shared__ double sp[256];
     __shared__ double sred[8];
     __shared__ double spj[64];
     pdl_trigger();
     pdl_wait();
     const int t = blockIdx.x;
-    topk_token(logits + (size_t)t * X, X, K, sel + t * K, wts + t * K, sv, sred, spj);
+    topk_token(logits + (size_t)t * X, X, K, sel + t * K, wts + t * K, sp, sred, spj);
 }
 
 // ---- gate/up + SwiGLU + Q8 re-quantisation ---------------------------------------------------
@@ -404,8 +408,8 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
     QMS_REQUIRE(d->gate_type == QMS_T_Q4_0 && d->up_type == QMS_T_Q4_0 && d->down_type == QMS_T_Q4_0,
                 QMS_CUDA_EUNSUPPORTED, "moe_create: expert types %d/%d/%d not supported (Q4_0)", d->gate_type,
                 d->up_type, d->down_type);
-    QMS_REQUIRE(E <= 4096 && F <= 2048 && X <= 256 && K <= 64, QMS_CUDA_EUNSUPPORTED,
-                "moe_create: n_embd <= 4096, n_ff <= 2048, n_expert <= 256, n_used <= 64 required");
+    QMS_REQUIRE(E <= 4096 && F <= 2048 && X <= 256 && K <= 64 && 2 * X <= E, QMS_CUDA_EUNSUPPORTED,
+                "moe_create: n_embd <= 4096, n_ff <= 2048, n_expert <= min(256, n_embd/2), n_used <= 64 required");
     int dev = 0;
     QMS_CK(cudaGetDevice(&dev));
     QmsCudaMoe *m = (QmsCudaMoe *)calloc(1, sizeof(QmsCudaMoe));

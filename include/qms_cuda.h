@@ -116,6 +116,23 @@ int qms_cuda_moe_set_kernel_events(QmsCudaMoe *m, void **events);
 int qms_cuda_moe_forward_host(QmsCudaMoe *m, const float *xn, int T, float *out, int *sel,
                               float *wts, float *logits);
 
+/* Routing that allocates nothing. It has no counterpart in the reference (the reference
+ * allocates freely on the host); it exists for callers that may not call cudaMalloc, such as
+ * code running under another framework's memory pool or allocator hooks, plugin hosts that
+ * forbid device allocation after start-up, or deployments that reserve all of HBM up front.
+ * Computes what qms_cuda_moe_forward reports as sel / wts / logits: router F32 [n_expert][n_embd]
+ * (16-byte aligned) against xn [T][n_embd]; sel [T][n_used] in selection order, wts [T][n_used],
+ * logits [T][n_expert] (optional, NULL to skip); all device pointers supplied by the caller.
+ * Its scratch lives in one fixed device array inside the library (384.25 KiB on every GPU that
+ * loads it, kept until exit): T <= 64, n_embd <= 4096 (multiple of 256), n_expert <= 256 and
+ * <= n_embd / 2, n_used <= min(n_expert, 64); larger sizes return QMS_CUDA_EINVAL with a message.
+ * The first call on each device looks up that array's device address, so make it before any
+ * stream capture. All calls share the one array: calls that overlap on the GPU (other streams,
+ * other host threads) race and must be serialised by the caller. */
+int qms_cuda_moe_route_noalloc(const float *router, int n_expert, int n_embd, int n_used,
+                               const float *xn, int T, int *sel, float *wts, float *logits,
+                               void *stream);
+
 #ifdef __cplusplus
 }
 #endif

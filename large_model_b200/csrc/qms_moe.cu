@@ -598,3 +598,79 @@ int qms_cuda_moe_forward_host(QmsCudaMoe *m, const float *xn, int T, float *out,
 }
 
 }  // extern "C"
+
+// ---- routing without allocation --------------------------------------------------------------
+// Some callers may not call cudaMalloc at all: code running inside another framework's memory
+// pool or allocator hooks, plugin hosts that forbid device allocation after start-up, and
+// deployments that pin every byte of HBM up front. qms_cuda_moe_route_noalloc serves them:
+// it runs the same router kernel (Q8 rows, exact-order logits, softmax/top-k) with its scratch
+// in the fixed array below instead of a layer handle's cudaMalloc'd scratch. The array holds
+// at most kNoAllocMaxT tokens of n_embd <= 4096 and n_expert <= 256 (384.25 KiB); every GPU
+// that loads the library keeps it until the process exits.
+namespace qms {
+
+constexpr int kNoAllocMaxT = 64;
+constexpr int kNoAllocMaxE = 4096;
+constexpr int kNoAllocMaxX = 256;
+constexpr size_t kNaXqQ = (size_t)kNoAllocMaxT * kNoAllocMaxE;              // int8 rows
+constexpr size_t kNaXqD = (size_t)kNoAllocMaxT * (kNoAllocMaxE / 32) * 4;   // block scales
+constexpr size_t kNaXqS = kNaXqD;                                           // block sums
+constexpr size_t kNaLogits = (size_t)kNoAllocMaxT * kNoAllocMaxX * 4;       // router logits
+constexpr size_t kNaCnt = 256;                                              // arrival counter
+constexpr size_t kNoAllocScratchBytes = kNaXqQ + kNaXqD + kNaXqS + kNaLogits + kNaCnt;
+
+static __device__ __align__(256) unsigned char g_route_scratch[kNoAllocScratchBytes];
+
+// Device address of g_route_scratch per device ordinal, looked up once with that device current.
+constexpr int kNoAllocMaxDevices = 64;
+static unsigned char *g_route_scratch_ptr[kNoAllocMaxDevices];
+
+static int route_scratch_ptr(int dev, unsigned char **out) {
+    QMS_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, QMS_CUDA_EINVAL, "moe_route_noalloc: device %d unsupported", dev);
+    unsigned char *p = __atomic_load_n(&g_route_scratch_ptr[dev], __ATOMIC_ACQUIRE);
+    if (!p) {
+        const cudaError_t e = cudaGetSymbolAddress((void **)&p, g_route_scratch);
+        if (e != cudaSuccess || !p) {
+            set_error("moe_route_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev, cudaGetErrorString(e));
+            return QMS_CUDA_ECUDA;
+        }
+        __atomic_store_n(&g_route_scratch_ptr[dev], p, __ATOMIC_RELEASE);
+    }
+    *out = p;
+    return QMS_CUDA_OK;
+}
+
+}  // namespace qms
+
+extern "C" int qms_cuda_moe_route_noalloc(const float *router, int n_expert, int n_embd, int n_used, const float *xn,
+                                          int T, int *sel, float *wts, float *logits, void *stream) {
+    const int X = n_expert, E = n_embd, K = n_used;
+    QMS_REQUIRE(router && xn && sel && wts && T >= 0, QMS_CUDA_EINVAL, "moe_route_noalloc: bad arguments");
+    QMS_REQUIRE(T <= kNoAllocMaxT, QMS_CUDA_EINVAL,
+                "moe_route_noalloc: T=%d exceeds the fixed scratch limit of %d tokens per call", T, kNoAllocMaxT);
+    QMS_REQUIRE(E > 0 && E % 256 == 0 && E <= kNoAllocMaxE, QMS_CUDA_EINVAL,
+                "moe_route_noalloc: n_embd=%d must be a multiple of 256 and at most %d", E, kNoAllocMaxE);
+    QMS_REQUIRE(X > 0 && X <= kNoAllocMaxX && 2 * X <= E && K > 0 && K <= X && K <= 64, QMS_CUDA_EINVAL,
+                "moe_route_noalloc: need 0 < n_used <= min(n_expert, 64) and n_expert <= min(%d, n_embd/2)",
+                kNoAllocMaxX);
+    QMS_REQUIRE(((uintptr_t)router & 15) == 0, QMS_CUDA_EINVAL, "moe_route_noalloc: router must be 16-byte aligned");
+    if (T == 0) return QMS_CUDA_OK;
+    int dev = -1;
+    QMS_CK(cudaGetDevice(&dev));
+    unsigned char *p = nullptr;
+    const int rc = route_scratch_ptr(dev, &p);
+    if (rc) return rc;
+    int8_t *xq_q = (int8_t *)p;
+    float *xq_d = (float *)(p + kNaXqQ);
+    int *xq_s = (int *)(p + kNaXqQ + kNaXqD);
+    float *lg = logits ? logits : (float *)(p + kNaXqQ + kNaXqD + kNaXqS);
+    int *cnt = (int *)(p + kNaXqQ + kNaXqD + kNaXqS + kNaLogits);
+    const cudaStream_t s = (cudaStream_t)stream;
+    QMS_CK(cudaMemsetAsync(cnt, 0, sizeof(int), s));   // the arrival counter must start at zero
+    const int topk_in_router = T <= kTopkInRouterMaxT;
+    k_moe_router<<<X, 256, (size_t)E * 4, s>>>(router, X, E, xn, T, K, xq_q, xq_d, xq_s, lg, sel, wts, cnt,
+                                               topk_in_router);
+    QMS_CK(cudaGetLastError());
+    if (!topk_in_router) QMS_CK(launch_pdl(k_moe_topk, dim3(T), dim3(256), 0, s, (const float *)lg, X, K, sel, wts));
+    return QMS_CUDA_OK;
+}

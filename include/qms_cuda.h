@@ -31,7 +31,8 @@ enum {
     QMS_CUDA_ECUDA = -2,        /* a CUDA runtime call failed */
     QMS_CUDA_ENOMEM = -3,       /* device allocation failed */
     QMS_CUDA_EUNSUPPORTED = -4, /* type/shape outside what the kernels implement */
-    QMS_CUDA_ENODEV = -5        /* no sm_100 device */
+    QMS_CUDA_ENODEV = -5,       /* no sm_100 device */
+    QMS_CUDA_ETIMEOUT = -6      /* a bounded wait inside a kernel gave up (see qms_cuda_moe_status) */
 };
 
 /* Activation block: 32 int8 values with one fp32 scale; same 44-byte layout as the
@@ -105,10 +106,18 @@ int qms_cuda_moe_reserve(QmsCudaMoe *m, int T);
 int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int *sel,
                          float *wts, float *logits, const float *resid, void *stream);
 
+/* Waits for the device and reports whether any bounded wait inside the layer's kernels gave up
+ * since the last call (QMS_CUDA_ETIMEOUT; the outputs of the affected call are invalid), then
+ * clears the flag. The batch-1 kernels never spin without a limit, so a stuck pipeline turns into
+ * this status instead of a hung GPU. No reference counterpart (the reference has no device). */
+int qms_cuda_moe_status(QmsCudaMoe *m);
+
 /* Kernel timing hook: with events non-NULL (an array of 6 cudaEvent_t), every following forward
- * records events[2i] before and events[2i+1] after its kernel i (0 router+top-k, 1 gate/up,
- * 2 down+combine) on the launch stream; this serialises the three kernels (no programmatic
- * overlap). NULL turns the hook off. */
+ * records events[2i] before and events[2i+1] after its stage i on the launch stream: stage 0 is
+ * routing (router + top-k), stage 1 the expert products (gate/up + SwiGLU + down + combine in one
+ * kernel for T == 1; gate/up alone otherwise) and stage 2 the separate down + combine kernel of
+ * T > 1 (empty for T == 1). The events serialise the kernels (no programmatic overlap). NULL turns
+ * the hook off. */
 int qms_cuda_moe_set_kernel_events(QmsCudaMoe *m, void **events);
 
 /* Same through host buffers (xn, out and the optional outputs in host memory): copies in,

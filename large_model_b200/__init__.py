@@ -24,7 +24,7 @@ LIB_PATH = PKG / "libqms_cuda.so"
 HEADER = PKG.parent / "include" / "qms_cuda.h"
 
 T_F32, T_F16, T_Q4_0, T_Q4_1, T_Q8_0, T_Q6_K = 0, 1, 2, 3, 8, 14
-OK, EINVAL, ECUDA, ENOMEM, EUNSUPPORTED, ENODEV = 0, -1, -2, -3, -4, -5
+OK, EINVAL, ECUDA, ENOMEM, EUNSUPPORTED, ENODEV, ETIMEOUT = 0, -1, -2, -3, -4, -5, -6
 
 Q8_DTYPE = np.dtype([("d", "<f4"), ("ds", "<f4"), ("s16", "<i2", (2,)), ("q", "i1", (32,))])
 
@@ -69,6 +69,7 @@ def lib() -> C.CDLL:
     L.qms_cuda_moe_forward.argtypes = [vp, vp, i32, vp, vp, vp, vp, vp, vp]
     L.qms_cuda_moe_forward_host.argtypes = [vp, vp, i32, vp, vp, vp, vp]
     L.qms_cuda_moe_set_kernel_events.argtypes = [vp, C.POINTER(vp)]
+    L.qms_cuda_moe_status.argtypes = [vp]
     _lib = L
     return L
 
@@ -171,6 +172,10 @@ class MoeLayer:
     @property
     def device_bytes(self) -> int:
         return lib().qms_cuda_moe_device_bytes(self.h)
+
+    def status(self):
+        """Raise if a bounded wait inside the layer's kernels gave up since the last check."""
+        check(lib().qms_cuda_moe_status(self.h))
 
     def reserve(self, T: int):
         check(lib().qms_cuda_moe_reserve(self.h, T))

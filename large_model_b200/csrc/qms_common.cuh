@@ -122,6 +122,26 @@ __device__ __forceinline__ Q8Lane quantize_lane(float x) {
     return r;
 }
 
+// ---- release / acquire atomics (gpu scope) -------------------------------------------------
+// A release add publishes every write this thread has made and, through a preceding barrier
+// (__syncwarp / __syncthreads), every write of the threads that took part in it; an acquire read
+// (or acq_rel add) makes those writes visible to the reader. No separate membar stalls the thread.
+__device__ __forceinline__ void red_add_release(int *p, int v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int atom_add_acq_rel(int *p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ int ld_acquire(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // ---- programmatic dependent launch ---------------------------------------------------------
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

@@ -1,7 +1,8 @@
-// qms_moe.cu - the Qwen3-MoE feed-forward block on B200 (sm_100a).
+// qms_moe.cu - the Qwen3-MoE feed-forward block on B200 (sm_100a): layer lifetime, the general
+// (any T) kernels and the host entry points.
 //
 // Reference: moe() in src/model.c:1032-1167 with moe_group_fast (src/model.c:969-1007).
-// One forward call is three kernels chained with programmatic dependent launch:
+// Batch-1 decode (T == 1) runs the streaming kernels of qms_moe_stream.cu. Other T run:
 //   k_moe_router   X CTAs: Q8 quantisation of xn (src/kernels.c:34-53), router logits in the
 //                  reference's exact F32 order (src/kernels.c:202-219); the last CTA to finish
 //                  does softmax / top-k / renormalisation (src/model.c:1045-1064) for T <= 4,
@@ -12,118 +13,41 @@
 //   k_moe_down     one CTA per (token, 8 output rows): down rows of all n_used experts
 //                  (phase 3, :998-1005), then the weighted sum in selection order with one
 //                  fused multiply-add per expert (:1152-1162), plus the optional residual.
-// Expert weights are repacked at load into 16-byte-aligned rows (qms_common.cuh) so each
-// Q4_0 block is one 128-bit load; gate row f and up row f of an expert are stored adjacently.
+// Expert weights are repacked at load into the staged chunk layout of qms_moe.cuh.
 #include <string.h>
 
 #include <algorithm>
 
-#include "qms_common.cuh"
+#include "qms_moe.cuh"
 #include "qms_router.cuh"
 
 using namespace qms;
 
-struct QmsCudaMoe {
-    int device;
-    int E, X, K, F, nbE, nbF;
-    int gate_type, up_type, down_type;
-    float *router;       // [X][E] F32
-    uint8_t *gu;         // [X][F][2] repacked rows of E (gate, up)
-    uint8_t *dn;         // [X][E] repacked rows of F
-    size_t gu_row, gu_expert, dn_row, dn_expert, weight_bytes;
-    // scratch, sized for cap_T tokens
-    int cap_T;
-    void *scratch;
-    size_t scratch_bytes;
-    int8_t *xq_q;
-    float *xq_d;
-    int *xq_s;
-    float *logits;
-    int *sel;
-    float *wts;
-    float *act;
-    int8_t *aq_q;
-    float *aq_d;
-    int *aq_s;
-    int *cnt;            // [0]: router arrivals; [1 + slot*nbF + g]: gate/up group arrivals
-    // host-buffer entry point
-    cudaStream_t hstream;
-    float *d_in, *d_out;
-    int io_cap_T;
-    // optional per-kernel timing events (qms_cuda_moe_set_kernel_events)
-    cudaEvent_t ev[6];
-    int timing;
-};
-
 namespace qms {
 
-constexpr int kTopkInRouterMaxT = 4;   // above this, k_moe_topk runs one CTA per token
 constexpr int kGateUpRows = 8;         // f values per gate/up CTA (one per warp)
 constexpr int kDownRows = 8;           // output rows per down CTA
 
-// ---- load-time repack (GGUF Q4_0 rows -> nibble plane + scale plane) -----------------------
-__global__ void k_repack_q4_0(const uint8_t *__restrict__ src, int64_t nrows, int nb, uint8_t *__restrict__ dst,
-                              size_t dst_stride, int row_mul, int row_add) {
+// ---- load-time repack: GGUF Q4_0 rows -> staged chunks -----------------------------------------
+// which = 0 / 1: gate / up rows of a stacked [X][F] tensor; which = 2: down rows of [X][E].
+__global__ void k_repack_q4_0(const uint8_t *__restrict__ src, int64_t nrows, int nb, int rows_per_expert,
+                              int which, Chunked c, uint8_t *__restrict__ dst, size_t expert_bytes) {
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= nrows * nb) return;
-    const int64_t r = idx / nb;
+    const int64_t R = idx / nb;
     const int b = (int)(idx % nb);
+    const int e = (int)(R / rows_per_expert), row = (int)(R % rows_per_expert);
     const uint16_t *s = reinterpret_cast<const uint16_t *>(src + idx * 18);
-    uint8_t *row = dst + (size_t)(r * row_mul + row_add) * dst_stride;
+    const size_t chunk = which == 2 ? dn_chunk(c, row, b) : gu_chunk(c, row, which, b);
+    const int rr = which == 2 ? (row & 7) : ((which * 32 + (row & 31)) & 7);
+    uint8_t *cp = dst + (size_t)e * expert_bytes + chunk * c.GB;
     uint4 v;
     v.x = (uint32_t)s[1] | ((uint32_t)s[2] << 16);
     v.y = (uint32_t)s[3] | ((uint32_t)s[4] << 16);
     v.z = (uint32_t)s[5] | ((uint32_t)s[6] << 16);
     v.w = (uint32_t)s[7] | ((uint32_t)s[8] << 16);
-    *reinterpret_cast<uint4 *>(row + (size_t)b * 16) = v;
-    *reinterpret_cast<uint16_t *>(row + (size_t)nb * 16 + (size_t)b * 2) = s[0];
-}
-
-// ---- top-k of one token by a whole CTA (blockDim.x >= X, X <= 256) --------------------------
-// The reference (src/model.c:1045-1064): prob[e] = exp((double)l_e - max) / z in double, then
-// top-k by repeated strict-'>' argmax over prob, so ties (including probabilities that
-// underflow to exactly 0) go to the lower expert index; weights (float)(p_j / sum_j p_j) with
-// the sum taken in selection order. Here each thread owns one expert: its rank (the number of
-// experts with a larger p, or an equal p and a lower index) is its position in the selection
-// order. z is summed as a tree (the reference sums sequentially); the difference is ~1e-16
-// relative, below the float resolution of the weights.
-__device__ void topk_token(const float *__restrict__ lg, int X, int K, int *__restrict__ sel, float *__restrict__ wts,
-                           double *sp, double *sred, double *spj) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const float v = tid < X ? __ldcg(lg + tid) : -INFINITY;
-    float mx = warp_max(v);
-    if (lane == 0) sred[warp] = mx;
-    __syncthreads();
-    mx = (float)sred[0];
-    for (int i = 1; i < nw; i++) mx = fmaxf(mx, (float)sred[i]);
-    const double ex = tid < X ? exp((double)v - (double)mx) : 0.0;
-    double z = ex;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-    __syncthreads();
-    if (lane == 0) sred[warp] = z;
-    __syncthreads();
-    z = 0.0;
-    for (int i = 0; i < nw; i++) z += sred[i];
-    const double p = ex / z;
-    if (tid < X) sp[tid] = p;
-    __syncthreads();
-    if (tid < X) {
-        int rank = 0;
-        for (int j = 0; j < tid; j++) rank += sp[j] >= p;
-        for (int j = tid + 1; j < X; j++) rank += sp[j] > p;
-        if (rank < K) {
-            sel[rank] = tid;
-            spj[rank] = p;
-        }
-    }
-    __syncthreads();
-    if (tid == 0) {
-        double ws = 0.0;
-        for (int j = 0; j < K; j++) ws += spj[j];
-        for (int j = 0; j < K; j++) wts[j] = (float)(spj[j] / ws);
-    }
-    __syncthreads();
+    *reinterpret_cast<uint4 *>(cp + chunk_nib_off(c.SB, rr, b % c.SB)) = v;
+    *reinterpret_cast<uint16_t *>(cp + chunk_scale_off(c.SB, rr, b % c.SB)) = s[0];
 }
 
 // ---- router: quantise xn, logits, (last CTA) top-k --------------------------------------------
@@ -134,8 +58,6 @@ __global__ void __launch_bounds__(256) k_moe_router(const float *__restrict__ W,
                                                     int *__restrict__ cnt, int do_topk) {
     extern __shared__ float4 smem4[];
     float *srow = reinterpret_cast<float *>(smem4);
-    __shared__ double sred[8];
-    __shared__ double spj[64];
     __shared__ int s_last;
     pdl_trigger();
     const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -174,25 +96,23 @@ __global__ void __launch_bounds__(256) k_moe_router(const float *__restrict__ W,
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    double *sp = reinterpret_cast<double *>(smem4);   // X doubles; X <= E / 2 (checked at create)
-    for (int t = 0; t < T; t++) topk_token(logits + (size_t)t * X, X, K, sel + t * K, wts + t * K, sp, sred, spj);
+    __shared__ int s_sel[64];
+    for (int t = 0; t < T; t++) topk_token(logits + (size_t)t * X, X, K, sel + t * K, wts + t * K, s_sel);
     if (tid == 0) *cnt = 0;
 }
 
 __global__ void __launch_bounds__(256) k_moe_topk(const float *__restrict__ logits, int X, int K, int *__restrict__ sel,
                                                   float *__restrict__ wts) {
-    __shared__ double sp[256];
-    __shared__ double sred[8];
-    __shared__ double spj[64];
+    __shared__ int s_sel[64];
     pdl_trigger();
     pdl_wait();
     const int t = blockIdx.x;
-    topk_token(logits + (size_t)t * X, X, K, sel + t * K, wts + t * K, sp, sred, spj);
+    topk_token(logits + (size_t)t * X, X, K, sel + t * K, wts + t * K, s_sel);
 }
 
-// ---- gate/up + SwiGLU + Q8 re-quantisation ---------------------------------------------------
+// ---- gate/up + SwiGLU + Q8 re-quantisation (any T) -------------------------------------------
 template <int NBL>
-__global__ void __launch_bounds__(256) k_moe_gate_up(const uint8_t *__restrict__ gu, size_t gu_expert, size_t gu_row,
+__global__ void __launch_bounds__(256) k_moe_gate_up(const uint8_t *__restrict__ gu, size_t gu_expert, Chunked c,
                                                      int nbE, int F, int K, const int8_t *__restrict__ xq_q,
                                                      const float *__restrict__ xq_d, const int *__restrict__ xq_s,
                                                      const int *__restrict__ sel, float *__restrict__ act,
@@ -204,18 +124,21 @@ __global__ void __launch_bounds__(256) k_moe_gate_up(const uint8_t *__restrict__
     const int slot = blockIdx.y, t = slot / K;
     pdl_wait();
     const int e = __ldcg(sel + slot);
-    const uint8_t *rg = gu + (size_t)e * gu_expert + (size_t)(2 * f) * gu_row;
-    const uint8_t *ru = rg + gu_row;
+    const uint8_t *ge = gu + (size_t)e * gu_expert;
+    const int rr = f & 7;
     uint4 ng[NBL], nu[NBL];
     uint16_t sg[NBL], su[NBL];
 #pragma unroll
     for (int i = 0; i < NBL; i++) {
         const int b = lane + 32 * i;
         if (b < nbE) {
-            ng[i] = ld_stream16(rg + (size_t)b * 16);
-            nu[i] = ld_stream16(ru + (size_t)b * 16);
-            sg[i] = ld_stream2(rg + (size_t)nbE * 16 + b * 2);
-            su[i] = ld_stream2(ru + (size_t)nbE * 16 + b * 2);
+            const uint8_t *cg = ge + gu_chunk(c, f, 0, b) * c.GB;
+            const uint8_t *cu = cg + 4 * (size_t)c.GB;          // up rows: chunks 4-7 of the stage
+            const int bl = b % c.SB;
+            ng[i] = ld_stream16(cg + chunk_nib_off(c.SB, rr, bl));
+            nu[i] = ld_stream16(cu + chunk_nib_off(c.SB, rr, bl));
+            sg[i] = ld_stream2(cg + chunk_scale_off(c.SB, rr, bl));
+            su[i] = ld_stream2(cu + chunk_scale_off(c.SB, rr, bl));
         }
     }
     const int8_t *xq = xq_q + (size_t)t * nbE * 32;
@@ -242,10 +165,10 @@ __global__ void __launch_bounds__(256) k_moe_gate_up(const uint8_t *__restrict__
     __syncthreads();
     pdl_trigger();
     const int nbF = F / 32, grp = f / 32;
-    int *c = gcnt + (size_t)slot * nbF + grp;
+    int *cn = gcnt + (size_t)slot * nbF + grp;
     if (threadIdx.x == 0) {
         __threadfence();
-        s_last = atomicAdd(c, kGateUpRows) == 32 - kGateUpRows;
+        s_last = atomicAdd(cn, kGateUpRows) == 32 - kGateUpRows;
     }
     __syncthreads();
     if (s_last && warp == 0) {
@@ -256,14 +179,14 @@ __global__ void __launch_bounds__(256) k_moe_gate_up(const uint8_t *__restrict__
         if (lane == 0) {
             aq_d[(size_t)slot * nbF + grp] = r.d;
             aq_s[(size_t)slot * nbF + grp] = r.sum;
-            *c = 0;
+            *cn = 0;
         }
     }
 }
 
-// ---- down + weighted combine (+ residual) ----------------------------------------------------
+// ---- down + weighted combine (+ residual), any T ----------------------------------------------
 template <int NBL>
-__global__ void __launch_bounds__(256) k_moe_down(const uint8_t *__restrict__ dn, size_t dn_expert, size_t dn_row,
+__global__ void __launch_bounds__(256) k_moe_down(const uint8_t *__restrict__ dn, size_t dn_expert, Chunked c,
                                                   int nbF, int E, int K, const int8_t *__restrict__ aq_q,
                                                   const float *__restrict__ aq_d, const int *__restrict__ aq_s,
                                                   const int *__restrict__ sel, const float *__restrict__ wts,
@@ -295,14 +218,17 @@ __global__ void __launch_bounds__(256) k_moe_down(const uint8_t *__restrict__ dn
             }
         }
         const int e = __ldcg(sel + slot);
-        const uint8_t *row = dn + (size_t)e * dn_expert + (size_t)(i0 + r) * dn_row;
+        const int row = i0 + r;
+        const uint8_t *de = dn + (size_t)e * dn_expert;
         float acc = 0.0f;
 #pragma unroll
         for (int i = 0; i < NBL; i++) {
             const int b = lane + 32 * i;
             if (b < nbF) {
-                const uint4 nib = ld_stream16(row + (size_t)b * 16);
-                const float dw = h2f(ld_stream2(row + (size_t)nbF * 16 + b * 2));
+                const uint8_t *ch = de + dn_chunk(c, row, b) * c.GB;
+                const int bl = b % c.SB;
+                const uint4 nib = ld_stream16(ch + chunk_nib_off(c.SB, row & 7, bl));
+                const float dw = h2f(ld_stream2(ch + chunk_scale_off(c.SB, row & 7, bl)));
                 acc = fmaf((float)(q4_block_isum(nib, xa0[i], xa1[i]) - xs8[i]), dw * xd[i], acc);
             }
         }
@@ -319,20 +245,13 @@ __global__ void __launch_bounds__(256) k_moe_down(const uint8_t *__restrict__ dn
     }
 }
 
-template <typename... P, typename... A>
-static cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A... args) {
-    cudaLaunchConfig_t cfg;
-    memset(&cfg, 0, sizeof cfg);
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, ((P)args)...);
+// Lane-major copy of the router for the batch-1 kernel: row e, element 16*i + k at [e][k][i].
+__global__ void k_router_lane_major(const float *__restrict__ W, int X, int E, float *__restrict__ Wlm) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)X * E) return;
+    const int64_t e = idx / E;
+    const int j = (int)(idx % E), L = E / 16;
+    Wlm[e * E + (int64_t)(j & 15) * L + (j >> 4)] = W[idx];
 }
 
 static size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -344,8 +263,8 @@ static int ensure_device(int dev) {
     return QMS_CUDA_OK;
 }
 
-static int upload_q4_0(const void *src, int on_device, int64_t nrows, int nb, uint8_t *dst, size_t stride, int mul,
-                       int add) {
+static int upload_q4_0(const void *src, int on_device, int64_t nrows, int nb, int rows_per_expert, int which,
+                       Chunked c, uint8_t *dst, size_t expert_bytes) {
     const size_t bytes = (size_t)nrows * nb * 18;
     const uint8_t *dsrc = (const uint8_t *)src;
     uint8_t *tmp = nullptr;
@@ -364,7 +283,8 @@ static int upload_q4_0(const void *src, int on_device, int64_t nrows, int nb, ui
         dsrc = tmp;
     }
     const int64_t n = nrows * nb;
-    k_repack_q4_0<<<(unsigned)((n + 255) / 256), 256>>>(dsrc, nrows, nb, dst, stride, mul, add);
+    k_repack_q4_0<<<(unsigned)((n + 255) / 256), 256>>>(dsrc, nrows, nb, rows_per_expert, which, c, dst,
+                                                        expert_bytes);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (tmp) cudaFree(tmp);
@@ -385,6 +305,7 @@ void qms_cuda_moe_destroy(QmsCudaMoe *m) {
     cudaGetDevice(&cur);
     cudaSetDevice(m->device);
     cudaFree(m->router);
+    cudaFree(m->router_lm);
     cudaFree(m->gu);
     cudaFree(m->dn);
     cudaFree(m->scratch);
@@ -405,6 +326,8 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
     // the reference's integer fast path condition (src/model.c:1090-1093)
     QMS_REQUIRE(E % 256 == 0 && F % 32 == 0, QMS_CUDA_EUNSUPPORTED,
                 "moe_create: n_embd %% 256 and n_ff %% 32 must be 0 (integer fast path)");
+    QMS_REQUIRE(F % 256 == 0, QMS_CUDA_EUNSUPPORTED,
+                "moe_create: n_ff %% 256 must be 0 (staged expert layout; all Qwen3-MoE shapes qualify)");
     QMS_REQUIRE(d->gate_type == QMS_T_Q4_0 && d->up_type == QMS_T_Q4_0 && d->down_type == QMS_T_Q4_0,
                 QMS_CUDA_EUNSUPPORTED, "moe_create: expert types %d/%d/%d not supported (Q4_0)", d->gate_type,
                 d->up_type, d->down_type);
@@ -415,35 +338,43 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
     QmsCudaMoe *m = (QmsCudaMoe *)calloc(1, sizeof(QmsCudaMoe));
     QMS_REQUIRE(m, QMS_CUDA_ENOMEM, "moe_create: out of host memory");
     m->device = dev;
+    if (cudaDeviceGetAttribute(&m->nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) m->nsm = 148;
     m->E = E; m->X = X; m->K = K; m->F = F;
     m->nbE = E / 32; m->nbF = F / 32;
     m->gate_type = d->gate_type; m->up_type = d->up_type; m->down_type = d->down_type;
-    m->gu_row = q4_row_stride(m->nbE);
-    m->gu_expert = m->gu_row * 2 * (size_t)F;
-    m->dn_row = q4_row_stride(m->nbF);
-    m->dn_expert = m->dn_row * (size_t)E;
+    m->cgu = make_chunked(m->nbE);
+    m->cdn = make_chunked(m->nbF);
+    m->gu_expert = (size_t)2 * F * m->nbE * 18;
+    m->dn_expert = (size_t)E * m->nbF * 18;
     const size_t rb = (size_t)X * E * 4, gb = m->gu_expert * X, db = m->dn_expert * X;
     m->weight_bytes = rb + gb + db;
-    if (cudaMalloc(&m->router, rb) != cudaSuccess || cudaMalloc(&m->gu, gb) != cudaSuccess ||
-        cudaMalloc(&m->dn, db) != cudaSuccess) {
+    if (cudaMalloc(&m->router, rb) != cudaSuccess || cudaMalloc(&m->router_lm, rb) != cudaSuccess ||
+        cudaMalloc(&m->gu, gb) != cudaSuccess || cudaMalloc(&m->dn, db) != cudaSuccess) {
         cudaGetLastError();
         qms_cuda_moe_destroy(m);
         set_error("moe_create: cannot allocate %.2f GB of weights", (rb + gb + db) / 1e9);
         return QMS_CUDA_ENOMEM;
     }
     int rc = QMS_CUDA_OK;
-    if (cudaMemset(m->gu, 0, gb) != cudaSuccess || cudaMemset(m->dn, 0, db) != cudaSuccess ||
-        cudaMemcpy(m->router, d->router, rb, d->src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice) !=
-            cudaSuccess) {
+    if (cudaMemcpy(m->router, d->router, rb, d->src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice) !=
+        cudaSuccess) {
         set_error("moe_create: %s", cudaGetErrorString(cudaGetLastError()));
         rc = QMS_CUDA_ECUDA;
     }
+    if (rc == QMS_CUDA_OK) {
+        k_router_lane_major<<<(unsigned)(((int64_t)X * E + 255) / 256), 256>>>(m->router, X, E, m->router_lm);
+        if (cudaGetLastError() != cudaSuccess) {
+            set_error("moe_create: router layout kernel failed");
+            rc = QMS_CUDA_ECUDA;
+        }
+    }
     if (rc == QMS_CUDA_OK)
-        rc = upload_q4_0(d->gate, d->src_on_device, (int64_t)X * F, m->nbE, m->gu, m->gu_row, 2, 0);
+        rc = upload_q4_0(d->gate, d->src_on_device, (int64_t)X * F, m->nbE, F, 0, m->cgu, m->gu, m->gu_expert);
     if (rc == QMS_CUDA_OK)
-        rc = upload_q4_0(d->up, d->src_on_device, (int64_t)X * F, m->nbE, m->gu, m->gu_row, 2, 1);
+        rc = upload_q4_0(d->up, d->src_on_device, (int64_t)X * F, m->nbE, F, 1, m->cgu, m->gu, m->gu_expert);
     if (rc == QMS_CUDA_OK)
-        rc = upload_q4_0(d->down, d->src_on_device, (int64_t)X * E, m->nbF, m->dn, m->dn_row, 1, 0);
+        rc = upload_q4_0(d->down, d->src_on_device, (int64_t)X * E, m->nbF, E, 2, m->cdn, m->dn, m->dn_expert);
+    if (rc == QMS_CUDA_OK) rc = stream_prepare(m);
     if (rc != QMS_CUDA_OK) {
         qms_cuda_moe_destroy(m);
         return rc;
@@ -476,6 +407,13 @@ int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
     const size_t o_aq_d = off; off += al256(TK * m->nbF * 4);
     const size_t o_aq_s = off; off += al256(TK * m->nbF * 4);
     const size_t o_cnt = off; off += al256((1 + TK * m->nbF) * 4);
+    const size_t o_err = off; off += 256;
+    size_t pg = 0, pd = 0, cg = 0, cd = 0;
+    stream_scratch_sizes(m, &pg, &pd, &cg, &cd);
+    const size_t o_pgu = off; off += al256(pg);
+    const size_t o_pdn = off; off += al256(pd);
+    const size_t o_cgu = off; off += al256(cg);
+    const size_t o_cdn = off; off += al256(cd);
     void *p = nullptr;
     if (cudaMalloc(&p, off) != cudaSuccess) {
         cudaGetLastError();
@@ -502,6 +440,11 @@ int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
     m->aq_d = (float *)(b + o_aq_d);
     m->aq_s = (int *)(b + o_aq_s);
     m->cnt = (int *)(b + o_cnt);
+    m->err = (int *)(b + o_err);
+    m->part_gu = (float *)(b + o_pgu);
+    m->part_dn = (float *)(b + o_pdn);
+    m->tcnt_gu = (int *)(b + o_cgu);
+    m->tcnt_dn = (int *)(b + o_cdn);
     m->cap_T = T;
     return QMS_CUDA_OK;
 }
@@ -521,34 +464,40 @@ int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int 
         if ((rc = qms_cuda_moe_reserve(m, T))) return rc;
     }
     const cudaStream_t s = (cudaStream_t)stream;
-    const int topk_in_router = T <= kTopkInRouterMaxT;
-    const size_t rsmem = (size_t)m->E * 4;
-    if (m->timing) QMS_CK(cudaEventRecord(m->ev[0], s));
-    k_moe_router<<<m->X, 256, rsmem, s>>>(m->router, m->X, m->E, xn, T, m->K, m->xq_q, m->xq_d, m->xq_s, m->logits,
-                                         m->sel, m->wts, m->cnt, topk_in_router);
-    QMS_CK(cudaGetLastError());
-    if (!topk_in_router)
-        QMS_CK(launch_pdl(k_moe_topk, dim3(T), dim3(256), 0, s, (const float *)m->logits, m->X, m->K, m->sel, m->wts));
-    if (m->timing) {
-        QMS_CK(cudaEventRecord(m->ev[1], s));
-        QMS_CK(cudaEventRecord(m->ev[2], s));
+    if (T == 1 && m->stream_ok && ((uintptr_t)xn & 15) == 0) {
+        if ((rc = stream_forward_bs1(m, xn, out, resid, s))) return rc;
+    } else {
+        const int topk_in_router = T <= kTopkInRouterMaxT;
+        const size_t rsmem = (size_t)m->E * 4;
+        if (m->timing) QMS_CK(cudaEventRecord(m->ev[0], s));
+        k_moe_router<<<m->X, 256, rsmem, s>>>(m->router, m->X, m->E, xn, T, m->K, m->xq_q, m->xq_d, m->xq_s,
+                                             m->logits, m->sel, m->wts, m->cnt, topk_in_router);
+        QMS_CK(cudaGetLastError());
+        if (!topk_in_router)
+            QMS_CK(launch_pdl(k_moe_topk, dim3(T), dim3(256), 0, s, (const float *)m->logits, m->X, m->K, m->sel,
+                              m->wts));
+        if (m->timing) {
+            QMS_CK(cudaEventRecord(m->ev[1], s));
+            QMS_CK(cudaEventRecord(m->ev[2], s));
+        }
+        const dim3 ggrid(m->F / kGateUpRows, T * m->K);
+        const int nbl = (m->nbE + 31) / 32;
+        auto gk = nbl == 1 ? k_moe_gate_up<1> : nbl == 2 ? k_moe_gate_up<2> : nbl == 3 ? k_moe_gate_up<3>
+                                                                                         : k_moe_gate_up<4>;
+        QMS_CK(launch_pdl(gk, ggrid, dim3(256), 0, s, (const uint8_t *)m->gu, m->gu_expert, m->cgu, m->nbE, m->F,
+                          m->K, (const int8_t *)m->xq_q, (const float *)m->xq_d, (const int *)m->xq_s,
+                          (const int *)m->sel, m->act, m->aq_q, m->aq_d, m->aq_s, m->cnt + 1));
+        if (m->timing) {
+            QMS_CK(cudaEventRecord(m->ev[3], s));
+            QMS_CK(cudaEventRecord(m->ev[4], s));
+        }
+        const dim3 dgrid(m->E / kDownRows, T);
+        auto dk = m->nbF <= 32 ? k_moe_down<1> : k_moe_down<2>;
+        QMS_CK(launch_pdl(dk, dgrid, dim3(256), (size_t)m->K * kDownRows * 4, s, (const uint8_t *)m->dn,
+                          m->dn_expert, m->cdn, m->nbF, m->E, m->K, (const int8_t *)m->aq_q, (const float *)m->aq_d,
+                          (const int *)m->aq_s, (const int *)m->sel, (const float *)m->wts, resid, out));
+        if (m->timing) QMS_CK(cudaEventRecord(m->ev[5], s));
     }
-    const dim3 ggrid(m->F / kGateUpRows, T * m->K);
-    const int nbl = (m->nbE + 31) / 32;
-    auto gk = nbl == 1 ? k_moe_gate_up<1> : nbl == 2 ? k_moe_gate_up<2> : nbl == 3 ? k_moe_gate_up<3> : k_moe_gate_up<4>;
-    QMS_CK(launch_pdl(gk, ggrid, dim3(256), 0, s, (const uint8_t *)m->gu, m->gu_expert, m->gu_row, m->nbE, m->F, m->K,
-                      (const int8_t *)m->xq_q, (const float *)m->xq_d, (const int *)m->xq_s, (const int *)m->sel,
-                      m->act, m->aq_q, m->aq_d, m->aq_s, m->cnt + 1));
-    if (m->timing) {
-        QMS_CK(cudaEventRecord(m->ev[3], s));
-        QMS_CK(cudaEventRecord(m->ev[4], s));
-    }
-    const dim3 dgrid(m->E / kDownRows, T);
-    auto dk = m->nbF <= 32 ? k_moe_down<1> : k_moe_down<2>;
-    QMS_CK(launch_pdl(dk, dgrid, dim3(256), (size_t)m->K * kDownRows * 4, s, (const uint8_t *)m->dn, m->dn_expert,
-                      m->dn_row, m->nbF, m->E, m->K, (const int8_t *)m->aq_q, (const float *)m->aq_d,
-                      (const int *)m->aq_s, (const int *)m->sel, (const float *)m->wts, resid, out));
-    if (m->timing) QMS_CK(cudaEventRecord(m->ev[5], s));
     const size_t TK = (size_t)T * m->K;
     if (sel) QMS_CK(cudaMemcpyAsync(sel, m->sel, TK * 4, cudaMemcpyDeviceToDevice, s));
     if (wts) QMS_CK(cudaMemcpyAsync(wts, m->wts, TK * 4, cudaMemcpyDeviceToDevice, s));
@@ -560,6 +509,22 @@ int qms_cuda_moe_set_kernel_events(QmsCudaMoe *m, void **events) {
     QMS_REQUIRE(m, QMS_CUDA_EINVAL, "moe_set_kernel_events: NULL layer");
     m->timing = events != nullptr;
     for (int i = 0; i < 6; i++) m->ev[i] = events ? (cudaEvent_t)events[i] : nullptr;
+    return QMS_CUDA_OK;
+}
+
+int qms_cuda_moe_status(QmsCudaMoe *m) {
+    QMS_REQUIRE(m, QMS_CUDA_EINVAL, "moe_status: NULL layer");
+    if (!m->err) return QMS_CUDA_OK;
+    int rc = ensure_device(m->device);
+    if (rc) return rc;
+    int flags = 0;
+    QMS_CK(cudaMemcpy(&flags, m->err, sizeof flags, cudaMemcpyDeviceToHost));
+    if (flags) {
+        QMS_CK(cudaMemset(m->err, 0, sizeof(int)));
+        set_error("moe: a bounded wait inside the decode kernels gave up (flags 0x%x); outputs of that call are "
+                  "invalid", flags);
+        return QMS_CUDA_ETIMEOUT;
+    }
     return QMS_CUDA_OK;
 }
 

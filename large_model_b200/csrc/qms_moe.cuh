@@ -1,0 +1,200 @@
+// qms_moe.cuh - internal declarations shared by the MoE sources (not part of the C ABI).
+#pragma once
+
+#include <string.h>
+
+#include "qms_common.cuh"
+
+namespace qms {
+
+// ---- staged Q4_0 expert layout ---------------------------------------------------------------
+// Expert rows are repacked at load into "chunks" of 8 rows x SB blocks (SB = 16 or 8):
+//   [8 rows][SB blocks][16 bytes]  nibble planes (block b of row rr at (rr*SB + b)*16)
+//   [8 rows][SB blocks][2 bytes]   fp16 scales
+// so a chunk is 8*SB*18 bytes, the same bytes as the 8*SB ggml blocks it holds.
+//   gate/up of one expert: tiles of 32 f-values; a tile is nb/SB stages; a stage is 8 chunks:
+//     chunks 0-3 hold gate rows f0..f0+31, chunks 4-7 the up rows of the same f (row r of the
+//     tile = 8*chunk + rr; r < 32 gate row f0+r, r >= 32 up row f0+r-32).
+//   down of one expert: row-blocks of 8 output rows; a row-block is nb/SB consecutive chunks.
+// One pipeline stage of the decode kernels is 8 chunks, i.e. one contiguous bulk copy for gate/up
+// and eight chunk copies (one per selected expert) for down.
+struct Chunked {
+    int SB;        // blocks per chunk row
+    int S;         // chunks along one row (nb / SB)
+    uint32_t GB;   // chunk bytes
+};
+
+__host__ __device__ inline Chunked make_chunked(int nb) {
+    Chunked c;
+    c.SB = nb % 16 == 0 ? 16 : 8;
+    c.S = nb / c.SB;
+    c.GB = (uint32_t)(8 * c.SB * 18);
+    return c;
+}
+
+// chunk index of (gate/up row pair f, which) at block b, within one expert
+__host__ __device__ inline size_t gu_chunk(const Chunked &c, int f, int which, int b) {
+    const int t = f >> 5, r = which * 32 + (f & 31);
+    return ((size_t)t * c.S + b / c.SB) * 8 + (r >> 3);
+}
+
+// chunk index of down row i at block b, within one expert
+__host__ __device__ inline size_t dn_chunk(const Chunked &c, int i, int b) {
+    return (size_t)(i >> 3) * c.S + b / c.SB;
+}
+
+__host__ __device__ inline uint32_t chunk_nib_off(int SB, int rr, int bl) { return (uint32_t)(rr * SB + bl) * 16; }
+__host__ __device__ inline uint32_t chunk_scale_off(int SB, int rr, int bl) {
+    return (uint32_t)(8 * SB * 16 + (rr * SB + bl) * 2);
+}
+
+constexpr int kTopkInRouterMaxT = 4;   // above this, k_moe_topk runs one CTA per token
+
+// ---- top-k of one token by a whole CTA (blockDim.x >= X, X <= 256) --------------------------
+// The reference (src/model.c:1045-1064): prob[e] = exp((double)l_e - max) / z in double, then
+// top-k by repeated strict-'>' argmax over prob, so ties (including probabilities that
+// underflow to exactly 0) go to the lower expert index; weights (float)(p_j / sum_j p_j) with
+// the sum taken in selection order. exp(l - max) / z is non-decreasing in l, so ranking the float
+// logits (ties to the lower index) gives the same selection and order whenever the double
+// probabilities of the top k+1 candidates are strictly decreasing; that is checked, and only if
+// two of them tie does every thread fall back to ranking the doubles themselves. z is summed as a
+// tree (the reference sums sequentially); the difference is ~1e-16 relative, below the float
+// resolution of the weights. Writes sel[0..K) and wts[0..K); s_sel receives sel as well.
+__device__ inline void topk_token(const float *__restrict__ lg, int X, int K, int *__restrict__ sel,
+                                  float *__restrict__ wts, int *s_sel) {
+    __shared__ double t_p[256];
+    __shared__ __align__(16) float t_v[256];
+    __shared__ double t_red[8];
+    __shared__ double t_pj[64];
+    __shared__ int t_cand[65];
+    __shared__ int t_tie;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const float v = tid < X ? __ldcg(lg + tid) : -INFINITY;
+    if (tid < X) t_v[tid] = v;
+    if (tid == 0) t_tie = 0;
+    float mx = warp_max(v);
+    if (lane == 0) t_red[warp] = mx;
+    __syncthreads();
+    mx = (float)t_red[0];
+    for (int i = 1; i < nw; i++) mx = fmaxf(mx, (float)t_red[i]);
+    const double ex = tid < X ? exp((double)v - (double)mx) : 0.0;
+    double z = ex;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+    __syncthreads();
+    if (lane == 0) t_red[warp] = z;
+    __syncthreads();
+    z = 0.0;
+    for (int i = 0; i < nw; i++) z += t_red[i];
+    const double p = ex / z;
+    if (tid < X) {
+        t_p[tid] = p;
+        int r0 = 0, r1 = 0, r2 = 0, r3 = 0;               // float rank, ties to the lower index
+        const float4 *v4 = reinterpret_cast<const float4 *>(t_v);
+        int j = 0;
+        for (; j + 4 <= X; j += 4) {
+            const float4 u = v4[j >> 2];
+            r0 += (u.x > v) | ((u.x == v) & (j + 0 < tid));
+            r1 += (u.y > v) | ((u.y == v) & (j + 1 < tid));
+            r2 += (u.z > v) | ((u.z == v) & (j + 2 < tid));
+            r3 += (u.w > v) | ((u.w == v) & (j + 3 < tid));
+        }
+        for (; j < X; j++) r0 += (t_v[j] > v) | ((t_v[j] == v) & (j < tid));
+        const int rank = r0 + r1 + r2 + r3;
+        if (rank <= K) t_cand[rank] = tid;
+    }
+    __syncthreads();
+    const int nchk = K < X ? K : K - 1;                   // pairs (r, r+1) that decide the selection
+    if (tid < nchk && !(t_p[t_cand[tid]] > t_p[t_cand[tid + 1]])) t_tie = 1;
+    __syncthreads();
+    if (!t_tie) {
+        if (tid < K) {
+            const int e = t_cand[tid];
+            sel[tid] = e;
+            s_sel[tid] = e;
+            t_pj[tid] = t_p[e];
+        }
+    } else if (tid < X) {                                 // exact ranking of the doubles
+        int rank = 0;
+        for (int j = 0; j < tid; j++) rank += t_p[j] >= p;
+        for (int j = tid + 1; j < X; j++) rank += t_p[j] > p;
+        if (rank < K) {
+            sel[rank] = tid;
+            s_sel[rank] = tid;
+            t_pj[rank] = p;
+        }
+    }
+    __syncthreads();
+    if (tid < K) {                                        // every thread sums in selection order
+        double ws = 0.0;
+        for (int j = 0; j < K; j++) ws += t_pj[j];
+        wts[tid] = (float)(t_pj[tid] / ws);
+    }
+    __syncthreads();
+}
+
+}  // namespace qms
+
+struct QmsCudaMoe {
+    int device, nsm;
+    int E, X, K, F, nbE, nbF;
+    int gate_type, up_type, down_type;
+    qms::Chunked cgu, cdn;
+    float *router;       // [X][E] F32
+    float *router_lm;    // [X][16][E/16]: element 16*i + k of a row at [k][i] (lane-major, batch-1 router)
+    uint8_t *gu;         // [X] experts of staged gate/up chunks
+    uint8_t *dn;         // [X] experts of staged down chunks
+    size_t gu_expert, dn_expert, weight_bytes;
+    int stream_ok;       // batch-1 streaming kernels usable for this shape
+    // scratch, sized for cap_T tokens
+    int cap_T;
+    void *scratch;
+    size_t scratch_bytes;
+    int8_t *xq_q;
+    float *xq_d;
+    int *xq_s;
+    float *logits;
+    int *sel;
+    float *wts;
+    float *act;
+    int8_t *aq_q;
+    float *aq_d;
+    int *aq_s;
+    int *cnt;            // [0]: router arrivals; [1 + slot*nbF + g]: gate/up group arrivals
+    int *err;            // device error flags (bounded waits that gave up)
+    float *part_gu, *part_dn;   // [tile][4 segments][64] partial row sums of tiles split across CTAs
+    int *tcnt_gu, *tcnt_dn;     // per-tile segment arrivals
+    int gu_nst, dn_nst;         // ring depth (stages) of the batch-1 kernels
+    // host-buffer entry point
+    cudaStream_t hstream;
+    float *d_in, *d_out;
+    int io_cap_T;
+    // optional per-kernel timing events (qms_cuda_moe_set_kernel_events)
+    cudaEvent_t ev[6];
+    int timing;
+};
+
+namespace qms {
+
+template <typename... P, typename... A>
+static cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A... args) {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, ((P)args)...);
+}
+
+// batch-1 decode kernels (qms_moe_stream.cu)
+int stream_prepare(QmsCudaMoe *m);     // shape check + kernel attributes; sets m->stream_ok
+int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *resid, cudaStream_t s);
+int stream_scratch_sizes(const QmsCudaMoe *m, size_t *part_gu, size_t *part_dn, size_t *cnt_gu, size_t *cnt_dn);
+
+}  // namespace qms

@@ -142,6 +142,21 @@ __device__ __forceinline__ int ld_acquire(const int *p) {
     return v;
 }
 
+// ---- flagged words ----------------------------------------------------------------------------
+// A 64-bit word holding 32 data bits and a 32-bit call stamp, written and read with single-copy
+// atomic 64-bit accesses: a reader that sees the current stamp sees the data written with it, so
+// producers publish with a plain store (no fence, no counter) and consumers poll the data itself.
+__device__ __forceinline__ void st_flagged(unsigned long long *p, uint32_t data, uint32_t stamp) {
+    const unsigned long long v = ((unsigned long long)stamp << 32) | data;
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_flagged(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // ---- programmatic dependent launch ---------------------------------------------------------
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

@@ -408,12 +408,12 @@ int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
     const size_t o_aq_s = off; off += al256(TK * m->nbF * 4);
     const size_t o_cnt = off; off += al256((1 + TK * m->nbF) * 4);
     const size_t o_err = off; off += 256;
-    size_t pg = 0, pd = 0, cg = 0, cd = 0;
-    stream_scratch_sizes(m, &pg, &pd, &cg, &cd);
+    size_t pg = 0, pd = 0, af = 0;
+    stream_scratch_sizes(m, &pg, &pd, &af);
     const size_t o_pgu = off; off += al256(pg);
     const size_t o_pdn = off; off += al256(pd);
-    const size_t o_cgu = off; off += al256(cg);
-    const size_t o_cdn = off; off += al256(cd);
+    const size_t o_aqf = off; off += al256(af);
+    const size_t o_stamp = off; off += 256;
     void *p = nullptr;
     if (cudaMalloc(&p, off) != cudaSuccess) {
         cudaGetLastError();
@@ -441,10 +441,10 @@ int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
     m->aq_s = (int *)(b + o_aq_s);
     m->cnt = (int *)(b + o_cnt);
     m->err = (int *)(b + o_err);
-    m->part_gu = (float *)(b + o_pgu);
-    m->part_dn = (float *)(b + o_pdn);
-    m->tcnt_gu = (int *)(b + o_cgu);
-    m->tcnt_dn = (int *)(b + o_cdn);
+    m->part_gu = (unsigned long long *)(b + o_pgu);
+    m->part_dn = (unsigned long long *)(b + o_pdn);
+    m->aq_flagged = (unsigned long long *)(b + o_aqf);
+    m->stamp = (unsigned *)(b + o_stamp);
     m->cap_T = T;
     return QMS_CUDA_OK;
 }

@@ -92,6 +92,7 @@ __device__ inline void topk_token(const float *__restrict__ lg, int X, int K, in
         int r0 = 0, r1 = 0, r2 = 0, r3 = 0;               // float rank, ties to the lower index
         const float4 *v4 = reinterpret_cast<const float4 *>(t_v);
         int j = 0;
+#pragma unroll 8
         for (; j + 4 <= X; j += 4) {
             const float4 u = v4[j >> 2];
             r0 += (u.x > v) | ((u.x == v) & (j + 0 < tid));
@@ -162,8 +163,10 @@ struct QmsCudaMoe {
     int *aq_s;
     int *cnt;            // [0]: router arrivals; [1 + slot*nbF + g]: gate/up group arrivals
     int *err;            // device error flags (bounded waits that gave up)
-    float *part_gu, *part_dn;   // [tile][4 segments][64] partial row sums of tiles split across CTAs
-    int *tcnt_gu, *tcnt_dn;     // per-tile segment arrivals
+    // batch-1 kernel exchange buffers, all in flagged words (data | call stamp << 32)
+    unsigned long long *part_gu, *part_dn;   // [tile][4 segments][64] partial sums of split tiles
+    unsigned long long *aq_flagged;          // [K*F/32 groups][10]: 8 words of q, d, sum
+    unsigned *stamp;                         // call stamp, advanced by the batch-1 router
     int gu_nst, dn_nst;         // ring depth (stages) of the batch-1 kernels
     // host-buffer entry point
     cudaStream_t hstream;
@@ -195,6 +198,6 @@ static cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t 
 // batch-1 decode kernels (qms_moe_stream.cu)
 int stream_prepare(QmsCudaMoe *m);     // shape check + kernel attributes; sets m->stream_ok
 int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *resid, cudaStream_t s);
-int stream_scratch_sizes(const QmsCudaMoe *m, size_t *part_gu, size_t *part_dn, size_t *cnt_gu, size_t *cnt_dn);
+int stream_scratch_sizes(const QmsCudaMoe *m, size_t *part_gu, size_t *part_dn, size_t *aq_flagged);
 
 }  // namespace qms

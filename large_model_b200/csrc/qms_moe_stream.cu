@@ -14,14 +14,19 @@
 //                  gate/up stages (eight chunks of 8 rows x 16 blocks, 18 KB) and then, without
 //                  waiting, its share of down stages into an mbarrier ring; eight consumer warps
 //                  run dp4a dots against the token's Q8 row. A gate/up tile is 32 gate + 32 up
-//                  rows, i.e. one SwiGLU + Q8 re-quantisation group (src/model.c:989-997). The
-//                  down phase needs every group's Q8 values, so the consumers wait (bounded) on a
-//                  grid-wide counter while the ring keeps filling with down chunks; a down tile
-//                  is 8 output rows x 8 experts, combined in selection order with one FMA per
-//                  expert (src/model.c:1152-1162) plus the optional residual.
+//                  rows, i.e. one SwiGLU + Q8 re-quantisation group (src/model.c:989-997),
+//                  finished by an epilogue warp. The down phase needs every group's Q8 values,
+//                  so the consumers gather them (bounded polls) while the ring keeps filling
+//                  with down chunks; a down tile is 8 output rows x 8 experts, combined in
+//                  selection order with one FMA per expert (src/model.c:1152-1162) plus the
+//                  optional residual.
 // Work is split over the CTAs by stages, not tiles, so every SM streams the same number of bytes
-// (+-1 stage). A tile split between CTAs leaves partial row sums in global memory; the CTA that
-// completes it adds them in segment order, so results do not depend on timing. The grid (one
+// (+-1 stage). A tile split between CTAs leaves partial row sums in global memory; the tile's last
+// CTA adds them in CTA order, so results do not depend on timing. Everything exchanged between
+// CTAs (partial sums, Q8 groups) travels as flagged words: 32 data bits plus the call's stamp in
+// one 64-bit store, so a reader polls the data itself and no fence or counter sits on the
+// critical path (under a saturating stream each global round trip costs about a microsecond).
+// The grid (one
 // CTA per SM) is always fully resident: the kernel needs most of an SM's shared memory and
 // nothing it waits for runs behind it; a wait that still runs out sets an error bit.
 // Every mbarrier wait is bounded: on timeout the kernel records an error bit in *err, stops
@@ -33,10 +38,12 @@
 
 namespace qms {
 
-constexpr int kConsumerWarps = 8;
+constexpr int kChunkWarps = 2;                     // consumer warps per chunk (8 rows / kChunkWarps each)
+constexpr int kConsumerWarps = 8 * kChunkWarps;    // a stage is 8 chunks
 constexpr int kStreamThreads = (kConsumerWarps + 2) * 32;   // + producer warp + epilogue warp
 constexpr int kMaxSegments = 4;                    // CTAs a tile may be split across
-constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr uint32_t kSpinLimit = 1u << 22;           // polls before a wait gives up (>= 0.1 s with backoff)
+constexpr uint32_t kPollBackoffNs = 100;
 constexpr size_t kSmemOptIn = 232448;              // 227 KB: per-block dynamic shared memory on sm_100
 constexpr size_t kRouterReserve = 40 * 1024;       // left free for the next call's router CTA
 
@@ -92,6 +99,8 @@ __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
 
 // Wait for phase `parity` of `bar`; give up when another thread set *abort or after kSpinLimit
 // polls (then set *abort and the error bit). Returns true when the phase completed.
+// A failed poll backs off briefly: mbarrier polls and the consumers' shared-memory loads and
+// shuffles share one pipe, so 17 warps polling flat out slow down the warps that have work.
 __device__ __forceinline__ bool wait_bounded(uint64_t *bar, uint32_t parity, volatile int *abort, int *err, int code) {
     uint32_t n = 0;
     while (!mbar_try_wait(bar, parity)) {
@@ -101,6 +110,7 @@ __device__ __forceinline__ bool wait_bounded(uint64_t *bar, uint32_t parity, vol
             atomicOr(err, code);
             return false;
         }
+        __nanosleep(kPollBackoffNs);
     }
     return true;
 }
@@ -118,11 +128,50 @@ __device__ __forceinline__ void drain_issued(uint64_t *full, int nst, int issued
     }
 }
 
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory"); }
 
 // Static split of U stage-units over G CTAs: CTA c owns [lo(c), lo(c+1)).
 __host__ __device__ inline int part_lo(int c, int U, int G) { return (int)((int64_t)c * U / G); }
 __host__ __device__ inline int part_owner(int u, int U, int G) { return (int)(((int64_t)(u + 1) * G - 1) / U); }
+
+// A CTA's units [u0, u1) form tile segments: a head segment (the end of a tile started by the
+// previous CTA), a tail segment (the start of a tile finished by the next CTA) and whole tiles in
+// between. Segments of split tiles are processed first, so the cross-CTA merges they need happen
+// early and a CTA's last work is a whole tile, which needs no merge.
+struct Segs {
+    int u0, u1, S, t_first, t_last, head_s0, tail_s1, nfull, full0, n;
+    __device__ Segs(int u0_, int u1_, int S_) : u0(u0_), u1(u1_), S(S_) {
+        n = 0;
+        if (u0 >= u1) return;
+        t_first = u0 / S;
+        t_last = (u1 - 1) / S;
+        head_s0 = u0 - t_first * S;
+        tail_s1 = u1 - t_last * S;                 // end stage (exclusive) of the last tile
+        const bool head = head_s0 != 0 || (t_first == t_last && tail_s1 != S);
+        const bool tail = t_last != t_first && tail_s1 != S;
+        full0 = head ? t_first + 1 : t_first;
+        const int full1 = tail ? t_last : t_last + 1;
+        nfull = full1 - full0;
+        n = (tail ? 1 : 0) + (head ? 1 : 0) + nfull;
+        has_head = head;
+        has_tail = tail;
+    }
+    bool has_head = false, has_tail = false;
+    // k-th segment in processing order: tail, head, then whole tiles
+    __device__ void get(int k, int &tile, int &s0, int &s1) const {
+        if (has_tail) {
+            if (k == 0) { tile = t_last; s0 = 0; s1 = tail_s1; return; }
+            k--;
+        }
+        if (has_head) {
+            if (k == 0) { tile = t_first; s0 = head_s0; s1 = t_first == t_last ? tail_s1 : S; return; }
+            k--;
+        }
+        tile = full0 + k;
+        s0 = 0;
+        s1 = S;
+    }
+};
 
 // Ring position: slot and phase of the it-th stage, advanced incrementally.
 struct Ring {
@@ -138,11 +187,12 @@ struct Ring {
     }
 };
 
-// One consumer warp's share of a stage: its chunk (8 rows x SB blocks) against one Q8 row.
+// One consumer warp's share of a stage: rows rs + RSTEP * (r0 + p) of its chunk (8 rows x SB
+// blocks, lane = row set rs x block bl) against one Q8 row.
 template <int SB>
 __device__ __forceinline__ void chunk_dot(const uint8_t *chunk, const int8_t *xq, const float *xd, const int *xs8,
-                                          int s, int bl, int rs, float (&acc)[SB / 4]) {
-    constexpr int P = SB / 4, RSTEP = 32 / SB;
+                                          int s, int bl, int rs, int r0, float (&acc)[SB / 4 / kChunkWarps]) {
+    constexpr int P = SB / 4 / kChunkWarps, RSTEP = 32 / SB;
     const int b = s * SB + bl;
     const int4 xa0 = *reinterpret_cast<const int4 *>(xq + b * 32);
     const int4 xa1 = *reinterpret_cast<const int4 *>(xq + b * 32 + 16);
@@ -150,7 +200,7 @@ __device__ __forceinline__ void chunk_dot(const uint8_t *chunk, const int8_t *xq
     const int s8 = xs8[b];
 #pragma unroll
     for (int p = 0; p < P; p++) {
-        const int rr = rs + p * RSTEP;
+        const int rr = rs + (r0 + p) * RSTEP;
         const uint4 nib = *reinterpret_cast<const uint4 *>(chunk + chunk_nib_off(SB, rr, bl));
         const float dw = h2f(*reinterpret_cast<const uint16_t *>(chunk + chunk_scale_off(SB, rr, bl)));
         acc[p] = fmaf((float)(q4_block_isum(nib, xa0, xa1) - s8), dw * d, acc[p]);
@@ -166,7 +216,7 @@ __global__ void __launch_bounds__(256) k_router_bs1(const float *__restrict__ Wl
                                                     float *__restrict__ xq_d, int *__restrict__ xq_s,
                                                     float *__restrict__ logits, int *__restrict__ sel,
                                                     float *__restrict__ wts, int *__restrict__ cnt,
-                                                    int *__restrict__ err) {
+                                                    unsigned *__restrict__ stamp, int *__restrict__ err) {
     extern __shared__ __align__(128) float rsm[];
     const int L = E / 16, PS = L + 4;
     float *srow = rsm;            // [16][PS]
@@ -245,7 +295,11 @@ __global__ void __launch_bounds__(256) k_router_bs1(const float *__restrict__ Wl
     __syncthreads();
     if (!s_last) return;
     topk_token(logits, X, K, sel, wts, s_sel);
-    if (tid == 0) *cnt = 0;
+    if (tid == 0) {
+        *cnt = 0;
+        const unsigned next = __ldcg(stamp) + 1;   // never 0: zeroed words are never current
+        *stamp = next ? next : 1;
+    }
 }
 
 // ---- gate/up + SwiGLU + Q8, then down + combine, in one stream (batch 1) ------------------------
@@ -256,44 +310,62 @@ struct FfnArgs {
     const int8_t *xq_q;
     const float *xq_d;
     const int *xq_s;
-    int8_t *aq_q;
-    float *aq_d;
-    int *aq_s;
-    float *part_gu, *part_dn;
-    int *tcnt_gu, *tcnt_dn;
+    unsigned long long *aq;               // [K*F/32 groups][10] flagged words: q (8 words), d, sum
+    unsigned long long *part_gu, *part_dn;
     const int *sel;
     const float *wts;
     const float *resid;
     float *out;
-    int *grid_cnt;    // [0]: gate/up tiles whose Q8 group is written, [1]: CTAs past the wait
+    const unsigned *stamp;                // this call's stamp, written by the router
     int *err;
 };
 
-// Epilogue-warp half of a tile split across CTAs: publish this CTA's 64 partial sums; the CTA
-// whose segment arrives last gets true and `v` (2 values per lane: [lane], [32 + lane]) holding
-// the full sums, added in segment order so the result does not depend on arrival order.
-__device__ __forceinline__ bool merge_partial(float *part, int *tcnt, int tile, int S, int U, int G, int c,
-                                              float (&v)[2]) {
-    const int lane = threadIdx.x & 31;
-    const int first = part_owner(tile * S, U, G);
-    const int segs = part_owner(tile * S + S - 1, U, G) - first + 1;
-    float *pt = part + (size_t)tile * kMaxSegments * 64;
-    pt[(c - first) * 64 + lane] = v[0];
-    pt[(c - first) * 64 + 32 + lane] = v[1];
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) last = atom_add_acq_rel(tcnt + tile, 1) == segs - 1;
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return false;
-    float a0 = 0.0f, a1 = 0.0f;
-    for (int q = 0; q < segs; q++) {
-        a0 += __ldcg(pt + q * 64 + lane);
-        a1 += __ldcg(pt + q * 64 + 32 + lane);
+constexpr int kAqWords = 10;              // flagged words per Q8 group
+
+// Poll a flagged word until it carries `stamp`; bounded like every other wait.
+__device__ __forceinline__ bool wait_flagged(const unsigned long long *p, uint32_t stamp, unsigned long long &v,
+                                             volatile int *abort, int *err, int code) {
+    uint32_t n = 0;
+    while ((uint32_t)(v >> 32) != stamp) {
+        if (*abort) return false;
+        if (++n == kSpinLimit) {
+            *abort = 1;
+            atomicOr(err, code);
+            return false;
+        }
+        __nanosleep(32);
+        v = ld_flagged(p);
     }
-    v[0] = a0;
-    v[1] = a1;
-    if (lane == 0) tcnt[tile] = 0;
     return true;
+}
+
+// Epilogue-warp half of a tile split across CTAs (2 sums per lane: [lane], [32 + lane]). Every
+// CTA but the tile's last publishes its partial sums as flagged words and returns false; the last
+// CTA polls them and returns true with the full sums, added in CTA order so the result does not
+// depend on timing. A CTA's non-last segments of split tiles are the first work it does, so the
+// last CTA rarely waits.
+__device__ __forceinline__ bool merge_partial(unsigned long long *part, int tile, int S, int U, int G, int c,
+                                              uint32_t stamp, float (&v)[2], volatile int *abort, int *err) {
+    const int lane = threadIdx.x & 31;
+    const int first = part_owner(tile * S, U, G), last = part_owner(tile * S + S - 1, U, G);
+    unsigned long long *pt = part + (size_t)tile * kMaxSegments * 64;
+    if (c != last) {
+        st_flagged(pt + (c - first) * 64 + lane, __float_as_uint(v[0]), stamp);
+        st_flagged(pt + (c - first) * 64 + 32 + lane, __float_as_uint(v[1]), stamp);
+        return false;
+    }
+    float a0 = 0.0f, a1 = 0.0f;
+    bool ok = true;
+    for (int q = 0; q < last - first; q++) {
+        unsigned long long w0 = ld_flagged(pt + q * 64 + lane), w1 = ld_flagged(pt + q * 64 + 32 + lane);
+        ok = ok && wait_flagged(pt + q * 64 + lane, stamp, w0, abort, err, ERR_GRID) &&
+             wait_flagged(pt + q * 64 + 32 + lane, stamp, w1, abort, err, ERR_GRID);
+        a0 += __uint_as_float((uint32_t)w0);
+        a1 += __uint_as_float((uint32_t)w1);
+    }
+    v[0] = a0 + v[0];
+    v[1] = a1 + v[1];
+    return __all_sync(0xffffffffu, ok);
 }
 
 constexpr int kSumBufs = 4;        // tile-sum hand-off buffers between consumer and epilogue warps
@@ -302,7 +374,7 @@ template <int SBG, int SBD>
 __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs a) {
     constexpr uint32_t GBG = 8 * SBG * 18, STG = 8 * GBG, GBD = 8 * SBD * 18, STD = 8 * GBD;
     constexpr uint32_t SLOT = STG > STD ? STG : STD;
-    constexpr int PG = SBG / 4, RSG = 32 / SBG, PD = SBD / 4, RSD = 32 / SBD;
+    constexpr int PG = SBG / 4 / kChunkWarps, RSG = 32 / SBG, PD = SBD / 4 / kChunkWarps, RSD = 32 / SBD;
     extern __shared__ __align__(128) uint8_t smem[];
     const int nst = a.nst, K = a.K, F = a.F, nbE = a.nbE, nbF = a.nbF;
     uint8_t *ring = smem;
@@ -317,11 +389,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
     float *sad = reinterpret_cast<float *>(saq + K * F);            // [K][nbF]
     int *sas = reinterpret_cast<int *>(sad + K * nbF);              // [K][nbF], 8 * sum
     float *sbuf = reinterpret_cast<float *>(sas + K * nbF);         // [kSumBufs][64] tile sums
-    __shared__ int s_abort, s_ok;
+    __shared__ int s_abort;
+    __shared__ const uint8_t *s_gu_base[8], *s_dn_base[8];   // producer: selected experts' weights
+    __shared__ float s_w[8];                                   // epilogue: routing weights
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = gridDim.x, c = blockIdx.x;
     const int Sg = nbE / SBG, tps = F / 32, ntg = K * tps, Ug = ntg * Sg;
     const int Sd = nbF / SBD, RBE = 8 / K, RT = 8 * RBE, Ud = (a.E / RT) * Sd;
+    const uint32_t WSD = (uint32_t)Sd * GBD;        // one chunk's share of a down stage (Sd slots)
     const int ug0 = part_lo(c, Ug, G), ug1 = part_lo(c + 1, Ug, G);
     const int ud0 = part_lo(c, Ud, G), ud1 = part_lo(c + 1, Ud, G);
     const size_t tile_bytes = (size_t)Sg * STG;
@@ -345,35 +420,62 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
     if (warp == kConsumerWarps) {                   // ---- producer: one stream, gate/up then down
         if (lane == 0) {
             const uint64_t pol = evict_first_policy();
-            int ex[8];
-            for (int j = 0; j < 8; j++) ex[j] = j < K ? __ldcg(a.sel + j) : 0;
+            // expert bases live in shared memory: a local array would sit in local memory, and
+            // every load from it that misses L1 queues behind the stream in L2
+            for (int j = 0; j < 8; j++) {
+                const int e = j < K ? __ldcg(a.sel + j) : 0;
+                s_gu_base[j] = a.gu + (size_t)e * a.gu_expert;
+            }
+            for (int gi = 0; gi < 8; gi++) s_dn_base[gi] = a.dn + (size_t)__ldcg(a.sel + gi / RBE) * a.dn_expert;
             Ring r(nst);
             int issued = 0;
             bool ok = true;
-            for (int u = ug0; u < ug1 && ok; u++) {
-                const int tile = u / Sg, s = u - tile * Sg;
-                const uint8_t *src = a.gu + (size_t)ex[tile / tps] * a.gu_expert + (size_t)(tile % tps) * tile_bytes;
-                if (issued >= nst && !(ok = wait_bounded(&empty[r.slot], r.phase ^ 1, abort_flag, a.err, ERR_PRODUCER)))
+            const Segs sg(ug0, ug1, Sg), sd(ud0, ud1, Sd);
+            for (int k = 0; k < sg.n && ok; k++) {
+                int tile, s0, s1;
+                sg.get(k, tile, s0, s1);
+                const uint8_t *src = s_gu_base[tile / tps] + (size_t)(tile % tps) * tile_bytes;
+                for (int s = s0; s < s1 && ok; s++) {
+                    if (issued >= nst &&
+                        !(ok = wait_bounded(&empty[r.slot], r.phase ^ 1, abort_flag, a.err, ERR_PRODUCER)))
+                        break;
+                    mbar_arrive_expect_tx(&full[r.slot], STG);
+                    bulk_load(ring + (size_t)r.slot * SLOT, src + (size_t)s * STG, STG, &full[r.slot], pol);
+                    issued++;
+                    r.next();
+                }
+            }
+            // The ring fills with down chunks while the consumers wait for every CTA's SwiGLU groups.
+            // First pad to a multiple of Sd slots with stages that carry no data.
+            while (r.slot % Sd != 0 && ok) {
+                if (issued >= nst &&
+                    !(ok = wait_bounded(&empty[r.slot], r.phase ^ 1, abort_flag, a.err, ERR_PRODUCER)))
                     break;
-                mbar_arrive_expect_tx(&full[r.slot], STG);
-                bulk_load(ring + (size_t)r.slot * SLOT, src + (size_t)s * STG, STG, &full[r.slot], pol);
+                mbar_arrive(&full[r.slot]);
                 issued++;
                 r.next();
             }
-            const uint8_t *base[8];
-            for (int gi = 0; gi < 8; gi++) base[gi] = a.dn + (size_t)ex[gi / RBE] * a.dn_expert;
-            for (int u = ud0; u < ud1 && ok; u++) {
-                const int tile = u / Sd, s = u - tile * Sd;
-                if (issued >= nst && !(ok = wait_bounded(&empty[r.slot], r.phase ^ 1, abort_flag, a.err, ERR_PRODUCER)))
-                    break;
-                mbar_arrive_expect_tx(&full[r.slot], STD);
+            for (int k = 0; k < sd.n && ok; k++) {
+                int tile, s0, s1;
+                sd.get(k, tile, s0, s1);
+                // A down stage is one tile segment: per chunk (expert / row block) its stages s0..s1
+                // are adjacent in HBM, so it is ONE copy of up to Sd * GBD bytes (many small copies
+                // stream far slower). It takes Sd whole slots starting at a multiple of Sd (nst is
+                // one, so it never wraps).
+                for (int q = 0; q < Sd && ok; q++)
+                    if (issued + q >= nst)
+                        ok = wait_bounded(&empty[r.slot + q], r.phase ^ 1, abort_flag, a.err, ERR_PRODUCER);
+                if (!ok) break;
+                const uint32_t bytes = (uint32_t)(s1 - s0) * GBD;
+                mbar_arrive_expect_tx(&full[r.slot], 8 * bytes);
                 uint8_t *dst = ring + (size_t)r.slot * SLOT;
                 for (int gi = 0; gi < 8; gi++) {
                     const size_t rb = (size_t)tile * RBE + gi % RBE;
-                    bulk_load(dst + gi * GBD, base[gi] + (rb * Sd + s) * GBD, GBD, &full[r.slot], pol);
+                    bulk_load(dst + gi * WSD, s_dn_base[gi] + (rb * Sd + s0) * GBD, bytes, &full[r.slot], pol);
                 }
-                issued++;
-                r.next();
+                for (int q = 1; q < Sd; q++) mbar_arrive(&full[r.slot + q]);
+                issued += Sd;
+                for (int q = 0; q < Sd; q++) r.next();
             }
             if (!ok || *abort_flag) drain_issued(full, nst, issued, a.err);
         }
@@ -383,16 +485,16 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
     if (warp == kConsumerWarps + 1) {               // ---- epilogue warp: SwiGLU/Q8, merges, combine
         Ring sr(kSumBufs);
         bool ok = true;
+        const uint32_t stamp = __ldcg(a.stamp);
         for (int pass = 0; pass < 2; pass++) {
             const bool gate = pass == 0;
             const int S = gate ? Sg : Sd, U = gate ? Ug : Ud;
-            const int u0 = gate ? ug0 : ud0, u1 = gate ? ug1 : ud1;
-            float w[8];
-            if (!gate)
-                for (int j = 0; j < 8; j++) w[j] = j < K ? __ldcg(a.wts + j) : 0.0f;
-            for (int u = u0; u < u1;) {
-                const int tile = u / S, s0 = u - tile * S, s1 = min(S, s0 + (u1 - u));
-                u += s1 - s0;
+            const Segs sq(gate ? ug0 : ud0, gate ? ug1 : ud1, S);
+            if (!gate && lane < 8) s_w[lane] = lane < K ? __ldcg(a.wts + lane) : 0.0f;
+            __syncwarp();
+            for (int k = 0; k < sq.n; k++) {
+                int tile, s0, s1;
+                sq.get(k, tile, s0, s1);
                 if (ok) ok = __all_sync(0xffffffffu, wait_bounded(&sfull[sr.slot], sr.phase, abort_flag, a.err,
                                                                   ERR_CONSUMER));
                 float v[2] = {sbuf[sr.slot * 64 + lane], sbuf[sr.slot * 64 + 32 + lane]};
@@ -402,21 +504,19 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
                 if (!ok) continue;
                 bool mine = true;
                 if (!(s0 == 0 && s1 == S))
-                    mine = merge_partial(gate ? a.part_gu : a.part_dn, gate ? a.tcnt_gu : a.tcnt_dn, tile, S, U, G, c,
-                                         v);
+                    mine = merge_partial(gate ? a.part_gu : a.part_dn, tile, S, U, G, c, stamp, v, abort_flag, a.err);
                 if (!mine) continue;
                 if (gate) {                         // rows 0-31: gate f0+lane, rows 32-63: up f0+lane
-                    const int slot = tile / tps, t = tile % tps;
+                    // Q8 group `tile` (expert slot tile / tps, values f0..f0+31) as flagged words
                     const float av = __fmul_rn(__fdiv_rn(v[0], __fadd_rn(1.0f, expf(-v[0]))), v[1]);
                     const Q8Lane q8 = quantize_lane(av);
-                    const size_t base = (size_t)slot * F + (size_t)t * 32;
-                    a.aq_q[base + lane] = (int8_t)q8.q;
-                    if (lane == 0) {
-                        a.aq_d[(size_t)slot * tps + t] = q8.d;
-                        a.aq_s[(size_t)slot * tps + t] = q8.sum;
-                    }
-                    __syncwarp();
-                    if (lane == 0) red_add_release(a.grid_cnt, 1);   // one more Q8 group is visible
+                    uint32_t b4 = (uint32_t)(q8.q & 0xff) << (8 * (lane & 3));
+                    b4 |= __shfl_xor_sync(0xffffffffu, b4, 1);
+                    b4 |= __shfl_xor_sync(0xffffffffu, b4, 2);
+                    unsigned long long *dst = a.aq + (size_t)tile * kAqWords;
+                    if ((lane & 3) == 0) st_flagged(dst + (lane >> 2), b4, stamp);
+                    if (lane == 1) st_flagged(dst + 8, __float_as_uint(q8.d), stamp);
+                    if (lane == 2) st_flagged(dst + 9, (uint32_t)q8.sum, stamp);
                 } else {                            // sum index (j*RBE + rbi)*8 + rr: expert j, row rr of block rbi
                     const int rbi = (lane >> 3) & 7, rr = lane & 7;
                     float o = 0.0f;
@@ -424,7 +524,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
                         const int idx = (jj * RBE + rbi) * 8 + rr;
                         const float lo = __shfl_sync(0xffffffffu, v[0], idx & 31);
                         const float hi = __shfl_sync(0xffffffffu, v[1], idx & 31);
-                        o = __fmaf_rn(w[jj], idx < 32 ? lo : hi, o);
+                        o = __fmaf_rn(s_w[jj], idx < 32 ? lo : hi, o);
                     }
                     if (lane < RT) {
                         const int i = tile * RT + lane;
@@ -446,16 +546,16 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
         sxs[i] = 8 * __ldcg(a.xq_s + i);
     }
     consumer_sync();
-    const int g = warp;
+    const int g = warp / kChunkWarps, half = warp % kChunkWarps;   // chunk of the stage, row part
     Ring r(nst), sr(kSumBufs);
     int handed = 0;
     bool ok = true;
-    // hand a tile's 64 sums (8 per warp) to the epilogue warp
+    // hand a tile's 64 sums (8 per chunk) to the epilogue warp
     auto hand_off = [&](const float *acc, int P, int RS, int bl, int rs) {
         if (handed >= kSumBufs && ok)
             ok = __all_sync(0xffffffffu, wait_bounded(&sempty[sr.slot], sr.phase ^ 1, abort_flag, a.err, ERR_CONSUMER));
         if (bl == 0)
-            for (int p = 0; p < P; p++) sbuf[sr.slot * 64 + g * 8 + rs + p * RS] = acc[p];
+            for (int p = 0; p < P; p++) sbuf[sr.slot * 64 + g * 8 + rs + (half * P + p) * RS] = acc[p];
         __syncwarp();
         if (lane == 0) mbar_arrive(&sfull[sr.slot]);
         sr.next();
@@ -463,20 +563,21 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
     };
     {
         const int bl = lane % SBG, rs = lane / SBG;
-        for (int u = ug0; u < ug1;) {
-            const int tile = u / Sg, s0 = u - tile * Sg, s1 = min(Sg, s0 + (ug1 - u));
+        const Segs sq(ug0, ug1, Sg);
+        for (int k = 0; k < sq.n; k++) {
+            int tile, s0, s1;
+            sq.get(k, tile, s0, s1);
             float acc[PG];
 #pragma unroll
             for (int p = 0; p < PG; p++) acc[p] = 0.0f;
             for (int s = s0; s < s1; s++, r.next()) {
                 if (ok) ok = __all_sync(0xffffffffu, wait_bounded(&full[r.slot], r.phase, abort_flag, a.err, ERR_CONSUMER));
                 if (ok) {
-                    chunk_dot<SBG>(ring + (size_t)r.slot * SLOT + g * GBG, sxq, sxd, sxs, s, bl, rs, acc);
+                    chunk_dot<SBG>(ring + (size_t)r.slot * SLOT + g * GBG, sxq, sxd, sxs, s, bl, rs, half * PG, acc);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[r.slot]);
                 }
             }
-            u += s1 - s0;
 #pragma unroll
             for (int p = 0; p < PG; p++)
 #pragma unroll
@@ -485,56 +586,89 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
         }
     }
 
-    // ---- phase B: wait until every CTA's Q8 groups are written, then down + combine
-    if (tid == 0) {
-        int okg = 1;
-        uint32_t n = 0;
-        while (ld_acquire(a.grid_cnt) < ntg) {
-            if (*abort_flag || ++n == kSpinLimit) {
-                okg = 0;
-                if (!*abort_flag) atomicOr(a.err, ERR_GRID);
-                *abort_flag = 1;
-                break;
-            }
-            __nanosleep(32);
-        }
-        // the last CTA past the wait re-arms both counters for the next call
-        if (atomicAdd(a.grid_cnt + 1, 1) == G - 1) {
-            atomicExch(a.grid_cnt, 0);
-            atomicExch(a.grid_cnt + 1, 0);
-        }
-        s_ok = okg;
+    // the producer's padding slots before the first down stage, released before the wait so the
+    // ring can fill with down stages meanwhile
+    for (; r.slot % Sd != 0; r.next()) {
+        if (ok) ok = __all_sync(0xffffffffu, wait_bounded(&full[r.slot], r.phase, abort_flag, a.err, ERR_CONSUMER));
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(&empty[r.slot]);
     }
-    consumer_sync();
-    ok = ok && s_ok;
+
+    // ---- phase B: gather every CTA's Q8 groups as they appear, then down + combine. Each thread
+    // keeps all its words in flight and re-polls only the pending ones, one round trip per round.
     if (ok) {
-        for (int i = tid; i < K * F / 16; i += kConsumerWarps * 32)
-            reinterpret_cast<int4 *>(saq)[i] = __ldcg(reinterpret_cast<const int4 *>(a.aq_q) + i);
-        for (int i = tid; i < K * nbF; i += kConsumerWarps * 32) {
-            sad[i] = __ldcg(a.aq_d + i);
-            sas[i] = 8 * __ldcg(a.aq_s + i);
+        const uint32_t stamp = __ldcg(a.stamp);
+        const int nw = ntg * kAqWords;
+        constexpr int kBatch = 8;
+        for (int i0 = tid; i0 < nw && ok; i0 += kBatch * kConsumerWarps * 32) {
+            unsigned long long v[kBatch];
+            uint32_t pending = 0;
+#pragma unroll
+            for (int b = 0; b < kBatch; b++) {
+                const int i = i0 + b * kConsumerWarps * 32;
+                v[b] = i < nw ? ld_flagged(a.aq + i) : 0ull;
+            }
+            uint32_t n = 0;
+            for (;;) {
+#pragma unroll
+                for (int b = 0; b < kBatch; b++) {
+                    const int i = i0 + b * kConsumerWarps * 32;
+                    if (i < nw && (uint32_t)(v[b] >> 32) != stamp) pending |= 1u << b;
+                }
+                if (!pending) break;
+                if (*abort_flag) {
+                    ok = false;
+                    break;
+                }
+                if (++n == kSpinLimit) {
+                    *abort_flag = 1;
+                    atomicOr(a.err, ERR_GRID);
+                    ok = false;
+                    break;
+                }
+                __nanosleep(64);
+#pragma unroll
+                for (int b = 0; b < kBatch; b++)
+                    if (pending & (1u << b)) v[b] = ld_flagged(a.aq + i0 + b * kConsumerWarps * 32);
+                pending = 0;
+            }
+            if (!ok) break;
+#pragma unroll
+            for (int b = 0; b < kBatch; b++) {
+                const int i = i0 + b * kConsumerWarps * 32;
+                if (i >= nw) continue;
+                const int gi = i / kAqWords, w = i - gi * kAqWords;
+                const uint32_t d = (uint32_t)v[b];
+                if (w < 8) reinterpret_cast<uint32_t *>(saq)[gi * 8 + w] = d;
+                else if (w == 8) sad[gi] = __uint_as_float(d);
+                else sas[gi] = 8 * (int)d;
+            }
         }
     }
     consumer_sync();
+    ok = ok && !*abort_flag;                        // every failed wait raised the abort flag
     {
         const int j = g / RBE, bl = lane % SBD, rs = lane / SBD;
         const int8_t *xq = saq + (size_t)j * F;
         const float *xdv = sad + j * nbF;
         const int *xsv = sas + j * nbF;
-        for (int u = ud0; u < ud1;) {
-            const int tile = u / Sd, s0 = u - tile * Sd, s1 = min(Sd, s0 + (ud1 - u));
+        const Segs sq(ud0, ud1, Sd);
+        for (int k = 0; k < sq.n; k++) {
+            int tile, s0, s1;
+            sq.get(k, tile, s0, s1);
             float acc[PD];
 #pragma unroll
             for (int p = 0; p < PD; p++) acc[p] = 0.0f;
-            for (int s = s0; s < s1; s++, r.next()) {
-                if (ok) ok = __all_sync(0xffffffffu, wait_bounded(&full[r.slot], r.phase, abort_flag, a.err, ERR_CONSUMER));
-                if (ok) {
-                    chunk_dot<SBD>(ring + (size_t)r.slot * SLOT + g * GBD, xq, xdv, xsv, s, bl, rs, acc);
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[r.slot]);
-                }
+            if (ok) ok = __all_sync(0xffffffffu, wait_bounded(&full[r.slot], r.phase, abort_flag, a.err, ERR_CONSUMER));
+            if (ok) {
+                const uint8_t *chunk = ring + (size_t)r.slot * SLOT + g * WSD;   // [chunk][stage s0..s1]
+                for (int s = s0; s < s1; s++)
+                    chunk_dot<SBD>(chunk + (s - s0) * GBD, xq, xdv, xsv, s, bl, rs, half * PD, acc);
+                __syncwarp();
+                if (lane == 0)
+                    for (int q = 0; q < Sd; q++) mbar_arrive(&empty[r.slot + q]);
             }
-            u += s1 - s0;
+            for (int q = 0; q < Sd; q++) r.next();
 #pragma unroll
             for (int p = 0; p < PD; p++)
 #pragma unroll
@@ -571,9 +705,11 @@ int stream_prepare(QmsCudaMoe *m) {
     if (!(m->K == 1 || m->K == 2 || m->K == 4 || m->K == 8) || m->X > 256 || 2 * m->X > m->E) return QMS_CUDA_OK;
     if (m->nbE % m->cgu.SB || m->nbF % m->cdn.SB) return QMS_CUDA_OK;
     // the deepest ring that still leaves room for the next call's router CTA on the same SM
-    m->gu_nst = (int)std::min<size_t>(12, (kSmemOptIn - kRouterReserve - ffn_fixed(m)) / (ffn_slot(m) + 16));
+    // (a multiple of the down stage width cdn.S, so a down stage never wraps around the ring)
+    const int fit = (int)std::min<size_t>(12, (kSmemOptIn - kRouterReserve - ffn_fixed(m)) / (ffn_slot(m) + 16));
+    m->gu_nst = fit / m->cdn.S * m->cdn.S;
     m->dn_nst = m->gu_nst;
-    if (m->gu_nst < 4) return QMS_CUDA_OK;
+    if (m->gu_nst < 4 || m->gu_nst < m->cdn.S) return QMS_CUDA_OK;
     const int Ugu = m->K * (m->F / 32) * m->cgu.S, Udn = (m->E / (64 / m->K)) * m->cdn.S;
     if (max_segments(Ugu, m->cgu.S, m->nsm) > kMaxSegments || max_segments(Udn, m->cdn.S, m->nsm) > kMaxSegments)
         return QMS_CUDA_OK;
@@ -587,19 +723,19 @@ int stream_prepare(QmsCudaMoe *m) {
     return QMS_CUDA_OK;
 }
 
-int stream_scratch_sizes(const QmsCudaMoe *m, size_t *part_gu, size_t *part_dn, size_t *cnt_gu, size_t *cnt_dn) {
+int stream_scratch_sizes(const QmsCudaMoe *m, size_t *part_gu, size_t *part_dn, size_t *aq_flagged) {
     const int tiles_gu = m->K * (m->F / 32), tiles_dn = m->E / (64 / std::max(1, std::min(8, m->K)));
-    *part_gu = (size_t)tiles_gu * kMaxSegments * 64 * 4;
-    *part_dn = (size_t)tiles_dn * kMaxSegments * 64 * 4;
-    *cnt_gu = (size_t)tiles_gu * 4 + 64;           // + the two grid counters
-    *cnt_dn = (size_t)tiles_dn * 4;
+    *part_gu = (size_t)tiles_gu * kMaxSegments * 64 * 8;
+    *part_dn = (size_t)tiles_dn * kMaxSegments * 64 * 8;
+    *aq_flagged = (size_t)tiles_gu * kAqWords * 8;
     return QMS_CUDA_OK;
 }
 
 int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *resid, cudaStream_t s) {
     if (m->timing) QMS_CK(cudaEventRecord(m->ev[0], s));
     QMS_CK(launch_pdl(k_router_bs1, dim3(m->X), dim3(256), router_smem(m->E), s, (const float *)m->router_lm, m->X,
-                      m->E, xn, m->K, m->xq_q, m->xq_d, m->xq_s, m->logits, m->sel, m->wts, m->cnt, m->err));
+                      m->E, xn, m->K, m->xq_q, m->xq_d, m->xq_s, m->logits, m->sel, m->wts, m->cnt, m->stamp,
+                      m->err));
     if (m->timing) {
         QMS_CK(cudaEventRecord(m->ev[1], s));
         QMS_CK(cudaEventRecord(m->ev[2], s));
@@ -618,18 +754,14 @@ int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *
     a.xq_q = m->xq_q;
     a.xq_d = m->xq_d;
     a.xq_s = m->xq_s;
-    a.aq_q = m->aq_q;
-    a.aq_d = m->aq_d;
-    a.aq_s = m->aq_s;
+    a.aq = m->aq_flagged;
     a.part_gu = m->part_gu;
     a.part_dn = m->part_dn;
-    a.tcnt_gu = m->tcnt_gu;
-    a.tcnt_dn = m->tcnt_dn;
     a.sel = m->sel;
     a.wts = m->wts;
     a.resid = resid;
     a.out = out;
-    a.grid_cnt = m->tcnt_gu + m->K * (m->F / 32);
+    a.stamp = m->stamp;
     a.err = m->err;
     QMS_CK(launch_pdl(ffn_kernel(m), dim3(m->nsm), dim3(kStreamThreads), ffn_smem(m), s, a));
     if (m->timing) {

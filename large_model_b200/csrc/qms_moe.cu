@@ -408,12 +408,13 @@ int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
     const size_t o_aq_s = off; off += al256(TK * m->nbF * 4);
     const size_t o_cnt = off; off += al256((1 + TK * m->nbF) * 4);
     const size_t o_err = off; off += 256;
-    size_t pg = 0, pd = 0, af = 0;
-    stream_scratch_sizes(m, &pg, &pd, &af);
-    const size_t o_pgu = off; off += al256(pg);
-    const size_t o_pdn = off; off += al256(pd);
-    const size_t o_aqf = off; off += al256(af);
-    const size_t o_stamp = off; off += 256;
+    StreamScratch ss;
+    stream_scratch_sizes(m, &ss);
+    const size_t o_lgf = off; off += al256(ss.lg_flagged);
+    const size_t o_stamps = off; off += al256(ss.stamps);
+    const size_t o_aqf = off; off += al256(ss.aq_flagged);
+    const size_t o_pgu = off; off += al256(ss.part_gu);
+    const size_t o_pdn = off; off += al256(ss.part_dn);
     void *p = nullptr;
     if (cudaMalloc(&p, off) != cudaSuccess) {
         cudaGetLastError();
@@ -441,10 +442,11 @@ int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
     m->aq_s = (int *)(b + o_aq_s);
     m->cnt = (int *)(b + o_cnt);
     m->err = (int *)(b + o_err);
+    m->lg_flagged = (unsigned long long *)(b + o_lgf);
+    m->stamps = (unsigned *)(b + o_stamps);
+    m->aq_flagged = (unsigned long long *)(b + o_aqf);
     m->part_gu = (unsigned long long *)(b + o_pgu);
     m->part_dn = (unsigned long long *)(b + o_pdn);
-    m->aq_flagged = (unsigned long long *)(b + o_aqf);
-    m->stamp = (unsigned *)(b + o_stamp);
     m->cap_T = T;
     return QMS_CUDA_OK;
 }

@@ -163,11 +163,12 @@ struct QmsCudaMoe {
     int *aq_s;
     int *cnt;            // [0]: router arrivals; [1 + slot*nbF + g]: gate/up group arrivals
     int *err;            // device error flags (bounded waits that gave up)
-    // batch-1 kernel exchange buffers, all in flagged words (data | call stamp << 32)
-    unsigned long long *part_gu, *part_dn;   // [tile][4 segments][64] partial sums of split tiles
+    // batch-1 kernel exchange buffers, in flagged words (data | call stamp << 32)
+    unsigned long long *lg_flagged;          // [X] router logits
     unsigned long long *aq_flagged;          // [K*F/32 groups][10]: 8 words of q, d, sum
-    unsigned *stamp;                         // call stamp, advanced by the batch-1 router
-    int gu_nst, dn_nst;         // ring depth (stages) of the batch-1 kernels
+    unsigned long long *part_gu, *part_dn;   // [tile][segments][64] partial sums of split tiles
+    unsigned *stamps;                        // [nsm] per-CTA call stamps
+    int gu_nst, dn_nst;         // ring depth (slots) of the batch-1 kernel
     // host-buffer entry point
     cudaStream_t hstream;
     float *d_in, *d_out;
@@ -198,6 +199,9 @@ static cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t 
 // batch-1 decode kernels (qms_moe_stream.cu)
 int stream_prepare(QmsCudaMoe *m);     // shape check + kernel attributes; sets m->stream_ok
 int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *resid, cudaStream_t s);
-int stream_scratch_sizes(const QmsCudaMoe *m, size_t *part_gu, size_t *part_dn, size_t *aq_flagged);
+struct StreamScratch {                 // bytes of the batch-1 kernel's exchange buffers
+    size_t lg_flagged, stamps, aq_flagged, part_gu, part_dn;
+};
+int stream_scratch_sizes(const QmsCudaMoe *m, StreamScratch *sz);
 
 }  // namespace qms

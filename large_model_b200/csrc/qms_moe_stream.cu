@@ -1,36 +1,33 @@
-// qms_moe_stream.cu - batch-1 decode of the MoE block, streamed from HBM with TMA bulk copies.
+// qms_moe_stream.cu - batch-1 decode of the MoE block as ONE kernel per call, streamed from HBM
+// with TMA bulk copies.
 //
 // A decode token reads 8 experts x 10.6 MB of Q4_0 weights per 235B layer and does ~3.5 integer
-// ops per byte, so the block is bound by HBM bandwidth, and on B200 every separately launched
-// stream of a few tens of MB loses several microseconds to ramp-up and tail. So a call is two
-// kernels chained with programmatic dependent launch (PDL):
-//   k_router_bs1   one CTA per router row. Its weight row (16 KB, stored lane-major) is
-//                  bulk-copied into shared memory BEFORE griddepcontrol.wait, i.e. while the
-//                  previous kernel still runs; then xn is read, quantised to Q8, the logit is
-//                  computed in the reference's exact F32 order and the last CTA to finish ranks
-//                  the experts.
-//   k_stream_ffn   persistent, one CTA per SM, ONE continuous stream of all the call's expert
-//                  bytes: a producer thread bulk-copies (cp.async.bulk) first the CTA's share of
-//                  gate/up stages (eight chunks of 8 rows x 16 blocks, 18 KB) and then, without
-//                  waiting, its share of down stages into an mbarrier ring; eight consumer warps
-//                  run dp4a dots against the token's Q8 row. A gate/up tile is 32 gate + 32 up
-//                  rows, i.e. one SwiGLU + Q8 re-quantisation group (src/model.c:989-997),
-//                  finished by an epilogue warp. The down phase needs every group's Q8 values,
-//                  so the consumers gather them (bounded polls) while the ring keeps filling
-//                  with down chunks; a down tile is 8 output rows x 8 experts, combined in
-//                  selection order with one FMA per expert (src/model.c:1152-1162) plus the
-//                  optional residual.
+// ops per byte, so the block is bound by HBM bandwidth; on B200 every separately launched stream
+// of a few tens of MB loses microseconds to launch, ramp-up and tail, and every global round trip
+// taken while the stream saturates HBM costs a microsecond or more. k_decode_bs1 is persistent
+// (one CTA per SM: 16 consumer warps, a producer warp, an epilogue warp) and does:
+//   routing   CTA e < X bulk-copies router row e (stored lane-major) into shared memory before
+//             griddepcontrol.wait, computes logit e in the reference's exact F32 order and
+//             publishes it; every CTA quantises xn to Q8 itself, gathers the X logits and selects
+//             the experts itself, so no CTA waits for a designated one and no second kernel runs;
+//   gate/up   the CTA's share of all K experts' gate/up stages (eight chunks of 8 rows x 16
+//             blocks, 18 KB) is bulk-copied into an mbarrier ring; consumer warps run dp4a dots
+//             against the token's Q8 row. A tile is 32 gate + 32 up rows, i.e. one SwiGLU + Q8
+//             re-quantisation group (src/model.c:989-997), finished by the epilogue warp;
+//   down      the consumers gather every CTA's Q8 groups (bounded polls) while the ring keeps
+//             filling with down chunks; a down tile is 8 output rows x 8 experts, combined in
+//             selection order with one FMA per expert (src/model.c:1152-1162) plus the optional
+//             residual.
 // Work is split over the CTAs by stages, not tiles, so every SM streams the same number of bytes
 // (+-1 stage). A tile split between CTAs leaves partial row sums in global memory; the tile's last
 // CTA adds them in CTA order, so results do not depend on timing. Everything exchanged between
-// CTAs (partial sums, Q8 groups) travels as flagged words: 32 data bits plus the call's stamp in
-// one 64-bit store, so a reader polls the data itself and no fence or counter sits on the
-// critical path (under a saturating stream each global round trip costs about a microsecond).
-// The grid (one
-// CTA per SM) is always fully resident: the kernel needs most of an SM's shared memory and
-// nothing it waits for runs behind it; a wait that still runs out sets an error bit.
-// Every mbarrier wait is bounded: on timeout the kernel records an error bit in *err, stops
-// issuing copies, waits (bounded) for the copies it already issued and returns.
+// CTAs (logits, partial sums, Q8 groups) travels as flagged words: 32 data bits and a call stamp in
+// one 64-bit store, so a reader polls the data itself and no fence, atomic or counter sits on the
+// critical path. Each CTA keeps its own stamp word (all CTAs run every call, so they agree). The
+// grid (one CTA per SM) is always fully resident: the kernel needs most of an SM's shared memory
+// and nothing it waits for runs behind it. Every wait is bounded: on timeout the kernel records an
+// error bit in *err, stops issuing copies, waits (bounded) for the copies it already issued and
+// returns.
 #include <algorithm>
 
 #include "qms_moe.cuh"
@@ -45,7 +42,9 @@ constexpr int kMaxSegments = 4;                    // CTAs a tile may be split a
 constexpr uint32_t kSpinLimit = 1u << 22;           // polls before a wait gives up (>= 0.1 s with backoff)
 constexpr uint32_t kPollBackoffNs = 100;
 constexpr size_t kSmemOptIn = 232448;              // 227 KB: per-block dynamic shared memory on sm_100
-constexpr size_t kRouterReserve = 40 * 1024;       // left free for the next call's router CTA
+#ifndef QMS_STREAM_MAX_RING
+#define QMS_STREAM_MAX_RING 12
+#endif
 
 enum { ERR_CONSUMER = 1, ERR_PRODUCER = 2, ERR_GRID = 4, ERR_ROUTER = 16, ERR_DRAIN = 32 };
 
@@ -207,116 +206,136 @@ __device__ __forceinline__ void chunk_dot(const uint8_t *chunk, const int8_t *xq
     }
 }
 
-// ---- router (batch 1) --------------------------------------------------------------------------
-// The row is stored lane-major ([k][i] = element 16*i + k), so lane k of the exact-order dot reads
-// its 256-long FMA chain with 128-bit loads; shared memory pads each lane's run by 16 bytes so
-// the 16 lanes hit different banks.
-__global__ void __launch_bounds__(256) k_router_bs1(const float *__restrict__ Wlm, int X, int E,
-                                                    const float *__restrict__ xn, int K, int8_t *__restrict__ xq_q,
-                                                    float *__restrict__ xq_d, int *__restrict__ xq_s,
-                                                    float *__restrict__ logits, int *__restrict__ sel,
-                                                    float *__restrict__ wts, int *__restrict__ cnt,
-                                                    unsigned *__restrict__ stamp, int *__restrict__ err) {
-    extern __shared__ __align__(128) float rsm[];
-    const int L = E / 16, PS = L + 4;
-    float *srow = rsm;            // [16][PS]
-    float *sx = rsm + 16 * PS;    // [16][PS]
-    __shared__ __align__(8) uint64_t bar;
-    __shared__ int s_sel[64];
-    __shared__ int s_last, s_abort;
-    const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid == 0) {
-        s_abort = 0;
-        mbar_init(&bar, 1);
-        fence_mbar_init();
-        mbar_arrive_expect_tx(&bar, (uint32_t)E * 4);
-        const uint64_t pol = evict_first_policy();
-        for (int k = 0; k < 16; k++)
-            bulk_load(srow + k * PS, Wlm + (size_t)e * E + (size_t)k * L, (uint32_t)L * 4, &bar, pol);
-    }
-    pdl_trigger();
-    pdl_wait();                                    // xn comes from the previous kernel
-    for (int q = tid; q < E / 4; q += blockDim.x) {
-        const float4 v = __ldcg(reinterpret_cast<const float4 *>(xn) + q);
-        const int j = 4 * q;
-        sx[((j + 0) & 15) * PS + ((j + 0) >> 4)] = v.x;
-        sx[((j + 1) & 15) * PS + ((j + 1) >> 4)] = v.y;
-        sx[((j + 2) & 15) * PS + ((j + 2) >> 4)] = v.z;
-        sx[((j + 3) & 15) * PS + ((j + 3) >> 4)] = v.w;
-    }
-    __syncthreads();
-    for (int b = e + X * (warp - 1); warp > 0 && b < E / 32; b += X * 7) {   // warp 0 runs the chain
-        const int j = b * 32 + lane;
-        const Q8Lane r = quantize_lane(sx[(j & 15) * PS + (j >> 4)]);
-        xq_q[j] = (int8_t)r.q;
-        if (lane == 0) {
-            xq_d[b] = r.d;
-            xq_s[b] = r.sum;
+// ---- routing inside the decode kernel -----------------------------------------------------------
+// The reference (src/model.c:1045-1064) takes prob[e] = exp((double)l_e - max) / z in double,
+// picks the top k by repeated strict-'>' argmax over prob (ties, including probabilities that
+// underflow to 0, go to the lower index) and weighs them (float)(p_j / sum_j p_j), the sum in
+// selection order. On B200 a dependent double operation costs ~90 cycles, so the critical path
+// ranks the float logits instead (ties to the lower index; exp(l - max) / z is non-decreasing in
+// l, so the order agrees) and proves the agreement from the double exponentials of the top K+1
+// alone: if each exceeds the next by more than the rounding of one division, their
+// probabilities are strictly decreasing. Only when that proof fails does the selection wait for
+// the exact double ranking; z, the probabilities and the weights are computed after the experts
+// are known, while the first weights stream in.
+
+// Float rank of every logit (ties to the lower index), split over tpl = 512 / X threads per logit
+// (lanes tpl*e .. tpl*e + tpl - 1). Thread `part` of a logit reads float4 groups part, part + tpl,
+// ... so the lanes of a warp hit different banks (contiguous spans per part would all map to the
+// same banks and serialise). lg is padded with -inf up to kLogitPad entries; t_cand[r] = the logit
+// of rank r for r <= K. Called by all consumer threads.
+constexpr int kLogitPad = 256;
+__device__ __forceinline__ void rank_candidates(const float *lg, int X, int K, int tid, int *t_cand) {
+    const int tpl = X <= 128 ? 4 : 2;
+    const int e = tid / tpl, part = tid % tpl;
+    const int n4 = (X + 4 * tpl - 1) / (4 * tpl);    // float4 groups per thread; 4 * tpl * n4 <= kLogitPad
+    int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
+    if (e < X) {
+        const float v = lg[e];
+        const float4 *l4 = reinterpret_cast<const float4 *>(lg);
+#pragma unroll 8
+        for (int q = 0; q < n4; q++) {
+            const int f = part + tpl * q;
+            const float4 u = l4[f];
+            const int jj = 4 * f;
+            r0 += (u.x > v) | ((u.x == v) & (jj + 0 < e));
+            r1 += (u.y > v) | ((u.y == v) & (jj + 1 < e));
+            r2 += (u.z > v) | ((u.z == v) & (jj + 2 < e));
+            r3 += (u.w > v) | ((u.w == v) & (jj + 3 < e));
         }
     }
-    if (warp == 0) {
-        const bool ok = __all_sync(0xffffffffu, wait_bounded(&bar, 0, &s_abort, err, ERR_ROUTER));
-        const int k = lane & 15;
-        const float *w = srow + k * PS, *x = sx + k * PS;
-        float acc = 0.0f;
-        int i = 0;
-        for (; i + 32 <= L; i += 32) {             // 8 loads of each operand in flight per batch
-            float4 w4[8], x4[8];
+    int rank = r0 + r1 + r2 + r3;
+    rank += __shfl_xor_sync(0xffffffffu, rank, 1);
+    if (tpl == 4) rank += __shfl_xor_sync(0xffffffffu, rank, 2);
+    if (e < X && part == 0 && rank <= K) t_cand[rank] = e;
+}
+
+// Warp 0: turns the float candidates into the reference's selection. Returns after s_sel holds
+// it (verified, or ranked exactly); route_weights then finishes the probabilities and weights.
+__device__ void route_select(const float *lg, int X, int K, const int *t_cand, int *s_sel, double *t_ex,
+                             double *t_pj, double &z) {
+    const int lane = threadIdx.x & 31;
+    const int nc = K < X ? K + 1 : K, nchk = K < X ? K : K - 1;
+    const double mx = (double)lg[t_cand[0]];        // the largest logit
+    bool exact = nc > 32;
+    if (!exact) {
+        const double ex = lane < nc ? exp((double)lg[t_cand[lane]] - mx) : 0.0;
+        const double nx = __shfl_down_sync(0xffffffffu, ex, 1);
+        // p_r > p_{r+1} is certain once ex_r > ex_{r+1} (1 + 2^-48) and ex_r is far from the
+        // subnormal range (then p = ex / z >= 2^-1008 is normal too): one division by z rounds
+        // by at most 2^-53 relative. NaN logits fail the test and take the exact path.
+        exact = __any_sync(0xffffffffu, (lane < nchk && !(ex > nx * (1.0 + 0x1p-48))) || (lane < nc && !(ex >= 0x1p-1000)));
+        if (!exact && lane < K) s_sel[lane] = t_cand[lane];
+    }
+    z = 0.0;                                        // z in topk_token's order (qms_moe.cuh)
+    if (!exact) return;
+    for (int b = 0; b < X; b += 32) {
+        const int e = b + lane;
+        const double x = e < X ? exp((double)lg[e] - mx) : 0.0;
+        if (e < X) t_ex[e] = x;
+        double zb = x;
 #pragma unroll
-            for (int q = 0; q < 8; q++) {
-                w4[q] = *reinterpret_cast<const float4 *>(w + i + 4 * q);
-                x4[q] = *reinterpret_cast<const float4 *>(x + i + 4 * q);
-            }
+        for (int o = 16; o > 0; o >>= 1) zb += __shfl_xor_sync(0xffffffffu, zb, o);
+        z += zb;
+    }
+    __syncwarp();
+    for (int e = lane; e < X; e += 32) t_ex[e] = t_ex[e] / z;   // probabilities
+    __syncwarp();
+    for (int e = lane; e < X; e += 32) {            // exact ranking of the doubles
+        const double p = t_ex[e];
+        int rk = 0;
+        for (int j = 0; j < e; j++) rk += t_ex[j] >= p;
+        for (int j = e + 1; j < X; j++) rk += t_ex[j] > p;
+        if (rk < K) {
+            s_sel[rk] = e;
+            t_pj[rk] = p;
+        }
+    }
+    z = -1.0;                                       // t_pj is final
+    __syncwarp();
+}
+
+// Warp 0, after route_select: the weights (float)(p_j / sum_j p_j), sum in selection order.
+__device__ void route_weights(const float *lg, int X, int K, const int *s_sel, double *t_pj, double z,
+                              float *s_w, int *sel, float *wts) {
+    const int lane = threadIdx.x & 31;
+    if (z >= 0.0) {                                 // verified selection: z and p_j still to come
+        const double mx = (double)lg[s_sel[0]];
+        for (int b = 0; b < X; b += 32) {
+            const int e = b + lane;
+            double zb = e < X ? exp((double)lg[e] - mx) : 0.0;
 #pragma unroll
-            for (int q = 0; q < 8; q++) {
-                acc = __fmaf_rn(w4[q].x, x4[q].x, acc);
-                acc = __fmaf_rn(w4[q].y, x4[q].y, acc);
-                acc = __fmaf_rn(w4[q].z, x4[q].z, acc);
-                acc = __fmaf_rn(w4[q].w, x4[q].w, acc);
-            }
+            for (int o = 16; o > 0; o >>= 1) zb += __shfl_xor_sync(0xffffffffu, zb, o);
+            z += zb;
         }
-        for (; i < L; i += 4) {
-            const float4 w4 = *reinterpret_cast<const float4 *>(w + i);
-            const float4 x4 = *reinterpret_cast<const float4 *>(x + i);
-            acc = __fmaf_rn(w4.x, x4.x, acc);
-            acc = __fmaf_rn(w4.y, x4.y, acc);
-            acc = __fmaf_rn(w4.z, x4.z, acc);
-            acc = __fmaf_rn(w4.w, x4.w, acc);
-        }
-        acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 8, 16));
-        acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4, 16));
-        acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2, 16));
-        acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1, 16));
-        if (lane == 0) {
-            logits[e] = ok ? acc : 0.0f;
-            s_last = atom_add_acq_rel(cnt, 1) == X - 1;   // publishes the logit, sees the others'
-        }
+        for (int t = lane; t < K; t += 32) t_pj[t] = exp((double)lg[s_sel[t]] - mx) / z;
+        __syncwarp();
     }
-    __syncthreads();
-    if (!s_last) return;
-    topk_token(logits, X, K, sel, wts, s_sel);
-    if (tid == 0) {
-        *cnt = 0;
-        const unsigned next = __ldcg(stamp) + 1;   // never 0: zeroed words are never current
-        *stamp = next ? next : 1;
+    for (int t = lane; t < K; t += 32) {
+        double ws = 0.0;
+        for (int j = 0; j < K; j++) ws += t_pj[j];
+        const float w = (float)(t_pj[t] / ws);
+        s_w[t] = w;
+        if (sel) sel[t] = s_sel[t];
+        if (wts) wts[t] = w;
     }
+    __syncwarp();
 }
 
 // ---- gate/up + SwiGLU + Q8, then down + combine, in one stream (batch 1) ------------------------
-struct FfnArgs {
-    const uint8_t *gu, *dn;
-    size_t gu_expert, dn_expert;
-    int nbE, nbF, F, E, K, nst;
-    const int8_t *xq_q;
-    const float *xq_d;
-    const int *xq_s;
-    unsigned long long *aq;               // [K*F/32 groups][10] flagged words: q (8 words), d, sum
-    unsigned long long *part_gu, *part_dn;
-    const int *sel;
-    const float *wts;
-    const float *resid;
+struct DecodeArgs {
+    const float *router_lm;               // [X][16][E/16]: element 16*i + k of a row at [k][i]
+    const float *xn, *resid;
     float *out;
-    const unsigned *stamp;                // this call's stamp, written by the router
+    const uint8_t *gu, *dn;               // staged experts
+    size_t gu_expert, dn_expert;
+    int nbE, nbF, F, E, K, X, nst;
+    unsigned long long *lgf;              // [X] flagged logits
+    unsigned long long *aq;               // [K*F/32 groups][10] flagged Q8 groups: q (8 words), d, sum
+    unsigned long long *part_gu, *part_dn;   // flagged partial sums of tiles split across CTAs
+    unsigned *stamps;                     // [G] per-CTA call stamps
+    float *logits;                        // optional outputs (NULL to skip): [X]
+    int *sel;                             // [K] (written by CTA 0)
+    float *wts;                           // [K] (written by CTA 0)
     int *err;
 };
 
@@ -371,27 +390,38 @@ __device__ __forceinline__ bool merge_partial(unsigned long long *part, int tile
 constexpr int kSumBufs = 4;        // tile-sum hand-off buffers between consumer and epilogue warps
 
 template <int SBG, int SBD>
-__global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs a) {
+__global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeArgs a) {
     constexpr uint32_t GBG = 8 * SBG * 18, STG = 8 * GBG, GBD = 8 * SBD * 18, STD = 8 * GBD;
     constexpr uint32_t SLOT = STG > STD ? STG : STD;
     constexpr int PG = SBG / 4 / kChunkWarps, RSG = 32 / SBG, PD = SBD / 4 / kChunkWarps, RSD = 32 / SBD;
     extern __shared__ __align__(128) uint8_t smem[];
-    const int nst = a.nst, K = a.K, F = a.F, nbE = a.nbE, nbF = a.nbF;
+    const int nst = a.nst, K = a.K, F = a.F, E = a.E, X = a.X, nbE = a.nbE, nbF = a.nbF;
     uint8_t *ring = smem;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)nst * SLOT);
     uint64_t *empty = full + nst;
     uint64_t *sfull = empty + nst;                                  // [kSumBufs] sums written
     uint64_t *sempty = sfull + kSumBufs;                            // [kSumBufs] sums consumed
-    int8_t *sxq = reinterpret_cast<int8_t *>(sempty + kSumBufs);   // [nbE*32]
+    uint64_t *rbar = sempty + kSumBufs;                             // router row landed
+    uint64_t *selbar = rbar + 1;                                    // experts chosen
+    int8_t *sxq = reinterpret_cast<int8_t *>(selbar + 1);          // [nbE*32] the token's Q8 row
     float *sxd = reinterpret_cast<float *>(sxq + nbE * 32);         // [nbE]
     int *sxs = reinterpret_cast<int *>(sxd + nbE);                  // [nbE], 8 * sum
     int8_t *saq = reinterpret_cast<int8_t *>(sxs + nbE);            // [K][F]
     float *sad = reinterpret_cast<float *>(saq + K * F);            // [K][nbF]
     int *sas = reinterpret_cast<int *>(sad + K * nbF);              // [K][nbF], 8 * sum
     float *sbuf = reinterpret_cast<float *>(sas + K * nbF);         // [kSumBufs][64] tile sums
+    float *slg = sbuf + kSumBufs * 64;                              // [kLogitPad] this call's logits
+    // routing scratch inside the ring, which carries no stage before the experts are known
+    const int L = E / 16, PS = L + 4;
+    float *srow = reinterpret_cast<float *>(ring);                  // [16][PS] router row, lane-major
+    float *sx = srow + 16 * PS;                                     // [16][PS] xn, lane-major
     __shared__ int s_abort;
     __shared__ const uint8_t *s_gu_base[8], *s_dn_base[8];   // producer: selected experts' weights
-    __shared__ float s_w[8];                                   // epilogue: routing weights
+    __shared__ int s_sel[64];
+    __shared__ float s_w[64];                                  // epilogue: routing weights
+    __shared__ uint32_t s_stamp;
+    __shared__ int t_cand[65];                                 // routing: float rank -> logit
+    __shared__ double t_ex[256], t_pj[64], s_z;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = gridDim.x, c = blockIdx.x;
     const int Sg = nbE / SBG, tps = F / 32, ntg = K * tps, Ug = ntg * Sg;
@@ -410,26 +440,31 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
             mbar_init(&sfull[i], kConsumerWarps);
             mbar_init(&sempty[i], 1);
         }
+        mbar_init(rbar, 1);
+        mbar_init(selbar, 1);
         fence_mbar_init();
+        if (c < X) {                                // router row c, lane-major, before the wait
+            mbar_arrive_expect_tx(rbar, (uint32_t)E * 4);
+            const uint64_t pol = evict_first_policy();
+            for (int k = 0; k < 16; k++)
+                bulk_load(srow + k * PS, a.router_lm + (size_t)c * E + (size_t)k * L, (uint32_t)L * 4, rbar, pol);
+        }
     }
     __syncthreads();
-    pdl_trigger();                                  // the next router may prefetch its weights
-    pdl_wait();                                     // selection and Q8 row come from the router
+    pdl_trigger();                                  // the next call's kernel may stage its router row
+    pdl_wait();                                     // xn comes from the previous kernel
     volatile int *abort_flag = &s_abort;
 
     if (warp == kConsumerWarps) {                   // ---- producer: one stream, gate/up then down
         if (lane == 0) {
+            bool ok = wait_bounded(selbar, 0, abort_flag, a.err, ERR_PRODUCER) && !*abort_flag;
             const uint64_t pol = evict_first_policy();
             // expert bases live in shared memory: a local array would sit in local memory, and
             // every load from it that misses L1 queues behind the stream in L2
-            for (int j = 0; j < 8; j++) {
-                const int e = j < K ? __ldcg(a.sel + j) : 0;
-                s_gu_base[j] = a.gu + (size_t)e * a.gu_expert;
-            }
-            for (int gi = 0; gi < 8; gi++) s_dn_base[gi] = a.dn + (size_t)__ldcg(a.sel + gi / RBE) * a.dn_expert;
+            for (int j = 0; j < 8; j++) s_gu_base[j] = a.gu + (size_t)(j < K ? s_sel[j] : 0) * a.gu_expert;
+            for (int gi = 0; gi < 8; gi++) s_dn_base[gi] = a.dn + (size_t)s_sel[gi / RBE] * a.dn_expert;
             Ring r(nst);
             int issued = 0;
-            bool ok = true;
             const Segs sg(ug0, ug1, Sg), sd(ud0, ud1, Sd);
             for (int k = 0; k < sg.n && ok; k++) {
                 int tile, s0, s1;
@@ -483,15 +518,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
     }
 
     if (warp == kConsumerWarps + 1) {               // ---- epilogue warp: SwiGLU/Q8, merges, combine
+        // first the routing weights (the combine needs them, the experts' gate/up does not)
+        bool ok = __all_sync(0xffffffffu, wait_bounded(selbar, 0, abort_flag, a.err, ERR_CONSUMER)) && !*abort_flag;
+        if (ok) route_weights(slg, X, K, s_sel, t_pj, s_z, s_w, c == 0 ? a.sel : nullptr, c == 0 ? a.wts : nullptr);
         Ring sr(kSumBufs);
-        bool ok = true;
-        const uint32_t stamp = __ldcg(a.stamp);
+        const uint32_t stamp = s_stamp;
         for (int pass = 0; pass < 2; pass++) {
             const bool gate = pass == 0;
             const int S = gate ? Sg : Sd, U = gate ? Ug : Ud;
             const Segs sq(gate ? ug0 : ud0, gate ? ug1 : ud1, S);
-            if (!gate && lane < 8) s_w[lane] = lane < K ? __ldcg(a.wts + lane) : 0.0f;
-            __syncwarp();
             for (int k = 0; k < sq.n; k++) {
                 int tile, s0, s1;
                 sq.get(k, tile, s0, s1);
@@ -537,19 +572,96 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
         return;
     }
 
-    // ---- consumers, phase A: gate/up
+    // ---- consumers: routing first (the producer and the epilogue wait for it)
     const int tid = threadIdx.x;
-    for (int i = tid; i < nbE * 2; i += kConsumerWarps * 32)
-        reinterpret_cast<int4 *>(sxq)[i] = __ldcg(reinterpret_cast<const int4 *>(a.xq_q) + i);
-    for (int i = tid; i < nbE; i += kConsumerWarps * 32) {
-        sxd[i] = __ldcg(a.xq_d + i);
-        sxs[i] = 8 * __ldcg(a.xq_s + i);
+    if (tid == 0) {
+        const unsigned next = __ldcg(a.stamps + c) + 1;   // never 0: zeroed words are never current
+        s_stamp = next ? next : 1;
+        a.stamps[c] = s_stamp;
+    }
+    for (int q = tid; q < E / 4; q += kConsumerWarps * 32) {
+        const float4 v = __ldcg(reinterpret_cast<const float4 *>(a.xn) + q);
+        const int j = 4 * q;
+        sx[((j + 0) & 15) * PS + ((j + 0) >> 4)] = v.x;
+        sx[((j + 1) & 15) * PS + ((j + 1) >> 4)] = v.y;
+        sx[((j + 2) & 15) * PS + ((j + 2) >> 4)] = v.z;
+        sx[((j + 3) & 15) * PS + ((j + 3) >> 4)] = v.w;
     }
     consumer_sync();
+    const uint32_t stamp = s_stamp;
+    bool ok = true;
+    if (warp == 0) {
+        if (c < X) {                                // logit c in qms_vec_dot_f32's exact order
+            ok = __all_sync(0xffffffffu, wait_bounded(rbar, 0, abort_flag, a.err, ERR_ROUTER));
+            const int k = lane & 15;
+            const float *w = srow + k * PS, *x = sx + k * PS;
+            float acc = 0.0f;
+            int i = 0;
+            for (; i + 32 <= L; i += 32) {         // 8 loads of each operand in flight per batch
+                float4 w4[8], x4[8];
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    w4[q] = *reinterpret_cast<const float4 *>(w + i + 4 * q);
+                    x4[q] = *reinterpret_cast<const float4 *>(x + i + 4 * q);
+                }
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    acc = __fmaf_rn(w4[q].x, x4[q].x, acc);
+                    acc = __fmaf_rn(w4[q].y, x4[q].y, acc);
+                    acc = __fmaf_rn(w4[q].z, x4[q].z, acc);
+                    acc = __fmaf_rn(w4[q].w, x4[q].w, acc);
+                }
+            }
+            for (; i < L; i += 4) {
+                const float4 w4 = *reinterpret_cast<const float4 *>(w + i);
+                const float4 x4 = *reinterpret_cast<const float4 *>(x + i);
+                acc = __fmaf_rn(w4.x, x4.x, acc);
+                acc = __fmaf_rn(w4.y, x4.y, acc);
+                acc = __fmaf_rn(w4.z, x4.z, acc);
+                acc = __fmaf_rn(w4.w, x4.w, acc);
+            }
+            acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 8, 16));
+            acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4, 16));
+            acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2, 16));
+            acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1, 16));
+            if (lane == 0 && ok) {
+                st_flagged(a.lgf + c, __float_as_uint(acc), stamp);
+                if (a.logits) a.logits[c] = acc;
+            }
+        }
+    } else {                                        // the token's Q8 row (src/kernels.c:34-53)
+        for (int b = warp - 1; b < nbE; b += kConsumerWarps - 1) {
+            const int j = b * 32 + lane;
+            const Q8Lane r = quantize_lane(sx[(j & 15) * PS + (j >> 4)]);
+            sxq[j] = (int8_t)r.q;
+            if (lane == 0) {
+                sxd[b] = r.d;
+                sxs[b] = 8 * r.sum;
+            }
+        }
+    }
+    if (tid < X) {                                  // every CTA's logit
+        unsigned long long v = ld_flagged(a.lgf + tid);
+        if (wait_flagged(a.lgf + tid, stamp, v, abort_flag, a.err, ERR_ROUTER)) slg[tid] = __uint_as_float((uint32_t)v);
+    } else if (tid < kLogitPad) {
+        slg[tid] = -INFINITY;                       // padding the rank loop may read
+    }
+    consumer_sync();
+    rank_candidates(slg, X, K, tid, t_cand);
+    consumer_sync();
+    if (warp == 0) {
+        double z = 0.0;
+        if (!*abort_flag) route_select(slg, X, K, t_cand, s_sel, t_ex, t_pj, z);
+        if (lane == 0) s_z = z;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(selbar);         // producer and epilogue may start (they check the abort flag)
+    }
+    ok = !*abort_flag;
+
+    // ---- consumers, phase A: gate/up
     const int g = warp / kChunkWarps, half = warp % kChunkWarps;   // chunk of the stage, row part
     Ring r(nst), sr(kSumBufs);
     int handed = 0;
-    bool ok = true;
     // hand a tile's 64 sums (8 per chunk) to the epilogue warp
     auto hand_off = [&](const float *acc, int P, int RS, int bl, int rs) {
         if (handed >= kSumBufs && ok)
@@ -597,7 +709,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
     // ---- phase B: gather every CTA's Q8 groups as they appear, then down + combine. Each thread
     // keeps all its words in flight and re-polls only the pending ones, one round trip per round.
     if (ok) {
-        const uint32_t stamp = __ldcg(a.stamp);
         const int nw = ntg * kAqWords;
         constexpr int kBatch = 8;
         for (int i0 = tid; i0 < nw && ok; i0 += kBatch * kConsumerWarps * 32) {
@@ -679,13 +790,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_stream_ffn(const FfnArgs 
 }
 
 // ---- host side -----------------------------------------------------------------------------------
-static uint32_t ffn_slot(const QmsCudaMoe *m) { return 8 * std::max(m->cgu.GB, m->cdn.GB); }
-static size_t ffn_fixed(const QmsCudaMoe *m) {
-    return 2 * kSumBufs * 8 + (size_t)m->nbE * 40 + (size_t)m->K * m->F + (size_t)m->K * m->nbF * 8 +
-           kSumBufs * 64 * 4;
+static uint32_t dec_slot(const QmsCudaMoe *m) { return 8 * std::max(m->cgu.GB, m->cdn.GB); }
+static size_t dec_fixed(const QmsCudaMoe *m) {
+    return (2 * kSumBufs + 2) * 8 + (size_t)m->nbE * 40 + (size_t)m->K * m->F + (size_t)m->K * m->nbF * 8 +
+           kSumBufs * 64 * 4 + (size_t)kLogitPad * 4;
 }
-static size_t ffn_smem(const QmsCudaMoe *m) { return (size_t)m->gu_nst * (ffn_slot(m) + 16) + ffn_fixed(m); }
-static size_t router_smem(int E) { return (size_t)2 * 16 * (E / 16 + 4) * 4; }
+static size_t dec_smem(const QmsCudaMoe *m) { return (size_t)m->gu_nst * (dec_slot(m) + 16) + dec_fixed(m); }
 
 static int max_segments(int U, int S, int G) {
     int worst = 1;
@@ -694,53 +804,53 @@ static int max_segments(int U, int S, int G) {
     return worst;
 }
 
-typedef void (*FfnKernel)(const FfnArgs);
-static FfnKernel ffn_kernel(const QmsCudaMoe *m) {
-    if (m->cgu.SB == 16) return m->cdn.SB == 16 ? k_stream_ffn<16, 16> : k_stream_ffn<16, 8>;
-    return m->cdn.SB == 16 ? k_stream_ffn<8, 16> : k_stream_ffn<8, 8>;
+typedef void (*DecodeKernel)(const DecodeArgs);
+static DecodeKernel dec_kernel(const QmsCudaMoe *m) {
+    if (m->cgu.SB == 16) return m->cdn.SB == 16 ? k_decode_bs1<16, 16> : k_decode_bs1<16, 8>;
+    return m->cdn.SB == 16 ? k_decode_bs1<8, 16> : k_decode_bs1<8, 8>;
 }
 
 int stream_prepare(QmsCudaMoe *m) {
     m->stream_ok = 0;
     if (!(m->K == 1 || m->K == 2 || m->K == 4 || m->K == 8) || m->X > 256 || 2 * m->X > m->E) return QMS_CUDA_OK;
     if (m->nbE % m->cgu.SB || m->nbF % m->cdn.SB) return QMS_CUDA_OK;
-    // the deepest ring that still leaves room for the next call's router CTA on the same SM
-    // (a multiple of the down stage width cdn.S, so a down stage never wraps around the ring)
-    const int fit = (int)std::min<size_t>(12, (kSmemOptIn - kRouterReserve - ffn_fixed(m)) / (ffn_slot(m) + 16));
+    const uint32_t slot = dec_slot(m);
+    cudaFuncAttributes fa;
+    QMS_CK(cudaFuncGetAttributes(&fa, dec_kernel(m)));
+    // the deepest ring that fits, a multiple of the down stage width cdn.S so a down stage never
+    // wraps around it; routing scratch (router row + xn, lane-major) lives in its first slots
+    const size_t avail = kSmemOptIn - fa.sharedSizeBytes - dec_fixed(m);
+    const int fit = (int)std::min<size_t>(QMS_STREAM_MAX_RING, avail / (slot + 16));
     m->gu_nst = fit / m->cdn.S * m->cdn.S;
     m->dn_nst = m->gu_nst;
     if (m->gu_nst < 4 || m->gu_nst < m->cdn.S) return QMS_CUDA_OK;
+    if ((size_t)2 * 16 * (m->E / 16 + 4) * 4 > (size_t)m->gu_nst * slot) return QMS_CUDA_OK;
     const int Ugu = m->K * (m->F / 32) * m->cgu.S, Udn = (m->E / (64 / m->K)) * m->cdn.S;
     if (max_segments(Ugu, m->cgu.S, m->nsm) > kMaxSegments || max_segments(Udn, m->cdn.S, m->nsm) > kMaxSegments)
         return QMS_CUDA_OK;
-    const FfnKernel fk = ffn_kernel(m);
-    QMS_CK(cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ffn_smem(m)));
-    QMS_CK(cudaFuncSetAttribute(k_router_bs1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router_smem(m->E)));
-    // one shared-memory carveout for both kernels: no L1/shared reconfiguration between them
-    QMS_CK(cudaFuncSetAttribute(fk, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-    QMS_CK(cudaFuncSetAttribute(k_router_bs1, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    const DecodeKernel dk = dec_kernel(m);
+    QMS_CK(cudaFuncSetAttribute(dk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dec_smem(m)));
+    QMS_CK(cudaFuncSetAttribute(dk, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     m->stream_ok = 1;
     return QMS_CUDA_OK;
 }
 
-int stream_scratch_sizes(const QmsCudaMoe *m, size_t *part_gu, size_t *part_dn, size_t *aq_flagged) {
+int stream_scratch_sizes(const QmsCudaMoe *m, StreamScratch *sz) {
     const int tiles_gu = m->K * (m->F / 32), tiles_dn = m->E / (64 / std::max(1, std::min(8, m->K)));
-    *part_gu = (size_t)tiles_gu * kMaxSegments * 64 * 8;
-    *part_dn = (size_t)tiles_dn * kMaxSegments * 64 * 8;
-    *aq_flagged = (size_t)tiles_gu * kAqWords * 8;
+    sz->lg_flagged = (size_t)m->X * 8;
+    sz->stamps = (size_t)m->nsm * 4;
+    sz->aq_flagged = (size_t)tiles_gu * kAqWords * 8;
+    sz->part_gu = (size_t)tiles_gu * kMaxSegments * 64 * 8;
+    sz->part_dn = (size_t)tiles_dn * kMaxSegments * 64 * 8;
     return QMS_CUDA_OK;
 }
 
 int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *resid, cudaStream_t s) {
-    if (m->timing) QMS_CK(cudaEventRecord(m->ev[0], s));
-    QMS_CK(launch_pdl(k_router_bs1, dim3(m->X), dim3(256), router_smem(m->E), s, (const float *)m->router_lm, m->X,
-                      m->E, xn, m->K, m->xq_q, m->xq_d, m->xq_s, m->logits, m->sel, m->wts, m->cnt, m->stamp,
-                      m->err));
-    if (m->timing) {
-        QMS_CK(cudaEventRecord(m->ev[1], s));
-        QMS_CK(cudaEventRecord(m->ev[2], s));
-    }
-    FfnArgs a;
+    DecodeArgs a;
+    a.router_lm = m->router_lm;
+    a.xn = xn;
+    a.resid = resid;
+    a.out = out;
     a.gu = m->gu;
     a.dn = m->dn;
     a.gu_expert = m->gu_expert;
@@ -750,20 +860,23 @@ int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *
     a.F = m->F;
     a.E = m->E;
     a.K = m->K;
+    a.X = m->X;
     a.nst = m->gu_nst;
-    a.xq_q = m->xq_q;
-    a.xq_d = m->xq_d;
-    a.xq_s = m->xq_s;
+    a.lgf = m->lg_flagged;
     a.aq = m->aq_flagged;
     a.part_gu = m->part_gu;
     a.part_dn = m->part_dn;
+    a.stamps = m->stamps;
+    a.logits = m->logits;
     a.sel = m->sel;
     a.wts = m->wts;
-    a.resid = resid;
-    a.out = out;
-    a.stamp = m->stamp;
     a.err = m->err;
-    QMS_CK(launch_pdl(ffn_kernel(m), dim3(m->nsm), dim3(kStreamThreads), ffn_smem(m), s, a));
+    if (m->timing) {
+        QMS_CK(cudaEventRecord(m->ev[0], s));
+        QMS_CK(cudaEventRecord(m->ev[1], s));
+        QMS_CK(cudaEventRecord(m->ev[2], s));
+    }
+    QMS_CK(launch_pdl(dec_kernel(m), dim3(m->nsm), dim3(kStreamThreads), dec_smem(m), s, a));
     if (m->timing) {
         QMS_CK(cudaEventRecord(m->ev[3], s));
         QMS_CK(cudaEventRecord(m->ev[4], s));

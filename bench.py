@@ -42,9 +42,10 @@ def bytes_per_token_layer(E=4096, X=128, K=8, F=1536) -> int:
     return K * expert + X * E * 4            # + F32 router
 
 
-def ffn_bytes_per_launch(E=4096, K=8, F=1536) -> int:
-    """Expert bytes one batch-1 call streams in k_stream_ffn: gate, up and down of K experts."""
-    return K * 3 * F * (E // 32) * 18
+def bytes_per_launch(E=4096, X=128, K=8, F=1536) -> int:
+    """Bytes one batch-1 call of k_decode_bs1 must read: the F32 router and the gate, up and down
+    weights of the K selected experts (the whole MoE block is one kernel)."""
+    return bytes_per_token_layer(E, X, K, F)
 
 
 def peaks() -> tuple[float, str]:
@@ -55,8 +56,8 @@ def peaks() -> tuple[float, str]:
 
 
 def profile_traffic() -> float | None:
-    """DRAM bytes per k_stream_ffn launch from the committed ncu summary, if present."""
-    p = ROOT / "profiles" / "k_stream_ffn_235b_bs1.md"
+    """DRAM bytes per k_decode_bs1 launch from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "k_decode_bs1_235b.md"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -301,7 +302,7 @@ def main():
             ksum[i] += kev[2 * i].elapsed_time(kev[2 * i + 1])
     kms = [s / nk for s in ksum]
     peak, peak_kind = peaks()
-    ffn_gbs = ffn_bytes_per_launch() / (kms[1] / 1e3) / 1e9
+    kern_gbs = bytes_per_launch() / (kms[1] / 1e3) / 1e9
 
     # end to end through the host-buffer entry point (pinned host memory, copies in the timed region)
     xh = torch.empty((a.tokens, E), dtype=torch.float32, pin_memory=True)
@@ -337,17 +338,18 @@ def main():
                        "us_per_token_layer": round(ms * 1e3 / (a.steps * a.tokens), 3),
                        "l2": f"inputs larger than L2 ({a.layers} layers x 1.36 GB resident)",
                        "graph": graph is not None, "parallelism": f"replicas x{world}"},
-            "roofline": {"bound": "hbm", "kernel": "k_stream_ffn", "achieved": round(ffn_gbs, 1), "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": "k_decode_bs1", "achieved": round(kern_gbs, 1), "peak": peak,
                          "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                         else "fallback", "unit": "GB/s", "frac": round(ffn_gbs / peak, 4),
-                         "traffic": traffic, "bytes_per_launch": ffn_bytes_per_launch(),
-                         "kernel_us": {"router_topk": round(kms[0] * 1e3, 2), "ffn": round(kms[1] * 1e3, 2)},
+                         else "fallback", "unit": "GB/s", "frac": round(kern_gbs / peak, 4),
+                         "traffic": traffic, "bytes_per_launch": bytes_per_launch(),
+                         "kernel_us": {"k_decode_bs1": round(kms[1] * 1e3, 2)},
+                         "timing": "launch alone, CUDA events on its stream (no overlap with the previous call)",
                          "op_frac": round(value / world / peak, 4)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": a.tokens * E * 4,
                     "d2h_bytes_per_step": a.tokens * E * 4,
-                    "note": "qms_cuda_moe_forward_host per token: copy in, 3 kernels, copy out, wait"},
-            "gpu_launches": 3 * a.tokens * a.steps,
+                    "note": "qms_cuda_moe_forward_host per token: copy in, 1 kernel, copy out, wait"},
+            "gpu_launches": a.tokens * a.steps,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

@@ -113,11 +113,11 @@ int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int 
 int qms_cuda_moe_status(QmsCudaMoe *m);
 
 /* Kernel timing hook: with events non-NULL (an array of 6 cudaEvent_t), every following forward
- * records events[2i] before and events[2i+1] after its stage i on the launch stream: stage 0 is
- * routing (router + top-k), stage 1 the expert products (gate/up + SwiGLU + down + combine in one
- * kernel for T == 1; gate/up alone otherwise) and stage 2 the separate down + combine kernel of
- * T > 1 (empty for T == 1). The events serialise the kernels (no programmatic overlap). NULL turns
- * the hook off. */
+ * records events[2i] before and events[2i+1] after its stage i on the launch stream. For T == 1
+ * the whole block is one kernel (routing, gate/up, SwiGLU, down, combine): it is stage 1, and
+ * stages 0 and 2 are empty. For T > 1 stage 0 is routing, stage 1 gate/up + SwiGLU and stage 2
+ * down + combine. The events serialise the kernels (no programmatic overlap). NULL turns the
+ * hook off. */
 int qms_cuda_moe_set_kernel_events(QmsCudaMoe *m, void **events);
 
 /* Same through host buffers (xn, out and the optional outputs in host memory): copies in,

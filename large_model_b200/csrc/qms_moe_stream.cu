@@ -249,25 +249,11 @@ __device__ __forceinline__ void rank_candidates(const float *lg, int X, int K, i
     if (e < X && part == 0 && rank <= K) t_cand[rank] = e;
 }
 
-// Warp 0: turns the float candidates into the reference's selection. Returns after s_sel holds
-// it (verified, or ranked exactly); route_weights then finishes the probabilities and weights.
-__device__ void route_select(const float *lg, int X, int K, const int *t_cand, int *s_sel, double *t_ex,
-                             double *t_pj, double &z) {
+// The exact ranking of the double probabilities (ties, underflow, NaN): cold, kept out of line.
+__device__ __noinline__ void route_exact(const float *lg, int X, int K, double mx, int *s_sel, double *t_ex,
+                                         double *t_pj, double &z) {
     const int lane = threadIdx.x & 31;
-    const int nc = K < X ? K + 1 : K, nchk = K < X ? K : K - 1;
-    const double mx = (double)lg[t_cand[0]];        // the largest logit
-    bool exact = nc > 32;
-    if (!exact) {
-        const double ex = lane < nc ? exp((double)lg[t_cand[lane]] - mx) : 0.0;
-        const double nx = __shfl_down_sync(0xffffffffu, ex, 1);
-        // p_r > p_{r+1} is certain once ex_r > ex_{r+1} (1 + 2^-48) and ex_r is far from the
-        // subnormal range (then p = ex / z >= 2^-1008 is normal too): one division by z rounds
-        // by at most 2^-53 relative. NaN logits fail the test and take the exact path.
-        exact = __any_sync(0xffffffffu, (lane < nchk && !(ex > nx * (1.0 + 0x1p-48))) || (lane < nc && !(ex >= 0x1p-1000)));
-        if (!exact && lane < K) s_sel[lane] = t_cand[lane];
-    }
     z = 0.0;                                        // z in topk_token's order (qms_moe.cuh)
-    if (!exact) return;
     for (int b = 0; b < X; b += 32) {
         const int e = b + lane;
         const double x = e < X ? exp((double)lg[e] - mx) : 0.0;
@@ -292,6 +278,27 @@ __device__ void route_select(const float *lg, int X, int K, const int *t_cand, i
     }
     z = -1.0;                                       // t_pj is final
     __syncwarp();
+}
+
+// Warp 0: turns the float candidates into the reference's selection. Returns after s_sel holds
+// it (verified, or ranked exactly); route_weights then finishes the probabilities and weights.
+__device__ void route_select(const float *lg, int X, int K, const int *t_cand, int *s_sel, double *t_ex,
+                             double *t_pj, double &z) {
+    const int lane = threadIdx.x & 31;
+    const int nc = K < X ? K + 1 : K, nchk = K < X ? K : K - 1;
+    const double mx = (double)lg[t_cand[0]];        // the largest logit
+    bool exact = nc > 32;
+    if (!exact) {
+        const double ex = lane < nc ? exp((double)lg[t_cand[lane]] - mx) : 0.0;
+        const double nx = __shfl_down_sync(0xffffffffu, ex, 1);
+        // p_r > p_{r+1} is certain once ex_r > ex_{r+1} (1 + 2^-48) and ex_r is far from the
+        // subnormal range (then p = ex / z >= 2^-1008 is normal too): one division by z rounds
+        // by at most 2^-53 relative. NaN logits fail the test and take the exact path.
+        exact = __any_sync(0xffffffffu, (lane < nchk && !(ex > nx * (1.0 + 0x1p-48))) || (lane < nc && !(ex >= 0x1p-1000)));
+        if (!exact && lane < K) s_sel[lane] = t_cand[lane];
+    }
+    z = 0.0;
+    if (exact) route_exact(lg, X, K, mx, s_sel, t_ex, t_pj, z);
 }
 
 // Warp 0, after route_select: the weights (float)(p_j / sum_j p_j), sum in selection order.

@@ -89,7 +89,8 @@ typedef struct QmsCudaMoe QmsCudaMoe;
 
 /* Upload (or copy from device) and repack one layer into HBM on the current device. The
  * source buffers are not retained. Replaces load_experts / load_mat for one layer
- * (src/model.c:133-157, 359-362). */
+ * (src/model.c:133-157, 359-362). Types: gate and up Q4_0; down Q4_0 or Q4_1 (the GGUF mixes
+ * that store ffn_down_exps one step wider); anything else is QMS_CUDA_EUNSUPPORTED. */
 int qms_cuda_moe_create(const QmsCudaMoeDesc *desc, QmsCudaMoe **out);
 void qms_cuda_moe_destroy(QmsCudaMoe *m);
 /* Bytes of device memory held by the layer (weights + scratch). */

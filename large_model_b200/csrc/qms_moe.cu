@@ -28,16 +28,17 @@ namespace qms {
 constexpr int kGateUpRows = 8;         // f values per gate/up CTA (one per warp)
 constexpr int kDownRows = 8;           // output rows per down CTA
 
-// ---- load-time repack: GGUF Q4_0 rows -> staged chunks -----------------------------------------
-// which = 0 / 1: gate / up rows of a stacked [X][F] tensor; which = 2: down rows of [X][E].
-__global__ void k_repack_q4_0(const uint8_t *__restrict__ src, int64_t nrows, int nb, int rows_per_expert,
-                              int which, Chunked c, uint8_t *__restrict__ dst, size_t expert_bytes) {
+// ---- load-time repack: GGUF Q4_0 / Q4_1 rows -> staged chunks ----------------------------------
+// which = 0 / 1: gate / up rows of a stacked [X][F] tensor; which = 2: down rows of [X][E]. A
+// Q4_1 block {d, m, qs[16]} keeps d in the scale plane and m in the min plane.
+__global__ void k_repack_q4(const uint8_t *__restrict__ src, int64_t nrows, int nb, int rows_per_expert,
+                            int which, Chunked c, uint8_t *__restrict__ dst, size_t expert_bytes) {
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= nrows * nb) return;
     const int64_t R = idx / nb;
     const int b = (int)(idx % nb);
     const int e = (int)(R / rows_per_expert), row = (int)(R % rows_per_expert);
-    const uint16_t *s = reinterpret_cast<const uint16_t *>(src + idx * 18);
+    const uint16_t *s = reinterpret_cast<const uint16_t *>(src + idx * (c.q1 ? 20 : 18)) + c.q1;
     const size_t chunk = which == 2 ? dn_chunk(c, row, b) : gu_chunk(c, row, which, b);
     const int rr = which == 2 ? (row & 7) : ((which * 32 + (row & 31)) & 7);
     uint8_t *cp = dst + (size_t)e * expert_bytes + chunk * c.GB;
@@ -47,7 +48,8 @@ __global__ void k_repack_q4_0(const uint8_t *__restrict__ src, int64_t nrows, in
     v.z = (uint32_t)s[5] | ((uint32_t)s[6] << 16);
     v.w = (uint32_t)s[7] | ((uint32_t)s[8] << 16);
     *reinterpret_cast<uint4 *>(cp + chunk_nib_off(c.SB, rr, b % c.SB)) = v;
-    *reinterpret_cast<uint16_t *>(cp + chunk_scale_off(c.SB, rr, b % c.SB)) = s[0];
+    *reinterpret_cast<uint16_t *>(cp + chunk_scale_off(c.SB, rr, b % c.SB)) = s[-c.q1];
+    if (c.q1) *reinterpret_cast<uint16_t *>(cp + chunk_min_off(c.SB, rr, b % c.SB)) = s[0];
 }
 
 // ---- router: quantise xn, logits, (last CTA) top-k --------------------------------------------
@@ -213,7 +215,7 @@ __global__ void __launch_bounds__(256) k_moe_down(const uint8_t *__restrict__ dn
                     xa0[i] = __ldcg(reinterpret_cast<const int4 *>(a));
                     xa1[i] = __ldcg(reinterpret_cast<const int4 *>(a + 16));
                     xd[i] = __ldcg(aq_d + (size_t)slot * nbF + b);
-                    xs8[i] = 8 * __ldcg(aq_s + (size_t)slot * nbF + b);
+                    xs8[i] = __ldcg(aq_s + (size_t)slot * nbF + b);   // block sum
                 }
             }
         }
@@ -229,7 +231,13 @@ __global__ void __launch_bounds__(256) k_moe_down(const uint8_t *__restrict__ dn
                 const int bl = b % c.SB;
                 const uint4 nib = ld_stream16(ch + chunk_nib_off(c.SB, row & 7, bl));
                 const float dw = h2f(ld_stream2(ch + chunk_scale_off(c.SB, row & 7, bl)));
-                acc = fmaf((float)(q4_block_isum(nib, xa0[i], xa1[i]) - xs8[i]), dw * xd[i], acc);
+                if (c.q1) {                         // d q + m: d dx isum + m ds (src/kernels.c:109-121)
+                    const float mw = h2f(ld_stream2(ch + chunk_min_off(c.SB, row & 7, bl)));
+                    acc = fmaf((float)q4_block_isum(nib, xa0[i], xa1[i]), dw * xd[i], acc);
+                    acc = fmaf(mw, xd[i] * (float)xs8[i], acc);
+                } else {                            // d (q - 8): the -8 folded into the block sum
+                    acc = fmaf((float)(q4_block_isum(nib, xa0[i], xa1[i]) - 8 * xs8[i]), dw * xd[i], acc);
+                }
             }
         }
         acc = warp_sum(acc);
@@ -263,9 +271,9 @@ static int ensure_device(int dev) {
     return QMS_CUDA_OK;
 }
 
-static int upload_q4_0(const void *src, int on_device, int64_t nrows, int nb, int rows_per_expert, int which,
-                       Chunked c, uint8_t *dst, size_t expert_bytes) {
-    const size_t bytes = (size_t)nrows * nb * 18;
+static int upload_q4(const void *src, int on_device, int64_t nrows, int nb, int rows_per_expert, int which,
+                     Chunked c, uint8_t *dst, size_t expert_bytes) {
+    const size_t bytes = (size_t)nrows * nb * (c.q1 ? 20 : 18);
     const uint8_t *dsrc = (const uint8_t *)src;
     uint8_t *tmp = nullptr;
     if (!on_device) {
@@ -283,8 +291,8 @@ static int upload_q4_0(const void *src, int on_device, int64_t nrows, int nb, in
         dsrc = tmp;
     }
     const int64_t n = nrows * nb;
-    k_repack_q4_0<<<(unsigned)((n + 255) / 256), 256>>>(dsrc, nrows, nb, rows_per_expert, which, c, dst,
-                                                        expert_bytes);
+    k_repack_q4<<<(unsigned)((n + 255) / 256), 256>>>(dsrc, nrows, nb, rows_per_expert, which, c, dst,
+                                                      expert_bytes);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (tmp) cudaFree(tmp);
@@ -328,9 +336,10 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
                 "moe_create: n_embd %% 256 and n_ff %% 32 must be 0 (integer fast path)");
     QMS_REQUIRE(F % 256 == 0, QMS_CUDA_EUNSUPPORTED,
                 "moe_create: n_ff %% 256 must be 0 (staged expert layout; all Qwen3-MoE shapes qualify)");
-    QMS_REQUIRE(d->gate_type == QMS_T_Q4_0 && d->up_type == QMS_T_Q4_0 && d->down_type == QMS_T_Q4_0,
-                QMS_CUDA_EUNSUPPORTED, "moe_create: expert types %d/%d/%d not supported (Q4_0)", d->gate_type,
-                d->up_type, d->down_type);
+    QMS_REQUIRE(d->gate_type == QMS_T_Q4_0 && d->up_type == QMS_T_Q4_0 &&
+                    (d->down_type == QMS_T_Q4_0 || d->down_type == QMS_T_Q4_1),
+                QMS_CUDA_EUNSUPPORTED, "moe_create: expert types %d/%d/%d not supported (Q4_0 gate/up, Q4_0 or Q4_1 down)",
+                d->gate_type, d->up_type, d->down_type);
     QMS_REQUIRE(E <= 4096 && F <= 2048 && X <= 256 && K <= 64 && 2 * X <= E, QMS_CUDA_EUNSUPPORTED,
                 "moe_create: n_embd <= 4096, n_ff <= 2048, n_expert <= min(256, n_embd/2), n_used <= 64 required");
     int dev = 0;
@@ -343,9 +352,9 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
     m->nbE = E / 32; m->nbF = F / 32;
     m->gate_type = d->gate_type; m->up_type = d->up_type; m->down_type = d->down_type;
     m->cgu = make_chunked(m->nbE);
-    m->cdn = make_chunked(m->nbF);
+    m->cdn = make_chunked(m->nbF, d->down_type == QMS_T_Q4_1);
     m->gu_expert = (size_t)2 * F * m->nbE * 18;
-    m->dn_expert = (size_t)E * m->nbF * 18;
+    m->dn_expert = (size_t)E * m->nbF * (m->cdn.q1 ? 20 : 18);
     const size_t rb = (size_t)X * E * 4, gb = m->gu_expert * X, db = m->dn_expert * X;
     m->weight_bytes = rb + gb + db;
     if (cudaMalloc(&m->router, rb) != cudaSuccess || cudaMalloc(&m->router_lm, rb) != cudaSuccess ||
@@ -369,11 +378,11 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
         }
     }
     if (rc == QMS_CUDA_OK)
-        rc = upload_q4_0(d->gate, d->src_on_device, (int64_t)X * F, m->nbE, F, 0, m->cgu, m->gu, m->gu_expert);
+        rc = upload_q4(d->gate, d->src_on_device, (int64_t)X * F, m->nbE, F, 0, m->cgu, m->gu, m->gu_expert);
     if (rc == QMS_CUDA_OK)
-        rc = upload_q4_0(d->up, d->src_on_device, (int64_t)X * F, m->nbE, F, 1, m->cgu, m->gu, m->gu_expert);
+        rc = upload_q4(d->up, d->src_on_device, (int64_t)X * F, m->nbE, F, 1, m->cgu, m->gu, m->gu_expert);
     if (rc == QMS_CUDA_OK)
-        rc = upload_q4_0(d->down, d->src_on_device, (int64_t)X * E, m->nbF, E, 2, m->cdn, m->dn, m->dn_expert);
+        rc = upload_q4(d->down, d->src_on_device, (int64_t)X * E, m->nbF, E, 2, m->cdn, m->dn, m->dn_expert);
     if (rc == QMS_CUDA_OK) rc = stream_prepare(m);
     if (rc != QMS_CUDA_OK) {
         qms_cuda_moe_destroy(m);

@@ -21,14 +21,16 @@ namespace qms {
 struct Chunked {
     int SB;        // blocks per chunk row
     int S;         // chunks along one row (nb / SB)
+    int q1;        // 1: Q4_1 blocks (a min plane follows the scale plane), 0: Q4_0
     uint32_t GB;   // chunk bytes
 };
 
-__host__ __device__ inline Chunked make_chunked(int nb) {
+__host__ __device__ inline Chunked make_chunked(int nb, int q1 = 0) {
     Chunked c;
     c.SB = nb % 16 == 0 ? 16 : 8;
     c.S = nb / c.SB;
-    c.GB = (uint32_t)(8 * c.SB * 18);
+    c.q1 = q1;
+    c.GB = (uint32_t)(8 * c.SB * (q1 ? 20 : 18));
     return c;
 }
 
@@ -46,6 +48,10 @@ __host__ __device__ inline size_t dn_chunk(const Chunked &c, int i, int b) {
 __host__ __device__ inline uint32_t chunk_nib_off(int SB, int rr, int bl) { return (uint32_t)(rr * SB + bl) * 16; }
 __host__ __device__ inline uint32_t chunk_scale_off(int SB, int rr, int bl) {
     return (uint32_t)(8 * SB * 16 + (rr * SB + bl) * 2);
+}
+// Q4_1 chunks: the fp16 min m of block (rr, bl), after the scale plane
+__host__ __device__ inline uint32_t chunk_min_off(int SB, int rr, int bl) {
+    return (uint32_t)(8 * SB * 18 + (rr * SB + bl) * 2);
 }
 
 constexpr int kTopkInRouterMaxT = 4;   // above this, k_moe_topk runs one CTA per token

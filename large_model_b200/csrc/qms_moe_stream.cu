@@ -206,6 +206,28 @@ __device__ __forceinline__ void chunk_dot(const uint8_t *chunk, const int8_t *xq
     }
 }
 
+// The same for Q4_1 chunks (value d q + m): d dx isum + m ds with ds = dx * (float)sum, the
+// activation block's sum term of src/kernels.c:109-121; xs holds the plain block sums.
+template <int SB>
+__device__ __forceinline__ void chunk_dot_q41(const uint8_t *chunk, const int8_t *xq, const float *xd, const int *xs,
+                                              int s, int bl, int rs, int r0, float (&acc)[SB / 4 / kChunkWarps]) {
+    constexpr int P = SB / 4 / kChunkWarps, RSTEP = 32 / SB;
+    const int b = s * SB + bl;
+    const int4 xa0 = *reinterpret_cast<const int4 *>(xq + b * 32);
+    const int4 xa1 = *reinterpret_cast<const int4 *>(xq + b * 32 + 16);
+    const float d = xd[b];
+    const float ds = d * (float)xs[b];
+#pragma unroll
+    for (int p = 0; p < P; p++) {
+        const int rr = rs + (r0 + p) * RSTEP;
+        const uint4 nib = *reinterpret_cast<const uint4 *>(chunk + chunk_nib_off(SB, rr, bl));
+        const float dw = h2f(*reinterpret_cast<const uint16_t *>(chunk + chunk_scale_off(SB, rr, bl)));
+        const float mw = h2f(*reinterpret_cast<const uint16_t *>(chunk + chunk_min_off(SB, rr, bl)));
+        acc[p] = fmaf((float)q4_block_isum(nib, xa0, xa1), dw * d, acc[p]);
+        acc[p] = fmaf(mw, ds, acc[p]);
+    }
+}
+
 // ---- routing inside the decode kernel -----------------------------------------------------------
 // The reference (src/model.c:1045-1064) takes prob[e] = exp((double)l_e - max) / z in double,
 // picks the top k by repeated strict-'>' argmax over prob (ties, including probabilities that
@@ -396,9 +418,10 @@ __device__ __forceinline__ bool merge_partial(unsigned long long *part, int tile
 
 constexpr int kSumBufs = 4;        // tile-sum hand-off buffers between consumer and epilogue warps
 
-template <int SBG, int SBD>
+template <int SBG, int SBD, int DQ1>
 __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeArgs a) {
-    constexpr uint32_t GBG = 8 * SBG * 18, STG = 8 * GBG, GBD = 8 * SBD * 18, STD = 8 * GBD;
+    // DQ1: down weights are Q4_1 (chunks carry a min plane), else Q4_0
+    constexpr uint32_t GBG = 8 * SBG * 18, STG = 8 * GBG, GBD = 8 * SBD * (DQ1 ? 20 : 18), STD = 8 * GBD;
     constexpr uint32_t SLOT = STG > STD ? STG : STD;
     constexpr int PG = SBG / 4 / kChunkWarps, RSG = 32 / SBG, PD = SBD / 4 / kChunkWarps, RSD = 32 / SBD;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -759,7 +782,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
                 const uint32_t d = (uint32_t)v[b];
                 if (w < 8) reinterpret_cast<uint32_t *>(saq)[gi * 8 + w] = d;
                 else if (w == 8) sad[gi] = __uint_as_float(d);
-                else sas[gi] = 8 * (int)d;
+                else sas[gi] = DQ1 ? (int)d : 8 * (int)d;   // block sum (Q4_1) or 8 x it (Q4_0)
             }
         }
     }
@@ -781,7 +804,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
             if (ok) {
                 const uint8_t *chunk = ring + (size_t)r.slot * SLOT + g * WSD;   // [chunk][stage s0..s1]
                 for (int s = s0; s < s1; s++)
-                    chunk_dot<SBD>(chunk + (s - s0) * GBD, xq, xdv, xsv, s, bl, rs, half * PD, acc);
+                    if (DQ1) chunk_dot_q41<SBD>(chunk + (s - s0) * GBD, xq, xdv, xsv, s, bl, rs, half * PD, acc);
+                    else chunk_dot<SBD>(chunk + (s - s0) * GBD, xq, xdv, xsv, s, bl, rs, half * PD, acc);
                 __syncwarp();
                 if (lane == 0)
                     for (int q = 0; q < Sd; q++) mbar_arrive(&empty[r.slot + q]);
@@ -813,8 +837,12 @@ static int max_segments(int U, int S, int G) {
 
 typedef void (*DecodeKernel)(const DecodeArgs);
 static DecodeKernel dec_kernel(const QmsCudaMoe *m) {
-    if (m->cgu.SB == 16) return m->cdn.SB == 16 ? k_decode_bs1<16, 16> : k_decode_bs1<16, 8>;
-    return m->cdn.SB == 16 ? k_decode_bs1<8, 16> : k_decode_bs1<8, 8>;
+    if (m->cdn.q1) {
+        if (m->cgu.SB == 16) return m->cdn.SB == 16 ? k_decode_bs1<16, 16, 1> : k_decode_bs1<16, 8, 1>;
+        return m->cdn.SB == 16 ? k_decode_bs1<8, 16, 1> : k_decode_bs1<8, 8, 1>;
+    }
+    if (m->cgu.SB == 16) return m->cdn.SB == 16 ? k_decode_bs1<16, 16, 0> : k_decode_bs1<16, 8, 0>;
+    return m->cdn.SB == 16 ? k_decode_bs1<8, 16, 0> : k_decode_bs1<8, 8, 0>;
 }
 
 int stream_prepare(QmsCudaMoe *m) {

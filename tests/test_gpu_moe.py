@@ -55,6 +55,17 @@ def test_moe_matches_oracle(cuda, oracle, shape, T):
     m.close()
 
 
+@pytest.mark.parametrize("shape,T", [("tiny", 1), ("tiny", 7), ("30b", 1), ("30b", 4),
+                                     ("235b", 1), ("235b", 6)])
+def test_moe_q4_1_down_matches_oracle(cuda, oracle, shape, T):
+    """ffn_down_exps stored as Q4_1 (per-block scale and minimum), batch 1 and batched kernels."""
+    layer = synth.make_moe_layer(shape, seed=71 + T, down_type=synth.T_Q4_1)
+    xn = synth.make_hidden(layer.n_embd, T, seed=81 + T)
+    m, out, sel, w, logits = _run(cuda, layer, xn)
+    _check(oracle, layer, xn, out, sel, w, logits, f"q4_1 {shape} T={T}")
+    m.close()
+
+
 def test_moe_golden_reference(cuda, golden):
     """Against outputs produced by the reference's own moe() (tests/golden)."""
     for name, (layer, xn) in cases.moe_cases().items():

@@ -109,6 +109,18 @@ def test_oracle_matches_reference_live(oracle, reference):
     assert oracle.quantize_q8(x).tobytes() == reference.quantize_q8(x).tobytes()
 
 
+def test_oracle_matches_reference_q4_1_down(oracle, reference):
+    """Q4_1 ffn_down_exps (src/kernels.c:109-121 dot, d*q + m blocks) bit-exact against the reference."""
+    from large_model_b200 import synth
+    for shape, T, seed in (("tiny", 5, 61), ("30b", 1, 62)):
+        layer = synth.make_moe_layer(shape, seed=seed, down_type=synth.T_Q4_1)
+        xn = synth.make_hidden(layer.n_embd, T, seed=seed + 100)
+        out, sel, _, _ = oracle.moe(layer, xn)
+        ref_out, trace = reference.moe(layer, xn, trace=True)
+        assert np.array_equal(out.view(np.uint32), ref_out.view(np.uint32)), (shape, rel_l2(out, ref_out))
+        assert sorted(set(sel.ravel().tolist())) == trace.tolist()
+
+
 def test_moe_rejects_non_fast_shapes(oracle):
     from large_model_b200 import synth
     layer = synth.make_moe_layer((288, 4, 2, 64), seed=1)   # 288 % 256 != 0: reference uses exact math

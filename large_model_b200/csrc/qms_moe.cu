@@ -10,10 +10,10 @@
 //   k_moe_gate_up  one warp per (slot, f): gate row f and up row f of the slot's expert against
 //                  the token's Q8 row (phase 1, :979-988), a = silu(g) * u (:994); the CTA that
 //                  completes a 32-row group re-quantises it to Q8 (phase 2, :995).
-//   k_moe_down     one CTA per (token, 8 output rows): down rows of all n_used experts
+//   k_moe_down     one CTA per (token, 32 output rows): down rows of all n_used experts
 //                  (phase 3, :998-1005), then the weighted sum in selection order with one
 //                  fused multiply-add per expert (:1152-1162), plus the optional residual.
-// Expert weights are repacked at load into the staged chunk layout of qms_moe.cuh.
+// Expert weights are repacked at load into the staged layouts of qms_moe.cuh.
 #include <string.h>
 
 #include <algorithm>
@@ -26,30 +26,48 @@ using namespace qms;
 namespace qms {
 
 constexpr int kGateUpRows = 8;         // f values per gate/up CTA (one per warp)
-constexpr int kDownRows = 8;           // output rows per down CTA
+constexpr int kDownRows = 32;          // output rows per down CTA (one per lane)
 
-// ---- load-time repack: GGUF Q4_0 / Q4_1 rows -> staged chunks ----------------------------------
-// which = 0 / 1: gate / up rows of a stacked [X][F] tensor; which = 2: down rows of [X][E]. A
-// Q4_1 block {d, m, qs[16]} keeps d in the scale plane and m in the min plane.
-__global__ void k_repack_q4(const uint8_t *__restrict__ src, int64_t nrows, int nb, int rows_per_expert,
-                            int which, Chunked c, uint8_t *__restrict__ dst, size_t expert_bytes) {
+// ---- load-time repack: GGUF rows -> staged layouts (qms_moe.cuh) --------------------------------
+// gate (which 0) / up (which 1) Q4_0 rows of a stacked [X][F] tensor -> chunks
+__global__ void k_repack_gu(const uint8_t *__restrict__ src, int64_t nrows, int nb, int F, int which, Chunked c,
+                            uint8_t *__restrict__ dst, size_t expert_bytes) {
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= nrows * nb) return;
     const int64_t R = idx / nb;
     const int b = (int)(idx % nb);
-    const int e = (int)(R / rows_per_expert), row = (int)(R % rows_per_expert);
-    const uint16_t *s = reinterpret_cast<const uint16_t *>(src + idx * (c.q1 ? 20 : 18)) + c.q1;
-    const size_t chunk = which == 2 ? dn_chunk(c, row, b) : gu_chunk(c, row, which, b);
-    const int rr = which == 2 ? (row & 7) : ((which * 32 + (row & 31)) & 7);
-    uint8_t *cp = dst + (size_t)e * expert_bytes + chunk * c.GB;
+    const int e = (int)(R / F), row = (int)(R % F);
+    const uint16_t *s = reinterpret_cast<const uint16_t *>(src + idx * 18);
+    const int rr = (which * 32 + (row & 31)) & 7;
+    uint8_t *cp = dst + (size_t)e * expert_bytes + gu_chunk(c, row, which, b) * c.GB;
     uint4 v;
     v.x = (uint32_t)s[1] | ((uint32_t)s[2] << 16);
     v.y = (uint32_t)s[3] | ((uint32_t)s[4] << 16);
     v.z = (uint32_t)s[5] | ((uint32_t)s[6] << 16);
     v.w = (uint32_t)s[7] | ((uint32_t)s[8] << 16);
     *reinterpret_cast<uint4 *>(cp + chunk_nib_off(c.SB, rr, b % c.SB)) = v;
-    *reinterpret_cast<uint16_t *>(cp + chunk_scale_off(c.SB, rr, b % c.SB)) = s[-c.q1];
-    if (c.q1) *reinterpret_cast<uint16_t *>(cp + chunk_min_off(c.SB, rr, b % c.SB)) = s[0];
+    *reinterpret_cast<uint16_t *>(cp + chunk_scale_off(c.SB, rr, b % c.SB)) = s[0];
+}
+
+// down Q4_0 / Q4_1 rows of a stacked [X][E] tensor -> column stages; a Q4_1 block {d, m, qs[16]}
+// keeps d in the scale plane and m in the min plane
+__global__ void k_repack_dn(const uint8_t *__restrict__ src, int64_t nrows, int nb, int E, DnCols d,
+                            uint8_t *__restrict__ dst, size_t expert_bytes) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= nrows * nb) return;
+    const int64_t R = idx / nb;
+    const int b = (int)(idx % nb);
+    const int e = (int)(R / E), row = (int)(R % E);
+    const uint16_t *s = reinterpret_cast<const uint16_t *>(src + idx * (d.q1 ? 20 : 18)) + d.q1;
+    uint8_t *sp = dst + (size_t)e * expert_bytes + dn_stage_off(d, b, row);
+    uint4 v;
+    v.x = (uint32_t)s[1] | ((uint32_t)s[2] << 16);
+    v.y = (uint32_t)s[3] | ((uint32_t)s[4] << 16);
+    v.z = (uint32_t)s[5] | ((uint32_t)s[6] << 16);
+    v.w = (uint32_t)s[7] | ((uint32_t)s[8] << 16);
+    *reinterpret_cast<uint4 *>(sp + dn_nib_off(d, row)) = v;
+    *reinterpret_cast<uint16_t *>(sp + dn_scale_off(d, row)) = s[-d.q1];
+    if (d.q1) *reinterpret_cast<uint16_t *>(sp + dn_min_off(d, row)) = s[0];
 }
 
 // ---- router: quantise xn, logits, (last CTA) top-k --------------------------------------------
@@ -187,61 +205,51 @@ __global__ void __launch_bounds__(256) k_moe_gate_up(const uint8_t *__restrict__
 }
 
 // ---- down + weighted combine (+ residual), any T ----------------------------------------------
-template <int NBL>
-__global__ void __launch_bounds__(256) k_moe_down(const uint8_t *__restrict__ dn, size_t dn_expert, Chunked c,
+// One CTA per (kDownRows output rows, token): warp k computes those rows of expert slot k (lane =
+// row), blocks in order, reading 512 contiguous bytes of nibbles per block from the column
+// stages; the token's K Q8 activation rows are staged in shared memory first.
+__global__ void __launch_bounds__(256) k_moe_down(const uint8_t *__restrict__ dn, size_t dn_expert, DnCols dc,
                                                   int nbF, int E, int K, const int8_t *__restrict__ aq_q,
                                                   const float *__restrict__ aq_d, const int *__restrict__ aq_s,
                                                   const int *__restrict__ sel, const float *__restrict__ wts,
                                                   const float *resid, float *out) {
-    extern __shared__ float sdn[];   // [K][kDownRows]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i0 = blockIdx.x * kDownRows, t = blockIdx.y;
-    const int F = nbF * 32;
+    extern __shared__ __align__(16) uint8_t sdm[];
+    const int F = nbF * 32, t = blockIdx.y, i0 = blockIdx.x * kDownRows;
+    int8_t *sq = reinterpret_cast<int8_t *>(sdm);                   // [K][F]
+    float *sd = reinterpret_cast<float *>(sdm + (size_t)K * F);     // [K][nbF]
+    int *ss = reinterpret_cast<int *>(sd + K * nbF);                // [K][nbF] block sums
+    float *sdn = reinterpret_cast<float *>(ss + K * nbF);           // [K][kDownRows]
     pdl_wait();
-    int cur = -1;
-    int4 xa0[NBL], xa1[NBL];
-    float xd[NBL];
-    int xs8[NBL];
-    for (int p = warp; p < K * kDownRows; p += 8) {
-        const int k = p % K, r = p / K;
-        const int slot = t * K + k;
-        if (k != cur) {
-            cur = k;
-#pragma unroll
-            for (int i = 0; i < NBL; i++) {
-                const int b = lane + 32 * i;
-                if (b < nbF) {
-                    const int8_t *a = aq_q + (size_t)slot * F + b * 32;
-                    xa0[i] = __ldcg(reinterpret_cast<const int4 *>(a));
-                    xa1[i] = __ldcg(reinterpret_cast<const int4 *>(a + 16));
-                    xd[i] = __ldcg(aq_d + (size_t)slot * nbF + b);
-                    xs8[i] = __ldcg(aq_s + (size_t)slot * nbF + b);   // block sum
-                }
-            }
-        }
-        const int e = __ldcg(sel + slot);
-        const int row = i0 + r;
-        const uint8_t *de = dn + (size_t)e * dn_expert;
+    const int4 *gq = reinterpret_cast<const int4 *>(aq_q + (size_t)t * K * F);
+    for (int i = threadIdx.x; i < K * F / 16; i += blockDim.x) reinterpret_cast<int4 *>(sq)[i] = __ldcg(gq + i);
+    for (int i = threadIdx.x; i < K * nbF; i += blockDim.x) {
+        sd[i] = __ldcg(aq_d + (size_t)t * K * nbF + i);
+        ss[i] = __ldcg(aq_s + (size_t)t * K * nbF + i);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = i0 + lane;
+    for (int k = warp; k < K; k += blockDim.x >> 5) {
+        const uint8_t *de = dn + (size_t)__ldcg(sel + t * K + k) * dn_expert;
+        const int8_t *xq = sq + (size_t)k * F;
         float acc = 0.0f;
-#pragma unroll
-        for (int i = 0; i < NBL; i++) {
-            const int b = lane + 32 * i;
-            if (b < nbF) {
-                const uint8_t *ch = de + dn_chunk(c, row, b) * c.GB;
-                const int bl = b % c.SB;
-                const uint4 nib = ld_stream16(ch + chunk_nib_off(c.SB, row & 7, bl));
-                const float dw = h2f(ld_stream2(ch + chunk_scale_off(c.SB, row & 7, bl)));
-                if (c.q1) {                         // d q + m: d dx isum + m ds (src/kernels.c:109-121)
-                    const float mw = h2f(ld_stream2(ch + chunk_min_off(c.SB, row & 7, bl)));
-                    acc = fmaf((float)q4_block_isum(nib, xa0[i], xa1[i]), dw * xd[i], acc);
-                    acc = fmaf(mw, xd[i] * (float)xs8[i], acc);
-                } else {                            // d (q - 8): the -8 folded into the block sum
-                    acc = fmaf((float)(q4_block_isum(nib, xa0[i], xa1[i]) - 8 * xs8[i]), dw * xd[i], acc);
-                }
+#pragma unroll 4
+        for (int b = 0; b < nbF; b++) {
+            const uint8_t *st = de + dn_stage_off(dc, b, row);
+            const uint4 nib = ld_stream16(st + dn_nib_off(dc, row));
+            const float dw = h2f(ld_stream2(st + dn_scale_off(dc, row)));
+            const int4 xa0 = *reinterpret_cast<const int4 *>(xq + b * 32);
+            const int4 xa1 = *reinterpret_cast<const int4 *>(xq + b * 32 + 16);
+            const float xd = sd[k * nbF + b];
+            const int xs = ss[k * nbF + b];
+            if (dc.q1) {                            // d q + m: d dx isum + m ds (src/kernels.c:109-121)
+                const float mw = h2f(ld_stream2(st + dn_min_off(dc, row)));
+                acc = fmaf((float)q4_block_isum(nib, xa0, xa1), dw * xd, acc);
+                acc = fmaf(mw, xd * (float)xs, acc);
+            } else {                                // d (q - 8): the -8 folded into the block sum
+                acc = fmaf((float)(q4_block_isum(nib, xa0, xa1) - 8 * xs), dw * xd, acc);
             }
         }
-        acc = warp_sum(acc);
-        if (lane == 0) sdn[k * kDownRows + r] = acc;
+        sdn[k * kDownRows + lane] = acc;
     }
     __syncthreads();
     if (threadIdx.x < kDownRows) {
@@ -251,6 +259,10 @@ __global__ void __launch_bounds__(256) k_moe_down(const uint8_t *__restrict__ dn
         if (resid) o = __fadd_rn(resid[(size_t)t * E + i], o);
         out[(size_t)t * E + i] = o;
     }
+}
+
+static size_t down_smem(const QmsCudaMoe *m) {
+    return (size_t)m->K * m->F + (size_t)m->K * m->nbF * 8 + (size_t)m->K * kDownRows * 4;
 }
 
 // Lane-major copy of the router for the batch-1 kernel: row e, element 16*i + k at [e][k][i].
@@ -271,9 +283,12 @@ static int ensure_device(int dev) {
     return QMS_CUDA_OK;
 }
 
-static int upload_q4(const void *src, int on_device, int64_t nrows, int nb, int rows_per_expert, int which,
-                     Chunked c, uint8_t *dst, size_t expert_bytes) {
-    const size_t bytes = (size_t)nrows * nb * (c.q1 ? 20 : 18);
+// Upload one stacked expert tensor (host or device source) and repack it: which = 0 / 1 gate / up
+// rows into chunks, which = 2 down rows into column stages.
+static int upload_q4(const QmsCudaMoe *m, const void *src, int on_device, int which, uint8_t *dst) {
+    const int64_t nrows = (int64_t)m->X * (which == 2 ? m->E : m->F);
+    const int nb = which == 2 ? m->nbF : m->nbE;
+    const size_t bytes = (size_t)nrows * nb * (which == 2 && m->dcol.q1 ? 20 : 18);
     const uint8_t *dsrc = (const uint8_t *)src;
     uint8_t *tmp = nullptr;
     if (!on_device) {
@@ -291,8 +306,9 @@ static int upload_q4(const void *src, int on_device, int64_t nrows, int nb, int 
         dsrc = tmp;
     }
     const int64_t n = nrows * nb;
-    k_repack_q4<<<(unsigned)((n + 255) / 256), 256>>>(dsrc, nrows, nb, rows_per_expert, which, c, dst,
-                                                      expert_bytes);
+    const unsigned grid = (unsigned)((n + 255) / 256);
+    if (which == 2) k_repack_dn<<<grid, 256>>>(dsrc, nrows, nb, m->E, m->dcol, dst, m->dn_expert);
+    else k_repack_gu<<<grid, 256>>>(dsrc, nrows, nb, m->F, which, m->cgu, dst, m->gu_expert);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (tmp) cudaFree(tmp);
@@ -352,9 +368,9 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
     m->nbE = E / 32; m->nbF = F / 32;
     m->gate_type = d->gate_type; m->up_type = d->up_type; m->down_type = d->down_type;
     m->cgu = make_chunked(m->nbE);
-    m->cdn = make_chunked(m->nbF, d->down_type == QMS_T_Q4_1);
+    m->dcol = make_dncols(E, d->down_type == QMS_T_Q4_1);
     m->gu_expert = (size_t)2 * F * m->nbE * 18;
-    m->dn_expert = (size_t)E * m->nbF * (m->cdn.q1 ? 20 : 18);
+    m->dn_expert = (size_t)E * m->nbF * (m->dcol.q1 ? 20 : 18);
     const size_t rb = (size_t)X * E * 4, gb = m->gu_expert * X, db = m->dn_expert * X;
     m->weight_bytes = rb + gb + db;
     if (cudaMalloc(&m->router, rb) != cudaSuccess || cudaMalloc(&m->router_lm, rb) != cudaSuccess ||
@@ -377,12 +393,14 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
             rc = QMS_CUDA_ECUDA;
         }
     }
-    if (rc == QMS_CUDA_OK)
-        rc = upload_q4(d->gate, d->src_on_device, (int64_t)X * F, m->nbE, F, 0, m->cgu, m->gu, m->gu_expert);
-    if (rc == QMS_CUDA_OK)
-        rc = upload_q4(d->up, d->src_on_device, (int64_t)X * F, m->nbE, F, 1, m->cgu, m->gu, m->gu_expert);
-    if (rc == QMS_CUDA_OK)
-        rc = upload_q4(d->down, d->src_on_device, (int64_t)X * E, m->nbF, E, 2, m->cdn, m->dn, m->dn_expert);
+    if (rc == QMS_CUDA_OK) rc = upload_q4(m, d->gate, d->src_on_device, 0, m->gu);
+    if (rc == QMS_CUDA_OK) rc = upload_q4(m, d->up, d->src_on_device, 1, m->gu);
+    if (rc == QMS_CUDA_OK) rc = upload_q4(m, d->down, d->src_on_device, 2, m->dn);
+    if (rc == QMS_CUDA_OK && down_smem(m) > 48 * 1024 &&
+        cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)down_smem(m)) != cudaSuccess) {
+        set_error("moe_create: %s", cudaGetErrorString(cudaGetLastError()));
+        rc = QMS_CUDA_ECUDA;
+    }
     if (rc == QMS_CUDA_OK) rc = stream_prepare(m);
     if (rc != QMS_CUDA_OK) {
         qms_cuda_moe_destroy(m);
@@ -423,7 +441,7 @@ int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
     const size_t o_stamps = off; off += al256(ss.stamps);
     const size_t o_aqf = off; off += al256(ss.aq_flagged);
     const size_t o_pgu = off; off += al256(ss.part_gu);
-    const size_t o_pdn = off; off += al256(ss.part_dn);
+    const size_t o_fin = off; off += al256(ss.fin);
     void *p = nullptr;
     if (cudaMalloc(&p, off) != cudaSuccess) {
         cudaGetLastError();
@@ -455,7 +473,7 @@ int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
     m->stamps = (unsigned *)(b + o_stamps);
     m->aq_flagged = (unsigned long long *)(b + o_aqf);
     m->part_gu = (unsigned long long *)(b + o_pgu);
-    m->part_dn = (unsigned long long *)(b + o_pdn);
+    m->fin = (unsigned long long *)(b + o_fin);
     m->cap_T = T;
     return QMS_CUDA_OK;
 }
@@ -503,9 +521,8 @@ int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int 
             QMS_CK(cudaEventRecord(m->ev[4], s));
         }
         const dim3 dgrid(m->E / kDownRows, T);
-        auto dk = m->nbF <= 32 ? k_moe_down<1> : k_moe_down<2>;
-        QMS_CK(launch_pdl(dk, dgrid, dim3(256), (size_t)m->K * kDownRows * 4, s, (const uint8_t *)m->dn,
-                          m->dn_expert, m->cdn, m->nbF, m->E, m->K, (const int8_t *)m->aq_q, (const float *)m->aq_d,
+        QMS_CK(launch_pdl(k_moe_down, dgrid, dim3(256), down_smem(m), s, (const uint8_t *)m->dn, m->dn_expert,
+                          m->dcol, m->nbF, m->E, m->K, (const int8_t *)m->aq_q, (const float *)m->aq_d,
                           (const int *)m->aq_s, (const int *)m->sel, (const float *)m->wts, resid, out));
         if (m->timing) QMS_CK(cudaEventRecord(m->ev[5], s));
     }

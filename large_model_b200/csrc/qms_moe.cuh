@@ -7,30 +7,25 @@
 
 namespace qms {
 
-// ---- staged Q4_0 expert layout ---------------------------------------------------------------
-// Expert rows are repacked at load into "chunks" of 8 rows x SB blocks (SB = 16 or 8):
+// ---- staged expert layouts ---------------------------------------------------------------------
+// gate/up rows are repacked at load into "chunks" of 8 rows x SB blocks (SB = 16 or 8):
 //   [8 rows][SB blocks][16 bytes]  nibble planes (block b of row rr at (rr*SB + b)*16)
 //   [8 rows][SB blocks][2 bytes]   fp16 scales
-// so a chunk is 8*SB*18 bytes, the same bytes as the 8*SB ggml blocks it holds.
-//   gate/up of one expert: tiles of 32 f-values; a tile is nb/SB stages; a stage is 8 chunks:
-//     chunks 0-3 hold gate rows f0..f0+31, chunks 4-7 the up rows of the same f (row r of the
-//     tile = 8*chunk + rr; r < 32 gate row f0+r, r >= 32 up row f0+r-32).
-//   down of one expert: row-blocks of 8 output rows; a row-block is nb/SB consecutive chunks.
-// One pipeline stage of the decode kernels is 8 chunks, i.e. one contiguous bulk copy for gate/up
-// and eight chunk copies (one per selected expert) for down.
+// so a chunk is 8*SB*18 bytes, the same bytes as the 8*SB ggml blocks it holds. The gate/up rows
+// of one expert form tiles of 32 f-values; a tile is nb/SB stages; a stage is 8 chunks: chunks 0-3
+// hold gate rows f0..f0+31, chunks 4-7 the up rows of the same f (row r of the tile = 8*chunk +
+// rr; r < 32 gate row f0+r, r >= 32 up row f0+r-32). One stage is one contiguous bulk copy.
 struct Chunked {
     int SB;        // blocks per chunk row
     int S;         // chunks along one row (nb / SB)
-    int q1;        // 1: Q4_1 blocks (a min plane follows the scale plane), 0: Q4_0
     uint32_t GB;   // chunk bytes
 };
 
-__host__ __device__ inline Chunked make_chunked(int nb, int q1 = 0) {
+__host__ __device__ inline Chunked make_chunked(int nb) {
     Chunked c;
     c.SB = nb % 16 == 0 ? 16 : 8;
     c.S = nb / c.SB;
-    c.q1 = q1;
-    c.GB = (uint32_t)(8 * c.SB * (q1 ? 20 : 18));
+    c.GB = (uint32_t)(8 * c.SB * 18);
     return c;
 }
 
@@ -40,19 +35,40 @@ __host__ __device__ inline size_t gu_chunk(const Chunked &c, int f, int which, i
     return ((size_t)t * c.S + b / c.SB) * 8 + (r >> 3);
 }
 
-// chunk index of down row i at block b, within one expert
-__host__ __device__ inline size_t dn_chunk(const Chunked &c, int i, int b) {
-    return (size_t)(i >> 3) * c.S + b / c.SB;
-}
-
 __host__ __device__ inline uint32_t chunk_nib_off(int SB, int rr, int bl) { return (uint32_t)(rr * SB + bl) * 16; }
 __host__ __device__ inline uint32_t chunk_scale_off(int SB, int rr, int bl) {
     return (uint32_t)(8 * SB * 16 + (rr * SB + bl) * 2);
 }
-// Q4_1 chunks: the fp16 min m of block (rr, bl), after the scale plane
-__host__ __device__ inline uint32_t chunk_min_off(int SB, int rr, int bl) {
-    return (uint32_t)(8 * SB * 18 + (rr * SB + bl) * 2);
+
+// down rows (E rows of nbF blocks, Q4_0 or Q4_1) are repacked into "column stages": for each
+// block column b (32 values of the intermediate activation, i.e. one SwiGLU/Q8 group) the
+// expert's rows are stored in Rq = E/RD stages of RD consecutive rows:
+//   [RD rows][16 bytes] nibbles, [RD rows][2 bytes] fp16 d, (Q4_1 only) [RD rows][2 bytes] fp16 m
+// Stage (b, q) sits at (b*Rq + q)*STD within the expert, so the down work of one Q8 group is Rq
+// adjacent stages and a warp reading 32 consecutive rows of one block reads 512 contiguous bytes.
+struct DnCols {
+    int RD;        // rows per stage
+    int Rq;        // stages per block column (E / RD)
+    int q1;        // 1: Q4_1 blocks, 0: Q4_0
+    uint32_t STD;  // stage bytes, RD * (20 or 18)
+};
+
+__host__ __device__ inline DnCols make_dncols(int E, int q1) {
+    DnCols d;
+    d.RD = E % 1024 == 0 ? 1024 : E % 512 == 0 ? 512 : 256;
+    d.Rq = E / d.RD;
+    d.q1 = q1;
+    d.STD = (uint32_t)(d.RD * (q1 ? 20 : 18));
+    return d;
 }
+
+// byte offset of stage (block column b, row i) and of row i's fields within it
+__host__ __device__ inline size_t dn_stage_off(const DnCols &d, int b, int i) {
+    return (size_t)(b * d.Rq + i / d.RD) * d.STD;
+}
+__host__ __device__ inline uint32_t dn_nib_off(const DnCols &d, int i) { return (uint32_t)(i % d.RD) * 16; }
+__host__ __device__ inline uint32_t dn_scale_off(const DnCols &d, int i) { return (uint32_t)(d.RD * 16 + (i % d.RD) * 2); }
+__host__ __device__ inline uint32_t dn_min_off(const DnCols &d, int i) { return (uint32_t)(d.RD * 18 + (i % d.RD) * 2); }
 
 constexpr int kTopkInRouterMaxT = 4;   // above this, k_moe_topk runs one CTA per token
 
@@ -146,11 +162,12 @@ struct QmsCudaMoe {
     int device, nsm;
     int E, X, K, F, nbE, nbF;
     int gate_type, up_type, down_type;
-    qms::Chunked cgu, cdn;
+    qms::Chunked cgu;    // gate/up chunks
+    qms::DnCols dcol;    // down column stages
     float *router;       // [X][E] F32
     float *router_lm;    // [X][16][E/16]: element 16*i + k of a row at [k][i] (lane-major, batch-1 router)
     uint8_t *gu;         // [X] experts of staged gate/up chunks
-    uint8_t *dn;         // [X] experts of staged down chunks
+    uint8_t *dn;         // [X] experts of down column stages
     size_t gu_expert, dn_expert, weight_bytes;
     int stream_ok;       // batch-1 streaming kernels usable for this shape
     // scratch, sized for cap_T tokens
@@ -170,11 +187,12 @@ struct QmsCudaMoe {
     int *cnt;            // [0]: router arrivals; [1 + slot*nbF + g]: gate/up group arrivals
     int *err;            // device error flags (bounded waits that gave up)
     // batch-1 kernel exchange buffers, in flagged words (data | call stamp << 32)
-    unsigned long long *lg_flagged;          // [X] router logits
+    unsigned long long *lg_flagged;          // [copies][X] router logits
     unsigned long long *aq_flagged;          // [K*F/32 groups][10]: 8 words of q, d, sum
-    unsigned long long *part_gu, *part_dn;   // [tile][segments][64] partial sums of split tiles
+    unsigned long long *part_gu;             // [tile][segments][64] partial gate/up sums of split tiles
+    unsigned long long *fin;                 // [nsm * E] per-CTA partial outputs
     unsigned *stamps;                        // [nsm] per-CTA call stamps
-    int gu_nst, dn_nst;         // ring depth (slots) of the batch-1 kernel
+    int nst;                    // ring depth (slots) of the batch-1 kernel
     // host-buffer entry point
     cudaStream_t hstream;
     float *d_in, *d_out;
@@ -206,7 +224,7 @@ static cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t 
 int stream_prepare(QmsCudaMoe *m);     // shape check + kernel attributes; sets m->stream_ok
 int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *resid, cudaStream_t s);
 struct StreamScratch {                 // bytes of the batch-1 kernel's exchange buffers
-    size_t lg_flagged, stamps, aq_flagged, part_gu, part_dn;
+    size_t lg_flagged, stamps, aq_flagged, part_gu, fin;
 };
 int stream_scratch_sizes(const QmsCudaMoe *m, StreamScratch *sz);
 

@@ -10,24 +10,32 @@
 //             griddepcontrol.wait, computes logit e in the reference's exact F32 order and
 //             publishes it; every CTA quantises xn to Q8 itself, gathers the X logits and selects
 //             the experts itself, so no CTA waits for a designated one and no second kernel runs;
-//   gate/up   the CTA's share of all K experts' gate/up stages (eight chunks of 8 rows x 16
-//             blocks, 18 KB) is bulk-copied into an mbarrier ring; consumer warps run dp4a dots
-//             against the token's Q8 row. A tile is 32 gate + 32 up rows, i.e. one SwiGLU + Q8
-//             re-quantisation group (src/model.c:989-997), finished by the epilogue warp;
-//   down      the consumers gather every CTA's Q8 groups (bounded polls) while the ring keeps
-//             filling with down chunks; a down tile is 8 output rows x 8 experts, combined in
-//             selection order with one FMA per expert (src/model.c:1152-1162) plus the optional
-//             residual.
-// Work is split over the CTAs by stages, not tiles, so every SM streams the same number of bytes
-// (+-1 stage). A tile split between CTAs leaves partial row sums in global memory; the tile's last
-// CTA adds them in CTA order, so results do not depend on timing. Everything exchanged between
-// CTAs (logits, partial sums, Q8 groups) travels as flagged words: 32 data bits and a call stamp in
-// one 64-bit store, so a reader polls the data itself and no fence, atomic or counter sits on the
-// critical path. Each CTA keeps its own stamp word (all CTAs run every call, so they agree). The
-// grid (one CTA per SM) is always fully resident: the kernel needs most of an SM's shared memory
-// and nothing it waits for runs behind it. Every wait is bounded: on timeout the kernel records an
-// error bit in *err, stops issuing copies, waits (bounded) for the copies it already issued and
-// returns.
+//   tiles     a tile is one 32-value group of one selected expert's intermediate activation,
+//             i.e. one SwiGLU + Q8 group (src/model.c:989-997). Its work is Sg gate/up stages (32
+//             gate + 32 up rows over all E/32 blocks: eight chunks of 8 rows x 16 blocks, 18 KB)
+//             followed by Rq down stages (the group's block column of the expert's down matrix,
+//             RD rows x one block each). All tiles' stages are split evenly over the CTAs, so every
+//             SM streams the same bytes (+-1 stage), and a CTA does the down work of the tiles it
+//             finished itself: nothing grid-wide separates gate/up from down, and the producer
+//             streams gate/up of tile k+1 before down of tile k so the SwiGLU never stalls it;
+//   gate/up   consumer warps run dp4a dots against the token's Q8 row; the epilogue warp turns a
+//             tile's 64 sums into silu(g)*u and its Q8 group;
+//   down      the consumers add w_j * (the group's down dots) into a partial output vector in
+//             shared memory (the down product split over the intermediate dimension);
+//   combine   every CTA publishes its partial vector; CTA c then sums its share of the E rows over
+//             all CTAs in CTA order, adds the optional residual and writes them.
+// A tile split between two CTAs hands over its partial gate/up sums or its finished Q8 group
+// through global memory: the CTA that produces the hand-over processes that tile first, the CTA
+// that takes it processes that tile last. Everything exchanged between CTAs travels as flagged
+// words: 32 data bits and a call stamp in one 64-bit store, so a reader polls the data itself and
+// no fence, atomic or counter sits on the critical path. Each CTA keeps its own stamp word (all
+// CTAs run every call, so they agree). The grid (one CTA per SM) is always fully resident: the
+// kernel needs most of an SM's shared memory and nothing it waits for runs behind it. Results do
+// not depend on timing: every sum has a fixed order. Every wait is bounded: on timeout the kernel
+// records an error bit in *err, stops issuing copies, waits (bounded) for the copies it already
+// issued and returns.
+#include <stdlib.h>
+
 #include <algorithm>
 
 #include "qms_moe.cuh"
@@ -39,11 +47,16 @@ constexpr int kChunkWarps = 2;                     // consumer warps per chunk (
 constexpr int kConsumerWarps = 8 * kChunkWarps;    // a stage is 8 chunks
 constexpr int kStreamThreads = (kConsumerWarps + 2) * 32;   // + producer warp + epilogue warp
 constexpr int kMaxSegments = 4;                    // CTAs a tile may be split across
+constexpr int kMaxGrid = 256;                      // CTAs (SMs) the combine tables cover
+constexpr int kLogitCopies = 16;                   // copies of the logit words (readers spread over lines)
 constexpr uint32_t kSpinLimit = 1u << 22;           // polls before a wait gives up (>= 0.1 s with backoff)
 constexpr uint32_t kPollBackoffNs = 100;
 constexpr size_t kSmemOptIn = 232448;              // 227 KB: per-block dynamic shared memory on sm_100
+// Ring slots (stages in flight per SM). 148 SMs x 6 x 18 KB = 16 MB in flight already covers
+// HBM's bandwidth-latency product; deeper rings only lengthen the queue a late-starting SM waits
+// behind. The environment variable QMS_STREAM_RING (2..32) overrides it for tuning.
 #ifndef QMS_STREAM_MAX_RING
-#define QMS_STREAM_MAX_RING 12
+#define QMS_STREAM_MAX_RING 6
 #endif
 
 enum { ERR_CONSUMER = 1, ERR_PRODUCER = 2, ERR_GRID = 4, ERR_ROUTER = 16, ERR_DRAIN = 32 };
@@ -129,48 +142,37 @@ __device__ __forceinline__ void drain_issued(uint64_t *full, int nst, int issued
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory"); }
 
-// Static split of U stage-units over G CTAs: CTA c owns [lo(c), lo(c+1)).
-__host__ __device__ inline int part_lo(int c, int U, int G) { return (int)((int64_t)c * U / G); }
-__host__ __device__ inline int part_owner(int u, int U, int G) { return (int)(((int64_t)(u + 1) * G - 1) / U); }
+// Static split of U units over G CTAs: CTA c owns [lo(c), lo(c+1)). 32-bit arithmetic (a 64-bit
+// division is a long instruction sequence on the GPU): the host checks U * G < 2^31.
+__host__ __device__ inline int part_lo(int c, int U, int G) { return c * U / G; }
+__host__ __device__ inline int part_owner(int u, int U, int G) { return ((u + 1) * G - 1) / U; }
 
-// A CTA's units [u0, u1) form tile segments: a head segment (the end of a tile started by the
-// previous CTA), a tail segment (the start of a tile finished by the next CTA) and whole tiles in
-// between. Segments of split tiles are processed first, so the cross-CTA merges they need happen
-// early and a CTA's last work is a whole tile, which needs no merge.
-struct Segs {
-    int u0, u1, S, t_first, t_last, head_s0, tail_s1, nfull, full0, n;
-    __device__ Segs(int u0_, int u1_, int S_) : u0(u0_), u1(u1_), S(S_) {
-        n = 0;
-        if (u0 >= u1) return;
-        t_first = u0 / S;
-        t_last = (u1 - 1) / S;
-        head_s0 = u0 - t_first * S;
-        tail_s1 = u1 - t_last * S;                 // end stage (exclusive) of the last tile
-        const bool head = head_s0 != 0 || (t_first == t_last && tail_s1 != S);
-        const bool tail = t_last != t_first && tail_s1 != S;
-        full0 = head ? t_first + 1 : t_first;
-        const int full1 = tail ? t_last : t_last + 1;
-        nfull = full1 - full0;
-        n = (tail ? 1 : 0) + (head ? 1 : 0) + nfull;
-        has_head = head;
-        has_tail = tail;
-    }
-    bool has_head = false, has_tail = false;
-    // k-th segment in processing order: tail, head, then whole tiles
-    __device__ void get(int k, int &tile, int &s0, int &s1) const {
-        if (has_tail) {
-            if (k == 0) { tile = t_last; s0 = 0; s1 = tail_s1; return; }
-            k--;
+constexpr int kMaxTiles = 8;                       // tiles one CTA touches (checked on the host)
+
+// The tiles CTA range [u0, u1) of the unit sequence touches (UT units per tile), in processing
+// order: the tile it shares with the next CTA first (the next CTA needs its hand-over), then whole
+// tiles, then the tile it shares with the previous CTA (it takes that CTA's hand-over); s0/s1 are
+// the CTA's units [s0, s1) within each tile. Writes at most kMaxTiles entries, returns the count.
+__host__ __device__ inline int make_jobs(int u0, int u1, int UT, int *tile, int *s0, int *s1) {
+    if (u0 >= u1) return 0;
+    const int tf = u0 / UT, tl = (u1 - 1) / UT;
+    const bool split = tf != tl;
+    const bool tail = split && u1 < (tl + 1) * UT, head = split && u0 > tf * UT;
+    int n = 0;
+    for (int k = 0; k < tl - tf + 1; k++) {
+        int t = tf + k;
+        if (tail) t = k == 0 ? tl : tf + k - 1 + (head ? 1 : 0);
+        else if (head) t = tf + k + 1;
+        if (head && k == tl - tf) t = tf;
+        if (n < kMaxTiles) {
+            tile[n] = t;
+            s0[n] = u0 > t * UT ? u0 - t * UT : 0;
+            s1[n] = u1 < (t + 1) * UT ? u1 - t * UT : UT;
         }
-        if (has_head) {
-            if (k == 0) { tile = t_first; s0 = head_s0; s1 = t_first == t_last ? tail_s1 : S; return; }
-            k--;
-        }
-        tile = full0 + k;
-        s0 = 0;
-        s1 = S;
+        n++;
     }
-};
+    return n;
+}
 
 // Ring position: slot and phase of the it-th stage, advanced incrementally.
 struct Ring {
@@ -203,28 +205,6 @@ __device__ __forceinline__ void chunk_dot(const uint8_t *chunk, const int8_t *xq
         const uint4 nib = *reinterpret_cast<const uint4 *>(chunk + chunk_nib_off(SB, rr, bl));
         const float dw = h2f(*reinterpret_cast<const uint16_t *>(chunk + chunk_scale_off(SB, rr, bl)));
         acc[p] = fmaf((float)(q4_block_isum(nib, xa0, xa1) - s8), dw * d, acc[p]);
-    }
-}
-
-// The same for Q4_1 chunks (value d q + m): d dx isum + m ds with ds = dx * (float)sum, the
-// activation block's sum term of src/kernels.c:109-121; xs holds the plain block sums.
-template <int SB>
-__device__ __forceinline__ void chunk_dot_q41(const uint8_t *chunk, const int8_t *xq, const float *xd, const int *xs,
-                                              int s, int bl, int rs, int r0, float (&acc)[SB / 4 / kChunkWarps]) {
-    constexpr int P = SB / 4 / kChunkWarps, RSTEP = 32 / SB;
-    const int b = s * SB + bl;
-    const int4 xa0 = *reinterpret_cast<const int4 *>(xq + b * 32);
-    const int4 xa1 = *reinterpret_cast<const int4 *>(xq + b * 32 + 16);
-    const float d = xd[b];
-    const float ds = d * (float)xs[b];
-#pragma unroll
-    for (int p = 0; p < P; p++) {
-        const int rr = rs + (r0 + p) * RSTEP;
-        const uint4 nib = *reinterpret_cast<const uint4 *>(chunk + chunk_nib_off(SB, rr, bl));
-        const float dw = h2f(*reinterpret_cast<const uint16_t *>(chunk + chunk_scale_off(SB, rr, bl)));
-        const float mw = h2f(*reinterpret_cast<const uint16_t *>(chunk + chunk_min_off(SB, rr, bl)));
-        acc[p] = fmaf((float)q4_block_isum(nib, xa0, xa1), dw * d, acc[p]);
-        acc[p] = fmaf(mw, ds, acc[p]);
     }
 }
 
@@ -350,17 +330,19 @@ __device__ void route_weights(const float *lg, int X, int K, const int *s_sel, d
     __syncwarp();
 }
 
-// ---- gate/up + SwiGLU + Q8, then down + combine, in one stream (batch 1) ------------------------
+// ---- gate/up + SwiGLU + Q8, down, combine in one stream (batch 1) ------------------------------
 struct DecodeArgs {
     const float *router_lm;               // [X][16][E/16]: element 16*i + k of a row at [k][i]
     const float *xn, *resid;
     float *out;
-    const uint8_t *gu, *dn;               // staged experts
+    const uint8_t *gu, *dn;               // staged experts: gate/up chunks, down column stages
     size_t gu_expert, dn_expert;
-    int nbE, nbF, F, E, K, X, nst;
-    unsigned long long *lgf;              // [X] flagged logits
-    unsigned long long *aq;               // [K*F/32 groups][10] flagged Q8 groups: q (8 words), d, sum
-    unsigned long long *part_gu, *part_dn;   // flagged partial sums of tiles split across CTAs
+    int nbE, F, E, K, X, nst, RD;
+    uint32_t slot;                        // ring slot bytes
+    unsigned long long *lgf;              // [kLogitCopies][X] flagged logits
+    unsigned long long *aq;               // [tiles][10] flagged Q8 groups: q (8 words), d, sum
+    unsigned long long *part_gu;          // [tiles][kMaxSegments][64] flagged partial gate/up sums
+    unsigned long long *fin;              // [G][E] flagged partial outputs, one vector per CTA
     unsigned *stamps;                     // [G] per-CTA call stamps
     float *logits;                        // optional outputs (NULL to skip): [X]
     int *sel;                             // [K] (written by CTA 0)
@@ -387,24 +369,16 @@ __device__ __forceinline__ bool wait_flagged(const unsigned long long *p, uint32
     return true;
 }
 
-// Epilogue-warp half of a tile split across CTAs (2 sums per lane: [lane], [32 + lane]). Every
-// CTA but the tile's last publishes its partial sums as flagged words and returns false; the last
-// CTA polls them and returns true with the full sums, added in CTA order so the result does not
-// depend on timing. A CTA's non-last segments of split tiles are the first work it does, so the
-// last CTA rarely waits.
-__device__ __forceinline__ bool merge_partial(unsigned long long *part, int tile, int S, int U, int G, int c,
-                                              uint32_t stamp, float (&v)[2], volatile int *abort, int *err) {
+// Epilogue warp, tile whose gate/up this CTA finishes after `nprev` earlier CTAs: adds their
+// flagged partial sums (slots 0 .. nprev-1, 2 per lane) in CTA order before its own, so the result
+// does not depend on timing. The earlier CTAs published them as the first work of their call.
+__device__ __forceinline__ bool add_partials(const unsigned long long *part, int tile, int nprev, uint32_t stamp,
+                                             float (&v)[2], volatile int *abort, int *err) {
     const int lane = threadIdx.x & 31;
-    const int first = part_owner(tile * S, U, G), last = part_owner(tile * S + S - 1, U, G);
-    unsigned long long *pt = part + (size_t)tile * kMaxSegments * 64;
-    if (c != last) {
-        st_flagged(pt + (c - first) * 64 + lane, __float_as_uint(v[0]), stamp);
-        st_flagged(pt + (c - first) * 64 + 32 + lane, __float_as_uint(v[1]), stamp);
-        return false;
-    }
+    const unsigned long long *pt = part + (size_t)tile * kMaxSegments * 64;
     float a0 = 0.0f, a1 = 0.0f;
     bool ok = true;
-    for (int q = 0; q < last - first; q++) {
+    for (int q = 0; q < nprev; q++) {
         unsigned long long w0 = ld_flagged(pt + q * 64 + lane), w1 = ld_flagged(pt + q * 64 + 32 + lane);
         ok = ok && wait_flagged(pt + q * 64 + lane, stamp, w0, abort, err, ERR_GRID) &&
              wait_flagged(pt + q * 64 + 32 + lane, stamp, w1, abort, err, ERR_GRID);
@@ -418,14 +392,14 @@ __device__ __forceinline__ bool merge_partial(unsigned long long *part, int tile
 
 constexpr int kSumBufs = 4;        // tile-sum hand-off buffers between consumer and epilogue warps
 
-template <int SBG, int SBD, int DQ1>
+template <int SBG, int DQ1>
 __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeArgs a) {
-    // DQ1: down weights are Q4_1 (chunks carry a min plane), else Q4_0
-    constexpr uint32_t GBG = 8 * SBG * 18, STG = 8 * GBG, GBD = 8 * SBD * (DQ1 ? 20 : 18), STD = 8 * GBD;
-    constexpr uint32_t SLOT = STG > STD ? STG : STD;
-    constexpr int PG = SBG / 4 / kChunkWarps, RSG = 32 / SBG, PD = SBD / 4 / kChunkWarps, RSD = 32 / SBD;
+    // SBG: blocks per gate/up chunk row; DQ1: down weights are Q4_1 (stages carry a min plane)
+    constexpr uint32_t GBG = 8 * SBG * 18, STG = 8 * GBG;
+    constexpr int PG = SBG / 4 / kChunkWarps, RSG = 32 / SBG;
     extern __shared__ __align__(128) uint8_t smem[];
-    const int nst = a.nst, K = a.K, F = a.F, E = a.E, X = a.X, nbE = a.nbE, nbF = a.nbF;
+    const int nst = a.nst, K = a.K, F = a.F, E = a.E, X = a.X, nbE = a.nbE, RD = a.RD;
+    const uint32_t SLOT = a.slot, STD = (uint32_t)RD * (DQ1 ? 20 : 18);
     uint8_t *ring = smem;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)nst * SLOT);
     uint64_t *empty = full + nst;
@@ -433,13 +407,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
     uint64_t *sempty = sfull + kSumBufs;                            // [kSumBufs] sums consumed
     uint64_t *rbar = sempty + kSumBufs;                             // router row landed
     uint64_t *selbar = rbar + 1;                                    // experts chosen
-    int8_t *sxq = reinterpret_cast<int8_t *>(selbar + 1);          // [nbE*32] the token's Q8 row
+    uint64_t *qbar = selbar + 1;                                    // [kMaxTiles] tile's Q8 group ready
+    float *sacc = reinterpret_cast<float *>(qbar + kMaxTiles);     // [E] this CTA's partial output
+    int8_t *sxq = reinterpret_cast<int8_t *>(sacc + E);             // [nbE*32] the token's Q8 row
     float *sxd = reinterpret_cast<float *>(sxq + nbE * 32);         // [nbE]
     int *sxs = reinterpret_cast<int *>(sxd + nbE);                  // [nbE], 8 * sum
-    int8_t *saq = reinterpret_cast<int8_t *>(sxs + nbE);            // [K][F]
-    float *sad = reinterpret_cast<float *>(saq + K * F);            // [K][nbF]
-    int *sas = reinterpret_cast<int *>(sad + K * nbF);              // [K][nbF], 8 * sum
-    float *sbuf = reinterpret_cast<float *>(sas + K * nbF);         // [kSumBufs][64] tile sums
+    int8_t *sq8 = reinterpret_cast<int8_t *>(sxs + nbE);            // [kMaxTiles][32] tiles' Q8 groups
+    float *sq8d = reinterpret_cast<float *>(sq8 + kMaxTiles * 32);  // [kMaxTiles]
+    int *sq8s = reinterpret_cast<int *>(sq8d + kMaxTiles);          // [kMaxTiles] sum (Q4_1) or 8 x sum
+    float *sbuf = reinterpret_cast<float *>(sq8s + kMaxTiles);      // [kSumBufs][64] tile sums
     float *slg = sbuf + kSumBufs * 64;                              // [kLogitPad] this call's logits
     // routing scratch inside the ring, which carries no stage before the experts are known
     const int L = E / 16, PS = L + 4;
@@ -448,17 +424,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
     __shared__ int s_abort;
     __shared__ const uint8_t *s_gu_base[8], *s_dn_base[8];   // producer: selected experts' weights
     __shared__ int s_sel[64];
-    __shared__ float s_w[64];                                  // epilogue: routing weights
+    __shared__ float s_w[64];                                  // routing weights
     __shared__ uint32_t s_stamp;
     __shared__ int t_cand[65];                                 // routing: float rank -> logit
     __shared__ double t_ex[256], t_pj[64], s_z;
+    __shared__ int s_jn, s_jt[kMaxTiles], s_j0[kMaxTiles], s_j1[kMaxTiles];   // this CTA's tiles
+    __shared__ int s_rb[kMaxGrid + 1];                         // combine: CTA r reduces rows [s_rb[r], s_rb[r+1])
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = gridDim.x, c = blockIdx.x;
-    const int Sg = nbE / SBG, tps = F / 32, ntg = K * tps, Ug = ntg * Sg;
-    const int Sd = nbF / SBD, RBE = 8 / K, RT = 8 * RBE, Ud = (a.E / RT) * Sd;
-    const uint32_t WSD = (uint32_t)Sd * GBD;        // one chunk's share of a down stage (Sd slots)
-    const int ug0 = part_lo(c, Ug, G), ug1 = part_lo(c + 1, Ug, G);
-    const int ud0 = part_lo(c, Ud, G), ud1 = part_lo(c + 1, Ud, G);
+    const int Sg = nbE / SBG, tps = F / 32, Rq = E / RD, UT = Sg + Rq, U = K * tps * UT;
     const size_t tile_bytes = (size_t)Sg * STG;
     if (threadIdx.x == 0) {
         s_abort = 0;
@@ -472,7 +446,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
         }
         mbar_init(rbar, 1);
         mbar_init(selbar, 1);
+        for (int i = 0; i < kMaxTiles; i++) mbar_init(&qbar[i], 1);
         fence_mbar_init();
+        s_jn = make_jobs(part_lo(c, U, G), part_lo(c + 1, U, G), UT, s_jt, s_j0, s_j1);
         if (c < X) {                                // router row c, lane-major, before the wait
             mbar_arrive_expect_tx(rbar, (uint32_t)E * 4);
             const uint64_t pol = evict_first_policy();
@@ -480,86 +456,71 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
                 bulk_load(srow + k * PS, a.router_lm + (size_t)c * E + (size_t)k * L, (uint32_t)L * 4, rbar, pol);
         }
     }
+    for (int i = threadIdx.x; i <= G; i += blockDim.x) s_rb[i] = part_lo(i, E, G);
     __syncthreads();
     pdl_trigger();                                  // the next call's kernel may stage its router row
     pdl_wait();                                     // xn comes from the previous kernel
     volatile int *abort_flag = &s_abort;
+    const int nj = s_jn;
 
-    if (warp == kConsumerWarps) {                   // ---- producer: one stream, gate/up then down
+    if (warp == kConsumerWarps) {                   // ---- producer: one stream of stages
         if (lane == 0) {
             bool ok = wait_bounded(selbar, 0, abort_flag, a.err, ERR_PRODUCER) && !*abort_flag;
             const uint64_t pol = evict_first_policy();
             // expert bases live in shared memory: a local array would sit in local memory, and
             // every load from it that misses L1 queues behind the stream in L2
-            for (int j = 0; j < 8; j++) s_gu_base[j] = a.gu + (size_t)(j < K ? s_sel[j] : 0) * a.gu_expert;
-            for (int gi = 0; gi < 8; gi++) s_dn_base[gi] = a.dn + (size_t)s_sel[gi / RBE] * a.dn_expert;
+            for (int j = 0; j < K; j++) {
+                s_gu_base[j] = a.gu + (size_t)s_sel[j] * a.gu_expert;
+                s_dn_base[j] = a.dn + (size_t)s_sel[j] * a.dn_expert;
+            }
             Ring r(nst);
             int issued = 0;
-            const Segs sg(ug0, ug1, Sg), sd(ud0, ud1, Sd);
-            for (int k = 0; k < sg.n && ok; k++) {
-                int tile, s0, s1;
-                sg.get(k, tile, s0, s1);
-                const uint8_t *src = s_gu_base[tile / tps] + (size_t)(tile % tps) * tile_bytes;
-                for (int s = s0; s < s1 && ok; s++) {
-                    if (issued >= nst &&
-                        !(ok = wait_bounded(&empty[r.slot], r.phase ^ 1, abort_flag, a.err, ERR_PRODUCER)))
-                        break;
-                    mbar_arrive_expect_tx(&full[r.slot], STG);
-                    bulk_load(ring + (size_t)r.slot * SLOT, src + (size_t)s * STG, STG, &full[r.slot], pol);
-                    issued++;
-                    r.next();
+            // step k: gate/up stages of tile k, then down stages of tile k - 1
+            for (int k = 0; k <= nj && ok; k++) {
+                for (int h = 0; h < 2 && ok; h++) {
+                    const int kk = k - h;
+                    if (h == 0 ? k == nj : k == 0) continue;
+                    const int t = s_jt[kk], s0 = s_j0[kk], s1 = s_j1[kk];
+                    int lo, hi;
+                    const uint8_t *src;
+                    uint32_t bytes;
+                    if (h == 0) {
+                        lo = s0;
+                        hi = s1 < Sg ? s1 : Sg;
+                        src = s_gu_base[t / tps] + (size_t)(t % tps) * tile_bytes;
+                        bytes = STG;
+                    } else {
+                        lo = (s0 > Sg ? s0 : Sg) - Sg;
+                        hi = s1 - Sg;
+                        src = s_dn_base[t / tps] + (size_t)(t % tps) * Rq * STD;
+                        bytes = STD;
+                    }
+                    for (int q = lo; q < hi && ok; q++) {
+                        if (issued >= nst &&
+                            !(ok = wait_bounded(&empty[r.slot], r.phase ^ 1, abort_flag, a.err, ERR_PRODUCER)))
+                            break;
+                        mbar_arrive_expect_tx(&full[r.slot], bytes);
+                        bulk_load(ring + (size_t)r.slot * SLOT, src + (size_t)q * bytes, bytes, &full[r.slot], pol);
+                        issued++;
+                        r.next();
+                    }
                 }
-            }
-            // The ring fills with down chunks while the consumers wait for every CTA's SwiGLU groups.
-            // First pad to a multiple of Sd slots with stages that carry no data.
-            while (r.slot % Sd != 0 && ok) {
-                if (issued >= nst &&
-                    !(ok = wait_bounded(&empty[r.slot], r.phase ^ 1, abort_flag, a.err, ERR_PRODUCER)))
-                    break;
-                mbar_arrive(&full[r.slot]);
-                issued++;
-                r.next();
-            }
-            for (int k = 0; k < sd.n && ok; k++) {
-                int tile, s0, s1;
-                sd.get(k, tile, s0, s1);
-                // A down stage is one tile segment: per chunk (expert / row block) its stages s0..s1
-                // are adjacent in HBM, so it is ONE copy of up to Sd * GBD bytes (many small copies
-                // stream far slower). It takes Sd whole slots starting at a multiple of Sd (nst is
-                // one, so it never wraps).
-                for (int q = 0; q < Sd && ok; q++)
-                    if (issued + q >= nst)
-                        ok = wait_bounded(&empty[r.slot + q], r.phase ^ 1, abort_flag, a.err, ERR_PRODUCER);
-                if (!ok) break;
-                const uint32_t bytes = (uint32_t)(s1 - s0) * GBD;
-                mbar_arrive_expect_tx(&full[r.slot], 8 * bytes);
-                uint8_t *dst = ring + (size_t)r.slot * SLOT;
-                for (int gi = 0; gi < 8; gi++) {
-                    const size_t rb = (size_t)tile * RBE + gi % RBE;
-                    bulk_load(dst + gi * WSD, s_dn_base[gi] + (rb * Sd + s0) * GBD, bytes, &full[r.slot], pol);
-                }
-                for (int q = 1; q < Sd; q++) mbar_arrive(&full[r.slot + q]);
-                issued += Sd;
-                for (int q = 0; q < Sd; q++) r.next();
             }
             if (!ok || *abort_flag) drain_issued(full, nst, issued, a.err);
         }
         return;
     }
 
-    if (warp == kConsumerWarps + 1) {               // ---- epilogue warp: SwiGLU/Q8, merges, combine
-        // first the routing weights (the combine needs them, the experts' gate/up does not)
+    if (warp == kConsumerWarps + 1) {               // ---- epilogue warp: merges, SwiGLU, Q8 groups
+        // first the routing weights (the down work needs them, gate/up does not)
         bool ok = __all_sync(0xffffffffu, wait_bounded(selbar, 0, abort_flag, a.err, ERR_CONSUMER)) && !*abort_flag;
         if (ok) route_weights(slg, X, K, s_sel, t_pj, s_z, s_w, c == 0 ? a.sel : nullptr, c == 0 ? a.wts : nullptr);
         Ring sr(kSumBufs);
         const uint32_t stamp = s_stamp;
-        for (int pass = 0; pass < 2; pass++) {
-            const bool gate = pass == 0;
-            const int S = gate ? Sg : Sd, U = gate ? Ug : Ud;
-            const Segs sq(gate ? ug0 : ud0, gate ? ug1 : ud1, S);
-            for (int k = 0; k < sq.n; k++) {
-                int tile, s0, s1;
-                sq.get(k, tile, s0, s1);
+        for (int k = 0; k < nj; k++) {
+            const int t = s_jt[k], s0 = s_j0[k], s1 = s_j1[k];
+            unsigned long long *gq = a.aq + (size_t)t * kAqWords;
+            if (s0 < Sg) {                          // gate/up sums of this CTA's part of the tile
                 if (ok) ok = __all_sync(0xffffffffu, wait_bounded(&sfull[sr.slot], sr.phase, abort_flag, a.err,
                                                                   ERR_CONSUMER));
                 float v[2] = {sbuf[sr.slot * 64 + lane], sbuf[sr.slot * 64 + 32 + lane]};
@@ -567,37 +528,44 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
                 if (lane == 0) mbar_arrive(&sempty[sr.slot]);
                 sr.next();
                 if (!ok) continue;
-                bool mine = true;
-                if (!(s0 == 0 && s1 == S))
-                    mine = merge_partial(gate ? a.part_gu : a.part_dn, tile, S, U, G, c, stamp, v, abort_flag, a.err);
-                if (!mine) continue;
-                if (gate) {                         // rows 0-31: gate f0+lane, rows 32-63: up f0+lane
-                    // Q8 group `tile` (expert slot tile / tps, values f0..f0+31) as flagged words
-                    const float av = __fmul_rn(__fdiv_rn(v[0], __fadd_rn(1.0f, expf(-v[0]))), v[1]);
-                    const Q8Lane q8 = quantize_lane(av);
+                const int first = part_owner(t * UT, U, G);
+                if (s1 < Sg) {                      // a later CTA finishes this tile's gate/up
+                    unsigned long long *pt = a.part_gu + ((size_t)t * kMaxSegments + (c - first)) * 64;
+                    st_flagged(pt + lane, __float_as_uint(v[0]), stamp);
+                    st_flagged(pt + 32 + lane, __float_as_uint(v[1]), stamp);
+                    continue;
+                }
+                if (c > first) ok = add_partials(a.part_gu, t, c - first, stamp, v, abort_flag, a.err);
+                if (!ok) continue;
+                // rows 0-31: gate f0+lane, rows 32-63: up f0+lane -> a = silu(g) * u, its Q8 group
+                const float av = __fmul_rn(__fdiv_rn(v[0], __fadd_rn(1.0f, expf(-v[0]))), v[1]);
+                const Q8Lane q8 = quantize_lane(av);
+                sq8[k * 32 + lane] = (int8_t)q8.q;
+                if (lane == 0) {
+                    sq8d[k] = q8.d;
+                    sq8s[k] = DQ1 ? q8.sum : 8 * q8.sum;
+                }
+                if (s1 < UT) {                      // a later CTA does part of the tile's down work
                     uint32_t b4 = (uint32_t)(q8.q & 0xff) << (8 * (lane & 3));
                     b4 |= __shfl_xor_sync(0xffffffffu, b4, 1);
                     b4 |= __shfl_xor_sync(0xffffffffu, b4, 2);
-                    unsigned long long *dst = a.aq + (size_t)tile * kAqWords;
-                    if ((lane & 3) == 0) st_flagged(dst + (lane >> 2), b4, stamp);
-                    if (lane == 1) st_flagged(dst + 8, __float_as_uint(q8.d), stamp);
-                    if (lane == 2) st_flagged(dst + 9, (uint32_t)q8.sum, stamp);
-                } else {                            // sum index (j*RBE + rbi)*8 + rr: expert j, row rr of block rbi
-                    const int rbi = (lane >> 3) & 7, rr = lane & 7;
-                    float o = 0.0f;
-                    for (int jj = 0; jj < K; jj++) {
-                        const int idx = (jj * RBE + rbi) * 8 + rr;
-                        const float lo = __shfl_sync(0xffffffffu, v[0], idx & 31);
-                        const float hi = __shfl_sync(0xffffffffu, v[1], idx & 31);
-                        o = __fmaf_rn(s_w[jj], idx < 32 ? lo : hi, o);
-                    }
-                    if (lane < RT) {
-                        const int i = tile * RT + lane;
-                        if (a.resid) o = __fadd_rn(a.resid[i], o);
-                        a.out[i] = o;
-                    }
+                    if ((lane & 3) == 0) st_flagged(gq + (lane >> 2), b4, stamp);
+                    if (lane == 1) st_flagged(gq + 8, __float_as_uint(q8.d), stamp);
+                    if (lane == 2) st_flagged(gq + 9, (uint32_t)q8.sum, stamp);
                 }
+            } else {                                // down work only: the Q8 group of an earlier CTA
+                if (!ok) continue;
+                unsigned long long w = lane < kAqWords ? ld_flagged(gq + lane) : 0ull;
+                ok = __all_sync(0xffffffffu, lane >= kAqWords || wait_flagged(gq + lane, stamp, w, abort_flag, a.err,
+                                                                              ERR_GRID));
+                if (!ok) continue;
+                const uint32_t d = (uint32_t)w;
+                if (lane < 8) reinterpret_cast<uint32_t *>(sq8 + k * 32)[lane] = d;
+                else if (lane == 8) sq8d[k] = __uint_as_float(d);
+                else if (lane == 9) sq8s[k] = DQ1 ? (int)d : 8 * (int)d;
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&qbar[k]);
         }
         return;
     }
@@ -609,13 +577,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
         s_stamp = next ? next : 1;
         a.stamps[c] = s_stamp;
     }
-    for (int q = tid; q < E / 4; q += kConsumerWarps * 32) {
+    // every CTA reads all of xn: start each CTA at a different 128-byte line so the 148 readers
+    // of each line do not arrive at once
+    const int n4 = E / 4, rot = (c * 8) % n4;
+    for (int q0 = tid; q0 < n4; q0 += kConsumerWarps * 32) {
+        const int q = q0 + rot < n4 ? q0 + rot : q0 + rot - n4;
         const float4 v = __ldcg(reinterpret_cast<const float4 *>(a.xn) + q);
         const int j = 4 * q;
         sx[((j + 0) & 15) * PS + ((j + 0) >> 4)] = v.x;
         sx[((j + 1) & 15) * PS + ((j + 1) >> 4)] = v.y;
         sx[((j + 2) & 15) * PS + ((j + 2) >> 4)] = v.z;
         sx[((j + 3) & 15) * PS + ((j + 3) >> 4)] = v.w;
+        reinterpret_cast<float4 *>(sacc)[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
     consumer_sync();
     const uint32_t stamp = s_stamp;
@@ -654,25 +627,48 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
             acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4, 16));
             acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2, 16));
             acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1, 16));
-            if (lane == 0 && ok) {
-                st_flagged(a.lgf + c, __float_as_uint(acc), stamp);
-                if (a.logits) a.logits[c] = acc;
-            }
+            acc = __shfl_sync(0xffffffffu, acc, 0);
+            if (lane < kLogitCopies && ok) st_flagged(a.lgf + lane * X + c, __float_as_uint(acc), stamp);
+            if (lane == 0 && ok && a.logits) a.logits[c] = acc;
         }
     } else {                                        // the token's Q8 row (src/kernels.c:34-53)
-        for (int b = warp - 1; b < nbE; b += kConsumerWarps - 1) {
-            const int j = b * 32 + lane;
-            const Q8Lane r = quantize_lane(sx[(j & 15) * PS + (j >> 4)]);
-            sxq[j] = (int8_t)r.q;
-            if (lane == 0) {
-                sxd[b] = r.d;
-                sxs[b] = 8 * r.sum;
+        // four threads per 32-block, eight values each: a warp-wide reduction per block would make
+        // each warp run ~9 blocks of dependent shuffles back to back
+        for (int v = tid - 32; v < nbE * 4; v += (kConsumerWarps - 1) * 32) {   // warp-uniform: nbE % 8 == 0
+            const int b = v >> 2, p = v & 3;
+            const float *xs = sx + 8 * (p & 1) * PS + 2 * b + (p >> 1);   // element 32b + 8p + m at xs[m * PS]
+            float x[8], amax = 0.0f;
+#pragma unroll
+            for (int m = 0; m < 8; m++) {
+                x[m] = xs[m * PS];
+                amax = fmaxf(amax, fabsf(x[m]));
+            }
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            uint32_t w0 = 0, w1 = 0;
+            int sum = 0;
+#pragma unroll
+            for (int m = 0; m < 8; m++) {
+                const int q = __float2int_rn(__fmul_rn(x[m], id));
+                sum += q;
+                if (m < 4) w0 |= (uint32_t)(q & 0xff) << (8 * m);
+                else w1 |= (uint32_t)(q & 0xff) << (8 * (m - 4));
+            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            *reinterpret_cast<uint2 *>(sxq + 32 * b + 8 * p) = make_uint2(w0, w1);
+            if (p == 0) {
+                sxd[b] = d;
+                sxs[b] = 8 * sum;
             }
         }
     }
-    if (tid < X) {                                  // every CTA's logit
-        unsigned long long v = ld_flagged(a.lgf + tid);
-        if (wait_flagged(a.lgf + tid, stamp, v, abort_flag, a.err, ERR_ROUTER)) slg[tid] = __uint_as_float((uint32_t)v);
+    if (tid < X) {                                  // every CTA's logit, from this CTA's copy
+        const unsigned long long *lw = a.lgf + (c % kLogitCopies) * X + tid;
+        unsigned long long v = ld_flagged(lw);
+        if (wait_flagged(lw, stamp, v, abort_flag, a.err, ERR_ROUTER)) slg[tid] = __uint_as_float((uint32_t)v);
     } else if (tid < kLogitPad) {
         slg[tid] = -INFINITY;                       // padding the rank loop may read
     }
@@ -688,181 +684,222 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
     }
     ok = !*abort_flag;
 
-    // ---- consumers, phase A: gate/up
-    const int g = warp / kChunkWarps, half = warp % kChunkWarps;   // chunk of the stage, row part
+    // ---- consumers: the stream, in the producer's order
+    const int g = warp / kChunkWarps, half = warp % kChunkWarps;   // chunk of a gate/up stage, row part
     Ring r(nst), sr(kSumBufs);
     int handed = 0;
-    // hand a tile's 64 sums (8 per chunk) to the epilogue warp
-    auto hand_off = [&](const float *acc, int P, int RS, int bl, int rs) {
-        if (handed >= kSumBufs && ok)
-            ok = __all_sync(0xffffffffu, wait_bounded(&sempty[sr.slot], sr.phase ^ 1, abort_flag, a.err, ERR_CONSUMER));
-        if (bl == 0)
-            for (int p = 0; p < P; p++) sbuf[sr.slot * 64 + g * 8 + rs + (half * P + p) * RS] = acc[p];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sfull[sr.slot]);
-        sr.next();
-        handed++;
+    // the partial output row q*RD + i belongs to thread i % 512 throughout: that thread updates it
+    // and publishes it (fin[c][row]) once the CTA's last down stage touching it is done
+    unsigned long long *fin_c = a.fin + (size_t)c * E;
+    bool published = false;
+    auto publish_rows = [&](int qa, int qb) {
+        for (int q = qa; q < qb; q++)
+            for (int i = tid; i < RD; i += kConsumerWarps * 32)
+                st_flagged(fin_c + q * RD + i, __float_as_uint(sacc[q * RD + i]), stamp);
     };
-    {
-        const int bl = lane % SBG, rs = lane / SBG;
-        const Segs sq(ug0, ug1, Sg);
-        for (int k = 0; k < sq.n; k++) {
-            int tile, s0, s1;
-            sq.get(k, tile, s0, s1);
-            float acc[PG];
+    const int bl = lane % SBG, rs = lane / SBG;
+    for (int k = 0; k <= nj; k++) {
+        if (k < nj) {                               // gate/up stages of tile k
+            const int s0 = s_j0[k], s1 = s_j1[k] < Sg ? s_j1[k] : Sg;
+            if (s0 < s1) {
+                float acc[PG];
 #pragma unroll
-            for (int p = 0; p < PG; p++) acc[p] = 0.0f;
-            for (int s = s0; s < s1; s++, r.next()) {
-                if (ok) ok = __all_sync(0xffffffffu, wait_bounded(&full[r.slot], r.phase, abort_flag, a.err, ERR_CONSUMER));
+                for (int p = 0; p < PG; p++) acc[p] = 0.0f;
+                for (int s = s0; s < s1; s++, r.next()) {
+                    if (ok) ok = __all_sync(0xffffffffu, wait_bounded(&full[r.slot], r.phase, abort_flag, a.err, ERR_CONSUMER));
+                    if (ok) {
+                        chunk_dot<SBG>(ring + (size_t)r.slot * SLOT + g * GBG, sxq, sxd, sxs, s, bl, rs, half * PG, acc);
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&empty[r.slot]);
+                    }
+                }
+#pragma unroll
+                for (int p = 0; p < PG; p++)
+#pragma unroll
+                    for (int o = SBG / 2; o > 0; o >>= 1) acc[p] += __shfl_xor_sync(0xffffffffu, acc[p], o);
+                // hand the tile's 64 sums (8 per chunk) to the epilogue warp
+                if (handed >= kSumBufs && ok)
+                    ok = __all_sync(0xffffffffu, wait_bounded(&sempty[sr.slot], sr.phase ^ 1, abort_flag, a.err,
+                                                              ERR_CONSUMER));
+                if (bl == 0)
+                    for (int p = 0; p < PG; p++) sbuf[sr.slot * 64 + g * 8 + rs + (half * PG + p) * RSG] = acc[p];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sfull[sr.slot]);
+                sr.next();
+                handed++;
+            }
+        }
+        if (k > 0) {                                // down stages of tile k - 1
+            const int kk = k - 1, t = s_jt[kk];
+            const int q0 = (s_j0[kk] > Sg ? s_j0[kk] : Sg) - Sg, q1 = s_j1[kk] - Sg;
+            // the last tile's down stages come last in the stream: rows outside them are final
+            // now, and each of its stages finishes its rows (a row is only ever updated by the
+            // thread that publishes it, so no barrier is needed)
+            const bool last = kk == nj - 1;
+            if (last && ok) publish_rows(0, q0 > 0 ? q0 : 0);
+            if (q0 < q1) {
+                if (ok) ok = __all_sync(0xffffffffu, wait_bounded(&qbar[kk], 0, abort_flag, a.err, ERR_CONSUMER));
+                int4 xa0 = make_int4(0, 0, 0, 0), xa1 = xa0;
+                float xd = 0.0f, wj = 0.0f;
+                int xs = 0;
                 if (ok) {
-                    chunk_dot<SBG>(ring + (size_t)r.slot * SLOT + g * GBG, sxq, sxd, sxs, s, bl, rs, half * PG, acc);
+                    xa0 = *reinterpret_cast<const int4 *>(sq8 + kk * 32);
+                    xa1 = *reinterpret_cast<const int4 *>(sq8 + kk * 32 + 16);
+                    xd = sq8d[kk];
+                    xs = sq8s[kk];
+                    wj = s_w[t / tps];
+                }
+                for (int q = q0; q < q1; q++, r.next()) {
+                    if (ok) ok = __all_sync(0xffffffffu, wait_bounded(&full[r.slot], r.phase, abort_flag, a.err, ERR_CONSUMER));
+                    if (!ok) continue;
+                    const uint8_t *st = ring + (size_t)r.slot * SLOT;
+                    float *pa = sacc + q * RD;
+#pragma unroll 2
+                    for (int i = tid; i < RD; i += kConsumerWarps * 32) {
+                        const uint4 nib = *reinterpret_cast<const uint4 *>(st + i * 16);
+                        const float dw = h2f(*reinterpret_cast<const uint16_t *>(st + RD * 16 + i * 2));
+                        const int isum = q4_block_isum(nib, xa0, xa1);
+                        float term;
+                        if (DQ1) {                  // d q + m: d dx isum + m ds (src/kernels.c:109-121)
+                            const float mw = h2f(*reinterpret_cast<const uint16_t *>(st + RD * 18 + i * 2));
+                            term = fmaf((float)isum, dw * xd, mw * (xd * (float)xs));
+                        } else {                    // d (q - 8): the -8 folded into the block sum
+                            term = (float)(isum - xs) * (dw * xd);
+                        }
+                        const float o = fmaf(wj, term, pa[i]);
+                        pa[i] = o;
+                        if (last) st_flagged(fin_c + q * RD + i, __float_as_uint(o), stamp);
+                    }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[r.slot]);
                 }
             }
-#pragma unroll
-            for (int p = 0; p < PG; p++)
-#pragma unroll
-                for (int o = SBG / 2; o > 0; o >>= 1) acc[p] += __shfl_xor_sync(0xffffffffu, acc[p], o);
-            hand_off(acc, PG, RSG, bl, rs);
+            if (last && ok) {
+                publish_rows(q1 > q0 ? q1 : q0, Rq);
+                published = true;
+            }
         }
     }
+    if (!published && ok) publish_rows(0, Rq);      // no down work came last (or none at all)
 
-    // the producer's padding slots before the first down stage, released before the wait so the
-    // ring can fill with down stages meanwhile
-    for (; r.slot % Sd != 0; r.next()) {
-        if (ok) ok = __all_sync(0xffffffffu, wait_bounded(&full[r.slot], r.phase, abort_flag, a.err, ERR_CONSUMER));
-        __syncwarp();
-        if (ok && lane == 0) mbar_arrive(&empty[r.slot]);
-    }
-
-    // ---- phase B: gather every CTA's Q8 groups as they appear, then down + combine. Each thread
-    // keeps all its words in flight and re-polls only the pending ones, one round trip per round.
-    if (ok) {
-        const int nw = ntg * kAqWords;
-        constexpr int kBatch = 8;
-        for (int i0 = tid; i0 < nw && ok; i0 += kBatch * kConsumerWarps * 32) {
-            unsigned long long v[kBatch];
-            uint32_t pending = 0;
+    // ---- combine: CTA c sums rows R0 .. R0+nr-1 over every CTA's partial vector, in CTA order
+    consumer_sync();                                // the ring is idle: it receives the partials
+    const int R0 = s_rb[c], nr = s_rb[c + 1] - R0;
+    float *red = reinterpret_cast<float *>(ring);   // [G][nr]
+    if (!*abort_flag) {
+        // warp w polls CTAs w, w + 16, ... (lane = row), all words in flight, stale ones re-polled
+        constexpr int kSrc = (kMaxGrid + kConsumerWarps - 1) / kConsumerWarps;
+        for (int i0 = 0; i0 < nr; i0 += 32) {
+            const int i = i0 + lane;
+            unsigned long long v[kSrc];
 #pragma unroll
-            for (int b = 0; b < kBatch; b++) {
-                const int i = i0 + b * kConsumerWarps * 32;
-                v[b] = i < nw ? ld_flagged(a.aq + i) : 0ull;
+            for (int j = 0; j < kSrc; j++) {
+                const int q = warp + j * kConsumerWarps;
+                v[j] = q < G && i < nr ? ld_flagged(a.fin + (size_t)q * E + R0 + i) : 0ull;
             }
             uint32_t n = 0;
-            for (;;) {
+            bool done = false;
+            while (!done) {
+                uint32_t pending = 0;
 #pragma unroll
-                for (int b = 0; b < kBatch; b++) {
-                    const int i = i0 + b * kConsumerWarps * 32;
-                    if (i < nw && (uint32_t)(v[b] >> 32) != stamp) pending |= 1u << b;
+                for (int j = 0; j < kSrc; j++) {
+                    const int q = warp + j * kConsumerWarps;
+                    if (q < G && i < nr && (uint32_t)(v[j] >> 32) != stamp) pending |= 1u << j;
                 }
-                if (!pending) break;
-                if (*abort_flag) {
-                    ok = false;
+                if (!pending) {
+                    done = true;
                     break;
                 }
+                if (*abort_flag) break;
                 if (++n == kSpinLimit) {
                     *abort_flag = 1;
                     atomicOr(a.err, ERR_GRID);
-                    ok = false;
                     break;
                 }
                 __nanosleep(64);
 #pragma unroll
-                for (int b = 0; b < kBatch; b++)
-                    if (pending & (1u << b)) v[b] = ld_flagged(a.aq + i0 + b * kConsumerWarps * 32);
-                pending = 0;
+                for (int j = 0; j < kSrc; j++)
+                    if (pending & (1u << j)) v[j] = ld_flagged(a.fin + (size_t)(warp + j * kConsumerWarps) * E + R0 + i);
             }
-            if (!ok) break;
+            if (!done) break;
 #pragma unroll
-            for (int b = 0; b < kBatch; b++) {
-                const int i = i0 + b * kConsumerWarps * 32;
-                if (i >= nw) continue;
-                const int gi = i / kAqWords, w = i - gi * kAqWords;
-                const uint32_t d = (uint32_t)v[b];
-                if (w < 8) reinterpret_cast<uint32_t *>(saq)[gi * 8 + w] = d;
-                else if (w == 8) sad[gi] = __uint_as_float(d);
-                else sas[gi] = DQ1 ? (int)d : 8 * (int)d;   // block sum (Q4_1) or 8 x it (Q4_0)
+            for (int j = 0; j < kSrc; j++) {
+                const int q = warp + j * kConsumerWarps;
+                if (q < G && i < nr) red[q * nr + i] = __uint_as_float((uint32_t)v[j]);
             }
         }
     }
     consumer_sync();
-    ok = ok && !*abort_flag;                        // every failed wait raised the abort flag
-    {
-        const int j = g / RBE, bl = lane % SBD, rs = lane / SBD;
-        const int8_t *xq = saq + (size_t)j * F;
-        const float *xdv = sad + j * nbF;
-        const int *xsv = sas + j * nbF;
-        const Segs sq(ud0, ud1, Sd);
-        for (int k = 0; k < sq.n; k++) {
-            int tile, s0, s1;
-            sq.get(k, tile, s0, s1);
-            float acc[PD];
-#pragma unroll
-            for (int p = 0; p < PD; p++) acc[p] = 0.0f;
-            if (ok) ok = __all_sync(0xffffffffu, wait_bounded(&full[r.slot], r.phase, abort_flag, a.err, ERR_CONSUMER));
-            if (ok) {
-                const uint8_t *chunk = ring + (size_t)r.slot * SLOT + g * WSD;   // [chunk][stage s0..s1]
-                for (int s = s0; s < s1; s++)
-                    if (DQ1) chunk_dot_q41<SBD>(chunk + (s - s0) * GBD, xq, xdv, xsv, s, bl, rs, half * PD, acc);
-                    else chunk_dot<SBD>(chunk + (s - s0) * GBD, xq, xdv, xsv, s, bl, rs, half * PD, acc);
-                __syncwarp();
-                if (lane == 0)
-                    for (int q = 0; q < Sd; q++) mbar_arrive(&empty[r.slot + q]);
-            }
-            for (int q = 0; q < Sd; q++) r.next();
-#pragma unroll
-            for (int p = 0; p < PD; p++)
-#pragma unroll
-                for (int o = SBD / 2; o > 0; o >>= 1) acc[p] += __shfl_xor_sync(0xffffffffu, acc[p], o);
-            hand_off(acc, PD, RSD, bl, rs);
+    if (*abort_flag) return;
+    // 16 threads per row, each sums every 16th CTA in order, then a fixed tree
+    for (int i0 = 0; i0 < nr; i0 += kConsumerWarps * 2) {
+        const int i = i0 + (tid >> 4), p = tid & 15;
+        float sum = 0.0f;
+        if (i < nr)
+            for (int q = p; q < G; q += 16) sum += red[q * nr + i];
+        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        if (p == 0 && i < nr) {
+            float o = sum;
+            if (a.resid) o = __fadd_rn(a.resid[R0 + i], o);
+            a.out[R0 + i] = o;
         }
     }
 }
 
 // ---- host side -----------------------------------------------------------------------------------
-static uint32_t dec_slot(const QmsCudaMoe *m) { return 8 * std::max(m->cgu.GB, m->cdn.GB); }
+static uint32_t dec_slot(const QmsCudaMoe *m) {
+    const uint32_t stg = 8 * m->cgu.GB, std_ = m->dcol.STD;
+    return stg > std_ ? stg : std_;
+}
 static size_t dec_fixed(const QmsCudaMoe *m) {
-    return (2 * kSumBufs + 2) * 8 + (size_t)m->nbE * 40 + (size_t)m->K * m->F + (size_t)m->K * m->nbF * 8 +
+    return (2 * kSumBufs + 2 + kMaxTiles) * 8 + (size_t)m->E * 4 + (size_t)m->nbE * 40 + kMaxTiles * 40 +
            kSumBufs * 64 * 4 + (size_t)kLogitPad * 4;
 }
-static size_t dec_smem(const QmsCudaMoe *m) { return (size_t)m->gu_nst * (dec_slot(m) + 16) + dec_fixed(m); }
-
-static int max_segments(int U, int S, int G) {
-    int worst = 1;
-    for (int tile = 0; tile * S < U; tile++)
-        worst = std::max(worst, part_owner(tile * S + S - 1, U, G) - part_owner(tile * S, U, G) + 1);
-    return worst;
-}
+static size_t dec_smem(const QmsCudaMoe *m) { return (size_t)m->nst * (dec_slot(m) + 16) + dec_fixed(m); }
 
 typedef void (*DecodeKernel)(const DecodeArgs);
 static DecodeKernel dec_kernel(const QmsCudaMoe *m) {
-    if (m->cdn.q1) {
-        if (m->cgu.SB == 16) return m->cdn.SB == 16 ? k_decode_bs1<16, 16, 1> : k_decode_bs1<16, 8, 1>;
-        return m->cdn.SB == 16 ? k_decode_bs1<8, 16, 1> : k_decode_bs1<8, 8, 1>;
-    }
-    if (m->cgu.SB == 16) return m->cdn.SB == 16 ? k_decode_bs1<16, 16, 0> : k_decode_bs1<16, 8, 0>;
-    return m->cdn.SB == 16 ? k_decode_bs1<8, 16, 0> : k_decode_bs1<8, 8, 0>;
+    if (m->dcol.q1) return m->cgu.SB == 16 ? k_decode_bs1<16, 1> : k_decode_bs1<8, 1>;
+    return m->cgu.SB == 16 ? k_decode_bs1<16, 0> : k_decode_bs1<8, 0>;
+}
+
+// Largest number of tiles one CTA touches, and of CTAs one tile's gate/up part spans.
+static void job_bounds(const QmsCudaMoe *m, int *max_tiles, int *max_segs) {
+    const int G = m->nsm, Sg = m->cgu.S, UT = Sg + m->dcol.Rq, ntg = m->K * (m->F / 32), U = ntg * UT;
+    int jt[kMaxTiles], j0[kMaxTiles], j1[kMaxTiles];
+    *max_tiles = 0;
+    for (int c = 0; c < G; c++) *max_tiles = std::max(*max_tiles, make_jobs(part_lo(c, U, G), part_lo(c + 1, U, G), UT, jt, j0, j1));
+    *max_segs = 1;
+    for (int t = 0; t < ntg; t++)
+        *max_segs = std::max(*max_segs, part_owner(t * UT + Sg - 1, U, G) - part_owner(t * UT, U, G) + 1);
 }
 
 int stream_prepare(QmsCudaMoe *m) {
     m->stream_ok = 0;
-    if (!(m->K == 1 || m->K == 2 || m->K == 4 || m->K == 8) || m->X > 256 || 2 * m->X > m->E) return QMS_CUDA_OK;
-    if (m->nbE % m->cgu.SB || m->nbF % m->cdn.SB) return QMS_CUDA_OK;
+    if (m->K > 8 || m->X > 256 || 2 * m->X > m->E || m->nsm > kMaxGrid) return QMS_CUDA_OK;
+    const int64_t units = (int64_t)m->K * (m->F / 32) * (m->cgu.S + m->dcol.Rq);
+    if ((units + 1) * m->nsm >= (1ll << 31) || (int64_t)(m->E + 1) * m->nsm >= (1ll << 31)) return QMS_CUDA_OK;
+    if (m->nbE % m->cgu.SB) return QMS_CUDA_OK;
     const uint32_t slot = dec_slot(m);
     cudaFuncAttributes fa;
     QMS_CK(cudaFuncGetAttributes(&fa, dec_kernel(m)));
-    // the deepest ring that fits, a multiple of the down stage width cdn.S so a down stage never
-    // wraps around it; routing scratch (router row + xn, lane-major) lives in its first slots
     const size_t avail = kSmemOptIn - fa.sharedSizeBytes - dec_fixed(m);
-    const int fit = (int)std::min<size_t>(QMS_STREAM_MAX_RING, avail / (slot + 16));
-    m->gu_nst = fit / m->cdn.S * m->cdn.S;
-    m->dn_nst = m->gu_nst;
-    if (m->gu_nst < 4 || m->gu_nst < m->cdn.S) return QMS_CUDA_OK;
-    if ((size_t)2 * 16 * (m->E / 16 + 4) * 4 > (size_t)m->gu_nst * slot) return QMS_CUDA_OK;
-    const int Ugu = m->K * (m->F / 32) * m->cgu.S, Udn = (m->E / (64 / m->K)) * m->cdn.S;
-    if (max_segments(Ugu, m->cgu.S, m->nsm) > kMaxSegments || max_segments(Udn, m->cdn.S, m->nsm) > kMaxSegments)
-        return QMS_CUDA_OK;
+    int want = QMS_STREAM_MAX_RING;
+    if (const char *env = getenv("QMS_STREAM_RING")) {
+        const int v = atoi(env);
+        if (v >= 2 && v <= 32) want = v;
+    }
+    m->nst = (int)std::min<size_t>((size_t)want, avail / (slot + 16));
+    if (m->nst < 2) return QMS_CUDA_OK;
+    const size_t ring = (size_t)m->nst * slot;
+    if ((size_t)2 * 16 * (m->E / 16 + 4) * 4 > ring) return QMS_CUDA_OK;             // routing scratch
+    if ((size_t)m->nsm * ((m->E + m->nsm - 1) / m->nsm) * 4 > ring) return QMS_CUDA_OK;   // combine scratch
+    int max_tiles, max_segs;
+    job_bounds(m, &max_tiles, &max_segs);
+    if (max_tiles > kMaxTiles || max_segs > kMaxSegments) return QMS_CUDA_OK;
     const DecodeKernel dk = dec_kernel(m);
     QMS_CK(cudaFuncSetAttribute(dk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dec_smem(m)));
     QMS_CK(cudaFuncSetAttribute(dk, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
@@ -871,12 +908,12 @@ int stream_prepare(QmsCudaMoe *m) {
 }
 
 int stream_scratch_sizes(const QmsCudaMoe *m, StreamScratch *sz) {
-    const int tiles_gu = m->K * (m->F / 32), tiles_dn = m->E / (64 / std::max(1, std::min(8, m->K)));
-    sz->lg_flagged = (size_t)m->X * 8;
+    const int tiles = m->K * (m->F / 32);
+    sz->lg_flagged = (size_t)kLogitCopies * m->X * 8;
     sz->stamps = (size_t)m->nsm * 4;
-    sz->aq_flagged = (size_t)tiles_gu * kAqWords * 8;
-    sz->part_gu = (size_t)tiles_gu * kMaxSegments * 64 * 8;
-    sz->part_dn = (size_t)tiles_dn * kMaxSegments * 64 * 8;
+    sz->aq_flagged = (size_t)tiles * kAqWords * 8;
+    sz->part_gu = (size_t)tiles * kMaxSegments * 64 * 8;
+    sz->fin = (size_t)m->nsm * m->E * 8;
     return QMS_CUDA_OK;
 }
 
@@ -891,16 +928,17 @@ int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *
     a.gu_expert = m->gu_expert;
     a.dn_expert = m->dn_expert;
     a.nbE = m->nbE;
-    a.nbF = m->nbF;
     a.F = m->F;
     a.E = m->E;
     a.K = m->K;
     a.X = m->X;
-    a.nst = m->gu_nst;
+    a.nst = m->nst;
+    a.RD = m->dcol.RD;
+    a.slot = dec_slot(m);
     a.lgf = m->lg_flagged;
     a.aq = m->aq_flagged;
     a.part_gu = m->part_gu;
-    a.part_dn = m->part_dn;
+    a.fin = m->fin;
     a.stamps = m->stamps;
     a.logits = m->logits;
     a.sel = m->sel;

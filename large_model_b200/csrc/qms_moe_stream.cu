@@ -407,7 +407,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
     uint64_t *sempty = sfull + kSumBufs;                            // [kSumBufs] sums consumed
     uint64_t *rbar = sempty + kSumBufs;                             // router row landed
     uint64_t *selbar = rbar + 1;                                    // experts chosen
-    uint64_t *qbar = selbar + 1;                                    // [kMaxTiles] tile's Q8 group ready
+    uint64_t *specbar = selbar + 1;                                 // float ranking done (t_cand)
+    uint64_t *ringbar = specbar + 1;                                // the ring holds the chosen experts
+    uint64_t *qbar = ringbar + 1;                                   // [kMaxTiles] tile's Q8 group ready
     float *sacc = reinterpret_cast<float *>(qbar + kMaxTiles);     // [E] this CTA's partial output
     int8_t *sxq = reinterpret_cast<int8_t *>(sacc + E);             // [nbE*32] the token's Q8 row
     float *sxd = reinterpret_cast<float *>(sxq + nbE * 32);         // [nbE]
@@ -422,7 +424,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
     float *srow = reinterpret_cast<float *>(ring);                  // [16][PS] router row, lane-major
     float *sx = srow + 16 * PS;                                     // [16][PS] xn, lane-major
     __shared__ int s_abort;
-    __shared__ const uint8_t *s_gu_base[8], *s_dn_base[8];   // producer: selected experts' weights
+    __shared__ const uint8_t *s_gu_base[8], *s_dn_base[8];   // producer: streamed experts' weights
+    __shared__ int s_spec[8];                                  // producer: the experts being streamed
     __shared__ int s_sel[64];
     __shared__ float s_w[64];                                  // routing weights
     __shared__ uint32_t s_stamp;
@@ -446,6 +449,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
         }
         mbar_init(rbar, 1);
         mbar_init(selbar, 1);
+        mbar_init(specbar, 1);
+        mbar_init(ringbar, 1);
+        for (int i = 0; i <= K; i++) t_cand[i] = 0;
         for (int i = 0; i < kMaxTiles; i++) mbar_init(&qbar[i], 1);
         fence_mbar_init();
         s_jn = make_jobs(part_lo(c, U, G), part_lo(c + 1, U, G), UT, s_jt, s_j0, s_j1);
@@ -465,48 +471,87 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
 
     if (warp == kConsumerWarps) {                   // ---- producer: one stream of stages
         if (lane == 0) {
-            bool ok = wait_bounded(selbar, 0, abort_flag, a.err, ERR_PRODUCER) && !*abort_flag;
             const uint64_t pol = evict_first_policy();
-            // expert bases live in shared memory: a local array would sit in local memory, and
-            // every load from it that misses L1 queues behind the stream in L2
-            for (int j = 0; j < K; j++) {
-                s_gu_base[j] = a.gu + (size_t)s_sel[j] * a.gu_expert;
-                s_dn_base[j] = a.dn + (size_t)s_sel[j] * a.dn_expert;
-            }
-            Ring r(nst);
-            int issued = 0;
-            // step k: gate/up stages of tile k, then down stages of tile k - 1
-            for (int k = 0; k <= nj && ok; k++) {
-                for (int h = 0; h < 2 && ok; h++) {
-                    const int kk = k - h;
-                    if (h == 0 ? k == nj : k == 0) continue;
-                    const int t = s_jt[kk], s0 = s_j0[kk], s1 = s_j1[kk];
-                    int lo, hi;
-                    const uint8_t *src;
-                    uint32_t bytes;
-                    if (h == 0) {
-                        lo = s0;
-                        hi = s1 < Sg ? s1 : Sg;
-                        src = s_gu_base[t / tps] + (size_t)(t % tps) * tile_bytes;
-                        bytes = STG;
+            // The stream starts on the float ranking's top K (t_cand) while warp 0 still proves it
+            // against the double probabilities; the selection is checked before the ring is handed
+            // to the consumers (ringbar). If they differ (ties of the exact ranking, NaN logits),
+            // the copies issued so far land, the ring is reset and the stream restarts.
+            bool ok = wait_bounded(specbar, 0, abort_flag, a.err, ERR_PRODUCER) && !*abort_flag;
+            bool valid = false;                     // the experts in use are the selection
+            for (int pass = 0; pass < 2 && ok; pass++) {
+                // expert bases live in shared memory: a local array would sit in local memory,
+                // and every load from it that misses L1 queues behind the stream in L2
+                for (int j = 0; j < K; j++) {
+                    int e = valid ? s_sel[j] : t_cand[j];
+                    if ((unsigned)e >= (unsigned)X) e = 0;   // speculative only: the check rejects it
+                    s_spec[j] = e;
+                    s_gu_base[j] = a.gu + (size_t)e * a.gu_expert;
+                    s_dn_base[j] = a.dn + (size_t)e * a.dn_expert;
+                }
+                bool restart = false;
+                auto check = [&]() {                // the proof is done: same experts?
+                    ok = wait_bounded(selbar, 0, abort_flag, a.err, ERR_PRODUCER) && !*abort_flag;
+                    if (!ok) return;
+                    bool same = true;
+                    for (int j = 0; j < K; j++) same = same && s_sel[j] == s_spec[j];
+                    if (same) {
+                        valid = true;
+                        mbar_arrive(ringbar);
                     } else {
-                        lo = (s0 > Sg ? s0 : Sg) - Sg;
-                        hi = s1 - Sg;
-                        src = s_dn_base[t / tps] + (size_t)(t % tps) * Rq * STD;
-                        bytes = STD;
+                        restart = true;
                     }
-                    for (int q = lo; q < hi && ok; q++) {
-                        if (issued >= nst &&
-                            !(ok = wait_bounded(&empty[r.slot], r.phase ^ 1, abort_flag, a.err, ERR_PRODUCER)))
-                            break;
-                        mbar_arrive_expect_tx(&full[r.slot], bytes);
-                        bulk_load(ring + (size_t)r.slot * SLOT, src + (size_t)q * bytes, bytes, &full[r.slot], pol);
-                        issued++;
-                        r.next();
+                };
+                Ring r(nst);
+                int issued = 0;
+                // step k: gate/up stages of tile k, then down stages of tile k - 1
+                for (int k = 0; k <= nj && ok && !restart; k++) {
+                    for (int h = 0; h < 2 && ok && !restart; h++) {
+                        const int kk = k - h;
+                        if (h == 0 ? k == nj : k == 0) continue;
+                        const int t = s_jt[kk], s0 = s_j0[kk], s1 = s_j1[kk];
+                        int lo, hi;
+                        const uint8_t *src;
+                        uint32_t bytes;
+                        if (h == 0) {
+                            lo = s0;
+                            hi = s1 < Sg ? s1 : Sg;
+                            src = s_gu_base[t / tps] + (size_t)(t % tps) * tile_bytes;
+                            bytes = STG;
+                        } else {
+                            lo = (s0 > Sg ? s0 : Sg) - Sg;
+                            hi = s1 - Sg;
+                            src = s_dn_base[t / tps] + (size_t)(t % tps) * Rq * STD;
+                            bytes = STD;
+                        }
+                        for (int q = lo; q < hi && ok; q++) {
+                            if (issued >= nst) {
+                                if (!valid && (check(), restart || !ok)) break;
+                                if (!(ok = wait_bounded(&empty[r.slot], r.phase ^ 1, abort_flag, a.err, ERR_PRODUCER)))
+                                    break;
+                            }
+                            mbar_arrive_expect_tx(&full[r.slot], bytes);
+                            bulk_load(ring + (size_t)r.slot * SLOT, src + (size_t)q * bytes, bytes, &full[r.slot], pol);
+                            issued++;
+                            r.next();
+                        }
                     }
                 }
+                if (ok && !valid && !restart) check();
+                if (!ok || *abort_flag) {
+                    drain_issued(full, nst, issued, a.err);
+                    break;
+                }
+                if (!restart) break;
+                // wrong experts: let the speculative copies land, reset the ring, start over
+                drain_issued(full, nst, issued, a.err);
+                for (int i = 0; i < nst; i++) {
+                    mbar_init(&full[i], 1);
+                    mbar_init(&empty[i], kConsumerWarps);
+                }
+                fence_mbar_init();
+                valid = true;
+                mbar_arrive(ringbar);
             }
-            if (!ok || *abort_flag) drain_issued(full, nst, issued, a.err);
         }
         return;
     }
@@ -598,30 +643,44 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
             ok = __all_sync(0xffffffffu, wait_bounded(rbar, 0, abort_flag, a.err, ERR_ROUTER));
             const int k = lane & 15;
             const float *w = srow + k * PS, *x = sx + k * PS;
+            // the chain is 256 dependent FMAs (E = 4096): operands of the next 8 elements are
+            // loaded while the current 8 multiply, so no shared-memory latency sits in the chain
             float acc = 0.0f;
-            int i = 0;
-            for (; i + 32 <= L; i += 32) {         // 8 loads of each operand in flight per batch
-                float4 w4[8], x4[8];
+            const int nch = L / 8;                  // L % 16 == 0 (E % 256 == 0): nch is even
+            float4 wa[2], xa[2], wb[2], xb[2];
 #pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    w4[q] = *reinterpret_cast<const float4 *>(w + i + 4 * q);
-                    x4[q] = *reinterpret_cast<const float4 *>(x + i + 4 * q);
-                }
-#pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    acc = __fmaf_rn(w4[q].x, x4[q].x, acc);
-                    acc = __fmaf_rn(w4[q].y, x4[q].y, acc);
-                    acc = __fmaf_rn(w4[q].z, x4[q].z, acc);
-                    acc = __fmaf_rn(w4[q].w, x4[q].w, acc);
-                }
+            for (int q = 0; q < 2; q++) {
+                wa[q] = *reinterpret_cast<const float4 *>(w + 4 * q);
+                xa[q] = *reinterpret_cast<const float4 *>(x + 4 * q);
             }
-            for (; i < L; i += 4) {
-                const float4 w4 = *reinterpret_cast<const float4 *>(w + i);
-                const float4 x4 = *reinterpret_cast<const float4 *>(x + i);
-                acc = __fmaf_rn(w4.x, x4.x, acc);
-                acc = __fmaf_rn(w4.y, x4.y, acc);
-                acc = __fmaf_rn(w4.z, x4.z, acc);
-                acc = __fmaf_rn(w4.w, x4.w, acc);
+            for (int ch = 0; ch < nch; ch += 2) {
+                const int ib = (ch + 1) * 8;
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    wb[q] = *reinterpret_cast<const float4 *>(w + ib + 4 * q);
+                    xb[q] = *reinterpret_cast<const float4 *>(x + ib + 4 * q);
+                }
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    acc = __fmaf_rn(wa[q].x, xa[q].x, acc);
+                    acc = __fmaf_rn(wa[q].y, xa[q].y, acc);
+                    acc = __fmaf_rn(wa[q].z, xa[q].z, acc);
+                    acc = __fmaf_rn(wa[q].w, xa[q].w, acc);
+                }
+                if (ch + 2 < nch) {
+#pragma unroll
+                    for (int q = 0; q < 2; q++) {
+                        wa[q] = *reinterpret_cast<const float4 *>(w + ib + 8 + 4 * q);
+                        xa[q] = *reinterpret_cast<const float4 *>(x + ib + 8 + 4 * q);
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    acc = __fmaf_rn(wb[q].x, xb[q].x, acc);
+                    acc = __fmaf_rn(wb[q].y, xb[q].y, acc);
+                    acc = __fmaf_rn(wb[q].z, xb[q].z, acc);
+                    acc = __fmaf_rn(wb[q].w, xb[q].w, acc);
+                }
             }
             acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 8, 16));
             acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4, 16));
@@ -675,6 +734,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
     consumer_sync();
     rank_candidates(slg, X, K, tid, t_cand);
     consumer_sync();
+    if (tid == 0) mbar_arrive(specbar);             // the producer may start on the float ranking
     if (warp == 0) {
         double z = 0.0;
         if (!*abort_flag) route_select(slg, X, K, t_cand, s_sel, t_ex, t_pj, z);
@@ -684,7 +744,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
     }
     ok = !*abort_flag;
 
-    // ---- consumers: the stream, in the producer's order
+    // ---- consumers: the stream, in the producer's order, once it carries the selected experts
+    if (ok) ok = __all_sync(0xffffffffu, wait_bounded(ringbar, 0, abort_flag, a.err, ERR_CONSUMER));
     const int g = warp / kChunkWarps, half = warp % kChunkWarps;   // chunk of a gate/up stage, row part
     Ring r(nst), sr(kSumBufs);
     int handed = 0;
@@ -855,7 +916,7 @@ static uint32_t dec_slot(const QmsCudaMoe *m) {
     return stg > std_ ? stg : std_;
 }
 static size_t dec_fixed(const QmsCudaMoe *m) {
-    return (2 * kSumBufs + 2 + kMaxTiles) * 8 + (size_t)m->E * 4 + (size_t)m->nbE * 40 + kMaxTiles * 40 +
+    return (2 * kSumBufs + 4 + kMaxTiles) * 8 + (size_t)m->E * 4 + (size_t)m->nbE * 40 + kMaxTiles * 40 +
            kSumBufs * 64 * 4 + (size_t)kLogitPad * 4;
 }
 static size_t dec_smem(const QmsCudaMoe *m) { return (size_t)m->nst * (dec_slot(m) + 16) + dec_fixed(m); }

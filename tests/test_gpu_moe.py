@@ -126,6 +126,34 @@ def test_moe_edge_cases(cuda, oracle):
     m2.close()
 
 
+@pytest.mark.parametrize("shape", ["tiny", "30b"])
+def test_decode_routing_edge_cases(cuda, oracle, shape):
+    """Batch-1 kernel (one call per token): its stream starts on the float ranking and is checked
+    against the exact double ranking. Zeros tie everywhere (same experts); at 1e-30 every
+    probability is exactly 1 in double and at 1e4 all but the top one underflow to 0, so the
+    exact ranking takes the lowest indices while the float ranking does not: the kernel must
+    restart its stream on the selected experts."""
+    import torch
+    layer = synth.make_moe_layer(shape, seed=12)
+    E = layer.n_embd
+    xs = synth.make_hidden(E, 6, seed=13)
+    xs[0] = 0.0
+    xs[1] *= 1e-30
+    xs[2] *= 1e4
+    xs[3, : E // 2] = 0.0
+    xs[4] *= -3.0
+    m = cuda.MoeLayer.from_synth(layer)
+    xd = torch.from_numpy(xs).cuda()
+    res = [m.route(xd[t:t + 1]) for t in range(xs.shape[0])]
+    torch.cuda.synchronize()
+    m.status()
+    out, sel, w, logits = (torch.cat([r[i] for r in res]).cpu().numpy() for i in range(4))
+    _check(oracle, layer, xs, out, sel, w, logits, f"decode edge {shape}")
+    K = layer.n_used
+    assert sel[0].tolist() == list(range(K)) and sel[1].tolist() == list(range(K))
+    m.close()
+
+
 def test_moe_host_entry_and_residual(cuda, oracle):
     import torch
     layer = synth.make_moe_layer("30b", seed=8)

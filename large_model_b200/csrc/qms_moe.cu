@@ -14,6 +14,7 @@
 //                  (phase 3, :998-1005), then the weighted sum in selection order with one
 //                  fused multiply-add per expert (:1152-1162), plus the optional residual.
 // Expert weights are repacked at load into the staged layouts of qms_moe.cuh.
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -27,6 +28,7 @@ namespace qms {
 
 constexpr int kGateUpRows = 8;         // f values per gate/up CTA (one per warp)
 constexpr int kDownRows = 32;          // output rows per down CTA (one per lane)
+constexpr int kMmaMinT = 16;           // tokens from which the grouped tensor-core kernels run
 
 // ---- load-time repack: GGUF rows -> staged layouts (qms_moe.cuh) --------------------------------
 // gate (which 0) / up (which 1) Q4_0 rows of a stacked [X][F] tensor -> chunks
@@ -402,6 +404,11 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
         rc = QMS_CUDA_ECUDA;
     }
     if (rc == QMS_CUDA_OK) rc = stream_prepare(m);
+    if (rc == QMS_CUDA_OK && mma_supported(m)) {
+        m->mma_min_t = kMmaMinT;
+        if (const char *env = getenv("QMS_MMA_MIN_T")) m->mma_min_t = atoi(env);   // 0 turns the path off
+        if (m->mma_min_t > 0) rc = mma_prepare(m);
+    }
     if (rc != QMS_CUDA_OK) {
         qms_cuda_moe_destroy(m);
         return rc;
@@ -418,9 +425,10 @@ int64_t qms_cuda_moe_device_bytes(const QmsCudaMoe *m) {
 int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
     QMS_REQUIRE(m && T >= 0, QMS_CUDA_EINVAL, "moe_reserve: bad arguments");
     QMS_REQUIRE((int64_t)T * m->K <= 65535, QMS_CUDA_EINVAL, "moe: T * n_used must be <= 65535");
-    if (T <= m->cap_T) return QMS_CUDA_OK;
     int rc = ensure_device(m->device);
     if (rc) return rc;
+    if (m->mma_min_t > 0 && T >= m->mma_min_t && (rc = mma_reserve(m, T))) return rc;
+    if (T <= m->cap_T) return QMS_CUDA_OK;
     const size_t TK = (size_t)T * m->K;
     size_t off = 0;
     const size_t o_xq_q = off; off += al256((size_t)T * m->E);
@@ -509,6 +517,9 @@ int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int 
             QMS_CK(cudaEventRecord(m->ev[1], s));
             QMS_CK(cudaEventRecord(m->ev[2], s));
         }
+        if (m->mma_min_t > 0 && T >= m->mma_min_t) {
+            if ((rc = mma_forward(m, T, resid, out, s))) return rc;
+        } else {
         const dim3 ggrid(m->F / kGateUpRows, T * m->K);
         const int nbl = (m->nbE + 31) / 32;
         auto gk = nbl == 1 ? k_moe_gate_up<1> : nbl == 2 ? k_moe_gate_up<2> : nbl == 3 ? k_moe_gate_up<3>
@@ -525,6 +536,7 @@ int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int 
                           m->dcol, m->nbF, m->E, m->K, (const int8_t *)m->aq_q, (const float *)m->aq_d,
                           (const int *)m->aq_s, (const int *)m->sel, (const float *)m->wts, resid, out));
         if (m->timing) QMS_CK(cudaEventRecord(m->ev[5], s));
+        }
     }
     const size_t TK = (size_t)T * m->K;
     if (sel) QMS_CK(cudaMemcpyAsync(sel, m->sel, TK * 4, cudaMemcpyDeviceToDevice, s));

@@ -170,6 +170,7 @@ struct QmsCudaMoe {
     uint8_t *dn;         // [X] experts of down column stages
     size_t gu_expert, dn_expert, weight_bytes;
     int stream_ok;       // batch-1 streaming kernels usable for this shape
+    int mma_min_t;       // T from which the grouped tensor-core kernels run (0: never)
     // scratch, sized for cap_T tokens
     int cap_T;
     void *scratch;
@@ -227,5 +228,11 @@ struct StreamScratch {                 // bytes of the batch-1 kernel's exchange
     size_t lg_flagged, stamps, aq_flagged, part_gu, fin;
 };
 int stream_scratch_sizes(const QmsCudaMoe *m, StreamScratch *sz);
+
+// batched tensor-core kernels (qms_moe_mma.cu), T >= mma_min_t
+int mma_supported(const QmsCudaMoe *m);
+int mma_prepare(QmsCudaMoe *m);
+int mma_reserve(QmsCudaMoe *m, int T);
+int mma_forward(QmsCudaMoe *m, int T, const float *resid, float *out, cudaStream_t s);
 
 }  // namespace qms

@@ -126,6 +126,18 @@ def test_moe_edge_cases(cuda, oracle):
     m2.close()
 
 
+@pytest.mark.parametrize("shape,T,down", [("tiny", 16, 2), ("tiny", 70, 3), ("30b", 16, 2), ("30b", 130, 2),
+                                          ("235b", 16, 2), ("235b", 64, 3), ("235b", 200, 2)])
+def test_moe_grouped_mma_matches_oracle(cuda, oracle, shape, T, down):
+    """T >= 16: expert-grouped tcgen05 kind::i8 GEMMs (partial and multiple 64-slot tiles per expert,
+    Q4_0 and Q4_1 down) against the oracle, with the batch bars."""
+    layer = synth.make_moe_layer(shape, seed=91 + T, down_type=down)
+    xn = synth.make_hidden(layer.n_embd, T, seed=93 + T)
+    m, out, sel, w, logits = _run(cuda, layer, xn)
+    _check(oracle, layer, xn, out, sel, w, logits, f"mma {shape} T={T} down={down}")
+    m.close()
+
+
 @pytest.mark.parametrize("shape", ["tiny", "30b"])
 def test_decode_routing_edge_cases(cuda, oracle, shape):
     """Batch-1 kernel (one call per token): its stream starts on the float ranking and is checked

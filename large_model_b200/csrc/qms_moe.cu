@@ -3,10 +3,11 @@
 //
 // Reference: moe() in src/model.c:1032-1167 with moe_group_fast (src/model.c:969-1007).
 // Batch-1 decode (T == 1) runs the streaming kernels of qms_moe_stream.cu. Other T run:
-//   k_moe_router   X CTAs: Q8 quantisation of xn (src/kernels.c:34-53), router logits in the
-//                  reference's exact F32 order (src/kernels.c:202-219); the last CTA to finish
-//                  does softmax / top-k / renormalisation (src/model.c:1045-1064) for T <= 4,
-//                  k_moe_topk does it with one CTA per token for larger T.
+//   k_moe_router   T <= 4: X CTAs: Q8 quantisation of xn (src/kernels.c:34-53), router logits
+//                  in the reference's exact F32 order (src/kernels.c:202-219); the last CTA to
+//                  finish does softmax / top-k / renormalisation (src/model.c:1045-1064).
+//   larger T       k_quantize_rows, k_router_tiled (the same exact-order logits, tiled over
+//                  32 tokens x 32 experts in shared memory), k_moe_topk (one CTA per token).
 //   k_moe_gate_up  one warp per (slot, f): gate row f and up row f of the slot's expert against
 //                  the token's Q8 row (phase 1, :979-988), a = silu(g) * u (:994); the CTA that
 //                  completes a 32-row group re-quantises it to Q8 (phase 2, :995).
@@ -130,6 +131,101 @@ __global__ void __launch_bounds__(256) k_moe_topk(const float *__restrict__ logi
     pdl_wait();
     const int t = blockIdx.x;
     topk_token(logits + (size_t)t * X, X, K, sel + t * K, wts + t * K, s_sel);
+}
+
+// ---- router for larger T: Q8 rows, then logits tiled over (tokens x experts) ----------------------
+// One warp per 32-block of xn: the quantiser of src/kernels.c:34-53.
+__global__ void __launch_bounds__(256) k_quantize_rows(const float *__restrict__ xn, int64_t nblocks,
+                                                       int8_t *__restrict__ xq_q, float *__restrict__ xq_d,
+                                                       int *__restrict__ xq_s) {
+    const int lane = threadIdx.x & 31;
+    pdl_wait();
+    for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < nblocks;
+         b += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+        const Q8Lane r = quantize_lane(xn[b * 32 + lane]);
+        xq_q[b * 32 + lane] = (int8_t)r.q;
+        if (lane == 0) {
+            xq_d[b] = r.d;
+            xq_s[b] = r.sum;
+        }
+    }
+}
+
+// logits[t][e] for a tile of 32 tokens x 32 experts per CTA, in qms_vec_dot_f32's exact order
+// (src/kernels.c:202-219): thread (k, g) runs lane k's FMA chain for 8 tokens x 8 experts, over
+// shared-memory chunks of 128 elements, then the 16 lanes of a pair reduce with offsets 8, 4, 2, 1.
+constexpr int kRtTile = 32, kRtChunk = 128, kRtStride = kRtChunk + 4;
+__global__ void __launch_bounds__(256) k_router_tiled(const float *__restrict__ W, int X, int E,
+                                                      const float *__restrict__ xn, int T, float *__restrict__ logits) {
+    __shared__ __align__(16) float xs[kRtTile * kRtStride], ws[kRtTile * kRtStride];
+    const int tid = threadIdx.x, k = tid & 15, g = tid >> 4, gt = g >> 2, ge = g & 3;
+    const int t0 = blockIdx.x * kRtTile, e0 = blockIdx.y * kRtTile;
+    pdl_wait();
+    float acc[8][8];
+#pragma unroll
+    for (int a = 0; a < 8; a++)
+#pragma unroll
+        for (int b = 0; b < 8; b++) acc[a][b] = 0.0f;
+    for (int c0 = 0; c0 < E; c0 += kRtChunk) {
+        __syncthreads();
+        for (int i = tid; i < kRtTile * kRtChunk / 4; i += blockDim.x) {   // 32 rows x 32 float4
+            const int r = i / (kRtChunk / 4), c = (i % (kRtChunk / 4)) * 4;
+            const int t = t0 + r, e = e0 + r;
+            const float4 xv = t < T ? __ldg(reinterpret_cast<const float4 *>(xn + (size_t)t * E + c0 + c))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 wv = e < X ? __ldg(reinterpret_cast<const float4 *>(W + (size_t)e * E + c0 + c))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4 *>(xs + r * kRtStride + c) = xv;
+            *reinterpret_cast<float4 *>(ws + r * kRtStride + c) = wv;
+        }
+        __syncthreads();
+#pragma unroll 2
+        for (int st = 0; st < kRtChunk / 16; st++) {
+            const int c = 16 * st + k;
+            float xv[8], wv[8];
+#pragma unroll
+            for (int a = 0; a < 8; a++) xv[a] = xs[(gt * 8 + a) * kRtStride + c];
+#pragma unroll
+            for (int b = 0; b < 8; b++) wv[b] = ws[(ge * 8 + b) * kRtStride + c];
+#pragma unroll
+            for (int a = 0; a < 8; a++)
+#pragma unroll
+                for (int b = 0; b < 8; b++) acc[a][b] = __fmaf_rn(xv[a], wv[b], acc[a][b]);
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 8; a++)
+#pragma unroll
+        for (int b = 0; b < 8; b++) {
+            float v = acc[a][b];
+            v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 8, 16));
+            v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4, 16));
+            v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2, 16));
+            v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1, 16));
+            const int t = t0 + gt * 8 + a, e = e0 + ge * 8 + b;
+            if (k == 0 && t < T && e < X) logits[(size_t)t * X + e] = v;
+        }
+}
+
+// Router stage for any T: the fused one-kernel router for T <= kTopkInRouterMaxT, else quantiser,
+// tiled logits and one top-k CTA per token.
+static int launch_router(const float *router, int X, int E, const float *xn, int T, int K, int8_t *xq_q, float *xq_d,
+                         int *xq_s, float *lg, int *sel, float *wts, int *cnt, cudaStream_t s) {
+    if (T <= kTopkInRouterMaxT || ((uintptr_t)xn & 15) || ((uintptr_t)router & 15)) {
+        const int fused = T <= kTopkInRouterMaxT;
+        k_moe_router<<<X, 256, (size_t)E * 4, s>>>(router, X, E, xn, T, K, xq_q, xq_d, xq_s, lg, sel, wts, cnt, fused);
+        QMS_CK(cudaGetLastError());
+        if (!fused) QMS_CK(launch_pdl(k_moe_topk, dim3(T), dim3(256), 0, s, (const float *)lg, X, K, sel, wts));
+        return QMS_CUDA_OK;
+    }
+    const int64_t nblocks = (int64_t)T * (E / 32);
+    const unsigned qgrid = (unsigned)std::min<int64_t>((nblocks + 7) / 8, 4096);
+    k_quantize_rows<<<qgrid, 256, 0, s>>>(xn, nblocks, xq_q, xq_d, xq_s);
+    QMS_CK(cudaGetLastError());
+    QMS_CK(launch_pdl(k_router_tiled, dim3((T + kRtTile - 1) / kRtTile, (X + kRtTile - 1) / kRtTile), dim3(256), 0, s,
+                      router, X, E, xn, T, lg));
+    QMS_CK(launch_pdl(k_moe_topk, dim3(T), dim3(256), 0, s, (const float *)lg, X, K, sel, wts));
+    return QMS_CUDA_OK;
 }
 
 // ---- gate/up + SwiGLU + Q8 re-quantisation (any T) -------------------------------------------
@@ -504,15 +600,10 @@ int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int 
     if (T == 1 && m->stream_ok && ((uintptr_t)xn & 15) == 0) {
         if ((rc = stream_forward_bs1(m, xn, out, resid, s))) return rc;
     } else {
-        const int topk_in_router = T <= kTopkInRouterMaxT;
-        const size_t rsmem = (size_t)m->E * 4;
         if (m->timing) QMS_CK(cudaEventRecord(m->ev[0], s));
-        k_moe_router<<<m->X, 256, rsmem, s>>>(m->router, m->X, m->E, xn, T, m->K, m->xq_q, m->xq_d, m->xq_s,
-                                             m->logits, m->sel, m->wts, m->cnt, topk_in_router);
-        QMS_CK(cudaGetLastError());
-        if (!topk_in_router)
-            QMS_CK(launch_pdl(k_moe_topk, dim3(T), dim3(256), 0, s, (const float *)m->logits, m->X, m->K, m->sel,
-                              m->wts));
+        if ((rc = launch_router(m->router, m->X, m->E, xn, T, m->K, m->xq_q, m->xq_d, m->xq_s, m->logits, m->sel,
+                                m->wts, m->cnt, s)))
+            return rc;
         if (m->timing) {
             QMS_CK(cudaEventRecord(m->ev[1], s));
             QMS_CK(cudaEventRecord(m->ev[2], s));
@@ -672,10 +763,5 @@ extern "C" int qms_cuda_moe_route_noalloc(const float *router, int n_expert, int
     int *cnt = (int *)(p + kNaXqQ + kNaXqD + kNaXqS + kNaLogits);
     const cudaStream_t s = (cudaStream_t)stream;
     QMS_CK(cudaMemsetAsync(cnt, 0, sizeof(int), s));   // the arrival counter must start at zero
-    const int topk_in_router = T <= kTopkInRouterMaxT;
-    k_moe_router<<<X, 256, (size_t)E * 4, s>>>(router, X, E, xn, T, K, xq_q, xq_d, xq_s, lg, sel, wts, cnt,
-                                               topk_in_router);
-    QMS_CK(cudaGetLastError());
-    if (!topk_in_router) QMS_CK(launch_pdl(k_moe_topk, dim3(T), dim3(256), 0, s, (const float *)lg, X, K, sel, wts));
-    return QMS_CUDA_OK;
+    return launch_router(router, X, E, xn, T, K, xq_q, xq_d, xq_s, lg, sel, wts, cnt, s);
 }

@@ -31,9 +31,17 @@ constexpr int kMmaM = 128;                 // weight rows per tile (tensor-core 
 constexpr int kMmaN = 64;                  // slots per tile (tensor-core N)
 constexpr int kMmaRaw = 2;                 // raw stages in flight (TMA ring)
 constexpr int kMmaA = 8;                   // converted A blocks in flight
-constexpr int kMmaTm = 4;                  // TMEM int32 buffers (64 columns each)
-constexpr int kMmaThreads = 384;           // warp 0 TMA, 1 MMA, 2-3 convert, 4-11 epilogue
+#ifndef QMS_MMA_TMEM_BUFS
+#define QMS_MMA_TMEM_BUFS 8
+#endif
+constexpr int kMmaTm = QMS_MMA_TMEM_BUFS;  // TMEM int32 buffers (64 columns each; 8 fill all 512)
+#ifndef QMS_MMA_CONV_WARPS
+#define QMS_MMA_CONV_WARPS 4
+#endif
+constexpr int kMmaConvWarps = QMS_MMA_CONV_WARPS;   // Q4 -> int8 converter warps
 constexpr int kMmaEpiWarps = 8;
+constexpr int kMmaEpi0 = 2 + kMmaConvWarps;         // first epilogue warp
+constexpr int kMmaThreads = (2 + kMmaConvWarps + kMmaEpiWarps) * 32;   // warp 0 TMA, 1 MMA, converters, epilogue
 constexpr uint32_t kMmaSpin = 1u << 22;
 constexpr uint32_t kBTile = 2048;          // one block of a tile's B operand: 64 slots x 32 bytes
 constexpr uint32_t kABlock = 4096;         // one block of the A operand: 128 rows x 32 bytes
@@ -87,6 +95,29 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Packed pairs of fp32 (sm_100 f32x2 instructions): two lanes of work per instruction.
+__device__ __forceinline__ unsigned long long f2_bits(float2 v) {
+    return ((unsigned long long)__float_as_uint(v.y) << 32) | __float_as_uint(v.x);
+}
+__device__ __forceinline__ float2 f2_from(unsigned long long b) {
+    return make_float2(__uint_as_float((uint32_t)b), __uint_as_float((uint32_t)(b >> 32)));
+}
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+    return f2_from(d);
+}
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return f2_from(d);
+}
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return f2_from(d);
+}
+
 // Bounded wait on an mbarrier phase; on timeout set the CTA's abort flag and the error bit.
 __device__ __forceinline__ bool mma_wait(uint64_t *bar, uint32_t parity, volatile int *abort, int *err) {
     uint32_t n = 0;
@@ -97,7 +128,7 @@ __device__ __forceinline__ bool mma_wait(uint64_t *bar, uint32_t parity, volatil
             atomicOr(err, MMA_ERR);
             return false;
         }
-        __nanosleep(64);
+        if (n > 64) __nanosleep(32);
     }
     return true;
 }
@@ -244,10 +275,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
         s_abort = 0;
         for (int i = 0; i < kMmaRaw; i++) {
             mbar_init(&raw_full[i], 1);
-            mbar_init(&raw_empty[i], 2 + kMmaEpiWarps);
+            mbar_init(&raw_empty[i], kMmaConvWarps + kMmaEpiWarps);
         }
         for (int i = 0; i < kMmaA; i++) {
-            mbar_init(&a_full[i], 2);
+            mbar_init(&a_full[i], kMmaConvWarps);
             mbar_init(&a_empty[i], 1);
         }
         for (int i = 0; i < kMmaTm; i++) {
@@ -337,8 +368,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
                 }
             }
         }
-    } else if (warp < 4) {                                      // ---- converters: Q4 -> int8 A blocks
-        const int ct = threadIdx.x - 64;                        // 0..63
+    } else if (warp < kMmaEpi0) {                               // ---- converters: Q4 -> int8 A blocks
+        const int ct = threadIdx.x - 64;                        // 0 .. 32 * kMmaConvWarps - 1
         bool ok = true;
         for (int b = 0; b < nb && ok; b++) {
             const int s = b / SB, bl = b % SB, as = b % kMmaA;
@@ -348,8 +379,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
             const uint8_t *rs = raw + (size_t)(s % kMmaRaw) * RSLOT;
             uint8_t *ab = abuf + as * kABlock;
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int R = ct + 64 * h;
+            for (int h = 0; h < 4 / kMmaConvWarps; h++) {
+                const int R = ct + 32 * kMmaConvWarps * h;
                 const uint8_t *src;
                 if (GU) {
                     const int c = (R >> 6) * 8 + ((R & 63) >> 3), rr = R & 7;
@@ -362,13 +393,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
                 *reinterpret_cast<uint4 *>(ab + (R >> 3) * 128 + (R & 7) * 16) = lo;
                 *reinterpret_cast<uint4 *>(ab + 2048 + (R >> 3) * 128 + (R & 7) * 16) = hi;
             }
-            fence_async_smem();
+            fence_async_smem();                                 // generic-proxy writes -> tensor core
             __syncwarp();
             if (lane == 0) mbar_arrive(&a_full[as]);
             if (bl == SB - 1 && lane == 0) mbar_arrive(&raw_empty[s % kMmaRaw]);
         }
     } else {                                                    // ---- epilogue: 8 warps
-        const int q = warp & 3, ch = (warp - 4) >> 2, R = 32 * q + lane;
+        const int q = warp & 3, ch = (warp - kMmaEpi0) >> 2, R = 32 * q + lane;
         float acc[32];
 #pragma unroll
         for (int j = 0; j < 32; j++) acc[j] = 0.0f;
@@ -395,11 +426,22 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
             }
             const float *sx = reinterpret_cast<const float *>(rs + RA + RB) + bl * kMmaN + ch * 32;
             const int *su = reinterpret_cast<const int *>(rs + RA + RB + RS) + bl * kMmaN + ch * 32;
+            // int32 -> float without the conversion unit: |P| < 2^22, so 2^23 + 2^22 + P is exact
+            // in a float's mantissa; pairs of columns go through the packed f32x2 pipe
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const float xd = sx[j];
-                if (Q1) acc[j] = fmaf((float)(int)r[j], dw * xd, fmaf(mw, xd * (float)su[j], acc[j]));
-                else acc[j] = fmaf((float)(int)r[j], dw * xd, acc[j]);
+            for (int j = 0; j < 32; j += 2) {
+                const float2 xd = *reinterpret_cast<const float2 *>(sx + j);
+                float2 p2 = make_float2(__int_as_float((int)r[j] + 0x4B400000), __int_as_float((int)r[j + 1] + 0x4B400000));
+                p2 = f2_add(p2, make_float2(-12582912.0f, -12582912.0f));
+                const float2 sc = f2_mul(make_float2(dw, dw), xd);
+                float2 ac = make_float2(acc[j], acc[j + 1]);
+                if (Q1) {
+                    const float2 mc = f2_mul(make_float2(mw, mw), make_float2(xd.x * (float)su[j], xd.y * (float)su[j + 1]));
+                    ac = f2_add(ac, mc);
+                }
+                ac = f2_fma(p2, sc, ac);
+                acc[j] = ac.x;
+                acc[j + 1] = ac.y;
             }
             __syncwarp();
             if (bl == SB - 1 && lane == 0) mbar_arrive(&raw_empty[s % kMmaRaw]);

@@ -30,7 +30,8 @@ namespace qms {
 constexpr int kMmaM = 128;                 // weight rows per tile (tensor-core M)
 constexpr int kMmaN = 64;                  // slots per tile (tensor-core N)
 constexpr int kMmaRaw = 2;                 // raw stages in flight (TMA ring)
-constexpr int kMmaA = 8;                   // converted A blocks in flight
+constexpr int kMmaA = 16;                  // converted A blocks in flight
+constexpr int kMmaGrp = 4;                 // blocks a converter pass expands (one fence, one wait)
 #ifndef QMS_MMA_TMEM_BUFS
 #define QMS_MMA_TMEM_BUFS 8
 #endif
@@ -38,10 +39,12 @@ constexpr int kMmaTm = QMS_MMA_TMEM_BUFS;  // TMEM int32 buffers (64 columns eac
 #ifndef QMS_MMA_CONV_WARPS
 #define QMS_MMA_CONV_WARPS 4
 #endif
-constexpr int kMmaConvWarps = QMS_MMA_CONV_WARPS;   // Q4 -> int8 converter warps
-constexpr int kMmaEpiWarps = 8;
+constexpr int kMmaConvWarps = QMS_MMA_CONV_WARPS;   // Q4 -> int8 converter warps (4: one row per thread)
+constexpr int kMmaEpiWarps = 8;                     // 2 per TMEM lane quarter, 32 columns each
 constexpr int kMmaEpi0 = 2 + kMmaConvWarps;         // first epilogue warp
 constexpr int kMmaThreads = (2 + kMmaConvWarps + kMmaEpiWarps) * 32;   // warp 0 TMA, 1 MMA, converters, epilogue
+static_assert(kMmaConvWarps * 32 == kMmaM, "one A row per converter thread");
+static_assert(kMmaA % kMmaGrp == 0 && 8 % kMmaGrp == 0, "converter groups tile the ring and every stage");
 constexpr uint32_t kMmaSpin = 1u << 22;
 constexpr uint32_t kBTile = 2048;          // one block of a tile's B operand: 64 slots x 32 bytes
 constexpr uint32_t kABlock = 4096;         // one block of the A operand: 128 rows x 32 bytes
@@ -81,19 +84,6 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// 32 TMEM lanes (this warp's quarter) x 32 consecutive 32-bit columns.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
 
 // Packed pairs of fp32 (sm_100 f32x2 instructions): two lanes of work per instruction.
 __device__ __forceinline__ unsigned long long f2_bits(float2 v) {
@@ -259,7 +249,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
     uint64_t *raw_full = bars, *raw_empty = raw_full + kMmaRaw;
     uint64_t *a_full = raw_empty + kMmaRaw, *a_empty = a_full + kMmaA;
     uint64_t *tm_full = a_empty + kMmaA, *tm_empty = tm_full + kMmaTm;
-    float *xch = reinterpret_cast<float *>(tm_empty + kMmaTm);   // [2][2][32][33] up values for SwiGLU
+    float *xch = reinterpret_cast<float *>(raw);               // after the K loop: [2][2][32][33] up sums
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
 
@@ -347,18 +337,32 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
     } else if (warp == 1) {                                     // ---- MMA issuer
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_s8(kMmaM, kMmaN);
-            int issued = 0;
-            for (int b = 0; b < nb; b++) {
-                const int as = b % kMmaA, tb = b % kMmaTm, s = b / SB, bl = b % SB;
-                if (!mma_wait(&a_full[as], (b / kMmaA) & 1, abort_flag, a.err)) break;
-                if (b >= kMmaTm && !mma_wait(&tm_empty[tb], ((b / kMmaTm) & 1) ^ 1, abort_flag, a.err)) break;
-                tc_fence_after();
-                const uint64_t da = umma_desc(smem_u32(abuf + as * kABlock), 2048, 128);
-                const uint64_t db = umma_desc(smem_u32(raw + (size_t)(s % kMmaRaw) * RSLOT + RA + bl * kBTile), 1024, 128);
-                umma_s8(tmem + tb * kMmaN, da, db, idesc);
-                umma_commit(&tm_full[tb]);
-                umma_commit(&a_empty[as]);
-                issued++;
+            // one pass per converter group: the last slot's barrier implies the group's earlier ones
+            // (every converter warp arrives them in order), likewise for the epilogue's TMEM buffers
+            const uint32_t a0 = smem_u32(abuf), r0 = smem_u32(raw) + RA;
+            int issued = 0, s = 0, bl0 = 0;
+            for (int b0 = 0; b0 < nb; b0 += kMmaGrp) {
+                const int bl = b0 + kMmaGrp - 1;
+                if (!mma_wait(&a_full[bl % kMmaA], (bl / kMmaA) & 1, abort_flag, a.err)) break;
+                if (bl >= kMmaTm) {                             // TMEM buffers read out by the epilogue
+                    if (!mma_wait(&tm_empty[bl % kMmaTm], ((bl / kMmaTm) & 1) ^ 1, abort_flag, a.err)) break;
+                    tc_fence_after();
+                }
+                const uint32_t rb = r0 + (uint32_t)(s % kMmaRaw) * RSLOT + (uint32_t)bl0 * kBTile;
+#pragma unroll
+                for (int g = 0; g < kMmaGrp; g++) {
+                    const int b = b0 + g;
+                    const uint64_t da = umma_desc(a0 + (uint32_t)(b % kMmaA) * kABlock, 2048, 128);
+                    const uint64_t db = umma_desc(rb + (uint32_t)g * kBTile, 1024, 128);
+                    umma_s8(tmem + (b % kMmaTm) * kMmaN, da, db, idesc);
+                    umma_commit(&tm_full[b % kMmaTm]);
+                }
+                issued += kMmaGrp;
+                bl0 += kMmaGrp;
+                if (bl0 == SB) {
+                    bl0 = 0;
+                    s++;
+                }
             }
             // the tensor core must be idle before TMEM is freed
             if (issued > 0) {
@@ -369,88 +373,138 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
             }
         }
     } else if (warp < kMmaEpi0) {                               // ---- converters: Q4 -> int8 A blocks
-        const int ct = threadIdx.x - 64;                        // 0 .. 32 * kMmaConvWarps - 1
+        // thread ct expands row ct of kMmaGrp blocks per pass: one fence and one barrier arrival
+        // per block group rather than per block
+        const int R = threadIdx.x - 64;                         // 0..127 (kMmaConvWarps == 4)
         bool ok = true;
-        for (int b = 0; b < nb && ok; b++) {
-            const int s = b / SB, bl = b % SB, as = b % kMmaA;
-            if (bl == 0) ok = __all_sync(0xffffffffu, mma_wait(&raw_full[s % kMmaRaw], (s / kMmaRaw) & 1, abort_flag, a.err));
-            if (ok && b >= kMmaA) ok = __all_sync(0xffffffffu, mma_wait(&a_empty[as], ((b / kMmaA) & 1) ^ 1, abort_flag, a.err));
+        int s = 0, bl0 = 0;
+        for (int b0 = 0; b0 < nb && ok; b0 += kMmaGrp) {
+            if (bl0 == 0) ok = __all_sync(0xffffffffu, mma_wait(&raw_full[s % kMmaRaw], (s / kMmaRaw) & 1, abort_flag, a.err));
+            for (int g = 0; g < kMmaGrp && ok; g++) {
+                const int b = b0 + g;
+                if (b >= kMmaA) ok = __all_sync(0xffffffffu, mma_wait(&a_empty[b % kMmaA], ((b / kMmaA) & 1) ^ 1, abort_flag, a.err));
+            }
             if (!ok) break;
             const uint8_t *rs = raw + (size_t)(s % kMmaRaw) * RSLOT;
-            uint8_t *ab = abuf + as * kABlock;
+            const uint8_t *src;
+            uint32_t bstride;                                   // bytes from block bl to bl + 1 in the raw stage
+            if (GU) {
+                const int c = (R >> 6) * 8 + ((R & 63) >> 3), rr = R & 7;
+                src = rs + c * CP + (rr * SB + bl0) * 16;
+                bstride = 16;
+            } else {
+                src = rs + bl0 * (Q1 ? 2560 : 2304) + R * 16;
+                bstride = Q1 ? 2560 : 2304;
+            }
+            uint4 v[kMmaGrp];
 #pragma unroll
-            for (int h = 0; h < 4 / kMmaConvWarps; h++) {
-                const int R = ct + 32 * kMmaConvWarps * h;
-                const uint8_t *src;
-                if (GU) {
-                    const int c = (R >> 6) * 8 + ((R & 63) >> 3), rr = R & 7;
-                    src = rs + c * CP + (rr * SB + bl) * 16;
-                } else {
-                    src = rs + bl * (Q1 ? 2560 : 2304) + R * 16;
-                }
+            for (int g = 0; g < kMmaGrp; g++) v[g] = *reinterpret_cast<const uint4 *>(src + g * bstride);
+#pragma unroll
+            for (int g = 0; g < kMmaGrp; g++) {
                 uint4 lo, hi;
-                nib_to_s8(*reinterpret_cast<const uint4 *>(src), !Q1, lo, hi);
+                nib_to_s8(v[g], !Q1, lo, hi);
+                uint8_t *ab = abuf + ((b0 + g) % kMmaA) * kABlock;
                 *reinterpret_cast<uint4 *>(ab + (R >> 3) * 128 + (R & 7) * 16) = lo;
                 *reinterpret_cast<uint4 *>(ab + 2048 + (R >> 3) * 128 + (R & 7) * 16) = hi;
             }
             fence_async_smem();                                 // generic-proxy writes -> tensor core
             __syncwarp();
-            if (lane == 0) mbar_arrive(&a_full[as]);
-            if (bl == SB - 1 && lane == 0) mbar_arrive(&raw_empty[s % kMmaRaw]);
+            if (lane == 0)
+                for (int g = 0; g < kMmaGrp; g++) mbar_arrive(&a_full[(b0 + g) % kMmaA]);
+            bl0 += kMmaGrp;
+            if (bl0 == SB) {
+                if (lane == 0) mbar_arrive(&raw_empty[s % kMmaRaw]);
+                bl0 = 0;
+                s++;
+            }
         }
     } else {                                                    // ---- epilogue: 8 warps
-        const int q = warp & 3, ch = (warp - kMmaEpi0) >> 2, R = 32 * q + lane;
+        // two blocks per pass: one wait, one TMEM round trip and one release per pair, so the
+        // per-block bookkeeping stays small next to the 2 x 32 columns of scaling
+        const int q = warp & 3, cq = (warp - kMmaEpi0) >> 2, R = 32 * q + lane;   // lane quarter, column half
         float acc[32];
 #pragma unroll
         for (int j = 0; j < 32; j++) acc[j] = 0.0f;
         bool ok = true;
-        for (int b = 0; b < nb && ok; b++) {
-            const int tb = b % kMmaTm, s = b / SB, bl = b % SB;
-            ok = __all_sync(0xffffffffu, mma_wait(&tm_full[tb], (b / kMmaTm) & 1, abort_flag, a.err));
+        int s = 0, bl = 0;
+        for (int b = 0; b < nb && ok; b += 2) {
+            const int b1 = b + 1;                               // nb % 8 == 0: pairs never straddle the end
+            ok = __all_sync(0xffffffffu, mma_wait(&tm_full[b1 % kMmaTm], (b1 / kMmaTm) & 1, abort_flag, a.err));
             if (!ok) break;
+            if (warp == kMmaEpi0 && lane == 0) {                // the MMAs have read their A blocks
+                mbar_arrive(&a_empty[b % kMmaA]);
+                mbar_arrive(&a_empty[b1 % kMmaA]);
+            }
             tc_fence_after();
-            uint32_t r[32];
-            tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + tb * kMmaN + ch * 32, r);
+            uint32_t r[2][32];
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(r[i][0]), "=r"(r[i][1]), "=r"(r[i][2]), "=r"(r[i][3]), "=r"(r[i][4]), "=r"(r[i][5]),
+                      "=r"(r[i][6]), "=r"(r[i][7]), "=r"(r[i][8]), "=r"(r[i][9]), "=r"(r[i][10]), "=r"(r[i][11]),
+                      "=r"(r[i][12]), "=r"(r[i][13]), "=r"(r[i][14]), "=r"(r[i][15]), "=r"(r[i][16]), "=r"(r[i][17]),
+                      "=r"(r[i][18]), "=r"(r[i][19]), "=r"(r[i][20]), "=r"(r[i][21]), "=r"(r[i][22]), "=r"(r[i][23]),
+                      "=r"(r[i][24]), "=r"(r[i][25]), "=r"(r[i][26]), "=r"(r[i][27]), "=r"(r[i][28]), "=r"(r[i][29]),
+                      "=r"(r[i][30]), "=r"(r[i][31])
+                    : "r"(tmem + ((uint32_t)(32 * q) << 16) + ((b + i) % kMmaTm) * kMmaN + cq * 32));
+            }
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tm_empty[tb]);
-            const uint8_t *rs = raw + (size_t)(s % kMmaRaw) * RSLOT;
-            float dw, mw = 0.0f;
-            if (GU) {
-                const int c = (R >> 6) * 8 + ((R & 63) >> 3), rr = R & 7;
-                dw = h2f(*reinterpret_cast<const uint16_t *>(rs + c * CP + 8 * SB * 16 + (rr * SB + bl) * 2));
-            } else {
-                const uint8_t *pb = rs + bl * (Q1 ? 2560 : 2304);
-                dw = h2f(*reinterpret_cast<const uint16_t *>(pb + 2048 + R * 2));
-                if (Q1) mw = h2f(*reinterpret_cast<const uint16_t *>(pb + 2304 + R * 2));
+            if (lane == 0) {
+                mbar_arrive(&tm_empty[b % kMmaTm]);
+                mbar_arrive(&tm_empty[b1 % kMmaTm]);
             }
-            const float *sx = reinterpret_cast<const float *>(rs + RA + RB) + bl * kMmaN + ch * 32;
-            const int *su = reinterpret_cast<const int *>(rs + RA + RB + RS) + bl * kMmaN + ch * 32;
-            // int32 -> float without the conversion unit: |P| < 2^22, so 2^23 + 2^22 + P is exact
-            // in a float's mantissa; pairs of columns go through the packed f32x2 pipe
+            const uint8_t *rs = raw + (size_t)(s % kMmaRaw) * RSLOT;
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-                const float2 xd = *reinterpret_cast<const float2 *>(sx + j);
-                float2 p2 = make_float2(__int_as_float((int)r[j] + 0x4B400000), __int_as_float((int)r[j + 1] + 0x4B400000));
-                p2 = f2_add(p2, make_float2(-12582912.0f, -12582912.0f));
-                const float2 sc = f2_mul(make_float2(dw, dw), xd);
-                float2 ac = make_float2(acc[j], acc[j + 1]);
-                if (Q1) {
-                    const float2 mc = f2_mul(make_float2(mw, mw), make_float2(xd.x * (float)su[j], xd.y * (float)su[j + 1]));
-                    ac = f2_add(ac, mc);
+            for (int i = 0; i < 2; i++) {
+                float dw, mw = 0.0f;
+                if (GU) {
+                    const int c = (R >> 6) * 8 + ((R & 63) >> 3), rr = R & 7;
+                    dw = h2f(*reinterpret_cast<const uint16_t *>(rs + c * CP + 8 * SB * 16 + (rr * SB + bl + i) * 2));
+                } else {
+                    const uint8_t *pb = rs + (bl + i) * (Q1 ? 2560 : 2304);
+                    dw = h2f(*reinterpret_cast<const uint16_t *>(pb + 2048 + R * 2));
+                    if (Q1) mw = h2f(*reinterpret_cast<const uint16_t *>(pb + 2304 + R * 2));
                 }
-                ac = f2_fma(p2, sc, ac);
-                acc[j] = ac.x;
-                acc[j + 1] = ac.y;
+                const float *sx = reinterpret_cast<const float *>(rs + RA + RB) + (bl + i) * kMmaN + cq * 32;
+                const int *su = reinterpret_cast<const int *>(rs + RA + RB + RS) + (bl + i) * kMmaN + cq * 32;
+                // int32 -> float without the conversion unit: |P| < 2^22, so 2^23 + 2^22 + P is exact
+                // in a float's mantissa; pairs of columns go through the packed f32x2 pipe
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float2 xd = *reinterpret_cast<const float2 *>(sx + j);
+                    float2 p2 = make_float2(__int_as_float((int)r[i][j] + 0x4B400000),
+                                            __int_as_float((int)r[i][j + 1] + 0x4B400000));
+                    p2 = f2_add(p2, make_float2(-12582912.0f, -12582912.0f));
+                    const float2 sc = f2_mul(make_float2(dw, dw), xd);
+                    float2 ac = make_float2(acc[j], acc[j + 1]);
+                    if (Q1) {
+                        const float2 mc = f2_mul(make_float2(mw, mw), make_float2(xd.x * (float)su[j], xd.y * (float)su[j + 1]));
+                        ac = f2_add(ac, mc);
+                    }
+                    ac = f2_fma(p2, sc, ac);
+                    acc[j] = ac.x;
+                    acc[j + 1] = ac.y;
+                }
             }
             __syncwarp();
-            if (bl == SB - 1 && lane == 0) mbar_arrive(&raw_empty[s % kMmaRaw]);
+            bl += 2;
+            if (bl == SB) {
+                if (lane == 0) mbar_arrive(&raw_empty[s % kMmaRaw]);
+                bl = 0;
+                s++;
+            }
         }
+        // every epilogue warp is done with the raw stages before they hold the exchange
+        asm volatile("bar.sync 1, %0;" ::"n"(kMmaEpiWarps * 32) : "memory");
         if (GU) {
             // rows 0-31 / 64-95 (lane quarters 0, 2) are gate rows f, 32-63 / 96-127 the up rows of
             // the same f: the up warps hand their sums over, the gate warps finish the groups
             const int th = q >> 1;                                // which 64-row tile
-            float *xu = xch + ((th * 2 + ch) * 32 + lane) * 33;
+            float *xu = xch + ((th * 2 + cq) * 32 + lane) * 33;
             if (q & 1)
 #pragma unroll
                 for (int j = 0; j < 32; j++) xu[j] = acc[j];
@@ -459,7 +513,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
                 const int f = 64 * mt + 32 * th + lane, grp = f >> 5;
 #pragma unroll
                 for (int j = 0; j < 32; j++) {
-                    const int col = ch * 32 + j;
+                    const int col = cq * 32 + j;
                     if (col >= ncol) continue;                   // warp-uniform
                     const float g = acc[j], u = xu[j];
                     const float av = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
@@ -476,7 +530,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
             const int row = mt * kMmaM + R;
 #pragma unroll
             for (int j = 0; j < 32; j++) {
-                const int col = ch * 32 + j;
+                const int col = cq * 32 + j;
                 if (col >= ncol) continue;
                 const int slot = __ldcg(a.wk.slots + soff + col);
                 a.wk.dn[(size_t)slot * a.E + row] = acc[j];
@@ -507,7 +561,7 @@ __global__ void __launch_bounds__(256) k_mma_combine(const float *__restrict__ d
 static size_t mma_smem(const QmsCudaMoe *m, int SB, bool gu, bool q1) {
     const size_t RA = raw_a_bytes(gu, m->cgu.GB, SB, q1);
     const size_t RSLOT = (RA + (size_t)SB * kBTile + (size_t)SB * kMmaN * 4 * (q1 ? 2 : 1) + 127) & ~(size_t)127;
-    return kMmaRaw * RSLOT + kMmaA * kABlock + (2 * kMmaRaw + 2 * kMmaA + 2 * kMmaTm) * 8 + 4 * 32 * 33 * 4;
+    return kMmaRaw * RSLOT + kMmaA * kABlock + (2 * kMmaRaw + 2 * kMmaA + 2 * kMmaTm) * 8;
 }
 
 // Device workspace shared by every layer of the process (layers run one after another on a stream).
@@ -544,7 +598,7 @@ int mma_supported(const QmsCudaMoe *m) {
 }
 
 int mma_prepare(QmsCudaMoe *m) {
-    const int SBd = m->nbF % 16 == 0 ? 16 : 8;
+    const int SBd = 8;
     auto set = [](const void *k, size_t smem) -> int {
         QMS_CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         return QMS_CUDA_OK;
@@ -580,7 +634,7 @@ int mma_forward(QmsCudaMoe *m, int T, const float *resid, float *out, cudaStream
     }
     mma_layout(m, T, &w, &need, (char *)g_mma_ws.p);
     const int S = T * m->K, maxT = S / kMmaN + m->X;
-    const int SBd = m->nbF % 16 == 0 ? 16 : 8;
+    const int SBd = 8;                                  // down stages: 8 blocks (F/32 % 8 == 0)
     QMS_CK(launch_pdl(k_mma_group, dim3(1), dim3(1024), 0, s, (const int *)m->sel, S, m->X, maxT, w));
     QMS_CK(launch_pdl(k_mma_gather, dim3(maxT, 8), dim3(128), 0, s, (const int8_t *)m->xq_q, (const float *)m->xq_d,
                       (const int *)nullptr, m->nbE, m->K, w));

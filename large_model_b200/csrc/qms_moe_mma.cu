@@ -28,7 +28,8 @@
 namespace qms {
 
 constexpr int kMmaM = 128;                 // weight rows per tile (tensor-core M)
-constexpr int kMmaN = 64;                  // slots per tile (tensor-core N)
+constexpr int kMmaN = 64;                  // slots per tile (tensor-core N) at larger loads
+constexpr int kMmaNs = 16;                 // slots per tile when experts average few slots (batched decode)
 constexpr int kMmaRaw = 2;                 // raw stages in flight (TMA ring)
 constexpr int kMmaA = 16;                  // converted A blocks in flight
 constexpr int kMmaGrp = 4;                 // blocks a converter pass expands (one fence, one wait)
@@ -46,7 +47,6 @@ constexpr int kMmaThreads = (2 + kMmaConvWarps + kMmaEpiWarps) * 32;   // warp 0
 static_assert(kMmaConvWarps * 32 == kMmaM, "one A row per converter thread");
 static_assert(kMmaA % kMmaGrp == 0 && 8 % kMmaGrp == 0, "converter groups tile the ring and every stage");
 constexpr uint32_t kMmaSpin = 1u << 22;
-constexpr uint32_t kBTile = 2048;          // one block of a tile's B operand: 64 slots x 32 bytes
 constexpr uint32_t kABlock = 4096;         // one block of the A operand: 128 rows x 32 bytes
 constexpr uint32_t kChunkPad = 16;         // gap after each raw gate/up chunk: rows of different
                                            // chunks start in different shared-memory banks
@@ -108,6 +108,26 @@ __device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
     return f2_from(d);
 }
 
+// 32 TMEM lanes (this warp's quarter) x C consecutive 32-bit columns, C = 8 or 32 (not waited).
+template <int C>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[C]) {
+    if constexpr (C == 32) {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+              "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+              "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+            : "r"(taddr));
+    } else {
+        static_assert(C == 8, "8 or 32 columns");
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                     : "r"(taddr));
+    }
+}
+
 // Bounded wait on an mbarrier phase; on timeout set the CTA's abort flag and the error bit.
 __device__ __forceinline__ bool mma_wait(uint64_t *bar, uint32_t parity, volatile int *abort, int *err) {
     uint32_t n = 0;
@@ -145,8 +165,8 @@ struct MmaWork {
     float *dn;         // [T*K][E] down rows per slot
 };
 
-// One CTA: slots s = t*K + j grouped by expert sel[s]; tiles of 64 slots per expert.
-__global__ void __launch_bounds__(1024) k_mma_group(const int *__restrict__ sel, int S, int X, int maxT, MmaWork w) {
+// One CTA: slots s = t*K + j grouped by expert sel[s]; tiles of nw slots per expert.
+__global__ void __launch_bounds__(1024) k_mma_group(const int *__restrict__ sel, int S, int X, int maxT, int nw, MmaWork w) {
     __shared__ int s_cnt[256], s_off[257], s_toff[257];
     const int tid = threadIdx.x;
     pdl_wait();
@@ -163,7 +183,7 @@ __global__ void __launch_bounds__(1024) k_mma_group(const int *__restrict__ sel,
             s_off[e] = o;
             s_toff[e] = t;
             o += s_cnt[e];
-            t += (s_cnt[e] + kMmaN - 1) / kMmaN;
+            t += (s_cnt[e] + nw - 1) / nw;
         }
         s_off[X] = o;
         s_toff[X] = t < maxT ? t : maxT;
@@ -185,26 +205,28 @@ __global__ void __launch_bounds__(1024) k_mma_group(const int *__restrict__ sel,
 
 // B operands of every tile: column j of tile (e, n0) is slot slots[off[e] + n0 + j] (zeros past
 // the expert's count). Source row of slot s: s / rdiv (gate/up reads the token's Q8 row, down the
-// slot's). Block b of the tile: [K half][8-slot group][8 slots][16 bytes].
+// slot's). Block b of a tile of nw slots: [K half][nw/8 slot groups][8 slots][16 bytes]. One thread
+// per (slot, K half): blockDim = 2 * nw.
 __global__ void __launch_bounds__(128) k_mma_gather(const int8_t *__restrict__ q, const float *__restrict__ d,
-                                                    const int *__restrict__ sums, int nb, int rdiv, MmaWork w) {
+                                                    const int *__restrict__ sums, int nb, int rdiv, int nw, MmaWork w) {
     const int tl = blockIdx.x;
     pdl_wait();
     if (tl >= __ldcg(w.ntiles)) return;
-    const int tile = __ldcg(w.tiles + tl), e = tile & 0xFFFF, n0 = (tile >> 16) * kMmaN;
-    const int n = min(kMmaN, __ldcg(w.cnt + e) - n0);
+    const int tile = __ldcg(w.tiles + tl), e = tile & 0xFFFF, n0 = (tile >> 16) * nw;
+    const int n = min(nw, __ldcg(w.cnt + e) - n0);
     const int j = threadIdx.x >> 1, h = threadIdx.x & 1;
     const int slot = j < n ? __ldcg(w.slots + __ldcg(w.off + e) + n0 + j) : -1;
     const size_t row = slot >= 0 ? (size_t)(slot / rdiv) : 0;
     const int K = nb * 32;
+    const size_t bt = (size_t)nw * 32;                      // bytes of one block of the tile
     for (int b = blockIdx.y; b < nb; b += gridDim.y) {
         uint4 v = make_uint4(0, 0, 0, 0);
         if (slot >= 0) v = __ldcg(reinterpret_cast<const uint4 *>(q + row * K + b * 32 + h * 16));
-        int8_t *dst = w.bg + ((size_t)tl * nb + b) * kBTile;
-        *reinterpret_cast<uint4 *>(dst + h * 1024 + (j >> 3) * 128 + (j & 7) * 16) = v;
+        int8_t *dst = w.bg + ((size_t)tl * nb + b) * bt;
+        *reinterpret_cast<uint4 *>(dst + h * (nw * 16) + (j >> 3) * 128 + (j & 7) * 16) = v;
         if (h == 0) {
-            w.bs[((size_t)tl * nb + b) * kMmaN + j] = slot >= 0 ? __ldcg(d + row * nb + b) : 0.0f;
-            if (sums) w.bsum[((size_t)tl * nb + b) * kMmaN + j] = slot >= 0 ? __ldcg(sums + row * nb + b) : 0;
+            w.bs[((size_t)tl * nb + b) * nw + j] = slot >= 0 ? __ldcg(d + row * nb + b) : 0.0f;
+            if (sums) w.bsum[((size_t)tl * nb + b) * nw + j] = slot >= 0 ? __ldcg(sums + row * nb + b) : 0;
         }
     }
 }
@@ -233,14 +255,16 @@ __host__ __device__ inline uint32_t raw_a_bytes(bool gu, uint32_t chunk_bytes, i
     return gu ? 16u * (chunk_bytes + kChunkPad) : (uint32_t)SB * (q1 ? 2560u : 2304u);
 }
 
-template <bool GU, bool Q1>
+template <bool GU, bool Q1, int NW>
 __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
+    constexpr int EC = NW / 2;                                  // columns per epilogue warp
+    constexpr uint32_t BT = NW * 32;                            // one block of the B operand
     extern __shared__ __align__(1024) uint8_t smem[];
     const int SB = a.SB, nb = a.nb;
     const uint32_t GB = a.cgu.GB, CP = GB + kChunkPad;       // gate/up chunk bytes, chunk stride
     const uint32_t RA = raw_a_bytes(GU, GB, SB, Q1);           // raw A bytes per stage
-    const uint32_t RB = (uint32_t)SB * kBTile;                 // B operand bytes per stage
-    const uint32_t RS = (uint32_t)SB * kMmaN * 4;              // activation scales per stage
+    const uint32_t RB = (uint32_t)SB * BT;                     // B operand bytes per stage
+    const uint32_t RS = (uint32_t)SB * NW * 4;                 // activation scales per stage
     const uint32_t RU = Q1 ? RS : 0;                           // activation block sums per stage
     const uint32_t RSLOT = (RA + RB + RS + RU + 127) & ~127u;
     uint8_t *raw = smem;                                       // [kMmaRaw][RSLOT]
@@ -249,7 +273,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
     uint64_t *raw_full = bars, *raw_empty = raw_full + kMmaRaw;
     uint64_t *a_full = raw_empty + kMmaRaw, *a_empty = a_full + kMmaA;
     uint64_t *tm_full = a_empty + kMmaA, *tm_empty = tm_full + kMmaTm;
-    float *xch = reinterpret_cast<float *>(raw);               // after the K loop: [2][2][32][33] up sums
+    float *xch = reinterpret_cast<float *>(raw);               // after the K loop: [2][2][32][EC + 1] up sums
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
 
@@ -257,8 +281,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();                                                 // the tile list and operands come from the previous kernels
     if (tl >= __ldcg(a.wk.ntiles)) return;                     // uniform per CTA, before any barrier
-    const int tile = __ldcg(a.wk.tiles + tl), e = tile & 0xFFFF, n0 = (tile >> 16) * kMmaN;
-    const int ncol = min(kMmaN, __ldcg(a.wk.cnt + e) - n0);
+    const int tile = __ldcg(a.wk.tiles + tl), e = tile & 0xFFFF, n0 = (tile >> 16) * NW;
+    const int ncol = min(NW, __ldcg(a.wk.cnt + e) - n0);
     const int soff = __ldcg(a.wk.off + e) + n0;
 
     if (threadIdx.x == 0) {
@@ -279,7 +303,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                     "r"(kMmaTm * kMmaN)
+                     "r"(kMmaTm * NW)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -293,9 +317,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
     if (warp == 0) {                                            // ---- TMA producer
         if (lane == 0) {
             const uint8_t *we = a.w + (size_t)e * a.w_expert;
-            const int8_t *bg = a.wk.bg + (size_t)tl * nb * kBTile;
-            const float *bs = a.wk.bs + (size_t)tl * nb * kMmaN;
-            const int *bu = a.wk.bsum + (size_t)tl * nb * kMmaN;
+            const int8_t *bg = a.wk.bg + (size_t)tl * nb * BT;
+            const float *bs = a.wk.bs + (size_t)tl * nb * NW;
+            const int *bu = a.wk.bsum + (size_t)tl * nb * NW;
             const uint64_t pol = evict_first_policy();
             int issued = 0;
             bool ok = true;
@@ -323,8 +347,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
                     }
                 }
                 bulk_load(dst + RA, bg + (size_t)s * RB, RB, &raw_full[slot], pol);
-                bulk_load(dst + RA + RB, bs + (size_t)s * SB * kMmaN, RS, &raw_full[slot], pol);
-                if (Q1) bulk_load(dst + RA + RB + RS, bu + (size_t)s * SB * kMmaN, RU, &raw_full[slot], pol);
+                bulk_load(dst + RA + RB, bs + (size_t)s * SB * NW, RS, &raw_full[slot], pol);
+                if (Q1) bulk_load(dst + RA + RB + RS, bu + (size_t)s * SB * NW, RU, &raw_full[slot], pol);
                 issued++;
             }
             // copies still in flight after an abort must land before the CTA exits
@@ -336,7 +360,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
         }
     } else if (warp == 1) {                                     // ---- MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = umma_idesc_s8(kMmaM, kMmaN);
+            const uint32_t idesc = umma_idesc_s8(kMmaM, NW);
             // one pass per converter group: the last slot's barrier implies the group's earlier ones
             // (every converter warp arrives them in order), likewise for the epilogue's TMEM buffers
             const uint32_t a0 = smem_u32(abuf), r0 = smem_u32(raw) + RA;
@@ -348,13 +372,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
                     if (!mma_wait(&tm_empty[bl % kMmaTm], ((bl / kMmaTm) & 1) ^ 1, abort_flag, a.err)) break;
                     tc_fence_after();
                 }
-                const uint32_t rb = r0 + (uint32_t)(s % kMmaRaw) * RSLOT + (uint32_t)bl0 * kBTile;
+                const uint32_t rb = r0 + (uint32_t)(s % kMmaRaw) * RSLOT + (uint32_t)bl0 * BT;
 #pragma unroll
                 for (int g = 0; g < kMmaGrp; g++) {
                     const int b = b0 + g;
                     const uint64_t da = umma_desc(a0 + (uint32_t)(b % kMmaA) * kABlock, 2048, 128);
-                    const uint64_t db = umma_desc(rb + (uint32_t)g * kBTile, 1024, 128);
-                    umma_s8(tmem + (b % kMmaTm) * kMmaN, da, db, idesc);
+                    const uint64_t db = umma_desc(rb + (uint32_t)g * BT, NW * 16, 128);
+                    umma_s8(tmem + (b % kMmaTm) * NW, da, db, idesc);
                     umma_commit(&tm_full[b % kMmaTm]);
                 }
                 issued += kMmaGrp;
@@ -420,11 +444,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
         }
     } else {                                                    // ---- epilogue: 8 warps
         // two blocks per pass: one wait, one TMEM round trip and one release per pair, so the
-        // per-block bookkeeping stays small next to the 2 x 32 columns of scaling
-        const int q = warp & 3, cq = (warp - kMmaEpi0) >> 2, R = 32 * q + lane;   // lane quarter, column half
-        float acc[32];
+        // per-block bookkeeping stays small next to the 2 x EC columns of scaling
+        const int q = warp & 3, cq = (warp - kMmaEpi0) >> 2, R = 32 * q + lane;   // lane quarter, column half (EC columns)
+        float acc[EC];
 #pragma unroll
-        for (int j = 0; j < 32; j++) acc[j] = 0.0f;
+        for (int j = 0; j < EC; j++) acc[j] = 0.0f;
         bool ok = true;
         int s = 0, bl = 0;
         for (int b = 0; b < nb && ok; b += 2) {
@@ -436,20 +460,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
                 mbar_arrive(&a_empty[b1 % kMmaA]);
             }
             tc_fence_after();
-            uint32_t r[2][32];
+            uint32_t r[2][EC];
 #pragma unroll
-            for (int i = 0; i < 2; i++) {
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                    : "=r"(r[i][0]), "=r"(r[i][1]), "=r"(r[i][2]), "=r"(r[i][3]), "=r"(r[i][4]), "=r"(r[i][5]),
-                      "=r"(r[i][6]), "=r"(r[i][7]), "=r"(r[i][8]), "=r"(r[i][9]), "=r"(r[i][10]), "=r"(r[i][11]),
-                      "=r"(r[i][12]), "=r"(r[i][13]), "=r"(r[i][14]), "=r"(r[i][15]), "=r"(r[i][16]), "=r"(r[i][17]),
-                      "=r"(r[i][18]), "=r"(r[i][19]), "=r"(r[i][20]), "=r"(r[i][21]), "=r"(r[i][22]), "=r"(r[i][23]),
-                      "=r"(r[i][24]), "=r"(r[i][25]), "=r"(r[i][26]), "=r"(r[i][27]), "=r"(r[i][28]), "=r"(r[i][29]),
-                      "=r"(r[i][30]), "=r"(r[i][31])
-                    : "r"(tmem + ((uint32_t)(32 * q) << 16) + ((b + i) % kMmaTm) * kMmaN + cq * 32));
-            }
+            for (int i = 0; i < 2; i++)
+                tmem_ld<EC>(tmem + ((uint32_t)(32 * q) << 16) + ((b + i) % kMmaTm) * NW + cq * EC, r[i]);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
@@ -469,12 +483,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
                     dw = h2f(*reinterpret_cast<const uint16_t *>(pb + 2048 + R * 2));
                     if (Q1) mw = h2f(*reinterpret_cast<const uint16_t *>(pb + 2304 + R * 2));
                 }
-                const float *sx = reinterpret_cast<const float *>(rs + RA + RB) + (bl + i) * kMmaN + cq * 32;
-                const int *su = reinterpret_cast<const int *>(rs + RA + RB + RS) + (bl + i) * kMmaN + cq * 32;
+                const float *sx = reinterpret_cast<const float *>(rs + RA + RB) + (bl + i) * NW + cq * EC;
+                const int *su = reinterpret_cast<const int *>(rs + RA + RB + RS) + (bl + i) * NW + cq * EC;
                 // int32 -> float without the conversion unit: |P| < 2^22, so 2^23 + 2^22 + P is exact
                 // in a float's mantissa; pairs of columns go through the packed f32x2 pipe
 #pragma unroll
-                for (int j = 0; j < 32; j += 2) {
+                for (int j = 0; j < EC; j += 2) {
                     const float2 xd = *reinterpret_cast<const float2 *>(sx + j);
                     float2 p2 = make_float2(__int_as_float((int)r[i][j] + 0x4B400000),
                                             __int_as_float((int)r[i][j + 1] + 0x4B400000));
@@ -504,16 +518,16 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
             // rows 0-31 / 64-95 (lane quarters 0, 2) are gate rows f, 32-63 / 96-127 the up rows of
             // the same f: the up warps hand their sums over, the gate warps finish the groups
             const int th = q >> 1;                                // which 64-row tile
-            float *xu = xch + ((th * 2 + cq) * 32 + lane) * 33;
+            float *xu = xch + ((th * 2 + cq) * 32 + lane) * (EC + 1);
             if (q & 1)
 #pragma unroll
-                for (int j = 0; j < 32; j++) xu[j] = acc[j];
+                for (int j = 0; j < EC; j++) xu[j] = acc[j];
             asm volatile("bar.sync 1, %0;" ::"n"(kMmaEpiWarps * 32) : "memory");
             if (!(q & 1) && ok && !*abort_flag) {
                 const int f = 64 * mt + 32 * th + lane, grp = f >> 5;
 #pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    const int col = cq * 32 + j;
+                for (int j = 0; j < EC; j++) {
+                    const int col = cq * EC + j;
                     if (col >= ncol) continue;                   // warp-uniform
                     const float g = acc[j], u = xu[j];
                     const float av = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
@@ -529,8 +543,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
         } else if (ok && !*abort_flag) {
             const int row = mt * kMmaM + R;
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const int col = cq * 32 + j;
+            for (int j = 0; j < EC; j++) {
+                const int col = cq * EC + j;
                 if (col >= ncol) continue;
                 const int slot = __ldcg(a.wk.slots + soff + col);
                 a.wk.dn[(size_t)slot * a.E + row] = acc[j];
@@ -541,7 +555,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kMmaTm * kMmaN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kMmaTm * NW) : "memory");
     }
 }
 
@@ -558,9 +572,9 @@ __global__ void __launch_bounds__(256) k_mma_combine(const float *__restrict__ d
 }
 
 // ---- host side -------------------------------------------------------------------------------------
-static size_t mma_smem(const QmsCudaMoe *m, int SB, bool gu, bool q1) {
+static size_t mma_smem(const QmsCudaMoe *m, int SB, bool gu, bool q1, int nw) {
     const size_t RA = raw_a_bytes(gu, m->cgu.GB, SB, q1);
-    const size_t RSLOT = (RA + (size_t)SB * kBTile + (size_t)SB * kMmaN * 4 * (q1 ? 2 : 1) + 127) & ~(size_t)127;
+    const size_t RSLOT = (RA + (size_t)SB * nw * 32 + (size_t)SB * nw * 4 * (q1 ? 2 : 1) + 127) & ~(size_t)127;
     return kMmaRaw * RSLOT + kMmaA * kABlock + (2 * kMmaRaw + 2 * kMmaA + 2 * kMmaTm) * 8;
 }
 
@@ -571,8 +585,11 @@ static struct {
     int dev = -1;
 } g_mma_ws;
 
+// Tile width: 16 slots when experts average few slots (batched decode), else 64.
+static int mma_width(const QmsCudaMoe *m, int T) { return (int64_t)T * m->K <= (int64_t)24 * m->X ? kMmaNs : kMmaN; }
+
 static int mma_layout(const QmsCudaMoe *m, int T, MmaWork *w, size_t *bytes, char *base) {
-    const size_t S = (size_t)T * m->K, maxT = S / kMmaN + m->X;
+    const size_t nw = mma_width(m, T), S = (size_t)T * m->K, maxT = S / nw + m->X;
     const int nbmax = std::max(m->nbE, m->nbF);
     size_t off = 0;
     auto take = [&](size_t n) { size_t o = off; off += (n + 255) & ~(size_t)255; return base + o; };
@@ -583,9 +600,9 @@ static int mma_layout(const QmsCudaMoe *m, int T, MmaWork *w, size_t *bytes, cha
     w->pos = (int *)take(S * 4);
     w->slots = (int *)take(S * 4);
     w->tiles = (int *)take(maxT * 4);
-    w->bg = (int8_t *)take(maxT * nbmax * kBTile);
-    w->bs = (float *)take(maxT * nbmax * kMmaN * 4);
-    w->bsum = (int *)take(maxT * nbmax * kMmaN * 4);
+    w->bg = (int8_t *)take(maxT * nbmax * nw * 32);
+    w->bs = (float *)take(maxT * nbmax * nw * 4);
+    w->bsum = (int *)take(maxT * nbmax * nw * 4);
     w->dn = (float *)take(S * m->E * 4);
     *bytes = off;
     return QMS_CUDA_OK;
@@ -604,9 +621,32 @@ int mma_prepare(QmsCudaMoe *m) {
         return QMS_CUDA_OK;
     };
     int rc;
-    if ((rc = set((const void *)k_mma_gemm<true, false>, mma_smem(m, m->cgu.SB, true, false)))) return rc;
-    if ((rc = set((const void *)k_mma_gemm<false, false>, mma_smem(m, SBd, false, false)))) return rc;
-    if ((rc = set((const void *)k_mma_gemm<false, true>, mma_smem(m, SBd, false, true)))) return rc;
+    if ((rc = set((const void *)k_mma_gemm<true, false, kMmaN>, mma_smem(m, m->cgu.SB, true, false, kMmaN)))) return rc;
+    if ((rc = set((const void *)k_mma_gemm<false, false, kMmaN>, mma_smem(m, SBd, false, false, kMmaN)))) return rc;
+    if ((rc = set((const void *)k_mma_gemm<false, true, kMmaN>, mma_smem(m, SBd, false, true, kMmaN)))) return rc;
+    if ((rc = set((const void *)k_mma_gemm<true, false, kMmaNs>, mma_smem(m, m->cgu.SB, true, false, kMmaNs)))) return rc;
+    if ((rc = set((const void *)k_mma_gemm<false, false, kMmaNs>, mma_smem(m, SBd, false, false, kMmaNs)))) return rc;
+    if ((rc = set((const void *)k_mma_gemm<false, true, kMmaNs>, mma_smem(m, SBd, false, true, kMmaNs)))) return rc;
+    return QMS_CUDA_OK;
+}
+
+template <int NW>
+static int mma_gemms(QmsCudaMoe *m, const MmaArgs &g, const MmaArgs &d, int maxT, cudaStream_t s) {
+    const int SBd = d.SB;
+    QMS_CK(launch_pdl(k_mma_gemm<true, false, NW>, dim3(2 * m->F / kMmaM, maxT), dim3(kMmaThreads),
+                      mma_smem(m, g.SB, true, false, NW), s, g));
+    if (m->timing) {
+        QMS_CK(cudaEventRecord(m->ev[3], s));
+        QMS_CK(cudaEventRecord(m->ev[4], s));
+    }
+    QMS_CK(launch_pdl(k_mma_gather, dim3(maxT, 8), dim3(2 * NW), 0, s, (const int8_t *)m->aq_q, (const float *)m->aq_d,
+                      (const int *)m->aq_s, m->nbF, 1, NW, g.wk));
+    if (m->dcol.q1)
+        QMS_CK(launch_pdl(k_mma_gemm<false, true, NW>, dim3(m->E / kMmaM, maxT), dim3(kMmaThreads),
+                          mma_smem(m, SBd, false, true, NW), s, d));
+    else
+        QMS_CK(launch_pdl(k_mma_gemm<false, false, NW>, dim3(m->E / kMmaM, maxT), dim3(kMmaThreads),
+                          mma_smem(m, SBd, false, false, NW), s, d));
     return QMS_CUDA_OK;
 }
 
@@ -633,11 +673,10 @@ int mma_forward(QmsCudaMoe *m, int T, const float *resid, float *out, cudaStream
         g_mma_ws.dev = m->device;
     }
     mma_layout(m, T, &w, &need, (char *)g_mma_ws.p);
-    const int S = T * m->K, maxT = S / kMmaN + m->X;
-    const int SBd = 8;                                  // down stages: 8 blocks (F/32 % 8 == 0)
-    QMS_CK(launch_pdl(k_mma_group, dim3(1), dim3(1024), 0, s, (const int *)m->sel, S, m->X, maxT, w));
-    QMS_CK(launch_pdl(k_mma_gather, dim3(maxT, 8), dim3(128), 0, s, (const int8_t *)m->xq_q, (const float *)m->xq_d,
-                      (const int *)nullptr, m->nbE, m->K, w));
+    const int nw = mma_width(m, T), S = T * m->K, maxT = S / nw + m->X;
+    QMS_CK(launch_pdl(k_mma_group, dim3(1), dim3(1024), 0, s, (const int *)m->sel, S, m->X, maxT, nw, w));
+    QMS_CK(launch_pdl(k_mma_gather, dim3(maxT, 8), dim3(2 * nw), 0, s, (const int8_t *)m->xq_q, (const float *)m->xq_d,
+                      (const int *)nullptr, m->nbE, m->K, nw, w));
     MmaArgs g;
     memset(&g, 0, sizeof g);
     g.w = m->gu;
@@ -654,25 +693,13 @@ int mma_forward(QmsCudaMoe *m, int T, const float *resid, float *out, cudaStream
     g.aq_d = m->aq_d;
     g.aq_s = m->aq_s;
     g.err = m->err;
-    QMS_CK(launch_pdl(k_mma_gemm<true, false>, dim3(2 * m->F / kMmaM, maxT), dim3(kMmaThreads),
-                      mma_smem(m, g.SB, true, false), s, g));
-    if (m->timing) {
-        QMS_CK(cudaEventRecord(m->ev[3], s));
-        QMS_CK(cudaEventRecord(m->ev[4], s));
-    }
-    QMS_CK(launch_pdl(k_mma_gather, dim3(maxT, 8), dim3(128), 0, s, (const int8_t *)m->aq_q, (const float *)m->aq_d,
-                      (const int *)m->aq_s, m->nbF, 1, w));
     MmaArgs d = g;
     d.w = m->dn;
     d.w_expert = m->dn_expert;
     d.nb = m->nbF;
-    d.SB = SBd;
-    if (m->dcol.q1)
-        QMS_CK(launch_pdl(k_mma_gemm<false, true>, dim3(m->E / kMmaM, maxT), dim3(kMmaThreads), mma_smem(m, SBd, false, true),
-                          s, d));
-    else
-        QMS_CK(launch_pdl(k_mma_gemm<false, false>, dim3(m->E / kMmaM, maxT), dim3(kMmaThreads),
-                          mma_smem(m, SBd, false, false), s, d));
+    d.SB = 8;                                           // down stages: 8 blocks (F/32 % 8 == 0)
+    int rc = nw == kMmaNs ? mma_gemms<kMmaNs>(m, g, d, maxT, s) : mma_gemms<kMmaN>(m, g, d, maxT, s);
+    if (rc) return rc;
     QMS_CK(launch_pdl(k_mma_combine, dim3((m->E + 255) / 256, T), dim3(256), 0, s, (const float *)w.dn,
                       (const float *)m->wts, m->K, m->E, resid, out));
     if (m->timing) QMS_CK(cudaEventRecord(m->ev[5], s));

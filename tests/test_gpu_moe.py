@@ -126,11 +126,13 @@ def test_moe_edge_cases(cuda, oracle):
     m2.close()
 
 
-@pytest.mark.parametrize("shape,T,down", [("tiny", 16, 2), ("tiny", 70, 3), ("30b", 16, 2), ("30b", 130, 2),
-                                          ("235b", 16, 2), ("235b", 64, 3), ("235b", 200, 2)])
+@pytest.mark.parametrize("shape,T,down", [("tiny", 16, 2), ("tiny", 70, 3), ("tiny", 200, 3), ("30b", 16, 2),
+                                          ("30b", 130, 2), ("235b", 16, 2), ("235b", 64, 3), ("235b", 200, 2),
+                                          ("235b", 512, 2)])
 def test_moe_grouped_mma_matches_oracle(cuda, oracle, shape, T, down):
-    """T >= 16: expert-grouped tcgen05 kind::i8 GEMMs (partial and multiple 64-slot tiles per expert,
-    Q4_0 and Q4_1 down) against the oracle, with the batch bars."""
+    """T >= 16: expert-grouped tcgen05 kind::i8 GEMMs against the oracle, with the batch bars: 16-slot
+    tiles while experts average <= 24 slots, 64-slot tiles above (tiny T=200, 235B T=512); partial
+    and multiple tiles per expert; Q4_0 and Q4_1 down."""
     layer = synth.make_moe_layer(shape, seed=91 + T, down_type=down)
     xn = synth.make_hidden(layer.n_embd, T, seed=93 + T)
     m, out, sel, w, logits = _run(cuda, layer, xn)

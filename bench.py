@@ -144,6 +144,26 @@ def cpu_reference_rate(seconds: float = 8.0, max_calls: int = 2000, layers: int 
                       f"({dt:.1f} s, reference build {ref.variant}, {threads} OpenMP threads)"}, n, dt
 
 
+def cpu_reference_batched(T: int, seconds: float = 10.0, layers: int = 2):
+    """The reference's moe() on T-token calls (moe() is sequence-agnostic), all host threads."""
+    from oracle import Reference, host_threads
+    from large_model_b200 import synth
+    ref = Reference()
+    threads = host_threads()
+    ref.set_threads(threads)
+    ls = [synth.make_moe_layer(SHAPE, seed=1000 + i) for i in range(layers)]
+    xn = synth.make_hidden(ls[0].n_embd, T, seed=2001)
+    ref.moe(ls[0], xn[: min(T, 8)])                       # warm-up (page in, thread pool)
+    n, t0 = 0, time.perf_counter()
+    while n < 1 or (time.perf_counter() - t0 < seconds and n < 64):
+        ref.moe(ls[n % layers], xn)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n * T / dt, 1), "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"{n} T={T} moe() calls over {layers} seeded 235B-shape layers in host RAM "
+                      f"({dt:.1f} s, reference build {ref.variant}, {threads} OpenMP threads)"}
+
+
 def run_reference_arm(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -228,6 +248,9 @@ def run_batched(a):
     dev = torch.device("cuda", local)
     T = BATCH_T[a.mode]
     E, X, K, F = 4096, 128, 8, 1536
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        cpu = cpu_reference_batched(T, seconds=10.0 if T <= 256 else 20.0)
     layers = [device_layer(q, torch, 500 + 17 * i, dev) for i in range(2)]
     g = torch.Generator(device=dev)
     g.manual_seed(11)
@@ -326,7 +349,7 @@ def run_batched(a):
                            "l2": "inputs larger than L2 (2 layers x 1.36 GB resident)",
                            "routing": "seeded N(0,1) hidden states, N(0,0.02) router (near-uniform expert load)",
                            "parallelism": f"replicas x{world}"},
-                "roofline": roof, "cpu_baseline": None,
+                "roofline": roof, "cpu_baseline": cpu,
                 "e2e": {"value": round(T * e2e_n / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": T * E * 4,
                         "d2h_bytes_per_step": T * E * 4, "note": "qms_cuda_moe_forward_host per call"},
                 "gpu_launches": None, "clocks": clocks}

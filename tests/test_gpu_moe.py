@@ -190,6 +190,46 @@ def test_moe_host_entry_and_residual(cuda, oracle):
     m.close()
 
 
+def test_grouped_mma_residual_graph_and_determinism(cuda, oracle):
+    """Tensor-core path (T = 48): fused residual, output aliasing the residual, CUDA-graph capture
+    after reserve, bitwise reproducibility across calls."""
+    import torch
+    layer = synth.make_moe_layer("30b", seed=21)
+    T = 48
+    xn = synth.make_hidden(layer.n_embd, T, seed=22)
+    m = cuda.MoeLayer.from_synth(layer)
+    xd = torch.from_numpy(xn).cuda()
+    plain = m.forward(xd)
+    again = m.forward(xd)
+    torch.cuda.synchronize()
+    m.status()
+    assert torch.equal(plain, again)
+    o_out, _, _, _ = oracle.moe(layer, xn)
+    assert rel_l2(plain.cpu().numpy(), o_out) < OUT_TOL
+    resid = torch.from_numpy(synth.make_hidden(layer.n_embd, T, seed=23)).cuda()
+    fused = m.forward(xd, resid=resid)
+    h = resid.clone()
+    m.forward(xd, out=h, resid=h)
+    torch.cuda.synchronize()
+    assert torch.equal(fused, resid + plain) and torch.equal(h, fused)
+    m.reserve(T)
+    s = torch.cuda.Stream()
+    out = torch.empty_like(xd)
+    with torch.cuda.stream(s):
+        m.forward(xd, out=out, stream=s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        m.forward(xd, out=out, stream=s)
+    out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    m.status()
+    assert torch.equal(out, plain)
+    del g
+    m.close()
+
+
 def test_moe_deterministic_and_expert_permutation(cuda):
     """Size-independent properties at the 235B shape: repeated calls are bit-identical, and
     storing the experts in a different order (router rows permuted alike) changes only the

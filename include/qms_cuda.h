@@ -107,6 +107,27 @@ int qms_cuda_moe_reserve(QmsCudaMoe *m, int T);
 int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int *sel,
                          float *wts, float *logits, const float *resid, void *stream);
 
+/* ---- expert parallelism: route, expert FFNs, combine (no reference counterpart; the reference
+ * runs every expert in one process). A full layer runs them inside qms_cuda_moe_forward; a
+ * shard runs them under the caller's dispatch (all-to-all of rows, see large_model_b200/ep.py). */
+
+/* A layer holding experts [expert_base, expert_base + n_local) of the desc's n_expert routed
+ * ones: desc->router has all n_expert rows; desc->gate/up/down hold only the n_local experts
+ * (stacked in expert order). qms_cuda_moe_forward is refused on a shard. */
+int qms_cuda_moe_create_shard(const QmsCudaMoeDesc *desc, int expert_base, int n_local, QmsCudaMoe **out);
+/* Routing only (src/model.c:1043-1064): sel [T][n_used] (global expert ids, selection order) and
+ * wts [T][n_used], optional logits [T][n_expert]; device buffers. */
+int qms_cuda_moe_route(QmsCudaMoe *m, const float *xn, int T, int *sel, float *wts, float *logits, void *stream);
+/* Expert FFNs of S rows (moe_group_fast's phases 1-3 for one slot each, src/model.c:979-1005):
+ * x [S][n_embd] fp32, expert[S] local ids (0 .. n_local - 1), dn [S][n_embd] receives each row's
+ * down projection before weighting. Rows with an out-of-range id are skipped (dn left as is).
+ * Runs the grouped tensor-core kernels; device buffers. */
+int qms_cuda_moe_experts(QmsCudaMoe *m, const float *x, const int *expert, int S, float *dn, void *stream);
+/* out[t] = resid[t] + sum_j wts[t][j] * dn[t * n_used + j] in selection order (src/model.c:1152-1162);
+ * resid may be NULL; device buffers. */
+int qms_cuda_moe_combine(const float *dn, const float *wts, int T, int n_used, int n_embd, const float *resid,
+                         float *out, void *stream);
+
 /* Waits for the device and reports whether any bounded wait inside the layer's kernels gave up
  * since the last call (QMS_CUDA_ETIMEOUT; the outputs of the affected call are invalid), then
  * clears the flag. The batch-1 kernels never spin without a limit, so a stuck pipeline turns into

@@ -70,6 +70,10 @@ def lib() -> C.CDLL:
     L.qms_cuda_moe_forward_host.argtypes = [vp, vp, i32, vp, vp, vp, vp]
     L.qms_cuda_moe_set_kernel_events.argtypes = [vp, C.POINTER(vp)]
     L.qms_cuda_moe_status.argtypes = [vp]
+    L.qms_cuda_moe_create_shard.argtypes = [C.POINTER(MoeDesc), i32, i32, C.POINTER(vp)]
+    L.qms_cuda_moe_route.argtypes = [vp, vp, i32, vp, vp, vp, vp]
+    L.qms_cuda_moe_experts.argtypes = [vp, vp, vp, i32, vp, vp]
+    L.qms_cuda_moe_combine.argtypes = [vp, vp, i32, i32, i32, vp, vp, vp]
     _lib = L
     return L
 
@@ -141,17 +145,34 @@ class MoeLayer:
     """One resident MoE layer (the reference's moe(), src/model.c:1032)."""
 
     def __init__(self, n_embd: int, n_expert: int, n_used: int, n_ff: int, router, gate, up, down,
-                 gate_type: int = T_Q4_0, up_type: int = T_Q4_0, down_type: int = T_Q4_0):
+                 gate_type: int = T_Q4_0, up_type: int = T_Q4_0, down_type: int = T_Q4_0, shard=None):
+        """shard = (expert_base, n_local): gate/up/down hold only those experts (a shard for expert
+        parallelism, qms_cuda_moe_create_shard); the router always has all n_expert rows."""
         on_dev = not isinstance(router, np.ndarray)
         self._keep = (router, gate, up, down)
         ptr = (lambda a: a.ctypes.data) if not on_dev else (lambda t: t.data_ptr())
         d = MoeDesc(n_embd, n_expert, n_used, n_ff, gate_type, up_type, down_type,
                     ptr(router), ptr(gate), ptr(up), ptr(down), int(on_dev))
         h = C.c_void_p()
-        check(lib().qms_cuda_moe_create(C.byref(d), C.byref(h)))
+        if shard is None:
+            check(lib().qms_cuda_moe_create(C.byref(d), C.byref(h)))
+        else:
+            check(lib().qms_cuda_moe_create_shard(C.byref(d), int(shard[0]), int(shard[1]), C.byref(h)))
         self._keep = None
         self.h = h
         self.n_embd, self.n_expert, self.n_used, self.n_ff = n_embd, n_expert, n_used, n_ff
+        self.expert_base, self.n_local = (0, n_expert) if shard is None else (int(shard[0]), int(shard[1]))
+
+    @classmethod
+    def shard_from_synth(cls, layer, expert_base: int, n_local: int) -> "MoeLayer":
+        """Experts [expert_base, expert_base + n_local) of a synth layer (host arrays)."""
+        E, F = layer.n_embd, layer.n_ff
+        gu_bytes = F * (E // 32) * 18
+        dn_bytes = E * (F // 32) * (20 if layer.down_type == T_Q4_1 else 18)
+        sl = lambda a, per: np.ascontiguousarray(a[expert_base * per:(expert_base + n_local) * per])
+        return cls(E, layer.n_expert, layer.n_used, F, layer.router, sl(layer.gate, gu_bytes), sl(layer.up, gu_bytes),
+                   sl(layer.down, dn_bytes), layer.gate_type, layer.up_type, layer.down_type,
+                   shard=(expert_base, n_local))
 
     @classmethod
     def from_synth(cls, layer) -> "MoeLayer":
@@ -217,6 +238,26 @@ class MoeLayer:
         out = self.forward(xn, sel=sel, wts=wts, logits=logits)
         return out, sel, wts, logits
 
+    def route_only(self, xn, stream=None):
+        """Routing of T tokens (qms_cuda_moe_route): (sel, wts) CUDA int32 / float32 [T][n_used]."""
+        torch = _torch()
+        xn = xn.reshape(-1, self.n_embd)
+        T = xn.shape[0]
+        sel = torch.empty((T, self.n_used), dtype=torch.int32, device=xn.device)
+        wts = torch.empty((T, self.n_used), dtype=torch.float32, device=xn.device)
+        check(lib().qms_cuda_moe_route(self.h, _ptr(xn), T, _ptr(sel), _ptr(wts), None, _stream(stream)))
+        return sel, wts
+
+    def experts(self, x, expert, dn=None, stream=None):
+        """Expert FFNs of rows x [S][n_embd] with local expert ids expert [S] (qms_cuda_moe_experts):
+        returns dn [S][n_embd], the unweighted down rows."""
+        torch = _torch()
+        S = x.shape[0]
+        if dn is None:
+            dn = torch.empty((S, self.n_embd), dtype=torch.float32, device=x.device)
+        check(lib().qms_cuda_moe_experts(self.h, _ptr(x), _ptr(expert), S, _ptr(dn), _stream(stream)))
+        return dn
+
     def forward_host(self, xn: np.ndarray, out: np.ndarray | None = None, with_routing: bool = False):
         """Host-buffer entry point (copies in, runs, copies out, waits)."""
         xn = np.ascontiguousarray(xn, np.float32).reshape(-1, self.n_embd)
@@ -228,3 +269,14 @@ class MoeLayer:
         p = lambda a: None if a is None else C.c_void_p(a.ctypes.data)
         check(lib().qms_cuda_moe_forward_host(self.h, p(xn), T, p(out), p(sel), p(wts), None))
         return (out, sel, wts) if with_routing else out
+
+
+def combine(dn, wts, resid=None, out=None, stream=None):
+    """out[t] = resid[t] + sum_j wts[t][j] * dn[t*K + j] in selection order (qms_cuda_moe_combine)."""
+    torch = _torch()
+    T, K = wts.shape
+    E = dn.shape[-1]
+    if out is None:
+        out = torch.empty((T, E), dtype=torch.float32, device=dn.device)
+    check(lib().qms_cuda_moe_combine(_ptr(dn), _ptr(wts), T, K, E, _ptr(resid), _ptr(out), _stream(stream)))
+    return out

@@ -384,7 +384,7 @@ static int ensure_device(int dev) {
 // Upload one stacked expert tensor (host or device source) and repack it: which = 0 / 1 gate / up
 // rows into chunks, which = 2 down rows into column stages.
 static int upload_q4(const QmsCudaMoe *m, const void *src, int on_device, int which, uint8_t *dst) {
-    const int64_t nrows = (int64_t)m->X * (which == 2 ? m->E : m->F);
+    const int64_t nrows = (int64_t)m->n_local * (which == 2 ? m->E : m->F);
     const int nb = which == 2 ? m->nbF : m->nbE;
     const size_t bytes = (size_t)nrows * nb * (which == 2 && m->dcol.q1 ? 20 : 18);
     const uint8_t *dsrc = (const uint8_t *)src;
@@ -438,11 +438,13 @@ void qms_cuda_moe_destroy(QmsCudaMoe *m) {
     free(m);
 }
 
-int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
+static int create_impl(const QmsCudaMoeDesc *d, int base, int n_local, QmsCudaMoe **out) {
     clear_error();
     QMS_REQUIRE(d && out, QMS_CUDA_EINVAL, "moe_create: NULL argument");
     *out = nullptr;
     const int E = d->n_embd, X = d->n_expert, K = d->n_used, F = d->n_ff;
+    QMS_REQUIRE(base >= 0 && n_local >= 1 && base + n_local <= X, QMS_CUDA_EINVAL,
+                "moe_create_shard: experts [%d, %d) outside 0..%d", base, base + n_local, X);
     QMS_REQUIRE(d->router && d->gate && d->up && d->down, QMS_CUDA_EINVAL, "moe_create: NULL tensor");
     QMS_REQUIRE(E > 0 && X > 0 && K > 0 && F > 0 && K <= X, QMS_CUDA_EINVAL, "moe_create: bad dimensions");
     // the reference's integer fast path condition (src/model.c:1090-1093)
@@ -463,13 +465,14 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
     m->device = dev;
     if (cudaDeviceGetAttribute(&m->nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) m->nsm = 148;
     m->E = E; m->X = X; m->K = K; m->F = F;
+    m->n_local = n_local; m->expert_base = base;
     m->nbE = E / 32; m->nbF = F / 32;
     m->gate_type = d->gate_type; m->up_type = d->up_type; m->down_type = d->down_type;
     m->cgu = make_chunked(m->nbE);
     m->dcol = make_dncols(E, d->down_type == QMS_T_Q4_1);
     m->gu_expert = (size_t)2 * F * m->nbE * 18;
     m->dn_expert = (size_t)E * m->nbF * (m->dcol.q1 ? 20 : 18);
-    const size_t rb = (size_t)X * E * 4, gb = m->gu_expert * X, db = m->dn_expert * X;
+    const size_t rb = (size_t)X * E * 4, gb = m->gu_expert * n_local, db = m->dn_expert * n_local;
     m->weight_bytes = rb + gb + db;
     if (cudaMalloc(&m->router, rb) != cudaSuccess || cudaMalloc(&m->router_lm, rb) != cudaSuccess ||
         cudaMalloc(&m->gu, gb) != cudaSuccess || cudaMalloc(&m->dn, db) != cudaSuccess) {
@@ -499,7 +502,7 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
         set_error("moe_create: %s", cudaGetErrorString(cudaGetLastError()));
         rc = QMS_CUDA_ECUDA;
     }
-    if (rc == QMS_CUDA_OK) rc = stream_prepare(m);
+    if (rc == QMS_CUDA_OK && n_local == X) rc = stream_prepare(m);   // a shard has no batch-1 path
     if (rc == QMS_CUDA_OK && mma_supported(m)) {
         m->mma_min_t = kMmaMinT;
         if (const char *env = getenv("QMS_MMA_MIN_T")) m->mma_min_t = atoi(env);   // 0 turns the path off
@@ -511,6 +514,14 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
     }
     *out = m;
     return QMS_CUDA_OK;
+}
+
+int qms_cuda_moe_create(const QmsCudaMoeDesc *d, QmsCudaMoe **out) {
+    return create_impl(d, 0, d ? d->n_expert : 0, out);
+}
+
+int qms_cuda_moe_create_shard(const QmsCudaMoeDesc *d, int expert_base, int n_local, QmsCudaMoe **out) {
+    return create_impl(d, expert_base, n_local, out);
 }
 
 int64_t qms_cuda_moe_device_bytes(const QmsCudaMoe *m) {
@@ -587,6 +598,9 @@ int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int 
     QMS_REQUIRE(m && T >= 0, QMS_CUDA_EINVAL, "moe_forward: bad arguments");
     if (T == 0) return QMS_CUDA_OK;
     QMS_REQUIRE(xn && out, QMS_CUDA_EINVAL, "moe_forward: NULL xn or out");
+    QMS_REQUIRE(m->n_local == m->X, QMS_CUDA_EUNSUPPORTED,
+                "moe_forward: a shard layer holds experts [%d, %d) only; run route, experts and combine",
+                m->expert_base, m->expert_base + m->n_local);
     int rc = ensure_device(m->device);
     if (rc) return rc;
     if (T > m->cap_T) {
@@ -634,6 +648,61 @@ int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int 
     if (wts) QMS_CK(cudaMemcpyAsync(wts, m->wts, TK * 4, cudaMemcpyDeviceToDevice, s));
     if (logits) QMS_CK(cudaMemcpyAsync(logits, m->logits, (size_t)T * m->X * 4, cudaMemcpyDeviceToDevice, s));
     return QMS_CUDA_OK;
+}
+
+int qms_cuda_moe_route(QmsCudaMoe *m, const float *xn, int T, int *sel, float *wts, float *logits, void *stream) {
+    QMS_REQUIRE(m && T >= 0, QMS_CUDA_EINVAL, "moe_route: bad arguments");
+    if (T == 0) return QMS_CUDA_OK;
+    QMS_REQUIRE(xn && sel && wts, QMS_CUDA_EINVAL, "moe_route: NULL xn, sel or wts");
+    int rc = ensure_device(m->device);
+    if (rc) return rc;
+    if (T > m->cap_T) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        QMS_CK(cudaStreamIsCapturing((cudaStream_t)stream, &cs));
+        QMS_REQUIRE(cs == cudaStreamCaptureStatusNone, QMS_CUDA_EINVAL,
+                    "moe_route: scratch for T=%d must be reserved before graph capture", T);
+        if ((rc = qms_cuda_moe_reserve(m, T))) return rc;
+    }
+    const cudaStream_t s = (cudaStream_t)stream;
+    if ((rc = launch_router(m->router, m->X, m->E, xn, T, m->K, m->xq_q, m->xq_d, m->xq_s, m->logits, m->sel, m->wts,
+                            m->cnt, s)))
+        return rc;
+    const size_t TK = (size_t)T * m->K;
+    QMS_CK(cudaMemcpyAsync(sel, m->sel, TK * 4, cudaMemcpyDeviceToDevice, s));
+    QMS_CK(cudaMemcpyAsync(wts, m->wts, TK * 4, cudaMemcpyDeviceToDevice, s));
+    if (logits) QMS_CK(cudaMemcpyAsync(logits, m->logits, (size_t)T * m->X * 4, cudaMemcpyDeviceToDevice, s));
+    return QMS_CUDA_OK;
+}
+
+int qms_cuda_moe_experts(QmsCudaMoe *m, const float *x, const int *expert, int S, float *dn, void *stream) {
+    QMS_REQUIRE(m && S >= 0, QMS_CUDA_EINVAL, "moe_experts: bad arguments");
+    if (S == 0) return QMS_CUDA_OK;
+    QMS_REQUIRE(x && expert && dn, QMS_CUDA_EINVAL, "moe_experts: NULL x, expert or dn");
+    QMS_REQUIRE(m->mma_min_t > 0, QMS_CUDA_EUNSUPPORTED, "moe_experts: the grouped tensor-core path is off for this layer");
+    int rc = ensure_device(m->device);
+    if (rc) return rc;
+    const int T = (S + m->K - 1) / m->K;                 // scratch holds S rows of x and S SwiGLU rows
+    if (S > m->cap_T || T > m->cap_T) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        QMS_CK(cudaStreamIsCapturing((cudaStream_t)stream, &cs));
+        QMS_REQUIRE(cs == cudaStreamCaptureStatusNone, QMS_CUDA_EINVAL,
+                    "moe_experts: scratch for %d slots must be reserved before graph capture", S);
+        if ((rc = qms_cuda_moe_reserve(m, S))) return rc;
+    }
+    const cudaStream_t s = (cudaStream_t)stream;
+    const int64_t nblocks = (int64_t)S * m->nbE;
+    k_quantize_rows<<<(unsigned)std::min<int64_t>((nblocks + 7) / 8, 4096), 256, 0, s>>>(x, nblocks, m->xq_q, m->xq_d,
+                                                                                        m->xq_s);
+    QMS_CK(cudaGetLastError());
+    return mma_experts(m, S, expert, dn, s);
+}
+
+int qms_cuda_moe_combine(const float *dn, const float *wts, int T, int n_used, int n_embd, const float *resid,
+                         float *out, void *stream) {
+    QMS_REQUIRE(T >= 0 && n_used > 0 && n_embd > 0, QMS_CUDA_EINVAL, "moe_combine: bad arguments");
+    if (T == 0) return QMS_CUDA_OK;
+    QMS_REQUIRE(dn && wts && out, QMS_CUDA_EINVAL, "moe_combine: NULL dn, wts or out");
+    return mma_combine(dn, wts, T, n_used, n_embd, resid, out, (cudaStream_t)stream);
 }
 
 int qms_cuda_moe_set_kernel_events(QmsCudaMoe *m, void **events) {

@@ -161,6 +161,7 @@ __device__ inline void topk_token(const float *__restrict__ lg, int X, int K, in
 struct QmsCudaMoe {
     int device, nsm;
     int E, X, K, F, nbE, nbF;
+    int n_local, expert_base;  // experts held: [expert_base, expert_base + n_local) of the X routed
     int gate_type, up_type, down_type;
     qms::Chunked cgu;    // gate/up chunks
     qms::DnCols dcol;    // down column stages
@@ -234,5 +235,8 @@ int mma_supported(const QmsCudaMoe *m);
 int mma_prepare(QmsCudaMoe *m);
 int mma_reserve(QmsCudaMoe *m, int T);
 int mma_forward(QmsCudaMoe *m, int T, const float *resid, float *out, cudaStream_t s);
+int mma_experts(QmsCudaMoe *m, int S, const int *expert, float *dn, cudaStream_t s);
+int mma_combine(const float *dn, const float *wts, int T, int K, int E, const float *resid, float *out,
+                cudaStream_t s);
 
 }  // namespace qms

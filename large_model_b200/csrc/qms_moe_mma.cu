@@ -650,8 +650,10 @@ static int mma_gemms(QmsCudaMoe *m, const MmaArgs &g, const MmaArgs &d, int maxT
     return QMS_CUDA_OK;
 }
 
-// T > 1 tokens: router output (xq, sel, wts) already in m's scratch.
-int mma_forward(QmsCudaMoe *m, int T, const float *resid, float *out, cudaStream_t s) {
+// The expert FFNs of S slots: slot s has Q8 row s / rdiv in m's xq scratch and expert sel[s]
+// (0 .. nx-1); dn[s][E] receives its down row. Slots whose expert is out of range are skipped.
+static int mma_core(QmsCudaMoe *m, int S, const int *sel, int nx, int rdiv, float *dn, cudaStream_t s) {
+    const int T = (S + m->K - 1) / m->K;                 // workspace is sized in tokens of K slots
     MmaWork w;
     size_t need = 0;
     mma_layout(m, T, &w, &need, nullptr);
@@ -659,24 +661,25 @@ int mma_forward(QmsCudaMoe *m, int T, const float *resid, float *out, cudaStream
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         QMS_CK(cudaStreamIsCapturing(s, &cs));
         QMS_REQUIRE(cs == cudaStreamCaptureStatusNone, QMS_CUDA_EINVAL,
-                    "moe_forward: tensor-core workspace for T=%d must be reserved before graph capture", T);
+                    "moe: tensor-core workspace for %d slots must be reserved before graph capture", S);
         QMS_CK(cudaStreamSynchronize(s));
         if (g_mma_ws.p) cudaFree(g_mma_ws.p);
         g_mma_ws.p = nullptr;
         g_mma_ws.bytes = 0;
         if (cudaMalloc(&g_mma_ws.p, need) != cudaSuccess) {
             cudaGetLastError();
-            set_error("moe_forward: cannot allocate %zu bytes of tensor-core workspace", need);
+            set_error("moe: cannot allocate %zu bytes of tensor-core workspace", need);
             return QMS_CUDA_ENOMEM;
         }
         g_mma_ws.bytes = need;
         g_mma_ws.dev = m->device;
     }
     mma_layout(m, T, &w, &need, (char *)g_mma_ws.p);
-    const int nw = mma_width(m, T), S = T * m->K, maxT = S / nw + m->X;
-    QMS_CK(launch_pdl(k_mma_group, dim3(1), dim3(1024), 0, s, (const int *)m->sel, S, m->X, maxT, nw, w));
+    if (dn) w.dn = dn;
+    const int nw = mma_width(m, T), maxT = S / nw + nx;
+    QMS_CK(launch_pdl(k_mma_group, dim3(1), dim3(1024), 0, s, sel, S, nx, maxT, nw, w));
     QMS_CK(launch_pdl(k_mma_gather, dim3(maxT, 8), dim3(2 * nw), 0, s, (const int8_t *)m->xq_q, (const float *)m->xq_d,
-                      (const int *)nullptr, m->nbE, m->K, nw, w));
+                      (const int *)nullptr, m->nbE, rdiv, nw, w));
     MmaArgs g;
     memset(&g, 0, sizeof g);
     g.w = m->gu;
@@ -698,11 +701,32 @@ int mma_forward(QmsCudaMoe *m, int T, const float *resid, float *out, cudaStream
     d.w_expert = m->dn_expert;
     d.nb = m->nbF;
     d.SB = 8;                                           // down stages: 8 blocks (F/32 % 8 == 0)
-    int rc = nw == kMmaNs ? mma_gemms<kMmaNs>(m, g, d, maxT, s) : mma_gemms<kMmaN>(m, g, d, maxT, s);
+    return nw == kMmaNs ? mma_gemms<kMmaNs>(m, g, d, maxT, s) : mma_gemms<kMmaN>(m, g, d, maxT, s);
+}
+
+// T > 1 tokens: router output (xq, sel, wts) already in m's scratch.
+int mma_forward(QmsCudaMoe *m, int T, const float *resid, float *out, cudaStream_t s) {
+    int rc = mma_core(m, T * m->K, m->sel, m->X, m->K, nullptr, s);
     if (rc) return rc;
+    MmaWork w;
+    size_t need = 0;
+    mma_layout(m, T, &w, &need, (char *)g_mma_ws.p);
     QMS_CK(launch_pdl(k_mma_combine, dim3((m->E + 255) / 256, T), dim3(256), 0, s, (const float *)w.dn,
                       (const float *)m->wts, m->K, m->E, resid, out));
     if (m->timing) QMS_CK(cudaEventRecord(m->ev[5], s));
+    return QMS_CUDA_OK;
+}
+
+// Expert FFNs of S slots whose rows are already quantised in m's xq scratch (row s) - the expert
+// side of expert parallelism. expert[s] is a local expert id (0 .. n_local - 1).
+int mma_experts(QmsCudaMoe *m, int S, const int *expert, float *dn, cudaStream_t s) {
+    return mma_core(m, S, expert, m->n_local, 1, dn, s);
+}
+
+// out[t] = sum_j w[t][j] * dn[t*K + j] in selection order (+ resid)
+int mma_combine(const float *dn, const float *wts, int T, int K, int E, const float *resid, float *out,
+                cudaStream_t s) {
+    QMS_CK(launch_pdl(k_mma_combine, dim3((E + 255) / 256, T), dim3(256), 0, s, dn, wts, K, E, resid, out));
     return QMS_CUDA_OK;
 }
 

@@ -203,11 +203,13 @@ def run_reference_arm(a):
 
 # ---- GPU ---------------------------------------------------------------------------------------
 
-def device_layer(q, torch, seed: int, device):
+def device_layer(q, torch, seed: int, device, shard=None):
     """A 235B-shape layer drawn on the device with the config's distributions, then uploaded
-    through qms_cuda_moe_create from device memory (GGUF layout, repacked by the library)."""
+    through qms_cuda_moe_create from device memory (GGUF layout, repacked by the library).
+    shard = (expert_base, n_local): only those experts (an expert-parallel shard)."""
     from large_model_b200 import synth
     E, X, K, F = synth.MOE_SHAPES[SHAPE]
+    XL = X if shard is None else shard[1]
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     router = torch.randn((X, E), generator=g, device=device, dtype=torch.float32) * 0.02
@@ -220,8 +222,8 @@ def device_layer(q, torch, seed: int, device):
         blk[:, 2:] = nib.view(torch.uint8).view(nblocks, 16)
         return blk.view(-1)
 
-    gate, up, down = q4_0(X * F * E // 32), q4_0(X * F * E // 32), q4_0(X * E * F // 32)
-    m = q.MoeLayer(E, X, K, F, router, gate, up, down)
+    gate, up, down = q4_0(XL * F * E // 32), q4_0(XL * F * E // 32), q4_0(XL * E * F // 32)
+    m = q.MoeLayer(E, X, K, F, router, gate, up, down, shard=shard)
     del router, gate, up, down
     return m
 
@@ -251,9 +253,16 @@ def run_batched(a):
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:
         cpu = cpu_reference_batched(T, seconds=10.0 if T <= 256 else 20.0)
-    layers = [device_layer(q, torch, 500 + 17 * i, dev) for i in range(2)]
+    ep = a.ep and world > 1
+    if ep:                                            # expert parallelism: X / world experts per rank
+        from large_model_b200.ep import CudaBackend, ExpertParallelMoe
+        per = X // world
+        layers = [device_layer(q, torch, 500 + 17 * i, dev, shard=(rank * per, per)) for i in range(2)]
+        eps = [ExpertParallelMoe(CudaBackend(m), X, K, E) for m in layers]
+    else:
+        layers = [device_layer(q, torch, 500 + 17 * i, dev) for i in range(2)]
     g = torch.Generator(device=dev)
-    g.manual_seed(11)
+    g.manual_seed(11 + rank)                          # every rank its own tokens
     xs = [torch.randn((T, E), generator=g, device=dev, dtype=torch.float32) for _ in range(2)]
     out = torch.empty((T, E), device=dev, dtype=torch.float32)
     for m in layers:
@@ -263,16 +272,24 @@ def run_batched(a):
 
     def step():
         for c in range(calls):
-            layers[c % 2].forward(xs[(c // 2) % 2], out=out, stream=stream)
+            if ep:
+                eps[c % 2].forward(xs[(c // 2) % 2])
+            else:
+                layers[c % 2].forward(xs[(c // 2) % 2], out=out, stream=stream)
 
     with torch.cuda.stream(stream):
         for _ in range(a.warmup):
             step()
     torch.cuda.synchronize()
     # distinct experts per call (bytes a call must read)
+    # (under EP: the union over all ranks' tokens - each expert is read once, by its owner)
     distinct = []
     for i in range(2):
-        _, sel, _, _ = layers[i].route(xs[i])
+        sel, _ = layers[i].route_only(xs[i])
+        if ep:
+            sels = [torch.empty_like(sel) for _ in range(world)]
+            dist.all_gather(sels, sel)
+            sel = torch.cat(sels)
         distinct.append(len(torch.unique(sel)))
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
@@ -298,7 +315,7 @@ def run_batched(a):
     # per-stage timing (router, gate/up + SwiGLU, down + combine) of single calls
     kev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
     ksum = [0.0, 0.0, 0.0]
-    nk = 4
+    nk = 0 if ep else 4
     for c in range(nk):
         m = layers[c % 2]
         m.set_kernel_events(kev)
@@ -309,32 +326,41 @@ def run_batched(a):
         for i in range(3):
             ksum[i] += kev[2 * i].elapsed_time(kev[2 * i + 1]) / nk
     expert_bytes = 3 * F * (E // 32) * 18
-    call_bytes = X * E * 4 + statistics.mean(distinct) * expert_bytes
+    if ep:                                           # all ranks together, per call time
+        call_bytes = world * X * E * 4 + statistics.mean(distinct) * expert_bytes
+    else:
+        call_bytes = world * (X * E * 4 + statistics.mean(distinct) * expert_bytes)
     ops = T * K * 6 * F * E                          # gate, up, down: 3 F E multiply-adds per slot
     # end to end through the host-buffer entry point
     xh = torch.empty((T, E), dtype=torch.float32, pin_memory=True)
     xh.copy_(xs[0].cpu())
     oh = torch.empty_like(xh, pin_memory=True)
-    layers[0].forward_host(xh.numpy(), out=oh.numpy())
     e2e_n = 4 if T <= 256 else 2
-    t0 = time.perf_counter()
-    for i in range(e2e_n):
-        layers[i % 2].forward_host(xh.numpy(), out=oh.numpy())
-    e2e_s = time.perf_counter() - t0
+    e2e = None
+    if not ep:
+        layers[0].forward_host(xh.numpy(), out=oh.numpy())
+        t0 = time.perf_counter()
+        for i in range(e2e_n):
+            layers[i % 2].forward_host(xh.numpy(), out=oh.numpy())
+        e2e_s = time.perf_counter() - t0
+        e2e = {"value": round(T * e2e_n / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": T * E * 4,
+               "d2h_bytes_per_step": T * E * 4, "note": "qms_cuda_moe_forward_host per call"}
     if rank == 0:
         if a.mode == "bs64":
             peak, peak_kind = peaks()
             gbs = call_bytes / (call_ms / 1e3) / 1e9
             roof = {"bound": "hbm", "kernel": "whole block (router, k_mma_gemm x2, gathers, combine)",
-                    "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                    "achieved": round(gbs, 1), "peak": peak * world, "unit": "GB/s",
+                    "frac": round(gbs / (peak * world), 4),
                     "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                     "bytes_per_call": int(call_bytes), "distinct_experts_per_call": statistics.mean(distinct),
                     "traffic": None}
             metric, unit, value = "Qwen3-235B Q4_0 MoE-layer decode bs64 tokens/s (operator)", "tok/s", tok_s
         else:
-            tops = ops / (call_ms / 1e3) / 1e12
+            tops = world * ops / (call_ms / 1e3) / 1e12
             roof = {"bound": "tensor", "kernel": "whole block (router, k_mma_gemm x2, gathers, combine)",
-                    "achieved": round(tops, 1), "peak": 4500.0, "unit": "TOP/s", "frac": round(tops / 4500.0, 4),
+                    "achieved": round(tops, 1), "peak": 4500.0 * world, "unit": "TOP/s",
+                    "frac": round(tops / (4500.0 * world), 4),
                     "peak_kind": "nominal dense int8 (no measured int8 peak on this pool)", "traffic": None,
                     "ops_per_call": ops}
             metric, unit, value = "Qwen3-235B Q4_0 MoE-layer prefill tokens/s (operator, 4096-token calls)", "tok/s", tok_s
@@ -348,10 +374,9 @@ def run_batched(a):
                                         "down_combine": round(ksum[2], 4)},
                            "l2": "inputs larger than L2 (2 layers x 1.36 GB resident)",
                            "routing": "seeded N(0,1) hidden states, N(0,0.02) router (near-uniform expert load)",
-                           "parallelism": f"replicas x{world}"},
+                           "parallelism": f"expert-parallel x{world} (NCCL all-to-all)" if ep else f"replicas x{world}"},
                 "roofline": roof, "cpu_baseline": cpu,
-                "e2e": {"value": round(T * e2e_n / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": T * E * 4,
-                        "d2h_bytes_per_step": T * E * 4, "note": "qms_cuda_moe_forward_host per call"},
+                "e2e": e2e,
                 "gpu_launches": None, "clocks": clocks}
         print(json.dumps(line), flush=True)
     for m in layers:
@@ -373,6 +398,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--mode", default="decode", choices=["decode", "bs64", "prefill"])
+    ap.add_argument("--ep", action="store_true", help="batched modes under torchrun: shard the experts over the ranks")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":

@@ -507,6 +507,9 @@ static int create_impl(const QmsCudaMoeDesc *d, int base, int n_local, QmsCudaMo
         m->mma_min_t = kMmaMinT;
         if (const char *env = getenv("QMS_MMA_MIN_T")) m->mma_min_t = atoi(env);   // 0 turns the path off
         if (m->mma_min_t > 0) rc = mma_prepare(m);
+        const char *gv = getenv("QMS_GEMV");                                          // 0 turns the GEMV off
+        m->gemv = m->mma_min_t > 0 && gv_supported(m) && !(gv && atoi(gv) == 0);
+        if (rc == QMS_CUDA_OK && m->gemv) rc = gv_prepare(m);
     }
     if (rc != QMS_CUDA_OK) {
         qms_cuda_moe_destroy(m);

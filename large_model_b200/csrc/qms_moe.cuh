@@ -171,7 +171,8 @@ struct QmsCudaMoe {
     uint8_t *dn;         // [X] experts of down column stages
     size_t gu_expert, dn_expert, weight_bytes;
     int stream_ok;       // batch-1 streaming kernels usable for this shape
-    int mma_min_t;       // T from which the grouped tensor-core kernels run (0: never)
+    int mma_min_t;       // T from which the grouped kernels run (0: never)
+    int gemv;            // grouped GEMV (CUDA cores) for calls of few slots per expert
     // scratch, sized for cap_T tokens
     int cap_T;
     void *scratch;
@@ -238,5 +239,21 @@ int mma_forward(QmsCudaMoe *m, int T, const float *resid, float *out, cudaStream
 int mma_experts(QmsCudaMoe *m, int S, const int *expert, float *dn, cudaStream_t s);
 int mma_combine(const float *dn, const float *wts, int T, int K, int E, const float *resid, float *out,
                 cudaStream_t s);
+
+// Slots grouped by expert (k_mma_group): per expert its count, first position and first tile;
+// the tile list (expert | tile index << 16) and the slot ids in expert order.
+struct MmaWork {
+    int *cnt, *off, *toff, *ntiles, *pos, *slots, *tiles;
+    int8_t *bg;        // [tiles][nb][2048] tensor-core B operands
+    float *bs;         // [tiles][nb][64] activation scales
+    int *bsum;         // [tiles][nb][64] activation block sums (Q4_1 down)
+    float *dn;         // [T*K][E] down rows per slot
+};
+
+// batched expert-grouped GEMV kernels (qms_moe_gemv.cu), the grouped path when experts average
+// <= 24 slots per call (16-slot tiles)
+int gv_supported(const QmsCudaMoe *m);
+int gv_prepare(QmsCudaMoe *m);
+int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int rdiv, cudaStream_t s);
 
 }  // namespace qms

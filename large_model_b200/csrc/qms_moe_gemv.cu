@@ -1,0 +1,540 @@
+// qms_moe_gemv.cu - the MoE block for batched decode: expert-grouped GEMV on the CUDA cores.
+//
+// At batched-decode sizes the T*K slots spread over the X experts a few at a time, so a call is
+// one read of every selected expert's weights; on N = 1..16 columns the tensor cores would idle
+// while the per-block scale work dominates. Here each expert's weights stream from HBM once per
+// call and serve all of its slots. After the slots are grouped by expert (k_mma_group, tiles of
+// up to 16 slots of one expert, the reference's grouping of src/model.c:1066-1088):
+//   k_gv_gate_up  persistent, one CTA per SM, owning a contiguous range of (tile, 32-f) items. A
+//                 producer warp streams each item's gate/up stages (one bulk copy each, the staged
+//                 chunk layout) through a ring in shared memory; 8 consumer warps hold the tile's
+//                 Q8 activation rows in shared memory and form every (row, slot) dot with dp4a,
+//                 each 32-block's int32 sum scaled in fp32 (src/kernels.c:82-107); then SwiGLU and
+//                 the Q8 group of each slot's 32 f values (src/model.c:989-997).
+//   k_gv_down     the same over (tile, 256/512 down rows) items: per F/32 block column the rows'
+//                 column stage slice, against the slots' Q8 activation groups; writes each slot's
+//                 unweighted down row (src/model.c:999-1004), summed by k_mma_combine in selection
+//                 order. Q4_0 and Q4_1 down.
+// A 32-block's integer dot is exact; only the fp32 summation order differs from the reference.
+#include <string.h>
+
+#include <algorithm>
+
+#include "qms_async.cuh"
+#include "qms_moe.cuh"
+
+namespace qms {
+
+constexpr int kGvSlots = 16;                 // slots per tile (k_mma_group width)
+constexpr int kGvConsWarps = 8;
+constexpr int kGvCons = kGvConsWarps * 32;
+constexpr int kGvThreads = kGvCons + 32;     // + producer warp
+constexpr int kGvMaxRing = 16;
+constexpr size_t kGvSmemCap = 220 * 1024;
+constexpr uint32_t kGvSpin = 1u << 22;
+constexpr int kGvMagic = 0x4B400000;         // float bits of 2^23 + 2^22: int v -> float exactly for |v| < 2^22
+constexpr float kGvMagicF = 12582912.0f;
+
+enum { GV_ERR = 128 };
+
+struct GvArgs {
+    const uint8_t *w;          // staged experts: gate/up chunks or down column stages
+    size_t w_expert;
+    Chunked c;
+    DnCols dc;
+    int nb;                    // blocks along K: E/32 (gate/up) or F/32 (down)
+    int F, E;
+    MmaWork wk;                // slot groups: tiles, cnt, off, slots, ntiles
+    const int8_t *xq;          // activation rows [rows][nb * 32]
+    const float *xd;           // [rows][nb] block scales
+    const int *xs;             // [rows][nb] block sums
+    int rdiv;                  // activation row of slot s: s / rdiv
+    int ring;                  // stages in the shared-memory ring
+    uint32_t sst;              // bytes of one ring stage (multiple of 128)
+    int8_t *aq_q;              // gate/up out: [S][F] Q8 values
+    float *aq_d;               // [S][F/32]
+    int *aq_s;                 // [S][F/32]
+    float *dn;                 // down out: [S][E]
+    int *err;
+};
+
+// Bounded wait on an mbarrier phase; on timeout set the CTA's abort flag and the error bit.
+__device__ __forceinline__ bool gv_wait(uint64_t *bar, uint32_t parity, volatile int *abort, int *err) {
+    uint32_t n = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort) return false;
+        if (++n == kGvSpin) {
+            *abort = 1;
+            atomicOr(err, GV_ERR);
+            return false;
+        }
+        if (n > 64) __nanosleep(32);
+    }
+    return true;
+}
+
+__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kGvCons) : "memory"); }
+
+// Integer dot of one 32-block from pre-split nibble words: w[0..3] low nibbles (elements 0-15),
+// w[4..7] high nibbles (16-31); two independent dp4a chains.
+__device__ __forceinline__ int gv_isum(const uint32_t (&w)[8], uint4 x0, uint4 x1) {
+    int a = __dp4a((int)w[0], (int)x0.x, 0);
+    int b = __dp4a((int)w[4], (int)x1.x, 0);
+    a = __dp4a((int)w[1], (int)x0.y, a);
+    b = __dp4a((int)w[5], (int)x1.y, b);
+    a = __dp4a((int)w[2], (int)x0.z, a);
+    b = __dp4a((int)w[6], (int)x1.z, b);
+    a = __dp4a((int)w[3], (int)x0.w, a);
+    b = __dp4a((int)w[7], (int)x1.w, b);
+    return a + b;
+}
+
+__device__ __forceinline__ void gv_split(uint4 v, uint32_t (&w)[8]) {
+    const uint32_t m = 0x0F0F0F0Fu;
+    w[0] = v.x & m;
+    w[1] = v.y & m;
+    w[2] = v.z & m;
+    w[3] = v.w & m;
+    w[4] = (v.x >> 4) & m;
+    w[5] = (v.y >> 4) & m;
+    w[6] = (v.z >> 4) & m;
+    w[7] = (v.w >> 4) & m;
+}
+
+// This CTA's contiguous share of n items.
+__device__ __forceinline__ void gv_range(int n, int &lo, int &hi) {
+    lo = (int)((long long)n * blockIdx.x / gridDim.x);
+    hi = (int)((long long)n * (blockIdx.x + 1) / gridDim.x);
+}
+
+struct GvTile {
+    int e, off, ns;            // expert, first slot in the grouped list, slots in the tile
+};
+
+__device__ __forceinline__ GvTile gv_tile(const MmaWork &w, int tl) {
+    const int t = __ldcg(w.tiles + tl);
+    GvTile g;
+    g.e = t & 0xFFFF;
+    const int n0 = (t >> 16) * kGvSlots;
+    g.off = __ldcg(w.off + g.e) + n0;
+    g.ns = min(kGvSlots, __ldcg(w.cnt + g.e) - n0);
+    return g;
+}
+
+// Consumers: the tile's activation rows into shared memory, [slot][K half][block][16 bytes] (one
+// half of consecutive blocks is contiguous: conflict-free 16-byte reads), plus per (slot, block)
+// {scale bits, second word}: the block sum, or for Q4_1 down the product d * sum as float bits.
+template <bool DSUM>
+__device__ __forceinline__ void gv_stage_x(const GvArgs &a, const GvTile &g, int8_t *sx, uint2 *sxs) {
+    const int nb = a.nb, K32 = nb * 32;
+    for (int idx = threadIdx.x; idx < g.ns * nb * 2; idx += kGvCons) {
+        const int j = idx / (2 * nb), rem = idx - j * 2 * nb, h = rem / nb, b = rem - h * nb;
+        const int row = __ldcg(a.wk.slots + g.off + j) / a.rdiv;
+        const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(a.xq + (size_t)row * K32 + b * 32 + h * 16));
+        *reinterpret_cast<uint4 *>(sx + ((size_t)(j * 2 + h) * nb + b) * 16) = v;
+        if (h == 0) {
+            const float d = __ldcg(a.xd + (size_t)row * nb + b);
+            const int s = __ldcg(a.xs + (size_t)row * nb + b);
+            sxs[j * nb + b] = make_uint2(__float_as_uint(d), DSUM ? __float_as_uint(d * (float)s) : (uint32_t)s);
+        }
+    }
+}
+
+// Producer (one thread): for each item of [lo, hi), nst ring stages; src(expert base, item's
+// index within its tile, stage, ring slot, full barrier, policy) issues one stage's bulk copies.
+// Waits are bounded.
+template <typename Src>
+__device__ __forceinline__ void gv_produce(const GvArgs &a, int lo, int hi, int ipt, int nst, uint8_t *ring,
+                                           uint64_t *full, uint64_t *empty, volatile int *abort, Src src) {
+    const uint64_t pol = evict_first_policy();
+    int r = 0;
+    uint32_t par = 0, issued = 0;
+    bool ok = true;
+    int cur = -1;
+    const uint8_t *base = nullptr;
+    for (int item = lo; item < hi && ok; item++) {
+        const int tl = item / ipt, sub = item - tl * ipt;
+        if (tl != cur) {
+            cur = tl;
+            base = a.w + (size_t)(__ldcg(a.wk.tiles + tl) & 0xFFFF) * a.w_expert;
+        }
+        for (int st = 0; st < nst; st++) {
+            if (issued >= (uint32_t)a.ring && !(ok = gv_wait(&empty[r], par ^ 1, abort, a.err))) break;
+            if (*abort) {                  // consumers stopped: they no longer free stages
+                ok = false;
+                break;
+            }
+            src(base, sub, st, ring + (size_t)r * a.sst, &full[r], pol);
+            issued++;
+            if (++r == a.ring) {
+                r = 0;
+                par ^= 1;
+            }
+        }
+    }
+    // Copies still in flight land before the CTA exits (after a normal run every one of them has
+    // been consumed and these waits return at once). A consumer frees a stage only after it saw
+    // the stage's copy land, so no stage ever holds two copies.
+    const uint32_t n = issued < (uint32_t)a.ring ? issued : (uint32_t)a.ring;
+    for (uint32_t k = issued - n; k < issued; k++) {
+        uint32_t spin = 0;
+        while (!mbar_try_wait(&full[k % a.ring], (k / a.ring) & 1) && ++spin < kGvSpin) __nanosleep(64);
+    }
+}
+
+// ---- gate/up + SwiGLU + Q8 ---------------------------------------------------------------------------
+// Item (tile, ft): f values ft*32 .. +31 of the tile's expert; its nb/SB stages are the staged
+// chunks (8 chunks of 8 rows x SB blocks: chunks 0-3 gate rows, 4-7 up rows). Consumer thread t:
+// block b = t % SB of every stage, f values (t / SB) * FPT + i; FPT = SB / 8.
+template <int SB>
+__global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
+    constexpr int FPT = SB / 8;
+    constexpr uint32_t GB = 8u * SB * 18;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_abort;
+    const int nb = a.nb, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint8_t *ring = smem;
+    int8_t *sx = reinterpret_cast<int8_t *>(smem + (size_t)a.ring * a.sst);
+    uint2 *sxs = reinterpret_cast<uint2 *>(sx + (size_t)kGvSlots * nb * 32);
+    float *sact = reinterpret_cast<float *>(sxs + kGvSlots * nb);          // [2][slot][32]
+    uint64_t *full = reinterpret_cast<uint64_t *>(sact + 2 * kGvSlots * 32);
+    uint64_t *empty = full + a.ring;
+    if (tid == 0) {
+        s_abort = 0;
+        for (int r = 0; r < a.ring; r++) {
+            mbar_init(&full[r], 1);
+            mbar_init(&empty[r], kGvConsWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_trigger();
+    const int ipt = a.F / 32, nst = nb / SB;
+    int lo, hi;
+    gv_range(__ldcg(a.wk.ntiles) * ipt, lo, hi);
+    if (warp == kGvConsWarps) {
+        if (lane == 0)
+            gv_produce(a, lo, hi, ipt, nst, ring, full, empty, &s_abort,
+                       [&](const uint8_t *base, int sub, int st, uint8_t *dst, uint64_t *bar, uint64_t pol) {
+                           mbar_arrive_expect_tx(bar, 8 * GB);
+                           bulk_load(dst, base + ((size_t)(sub * nst + st) * 8) * GB, 8 * GB, bar, pol);
+                       });
+        return;
+    }
+    const int b = tid % SB, fg = tid / SB;
+    int r = 0;
+    uint32_t par = 0;
+    bool ok = true;
+    int cur = -1, buf = 0;
+    GvTile g{0, 0, 0};
+    for (int item = lo; item < hi; item++) {
+        const int tl = item / ipt, sub = item - tl * ipt;
+        if (tl != cur) {
+            cons_sync();                                   // every consumer is done with the old rows
+            cur = tl;
+            g = gv_tile(a.wk, tl);
+            gv_stage_x<false>(a, g, sx, sxs);
+            cons_sync();
+        }
+        float ag[FPT][kGvSlots], au[FPT][kGvSlots];
+#pragma unroll
+        for (int i = 0; i < FPT; i++)
+#pragma unroll
+            for (int j = 0; j < kGvSlots; j++) ag[i][j] = au[i][j] = 0.0f;
+        for (int st = 0; st < nst; st++) {
+            if (ok) ok = gv_wait(&full[r], par, &s_abort, a.err);
+            uint32_t wg[FPT][8], wu[FPT][8];
+            float dg[FPT], du[FPT];
+            if (ok) {
+                const uint8_t *stg = ring + (size_t)r * a.sst;
+#pragma unroll
+                for (int i = 0; i < FPT; i++) {
+                    const int f = fg * FPT + i;
+                    const uint8_t *cg = stg + (f >> 3) * GB, *cu = cg + 4 * GB;
+                    const uint32_t o = (uint32_t)((f & 7) * SB + b);
+                    gv_split(*reinterpret_cast<const uint4 *>(cg + o * 16), wg[i]);
+                    gv_split(*reinterpret_cast<const uint4 *>(cu + o * 16), wu[i]);
+                    dg[i] = h2f(*reinterpret_cast<const uint16_t *>(cg + 8 * SB * 16 + o * 2));
+                    du[i] = h2f(*reinterpret_cast<const uint16_t *>(cu + 8 * SB * 16 + o * 2));
+                }
+            }
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(&empty[r]);  // weights are in registers: free the stage
+            if (++r == a.ring) {
+                r = 0;
+                par ^= 1;
+            }
+            if (!ok) continue;
+            const int gb = st * SB + b;
+#pragma unroll
+            for (int j = 0; j < kGvSlots; j++) {
+                if (j < g.ns) {
+                    const uint4 x0 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2) * nb + gb) * 16);
+                    const uint4 x1 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2 + 1) * nb + gb) * 16);
+                    const uint2 xv = sxs[j * nb + gb];
+                    const float xd = __uint_as_float(xv.x);
+                    const int bias = kGvMagic - 8 * (int)xv.y;       // Q4_0: d (q - 8), -8 via the block sum
+#pragma unroll
+                    for (int i = 0; i < FPT; i++) {
+                        const float pg = __int_as_float(gv_isum(wg[i], x0, x1) + bias) - kGvMagicF;
+                        const float pu = __int_as_float(gv_isum(wu[i], x0, x1) + bias) - kGvMagicF;
+                        ag[i][j] = fmaf(pg, dg[i] * xd, ag[i][j]);
+                        au[i][j] = fmaf(pu, du[i] * xd, au[i][j]);
+                    }
+                }
+            }
+        }
+        // sums over the SB threads of each f group (adjacent lanes), SwiGLU, Q8 groups per slot
+        float *sa = sact + buf * kGvSlots * 32;
+#pragma unroll
+        for (int j = 0; j < kGvSlots; j++) {
+            if (j < g.ns) {
+#pragma unroll
+                for (int i = 0; i < FPT; i++) {
+#pragma unroll
+                    for (int o = SB / 2; o > 0; o >>= 1) {
+                        ag[i][j] += __shfl_xor_sync(0xffffffffu, ag[i][j], o);
+                        au[i][j] += __shfl_xor_sync(0xffffffffu, au[i][j], o);
+                    }
+                    if (b == 0) {
+                        const float gv = ag[i][j];
+                        const float s = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
+                        sa[j * 32 + fg * FPT + i] = __fmul_rn(s, au[i][j]);
+                    }
+                }
+            }
+        }
+        cons_sync();
+        for (int j = warp; j < g.ns; j += kGvConsWarps) {
+            const Q8Lane q = quantize_lane(sa[j * 32 + lane]);
+            if (ok) {
+                const int slot = __ldcg(a.wk.slots + g.off + j);
+                a.aq_q[(size_t)slot * a.F + sub * 32 + lane] = (int8_t)q.q;
+                if (lane == 0) {
+                    a.aq_d[(size_t)slot * ipt + sub] = q.d;
+                    a.aq_s[(size_t)slot * ipt + sub] = q.sum;
+                }
+            }
+        }
+        buf ^= 1;
+    }
+}
+
+// ---- down ------------------------------------------------------------------------------------------
+// Item (tile, rb): down rows rb*DNR .. +DNR-1 of the tile's expert (DNR = 256 * RPT, within one
+// column stage row range); stage st = block column st: the rows' nibbles, scales (and Q4_1 mins)
+// sliced from column stage (st, rows). Consumer thread t: rows t + 256 i.
+template <bool Q1, int RPT>
+__global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
+    constexpr int DNR = 256 * RPT;
+    constexpr uint32_t NIB = DNR * 16, SCL = DNR * 2;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_abort;
+    const int nb = a.nb, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint8_t *ring = smem;
+    int8_t *sx = reinterpret_cast<int8_t *>(smem + (size_t)a.ring * a.sst);
+    uint2 *sxs = reinterpret_cast<uint2 *>(sx + (size_t)kGvSlots * nb * 32);
+    uint64_t *full = reinterpret_cast<uint64_t *>(sxs + kGvSlots * nb);
+    uint64_t *empty = full + a.ring;
+    if (tid == 0) {
+        s_abort = 0;
+        for (int r = 0; r < a.ring; r++) {
+            mbar_init(&full[r], 1);
+            mbar_init(&empty[r], kGvConsWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_trigger();
+    const int ipt = a.E / DNR, nst = nb;
+    int lo, hi;
+    gv_range(__ldcg(a.wk.ntiles) * ipt, lo, hi);
+    if (warp == kGvConsWarps) {
+        if (lane == 0)
+            gv_produce(a, lo, hi, ipt, nst, ring, full, empty, &s_abort,
+                       [&](const uint8_t *base, int sub, int st, uint8_t *dst, uint64_t *bar, uint64_t pol) {
+                           const int row0 = sub * DNR;
+                           const uint8_t *stg = base + dn_stage_off(a.dc, st, row0);
+                           mbar_arrive_expect_tx(bar, NIB + SCL * (Q1 ? 2 : 1));
+                           bulk_load(dst, stg + dn_nib_off(a.dc, row0), NIB, bar, pol);
+                           bulk_load(dst + NIB, stg + dn_scale_off(a.dc, row0), SCL, bar, pol);
+                           if (Q1) bulk_load(dst + NIB + SCL, stg + dn_min_off(a.dc, row0), SCL, bar, pol);
+                       });
+        return;
+    }
+    int r = 0;
+    uint32_t par = 0;
+    bool ok = true;
+    int cur = -1;
+    GvTile g{0, 0, 0};
+    for (int item = lo; item < hi; item++) {
+        const int tl = item / ipt, sub = item - tl * ipt;
+        if (tl != cur) {
+            cons_sync();
+            cur = tl;
+            g = gv_tile(a.wk, tl);
+            gv_stage_x<Q1>(a, g, sx, sxs);
+            cons_sync();
+        }
+        float acc[RPT][kGvSlots];
+#pragma unroll
+        for (int i = 0; i < RPT; i++)
+#pragma unroll
+            for (int j = 0; j < kGvSlots; j++) acc[i][j] = 0.0f;
+        for (int st = 0; st < nst; st++) {
+            if (ok) ok = gv_wait(&full[r], par, &s_abort, a.err);
+            uint32_t wn[RPT][8];
+            float dw[RPT], mw[RPT];
+            if (ok) {
+                const uint8_t *stg = ring + (size_t)r * a.sst;
+#pragma unroll
+                for (int i = 0; i < RPT; i++) {
+                    const int row = tid + 256 * i;
+                    gv_split(*reinterpret_cast<const uint4 *>(stg + row * 16), wn[i]);
+                    dw[i] = h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + row * 2));
+                    mw[i] = Q1 ? h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + SCL + row * 2)) : 0.0f;
+                }
+            }
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(&empty[r]);
+            if (++r == a.ring) {
+                r = 0;
+                par ^= 1;
+            }
+            if (!ok) continue;
+#pragma unroll
+            for (int j = 0; j < kGvSlots; j++) {
+                if (j < g.ns) {
+                    const uint4 x0 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2) * nb + st) * 16);
+                    const uint4 x1 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2 + 1) * nb + st) * 16);
+                    const uint2 xv = sxs[j * nb + st];
+                    const float xd = __uint_as_float(xv.x);
+#pragma unroll
+                    for (int i = 0; i < RPT; i++) {
+                        if (Q1) {                          // d q + m: d dx isum + m (dx sum)  (src/kernels.c:109-121)
+                            const float p = __int_as_float(gv_isum(wn[i], x0, x1) + kGvMagic) - kGvMagicF;
+                            acc[i][j] = fmaf(p, dw[i] * xd, acc[i][j]);
+                            acc[i][j] = fmaf(mw[i], __uint_as_float(xv.y), acc[i][j]);
+                        } else {
+                            const float p = __int_as_float(gv_isum(wn[i], x0, x1) + (kGvMagic - 8 * (int)xv.y)) - kGvMagicF;
+                            acc[i][j] = fmaf(p, dw[i] * xd, acc[i][j]);
+                        }
+                    }
+                }
+            }
+        }
+        if (ok) {
+#pragma unroll
+            for (int j = 0; j < kGvSlots; j++) {
+                if (j < g.ns) {
+                    float *o = a.dn + (size_t)__ldcg(a.wk.slots + g.off + j) * a.E + sub * DNR + tid;
+#pragma unroll
+                    for (int i = 0; i < RPT; i++) o[256 * i] = acc[i][j];
+                }
+            }
+        }
+    }
+}
+
+// ---- host side -------------------------------------------------------------------------------------
+static uint32_t al128(size_t n) { return (uint32_t)((n + 127) & ~(size_t)127); }
+
+static int gv_dn_rpt(const QmsCudaMoe *m) { return m->dcol.RD % 512 == 0 ? 2 : 1; }
+
+static uint32_t gv_stage_bytes(const QmsCudaMoe *m, bool gu) {
+    if (gu) return al128(8 * (size_t)m->cgu.GB);
+    const size_t dnr = 256 * (size_t)gv_dn_rpt(m);
+    return al128(dnr * 16 + dnr * 2 * (m->dcol.q1 ? 2 : 1));
+}
+
+static size_t gv_fixed(const QmsCudaMoe *m, bool gu) {
+    const int nb = gu ? m->nbE : m->nbF;
+    return (size_t)kGvSlots * nb * 40 + (gu ? 2 * kGvSlots * 32 * 4 : 0);
+}
+
+static int gv_ring(const QmsCudaMoe *m, bool gu) {
+    const size_t fixed = gv_fixed(m, gu), sst = gv_stage_bytes(m, gu);
+    if (fixed + 2 * (sst + 16) > kGvSmemCap) return 0;
+    return (int)std::min<size_t>(kGvMaxRing, (kGvSmemCap - fixed) / (sst + 16));
+}
+
+static size_t gv_smem(const QmsCudaMoe *m, bool gu) {
+    const int ring = gv_ring(m, gu);
+    return (size_t)ring * gv_stage_bytes(m, gu) + gv_fixed(m, gu) + (size_t)ring * 16;
+}
+
+// Shapes the grouped GEMV covers: staged gate/up chunks of 16 or 8 blocks, down column stages of
+// >= 256 rows, both rings at least 2 stages deep.
+int gv_supported(const QmsCudaMoe *m) {
+    return (m->cgu.SB == 16 || m->cgu.SB == 8) && m->F % 32 == 0 && m->dcol.RD % 256 == 0 && m->E % 256 == 0 &&
+           m->X <= 256 && gv_ring(m, true) >= 2 && gv_ring(m, false) >= 2;
+}
+
+int gv_prepare(QmsCudaMoe *m) {
+    const void *gk = m->cgu.SB == 16 ? (const void *)k_gv_gate_up<16> : (const void *)k_gv_gate_up<8>;
+    QMS_CK(cudaFuncSetAttribute(gk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gv_smem(m, true)));
+    const bool q1 = m->dcol.q1;
+    const int rpt = gv_dn_rpt(m);
+    const void *dk = q1 ? (rpt == 2 ? (const void *)k_gv_down<true, 2> : (const void *)k_gv_down<true, 1>)
+                        : (rpt == 2 ? (const void *)k_gv_down<false, 2> : (const void *)k_gv_down<false, 1>);
+    QMS_CK(cudaFuncSetAttribute(dk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gv_smem(m, false)));
+    return QMS_CUDA_OK;
+}
+
+// gate/up + SwiGLU + Q8 into m's aq scratch, then down rows into w.dn, for the slots grouped in w
+// (tiles of kGvSlots); activation row of slot s: s / rdiv of m's xq scratch.
+int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int rdiv, cudaStream_t s) {
+    GvArgs g;
+    memset(&g, 0, sizeof g);
+    g.w = m->gu;
+    g.w_expert = m->gu_expert;
+    g.c = m->cgu;
+    g.dc = m->dcol;
+    g.nb = m->nbE;
+    g.F = m->F;
+    g.E = m->E;
+    g.wk = w;
+    g.xq = m->xq_q;
+    g.xd = m->xq_d;
+    g.xs = m->xq_s;
+    g.rdiv = rdiv;
+    g.ring = gv_ring(m, true);
+    g.sst = gv_stage_bytes(m, true);
+    g.aq_q = m->aq_q;
+    g.aq_d = m->aq_d;
+    g.aq_s = m->aq_s;
+    g.err = m->err;
+    const dim3 grid(m->nsm), block(kGvThreads);
+    if (m->cgu.SB == 16)
+        QMS_CK(launch_pdl(k_gv_gate_up<16>, grid, block, gv_smem(m, true), s, g));
+    else
+        QMS_CK(launch_pdl(k_gv_gate_up<8>, grid, block, gv_smem(m, true), s, g));
+    if (m->timing) {
+        QMS_CK(cudaEventRecord(m->ev[3], s));
+        QMS_CK(cudaEventRecord(m->ev[4], s));
+    }
+    GvArgs d = g;
+    d.w = m->dn;
+    d.w_expert = m->dn_expert;
+    d.nb = m->nbF;
+    d.xq = m->aq_q;
+    d.xd = m->aq_d;
+    d.xs = m->aq_s;
+    d.rdiv = 1;
+    d.ring = gv_ring(m, false);
+    d.sst = gv_stage_bytes(m, false);
+    d.dn = w.dn;
+    const size_t sm = gv_smem(m, false);
+    if (m->dcol.q1) {
+        if (gv_dn_rpt(m) == 2) QMS_CK(launch_pdl(k_gv_down<true, 2>, grid, block, sm, s, d));
+        else QMS_CK(launch_pdl(k_gv_down<true, 1>, grid, block, sm, s, d));
+    } else {
+        if (gv_dn_rpt(m) == 2) QMS_CK(launch_pdl(k_gv_down<false, 2>, grid, block, sm, s, d));
+        else QMS_CK(launch_pdl(k_gv_down<false, 1>, grid, block, sm, s, d));
+    }
+    return QMS_CUDA_OK;
+}
+
+}  // namespace qms

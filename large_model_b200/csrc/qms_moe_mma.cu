@@ -157,14 +157,6 @@ __device__ __forceinline__ void nib_to_s8(uint4 v, bool minus8, uint4 &lo, uint4
 }
 
 // ---- slot grouping -------------------------------------------------------------------------------
-struct MmaWork {
-    int *cnt, *off, *toff, *ntiles, *pos, *slots, *tiles;
-    int8_t *bg;        // [tiles][nb][2048] B operands
-    float *bs;         // [tiles][nb][64] activation scales
-    int *bsum;         // [tiles][nb][64] activation block sums (Q4_1 down)
-    float *dn;         // [T*K][E] down rows per slot
-};
-
 // One CTA: slots s = t*K + j grouped by expert sel[s]; tiles of nw slots per expert.
 __global__ void __launch_bounds__(1024) k_mma_group(const int *__restrict__ sel, int S, int X, int maxT, int nw, MmaWork w) {
     __shared__ int s_cnt[256], s_off[257], s_toff[257];
@@ -585,11 +577,13 @@ static struct {
     int dev = -1;
 } g_mma_ws;
 
-// Tile width: 16 slots when experts average few slots (batched decode), else 64.
-static int mma_width(const QmsCudaMoe *m, int T) { return (int64_t)T * m->K <= (int64_t)24 * m->X ? kMmaNs : kMmaN; }
+// Tile width for S slots over nx experts: 16 slots while the experts average <= 24 slots, else 64.
+static int mma_width(int S, int nx) { return (int64_t)S <= (int64_t)24 * nx ? kMmaNs : kMmaN; }
 
 static int mma_layout(const QmsCudaMoe *m, int T, MmaWork *w, size_t *bytes, char *base) {
-    const size_t nw = mma_width(m, T), S = (size_t)T * m->K, maxT = S / nw + m->X;
+    const size_t S = (size_t)T * m->K;
+    const size_t maxT = S / kMmaNs + m->X;                                  // tiles at the narrower width
+    const size_t bcols = std::max(maxT * kMmaNs, (S / kMmaN + m->X) * kMmaN);   // B columns at either width
     const int nbmax = std::max(m->nbE, m->nbF);
     size_t off = 0;
     auto take = [&](size_t n) { size_t o = off; off += (n + 255) & ~(size_t)255; return base + o; };
@@ -600,9 +594,9 @@ static int mma_layout(const QmsCudaMoe *m, int T, MmaWork *w, size_t *bytes, cha
     w->pos = (int *)take(S * 4);
     w->slots = (int *)take(S * 4);
     w->tiles = (int *)take(maxT * 4);
-    w->bg = (int8_t *)take(maxT * nbmax * nw * 32);
-    w->bs = (float *)take(maxT * nbmax * nw * 4);
-    w->bsum = (int *)take(maxT * nbmax * nw * 4);
+    w->bg = (int8_t *)take(bcols * nbmax * 32);
+    w->bs = (float *)take(bcols * nbmax * 4);
+    w->bsum = (int *)take(bcols * nbmax * 4);
     w->dn = (float *)take(S * m->E * 4);
     *bytes = off;
     return QMS_CUDA_OK;
@@ -676,8 +670,9 @@ static int mma_core(QmsCudaMoe *m, int S, const int *sel, int nx, int rdiv, floa
     }
     mma_layout(m, T, &w, &need, (char *)g_mma_ws.p);
     if (dn) w.dn = dn;
-    const int nw = mma_width(m, T), maxT = S / nw + nx;
+    const int nw = mma_width(S, nx), maxT = S / nw + nx;
     QMS_CK(launch_pdl(k_mma_group, dim3(1), dim3(1024), 0, s, sel, S, nx, maxT, nw, w));
+    if (m->gemv && nw == kMmaNs) return gv_gemms(m, w, rdiv, s);   // few slots per expert: CUDA cores
     QMS_CK(launch_pdl(k_mma_gather, dim3(maxT, 8), dim3(2 * nw), 0, s, (const int8_t *)m->xq_q, (const float *)m->xq_d,
                       (const int *)nullptr, m->nbE, rdiv, nw, w));
     MmaArgs g;

@@ -129,14 +129,30 @@ def test_moe_edge_cases(cuda, oracle):
 @pytest.mark.parametrize("shape,T,down", [("tiny", 16, 2), ("tiny", 70, 3), ("tiny", 200, 3), ("30b", 16, 2),
                                           ("30b", 130, 2), ("235b", 16, 2), ("235b", 64, 3), ("235b", 200, 2),
                                           ("235b", 512, 2)])
-def test_moe_grouped_mma_matches_oracle(cuda, oracle, shape, T, down):
+def test_moe_grouped_mma_matches_oracle(cuda, oracle, monkeypatch, shape, T, down):
     """T >= 16: expert-grouped tcgen05 kind::i8 GEMMs against the oracle, with the batch bars: 16-slot
     tiles while experts average <= 24 slots, 64-slot tiles above (tiny T=200, 235B T=512); partial
-    and multiple tiles per expert; Q4_0 and Q4_1 down."""
+    and multiple tiles per expert; Q4_0 and Q4_1 down. The grouped GEMV, which takes the 16-slot
+    calls by default, is switched off for these layers."""
+    monkeypatch.setenv("QMS_GEMV", "0")
     layer = synth.make_moe_layer(shape, seed=91 + T, down_type=down)
     xn = synth.make_hidden(layer.n_embd, T, seed=93 + T)
     m, out, sel, w, logits = _run(cuda, layer, xn)
     _check(oracle, layer, xn, out, sel, w, logits, f"mma {shape} T={T} down={down}")
+    m.close()
+
+
+@pytest.mark.parametrize("shape,T,down", [("tiny", 16, 2), ("tiny", 40, 3), ("tiny", 150, 2), ("30b", 16, 2),
+                                          ("30b", 64, 3), ("235b", 16, 2), ("235b", 64, 2), ("235b", 130, 3),
+                                          ("235b", 300, 2)])
+def test_moe_grouped_gemv_matches_oracle(cuda, oracle, shape, T, down):
+    """Batched decode (experts average <= 24 slots): the expert-grouped GEMV kernels (one weight read
+    per expert and call, dp4a over up to 16 slots per tile) against the oracle; Q4_0 and Q4_1 down;
+    one tile per expert (235B T=16/64) up to several per expert (tiny T=150, 235B T=300)."""
+    layer = synth.make_moe_layer(shape, seed=191 + T, down_type=down)
+    xn = synth.make_hidden(layer.n_embd, T, seed=193 + T)
+    m, out, sel, w, logits = _run(cuda, layer, xn)
+    _check(oracle, layer, xn, out, sel, w, logits, f"gemv {shape} T={T} down={down}")
     m.close()
 
 

@@ -157,6 +157,29 @@ __device__ __forceinline__ unsigned long long ld_flagged(const unsigned long lon
     return v;
 }
 
+// ---- packed pairs of fp32 (sm_100 f32x2 instructions): two lanes of work per instruction ---------
+__device__ __forceinline__ unsigned long long f2_bits(float2 v) {
+    return ((unsigned long long)__float_as_uint(v.y) << 32) | __float_as_uint(v.x);
+}
+__device__ __forceinline__ float2 f2_from(unsigned long long b) {
+    return make_float2(__uint_as_float((uint32_t)b), __uint_as_float((uint32_t)(b >> 32)));
+}
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+    return f2_from(d);
+}
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return f2_from(d);
+}
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return f2_from(d);
+}
+
 // ---- programmatic dependent launch ---------------------------------------------------------
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

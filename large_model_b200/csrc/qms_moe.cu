@@ -151,61 +151,79 @@ __global__ void __launch_bounds__(256) k_quantize_rows(const float *__restrict__
     }
 }
 
-// logits[t][e] for a tile of 32 tokens x 32 experts per CTA, in qms_vec_dot_f32's exact order
-// (src/kernels.c:202-219): thread (k, g) runs lane k's FMA chain for 8 tokens x 8 experts, over
-// shared-memory chunks of 128 elements, then the 16 lanes of a pair reduce with offsets 8, 4, 2, 1.
-constexpr int kRtTile = 32, kRtChunk = 128, kRtStride = kRtChunk + 4;
+// logits[t][e] for a tile of 4A tokens x 4A experts per CTA, in qms_vec_dot_f32's exact order
+// (src/kernels.c:202-219): thread (k, g) runs lane k's FMA chain for A tokens x A experts over
+// shared-memory chunks of 1024/A elements (the next chunk is loaded into registers while this one
+// is used), then the 16 lanes of a pair reduce with offsets 8, 4, 2, 1. A = 8 for large T; smaller
+// tiles give small batches more CTAs.
+template <int A>
 __global__ void __launch_bounds__(256) k_router_tiled(const float *__restrict__ W, int X, int E,
                                                       const float *__restrict__ xn, int T, float *__restrict__ logits) {
-    __shared__ __align__(16) float xs[kRtTile * kRtStride], ws[kRtTile * kRtStride];
+    constexpr int R = 4 * A, C = 1024 / A, S = C + 4, NV = R * C / 4 / 256;   // rows, chunk, stride, float4 per thread
+    __shared__ __align__(16) float xs[R * S], ws[R * S];
     const int tid = threadIdx.x, k = tid & 15, g = tid >> 4, gt = g >> 2, ge = g & 3;
-    const int t0 = blockIdx.x * kRtTile, e0 = blockIdx.y * kRtTile;
+    const int t0 = blockIdx.x * R, e0 = blockIdx.y * R;
     pdl_wait();
-    float acc[8][8];
+    float acc[A][A];
 #pragma unroll
-    for (int a = 0; a < 8; a++)
+    for (int a = 0; a < A; a++)
 #pragma unroll
-        for (int b = 0; b < 8; b++) acc[a][b] = 0.0f;
-    for (int c0 = 0; c0 < E; c0 += kRtChunk) {
-        __syncthreads();
-        for (int i = tid; i < kRtTile * kRtChunk / 4; i += blockDim.x) {   // 32 rows x 32 float4
-            const int r = i / (kRtChunk / 4), c = (i % (kRtChunk / 4)) * 4;
+        for (int b = 0; b < A; b++) acc[a][b] = 0.0f;
+    float4 px[NV], pw[NV];
+    auto fetch = [&](int c0) {
+#pragma unroll
+        for (int v = 0; v < NV; v++) {
+            const int i = tid + 256 * v, r = i / (C / 4), c = (i % (C / 4)) * 4;
             const int t = t0 + r, e = e0 + r;
-            const float4 xv = t < T ? __ldg(reinterpret_cast<const float4 *>(xn + (size_t)t * E + c0 + c))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float4 wv = e < X ? __ldg(reinterpret_cast<const float4 *>(W + (size_t)e * E + c0 + c))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-            *reinterpret_cast<float4 *>(xs + r * kRtStride + c) = xv;
-            *reinterpret_cast<float4 *>(ws + r * kRtStride + c) = wv;
+            const bool in = c0 + c < E;
+            px[v] = in && t < T ? __ldg(reinterpret_cast<const float4 *>(xn + (size_t)t * E + c0 + c))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            pw[v] = in && e < X ? __ldg(reinterpret_cast<const float4 *>(W + (size_t)e * E + c0 + c))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    fetch(0);
+    for (int c0 = 0; c0 < E; c0 += C) {
+        __syncthreads();
+#pragma unroll
+        for (int v = 0; v < NV; v++) {
+            const int i = tid + 256 * v, r = i / (C / 4), c = (i % (C / 4)) * 4;
+            *reinterpret_cast<float4 *>(xs + r * S + c) = px[v];
+            *reinterpret_cast<float4 *>(ws + r * S + c) = pw[v];
         }
         __syncthreads();
+        if (c0 + C < E) fetch(c0 + C);
+        const int len = min(C, E - c0);
 #pragma unroll 2
-        for (int st = 0; st < kRtChunk / 16; st++) {
+        for (int st = 0; st < len / 16; st++) {
             const int c = 16 * st + k;
-            float xv[8], wv[8];
+            float xv[A], wv[A];
 #pragma unroll
-            for (int a = 0; a < 8; a++) xv[a] = xs[(gt * 8 + a) * kRtStride + c];
+            for (int a = 0; a < A; a++) xv[a] = xs[(gt * A + a) * S + c];
 #pragma unroll
-            for (int b = 0; b < 8; b++) wv[b] = ws[(ge * 8 + b) * kRtStride + c];
+            for (int b = 0; b < A; b++) wv[b] = ws[(ge * A + b) * S + c];
 #pragma unroll
-            for (int a = 0; a < 8; a++)
+            for (int a = 0; a < A; a++)
 #pragma unroll
-                for (int b = 0; b < 8; b++) acc[a][b] = __fmaf_rn(xv[a], wv[b], acc[a][b]);
+                for (int b = 0; b < A; b++) acc[a][b] = __fmaf_rn(xv[a], wv[b], acc[a][b]);
         }
     }
 #pragma unroll
-    for (int a = 0; a < 8; a++)
+    for (int a = 0; a < A; a++)
 #pragma unroll
-        for (int b = 0; b < 8; b++) {
+        for (int b = 0; b < A; b++) {
             float v = acc[a][b];
             v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 8, 16));
             v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4, 16));
             v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2, 16));
             v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1, 16));
-            const int t = t0 + gt * 8 + a, e = e0 + ge * 8 + b;
+            const int t = t0 + gt * A + a, e = e0 + ge * A + b;
             if (k == 0 && t < T && e < X) logits[(size_t)t * X + e] = v;
         }
 }
+
+// CTAs of the tiled router for tile side 4A
+static int64_t router_ctas(int T, int X, int A) { return (int64_t)((T + 4 * A - 1) / (4 * A)) * ((X + 4 * A - 1) / (4 * A)); }
 
 // Router stage for any T: the fused one-kernel router for T <= kTopkInRouterMaxT, else quantiser,
 // tiled logits and one top-k CTA per token.
@@ -222,8 +240,11 @@ static int launch_router(const float *router, int X, int E, const float *xn, int
     const unsigned qgrid = (unsigned)std::min<int64_t>((nblocks + 7) / 8, 4096);
     k_quantize_rows<<<qgrid, 256, 0, s>>>(xn, nblocks, xq_q, xq_d, xq_s);
     QMS_CK(cudaGetLastError());
-    QMS_CK(launch_pdl(k_router_tiled, dim3((T + kRtTile - 1) / kRtTile, (X + kRtTile - 1) / kRtTile), dim3(256), 0, s,
-                      router, X, E, xn, T, lg));
+    const int A = router_ctas(T, X, 8) >= 296 ? 8 : router_ctas(T, X, 4) >= 296 ? 4 : 2;
+    const dim3 rgrid((T + 4 * A - 1) / (4 * A), (X + 4 * A - 1) / (4 * A));
+    if (A == 8) QMS_CK(launch_pdl(k_router_tiled<8>, rgrid, dim3(256), 0, s, router, X, E, xn, T, lg));
+    else if (A == 4) QMS_CK(launch_pdl(k_router_tiled<4>, rgrid, dim3(256), 0, s, router, X, E, xn, T, lg));
+    else QMS_CK(launch_pdl(k_router_tiled<2>, rgrid, dim3(256), 0, s, router, X, E, xn, T, lg));
     QMS_CK(launch_pdl(k_moe_topk, dim3(T), dim3(256), 0, s, (const float *)lg, X, K, sel, wts));
     return QMS_CUDA_OK;
 }

@@ -254,6 +254,6 @@ struct MmaWork {
 // <= 24 slots per call (16-slot tiles)
 int gv_supported(const QmsCudaMoe *m);
 int gv_prepare(QmsCudaMoe *m);
-int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int rdiv, cudaStream_t s);
+int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int maxT, int rdiv, cudaStream_t s);
 
 }  // namespace qms

@@ -30,10 +30,13 @@ constexpr int kGvConsWarps = 8;
 constexpr int kGvCons = kGvConsWarps * 32;
 constexpr int kGvThreads = kGvCons + 32;     // + producer warp
 constexpr int kGvMaxRing = 16;
-constexpr size_t kGvSmemCap = 220 * 1024;
+constexpr size_t kGvSmemCap = 216 * 1024;     // dynamic; + ~2.6 KB static stays under 227 KB
 constexpr uint32_t kGvSpin = 1u << 22;
 constexpr int kGvMagic = 0x4B400000;         // float bits of 2^23 + 2^22: int v -> float exactly for |v| < 2^22
 constexpr float kGvMagicF = 12582912.0f;
+constexpr int kGvMaxTiles = 640;             // tiles of a GEMV call: S / 16 + nx with S <= 24 nx, nx <= 256
+constexpr int kGvItemCost0 = 2;              // cost of an item beyond its slots (the weight stream), in slots
+constexpr int kGvDnRows = 512;               // down rows per item (2 per consumer thread)
 
 enum { GV_ERR = 128 };
 
@@ -75,18 +78,18 @@ __device__ __forceinline__ bool gv_wait(uint64_t *bar, uint32_t parity, volatile
 
 __device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kGvCons) : "memory"); }
 
-// Integer dot of one 32-block from pre-split nibble words: w[0..3] low nibbles (elements 0-15),
-// w[4..7] high nibbles (16-31); two independent dp4a chains.
-__device__ __forceinline__ int gv_isum(const uint32_t (&w)[8], uint4 x0, uint4 x1) {
-    int a = __dp4a((int)w[0], (int)x0.x, 0);
-    int b = __dp4a((int)w[4], (int)x1.x, 0);
-    a = __dp4a((int)w[1], (int)x0.y, a);
-    b = __dp4a((int)w[5], (int)x1.y, b);
-    a = __dp4a((int)w[2], (int)x0.z, a);
-    b = __dp4a((int)w[6], (int)x1.z, b);
-    a = __dp4a((int)w[3], (int)x0.w, a);
-    b = __dp4a((int)w[7], (int)x1.w, b);
-    return a + b;
+// bias + integer dot of one 32-block from pre-split nibble words (w[0..3] low nibbles = elements
+// 0-15, w[4..7] high nibbles = 16-31) against the two 16-byte halves of a Q8 block; one dp4a chain.
+__device__ __forceinline__ int gv_dot(const uint32_t (&w)[8], uint4 x0, uint4 x1, int bias) {
+    int s = __dp4a((int)w[0], (int)x0.x, bias);
+    s = __dp4a((int)w[1], (int)x0.y, s);
+    s = __dp4a((int)w[2], (int)x0.z, s);
+    s = __dp4a((int)w[3], (int)x0.w, s);
+    s = __dp4a((int)w[4], (int)x1.x, s);
+    s = __dp4a((int)w[5], (int)x1.y, s);
+    s = __dp4a((int)w[6], (int)x1.z, s);
+    s = __dp4a((int)w[7], (int)x1.w, s);
+    return s;
 }
 
 __device__ __forceinline__ void gv_split(uint4 v, uint32_t (&w)[8]) {
@@ -101,10 +104,9 @@ __device__ __forceinline__ void gv_split(uint4 v, uint32_t (&w)[8]) {
     w[7] = (v.w >> 4) & m;
 }
 
-// This CTA's contiguous share of n items.
-__device__ __forceinline__ void gv_range(int n, int &lo, int &hi) {
-    lo = (int)((long long)n * blockIdx.x / gridDim.x);
-    hi = (int)((long long)n * (blockIdx.x + 1) / gridDim.x);
+// Two magic-encoded integer dots (kGvMagic + v) as the floats v, exactly (|v| < 2^22).
+__device__ __forceinline__ float2 gv_unmagic(int a, int b) {
+    return f2_add(make_float2(__int_as_float(a), __int_as_float(b)), make_float2(-kGvMagicF, -kGvMagicF));
 }
 
 struct GvTile {
@@ -121,22 +123,71 @@ __device__ __forceinline__ GvTile gv_tile(const MmaWork &w, int tl) {
     return g;
 }
 
+// All threads: this CTA's contiguous range [lo, hi) of the ntiles * ipt items, split by cost (an
+// item of a tile with n slots costs n + kGvItemCost0): the CTA owns the items whose starting cost
+// falls in its share. s_pre: kGvMaxTiles + 1 ints of shared memory.
+__device__ __forceinline__ void gv_split_items(const MmaWork &w, int ntiles, int ipt, int *s_pre, int *s_lh,
+                                               int &lo, int &hi) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    for (int t = tid; t < ntiles; t += nt) s_pre[t] = gv_tile(w, t).ns + kGvItemCost0;
+    if (tid < 2) s_lh[tid] = ntiles * ipt;
+    __syncthreads();
+    if (tid < 32) {                                       // exclusive prefix of the per-item costs
+        const int per = (ntiles + 31) / 32, t0 = tid * per, t1 = min(ntiles, t0 + per);
+        int sum = 0;
+        for (int t = t0; t < t1; t++) sum += s_pre[t];
+        int inc = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, inc, o);
+            if (tid >= o) inc += v;
+        }
+        int run = inc - sum;
+        for (int t = t0; t < t1; t++) {
+            const int c = s_pre[t];
+            s_pre[t] = run;
+            run += c;
+        }
+        if (tid == 31) s_pre[ntiles] = inc;
+    }
+    __syncthreads();
+    const long long P = gridDim.x, tot = (long long)ipt * s_pre[ntiles];
+    for (int t = tid; t < ntiles; t += nt) {
+        const long long c0 = (long long)ipt * s_pre[t], wt = s_pre[t + 1] - s_pre[t];
+        for (int k = 0; k < 2; k++) {                     // first item with start * P >= bound
+            const long long bound = (long long)(blockIdx.x + k) * tot;
+            const long long need = bound - c0 * P;
+            const long long j = need <= 0 ? 0 : (need + wt * P - 1) / (wt * P);
+            if (j < ipt) atomicMin(&s_lh[k], t * ipt + (int)j);
+        }
+    }
+    __syncthreads();
+    lo = s_lh[0];
+    hi = s_lh[1];
+}
+
 // Consumers: the tile's activation rows into shared memory, [slot][K half][block][16 bytes] (one
 // half of consecutive blocks is contiguous: conflict-free 16-byte reads), plus per (slot, block)
-// {scale bits, second word}: the block sum, or for Q4_1 down the product d * sum as float bits.
-template <bool DSUM>
+// {scale bits, second word}: the dp4a chain's starting value kGvMagic - 8 * sum for Q4_0 weights,
+// or for Q4_1 the product d * sum as float bits. An odd slot count is padded with a zero row
+// (its results are never stored), so slots go in pairs.
+template <bool Q1>
 __device__ __forceinline__ void gv_stage_x(const GvArgs &a, const GvTile &g, int8_t *sx, uint2 *sxs) {
-    const int nb = a.nb, K32 = nb * 32;
-    for (int idx = threadIdx.x; idx < g.ns * nb * 2; idx += kGvCons) {
+    const int nb = a.nb, K32 = nb * 32, nsp = (g.ns + 1) & ~1;
+    for (int idx = threadIdx.x; idx < nsp * nb * 2; idx += kGvCons) {
         const int j = idx / (2 * nb), rem = idx - j * 2 * nb, h = rem / nb, b = rem - h * nb;
-        const int row = __ldcg(a.wk.slots + g.off + j) / a.rdiv;
-        const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(a.xq + (size_t)row * K32 + b * 32 + h * 16));
-        *reinterpret_cast<uint4 *>(sx + ((size_t)(j * 2 + h) * nb + b) * 16) = v;
-        if (h == 0) {
-            const float d = __ldcg(a.xd + (size_t)row * nb + b);
-            const int s = __ldcg(a.xs + (size_t)row * nb + b);
-            sxs[j * nb + b] = make_uint2(__float_as_uint(d), DSUM ? __float_as_uint(d * (float)s) : (uint32_t)s);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        float d = 0.0f;
+        int sm = 0;
+        if (j < g.ns) {
+            const int row = __ldcg(a.wk.slots + g.off + j) / a.rdiv;
+            v = __ldcg(reinterpret_cast<const uint4 *>(a.xq + (size_t)row * K32 + b * 32 + h * 16));
+            d = __ldcg(a.xd + (size_t)row * nb + b);
+            sm = __ldcg(a.xs + (size_t)row * nb + b);
         }
+        *reinterpret_cast<uint4 *>(sx + ((size_t)(j * 2 + h) * nb + b) * 16) = v;
+        if (h == 0) sxs[j * nb + b] = make_uint2(__float_as_uint(d), Q1 ? __float_as_uint(d * (float)sm)
+                                                                        : (uint32_t)(kGvMagic - 8 * sm));
     }
 }
 
@@ -183,15 +234,14 @@ __device__ __forceinline__ void gv_produce(const GvArgs &a, int lo, int hi, int 
 }
 
 // ---- gate/up + SwiGLU + Q8 ---------------------------------------------------------------------------
-// Item (tile, ft): f values ft*32 .. +31 of the tile's expert; its nb/SB stages are the staged
-// chunks (8 chunks of 8 rows x SB blocks: chunks 0-3 gate rows, 4-7 up rows). Consumer thread t:
-// block b = t % SB of every stage, f values (t / SB) * FPT + i; FPT = SB / 8.
-template <int SB>
+// Item (tile, ft): f values ft*32 .. +31 of the tile's expert; its nb/16 stages are the staged chunks
+// (8 chunks of 8 rows x 16 blocks: chunks 0-3 gate rows, 4-7 up rows). Consumer thread t: block
+// b = t % 16 of every stage, f values 2 * (t / 16) + i, i < 2; gate and up of one f go as a pair.
 __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
-    constexpr int FPT = SB / 8;
+    constexpr int SB = 16, FPT = 2;
     constexpr uint32_t GB = 8u * SB * 18;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int s_abort;
+    __shared__ int s_abort, s_lh[2], s_pre[kGvMaxTiles + 1];
     const int nb = a.nb, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint8_t *ring = smem;
     int8_t *sx = reinterpret_cast<int8_t *>(smem + (size_t)a.ring * a.sst);
@@ -207,12 +257,11 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
         }
         fence_mbar_init();
     }
-    __syncthreads();
     pdl_wait();
     pdl_trigger();
     const int ipt = a.F / 32, nst = nb / SB;
     int lo, hi;
-    gv_range(__ldcg(a.wk.ntiles) * ipt, lo, hi);
+    gv_split_items(a.wk, min(__ldcg(a.wk.ntiles), kGvMaxTiles), ipt, s_pre, s_lh, lo, hi);
     if (warp == kGvConsWarps) {
         if (lane == 0)
             gv_produce(a, lo, hi, ipt, nst, ring, full, empty, &s_abort,
@@ -237,15 +286,15 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
             gv_stage_x<false>(a, g, sx, sxs);
             cons_sync();
         }
-        float ag[FPT][kGvSlots], au[FPT][kGvSlots];
+        float2 acc[FPT][kGvSlots];                         // (gate, up) of f value i, slot j
 #pragma unroll
         for (int i = 0; i < FPT; i++)
 #pragma unroll
-            for (int j = 0; j < kGvSlots; j++) ag[i][j] = au[i][j] = 0.0f;
+            for (int j = 0; j < kGvSlots; j++) acc[i][j] = make_float2(0.0f, 0.0f);
         for (int st = 0; st < nst; st++) {
             if (ok) ok = gv_wait(&full[r], par, &s_abort, a.err);
             uint32_t wg[FPT][8], wu[FPT][8];
-            float dg[FPT], du[FPT];
+            float2 dgu[FPT];
             if (ok) {
                 const uint8_t *stg = ring + (size_t)r * a.sst;
 #pragma unroll
@@ -255,8 +304,8 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
                     const uint32_t o = (uint32_t)((f & 7) * SB + b);
                     gv_split(*reinterpret_cast<const uint4 *>(cg + o * 16), wg[i]);
                     gv_split(*reinterpret_cast<const uint4 *>(cu + o * 16), wu[i]);
-                    dg[i] = h2f(*reinterpret_cast<const uint16_t *>(cg + 8 * SB * 16 + o * 2));
-                    du[i] = h2f(*reinterpret_cast<const uint16_t *>(cu + 8 * SB * 16 + o * 2));
+                    dgu[i] = make_float2(h2f(*reinterpret_cast<const uint16_t *>(cg + 8 * SB * 16 + o * 2)),
+                                         h2f(*reinterpret_cast<const uint16_t *>(cu + 8 * SB * 16 + o * 2)));
                 }
             }
             __syncwarp();
@@ -268,39 +317,40 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
             if (!ok) continue;
             const int gb = st * SB + b;
 #pragma unroll
-            for (int j = 0; j < kGvSlots; j++) {
-                if (j < g.ns) {
-                    const uint4 x0 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2) * nb + gb) * 16);
-                    const uint4 x1 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2 + 1) * nb + gb) * 16);
-                    const uint2 xv = sxs[j * nb + gb];
-                    const float xd = __uint_as_float(xv.x);
-                    const int bias = kGvMagic - 8 * (int)xv.y;       // Q4_0: d (q - 8), -8 via the block sum
+            for (int jp = 0; jp < kGvSlots; jp += 2) {
+                if (jp < g.ns) {
 #pragma unroll
-                    for (int i = 0; i < FPT; i++) {
-                        const float pg = __int_as_float(gv_isum(wg[i], x0, x1) + bias) - kGvMagicF;
-                        const float pu = __int_as_float(gv_isum(wu[i], x0, x1) + bias) - kGvMagicF;
-                        ag[i][j] = fmaf(pg, dg[i] * xd, ag[i][j]);
-                        au[i][j] = fmaf(pu, du[i] * xd, au[i][j]);
+                    for (int j = jp; j < jp + 2; j++) {
+                        const uint4 x0 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2) * nb + gb) * 16);
+                        const uint4 x1 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2 + 1) * nb + gb) * 16);
+                        const uint2 xv = sxs[j * nb + gb];
+                        const float xd = __uint_as_float(xv.x);
+                        const int bias = (int)xv.y;                 // kGvMagic - 8 * sum: Q4_0 is d (q - 8)
+#pragma unroll
+                        for (int i = 0; i < FPT; i++) {
+                            const float2 p = gv_unmagic(gv_dot(wg[i], x0, x1, bias), gv_dot(wu[i], x0, x1, bias));
+                            acc[i][j] = f2_fma(p, f2_mul(dgu[i], make_float2(xd, xd)), acc[i][j]);
+                        }
                     }
                 }
             }
         }
-        // sums over the SB threads of each f group (adjacent lanes), SwiGLU, Q8 groups per slot
+        // sums over the 16 threads of each f pair (adjacent lanes), SwiGLU, Q8 groups per slot
         float *sa = sact + buf * kGvSlots * 32;
 #pragma unroll
         for (int j = 0; j < kGvSlots; j++) {
             if (j < g.ns) {
 #pragma unroll
                 for (int i = 0; i < FPT; i++) {
+                    float gs = acc[i][j].x, us = acc[i][j].y;
 #pragma unroll
                     for (int o = SB / 2; o > 0; o >>= 1) {
-                        ag[i][j] += __shfl_xor_sync(0xffffffffu, ag[i][j], o);
-                        au[i][j] += __shfl_xor_sync(0xffffffffu, au[i][j], o);
+                        gs += __shfl_xor_sync(0xffffffffu, gs, o);
+                        us += __shfl_xor_sync(0xffffffffu, us, o);
                     }
                     if (b == 0) {
-                        const float gv = ag[i][j];
-                        const float s = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
-                        sa[j * 32 + fg * FPT + i] = __fmul_rn(s, au[i][j]);
+                        const float sg = __fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs)));
+                        sa[j * 32 + fg * FPT + i] = __fmul_rn(sg, us);
                     }
                 }
             }
@@ -322,15 +372,15 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
 }
 
 // ---- down ------------------------------------------------------------------------------------------
-// Item (tile, rb): down rows rb*DNR .. +DNR-1 of the tile's expert (DNR = 256 * RPT, within one
-// column stage row range); stage st = block column st: the rows' nibbles, scales (and Q4_1 mins)
-// sliced from column stage (st, rows). Consumer thread t: rows t + 256 i.
-template <bool Q1, int RPT>
+// Item (tile, rb): down rows rb*512 .. +511 of the tile's expert (within one column stage row
+// range); stage st = block column st: the rows' nibbles, scales (and Q4_1 mins) sliced from
+// column stage (st, rows). Consumer thread t: rows t and t + 256, as a pair.
+template <bool Q1>
 __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
-    constexpr int DNR = 256 * RPT;
+    constexpr int DNR = kGvDnRows;
     constexpr uint32_t NIB = DNR * 16, SCL = DNR * 2;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int s_abort;
+    __shared__ int s_abort, s_lh[2], s_pre[kGvMaxTiles + 1];
     const int nb = a.nb, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint8_t *ring = smem;
     int8_t *sx = reinterpret_cast<int8_t *>(smem + (size_t)a.ring * a.sst);
@@ -345,12 +395,11 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
         }
         fence_mbar_init();
     }
-    __syncthreads();
     pdl_wait();
     pdl_trigger();
     const int ipt = a.E / DNR, nst = nb;
     int lo, hi;
-    gv_range(__ldcg(a.wk.ntiles) * ipt, lo, hi);
+    gv_split_items(a.wk, min(__ldcg(a.wk.ntiles), kGvMaxTiles), ipt, s_pre, s_lh, lo, hi);
     if (warp == kGvConsWarps) {
         if (lane == 0)
             gv_produce(a, lo, hi, ipt, nst, ring, full, empty, &s_abort,
@@ -378,24 +427,22 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
             gv_stage_x<Q1>(a, g, sx, sxs);
             cons_sync();
         }
-        float acc[RPT][kGvSlots];
+        float2 acc[kGvSlots];                              // rows (t, t + 256) of slot j
 #pragma unroll
-        for (int i = 0; i < RPT; i++)
-#pragma unroll
-            for (int j = 0; j < kGvSlots; j++) acc[i][j] = 0.0f;
+        for (int j = 0; j < kGvSlots; j++) acc[j] = make_float2(0.0f, 0.0f);
         for (int st = 0; st < nst; st++) {
             if (ok) ok = gv_wait(&full[r], par, &s_abort, a.err);
-            uint32_t wn[RPT][8];
-            float dw[RPT], mw[RPT];
+            uint32_t w0[8], w1[8];
+            float2 dw = make_float2(0.0f, 0.0f), mw = make_float2(0.0f, 0.0f);
             if (ok) {
                 const uint8_t *stg = ring + (size_t)r * a.sst;
-#pragma unroll
-                for (int i = 0; i < RPT; i++) {
-                    const int row = tid + 256 * i;
-                    gv_split(*reinterpret_cast<const uint4 *>(stg + row * 16), wn[i]);
-                    dw[i] = h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + row * 2));
-                    mw[i] = Q1 ? h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + SCL + row * 2)) : 0.0f;
-                }
+                gv_split(*reinterpret_cast<const uint4 *>(stg + tid * 16), w0);
+                gv_split(*reinterpret_cast<const uint4 *>(stg + (tid + 256) * 16), w1);
+                dw = make_float2(h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + tid * 2)),
+                                 h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + (tid + 256) * 2)));
+                if (Q1)
+                    mw = make_float2(h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + SCL + tid * 2)),
+                                     h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + SCL + (tid + 256) * 2)));
             }
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(&empty[r]);
@@ -405,21 +452,23 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
             }
             if (!ok) continue;
 #pragma unroll
-            for (int j = 0; j < kGvSlots; j++) {
-                if (j < g.ns) {
-                    const uint4 x0 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2) * nb + st) * 16);
-                    const uint4 x1 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2 + 1) * nb + st) * 16);
-                    const uint2 xv = sxs[j * nb + st];
-                    const float xd = __uint_as_float(xv.x);
+            for (int jp = 0; jp < kGvSlots; jp += 2) {
+                if (jp < g.ns) {
 #pragma unroll
-                    for (int i = 0; i < RPT; i++) {
+                    for (int j = jp; j < jp + 2; j++) {
+                        const uint4 x0 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2) * nb + st) * 16);
+                        const uint4 x1 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2 + 1) * nb + st) * 16);
+                        const uint2 xv = sxs[j * nb + st];
+                        const float xd = __uint_as_float(xv.x);
                         if (Q1) {                          // d q + m: d dx isum + m (dx sum)  (src/kernels.c:109-121)
-                            const float p = __int_as_float(gv_isum(wn[i], x0, x1) + kGvMagic) - kGvMagicF;
-                            acc[i][j] = fmaf(p, dw[i] * xd, acc[i][j]);
-                            acc[i][j] = fmaf(mw[i], __uint_as_float(xv.y), acc[i][j]);
-                        } else {
-                            const float p = __int_as_float(gv_isum(wn[i], x0, x1) + (kGvMagic - 8 * (int)xv.y)) - kGvMagicF;
-                            acc[i][j] = fmaf(p, dw[i] * xd, acc[i][j]);
+                            const float2 p = gv_unmagic(gv_dot(w0, x0, x1, kGvMagic), gv_dot(w1, x0, x1, kGvMagic));
+                            acc[j] = f2_fma(p, f2_mul(dw, make_float2(xd, xd)), acc[j]);
+                            const float ds = __uint_as_float(xv.y);
+                            acc[j] = f2_fma(mw, make_float2(ds, ds), acc[j]);
+                        } else {                           // d (q - 8): the -8 sits in the chain's start
+                            const int bias = (int)xv.y;
+                            const float2 p = gv_unmagic(gv_dot(w0, x0, x1, bias), gv_dot(w1, x0, x1, bias));
+                            acc[j] = f2_fma(p, f2_mul(dw, make_float2(xd, xd)), acc[j]);
                         }
                     }
                 }
@@ -430,8 +479,8 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
             for (int j = 0; j < kGvSlots; j++) {
                 if (j < g.ns) {
                     float *o = a.dn + (size_t)__ldcg(a.wk.slots + g.off + j) * a.E + sub * DNR + tid;
-#pragma unroll
-                    for (int i = 0; i < RPT; i++) o[256 * i] = acc[i][j];
+                    o[0] = acc[j].x;
+                    o[256] = acc[j].y;
                 }
             }
         }
@@ -441,12 +490,9 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
 // ---- host side -------------------------------------------------------------------------------------
 static uint32_t al128(size_t n) { return (uint32_t)((n + 127) & ~(size_t)127); }
 
-static int gv_dn_rpt(const QmsCudaMoe *m) { return m->dcol.RD % 512 == 0 ? 2 : 1; }
-
 static uint32_t gv_stage_bytes(const QmsCudaMoe *m, bool gu) {
     if (gu) return al128(8 * (size_t)m->cgu.GB);
-    const size_t dnr = 256 * (size_t)gv_dn_rpt(m);
-    return al128(dnr * 16 + dnr * 2 * (m->dcol.q1 ? 2 : 1));
+    return al128((size_t)kGvDnRows * 16 + (size_t)kGvDnRows * 2 * (m->dcol.q1 ? 2 : 1));
 }
 
 static size_t gv_fixed(const QmsCudaMoe *m, bool gu) {
@@ -465,27 +511,24 @@ static size_t gv_smem(const QmsCudaMoe *m, bool gu) {
     return (size_t)ring * gv_stage_bytes(m, gu) + gv_fixed(m, gu) + (size_t)ring * 16;
 }
 
-// Shapes the grouped GEMV covers: staged gate/up chunks of 16 or 8 blocks, down column stages of
-// >= 256 rows, both rings at least 2 stages deep.
+// Shapes the grouped GEMV covers: staged gate/up chunks of 16 blocks (n_embd % 512 == 0), down
+// column stages of >= 512 rows, F a multiple of 32, both rings at least 2 stages deep.
 int gv_supported(const QmsCudaMoe *m) {
-    return (m->cgu.SB == 16 || m->cgu.SB == 8) && m->F % 32 == 0 && m->dcol.RD % 256 == 0 && m->E % 256 == 0 &&
+    return m->cgu.SB == 16 && m->F % 32 == 0 && m->dcol.RD % kGvDnRows == 0 && m->E % kGvDnRows == 0 &&
            m->X <= 256 && gv_ring(m, true) >= 2 && gv_ring(m, false) >= 2;
 }
 
 int gv_prepare(QmsCudaMoe *m) {
-    const void *gk = m->cgu.SB == 16 ? (const void *)k_gv_gate_up<16> : (const void *)k_gv_gate_up<8>;
-    QMS_CK(cudaFuncSetAttribute(gk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gv_smem(m, true)));
-    const bool q1 = m->dcol.q1;
-    const int rpt = gv_dn_rpt(m);
-    const void *dk = q1 ? (rpt == 2 ? (const void *)k_gv_down<true, 2> : (const void *)k_gv_down<true, 1>)
-                        : (rpt == 2 ? (const void *)k_gv_down<false, 2> : (const void *)k_gv_down<false, 1>);
+    QMS_CK(cudaFuncSetAttribute(k_gv_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gv_smem(m, true)));
+    const void *dk = m->dcol.q1 ? (const void *)k_gv_down<true> : (const void *)k_gv_down<false>;
     QMS_CK(cudaFuncSetAttribute(dk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gv_smem(m, false)));
     return QMS_CUDA_OK;
 }
 
 // gate/up + SwiGLU + Q8 into m's aq scratch, then down rows into w.dn, for the slots grouped in w
-// (tiles of kGvSlots); activation row of slot s: s / rdiv of m's xq scratch.
-int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int rdiv, cudaStream_t s) {
+// (at most maxT tiles of kGvSlots); activation row of slot s: s / rdiv of m's xq scratch.
+int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int maxT, int rdiv, cudaStream_t s) {
+    QMS_REQUIRE(maxT <= kGvMaxTiles, QMS_CUDA_EINVAL, "moe: %d tiles exceed the grouped GEMV's %d", maxT, kGvMaxTiles);
     GvArgs g;
     memset(&g, 0, sizeof g);
     g.w = m->gu;
@@ -507,10 +550,7 @@ int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int rdiv, cudaStream_t s) {
     g.aq_s = m->aq_s;
     g.err = m->err;
     const dim3 grid(m->nsm), block(kGvThreads);
-    if (m->cgu.SB == 16)
-        QMS_CK(launch_pdl(k_gv_gate_up<16>, grid, block, gv_smem(m, true), s, g));
-    else
-        QMS_CK(launch_pdl(k_gv_gate_up<8>, grid, block, gv_smem(m, true), s, g));
+    QMS_CK(launch_pdl(k_gv_gate_up, grid, block, gv_smem(m, true), s, g));
     if (m->timing) {
         QMS_CK(cudaEventRecord(m->ev[3], s));
         QMS_CK(cudaEventRecord(m->ev[4], s));
@@ -526,14 +566,8 @@ int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int rdiv, cudaStream_t s) {
     d.ring = gv_ring(m, false);
     d.sst = gv_stage_bytes(m, false);
     d.dn = w.dn;
-    const size_t sm = gv_smem(m, false);
-    if (m->dcol.q1) {
-        if (gv_dn_rpt(m) == 2) QMS_CK(launch_pdl(k_gv_down<true, 2>, grid, block, sm, s, d));
-        else QMS_CK(launch_pdl(k_gv_down<true, 1>, grid, block, sm, s, d));
-    } else {
-        if (gv_dn_rpt(m) == 2) QMS_CK(launch_pdl(k_gv_down<false, 2>, grid, block, sm, s, d));
-        else QMS_CK(launch_pdl(k_gv_down<false, 1>, grid, block, sm, s, d));
-    }
+    if (m->dcol.q1) QMS_CK(launch_pdl(k_gv_down<true>, grid, block, gv_smem(m, false), s, d));
+    else QMS_CK(launch_pdl(k_gv_down<false>, grid, block, gv_smem(m, false), s, d));
     return QMS_CUDA_OK;
 }
 

@@ -85,29 +85,6 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// Packed pairs of fp32 (sm_100 f32x2 instructions): two lanes of work per instruction.
-__device__ __forceinline__ unsigned long long f2_bits(float2 v) {
-    return ((unsigned long long)__float_as_uint(v.y) << 32) | __float_as_uint(v.x);
-}
-__device__ __forceinline__ float2 f2_from(unsigned long long b) {
-    return make_float2(__uint_as_float((uint32_t)b), __uint_as_float((uint32_t)(b >> 32)));
-}
-__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
-    unsigned long long d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
-    return f2_from(d);
-}
-__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
-    unsigned long long d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-    return f2_from(d);
-}
-__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
-    unsigned long long d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-    return f2_from(d);
-}
-
 // 32 TMEM lanes (this warp's quarter) x C consecutive 32-bit columns, C = 8 or 32 (not waited).
 template <int C>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[C]) {
@@ -672,7 +649,7 @@ static int mma_core(QmsCudaMoe *m, int S, const int *sel, int nx, int rdiv, floa
     if (dn) w.dn = dn;
     const int nw = mma_width(S, nx), maxT = S / nw + nx;
     QMS_CK(launch_pdl(k_mma_group, dim3(1), dim3(1024), 0, s, sel, S, nx, maxT, nw, w));
-    if (m->gemv && nw == kMmaNs) return gv_gemms(m, w, rdiv, s);   // few slots per expert: CUDA cores
+    if (m->gemv && nw == kMmaNs) return gv_gemms(m, w, maxT, rdiv, s);   // few slots per expert: CUDA cores
     QMS_CK(launch_pdl(k_mma_gather, dim3(maxT, 8), dim3(2 * nw), 0, s, (const int8_t *)m->xq_q, (const float *)m->xq_d,
                       (const int *)nullptr, m->nbE, rdiv, nw, w));
     MmaArgs g;

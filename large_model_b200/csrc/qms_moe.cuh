@@ -248,12 +248,14 @@ struct MmaWork {
     float *bs;         // [tiles][nb][64] activation scales
     int *bsum;         // [tiles][nb][64] activation block sums (Q4_1 down)
     float *dn;         // [T*K][E] down rows per slot
+    float *dn2;        // [min(T*K, 24 X)][E] second K half of the grouped GEMV's down rows
 };
 
 // batched expert-grouped GEMV kernels (qms_moe_gemv.cu), the grouped path when experts average
 // <= 24 slots per call (16-slot tiles)
 int gv_supported(const QmsCudaMoe *m);
 int gv_prepare(QmsCudaMoe *m);
-int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int maxT, int rdiv, cudaStream_t s);
+int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int maxT, int S, int rdiv, float *dn, float *dn2, bool sum_halves,
+             cudaStream_t s);
 
 }  // namespace qms

@@ -5,16 +5,18 @@
 // while the per-block scale work dominates. Here each expert's weights stream from HBM once per
 // call and serve all of its slots. After the slots are grouped by expert (k_mma_group, tiles of
 // up to 16 slots of one expert, the reference's grouping of src/model.c:1066-1088):
-//   k_gv_gate_up  persistent, one CTA per SM, owning a contiguous range of (tile, 32-f) items. A
-//                 producer warp streams each item's gate/up stages (one bulk copy each, the staged
-//                 chunk layout) through a ring in shared memory; 8 consumer warps hold the tile's
-//                 Q8 activation rows in shared memory and form every (row, slot) dot with dp4a,
-//                 each 32-block's int32 sum scaled in fp32 (src/kernels.c:82-107); then SwiGLU and
-//                 the Q8 group of each slot's 32 f values (src/model.c:989-997).
-//   k_gv_down     the same over (tile, 256/512 down rows) items: per F/32 block column the rows'
-//                 column stage slice, against the slots' Q8 activation groups; writes each slot's
-//                 unweighted down row (src/model.c:999-1004), summed by k_mma_combine in selection
-//                 order. Q4_0 and Q4_1 down.
+//   k_gv_gate_up  persistent, one CTA per SM, owning a contiguous, cost-balanced range of
+//                 (tile, 32-f) items. A producer warp streams each item's gate/up stages (one
+//                 bulk copy each, the staged chunk layout) through a ring in shared memory; 16
+//                 consumer warps hold the tile's Q8 activation rows in shared memory and form
+//                 every (row, slot) dot with dp4a, each 32-block's int32 sum scaled in fp32
+//                 (src/kernels.c:82-107); then SwiGLU and the Q8 group of each slot's 32 f values
+//                 (src/model.c:989-997).
+//   k_gv_down     the same over (tile, column-stage rows, K half) items: whole column stages
+//                 (one bulk copy each) of one half of the F/32 block columns, against the slots'
+//                 Q8 activation groups; writes each slot's unweighted partial down row per half
+//                 (src/model.c:999-1004); the combine adds the halves and sums the slots in
+//                 selection order. Q4_0 and Q4_1 down.
 // A 32-block's integer dot is exact; only the fp32 summation order differs from the reference.
 #include <string.h>
 
@@ -26,7 +28,7 @@
 namespace qms {
 
 constexpr int kGvSlots = 16;                 // slots per tile (k_mma_group width)
-constexpr int kGvConsWarps = 8;
+constexpr int kGvConsWarps = 16;
 constexpr int kGvCons = kGvConsWarps * 32;
 constexpr int kGvThreads = kGvCons + 32;     // + producer warp
 constexpr int kGvMaxRing = 16;
@@ -36,7 +38,7 @@ constexpr int kGvMagic = 0x4B400000;         // float bits of 2^23 + 2^22: int v
 constexpr float kGvMagicF = 12582912.0f;
 constexpr int kGvMaxTiles = 640;             // tiles of a GEMV call: S / 16 + nx with S <= 24 nx, nx <= 256
 constexpr int kGvItemCost0 = 2;              // cost of an item beyond its slots (the weight stream), in slots
-constexpr int kGvDnRows = 512;               // down rows per item (2 per consumer thread)
+constexpr int kGvKParts = 2;                 // down items split the F/32 block columns in halves
 
 enum { GV_ERR = 128 };
 
@@ -57,7 +59,8 @@ struct GvArgs {
     int8_t *aq_q;              // gate/up out: [S][F] Q8 values
     float *aq_d;               // [S][F/32]
     int *aq_s;                 // [S][F/32]
-    float *dn;                 // down out: [S][E]
+    float *dn;                 // down out: [S][E] partial rows of the first K half
+    float *dn2;                //           [S][E] of the second half
     int *err;
 };
 
@@ -236,9 +239,9 @@ __device__ __forceinline__ void gv_produce(const GvArgs &a, int lo, int hi, int 
 // ---- gate/up + SwiGLU + Q8 ---------------------------------------------------------------------------
 // Item (tile, ft): f values ft*32 .. +31 of the tile's expert; its nb/16 stages are the staged chunks
 // (8 chunks of 8 rows x 16 blocks: chunks 0-3 gate rows, 4-7 up rows). Consumer thread t: block
-// b = t % 16 of every stage, f values 2 * (t / 16) + i, i < 2; gate and up of one f go as a pair.
+// b = t % 16 of every stage and f value t / 16; its gate and up rows go as a pair.
 __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
-    constexpr int SB = 16, FPT = 2;
+    constexpr int SB = 16;
     constexpr uint32_t GB = 8u * SB * 18;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_abort, s_lh[2], s_pre[kGvMaxTiles + 1];
@@ -271,7 +274,9 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
                        });
         return;
     }
-    const int b = tid % SB, fg = tid / SB;
+    const int b = tid % SB, f = tid / SB;
+    const uint32_t o = (uint32_t)((f & 7) * SB + b);
+    const uint32_t cgo = (uint32_t)(f >> 3) * GB;
     int r = 0;
     uint32_t par = 0;
     bool ok = true;
@@ -286,27 +291,19 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
             gv_stage_x<false>(a, g, sx, sxs);
             cons_sync();
         }
-        float2 acc[FPT][kGvSlots];                         // (gate, up) of f value i, slot j
+        float2 acc[kGvSlots];                              // (gate, up) of slot j
 #pragma unroll
-        for (int i = 0; i < FPT; i++)
-#pragma unroll
-            for (int j = 0; j < kGvSlots; j++) acc[i][j] = make_float2(0.0f, 0.0f);
+        for (int j = 0; j < kGvSlots; j++) acc[j] = make_float2(0.0f, 0.0f);
         for (int st = 0; st < nst; st++) {
             if (ok) ok = gv_wait(&full[r], par, &s_abort, a.err);
-            uint32_t wg[FPT][8], wu[FPT][8];
-            float2 dgu[FPT];
+            uint32_t wg[8], wu[8];
+            float2 dgu = make_float2(0.0f, 0.0f);
             if (ok) {
-                const uint8_t *stg = ring + (size_t)r * a.sst;
-#pragma unroll
-                for (int i = 0; i < FPT; i++) {
-                    const int f = fg * FPT + i;
-                    const uint8_t *cg = stg + (f >> 3) * GB, *cu = cg + 4 * GB;
-                    const uint32_t o = (uint32_t)((f & 7) * SB + b);
-                    gv_split(*reinterpret_cast<const uint4 *>(cg + o * 16), wg[i]);
-                    gv_split(*reinterpret_cast<const uint4 *>(cu + o * 16), wu[i]);
-                    dgu[i] = make_float2(h2f(*reinterpret_cast<const uint16_t *>(cg + 8 * SB * 16 + o * 2)),
-                                         h2f(*reinterpret_cast<const uint16_t *>(cu + 8 * SB * 16 + o * 2)));
-                }
+                const uint8_t *cg = ring + (size_t)r * a.sst + cgo, *cu = cg + 4 * GB;
+                gv_split(*reinterpret_cast<const uint4 *>(cg + o * 16), wg);
+                gv_split(*reinterpret_cast<const uint4 *>(cu + o * 16), wu);
+                dgu = make_float2(h2f(*reinterpret_cast<const uint16_t *>(cg + 8 * SB * 16 + o * 2)),
+                                  h2f(*reinterpret_cast<const uint16_t *>(cu + 8 * SB * 16 + o * 2)));
             }
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(&empty[r]);  // weights are in registers: free the stage
@@ -326,32 +323,26 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
                         const uint2 xv = sxs[j * nb + gb];
                         const float xd = __uint_as_float(xv.x);
                         const int bias = (int)xv.y;                 // kGvMagic - 8 * sum: Q4_0 is d (q - 8)
-#pragma unroll
-                        for (int i = 0; i < FPT; i++) {
-                            const float2 p = gv_unmagic(gv_dot(wg[i], x0, x1, bias), gv_dot(wu[i], x0, x1, bias));
-                            acc[i][j] = f2_fma(p, f2_mul(dgu[i], make_float2(xd, xd)), acc[i][j]);
-                        }
+                        const float2 p = gv_unmagic(gv_dot(wg, x0, x1, bias), gv_dot(wu, x0, x1, bias));
+                        acc[j] = f2_fma(p, f2_mul(dgu, make_float2(xd, xd)), acc[j]);
                     }
                 }
             }
         }
-        // sums over the 16 threads of each f pair (adjacent lanes), SwiGLU, Q8 groups per slot
+        // sums over the 16 threads of each f (adjacent lanes), SwiGLU, Q8 groups per slot
         float *sa = sact + buf * kGvSlots * 32;
 #pragma unroll
         for (int j = 0; j < kGvSlots; j++) {
             if (j < g.ns) {
+                float gs = acc[j].x, us = acc[j].y;
 #pragma unroll
-                for (int i = 0; i < FPT; i++) {
-                    float gs = acc[i][j].x, us = acc[i][j].y;
-#pragma unroll
-                    for (int o = SB / 2; o > 0; o >>= 1) {
-                        gs += __shfl_xor_sync(0xffffffffu, gs, o);
-                        us += __shfl_xor_sync(0xffffffffu, us, o);
-                    }
-                    if (b == 0) {
-                        const float sg = __fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs)));
-                        sa[j * 32 + fg * FPT + i] = __fmul_rn(sg, us);
-                    }
+                for (int m = SB / 2; m > 0; m >>= 1) {
+                    gs += __shfl_xor_sync(0xffffffffu, gs, m);
+                    us += __shfl_xor_sync(0xffffffffu, us, m);
+                }
+                if (b == 0) {
+                    const float sg = __fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs)));
+                    sa[j * 32 + f] = __fmul_rn(sg, us);
                 }
             }
         }
@@ -372,13 +363,13 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
 }
 
 // ---- down ------------------------------------------------------------------------------------------
-// Item (tile, rb): down rows rb*512 .. +511 of the tile's expert (within one column stage row
-// range); stage st = block column st: the rows' nibbles, scales (and Q4_1 mins) sliced from
-// column stage (st, rows). Consumer thread t: rows t and t + 256, as a pair.
-template <bool Q1>
+// Item (tile, q, kh): down rows q*RD .. +RD-1 of the tile's expert (column stage row range q) over
+// block columns kh*nb/2 .. +nb/2-1; stage st = the whole column stage (kh*nb/2 + st, q). Consumer
+// thread t: rows t + 512 i, i < RPT = RD / 512 (two rows go as a pair).
+template <bool Q1, int RPT>
 __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
-    constexpr int DNR = kGvDnRows;
-    constexpr uint32_t NIB = DNR * 16, SCL = DNR * 2;
+    constexpr int RD = 512 * RPT;
+    constexpr uint32_t NIB = RD * 16, SCL = RD * 2, STD = NIB + SCL * (Q1 ? 2 : 1);
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_abort, s_lh[2], s_pre[kGvMaxTiles + 1];
     const int nb = a.nb, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -397,19 +388,16 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
     }
     pdl_wait();
     pdl_trigger();
-    const int ipt = a.E / DNR, nst = nb;
+    const int Rq = a.dc.Rq, ipt = Rq * kGvKParts, nst = nb / kGvKParts;
     int lo, hi;
     gv_split_items(a.wk, min(__ldcg(a.wk.ntiles), kGvMaxTiles), ipt, s_pre, s_lh, lo, hi);
     if (warp == kGvConsWarps) {
         if (lane == 0)
             gv_produce(a, lo, hi, ipt, nst, ring, full, empty, &s_abort,
                        [&](const uint8_t *base, int sub, int st, uint8_t *dst, uint64_t *bar, uint64_t pol) {
-                           const int row0 = sub * DNR;
-                           const uint8_t *stg = base + dn_stage_off(a.dc, st, row0);
-                           mbar_arrive_expect_tx(bar, NIB + SCL * (Q1 ? 2 : 1));
-                           bulk_load(dst, stg + dn_nib_off(a.dc, row0), NIB, bar, pol);
-                           bulk_load(dst + NIB, stg + dn_scale_off(a.dc, row0), SCL, bar, pol);
-                           if (Q1) bulk_load(dst + NIB + SCL, stg + dn_min_off(a.dc, row0), SCL, bar, pol);
+                           const int kh = sub / Rq, q = sub - kh * Rq, bc = kh * nst + st;
+                           mbar_arrive_expect_tx(bar, STD);
+                           bulk_load(dst, base + (size_t)(bc * Rq + q) * STD, STD, bar, pol);
                        });
         return;
     }
@@ -419,7 +407,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
     int cur = -1;
     GvTile g{0, 0, 0};
     for (int item = lo; item < hi; item++) {
-        const int tl = item / ipt, sub = item - tl * ipt;
+        const int tl = item / ipt, sub = item - tl * ipt, kh = sub / Rq, q = sub - kh * Rq;
         if (tl != cur) {
             cons_sync();
             cur = tl;
@@ -427,7 +415,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
             gv_stage_x<Q1>(a, g, sx, sxs);
             cons_sync();
         }
-        float2 acc[kGvSlots];                              // rows (t, t + 256) of slot j
+        float2 acc[kGvSlots];                              // RPT 2: rows (t, t + 512); 1: .x only
 #pragma unroll
         for (int j = 0; j < kGvSlots; j++) acc[j] = make_float2(0.0f, 0.0f);
         for (int st = 0; st < nst; st++) {
@@ -436,13 +424,14 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
             float2 dw = make_float2(0.0f, 0.0f), mw = make_float2(0.0f, 0.0f);
             if (ok) {
                 const uint8_t *stg = ring + (size_t)r * a.sst;
+                const int r1 = RPT == 2 ? tid + 512 : tid;
                 gv_split(*reinterpret_cast<const uint4 *>(stg + tid * 16), w0);
-                gv_split(*reinterpret_cast<const uint4 *>(stg + (tid + 256) * 16), w1);
+                gv_split(*reinterpret_cast<const uint4 *>(stg + r1 * 16), w1);
                 dw = make_float2(h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + tid * 2)),
-                                 h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + (tid + 256) * 2)));
+                                 h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + r1 * 2)));
                 if (Q1)
                     mw = make_float2(h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + SCL + tid * 2)),
-                                     h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + SCL + (tid + 256) * 2)));
+                                     h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + SCL + r1 * 2)));
             }
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(&empty[r]);
@@ -451,23 +440,26 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
                 par ^= 1;
             }
             if (!ok) continue;
+            const int bc = kh * nst + st;
 #pragma unroll
             for (int jp = 0; jp < kGvSlots; jp += 2) {
                 if (jp < g.ns) {
 #pragma unroll
                     for (int j = jp; j < jp + 2; j++) {
-                        const uint4 x0 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2) * nb + st) * 16);
-                        const uint4 x1 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2 + 1) * nb + st) * 16);
-                        const uint2 xv = sxs[j * nb + st];
+                        const uint4 x0 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2) * nb + bc) * 16);
+                        const uint4 x1 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2 + 1) * nb + bc) * 16);
+                        const uint2 xv = sxs[j * nb + bc];
                         const float xd = __uint_as_float(xv.x);
                         if (Q1) {                          // d q + m: d dx isum + m (dx sum)  (src/kernels.c:109-121)
-                            const float2 p = gv_unmagic(gv_dot(w0, x0, x1, kGvMagic), gv_dot(w1, x0, x1, kGvMagic));
+                            const float2 p = gv_unmagic(gv_dot(w0, x0, x1, kGvMagic),
+                                                        RPT == 2 ? gv_dot(w1, x0, x1, kGvMagic) : kGvMagic);
                             acc[j] = f2_fma(p, f2_mul(dw, make_float2(xd, xd)), acc[j]);
                             const float ds = __uint_as_float(xv.y);
                             acc[j] = f2_fma(mw, make_float2(ds, ds), acc[j]);
                         } else {                           // d (q - 8): the -8 sits in the chain's start
                             const int bias = (int)xv.y;
-                            const float2 p = gv_unmagic(gv_dot(w0, x0, x1, bias), gv_dot(w1, x0, x1, bias));
+                            const float2 p = gv_unmagic(gv_dot(w0, x0, x1, bias),
+                                                        RPT == 2 ? gv_dot(w1, x0, x1, bias) : kGvMagic);
                             acc[j] = f2_fma(p, f2_mul(dw, make_float2(xd, xd)), acc[j]);
                         }
                     }
@@ -475,24 +467,31 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
             }
         }
         if (ok) {
+            float *dst = kh ? a.dn2 : a.dn;
 #pragma unroll
             for (int j = 0; j < kGvSlots; j++) {
                 if (j < g.ns) {
-                    float *o = a.dn + (size_t)__ldcg(a.wk.slots + g.off + j) * a.E + sub * DNR + tid;
+                    float *o = dst + (size_t)__ldcg(a.wk.slots + g.off + j) * a.E + q * RD + tid;
                     o[0] = acc[j].x;
-                    o[256] = acc[j].y;
+                    if (RPT == 2) o[512] = acc[j].y;
                 }
             }
         }
     }
 }
 
+// dn[i] += dn2[i]: the two K halves of the down rows into one (expert-parallel entry point)
+__global__ void __launch_bounds__(256) k_gv_add(float *__restrict__ dn, const float *__restrict__ dn2, int64_t n) {
+    pdl_wait();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dn[i] = __fadd_rn(dn[i], __ldcg(dn2 + i));
+}
+
 // ---- host side -------------------------------------------------------------------------------------
 static uint32_t al128(size_t n) { return (uint32_t)((n + 127) & ~(size_t)127); }
 
 static uint32_t gv_stage_bytes(const QmsCudaMoe *m, bool gu) {
-    if (gu) return al128(8 * (size_t)m->cgu.GB);
-    return al128((size_t)kGvDnRows * 16 + (size_t)kGvDnRows * 2 * (m->dcol.q1 ? 2 : 1));
+    return al128(gu ? 8 * (size_t)m->cgu.GB : (size_t)m->dcol.STD);
 }
 
 static size_t gv_fixed(const QmsCudaMoe *m, bool gu) {
@@ -512,22 +511,30 @@ static size_t gv_smem(const QmsCudaMoe *m, bool gu) {
 }
 
 // Shapes the grouped GEMV covers: staged gate/up chunks of 16 blocks (n_embd % 512 == 0), down
-// column stages of >= 512 rows, F a multiple of 32, both rings at least 2 stages deep.
+// column stages of 512 or 1024 rows, F a multiple of 64 (two K halves of whole blocks), both rings
+// at least 2 stages deep.
 int gv_supported(const QmsCudaMoe *m) {
-    return m->cgu.SB == 16 && m->F % 32 == 0 && m->dcol.RD % kGvDnRows == 0 && m->E % kGvDnRows == 0 &&
-           m->X <= 256 && gv_ring(m, true) >= 2 && gv_ring(m, false) >= 2;
+    return m->cgu.SB == 16 && m->F % 64 == 0 && (m->dcol.RD == 512 || m->dcol.RD == 1024) && m->X <= 256 &&
+           gv_ring(m, true) >= 2 && gv_ring(m, false) >= 2;
+}
+
+static const void *gv_down_kernel(const QmsCudaMoe *m) {
+    const bool q1 = m->dcol.q1, r2 = m->dcol.RD == 1024;
+    return q1 ? (r2 ? (const void *)k_gv_down<true, 2> : (const void *)k_gv_down<true, 1>)
+              : (r2 ? (const void *)k_gv_down<false, 2> : (const void *)k_gv_down<false, 1>);
 }
 
 int gv_prepare(QmsCudaMoe *m) {
     QMS_CK(cudaFuncSetAttribute(k_gv_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gv_smem(m, true)));
-    const void *dk = m->dcol.q1 ? (const void *)k_gv_down<true> : (const void *)k_gv_down<false>;
-    QMS_CK(cudaFuncSetAttribute(dk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gv_smem(m, false)));
+    QMS_CK(cudaFuncSetAttribute(gv_down_kernel(m), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gv_smem(m, false)));
     return QMS_CUDA_OK;
 }
 
-// gate/up + SwiGLU + Q8 into m's aq scratch, then down rows into w.dn, for the slots grouped in w
-// (at most maxT tiles of kGvSlots); activation row of slot s: s / rdiv of m's xq scratch.
-int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int maxT, int rdiv, cudaStream_t s) {
+// gate/up + SwiGLU + Q8 into m's aq scratch, then the two K halves of the down rows into dn and
+// dn2, for the slots grouped in w (at most maxT tiles of kGvSlots); activation row of slot s: s / rdiv
+// of m's xq scratch. With sum_halves the second half is added into dn (S slots).
+int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int maxT, int S, int rdiv, float *dn, float *dn2, bool sum_halves,
+             cudaStream_t s) {
     QMS_REQUIRE(maxT <= kGvMaxTiles, QMS_CUDA_EINVAL, "moe: %d tiles exceed the grouped GEMV's %d", maxT, kGvMaxTiles);
     GvArgs g;
     memset(&g, 0, sizeof g);
@@ -565,9 +572,21 @@ int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int maxT, int rdiv, cudaStream_t s
     d.rdiv = 1;
     d.ring = gv_ring(m, false);
     d.sst = gv_stage_bytes(m, false);
-    d.dn = w.dn;
-    if (m->dcol.q1) QMS_CK(launch_pdl(k_gv_down<true>, grid, block, gv_smem(m, false), s, d));
-    else QMS_CK(launch_pdl(k_gv_down<false>, grid, block, gv_smem(m, false), s, d));
+    d.dn = dn;
+    d.dn2 = dn2;
+    const size_t sm = gv_smem(m, false);
+    if (m->dcol.q1) {
+        if (m->dcol.RD == 1024) QMS_CK(launch_pdl(k_gv_down<true, 2>, grid, block, sm, s, d));
+        else QMS_CK(launch_pdl(k_gv_down<true, 1>, grid, block, sm, s, d));
+    } else {
+        if (m->dcol.RD == 1024) QMS_CK(launch_pdl(k_gv_down<false, 2>, grid, block, sm, s, d));
+        else QMS_CK(launch_pdl(k_gv_down<false, 1>, grid, block, sm, s, d));
+    }
+    if (sum_halves) {
+        const int64_t n = (int64_t)S * m->E;
+        QMS_CK(launch_pdl(k_gv_add, dim3((unsigned)std::min<int64_t>((n + 1023) / 1024, 4 * m->nsm)), dim3(256), 0, s,
+                          dn, (const float *)dn2, n));
+    }
     return QMS_CUDA_OK;
 }
 

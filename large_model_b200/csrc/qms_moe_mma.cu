@@ -529,13 +529,19 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
 }
 
 // out[t][i] = sum_j w[t][j] * dn[t*K + j][i] in selection order (src/model.c:1152-1162), + resid.
-__global__ void __launch_bounds__(256) k_mma_combine(const float *__restrict__ dn, const float *__restrict__ wts, int K,
-                                                     int E, const float *resid, float *out) {
+// dn2 (optional): second K half of each down row, added to the first before weighting.
+__global__ void __launch_bounds__(256) k_mma_combine(const float *__restrict__ dn, const float *__restrict__ dn2,
+                                                     const float *__restrict__ wts, int K, int E, const float *resid,
+                                                     float *out) {
     const int t = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
     pdl_wait();
     if (i >= E) return;
     float o = 0.0f;
-    for (int j = 0; j < K; j++) o = __fmaf_rn(__ldcg(wts + t * K + j), __ldcg(dn + ((size_t)t * K + j) * E + i), o);
+    for (int j = 0; j < K; j++) {
+        const size_t at = ((size_t)t * K + j) * E + i;
+        const float d = dn2 ? __fadd_rn(__ldcg(dn + at), __ldcg(dn2 + at)) : __ldcg(dn + at);
+        o = __fmaf_rn(__ldcg(wts + t * K + j), d, o);
+    }
     if (resid) o = __fadd_rn(resid[(size_t)t * E + i], o);
     out[(size_t)t * E + i] = o;
 }
@@ -575,6 +581,7 @@ static int mma_layout(const QmsCudaMoe *m, int T, MmaWork *w, size_t *bytes, cha
     w->bs = (float *)take(bcols * nbmax * 4);
     w->bsum = (int *)take(bcols * nbmax * 4);
     w->dn = (float *)take(S * m->E * 4);
+    w->dn2 = (float *)take(std::min(S, (size_t)24 * m->X) * m->E * 4);
     *bytes = off;
     return QMS_CUDA_OK;
 }
@@ -649,7 +656,8 @@ static int mma_core(QmsCudaMoe *m, int S, const int *sel, int nx, int rdiv, floa
     if (dn) w.dn = dn;
     const int nw = mma_width(S, nx), maxT = S / nw + nx;
     QMS_CK(launch_pdl(k_mma_group, dim3(1), dim3(1024), 0, s, sel, S, nx, maxT, nw, w));
-    if (m->gemv && nw == kMmaNs) return gv_gemms(m, w, maxT, rdiv, s);   // few slots per expert: CUDA cores
+    if (m->gemv && nw == kMmaNs)                       // few slots per expert: CUDA cores
+        return gv_gemms(m, w, maxT, S, rdiv, w.dn, w.dn2, dn != nullptr, s);
     QMS_CK(launch_pdl(k_mma_gather, dim3(maxT, 8), dim3(2 * nw), 0, s, (const int8_t *)m->xq_q, (const float *)m->xq_d,
                       (const int *)nullptr, m->nbE, rdiv, nw, w));
     MmaArgs g;
@@ -683,8 +691,9 @@ int mma_forward(QmsCudaMoe *m, int T, const float *resid, float *out, cudaStream
     MmaWork w;
     size_t need = 0;
     mma_layout(m, T, &w, &need, (char *)g_mma_ws.p);
+    const bool halves = m->gemv && mma_width(T * m->K, m->X) == kMmaNs;   // the grouped GEMV ran
     QMS_CK(launch_pdl(k_mma_combine, dim3((m->E + 255) / 256, T), dim3(256), 0, s, (const float *)w.dn,
-                      (const float *)m->wts, m->K, m->E, resid, out));
+                      halves ? (const float *)w.dn2 : nullptr, (const float *)m->wts, m->K, m->E, resid, out));
     if (m->timing) QMS_CK(cudaEventRecord(m->ev[5], s));
     return QMS_CUDA_OK;
 }
@@ -698,7 +707,8 @@ int mma_experts(QmsCudaMoe *m, int S, const int *expert, float *dn, cudaStream_t
 // out[t] = sum_j w[t][j] * dn[t*K + j] in selection order (+ resid)
 int mma_combine(const float *dn, const float *wts, int T, int K, int E, const float *resid, float *out,
                 cudaStream_t s) {
-    QMS_CK(launch_pdl(k_mma_combine, dim3((E + 255) / 256, T), dim3(256), 0, s, dn, wts, K, E, resid, out));
+    QMS_CK(launch_pdl(k_mma_combine, dim3((E + 255) / 256, T), dim3(256), 0, s, dn, (const float *)nullptr, wts, K, E,
+                      resid, out));
     return QMS_CUDA_OK;
 }
 

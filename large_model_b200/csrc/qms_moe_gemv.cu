@@ -37,7 +37,9 @@ constexpr uint32_t kGvSpin = 1u << 22;
 constexpr int kGvMagic = 0x4B400000;         // float bits of 2^23 + 2^22: int v -> float exactly for |v| < 2^22
 constexpr float kGvMagicF = 12582912.0f;
 constexpr int kGvMaxTiles = 640;             // tiles of a GEMV call: S / 16 + nx with S <= 24 nx, nx <= 256
-constexpr int kGvItemCost0 = 2;              // cost of an item beyond its slots (the weight stream), in slots
+constexpr int kGvItemCost0 = 3;              // cost of an item beyond its slot pairs (the weight stream), in slots
+constexpr int kGvXRow = kGvSlots * 32 + 16;  // shared-memory bytes of one block's activation values (all slots + pad)
+constexpr int kGvSRow = kGvSlots * 8 + 8;    // bytes of one block's {scale, second word} pairs (+ pad)
 constexpr int kGvKParts = 2;                 // down items split the F/32 block columns in halves
 
 enum { GV_ERR = 128 };
@@ -127,12 +129,12 @@ __device__ __forceinline__ GvTile gv_tile(const MmaWork &w, int tl) {
 }
 
 // All threads: this CTA's contiguous range [lo, hi) of the ntiles * ipt items, split by cost (an
-// item of a tile with n slots costs n + kGvItemCost0): the CTA owns the items whose starting cost
+// item of a tile with n slots costs n rounded up to pairs + kGvItemCost0): the CTA owns the items whose starting cost
 // falls in its share. s_pre: kGvMaxTiles + 1 ints of shared memory.
 __device__ __forceinline__ void gv_split_items(const MmaWork &w, int ntiles, int ipt, int *s_pre, int *s_lh,
                                                int &lo, int &hi) {
     const int tid = threadIdx.x, nt = blockDim.x;
-    for (int t = tid; t < ntiles; t += nt) s_pre[t] = gv_tile(w, t).ns + kGvItemCost0;
+    for (int t = tid; t < ntiles; t += nt) s_pre[t] = ((gv_tile(w, t).ns + 1) & ~1) + kGvItemCost0;
     if (tid < 2) s_lh[tid] = ntiles * ipt;
     __syncthreads();
     if (tid < 32) {                                       // exclusive prefix of the per-item costs
@@ -169,13 +171,14 @@ __device__ __forceinline__ void gv_split_items(const MmaWork &w, int ntiles, int
     hi = s_lh[1];
 }
 
-// Consumers: the tile's activation rows into shared memory, [slot][K half][block][16 bytes] (one
-// half of consecutive blocks is contiguous: conflict-free 16-byte reads), plus per (slot, block)
-// {scale bits, second word}: the dp4a chain's starting value kGvMagic - 8 * sum for Q4_0 weights,
-// or for Q4_1 the product d * sum as float bits. An odd slot count is padded with a zero row
-// (its results are never stored), so slots go in pairs.
+// Consumers: the tile's activation rows into shared memory, block-major: block b's 16-byte halves
+// of slot j at b * kGvXRow + j * 32 + h * 16, its {scale bits, second word} at b * kGvSRow + j * 8
+// (the pads put consecutive blocks in different banks; a thread's slots sit at fixed offsets).
+// The second word is the dp4a chain's starting value kGvMagic - 8 * sum for Q4_0 weights, or for
+// Q4_1 the product d * sum as float bits. An odd slot count is padded with a zero row (its results
+// are never stored), so slots go in pairs.
 template <bool Q1>
-__device__ __forceinline__ void gv_stage_x(const GvArgs &a, const GvTile &g, int8_t *sx, uint2 *sxs) {
+__device__ __forceinline__ void gv_stage_x(const GvArgs &a, const GvTile &g, int8_t *sx, uint8_t *sxs) {
     const int nb = a.nb, K32 = nb * 32, nsp = (g.ns + 1) & ~1;
     for (int idx = threadIdx.x; idx < nsp * nb * 2; idx += kGvCons) {
         const int j = idx / (2 * nb), rem = idx - j * 2 * nb, h = rem / nb, b = rem - h * nb;
@@ -188,9 +191,10 @@ __device__ __forceinline__ void gv_stage_x(const GvArgs &a, const GvTile &g, int
             d = __ldcg(a.xd + (size_t)row * nb + b);
             sm = __ldcg(a.xs + (size_t)row * nb + b);
         }
-        *reinterpret_cast<uint4 *>(sx + ((size_t)(j * 2 + h) * nb + b) * 16) = v;
-        if (h == 0) sxs[j * nb + b] = make_uint2(__float_as_uint(d), Q1 ? __float_as_uint(d * (float)sm)
-                                                                        : (uint32_t)(kGvMagic - 8 * sm));
+        *reinterpret_cast<uint4 *>(sx + (size_t)b * kGvXRow + j * 32 + h * 16) = v;
+        if (h == 0)
+            *reinterpret_cast<uint2 *>(sxs + (size_t)b * kGvSRow + j * 8) =
+                make_uint2(__float_as_uint(d), Q1 ? __float_as_uint(d * (float)sm) : (uint32_t)(kGvMagic - 8 * sm));
     }
 }
 
@@ -236,20 +240,100 @@ __device__ __forceinline__ void gv_produce(const GvArgs &a, int lo, int hi, int 
     }
 }
 
+// Ring position and status of a consumer thread, kept across items.
+struct GvRing {
+    int r;
+    uint32_t par;
+    bool ok;
+};
+
+// Consumer side of one ring stage: wait for it (bounded); the stage's shared memory, or nullptr once
+// the CTA has aborted. gv_release frees it after this thread's weights are in registers.
+__device__ __forceinline__ const uint8_t *gv_acquire(const GvArgs &a, GvRing &c, const uint8_t *ring, uint64_t *full,
+                                                     volatile int *abort) {
+    if (c.ok) c.ok = gv_wait(&full[c.r], c.par, abort, a.err);
+    return c.ok ? ring + (size_t)c.r * a.sst : nullptr;
+}
+
+__device__ __forceinline__ void gv_release(GvRing &c, uint64_t *empty, int lane, int nring) {
+    __syncwarp();
+    if (c.ok && lane == 0) mbar_arrive(&empty[c.r]);
+    if (++c.r == nring) {
+        c.r = 0;
+        c.par ^= 1;
+    }
+}
+
 // ---- gate/up + SwiGLU + Q8 ---------------------------------------------------------------------------
 // Item (tile, ft): f values ft*32 .. +31 of the tile's expert; its nb/16 stages are the staged chunks
 // (8 chunks of 8 rows x 16 blocks: chunks 0-3 gate rows, 4-7 up rows). Consumer thread t: block
 // b = t % 16 of every stage and f value t / 16; its gate and up rows go as a pair.
+constexpr int kGvSB = 16;
+constexpr uint32_t kGvGB = 8u * kGvSB * 18;
+
+// One item with NP slot pairs: the stage loop, then the sums over the 16 threads of each f (adjacent
+// lanes) and SwiGLU (src/model.c:989-997) into sa[slot][32].
+template <int NP>
+__device__ __forceinline__ void gv_gu_item(const GvArgs &a, GvRing &c, uint8_t *ring, uint64_t *full, uint64_t *empty,
+                                        volatile int *abort, const int8_t *sx, const uint8_t *sxs, float *sa, int nst) {
+    const int tid = threadIdx.x, lane = tid & 31, b = tid % kGvSB, f = tid / kGvSB;
+    const uint32_t o = (uint32_t)((f & 7) * kGvSB + b), cgo = (uint32_t)(f >> 3) * kGvGB;
+    float2 acc[2 * NP];                                   // (gate, up) of slot j
+#pragma unroll
+    for (int j = 0; j < 2 * NP; j++) acc[j] = make_float2(0.0f, 0.0f);
+    for (int st = 0; st < nst; st++) {
+        const uint8_t *stg = gv_acquire(a, c, ring, full, abort);
+        uint4 ng = make_uint4(0, 0, 0, 0), nu = ng;
+        float2 dgu = make_float2(0.0f, 0.0f);
+        if (stg) {
+            const uint8_t *cg = stg + cgo, *cu = cg + 4 * kGvGB;
+            ng = *reinterpret_cast<const uint4 *>(cg + o * 16);
+            nu = *reinterpret_cast<const uint4 *>(cu + o * 16);
+            dgu = make_float2(h2f(*reinterpret_cast<const uint16_t *>(cg + 8 * kGvSB * 16 + o * 2)),
+                              h2f(*reinterpret_cast<const uint16_t *>(cu + 8 * kGvSB * 16 + o * 2)));
+        }
+        gv_release(c, empty, lane, a.ring);
+        if (!stg) continue;
+        uint32_t wg[8], wu[8];
+        gv_split(ng, wg);
+        gv_split(nu, wu);
+        const int gb = st * kGvSB + b;
+        const int8_t *xb = sx + (size_t)gb * kGvXRow;
+        const uint8_t *sb = sxs + (size_t)gb * kGvSRow;
+#pragma unroll
+        for (int j = 0; j < 2 * NP; j++) {
+            const uint4 x0 = *reinterpret_cast<const uint4 *>(xb + j * 32);
+            const uint4 x1 = *reinterpret_cast<const uint4 *>(xb + j * 32 + 16);
+            const uint2 xv = *reinterpret_cast<const uint2 *>(sb + j * 8);
+            const float xd = __uint_as_float(xv.x);
+            const int bias = (int)xv.y;                         // kGvMagic - 8 * sum: Q4_0 is d (q - 8)
+            const float2 p = gv_unmagic(gv_dot(wg, x0, x1, bias), gv_dot(wu, x0, x1, bias));
+            acc[j] = f2_fma(p, f2_mul(dgu, make_float2(xd, xd)), acc[j]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 2 * NP; j++) {
+        float gs = acc[j].x, us = acc[j].y;
+#pragma unroll
+        for (int m = kGvSB / 2; m > 0; m >>= 1) {
+            gs += __shfl_xor_sync(0xffffffffu, gs, m);
+            us += __shfl_xor_sync(0xffffffffu, us, m);
+        }
+        if (b == 0) {
+            const float sg = __fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs)));
+            sa[j * 32 + f] = __fmul_rn(sg, us);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
-    constexpr int SB = 16;
-    constexpr uint32_t GB = 8u * SB * 18;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_abort, s_lh[2], s_pre[kGvMaxTiles + 1];
     const int nb = a.nb, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint8_t *ring = smem;
     int8_t *sx = reinterpret_cast<int8_t *>(smem + (size_t)a.ring * a.sst);
-    uint2 *sxs = reinterpret_cast<uint2 *>(sx + (size_t)kGvSlots * nb * 32);
-    float *sact = reinterpret_cast<float *>(sxs + kGvSlots * nb);          // [2][slot][32]
+    uint8_t *sxs = reinterpret_cast<uint8_t *>(sx + (size_t)nb * kGvXRow);
+    float *sact = reinterpret_cast<float *>(sxs + (size_t)nb * kGvSRow);   // [2][slot][32]
     uint64_t *full = reinterpret_cast<uint64_t *>(sact + 2 * kGvSlots * 32);
     uint64_t *empty = full + a.ring;
     if (tid == 0) {
@@ -262,24 +346,19 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
     }
     pdl_wait();
     pdl_trigger();
-    const int ipt = a.F / 32, nst = nb / SB;
+    const int ipt = a.F / 32, nst = nb / kGvSB;
     int lo, hi;
     gv_split_items(a.wk, min(__ldcg(a.wk.ntiles), kGvMaxTiles), ipt, s_pre, s_lh, lo, hi);
     if (warp == kGvConsWarps) {
         if (lane == 0)
             gv_produce(a, lo, hi, ipt, nst, ring, full, empty, &s_abort,
                        [&](const uint8_t *base, int sub, int st, uint8_t *dst, uint64_t *bar, uint64_t pol) {
-                           mbar_arrive_expect_tx(bar, 8 * GB);
-                           bulk_load(dst, base + ((size_t)(sub * nst + st) * 8) * GB, 8 * GB, bar, pol);
+                           mbar_arrive_expect_tx(bar, 8 * kGvGB);
+                           bulk_load(dst, base + ((size_t)(sub * nst + st) * 8) * kGvGB, 8 * kGvGB, bar, pol);
                        });
         return;
     }
-    const int b = tid % SB, f = tid / SB;
-    const uint32_t o = (uint32_t)((f & 7) * SB + b);
-    const uint32_t cgo = (uint32_t)(f >> 3) * GB;
-    int r = 0;
-    uint32_t par = 0;
-    bool ok = true;
+    GvRing c{0, 0, true};
     int cur = -1, buf = 0;
     GvTile g{0, 0, 0};
     for (int item = lo; item < hi; item++) {
@@ -291,65 +370,21 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
             gv_stage_x<false>(a, g, sx, sxs);
             cons_sync();
         }
-        float2 acc[kGvSlots];                              // (gate, up) of slot j
-#pragma unroll
-        for (int j = 0; j < kGvSlots; j++) acc[j] = make_float2(0.0f, 0.0f);
-        for (int st = 0; st < nst; st++) {
-            if (ok) ok = gv_wait(&full[r], par, &s_abort, a.err);
-            uint32_t wg[8], wu[8];
-            float2 dgu = make_float2(0.0f, 0.0f);
-            if (ok) {
-                const uint8_t *cg = ring + (size_t)r * a.sst + cgo, *cu = cg + 4 * GB;
-                gv_split(*reinterpret_cast<const uint4 *>(cg + o * 16), wg);
-                gv_split(*reinterpret_cast<const uint4 *>(cu + o * 16), wu);
-                dgu = make_float2(h2f(*reinterpret_cast<const uint16_t *>(cg + 8 * SB * 16 + o * 2)),
-                                  h2f(*reinterpret_cast<const uint16_t *>(cu + 8 * SB * 16 + o * 2)));
-            }
-            __syncwarp();
-            if (ok && lane == 0) mbar_arrive(&empty[r]);  // weights are in registers: free the stage
-            if (++r == a.ring) {
-                r = 0;
-                par ^= 1;
-            }
-            if (!ok) continue;
-            const int gb = st * SB + b;
-#pragma unroll
-            for (int jp = 0; jp < kGvSlots; jp += 2) {
-                if (jp < g.ns) {
-#pragma unroll
-                    for (int j = jp; j < jp + 2; j++) {
-                        const uint4 x0 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2) * nb + gb) * 16);
-                        const uint4 x1 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2 + 1) * nb + gb) * 16);
-                        const uint2 xv = sxs[j * nb + gb];
-                        const float xd = __uint_as_float(xv.x);
-                        const int bias = (int)xv.y;                 // kGvMagic - 8 * sum: Q4_0 is d (q - 8)
-                        const float2 p = gv_unmagic(gv_dot(wg, x0, x1, bias), gv_dot(wu, x0, x1, bias));
-                        acc[j] = f2_fma(p, f2_mul(dgu, make_float2(xd, xd)), acc[j]);
-                    }
-                }
-            }
-        }
-        // sums over the 16 threads of each f (adjacent lanes), SwiGLU, Q8 groups per slot
         float *sa = sact + buf * kGvSlots * 32;
-#pragma unroll
-        for (int j = 0; j < kGvSlots; j++) {
-            if (j < g.ns) {
-                float gs = acc[j].x, us = acc[j].y;
-#pragma unroll
-                for (int m = SB / 2; m > 0; m >>= 1) {
-                    gs += __shfl_xor_sync(0xffffffffu, gs, m);
-                    us += __shfl_xor_sync(0xffffffffu, us, m);
-                }
-                if (b == 0) {
-                    const float sg = __fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs)));
-                    sa[j * 32 + f] = __fmul_rn(sg, us);
-                }
-            }
+        switch ((g.ns + 1) >> 1) {
+            case 1: gv_gu_item<1>(a, c, ring, full, empty, &s_abort, sx, sxs, sa, nst); break;
+            case 2: gv_gu_item<2>(a, c, ring, full, empty, &s_abort, sx, sxs, sa, nst); break;
+            case 3: gv_gu_item<3>(a, c, ring, full, empty, &s_abort, sx, sxs, sa, nst); break;
+            case 4: gv_gu_item<4>(a, c, ring, full, empty, &s_abort, sx, sxs, sa, nst); break;
+            case 5: gv_gu_item<5>(a, c, ring, full, empty, &s_abort, sx, sxs, sa, nst); break;
+            case 6: gv_gu_item<6>(a, c, ring, full, empty, &s_abort, sx, sxs, sa, nst); break;
+            case 7: gv_gu_item<7>(a, c, ring, full, empty, &s_abort, sx, sxs, sa, nst); break;
+            default: gv_gu_item<8>(a, c, ring, full, empty, &s_abort, sx, sxs, sa, nst); break;
         }
         cons_sync();
-        for (int j = warp; j < g.ns; j += kGvConsWarps) {
+        for (int j = warp; j < g.ns; j += kGvConsWarps) {   // Q8 group of each slot's 32 f values
             const Q8Lane q = quantize_lane(sa[j * 32 + lane]);
-            if (ok) {
+            if (c.ok) {
                 const int slot = __ldcg(a.wk.slots + g.off + j);
                 a.aq_q[(size_t)slot * a.F + sub * 32 + lane] = (int8_t)q.q;
                 if (lane == 0) {
@@ -366,17 +401,79 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_gate_up(const GvArgs a) {
 // Item (tile, q, kh): down rows q*RD .. +RD-1 of the tile's expert (column stage row range q) over
 // block columns kh*nb/2 .. +nb/2-1; stage st = the whole column stage (kh*nb/2 + st, q). Consumer
 // thread t: rows t + 512 i, i < RPT = RD / 512 (two rows go as a pair).
+template <bool Q1, int RPT, int NP>
+__device__ __forceinline__ void gv_dn_item(const GvArgs &a, GvRing &c, uint8_t *ring, uint64_t *full, uint64_t *empty,
+                                        volatile int *abort, const int8_t *sx, const uint8_t *sxs, int nst, int kh,
+                                        int q, const GvTile &g) {
+    constexpr int RD = 512 * RPT;
+    constexpr uint32_t NIB = RD * 16, SCL = RD * 2;
+    const int tid = threadIdx.x, lane = tid & 31, r1 = RPT == 2 ? tid + 512 : tid;
+    float2 acc[2 * NP];                                   // RPT 2: rows (t, t + 512); 1: .x only
+#pragma unroll
+    for (int j = 0; j < 2 * NP; j++) acc[j] = make_float2(0.0f, 0.0f);
+    for (int st = 0; st < nst; st++) {
+        const uint8_t *stg = gv_acquire(a, c, ring, full, abort);
+        uint4 n0 = make_uint4(0, 0, 0, 0), n1 = n0;
+        float2 dw = make_float2(0.0f, 0.0f), mw = dw;
+        if (stg) {
+            n0 = *reinterpret_cast<const uint4 *>(stg + tid * 16);
+            n1 = *reinterpret_cast<const uint4 *>(stg + r1 * 16);
+            dw = make_float2(h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + tid * 2)),
+                             h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + r1 * 2)));
+            if (Q1)
+                mw = make_float2(h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + SCL + tid * 2)),
+                                 h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + SCL + r1 * 2)));
+        }
+        gv_release(c, empty, lane, a.ring);
+        if (!stg) continue;
+        uint32_t w0[8], w1[8];
+        gv_split(n0, w0);
+        gv_split(n1, w1);
+        const int bc = kh * nst + st;
+        const int8_t *xb = sx + (size_t)bc * kGvXRow;
+        const uint8_t *sb = sxs + (size_t)bc * kGvSRow;
+#pragma unroll
+        for (int j = 0; j < 2 * NP; j++) {
+            const uint4 x0 = *reinterpret_cast<const uint4 *>(xb + j * 32);
+            const uint4 x1 = *reinterpret_cast<const uint4 *>(xb + j * 32 + 16);
+            const uint2 xv = *reinterpret_cast<const uint2 *>(sb + j * 8);
+            const float xd = __uint_as_float(xv.x);
+            if (Q1) {                                  // d q + m: d dx isum + m (dx sum)  (src/kernels.c:109-121)
+                const float2 p = gv_unmagic(gv_dot(w0, x0, x1, kGvMagic), RPT == 2 ? gv_dot(w1, x0, x1, kGvMagic) : kGvMagic);
+                acc[j] = f2_fma(p, f2_mul(dw, make_float2(xd, xd)), acc[j]);
+                const float ds = __uint_as_float(xv.y);
+                acc[j] = f2_fma(mw, make_float2(ds, ds), acc[j]);
+            } else {                                   // d (q - 8): the -8 sits in the chain's start
+                const int bias = (int)xv.y;
+                const float2 p = gv_unmagic(gv_dot(w0, x0, x1, bias), RPT == 2 ? gv_dot(w1, x0, x1, bias) : kGvMagic);
+                acc[j] = f2_fma(p, f2_mul(dw, make_float2(xd, xd)), acc[j]);
+            }
+        }
+    }
+    if (c.ok) {
+        float *dst = kh ? a.dn2 : a.dn;
+#pragma unroll
+        for (int j = 0; j < 2 * NP; j++) {
+            if (j < 2 * NP - 1 || j < g.ns) {             // not the padding slot
+                float *o = dst + (size_t)__ldcg(a.wk.slots + g.off + j) * a.E + q * RD + tid;
+                o[0] = acc[j].x;
+                if (RPT == 2) o[512] = acc[j].y;
+            }
+        }
+    }
+}
+
 template <bool Q1, int RPT>
 __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
     constexpr int RD = 512 * RPT;
-    constexpr uint32_t NIB = RD * 16, SCL = RD * 2, STD = NIB + SCL * (Q1 ? 2 : 1);
+    constexpr uint32_t STD = RD * (Q1 ? 20 : 18);
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_abort, s_lh[2], s_pre[kGvMaxTiles + 1];
     const int nb = a.nb, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint8_t *ring = smem;
     int8_t *sx = reinterpret_cast<int8_t *>(smem + (size_t)a.ring * a.sst);
-    uint2 *sxs = reinterpret_cast<uint2 *>(sx + (size_t)kGvSlots * nb * 32);
-    uint64_t *full = reinterpret_cast<uint64_t *>(sxs + kGvSlots * nb);
+    uint8_t *sxs = reinterpret_cast<uint8_t *>(sx + (size_t)nb * kGvXRow);
+    uint64_t *full = reinterpret_cast<uint64_t *>(sxs + (size_t)nb * kGvSRow);
     uint64_t *empty = full + a.ring;
     if (tid == 0) {
         s_abort = 0;
@@ -401,9 +498,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
                        });
         return;
     }
-    int r = 0;
-    uint32_t par = 0;
-    bool ok = true;
+    GvRing c{0, 0, true};
     int cur = -1;
     GvTile g{0, 0, 0};
     for (int item = lo; item < hi; item++) {
@@ -415,67 +510,15 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
             gv_stage_x<Q1>(a, g, sx, sxs);
             cons_sync();
         }
-        float2 acc[kGvSlots];                              // RPT 2: rows (t, t + 512); 1: .x only
-#pragma unroll
-        for (int j = 0; j < kGvSlots; j++) acc[j] = make_float2(0.0f, 0.0f);
-        for (int st = 0; st < nst; st++) {
-            if (ok) ok = gv_wait(&full[r], par, &s_abort, a.err);
-            uint32_t w0[8], w1[8];
-            float2 dw = make_float2(0.0f, 0.0f), mw = make_float2(0.0f, 0.0f);
-            if (ok) {
-                const uint8_t *stg = ring + (size_t)r * a.sst;
-                const int r1 = RPT == 2 ? tid + 512 : tid;
-                gv_split(*reinterpret_cast<const uint4 *>(stg + tid * 16), w0);
-                gv_split(*reinterpret_cast<const uint4 *>(stg + r1 * 16), w1);
-                dw = make_float2(h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + tid * 2)),
-                                 h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + r1 * 2)));
-                if (Q1)
-                    mw = make_float2(h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + SCL + tid * 2)),
-                                     h2f(*reinterpret_cast<const uint16_t *>(stg + NIB + SCL + r1 * 2)));
-            }
-            __syncwarp();
-            if (ok && lane == 0) mbar_arrive(&empty[r]);
-            if (++r == a.ring) {
-                r = 0;
-                par ^= 1;
-            }
-            if (!ok) continue;
-            const int bc = kh * nst + st;
-#pragma unroll
-            for (int jp = 0; jp < kGvSlots; jp += 2) {
-                if (jp < g.ns) {
-#pragma unroll
-                    for (int j = jp; j < jp + 2; j++) {
-                        const uint4 x0 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2) * nb + bc) * 16);
-                        const uint4 x1 = *reinterpret_cast<const uint4 *>(sx + ((size_t)(j * 2 + 1) * nb + bc) * 16);
-                        const uint2 xv = sxs[j * nb + bc];
-                        const float xd = __uint_as_float(xv.x);
-                        if (Q1) {                          // d q + m: d dx isum + m (dx sum)  (src/kernels.c:109-121)
-                            const float2 p = gv_unmagic(gv_dot(w0, x0, x1, kGvMagic),
-                                                        RPT == 2 ? gv_dot(w1, x0, x1, kGvMagic) : kGvMagic);
-                            acc[j] = f2_fma(p, f2_mul(dw, make_float2(xd, xd)), acc[j]);
-                            const float ds = __uint_as_float(xv.y);
-                            acc[j] = f2_fma(mw, make_float2(ds, ds), acc[j]);
-                        } else {                           // d (q - 8): the -8 sits in the chain's start
-                            const int bias = (int)xv.y;
-                            const float2 p = gv_unmagic(gv_dot(w0, x0, x1, bias),
-                                                        RPT == 2 ? gv_dot(w1, x0, x1, bias) : kGvMagic);
-                            acc[j] = f2_fma(p, f2_mul(dw, make_float2(xd, xd)), acc[j]);
-                        }
-                    }
-                }
-            }
-        }
-        if (ok) {
-            float *dst = kh ? a.dn2 : a.dn;
-#pragma unroll
-            for (int j = 0; j < kGvSlots; j++) {
-                if (j < g.ns) {
-                    float *o = dst + (size_t)__ldcg(a.wk.slots + g.off + j) * a.E + q * RD + tid;
-                    o[0] = acc[j].x;
-                    if (RPT == 2) o[512] = acc[j].y;
-                }
-            }
+        switch ((g.ns + 1) >> 1) {
+            case 1: gv_dn_item<Q1, RPT, 1>(a, c, ring, full, empty, &s_abort, sx, sxs, nst, kh, q, g); break;
+            case 2: gv_dn_item<Q1, RPT, 2>(a, c, ring, full, empty, &s_abort, sx, sxs, nst, kh, q, g); break;
+            case 3: gv_dn_item<Q1, RPT, 3>(a, c, ring, full, empty, &s_abort, sx, sxs, nst, kh, q, g); break;
+            case 4: gv_dn_item<Q1, RPT, 4>(a, c, ring, full, empty, &s_abort, sx, sxs, nst, kh, q, g); break;
+            case 5: gv_dn_item<Q1, RPT, 5>(a, c, ring, full, empty, &s_abort, sx, sxs, nst, kh, q, g); break;
+            case 6: gv_dn_item<Q1, RPT, 6>(a, c, ring, full, empty, &s_abort, sx, sxs, nst, kh, q, g); break;
+            case 7: gv_dn_item<Q1, RPT, 7>(a, c, ring, full, empty, &s_abort, sx, sxs, nst, kh, q, g); break;
+            default: gv_dn_item<Q1, RPT, 8>(a, c, ring, full, empty, &s_abort, sx, sxs, nst, kh, q, g); break;
         }
     }
 }
@@ -496,7 +539,7 @@ static uint32_t gv_stage_bytes(const QmsCudaMoe *m, bool gu) {
 
 static size_t gv_fixed(const QmsCudaMoe *m, bool gu) {
     const int nb = gu ? m->nbE : m->nbF;
-    return (size_t)kGvSlots * nb * 40 + (gu ? 2 * kGvSlots * 32 * 4 : 0);
+    return (size_t)nb * (kGvXRow + kGvSRow) + (gu ? 2 * kGvSlots * 32 * 4 : 0);
 }
 
 static int gv_ring(const QmsCudaMoe *m, bool gu) {

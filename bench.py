@@ -349,16 +349,18 @@ def run_batched(a):
         if a.mode == "bs64":
             peak, peak_kind = peaks()
             gbs = call_bytes / (call_ms / 1e3) / 1e9
-            roof = {"bound": "hbm", "kernel": "whole block (router, k_mma_gemm x2, gathers, combine)",
+            roof = {"bound": "hbm", "kernel": "whole block (router, k_mma_group, k_gv_gate_up, k_gv_down, combine)",
                     "achieved": round(gbs, 1), "peak": peak * world, "unit": "GB/s",
                     "frac": round(gbs / (peak * world), 4),
                     "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                     "bytes_per_call": int(call_bytes), "distinct_experts_per_call": statistics.mean(distinct),
-                    "traffic": None}
+                    # DRAM bytes of k_gv_gate_up + k_gv_down for one call, one ncu capture
+                    # (profiles/k_gv_235b_bs64.md), against ~1.32 GB algorithmic
+                    "traffic": 1339233024 if world == 1 else None}
             metric, unit, value = "Qwen3-235B Q4_0 MoE-layer decode bs64 tokens/s (operator)", "tok/s", tok_s
         else:
             tops = world * ops / (call_ms / 1e3) / 1e12
-            roof = {"bound": "tensor", "kernel": "whole block (router, k_mma_gemm x2, gathers, combine)",
+            roof = {"bound": "tensor", "kernel": "whole block (router, k_mma_group, gathers, k_mma_gemm x2, combine)",
                     "achieved": round(tops, 1), "peak": 4500.0 * world, "unit": "TOP/s",
                     "frac": round(tops / (4500.0 * world), 4),
                     "peak_kind": "nominal dense int8 (no measured int8 peak on this pool)", "traffic": None,

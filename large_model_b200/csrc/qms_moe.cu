@@ -29,7 +29,9 @@ namespace qms {
 
 constexpr int kGateUpRows = 8;         // f values per gate/up CTA (one per warp)
 constexpr int kDownRows = 32;          // output rows per down CTA (one per lane)
-constexpr int kMmaMinT = 16;           // tokens from which the grouped tensor-core kernels run
+constexpr int kMmaMinT = 5;            // tokens from which the expert-grouped kernels run (GEMV, tensor cores):
+                                        // measured 158 vs 325 us (T = 8) and 190 vs 463 us (T = 12) against
+                                        // the per-slot dp4a kernels on a 235B layer
 
 // ---- load-time repack: GGUF rows -> staged layouts (qms_moe.cuh) --------------------------------
 // gate (which 0) / up (which 1) Q4_0 rows of a stacked [X][F] tensor -> chunks

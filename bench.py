@@ -343,8 +343,28 @@ def run_batched(a):
         for i in range(e2e_n):
             layers[i % 2].forward_host(xh.numpy(), out=oh.numpy())
         e2e_s = time.perf_counter() - t0
-        e2e = {"value": round(T * e2e_n / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": T * E * 4,
+        if dist:                                     # replicas: max over ranks, all ranks' tokens
+            t = torch.tensor([e2e_s], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        e2e = {"value": round(T * world * e2e_n / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": T * E * 4,
                "d2h_bytes_per_step": T * E * 4, "note": "qms_cuda_moe_forward_host per call"}
+    else:                                            # every rank: its tokens in from and out to pinned host memory
+        def host_call(i):
+            x = xh.to(dev, non_blocking=True)
+            oh.copy_(eps[i % 2].forward(x), non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        host_call(0)
+        dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(e2e_n):
+            host_call(i)
+        t = torch.tensor([time.perf_counter() - t0], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(T * world * e2e_n / float(t.item()), 1), "unit": "tok/s",
+               "h2d_bytes_per_step": T * E * 4, "d2h_bytes_per_step": T * E * 4,
+               "note": "per rank: its T tokens from pinned host memory, ExpertParallelMoe.forward, result to "
+                       "pinned host memory; max over ranks"}
     if rank == 0:
         if a.mode == "bs64":
             peak, peak_kind = peaks()

@@ -123,6 +123,11 @@ int qms_cuda_moe_route(QmsCudaMoe *m, const float *xn, int T, int *sel, float *w
  * down projection before weighting. Rows with an out-of-range id are skipped (dn left as is).
  * Runs the grouped tensor-core kernels; device buffers. */
 int qms_cuda_moe_experts(QmsCudaMoe *m, const float *x, const int *expert, int S, float *dn, void *stream);
+/* The same from rows already quantised: xq [S][n_embd/32] QmsQ8 blocks (e.g. from
+ * qms_cuda_quantize_q8, bit-identical to the reference's quantiser), so a dispatch sends 44 bytes
+ * per 32 values instead of 128 (moe_group_fast quantises each slot's input once, src/model.c:979-988).
+ * The results equal qms_cuda_moe_experts on the fp32 rows. */
+int qms_cuda_moe_experts_q8(QmsCudaMoe *m, const QmsQ8 *xq, const int *expert, int S, float *dn, void *stream);
 /* out[t] = resid[t] + sum_j wts[t][j] * dn[t * n_used + j] in selection order (src/model.c:1152-1162);
  * resid may be NULL; device buffers. */
 int qms_cuda_moe_combine(const float *dn, const float *wts, int T, int n_used, int n_embd, const float *resid,

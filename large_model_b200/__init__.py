@@ -73,6 +73,7 @@ def lib() -> C.CDLL:
     L.qms_cuda_moe_create_shard.argtypes = [C.POINTER(MoeDesc), i32, i32, C.POINTER(vp)]
     L.qms_cuda_moe_route.argtypes = [vp, vp, i32, vp, vp, vp, vp]
     L.qms_cuda_moe_experts.argtypes = [vp, vp, vp, i32, vp, vp]
+    L.qms_cuda_moe_experts_q8.argtypes = [vp, vp, vp, i32, vp, vp]
     L.qms_cuda_moe_combine.argtypes = [vp, vp, i32, i32, i32, vp, vp, vp]
     _lib = L
     return L
@@ -256,6 +257,16 @@ class MoeLayer:
         if dn is None:
             dn = torch.empty((S, self.n_embd), dtype=torch.float32, device=x.device)
         check(lib().qms_cuda_moe_experts(self.h, _ptr(x), _ptr(expert), S, _ptr(dn), _stream(stream)))
+        return dn
+
+    def experts_q8(self, xq, expert, dn=None, stream=None):
+        """The same from quantised rows (qms_cuda_moe_experts_q8): xq uint8 [S][n_embd/32 * 44], QmsQ8
+        blocks as quantize_q8 returns them."""
+        torch = _torch()
+        S = xq.shape[0]
+        if dn is None:
+            dn = torch.empty((S, self.n_embd), dtype=torch.float32, device=xq.device)
+        check(lib().qms_cuda_moe_experts_q8(self.h, _ptr(xq), _ptr(expert), S, _ptr(dn), _stream(stream)))
         return dn
 
     def forward_host(self, xn: np.ndarray, out: np.ndarray | None = None, with_routing: bool = False):

@@ -135,6 +135,21 @@ __global__ void __launch_bounds__(256) k_moe_topk(const float *__restrict__ logi
     topk_token(logits + (size_t)t * X, X, K, sel + t * K, wts + t * K, s_sel);
 }
 
+// QmsQ8 blocks (the reference's activation block, src/kernels.h:7-12) -> the planar Q8 rows the
+// grouped kernels read: values, scale, block sum (s16[0] + s16[1]). One thread per block.
+__global__ void __launch_bounds__(256) k_unpack_q8(const QmsQ8 *__restrict__ x, int64_t nblocks, int8_t *__restrict__ xq_q,
+                                                   float *__restrict__ xq_d, int *__restrict__ xq_s) {
+    for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nblocks; b += (int64_t)gridDim.x * blockDim.x) {
+        const QmsQ8 *blk = x + b;
+        const int *q = reinterpret_cast<const int *>(blk->q);             // 4-byte aligned inside the 44-byte block
+        int4 *dst = reinterpret_cast<int4 *>(xq_q + b * 32);
+        dst[0] = make_int4(__ldg(q + 0), __ldg(q + 1), __ldg(q + 2), __ldg(q + 3));
+        dst[1] = make_int4(__ldg(q + 4), __ldg(q + 5), __ldg(q + 6), __ldg(q + 7));
+        xq_d[b] = __ldg(&blk->d);
+        xq_s[b] = (int)__ldg(&blk->s16[0]) + (int)__ldg(&blk->s16[1]);
+    }
+}
+
 // ---- router for larger T: Q8 rows, then logits tiled over (tokens x experts) ----------------------
 // One warp per 32-block of xn: the quantiser of src/kernels.c:34-53.
 __global__ void __launch_bounds__(256) k_quantize_rows(const float *__restrict__ xn, int64_t nblocks,
@@ -718,6 +733,29 @@ int qms_cuda_moe_experts(QmsCudaMoe *m, const float *x, const int *expert, int S
     const cudaStream_t s = (cudaStream_t)stream;
     const int64_t nblocks = (int64_t)S * m->nbE;
     k_quantize_rows<<<(unsigned)std::min<int64_t>((nblocks + 7) / 8, 4096), 256, 0, s>>>(x, nblocks, m->xq_q, m->xq_d,
+                                                                                        m->xq_s);
+    QMS_CK(cudaGetLastError());
+    return mma_experts(m, S, expert, dn, s);
+}
+
+int qms_cuda_moe_experts_q8(QmsCudaMoe *m, const QmsQ8 *xq, const int *expert, int S, float *dn, void *stream) {
+    QMS_REQUIRE(m && S >= 0, QMS_CUDA_EINVAL, "moe_experts_q8: bad arguments");
+    if (S == 0) return QMS_CUDA_OK;
+    QMS_REQUIRE(xq && expert && dn, QMS_CUDA_EINVAL, "moe_experts_q8: NULL xq, expert or dn");
+    QMS_REQUIRE(m->mma_min_t > 0, QMS_CUDA_EUNSUPPORTED, "moe_experts_q8: the grouped path is off for this layer");
+    int rc = ensure_device(m->device);
+    if (rc) return rc;
+    const int T = (S + m->K - 1) / m->K;
+    if (S > m->cap_T || T > m->cap_T) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        QMS_CK(cudaStreamIsCapturing((cudaStream_t)stream, &cs));
+        QMS_REQUIRE(cs == cudaStreamCaptureStatusNone, QMS_CUDA_EINVAL,
+                    "moe_experts_q8: scratch for %d slots must be reserved before graph capture", S);
+        if ((rc = qms_cuda_moe_reserve(m, S))) return rc;
+    }
+    const cudaStream_t s = (cudaStream_t)stream;
+    const int64_t nblocks = (int64_t)S * m->nbE;
+    k_unpack_q8<<<(unsigned)std::min<int64_t>((nblocks + 255) / 256, 4096), 256, 0, s>>>(xq, nblocks, m->xq_q, m->xq_d,
                                                                                         m->xq_s);
     QMS_CK(cudaGetLastError());
     return mma_experts(m, S, expert, dn, s);

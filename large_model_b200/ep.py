@@ -5,10 +5,11 @@ Rank r holds experts [r * X/N, (r+1) * X/N) as a shard layer (qms_cuda_moe_creat
 full router. One call of a layer, on every rank:
 
 1. route its own tokens (replicated router, src/model.c:1043-1064): sel / wts [T][K];
-2. send every (token, slot) to the rank owning the slot's expert: an all-to-all of the per-rank
-   counts, then of the token rows (fp32) and of the local expert ids, in slot order;
-3. run the received rows through the local experts (grouped tensor-core GEMMs) into their
-   unweighted down rows;
+2. quantise its token rows once into Q8 blocks (the reference's QmsQ8, 44 bytes per 32 values,
+   src/kernels.h:7-12) and send every (token, slot) row to the rank owning the slot's expert: an
+   all-to-all of the per-rank counts, then of the Q8 rows and of the local expert ids, in slot order;
+3. run the received rows through the local experts (the grouped kernels) into their unweighted
+   down rows;
 4. return those rows with the reverse all-to-all;
 5. combine each token's K down rows in selection order, plus the residual (src/model.c:1152-1162).
 
@@ -32,8 +33,12 @@ class CudaBackend:
     def route(self, xn):
         return self.layer.route_only(xn)
 
-    def experts(self, x, local_expert):
-        return self.layer.experts(x, local_expert)
+    def quantize(self, xn):
+        from . import quantize_q8
+        return quantize_q8(xn)
+
+    def experts_q8(self, xq, local_expert):
+        return self.layer.experts_q8(xq, local_expert)
 
     def combine(self, dn, wts, resid):
         from . import combine
@@ -69,13 +74,14 @@ class ExpertParallelMoe:
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
         sc, rc = send_counts.tolist(), recv_counts.tolist()
         S = sum(rc)
-        send_x = xn[order // self.K].contiguous()
+        xq = self.backend.quantize(xn)                            # [T][E/32 * 44] bytes
+        send_x = xq[order // self.K].contiguous()
         send_e = (flat[order] % self.per_rank).to(torch.int32).contiguous()
-        recv_x = torch.empty((S, self.E), dtype=xn.dtype, device=dev)
+        recv_x = torch.empty((S, xq.shape[1]), dtype=xq.dtype, device=dev)
         recv_e = torch.empty((S,), dtype=torch.int32, device=dev)
         _all_to_all(recv_x, send_x, rc, sc, self.group)
         _all_to_all(recv_e, send_e, rc, sc, self.group)
-        dn_recv = self.backend.experts(recv_x, recv_e) if S else torch.empty((0, self.E), device=dev)
+        dn_recv = self.backend.experts_q8(recv_x, recv_e) if S else torch.empty((0, self.E), device=dev)
         dn_sorted = torch.empty((T * self.K, self.E), dtype=torch.float32, device=dev)
         _all_to_all(dn_sorted, dn_recv.contiguous(), sc, rc, self.group)
         dn = torch.empty_like(dn_sorted)

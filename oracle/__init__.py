@@ -60,6 +60,7 @@ class Oracle:
         L.orc_vec_dot_f32.argtypes = [vp, vp, i64]
         L.orc_vec_dot_f32.restype = C.c_float
         L.orc_matmul.argtypes = [i32, i64, i64, vp, vp, i32, vp]
+        L.orc_matmul_q8.argtypes = [i32, i64, i64, vp, vp, i32, vp]
         L.orc_route.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp]
         L.orc_moe.argtypes = [vp, vp, i32, vp, vp, vp, vp]
         L.orc_moe.restype = i32
@@ -96,6 +97,14 @@ class Oracle:
         x = np.ascontiguousarray(x, np.float32).reshape(-1, cols)
         y = np.empty((x.shape[0], rows), np.float32)
         self.lib.orc_matmul(typ, rows, cols, _p(np.ascontiguousarray(w)), _p(x), x.shape[0], _p(y))
+        return y
+
+    def matmul_q8(self, typ: int, rows: int, cols: int, w: np.ndarray, xq: np.ndarray) -> np.ndarray:
+        """matmul from quantised rows: xq holds T * cols/32 QmsQ8 records."""
+        xq = np.ascontiguousarray(xq).view(Q8_DTYPE).reshape(-1)
+        T = xq.size // (cols // 32)
+        y = np.empty((T, rows), np.float32)
+        self.lib.orc_matmul_q8(typ, rows, cols, _p(np.ascontiguousarray(w)), _p(xq), T, _p(y))
         return y
 
     def route(self, router: np.ndarray, K: int, xn: np.ndarray):

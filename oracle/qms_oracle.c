@@ -301,6 +301,18 @@ void orc_matmul(int type, int64_t rows, int64_t cols, const uint8_t *w, const fl
     free(xq);
 }
 
+/* The same from activations already quantised, T rows of cols/32 blocks each: the reference
+ * quantises a slot's input once and dots every row against it (src/model.c:979-988). */
+void orc_matmul_q8(int type, int64_t rows, int64_t cols, const uint8_t *w, const OrcQ8 *xq, int T, float *y)
+{
+    const uint64_t rb = orc_row_bytes(type, cols);
+    const int64_t nb = cols / 32;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++)
+        for (int t = 0; t < T; t++)
+            y[(size_t)t * rows + r] = orc_vec_dot_q8(type, w + (uint64_t)r * rb, xq + (size_t)t * nb, cols);
+}
+
 /* Router softmax, top-k and renormalisation (src/model.c:1043-1064): double softmax over all
  * experts, top-k by repeated argmax with strict '>' (ties go to the lower index), then
  * weights (float)(p / sum of the selected p) in selection order. */

@@ -1,8 +1,8 @@
 """Expert parallelism (large_model_b200/ep.py): the dispatch / return / combine logic.
 
-CPU: two gloo ranks, the compute steps from the oracle (the reference's integer path restated in
-C: route, per-slot gate/up/SwiGLU/down, weighted sum); the sharded result must equal the same
-backend run unsharded on one process, bit for bit. GPU (two B200s, NCCL): shard layers through the
+CPU: two and four gloo ranks, the compute steps from the oracle (the reference's integer path
+restated in C: route, per-slot gate/up/SwiGLU/down, weighted sum); the sharded result (rows sent
+as Q8 blocks) must equal the same backend run unsharded on one process from fp32 rows, bit for bit. GPU (two B200s, NCCL): shard layers through the
 C ABI against the unsharded layer's grouped path.
 """
 from __future__ import annotations
@@ -52,6 +52,24 @@ class OracleBackend:
             dw = L.down[e * self.dn_bytes:(e + 1) * self.dn_bytes]
             g = self.o.matmul(L.gate_type, F, E, gw, row)[0]
             u = self.o.matmul(L.up_type, F, E, uw, row)[0]
+            dn[i] = self.o.matmul(L.down_type, E, F, dw, self.o.swiglu(g, u))[0]
+        return torch.from_numpy(dn)
+
+    def quantize(self, xn):
+        rows = [self.o.quantize_q8(r).view(np.uint8) for r in xn.numpy()]
+        return torch.from_numpy(np.stack(rows)) if rows else torch.empty((0, xn.shape[1] // 32 * 44), dtype=torch.uint8)
+
+    def experts_q8(self, xq, local_expert):
+        L, E, F = self.layer, self.layer.n_embd, self.layer.n_ff
+        dn = np.empty((xq.shape[0], E), np.float32)
+        for i, (row, le) in enumerate(zip(xq.numpy(), local_expert.tolist())):
+            assert 0 <= le < self.n_local
+            e = self.base + le
+            gw = L.gate[e * self.gu_bytes:(e + 1) * self.gu_bytes]
+            uw = L.up[e * self.gu_bytes:(e + 1) * self.gu_bytes]
+            dw = L.down[e * self.dn_bytes:(e + 1) * self.dn_bytes]
+            g = self.o.matmul_q8(L.gate_type, F, E, gw, row)[0]
+            u = self.o.matmul_q8(L.up_type, F, E, uw, row)[0]
             dn[i] = self.o.matmul(L.down_type, E, F, dw, self.o.swiglu(g, u))[0]
         return torch.from_numpy(dn)
 
@@ -169,10 +187,14 @@ def test_shards_on_one_gpu_match_unsharded(shape, T, parts):
     flat = sel.reshape(-1).long()
     dn = torch.empty((T * K, E), dtype=torch.float32, device="cuda")
     rows = xn.repeat_interleave(K, dim=0)
+    xq = lmb.quantize_q8(rows)
     for p, sh in enumerate(shards):
         idx = torch.nonzero(flat // per == p).flatten()
         if idx.numel():
-            dn[idx] = sh.experts(rows[idx].contiguous(), (flat[idx] % per).to(torch.int32).contiguous())
+            ids = (flat[idx] % per).to(torch.int32).contiguous()
+            dn[idx] = sh.experts(rows[idx].contiguous(), ids)
+            # the same rows sent as QmsQ8 blocks (the expert-parallel dispatch format)
+            assert torch.equal(sh.experts_q8(xq[idx].contiguous(), ids), dn[idx])
     out = lmb.combine(dn, wts)
     full = lmb.MoeLayer.from_synth(layer)
     ref, ref_sel, _, _ = full.route(xn)

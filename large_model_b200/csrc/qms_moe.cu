@@ -19,6 +19,8 @@
 #include <string.h>
 
 #include <algorithm>
+#include <thread>
+#include <vector>
 
 #include "qms_moe.cuh"
 #include "qms_router.cuh"
@@ -35,11 +37,12 @@ constexpr int kMmaMinT = 5;            // tokens from which the expert-grouped k
 
 // ---- load-time repack: GGUF rows -> staged layouts (qms_moe.cuh) --------------------------------
 // gate (which 0) / up (which 1) Q4_0 rows of a stacked [X][F] tensor -> chunks
-__global__ void k_repack_gu(const uint8_t *__restrict__ src, int64_t nrows, int nb, int F, int which, Chunked c,
-                            uint8_t *__restrict__ dst, size_t expert_bytes) {
+// (rows row0 .. row0 + nrows - 1 of the tensor; src points at row row0)
+__global__ void k_repack_gu(const uint8_t *__restrict__ src, int64_t row0, int64_t nrows, int nb, int F, int which,
+                            Chunked c, uint8_t *__restrict__ dst, size_t expert_bytes) {
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= nrows * nb) return;
-    const int64_t R = idx / nb;
+    const int64_t R = row0 + idx / nb;
     const int b = (int)(idx % nb);
     const int e = (int)(R / F), row = (int)(R % F);
     const uint16_t *s = reinterpret_cast<const uint16_t *>(src + idx * 18);
@@ -56,11 +59,11 @@ __global__ void k_repack_gu(const uint8_t *__restrict__ src, int64_t nrows, int 
 
 // down Q4_0 / Q4_1 rows of a stacked [X][E] tensor -> column stages; a Q4_1 block {d, m, qs[16]}
 // keeps d in the scale plane and m in the min plane
-__global__ void k_repack_dn(const uint8_t *__restrict__ src, int64_t nrows, int nb, int E, DnCols d,
+__global__ void k_repack_dn(const uint8_t *__restrict__ src, int64_t row0, int64_t nrows, int nb, int E, DnCols d,
                             uint8_t *__restrict__ dst, size_t expert_bytes) {
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= nrows * nb) return;
-    const int64_t R = idx / nb;
+    const int64_t R = row0 + idx / nb;
     const int b = (int)(idx % nb);
     const int e = (int)(R / E), row = (int)(R % E);
     const uint16_t *s = reinterpret_cast<const uint16_t *>(src + idx * (d.q1 ? 20 : 18)) + d.q1;
@@ -421,33 +424,94 @@ static int ensure_device(int dev) {
 
 // Upload one stacked expert tensor (host or device source) and repack it: which = 0 / 1 gate / up
 // rows into chunks, which = 2 down rows into column stages.
-static int upload_q4(const QmsCudaMoe *m, const void *src, int on_device, int which, uint8_t *dst) {
-    const int64_t nrows = (int64_t)m->n_local * (which == 2 ? m->E : m->F);
-    const int nb = which == 2 ? m->nbF : m->nbE;
-    const size_t bytes = (size_t)nrows * nb * (which == 2 && m->dcol.q1 ? 20 : 18);
-    const uint8_t *dsrc = (const uint8_t *)src;
-    uint8_t *tmp = nullptr;
-    if (!on_device) {
-        if (cudaMalloc(&tmp, bytes) != cudaSuccess) {
-            cudaGetLastError();
-            set_error("moe_create: cannot allocate %zu bytes of staging", bytes);
-            return QMS_CUDA_ENOMEM;
+// Host-memory uploads go through a ring of two pinned host buffers and two device buffers of
+// kStageBytes: host threads copy chunk i + 1 into pinned memory while chunk i's DMA and repack
+// run on the upload stream, so a layer streams at the link rate instead of through the driver's
+// pageable-copy path, and no device buffer the size of a whole tensor is needed.
+constexpr size_t kStageBytes = 64u << 20;
+constexpr int kStageThreads = 8;
+
+struct UploadRing {
+    uint8_t *h[2] = {nullptr, nullptr};   // pinned host
+    uint8_t *d[2] = {nullptr, nullptr};   // device
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    cudaStream_t s = nullptr;
+    size_t cap = 0;                       // bytes per buffer
+    int used[2] = {0, 0};
+
+    int open(size_t largest) {            // largest: bytes of the biggest tensor to upload
+        cap = std::min(kStageBytes, (largest + 4095) & ~(size_t)4095);
+        for (int i = 0; i < 2; i++) {
+            if (cudaHostAlloc(&h[i], cap, cudaHostAllocDefault) != cudaSuccess || cudaMalloc(&d[i], cap) != cudaSuccess ||
+                cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) != cudaSuccess) {
+                cudaGetLastError();
+                set_error("moe_create: cannot set up the %zu-byte upload ring", cap);
+                return QMS_CUDA_ENOMEM;
+            }
         }
-        const cudaError_t e = cudaMemcpy(tmp, src, bytes, cudaMemcpyHostToDevice);
-        if (e != cudaSuccess) {
-            cudaFree(tmp);
-            set_error("moe_create: upload failed: %s", cudaGetErrorString(e));
-            return QMS_CUDA_ECUDA;
-        }
-        dsrc = tmp;
+        QMS_CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+        return QMS_CUDA_OK;
     }
+    ~UploadRing() {
+        if (s) cudaStreamSynchronize(s);
+        for (int i = 0; i < 2; i++) {
+            if (h[i]) cudaFreeHost(h[i]);
+            if (d[i]) cudaFree(d[i]);
+            if (ev[i]) cudaEventDestroy(ev[i]);
+        }
+        if (s) cudaStreamDestroy(s);
+    }
+};
+
+// memcpy of n bytes split over up to kStageThreads host threads
+static void parallel_copy(uint8_t *dst, const uint8_t *src, size_t n) {
+    const int nt = (int)std::min<size_t>(kStageThreads, std::max<size_t>(1, n >> 22));
+    if (nt <= 1) {
+        memcpy(dst, src, n);
+        return;
+    }
+    std::vector<std::thread> th;
+    const size_t per = (n + nt - 1) / nt;
+    for (int t = 0; t < nt; t++) {
+        const size_t a = (size_t)t * per, b = std::min(n, a + per);
+        if (a < b) th.emplace_back([=] { memcpy(dst + a, src + a, b - a); });
+    }
+    for (auto &x : th) x.join();
+}
+
+static int launch_repack(const QmsCudaMoe *m, int which, const uint8_t *src, int64_t row0, int64_t nrows, uint8_t *dst,
+                         cudaStream_t s) {
+    const int nb = which == 2 ? m->nbF : m->nbE;
     const int64_t n = nrows * nb;
     const unsigned grid = (unsigned)((n + 255) / 256);
-    if (which == 2) k_repack_dn<<<grid, 256>>>(dsrc, nrows, nb, m->E, m->dcol, dst, m->dn_expert);
-    else k_repack_gu<<<grid, 256>>>(dsrc, nrows, nb, m->F, which, m->cgu, dst, m->gu_expert);
-    cudaError_t e = cudaGetLastError();
-    if (e == cudaSuccess) e = cudaDeviceSynchronize();
-    if (tmp) cudaFree(tmp);
+    if (which == 2) k_repack_dn<<<grid, 256, 0, s>>>(src, row0, nrows, nb, m->E, m->dcol, dst, m->dn_expert);
+    else k_repack_gu<<<grid, 256, 0, s>>>(src, row0, nrows, nb, m->F, which, m->cgu, dst, m->gu_expert);
+    QMS_CK(cudaGetLastError());
+    return QMS_CUDA_OK;
+}
+
+static int upload_q4(const QmsCudaMoe *m, const void *src, int on_device, int which, uint8_t *dst, UploadRing *ring) {
+    const int64_t nrows = (int64_t)m->n_local * (which == 2 ? m->E : m->F);
+    const int nb = which == 2 ? m->nbF : m->nbE;
+    const size_t rb = (size_t)nb * (which == 2 && m->dcol.q1 ? 20 : 18);
+    int rc;
+    if (on_device) {
+        if ((rc = launch_repack(m, which, (const uint8_t *)src, 0, nrows, dst, 0))) return rc;
+    } else {
+        const int64_t per = (int64_t)(ring->cap / rb);
+        int slot = 0;
+        for (int64_t r0 = 0; r0 < nrows; r0 += per, slot ^= 1) {
+            const int64_t nr = std::min<int64_t>(per, nrows - r0);
+            if (ring->used[slot]) QMS_CK(cudaEventSynchronize(ring->ev[slot]));   // its last DMA and repack are done
+            parallel_copy(ring->h[slot], (const uint8_t *)src + (size_t)r0 * rb, (size_t)nr * rb);
+            QMS_CK(cudaMemcpyAsync(ring->d[slot], ring->h[slot], (size_t)nr * rb, cudaMemcpyHostToDevice, ring->s));
+            if ((rc = launch_repack(m, which, ring->d[slot], r0, nr, dst, ring->s))) return rc;
+            QMS_CK(cudaEventRecord(ring->ev[slot], ring->s));
+            ring->used[slot] = 1;
+        }
+        QMS_CK(cudaStreamSynchronize(ring->s));
+    }
+    cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         set_error("moe_create: repack failed: %s", cudaGetErrorString(e));
         return QMS_CUDA_ECUDA;
@@ -532,9 +596,15 @@ static int create_impl(const QmsCudaMoeDesc *d, int base, int n_local, QmsCudaMo
             rc = QMS_CUDA_ECUDA;
         }
     }
-    if (rc == QMS_CUDA_OK) rc = upload_q4(m, d->gate, d->src_on_device, 0, m->gu);
-    if (rc == QMS_CUDA_OK) rc = upload_q4(m, d->up, d->src_on_device, 1, m->gu);
-    if (rc == QMS_CUDA_OK) rc = upload_q4(m, d->down, d->src_on_device, 2, m->dn);
+    {
+        UploadRing ring;
+        const size_t gu_bytes = (size_t)n_local * F * (E / 32) * 18;
+        const size_t dn_bytes = (size_t)n_local * E * (F / 32) * (m->dcol.q1 ? 20 : 18);
+        if (rc == QMS_CUDA_OK && !d->src_on_device) rc = ring.open(std::max(gu_bytes, dn_bytes));
+        if (rc == QMS_CUDA_OK) rc = upload_q4(m, d->gate, d->src_on_device, 0, m->gu, &ring);
+        if (rc == QMS_CUDA_OK) rc = upload_q4(m, d->up, d->src_on_device, 1, m->gu, &ring);
+        if (rc == QMS_CUDA_OK) rc = upload_q4(m, d->down, d->src_on_device, 2, m->dn, &ring);
+    }
     if (rc == QMS_CUDA_OK && down_smem(m) > 48 * 1024 &&
         cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)down_smem(m)) != cudaSuccess) {
         set_error("moe_create: %s", cudaGetErrorString(cudaGetLastError()));

@@ -41,7 +41,12 @@ constexpr int kMmaTm = QMS_MMA_TMEM_BUFS;  // TMEM int32 buffers (64 columns eac
 #define QMS_MMA_CONV_WARPS 4
 #endif
 constexpr int kMmaConvWarps = QMS_MMA_CONV_WARPS;   // Q4 -> int8 converter warps (4: one row per thread)
-constexpr int kMmaEpiWarps = 8;                     // 2 per TMEM lane quarter, 32 columns each
+#ifndef QMS_MMA_EPI_WARPS
+#define QMS_MMA_EPI_WARPS 16
+#endif
+constexpr int kMmaEpiWarps = QMS_MMA_EPI_WARPS;     // per TMEM lane quarter kMmaEpiWarps / 4 column groups
+constexpr int kMmaColGroups = kMmaEpiWarps / 4;
+static_assert(kMmaEpiWarps % 4 == 0, "whole lane quarters");
 constexpr int kMmaEpi0 = 2 + kMmaConvWarps;         // first epilogue warp
 constexpr int kMmaThreads = (2 + kMmaConvWarps + kMmaEpiWarps) * 32;   // warp 0 TMA, 1 MMA, converters, epilogue
 static_assert(kMmaConvWarps * 32 == kMmaM, "one A row per converter thread");
@@ -85,7 +90,7 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// 32 TMEM lanes (this warp's quarter) x C consecutive 32-bit columns, C = 8 or 32 (not waited).
+// 32 TMEM lanes (this warp's quarter) x C consecutive 32-bit columns, C = 4, 8, 16 or 32 (not waited).
 template <int C>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[C]) {
     if constexpr (C == 32) {
@@ -97,10 +102,20 @@ __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[C]) {
               "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
               "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
             : "r"(taddr));
-    } else {
-        static_assert(C == 8, "8 or 32 columns");
+    } else if constexpr (C == 16) {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(taddr));
+    } else if constexpr (C == 8) {
         asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                     : "r"(taddr));
+    } else {
+        static_assert(C == 4, "4, 8, 16 or 32 columns");
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                      : "r"(taddr));
     }
 }
@@ -226,7 +241,7 @@ __host__ __device__ inline uint32_t raw_a_bytes(bool gu, uint32_t chunk_bytes, i
 
 template <bool GU, bool Q1, int NW>
 __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
-    constexpr int EC = NW / 2;                                  // columns per epilogue warp
+    constexpr int EC = NW / kMmaColGroups;                      // columns per epilogue warp
     constexpr uint32_t BT = NW * 32;                            // one block of the B operand
     extern __shared__ __align__(1024) uint8_t smem[];
     const int SB = a.SB, nb = a.nb;
@@ -242,7 +257,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
     uint64_t *raw_full = bars, *raw_empty = raw_full + kMmaRaw;
     uint64_t *a_full = raw_empty + kMmaRaw, *a_empty = a_full + kMmaA;
     uint64_t *tm_full = a_empty + kMmaA, *tm_empty = tm_full + kMmaTm;
-    float *xch = reinterpret_cast<float *>(raw);               // after the K loop: [2][2][32][EC + 1] up sums
+    float *xch = reinterpret_cast<float *>(raw);               // after the K loop: [2][groups][32][EC + 1] up sums
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
 
@@ -414,7 +429,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
     } else {                                                    // ---- epilogue: 8 warps
         // two blocks per pass: one wait, one TMEM round trip and one release per pair, so the
         // per-block bookkeeping stays small next to the 2 x EC columns of scaling
-        const int q = warp & 3, cq = (warp - kMmaEpi0) >> 2, R = 32 * q + lane;   // lane quarter, column half (EC columns)
+        const int q = warp & 3, cq = (warp - kMmaEpi0) >> 2, R = 32 * q + lane;   // lane quarter, column group (EC columns)
         float acc[EC];
 #pragma unroll
         for (int j = 0; j < EC; j++) acc[j] = 0.0f;
@@ -487,7 +502,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_gemm(const MmaArgs a) {
             // rows 0-31 / 64-95 (lane quarters 0, 2) are gate rows f, 32-63 / 96-127 the up rows of
             // the same f: the up warps hand their sums over, the gate warps finish the groups
             const int th = q >> 1;                                // which 64-row tile
-            float *xu = xch + ((th * 2 + cq) * 32 + lane) * (EC + 1);
+            float *xu = xch + ((th * kMmaColGroups + cq) * 32 + lane) * (EC + 1);
             if (q & 1)
 #pragma unroll
                 for (int j = 0; j < EC; j++) xu[j] = acc[j];

@@ -255,7 +255,7 @@ struct MmaWork {
 // <= 24 slots per call (16-slot tiles)
 int gv_supported(const QmsCudaMoe *m);
 int gv_prepare(QmsCudaMoe *m);
-int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int maxT, int S, int rdiv, float *dn, float *dn2, bool sum_halves,
-             cudaStream_t s);
+int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int maxT, int S, int nx, int rdiv, float *dn, float *dn2,
+             bool sum_halves, cudaStream_t s);
 
 }  // namespace qms

@@ -523,11 +523,25 @@ __global__ void __launch_bounds__(kGvThreads, 1) k_gv_down(const GvArgs a) {
     }
 }
 
-// dn[i] += dn2[i]: the two K halves of the down rows into one (expert-parallel entry point)
-__global__ void __launch_bounds__(256) k_gv_add(float *__restrict__ dn, const float *__restrict__ dn2, int64_t n) {
+// dn[s] += dn2[s] for every grouped slot s (rows whose expert id was out of range stay as they
+// were): the two K halves of the down rows into one (expert-parallel entry point). nx experts.
+__global__ void __launch_bounds__(256) k_gv_add(float *__restrict__ dn, const float *__restrict__ dn2, MmaWork w,
+                                                int nx, int E) {
     pdl_wait();
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        dn[i] = __fadd_rn(dn[i], __ldcg(dn2 + i));
+    const int nvalid = __ldcg(w.off + nx - 1) + __ldcg(w.cnt + nx - 1);
+    const int q = E / 4;                                    // float4 per row
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)nvalid * q;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int r = (int)(i / q), c = (int)(i - (int64_t)r * q);
+        const size_t at = (size_t)__ldcg(w.slots + r) * q + c;
+        float4 a = reinterpret_cast<float4 *>(dn)[at];
+        const float4 b = __ldcg(reinterpret_cast<const float4 *>(dn2) + at);
+        a.x = __fadd_rn(a.x, b.x);
+        a.y = __fadd_rn(a.y, b.y);
+        a.z = __fadd_rn(a.z, b.z);
+        a.w = __fadd_rn(a.w, b.w);
+        reinterpret_cast<float4 *>(dn)[at] = a;
+    }
 }
 
 // ---- host side -------------------------------------------------------------------------------------
@@ -576,8 +590,8 @@ int gv_prepare(QmsCudaMoe *m) {
 // gate/up + SwiGLU + Q8 into m's aq scratch, then the two K halves of the down rows into dn and
 // dn2, for the slots grouped in w (at most maxT tiles of kGvSlots); activation row of slot s: s / rdiv
 // of m's xq scratch. With sum_halves the second half is added into dn (S slots).
-int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int maxT, int S, int rdiv, float *dn, float *dn2, bool sum_halves,
-             cudaStream_t s) {
+int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int maxT, int S, int nx, int rdiv, float *dn, float *dn2,
+             bool sum_halves, cudaStream_t s) {
     QMS_REQUIRE(maxT <= kGvMaxTiles, QMS_CUDA_EINVAL, "moe: %d tiles exceed the grouped GEMV's %d", maxT, kGvMaxTiles);
     GvArgs g;
     memset(&g, 0, sizeof g);
@@ -626,9 +640,9 @@ int gv_gemms(QmsCudaMoe *m, const MmaWork &w, int maxT, int S, int rdiv, float *
         else QMS_CK(launch_pdl(k_gv_down<false, 1>, grid, block, sm, s, d));
     }
     if (sum_halves) {
-        const int64_t n = (int64_t)S * m->E;
-        QMS_CK(launch_pdl(k_gv_add, dim3((unsigned)std::min<int64_t>((n + 1023) / 1024, 4 * m->nsm)), dim3(256), 0, s,
-                          dn, (const float *)dn2, n));
+        const int64_t n = (int64_t)S * m->E / 4;
+        QMS_CK(launch_pdl(k_gv_add, dim3((unsigned)std::min<int64_t>((n + 255) / 256, 4 * m->nsm)), dim3(256), 0, s,
+                          dn, (const float *)dn2, w, nx, m->E));
     }
     return QMS_CUDA_OK;
 }

@@ -672,7 +672,7 @@ static int mma_core(QmsCudaMoe *m, int S, const int *sel, int nx, int rdiv, floa
     const int nw = mma_width(S, nx), maxT = S / nw + nx;
     QMS_CK(launch_pdl(k_mma_group, dim3(1), dim3(1024), 0, s, sel, S, nx, maxT, nw, w));
     if (m->gemv && nw == kMmaNs)                       // few slots per expert: CUDA cores
-        return gv_gemms(m, w, maxT, S, rdiv, w.dn, w.dn2, dn != nullptr, s);
+        return gv_gemms(m, w, maxT, S, nx, rdiv, w.dn, w.dn2, dn != nullptr, s);
     QMS_CK(launch_pdl(k_mma_gather, dim3(maxT, 8), dim3(2 * nw), 0, s, (const int8_t *)m->xq_q, (const float *)m->xq_d,
                       (const int *)nullptr, m->nbE, rdiv, nw, w));
     MmaArgs g;

@@ -209,3 +209,32 @@ def test_shards_on_one_gpu_match_unsharded(shape, T, parts):
     for sh in shards:
         sh.close()
     full.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("S", [24, 600])
+def test_experts_leave_out_of_range_rows(S):
+    """qms_cuda_moe_experts / _experts_q8 skip rows whose local expert id is out of range (their dn
+    rows keep what the caller put there) and the other rows come out as in a run without them.
+    S = 24 slots over 16 local experts runs the grouped GEMV, S = 600 the tensor-core GEMMs."""
+    import large_model_b200 as lmb
+    lmb.init(0)
+    layer = synth.make_moe_layer("tiny", seed=45)
+    per = layer.n_expert // 2
+    sh = lmb.MoeLayer.shard_from_synth(layer, 0, per)
+    g = torch.Generator().manual_seed(3)
+    x = torch.from_numpy(synth.make_hidden(layer.n_embd, S, seed=46)).cuda()
+    ids = torch.randint(0, per, (S,), generator=g).to(torch.int32)
+    r = torch.arange(S)
+    bad = r % 5 == 0
+    ids[bad] = torch.where(r[bad] % 2 == 0, torch.full_like(r[bad], -1), torch.full_like(r[bad], per + 3)).to(torch.int32)
+    ids, badc, okc = ids.cuda(), bad.cuda(), (~bad).cuda()
+    ref = sh.experts(x[okc].contiguous(), ids[okc].contiguous())
+    for run, rows in ((sh.experts, x), (sh.experts_q8, lmb.quantize_q8(x))):
+        dn = torch.full((S, layer.n_embd), 7.0, device="cuda")
+        run(rows, ids, dn=dn)
+        torch.cuda.synchronize()
+        sh.status()
+        assert torch.all(dn[badc] == 7.0)
+        assert torch.equal(dn[okc], ref)
+    sh.close()

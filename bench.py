@@ -16,9 +16,10 @@ decode does not shard, so there is no collective on the data path (scaling "weak
     python bench.py --mode bs64      # the same layer at T=64 tokens per call (config 4's bs64 operator)
     python bench.py --mode prefill   # T=4096 tokens per call (config 5's operator, per sequence)
 
-The batched modes run the expert-grouped tcgen05 GEMMs and print their own JSON line (bs64: HBM
-roofline over the distinct experts a call reads; prefill: int8 tensor roofline over the block's
-integer ops).
+The batched modes print their own JSON line: bs64 runs the expert-grouped GEMV (HBM roofline over
+the distinct experts a call reads), prefill the expert-grouped tcgen05 GEMMs (int8 tensor roofline
+over the block's integer ops). Under torch.distributed.run, `--ep` shards the experts over the
+ranks (NCCL all-to-all of the slots' Q8 rows) instead of running replicas.
 """
 from __future__ import annotations
 
@@ -365,6 +366,11 @@ def run_batched(a):
                "h2d_bytes_per_step": T * E * 4, "d2h_bytes_per_step": T * E * 4,
                "note": "per rank: its T tokens from pinned host memory, ExpertParallelMoe.forward, result to "
                        "pinned host memory; max over ranks"}
+    # kernels of this library per call (the routing, grouping, expert and combine kernels of the path
+    # the call takes; torch's own copies and all-to-alls under EP not counted)
+    gemv = T * K <= 24 * (X // world if ep else X)
+    per_call = (10 if gemv else 12) if ep else (7 if gemv else 9)
+    launches = per_call * calls * a.steps
     if rank == 0:
         if a.mode == "bs64":
             peak, peak_kind = peaks()
@@ -399,7 +405,7 @@ def run_batched(a):
                            "parallelism": f"expert-parallel x{world} (NCCL all-to-all)" if ep else f"replicas x{world}"},
                 "roofline": roof, "cpu_baseline": cpu,
                 "e2e": e2e,
-                "gpu_launches": None, "clocks": clocks}
+                "gpu_launches": launches, "clocks": clocks}
         print(json.dumps(line), flush=True)
     for m in layers:
         m.close()

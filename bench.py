@@ -369,7 +369,7 @@ def run_batched(a):
     # kernels of this library per call (the routing, grouping, expert and combine kernels of the path
     # the call takes; torch's own copies and all-to-alls under EP not counted)
     gemv = T * K <= 24 * (X // world if ep else X)
-    per_call = (10 if gemv else 12) if ep else (7 if gemv else 9)
+    per_call = (10 if gemv else 11) if ep else (7 if gemv else 9)
     launches = per_call * calls * a.steps
     if rank == 0:
         if a.mode == "bs64":

@@ -133,6 +133,17 @@ int qms_cuda_moe_experts_q8(QmsCudaMoe *m, const QmsQ8 *xq, const int *expert, i
 int qms_cuda_moe_combine(const float *dn, const float *wts, int T, int n_used, int n_embd, const float *resid,
                          float *out, void *stream);
 
+/* ---- chat path: token sampling on the device (src/chat.c:27-69) -------------------------------- */
+
+/* One draw of the reference's sampler, sample() (src/chat.c:36-69), on device memory: logits
+ * [vocab] fp32; temp <= 0 gives the argmax (first index among equal maxima); otherwise the K
+ * largest logits (K = top_k when 0 < top_k < vocab, else min(vocab, 1024)), weights
+ * exp((l - l_max) / temp) in double, the top-p prefix and one pcg32 draw (chat.c:27-33) from
+ * *rng, which is advanced. rng (device uint64) may be NULL when temp <= 0; *token (device int)
+ * receives the id. K above 1024 is QMS_CUDA_EUNSUPPORTED. Logits must be finite. */
+int qms_cuda_sample(const float *logits, int vocab, float temp, float top_p, int top_k, uint64_t *rng,
+                    int *token, void *stream);
+
 /* Waits for the device and reports whether any bounded wait inside the layer's kernels gave up
  * since the last call (QMS_CUDA_ETIMEOUT; the outputs of the affected call are invalid), then
  * clears the flag. The batch-1 kernels never spin without a limit, so a stuck pipeline turns into

@@ -74,6 +74,7 @@ def lib() -> C.CDLL:
     L.qms_cuda_moe_route.argtypes = [vp, vp, i32, vp, vp, vp, vp]
     L.qms_cuda_moe_experts.argtypes = [vp, vp, vp, i32, vp, vp]
     L.qms_cuda_moe_experts_q8.argtypes = [vp, vp, vp, i32, vp, vp]
+    L.qms_cuda_sample.argtypes = [vp, i32, C.c_float, C.c_float, i32, vp, vp, vp]
     L.qms_cuda_moe_combine.argtypes = [vp, vp, i32, i32, i32, vp, vp, vp]
     _lib = L
     return L
@@ -124,6 +125,18 @@ def quantize_q8(x):
     out = torch.empty((rows, n // 32 * 44), dtype=torch.uint8, device=x.device)
     check(lib().qms_cuda_quantize_q8(_ptr(x), n, rows, _ptr(out), _stream()))
     return out
+
+
+def sample(logits, temp: float, top_p: float, top_k: int, rng=None, token=None, stream=None):
+    """One draw of the chat sampler on the device (qms_cuda_sample): logits CUDA float32 [vocab];
+    rng a CUDA int64 [1] holding the uint64 generator state (advanced in place; may be None when
+    temp <= 0). Returns the CUDA int32 [1] token tensor."""
+    torch = _torch()
+    if token is None:
+        token = torch.empty((1,), dtype=torch.int32, device=logits.device)
+    check(lib().qms_cuda_sample(_ptr(logits.contiguous()), logits.numel(), float(temp), float(top_p), int(top_k),
+                                _ptr(rng), _ptr(token), _stream(stream)))
+    return token
 
 
 def matvec_q8(typ: int, w, rows: int, cols: int, xq, T: int):

@@ -61,6 +61,8 @@ class Oracle:
         L.orc_vec_dot_f32.restype = C.c_float
         L.orc_matmul.argtypes = [i32, i64, i64, vp, vp, i32, vp]
         L.orc_matmul_q8.argtypes = [i32, i64, i64, vp, vp, i32, vp]
+        L.orc_sample.argtypes = [vp, i32, C.c_float, C.c_float, i32, C.POINTER(C.c_uint64)]
+        L.orc_sample.restype = i32
         L.orc_route.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp]
         L.orc_moe.argtypes = [vp, vp, i32, vp, vp, vp, vp]
         L.orc_moe.restype = i32
@@ -106,6 +108,13 @@ class Oracle:
         y = np.empty((T, rows), np.float32)
         self.lib.orc_matmul_q8(typ, rows, cols, _p(np.ascontiguousarray(w)), _p(xq), T, _p(y))
         return y
+
+    def sample(self, logits: np.ndarray, temp: float, top_p: float, top_k: int, rng: int) -> tuple[int, int]:
+        """The chat sampler (src/chat.c:36-69) restated: (token, advanced rng state)."""
+        l = np.ascontiguousarray(logits, np.float32)
+        st = C.c_uint64(rng)
+        t = self.lib.orc_sample(_p(l), l.size, temp, top_p, top_k, C.byref(st))
+        return t, st.value
 
     def route(self, router: np.ndarray, K: int, xn: np.ndarray):
         X, E = router.shape
@@ -239,3 +248,22 @@ class Reference:
 
 def host_threads() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+class RefSampler:
+    """The reference's own sample() (src/chat.c:36-69) from oracle/_ref/libqms_ref_sample.so."""
+
+    def __init__(self):
+        path = HERE / "_ref" / "libqms_ref_sample.so"
+        if not path.exists():
+            raise FileNotFoundError(f"{path} is missing: make -C oracle ref")
+        self.lib = C.CDLL(str(path))
+        self.lib.ref_sample.argtypes = [C.c_void_p, C.c_int, C.c_float, C.c_float, C.c_int, C.POINTER(C.c_uint64)]
+        self.lib.ref_sample.restype = C.c_int
+
+    def sample(self, logits: np.ndarray, temp: float, top_p: float, top_k: int, rng: int) -> tuple[int, int]:
+        l = np.ascontiguousarray(logits, np.float32)
+        st = C.c_uint64(rng)
+        t = self.lib.ref_sample(l.ctypes.data_as(C.c_void_p), l.size, temp, top_p, top_k, C.byref(st))
+        return t, st.value
+

@@ -414,3 +414,66 @@ int orc_moe(const OrcMoe *L, const float *xn, int T, float *out, int *sel_out, f
     (void)nbF;
     return 0;
 }
+
+/* ---- token sampler (src/chat.c:27-69) ------------------------------------------------------ */
+/* PCG-XSH-RR step of the chat sampler's generator (chat.c:27-33). */
+static uint32_t orc_pcg32(uint64_t *s)
+{
+    const uint64_t x = *s;
+    *s = x * 6364136223846793005ull + 1442695040888963407ull;
+    const uint32_t v = (uint32_t)(((x >> 18) ^ x) >> 27);
+    const uint32_t r = (uint32_t)(x >> 59);
+    return (v >> r) | (v << ((32u - r) & 31u));
+}
+
+/* Restatement of sample() (chat.c:36-69): argmax when temp <= 0 (first maximum); otherwise the
+ * K largest logits (K = top_k when 0 < top_k < V, else min(V, 1024)) ordered by value descending,
+ * lower index first among equals; weights exp((l_j - l_0) / temp) in double; the shortest prefix
+ * whose normalised cumulative weight reaches top_p; one pcg32 draw scaled by that prefix's weight
+ * picks the token. *rng advances once per tempered draw. */
+int orc_sample(const float *l, int V, float temp, float top_p, int top_k, uint64_t *rng)
+{
+    int best = 0;
+    for (int i = 1; i < V; i++)
+        if (l[i] > l[best]) best = i;
+    if (temp <= 0.0f) return best;
+    const int K = (top_k > 0 && top_k < V) ? top_k : (V < 1024 ? V : 1024);
+    int *ix = (int *)malloc((size_t)K * sizeof(int));
+    double *w = (double *)malloc((size_t)K * sizeof(double));
+    int n = 0;
+    for (int i = 0; i < V; i++) {                 /* sorted insertion, ties keep the lower index first */
+        if (n == K && !(l[i] > l[ix[K - 1]])) continue;
+        int j = n < K ? n++ : K - 1;
+        for (; j > 0 && l[ix[j - 1]] < l[i]; j--) ix[j] = ix[j - 1];
+        ix[j] = i;
+    }
+    double z = 0.0;
+    for (int j = 0; j < n; j++) {
+        w[j] = exp(((double)l[ix[j]] - (double)l[ix[0]]) / (double)temp);
+        z += w[j];
+    }
+    int keep = n;
+    double c = 0.0;
+    for (int j = 0; j < n; j++) {
+        c += w[j] / z;
+        if (c >= (double)top_p) {
+            keep = j + 1;
+            break;
+        }
+    }
+    double zk = 0.0;
+    for (int j = 0; j < keep; j++) zk += w[j];
+    const double r = ((double)orc_pcg32(rng) / 4294967296.0) * zk;
+    int pick = ix[keep - 1];
+    double acc = 0.0;
+    for (int j = 0; j < keep; j++) {
+        acc += w[j];
+        if (r < acc) {
+            pick = ix[j];
+            break;
+        }
+    }
+    free(ix);
+    free(w);
+    return pick;
+}

@@ -44,6 +44,8 @@ float    orc_vec_dot_q8(int type, const uint8_t *w, const OrcQ8 *x, int64_t n);
 float    orc_vec_dot_f32(const float *w, const float *x, int64_t n);
 /* y[t][r] = W[r] . x[t] through the integer path (F32 weights: fp32 dot). */
 void     orc_matmul(int type, int64_t rows, int64_t cols, const uint8_t *w, const float *x, int T, float *y);
+void     orc_matmul_q8(int type, int64_t rows, int64_t cols, const uint8_t *w, const OrcQ8 *xq, int T, float *y);
+int      orc_sample(const float *logits, int V, float temp, float top_p, int top_k, uint64_t *rng);
 /* Router: logits, top-k ids in selection order, renormalised weights. */
 void     orc_route(const float *router, int n_expert, int n_embd, int n_used, const float *xn, int T,
                    float *logits, int *sel, float *wts);

@@ -111,3 +111,25 @@ def moe_cases() -> dict:
     mid = synth.make_moe_layer((1024, 64, 8, 512), seed=9)
     out["mid_t2"] = (mid, synth.make_hidden(mid.n_embd, 2, seed=10))
     return out
+
+
+def sampler_cases() -> dict:
+    """Logit rows and sampler settings for the chat sampler (src/chat.c:36-69): vocabularies from
+    5 to Qwen3's 151,936, ties at the top and rows of rounded values (many ties at the K-th),
+    greedy, default top_k (0 -> 1024), small and large top_k, top_p below and at 1."""
+    rng = np.random.default_rng(90)
+    out = {}
+    for i in range(48):
+        V = int([5, 37, 1000, 4096, 151936][i % 5])
+        scale = float([0.5, 2.0, 8.0][i % 3])
+        l = (rng.standard_normal(V) * scale).astype(np.float32)
+        if i % 7 == 0:
+            l[rng.integers(0, V, 6)] = l.max()
+        if i % 6 == 1:
+            l = np.round(l).astype(np.float32)
+        temp = float([0.0, 0.3, 0.7, 1.0, 1.5][i % 5 if i % 9 else 0])
+        top_p = float([0.5, 0.9, 0.95, 1.0][i % 4])
+        top_k = int([0, 1, 5, 40, 1024, 0][i % 6])
+        seed = int(rng.integers(0, 2**63))
+        out[f"s{i:02d}"] = (l, temp, top_p, top_k, seed)
+    return out

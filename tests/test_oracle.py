@@ -126,3 +126,39 @@ def test_moe_rejects_non_fast_shapes(oracle):
     layer = synth.make_moe_layer((288, 4, 2, 64), seed=1)   # 288 % 256 != 0: reference uses exact math
     with pytest.raises(ValueError):
         oracle.moe(layer, synth.make_hidden(288, 1))
+
+
+def _sampler_golden():
+    from conftest import ROOT
+    return np.load(ROOT / "tests" / "golden" / "sampler_golden.npz")
+
+
+def test_sampler_golden(oracle):
+    """The restated chat sampler (src/chat.c:36-69) against the reference's own draws: same
+    token and same generator state after each of two draws in a row."""
+    g = _sampler_golden()
+    for name, (l, temp, top_p, top_k, seed) in cases.sampler_cases().items():
+        assert str(g[f"{name}/sha"]) == cases.sha(l), f"{name}: input generation drifted"
+        st = seed
+        for k in range(2):
+            t, st = oracle.sample(l, temp, top_p, top_k, st)
+            assert t == int(g[f"{name}/tokens"][k]), f"{name} draw {k}"
+            assert st == int(g[f"{name}/states"][k]), f"{name} draw {k}: generator state"
+
+
+def test_sampler_random_vs_reference(oracle):
+    """More seeded draws straight against the reference build, where it is present."""
+    from oracle import RefSampler
+    try:
+        ref = RefSampler()
+    except FileNotFoundError:
+        pytest.skip("oracle/_ref/libqms_ref_sample.so is not present")
+    rng = np.random.default_rng(7)
+    for i in range(200):
+        V = int(rng.choice([3, 64, 3000, 151936]))
+        l = (rng.standard_normal(V) * rng.choice([0.3, 3.0])).astype(np.float32)
+        if i % 5 == 0:
+            l = np.round(l * 2).astype(np.float32)
+        args = (float(rng.choice([0.0, 0.5, 1.0, 2.0])), float(rng.choice([0.3, 0.9, 1.0])),
+                int(rng.choice([0, 2, 50, 1024, 3000])), int(rng.integers(0, 2**63)))
+        assert oracle.sample(l, *args) == ref.sample(l, *args), f"case {i}"

@@ -66,6 +66,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const float *__res
                                                               float top_p, int K, uint64_t *rng, int *token) {
     __shared__ unsigned long long s_k[kSampleMaxK];       // (~key << 32) | index, sorted ascending
     __shared__ double s_w[kSampleMaxK];
+    __shared__ double s_q[kSampleMaxK];                    // s_w / z
     __shared__ unsigned s_hist[256];
     __shared__ int s_warp[32];
     __shared__ float s_bv[32];
@@ -193,12 +194,13 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const float *__res
         s_z = z;
     }
     __syncthreads();
+    if (tid < K) s_q[tid] = __ddiv_rn(s_w[tid], s_z);       // IEEE division: the host's quotients
+    __syncthreads();
     if (tid == 0) {
-        const double z = s_z;
         int keep = K;
         double c = 0.0;
         for (int j = 0; j < K; j++) {
-            c = __dadd_rn(c, __ddiv_rn(s_w[j], z));
+            c = __dadd_rn(c, s_q[j]);
             if (c >= (double)top_p) {
                 keep = j + 1;
                 break;

@@ -11,6 +11,7 @@
  *   qms_vec_dot_q8/qms_matmul  src/kernels.h:19, src/quant.h:23-26 (src/quant.c:128-170)
  *   qms_vec_dot_f32            src/kernels.h:21   (src/kernels.c:202-221)
  *   moe()                      src/model.c:1032-1167, called from qms_forward (src/model.c:1284)
+ *   sample() (chat sampler)    src/chat.c:36-69 with pcg32() src/chat.c:27-33
  */
 #ifndef QMS_CUDA_H
 #define QMS_CUDA_H

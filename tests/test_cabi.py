@@ -56,6 +56,12 @@ def test_kernel_calls_validate_arguments():
     assert L.qms_cuda_matvec_q8(q.T_Q8_0, C.c_void_p(16), 4, 32, C.c_void_p(16), 1, C.c_void_p(16), None) == q.EUNSUPPORTED
     assert L.qms_cuda_matvec_q8(q.T_Q6_K, C.c_void_p(16), 4, 32, C.c_void_p(16), 1, C.c_void_p(16), None) == q.EINVAL
     assert L.qms_cuda_moe_forward(None, None, 1, None, None, None, None, None, None) == q.EINVAL
+    assert L.qms_cuda_moe_experts(None, None, None, 4, None, None) == q.EINVAL
+    assert L.qms_cuda_moe_experts_q8(None, None, None, 4, None, None) == q.EINVAL
+    p = C.c_void_p(16)
+    assert L.qms_cuda_sample(None, 10, 1.0, 0.9, 0, p, p, None) == q.EINVAL          # no logits
+    assert L.qms_cuda_sample(p, 10, 1.0, 0.9, 0, None, p, None) == q.EINVAL           # tempered draw without a state
+    assert L.qms_cuda_sample(p, 5000, 1.0, 0.9, 2000, p, p, None) == q.EUNSUPPORTED   # more than 1024 candidates
 
 
 def test_init_without_gpu_fails_loudly():

@@ -7,14 +7,17 @@
 //                  in the reference's exact F32 order (src/kernels.c:202-219); the last CTA to
 //                  finish does softmax / top-k / renormalisation (src/model.c:1045-1064).
 //   larger T       k_quantize_rows, k_router_tiled (the same exact-order logits, tiled over
-//                  32 tokens x 32 experts in shared memory), k_moe_topk (one CTA per token).
+//                  up to 32 tokens x 32 experts in shared memory), k_moe_topk (one CTA per token).
+// T >= 5 then runs the expert-grouped kernels (qms_moe_gemv.cu while experts average <= 24 slots,
+// qms_moe_mma.cu above); T = 2..4 the per-slot kernels below:
 //   k_moe_gate_up  one warp per (slot, f): gate row f and up row f of the slot's expert against
 //                  the token's Q8 row (phase 1, :979-988), a = silu(g) * u (:994); the CTA that
 //                  completes a 32-row group re-quantises it to Q8 (phase 2, :995).
 //   k_moe_down     one CTA per (token, 32 output rows): down rows of all n_used experts
 //                  (phase 3, :998-1005), then the weighted sum in selection order with one
 //                  fused multiply-add per expert (:1152-1162), plus the optional residual.
-// Expert weights are repacked at load into the staged layouts of qms_moe.cuh.
+// Expert weights are repacked at load into the staged layouts of qms_moe.cuh; from host memory
+// they stream through a pinned staging ring (upload_q4).
 #include <stdlib.h>
 #include <string.h>
 

@@ -1,19 +1,22 @@
-// qms_moe_mma.cu - the MoE block for T > 1 tokens (batched decode, prefill) on tcgen05 tensor
-// cores: expert-grouped GEMMs, one kind::i8 MMA per 32-element block, per-block scale epilogue.
+// qms_moe_mma.cu - the MoE block for T >= 5 tokens (batched decode, prefill): slot grouping, and
+// the expert-grouped GEMMs on tcgen05 tensor cores, one kind::i8 MMA per 32-element block with a
+// per-block scale epilogue.
 //
 // The reference's moe_group_fast (src/model.c:969-1007) groups the T*K (token, expert) slots by
 // expert (:1066-1088) and runs each expert's gate/up rows and down rows once over all of its slots.
-// Here every (expert, 64-slot tile) pair is one GEMM column tile:
-//   k_mma_group    counting sort of the slots by expert; tile list (expert, first slot)
+// Here every (expert, NW-slot tile) pair is one GEMM column tile (NW = 16 while the experts average
+// <= 24 slots, else 64; the 16-slot calls go to the grouped GEMV of qms_moe_gemv.cu when it covers
+// the shape):
+//   k_mma_group    counting sort of the slots by expert; tile list (expert, tile index)
 //   k_mma_gather   each tile's activations as MMA operands: the slots' Q8 rows rearranged into the
-//                  tensor core's K-major core-matrix layout (one 2 KB block per 32 values), plus
-//                  the per-block activation scales (and block sums for Q4_1 down)
-//   k_gu_mma       128 gate/up rows x 64 slots per CTA: per 32-block, converter warps expand the
+//                  tensor core's K-major core-matrix layout (one block of NW x 32 bytes per 32
+//                  values), plus the per-block activation scales (and block sums for Q4_1 down)
+//   k_mma_gemm<GU> 128 gate/up rows x NW slots per CTA: per 32-block, converter warps expand the
 //                  Q4_0 nibbles to int8 (q - 8), one thread issues tcgen05.mma kind::i8 into a
-//                  TMEM buffer (int32, exact), and 8 epilogue warps add P * (d_w * d_x) into fp32
+//                  TMEM buffer (int32, exact), and 16 epilogue warps add P * (d_w * d_x) into fp32
 //                  registers in block order (the reference's per-block scaling, src/kernels.c:82-107).
 //                  Then silu(g) * u and its Q8 groups per slot (src/model.c:989-997).
-//   k_dn_mma       128 down rows x 64 slots per CTA, the same pipeline over the F/32 blocks of the
+//   k_mma_gemm<dn> 128 down rows x NW slots per CTA, the same pipeline over the F/32 blocks of the
 //                  SwiGLU activations (Q4_1 down: q and the block sums, d q + m).
 //   k_mma_combine  out[t] = sum_j w[t][j] * dn[t*K + j] in selection order (+ residual).
 // A 32-block's int32 dot product is exact, so the per-block scaling happens in fp32 exactly as in

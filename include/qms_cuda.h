@@ -22,8 +22,11 @@
 extern "C" {
 #endif
 
-/* ggml tensor type ids, GGUF numbering (src/gguf.h:8-10). */
+/* ggml tensor type ids, GGUF numbering (src/gguf.h:8-10). A translation unit that also includes
+ * the reference's gguf.h (include guard QMS_GGUF_H) gets the same values from there. */
+#ifndef QMS_GGUF_H
 enum { QMS_T_F32 = 0, QMS_T_F16 = 1, QMS_T_Q4_0 = 2, QMS_T_Q4_1 = 3, QMS_T_Q8_0 = 8, QMS_T_Q6_K = 14 };
+#endif
 
 /* Status codes. */
 enum {
@@ -37,13 +40,16 @@ enum {
 };
 
 /* Activation block: 32 int8 values with one fp32 scale; same 44-byte layout as the
- * reference's QmsQ8 (src/kernels.h:7-12). */
+ * reference's QmsQ8 (src/kernels.h:7-12), which a translation unit that includes the reference's
+ * kernels.h (include guard QMS_KERNELS_H) uses instead. */
+#ifndef QMS_KERNELS_H
 typedef struct {
     float d;         /* scale: x ~= q * d */
     float ds;        /* d * sum(q[0..31]) */
     int16_t s16[2];  /* sum(q[0..15]), sum(q[16..31]) */
     int8_t q[32];
 } QmsQ8;
+#endif
 
 /* ---- library ---------------------------------------------------------------------------- */
 
@@ -163,6 +169,88 @@ int qms_cuda_moe_set_kernel_events(QmsCudaMoe *m, void **events);
  * runs, copies out and waits; the drop-in for the reference's host-memory moe() call. */
 int qms_cuda_moe_forward_host(QmsCudaMoe *m, const float *xn, int T, float *out, int *sel,
                               float *wts, float *logits);
+
+/* ---- whole model on the device: qms_model_load / qms_forward (src/model.h:135-141) ------------- */
+
+/* Model configuration and the trunk tensors, as read_cfg and qms_model_load hold them
+ * (src/model.c:279-312, :314-338). Tensors are in GGUF/ggml block layout, host memory
+ * (src_on_device 0) or device memory (1); they are copied (and repacked) on the current device and
+ * not retained. output == NULL means tied embeddings (the head multiplies by token_embd, as
+ * src/model.c:333-335 does). Supported types: embd Q4_0, Q4_1, Q8_0, Q6_K, F16 or F32; output
+ * (or tied embd) Q4_0, Q4_1 or Q6_K; n_embd % 256 == 0, head_dim 64 or 128 (<= QMS_MAX_HEAD_DIM). */
+typedef struct {
+    int n_layer, n_embd, n_head, n_head_kv, head_dim;
+    int n_expert, n_used, n_ff, vocab;
+    float eps;                 /* RMSNorm epsilon (the reference stores (float) of the GGUF value) */
+    double rope_base;          /* NEOX RoPE base */
+    int ctx;                   /* KV cache capacity in positions (fp32 K and V, [layer][pos][n_head_kv*head_dim]) */
+    int embd_type;
+    const void *embd;          /* token_embd.weight [vocab] rows of n_embd */
+    const float *out_norm;     /* output_norm.weight [n_embd] */
+    int output_type;
+    const void *output;        /* output.weight [vocab] rows of n_embd, or NULL (tied) */
+    int src_on_device;
+} QmsCudaModelDesc;
+
+/* One layer's tensors (QmsLayer, src/model.h:37-45): norms F32; q [n_head*head_dim], k and v
+ * [n_head_kv*head_dim] rows of n_embd, o [n_embd] rows of n_head*head_dim, all Q4_0 or Q4_1;
+ * moe.* the MoE block exactly as for qms_cuda_moe_create (its n_* fields must match the model). */
+typedef struct {
+    const float *attn_norm, *q_norm, *k_norm, *ffn_norm;
+    int q_type, k_type, v_type, o_type;
+    const void *q, *k, *v, *o;
+    QmsCudaMoeDesc moe;
+} QmsCudaLayerDesc;
+
+typedef struct QmsCudaModel QmsCudaModel;
+
+/* Allocate the model on the current device: trunk tensors, KV cache for desc->ctx positions and
+ * the forward's scratch. Layers are added with qms_cuda_model_set_layer; a forward before every
+ * layer is set fails. Replaces qms_model_load's allocation and reads (src/model.c:314-387). */
+int qms_cuda_model_create(const QmsCudaModelDesc *desc, QmsCudaModel **out);
+/* Upload layer l (0 <= l < n_layer); the source buffers may be freed afterwards, so a loader can
+ * stream a GGUF file layer by layer with one layer of host memory. */
+int qms_cuda_model_set_layer(QmsCudaModel *m, int l, const QmsCudaLayerDesc *ld);
+void qms_cuda_model_free(QmsCudaModel *m);
+/* Device bytes held (weights, KV cache, scratch). */
+int64_t qms_cuda_model_device_bytes(const QmsCudaModel *m);
+
+/* qms_forward (src/model.c:1252-1296) on host buffers: T tokens ids[0..T) at positions
+ * pos0..pos0+T-1, appending to the KV cache; logits (host fp32) receives [vocab] for the last
+ * position, or [T][vocab] when all_logits. Embedding dequant, per layer RMSNorm -> attention
+ * (QKV projections, QK-norm, NEOX RoPE, fp32 KV append, causal GQA, O projection) -> residual ->
+ * RMSNorm -> MoE -> residual, final RMSNorm and the head, all on the device; returns after the
+ * logits are on the host. pos0 + T > ctx or an id outside [0, vocab) is QMS_CUDA_EINVAL (the
+ * reference returns -1, src/model.c:1257,1264). sel_trace, when non-NULL (host int
+ * [n_layer][T][n_used]), receives every layer's selected experts in selection order, from which a
+ * caller writes the reference's --trace records (src/model.c:1102-1110). */
+int qms_cuda_forward(QmsCudaModel *m, const int *ids, int T, int pos0, float *logits, int all_logits,
+                     int *sel_trace);
+
+/* The same on device buffers, asynchronously on `stream`: ids (device int [T]); *pos (device int)
+ * is the position of ids[0] and is read by the kernels, so a captured graph can be replayed as
+ * the position advances. logits: device fp32 [all_logits ? T : 1][vocab]. T must not exceed the
+ * scratch reserved with qms_cuda_model_reserve (default 1); positions beyond ctx or invalid ids
+ * are not written and set the error reported by qms_cuda_model_status. */
+int qms_cuda_forward_dev(QmsCudaModel *m, const int *ids, int T, const int *pos, float *logits,
+                         int all_logits, void *stream);
+/* One greedy decode step entirely on the device (src/main.c:198-207, inc mode): the token *tok at
+ * position *pos (device ints) runs through the model; the argmax of its logits (first index
+ * among equal maxima, as argmax() in src/main.c) is written back to *tok, *pos is incremented,
+ * and logits (device fp32 [vocab], optional) receive the step's logits. Graph-capturable: a graph
+ * of N steps generates N tokens with no host round trip. */
+int qms_cuda_decode_step(QmsCudaModel *m, int *tok, int *pos, float *logits, void *stream);
+/* Make sure the forward's scratch covers T tokens (capture-safe afterwards). */
+int qms_cuda_model_reserve(QmsCudaModel *m, int T);
+/* Waits for the device; QMS_CUDA_EINVAL if a device-side check (position beyond ctx, bad id)
+ * refused work since the last call, QMS_CUDA_ETIMEOUT if a MoE kernel's bounded wait gave up. */
+int qms_cuda_model_status(QmsCudaModel *m);
+/* QMS_PROF-style section timers (src/model.h:143-150): with on != 0, every following
+ * qms_cuda_forward records CUDA events around its sections and adds their device time in ms to
+ * ms[0..6] = qkv, attn, o_proj, router, fetch (always 0: weights are resident), moe, output.
+ * For one-token calls routing runs inside the MoE kernel and is counted under moe. ms may be NULL
+ * to only switch; reading (ms non-NULL) returns the sums and clears them. */
+int qms_cuda_model_profile(QmsCudaModel *m, int on, double *ms);
 
 /* Routing that allocates nothing. It has no counterpart in the reference (the reference
  * allocates freely on the host); it exists for callers that may not call cudaMalloc, such as

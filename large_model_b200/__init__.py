@@ -7,6 +7,7 @@ with ctypes and mirrors the reference's operator interface for tests and benchma
     matvec_q8(type, W, xq, ...)  qms_matmul fast path / qms_vec_dot_q8 (src/quant.h:23)
     matvec_f32(W, x)             qms_vec_dot_f32   (src/kernels.h:21)
     MoeLayer(...).forward(xn)    moe()             (src/model.c:1032)
+    Model(...).forward(ids, pos) qms_forward       (src/model.c:1252), the whole token step
 
 Device buffers are torch CUDA tensors (plumbing only); every computation runs in
 libqms_cuda's kernels. There is no CPU fallback: if the library is missing or no sm_100 GPU is
@@ -40,6 +41,21 @@ class MoeDesc(C.Structure):
                 ("gate_type", C.c_int), ("up_type", C.c_int), ("down_type", C.c_int),
                 ("router", C.c_void_p), ("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p),
                 ("src_on_device", C.c_int)]
+
+
+class ModelDesc(C.Structure):
+    _fields_ = [("n_layer", C.c_int), ("n_embd", C.c_int), ("n_head", C.c_int), ("n_head_kv", C.c_int),
+                ("head_dim", C.c_int), ("n_expert", C.c_int), ("n_used", C.c_int), ("n_ff", C.c_int),
+                ("vocab", C.c_int), ("eps", C.c_float), ("rope_base", C.c_double), ("ctx", C.c_int),
+                ("embd_type", C.c_int), ("embd", C.c_void_p), ("out_norm", C.c_void_p),
+                ("output_type", C.c_int), ("output", C.c_void_p), ("src_on_device", C.c_int)]
+
+
+class LayerDesc(C.Structure):
+    _fields_ = [("attn_norm", C.c_void_p), ("q_norm", C.c_void_p), ("k_norm", C.c_void_p),
+                ("ffn_norm", C.c_void_p), ("q_type", C.c_int), ("k_type", C.c_int), ("v_type", C.c_int),
+                ("o_type", C.c_int), ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p),
+                ("o", C.c_void_p), ("moe", MoeDesc)]
 
 
 _lib = None
@@ -76,6 +92,19 @@ def lib() -> C.CDLL:
     L.qms_cuda_moe_experts_q8.argtypes = [vp, vp, vp, i32, vp, vp]
     L.qms_cuda_sample.argtypes = [vp, i32, C.c_float, C.c_float, i32, vp, vp, vp]
     L.qms_cuda_moe_combine.argtypes = [vp, vp, i32, i32, i32, vp, vp, vp]
+    L.qms_cuda_model_create.argtypes = [C.POINTER(ModelDesc), C.POINTER(vp)]
+    L.qms_cuda_model_set_layer.argtypes = [vp, i32, C.POINTER(LayerDesc)]
+    L.qms_cuda_model_free.argtypes = [vp]
+    L.qms_cuda_model_free.restype = None
+    L.qms_cuda_model_device_bytes.argtypes = [vp]
+    L.qms_cuda_model_device_bytes.restype = i64
+    L.qms_cuda_forward.argtypes = [vp, vp, i32, i32, vp, i32, vp]
+    L.qms_cuda_forward_dev.argtypes = [vp, vp, i32, vp, vp, i32, vp]
+    L.qms_cuda_decode_step.argtypes = [vp, vp, vp, vp, vp]
+    L.qms_cuda_model_reserve.argtypes = [vp, i32]
+    L.qms_cuda_model_status.argtypes = [vp]
+    L.qms_cuda_model_profile.argtypes = [vp, i32, vp]
+    L.qms_cuda_moe_route_noalloc.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp, vp]
     _lib = L
     return L
 
@@ -304,3 +333,115 @@ def combine(dn, wts, resid=None, out=None, stream=None):
         out = torch.empty((T, E), dtype=torch.float32, device=dn.device)
     check(lib().qms_cuda_moe_combine(_ptr(dn), _ptr(wts), T, K, E, _ptr(resid), _ptr(out), _stream(stream)))
     return out
+
+
+# ---- the whole model (qms_model_load / qms_forward, src/model.h:135-141) ------------------------------
+
+class Model:
+    """A Qwen3-MoE model resident on the current device (qms_cuda_model_*).
+
+    cfg: an object with the config fields of synth.ModelCfg. Tensors are added with the GGUF names
+    and layouts qms_model_load reads (src/model.c:314-387): `trunk` holds token_embd.weight,
+    output_norm.weight and (unless tied) output.weight; set_layer(l, tensors) takes layer l's
+    blk.{l}.* tensors. Arrays are numpy (host) or torch CUDA tensors (device)."""
+
+    def __init__(self, cfg, trunk: dict, ctx: int, embd_type: int = T_Q4_0, output_type: int | None = None):
+        on_dev = not isinstance(trunk["token_embd.weight"], np.ndarray)
+        ptr = (lambda a: a.ctypes.data) if not on_dev else (lambda t: t.data_ptr())
+        out = trunk.get("output.weight")
+        otype = (cfg.output_type if output_type is None else output_type) if out is not None else embd_type
+        d = ModelDesc(cfg.n_layer, cfg.n_embd, cfg.n_head, cfg.n_head_kv, cfg.head_dim, cfg.n_expert, cfg.n_used,
+                      cfg.n_ff, cfg.vocab, float(cfg.eps), float(cfg.rope_base), int(ctx), embd_type,
+                      ptr(trunk["token_embd.weight"]), ptr(trunk["output_norm.weight"]), otype,
+                      None if out is None else ptr(out), int(on_dev))
+        h = C.c_void_p()
+        check(lib().qms_cuda_model_create(C.byref(d), C.byref(h)))
+        self.h = h
+        self.cfg = cfg
+        self.ctx = ctx
+
+    def set_layer(self, l: int, t: dict, types: dict | None = None):
+        """t: the layer's tensors by their short names (attn_norm, attn_q_norm, attn_k_norm, ffn_norm,
+        attn_q, attn_k, attn_v, attn_output, ffn_gate_inp, ffn_gate_exps, ffn_up_exps, ffn_down_exps)."""
+        types = types or {}
+        on_dev = not isinstance(t["attn_q"], np.ndarray)
+        ptr = (lambda a: a.ctypes.data) if not on_dev else (lambda x: x.data_ptr())
+        c = self.cfg
+        ty = lambda k: types.get(k, T_Q4_0)
+        moe = MoeDesc(c.n_embd, c.n_expert, c.n_used, c.n_ff, ty("ffn_gate_exps"), ty("ffn_up_exps"),
+                      ty("ffn_down_exps"), ptr(t["ffn_gate_inp"]), ptr(t["ffn_gate_exps"]), ptr(t["ffn_up_exps"]),
+                      ptr(t["ffn_down_exps"]), int(on_dev))
+        ld = LayerDesc(ptr(t["attn_norm"]), ptr(t["attn_q_norm"]), ptr(t["attn_k_norm"]), ptr(t["ffn_norm"]),
+                       ty("attn_q"), ty("attn_k"), ty("attn_v"), ty("attn_output"), ptr(t["attn_q"]),
+                       ptr(t["attn_k"]), ptr(t["attn_v"]), ptr(t["attn_output"]), moe)
+        check(lib().qms_cuda_model_set_layer(self.h, int(l), C.byref(ld)))
+
+    @classmethod
+    def from_synth(cls, cfg, seed: int, ctx: int) -> "Model":
+        """The seeded synthetic model of synth.write_gguf (same bytes), uploaded tensor by tensor."""
+        from . import synth
+        names = synth.model_tensors(cfg)
+        trunk = {}
+        i = 0
+        while i < len(names) and not names[i][0].startswith("blk."):
+            trunk[names[i][0]] = np.ascontiguousarray(synth.tensor_data(cfg, seed, i))
+            i += 1
+        m = cls(cfg, trunk, ctx)
+        del trunk
+        for l in range(cfg.n_layer):
+            t = {}
+            while i < len(names) and names[i][0].startswith(f"blk.{l}."):
+                t[names[i][0].split(".")[2]] = np.ascontiguousarray(synth.tensor_data(cfg, seed, i))
+                i += 1
+            m.set_layer(l, t)
+        return m
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().qms_cuda_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def device_bytes(self) -> int:
+        return lib().qms_cuda_model_device_bytes(self.h)
+
+    def reserve(self, T: int):
+        check(lib().qms_cuda_model_reserve(self.h, T))
+
+    def status(self):
+        check(lib().qms_cuda_model_status(self.h))
+
+    def profile(self, on: bool = True):
+        """Switch the section timers; returns the sums since the last read (ms: qkv, attn, o_proj,
+        router, fetch, moe, output)."""
+        ms = (C.c_double * 7)()
+        check(lib().qms_cuda_model_profile(self.h, int(on), ms))
+        return list(ms)
+
+    def forward(self, ids, pos0: int, all_logits: bool = False, trace: bool = False):
+        """qms_forward on host buffers: returns logits (numpy [vocab] or [T][vocab]) and, with
+        trace, the selected experts [n_layer][T][n_used]."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        T = ids.shape[0]
+        V = self.cfg.vocab
+        logits = np.empty((T, V) if all_logits else (V,), np.float32)
+        sel = np.empty((self.cfg.n_layer, T, self.cfg.n_used), np.int32) if trace else None
+        check(lib().qms_cuda_forward(self.h, C.c_void_p(ids.ctypes.data), T, int(pos0),
+                                     C.c_void_p(logits.ctypes.data), int(all_logits),
+                                     None if sel is None else C.c_void_p(sel.ctypes.data)))
+        return (logits, sel) if trace else logits
+
+    def forward_dev(self, ids, pos, logits, all_logits: bool = False, stream=None):
+        """Device buffers (torch CUDA int32 ids [T], int32 pos [1], float32 logits)."""
+        check(lib().qms_cuda_forward_dev(self.h, _ptr(ids), ids.numel(), _ptr(pos), _ptr(logits), int(all_logits),
+                                         _stream(stream)))
+
+    def decode_step(self, tok, pos, logits=None, stream=None):
+        """One greedy step on the device: tok / pos torch CUDA int32 [1], updated in place."""
+        check(lib().qms_cuda_decode_step(self.h, _ptr(tok), _ptr(pos), _ptr(logits), _stream(stream)))

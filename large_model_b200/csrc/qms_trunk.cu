@@ -1,0 +1,687 @@
+// qms_trunk.cu - the rest of a Qwen3-MoE token step on B200 (sm_100a): embedding, RMSNorm,
+// Q4_0/Q4_1/Q6_K projections against Q8 activations, QK-norm + NEOX RoPE + fp32 KV append,
+// causal GQA attention, and the output head with a fused greedy argmax.
+//
+// Reference: qms_forward and attention() in src/model.c:403-497, 1252-1296; the integer dots of
+// src/kernels.c:82-195 (through qms_matmul_n, src/quant.c:128-170); qms_dequant_row (src/quant.c).
+//
+//   k_embed       one CTA per token: dequantise row ids[t] of token_embd (src/model.c:1273)
+//   k_rmsnorm     one CTA per row: double sum of squares, y = (float)(x * inv) * w
+//                 (src/model.c:403-409), optionally also the row's Q8 blocks (src/kernels.c:34-53)
+//   k_gemv        y = W x for W in repacked Q4_0 / Q4_1 / Q6_K rows (qms_matmul_n's integer path):
+//                 lanes of a warp split a row's blocks, dp4a dots per 32-block, fp32 accumulation;
+//                 the first rows' weights are loaded before griddepcontrol.wait, so the stream of
+//                 a projection starts while the previous kernel finishes. For one token the
+//                 prologue RMS-normalises and quantises x itself; the head variant also keeps a
+//                 running argmax and the last CTA writes the token (greedy decode on device).
+//   k_qk_rope     one warp per head row: QK-norm (RMSNorm over head_dim), NEOX rotation from
+//                 host-computed cos/sin tables (the reference's own double-precision angles), and
+//                 the K/V append to the fp32 cache (src/model.c:436-462)
+//   k_attention   one warp per q head, a CTA per group of heads sharing a KV head; scores in
+//                 qms_vec_dot_f32's exact order (sixteen FMA chains + the hsum tree), double
+//                 softmax, float accumulation of the V rows. One-token calls split the positions
+//                 over CTAs and the last CTA of a head group merges the splits.
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+
+#include "qms_moe.cuh"
+#include "qms_trunk.cuh"
+
+namespace qms {
+
+constexpr int kGemvWarps = 16;
+constexpr int kGemvThreads = kGemvWarps * 32;
+constexpr unsigned kFull = 0xffffffffu;
+
+// ---- load-time repack -------------------------------------------------------------------------------
+__global__ void k_repack_q4rows(const uint8_t *__restrict__ src, int64_t rows, int nb, int q1, size_t stride,
+                                uint8_t *__restrict__ dst) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * nb) return;
+    const int64_t r = i / nb;
+    const int b = (int)(i % nb);
+    const int bs = q1 ? 20 : 18;
+    const uint16_t *s = reinterpret_cast<const uint16_t *>(src + (size_t)r * nb * bs + (size_t)b * bs);
+    uint8_t *row = dst + (size_t)r * stride;
+    const uint16_t *qs = s + 1 + q1;
+    uint4 v;
+    v.x = (uint32_t)qs[0] | ((uint32_t)qs[1] << 16);
+    v.y = (uint32_t)qs[2] | ((uint32_t)qs[3] << 16);
+    v.z = (uint32_t)qs[4] | ((uint32_t)qs[5] << 16);
+    v.w = (uint32_t)qs[6] | ((uint32_t)qs[7] << 16);
+    *reinterpret_cast<uint4 *>(row + (size_t)b * 16) = v;
+    *reinterpret_cast<uint16_t *>(row + (size_t)nb * 16 + 2 * b) = s[0];
+    if (q1) *reinterpret_cast<uint16_t *>(row + (size_t)nb * 16 + pad16((size_t)nb * 2) + 2 * b) = s[1];
+}
+
+__global__ void k_repack_q6k(const uint8_t *__restrict__ src, int64_t rows, int nsb, size_t stride,
+                             uint8_t *__restrict__ dst) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * nsb) return;
+    const int64_t r = i / nsb;
+    const int sb = (int)(i % nsb);
+    const uint16_t *s = reinterpret_cast<const uint16_t *>(src + ((size_t)r * nsb + sb) * 210);
+    uint8_t *row = dst + (size_t)r * stride;
+    uint32_t *body = reinterpret_cast<uint32_t *>(row + (size_t)sb * 208);
+#pragma unroll 4
+    for (int k = 0; k < 52; k++) body[k] = (uint32_t)s[2 * k] | ((uint32_t)s[2 * k + 1] << 16);
+    *reinterpret_cast<uint16_t *>(row + (size_t)nsb * 208 + 2 * sb) = s[104];
+}
+
+int repack_rows(int type, const uint8_t *src, int64_t rows, int ncol, uint8_t *dst, cudaStream_t s) {
+    const size_t stride = rows_stride(type, ncol);
+    if (type == QMS_T_Q6_K) {
+        const int nsb = ncol / 256;
+        const int64_t n = rows * nsb;
+        k_repack_q6k<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src, rows, nsb, stride, dst);
+    } else {
+        const int nb = ncol / 32;
+        const int64_t n = rows * nb;
+        k_repack_q4rows<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src, rows, nb, type == QMS_T_Q4_1, stride, dst);
+    }
+    QMS_CK(cudaGetLastError());
+    return QMS_CUDA_OK;
+}
+
+// ---- shared pieces ------------------------------------------------------------------------------------
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_max_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+
+// 1 / sqrt(sum(x^2) / n + eps) in double for one row, by the whole CTA (src/model.c:405-407).
+// red: nwarps doubles of shared memory. Every thread returns the same value.
+__device__ double row_inv_rms(const float *__restrict__ x, int n, float eps, double *red) {
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const double v = (double)x[i];
+        ss = fma(v, v, ss);
+    }
+    ss = warp_sum_d(ss);
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[warp] = ss;
+    __syncthreads();
+    double tot = 0.0;
+    for (int i = 0; i < nw; i++) tot += red[i];
+    return 1.0 / sqrt(tot / n + (double)eps);
+}
+
+// The reference's normalised element: (float)(x * inv) * w, two roundings (src/model.c:408).
+__device__ __forceinline__ float norm_elem(float x, double inv, const float *w, int i) {
+    return w ? __fmul_rn((float)((double)x * inv), w[i]) : x;
+}
+
+// Q8 block meta as packed in GemvArgs::xs: q-sum of elements 0..15 (low half) and 16..31 (high half).
+__device__ __forceinline__ int pack_sums(const Q8Lane &r) { return (r.sum_lo & 0xffff) | ((r.sum - r.sum_lo) << 16); }
+__device__ __forceinline__ int sum_lo(int s) { return (int)(int16_t)(s & 0xffff); }
+__device__ __forceinline__ int sum_hi(int s) { return s >> 16; }
+
+// ---- embedding ---------------------------------------------------------------------------------------
+__device__ __forceinline__ float dequant_elem(int type, const uint8_t *row, int i) {
+    switch (type) {
+    case QMS_T_F32: return reinterpret_cast<const float *>(row)[i];
+    case QMS_T_F16: return h2f(reinterpret_cast<const uint16_t *>(row)[i]);
+    case QMS_T_Q4_0: {
+        const uint8_t *b = row + (size_t)(i >> 5) * 18;
+        const int j = i & 31;
+        const int q = j < 16 ? (b[2 + j] & 0x0F) : (b[2 + j - 16] >> 4);
+        return __fmul_rn((float)(q - 8), h2f(*reinterpret_cast<const uint16_t *>(b)));
+    }
+    case QMS_T_Q4_1: {
+        const uint8_t *b = row + (size_t)(i >> 5) * 20;
+        const int j = i & 31;
+        const int q = j < 16 ? (b[4 + j] & 0x0F) : (b[4 + j - 16] >> 4);
+        return __fmaf_rn((float)q, h2f(*reinterpret_cast<const uint16_t *>(b)),
+                         h2f(*reinterpret_cast<const uint16_t *>(b + 2)));
+    }
+    case QMS_T_Q8_0: {
+        const uint8_t *b = row + (size_t)(i >> 5) * 34;
+        return __fmul_rn((float)(int8_t)b[2 + (i & 31)], h2f(*reinterpret_cast<const uint16_t *>(b)));
+    }
+    default: {  // Q6_K, src/quant.c deq_q6_k
+        const uint8_t *b = row + (size_t)(i >> 8) * 210;
+        const int idx = i & 255, half = idx >> 7, r = idx & 127, quarter = r >> 5, l = r & 31;
+        const uint8_t *ql = b + half * 64, *qh = b + 128 + half * 32;
+        const int8_t *sc = reinterpret_cast<const int8_t *>(b + 192 + half * 8);
+        const int lo = (quarter & 1) ? ql[l + 32] : ql[l];
+        const int q = ((quarter < 2 ? lo & 0xF : lo >> 4) | (((qh[l] >> (2 * quarter)) & 3) << 4)) - 32;
+        const float d = h2f(*reinterpret_cast<const uint16_t *>(b + 208));
+        return __fmul_rn(__fmul_rn(d, (float)sc[(l >> 4) + 2 * quarter]), (float)q);
+    }
+    }
+}
+
+__global__ void __launch_bounds__(256) k_embed(int type, const uint8_t *__restrict__ embd, size_t rb, int vocab, int n,
+                                               const int *__restrict__ ids, float *__restrict__ h, int *err) {
+    const int t = blockIdx.x;
+    pdl_trigger();
+    pdl_wait();
+    const int id = ids[t];
+    float *out = h + (size_t)t * n;
+    if (id < 0 || id >= vocab) {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = 0.0f;
+        if (threadIdx.x == 0) atomicOr(err, 2);
+        return;
+    }
+    const uint8_t *row = embd + (size_t)id * rb;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = dequant_elem(type, row, i);
+}
+
+int launch_embed(int type, const uint8_t *embd, int vocab, int n, const int *ids, int T, float *h, int *err,
+                 cudaStream_t s) {
+    QMS_CK(launch_pdl(k_embed, dim3(T), dim3(256), 0, s, type, embd, ggml_row_bytes(type, n), vocab, n, ids, h, err));
+    return QMS_CUDA_OK;
+}
+
+// ---- RMSNorm (+ Q8 rows) ---------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, float eps,
+                                                 int n, float *__restrict__ y, int8_t *__restrict__ xq,
+                                                 float *__restrict__ xd, int *__restrict__ xs) {
+    __shared__ double red[8];
+    const int t = blockIdx.x;
+    pdl_trigger();
+    pdl_wait();
+    const float *xr = x + (size_t)t * n;
+    const double inv = w ? row_inv_rms(xr, n, eps, red) : 1.0;
+    if (y)
+        for (int i = threadIdx.x; i < n; i += blockDim.x) y[(size_t)t * n + i] = norm_elem(xr[i], inv, w, i);
+    if (xq) {
+        const int lane = threadIdx.x & 31, nb = n / 32;
+        for (int b = threadIdx.x >> 5; b < nb; b += blockDim.x >> 5) {
+            const Q8Lane r = quantize_lane(norm_elem(xr[32 * b + lane], inv, w, 32 * b + lane));
+            xq[(size_t)t * n + 32 * b + lane] = (int8_t)r.q;
+            if (lane == 0) {
+                xd[(size_t)t * nb + b] = r.d;
+                xs[(size_t)t * nb + b] = pack_sums(r);
+            }
+        }
+    }
+}
+
+int launch_rmsnorm(const float *x, const float *w, float eps, int T, int n, float *y, int8_t *xq, float *xd, int *xs,
+                   cudaStream_t s) {
+    QMS_CK(launch_pdl(k_rmsnorm, dim3(T), dim3(256), 0, s, x, w, eps, n, y, xq, xd, xs));
+    return QMS_CUDA_OK;
+}
+
+// ---- matrix-vector products ------------------------------------------------------------------------------
+// Units: a Q4 row is split into 32-blocks, a Q6_K row into half super-blocks (128 values = four
+// Q8 blocks). LPR lanes share a row (all 32 when the row has >= 32 units), each taking NU units.
+template <int WT, int NU>
+struct WRegs {
+    uint4 nib[WT == 2 ? 6 : NU];      // Q4: nibble planes; Q6_K: ql (4) and qh (2)
+    uint32_t sc[WT == 2 ? 2 : 1];     // Q6_K sub-scales
+    uint16_t d[NU];
+    uint16_t m[WT == 1 ? NU : 1];
+};
+
+__device__ __forceinline__ uint2 ld_stream8(const void *p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+template <int WT, int NU>
+__device__ __forceinline__ void load_row(const GemvArgs &a, int r, int li, int LPR, WRegs<WT, NU> &w) {
+    const uint8_t *row = a.w + (size_t)r * a.stride;
+    if constexpr (WT == 2) {
+        const int nsb = a.ncol / 256;
+        const int u = li, sb = u >> 1, h = u & 1;
+        const uint8_t *body = row + (size_t)sb * 208;
+#pragma unroll
+        for (int k = 0; k < 4; k++) w.nib[k] = ld_stream16(body + h * 64 + 16 * k);
+#pragma unroll
+        for (int k = 0; k < 2; k++) w.nib[4 + k] = ld_stream16(body + 128 + h * 32 + 16 * k);
+        const uint2 s = ld_stream8(body + 192 + h * 8);
+        w.sc[0] = s.x;
+        w.sc[1] = s.y;
+        w.d[0] = ld_stream2(row + (size_t)nsb * 208 + 2 * sb);
+    } else {
+        const int nb = a.ncol / 32;
+#pragma unroll
+        for (int j = 0; j < NU; j++) {
+            const int b = li + LPR * j;
+            w.nib[j] = ld_stream16(row + (size_t)b * 16);
+            w.d[j] = ld_stream2(row + (size_t)nb * 16 + 2 * b);
+            if constexpr (WT == 1) w.m[j] = ld_stream2(row + (size_t)nb * 16 + pad16((size_t)nb * 2) + 2 * b);
+        }
+    }
+}
+
+// dot of the lane's units against token tt of the staged Q8 tile
+template <int WT, int NU>
+__device__ __forceinline__ float lane_dot(const WRegs<WT, NU> &w, const int8_t *sq, const float *sd, const int *ss,
+                                          int ncol, int li, int LPR) {
+    const int nb = ncol / 32;
+    float acc = 0.0f;
+    if constexpr (WT == 2) {
+        const int sb = li >> 1, h = li & 1;
+        const float d6 = h2f(w.d[0]);
+        const uint32_t *qlw = reinterpret_cast<const uint32_t *>(&w.nib[0]);
+        const uint32_t *qhw = reinterpret_cast<const uint32_t *>(&w.nib[4]);
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            const int b = sb * 8 + h * 4 + g;
+            const int4 *x4 = reinterpret_cast<const int4 *>(sq + 32 * b);
+            const int4 xa0 = x4[0], xa1 = x4[1];
+            const int xw[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
+            int dlo = 0, dhi = 0;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint32_t q6 = ((qlw[(g & 1) * 8 + k] >> (4 * (g >> 1))) & 0x0F0F0F0Fu) |
+                                    (((qhw[k] >> (2 * g)) & 0x03030303u) << 4);
+                if (k < 4) dlo = __dp4a((int)q6, xw[k], dlo);
+                else dhi = __dp4a((int)q6, xw[k], dhi);
+            }
+            const uint32_t scw = w.sc[g >> 1];
+            const int sa = (int)(int8_t)(scw >> (16 * (g & 1))), sbv = (int)(int8_t)(scw >> (16 * (g & 1) + 8));
+            const int s = ss[b];
+            const int isum = sa * (dlo - 32 * sum_lo(s)) + sbv * (dhi - 32 * sum_hi(s));
+            acc = __fmaf_rn((float)isum, __fmul_rn(d6, sd[b]), acc);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < NU; j++) {
+            const int b = li + LPR * j;
+            const int4 *x4 = reinterpret_cast<const int4 *>(sq + 32 * b);
+            const int isum = q4_block_isum(w.nib[j], x4[0], x4[1]);
+            const float dx = sd[b];
+            const int s = ss[b], sum = sum_lo(s) + sum_hi(s);
+            const float dw = h2f(w.d[j]);
+            if constexpr (WT == 0) {
+                acc = __fmaf_rn((float)(isum - 8 * sum), __fmul_rn(dw, dx), acc);
+            } else {
+                acc = __fmaf_rn((float)isum, __fmul_rn(dw, dx), acc);
+                acc = __fmaf_rn(h2f(w.m[j]), __fmul_rn(dx, (float)sum), acc);
+            }
+        }
+    }
+    (void)nb;
+    return acc;
+}
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, int r) {
+    if (v != v) return 0ull;                                   // NaN never wins (argmax uses '>')
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (0xffffffffu - (uint32_t)r);   // ties: the lower index wins
+}
+
+template <int WT, int NU, bool F32IN>
+__global__ void __launch_bounds__(kGemvThreads) k_gemv(const GemvArgs a) {
+    extern __shared__ __align__(16) unsigned char gsm[];
+    __shared__ double red[kGemvWarps];
+    __shared__ unsigned long long s_best;
+    __shared__ int s_last;
+    const int ncol = a.ncol, nb = ncol / 32;
+    int8_t *sq = reinterpret_cast<int8_t *>(gsm);                        // [kGemvTile][ncol]
+    float *sd = reinterpret_cast<float *>(gsm + (size_t)kGemvTile * ncol);   // [kGemvTile][nb]
+    int *ss = reinterpret_cast<int *>(sd + (size_t)kGemvTile * nb);     // [kGemvTile][nb]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int units = WT == 2 ? ncol / 128 : nb;
+    const int LPR = units >= 32 ? 32 : units;
+    const int RPW = 32 / LPR, seg = lane / LPR, li = lane % LPR;
+    const int ngroups = (a.rows + RPW - 1) / RPW;
+    const int gw = blockIdx.x * kGemvWarps + warp, nwg = gridDim.x * kGemvWarps;
+    const bool argmax = a.amax != nullptr;
+    if (tid == 0) s_best = 0ull;
+
+    WRegs<WT, NU> cur, nxt;
+    auto row_of = [&](int g) { const int r = g * RPW + seg; return r < a.rows ? r : a.rows - 1; };
+    if (gw < ngroups) load_row<WT, NU>(a, row_of(gw), li, LPR, cur);   // weights never depend on earlier kernels
+    pdl_trigger();
+    pdl_wait();
+    unsigned long long best = 0ull;
+    for (int t0 = 0; t0 < a.T; t0 += kGemvTile) {
+        const int tn = min(kGemvTile, a.T - t0);
+        if (t0 > 0) {
+            __syncthreads();
+            if (gw < ngroups) load_row<WT, NU>(a, row_of(gw), li, LPR, cur);
+        }
+        if constexpr (F32IN) {
+            for (int t = 0; t < tn; t++) {
+                const float *xr = a.x + (size_t)(t0 + t) * a.ldx;
+                const double inv = a.nw ? row_inv_rms(xr, ncol, a.eps, red) : 1.0;
+                for (int b = warp; b < nb; b += kGemvWarps) {
+                    const Q8Lane r = quantize_lane(norm_elem(xr[32 * b + lane], inv, a.nw, 32 * b + lane));
+                    sq[(size_t)t * ncol + 32 * b + lane] = (int8_t)r.q;
+                    if (lane == 0) {
+                        sd[t * nb + b] = r.d;
+                        ss[t * nb + b] = pack_sums(r);
+                    }
+                }
+            }
+        } else {
+            const int4 *src = reinterpret_cast<const int4 *>(a.xq + (size_t)t0 * ncol);
+            int4 *dst = reinterpret_cast<int4 *>(sq);
+            for (int i = tid; i < tn * ncol / 16; i += kGemvThreads) dst[i] = __ldcg(src + i);
+            for (int i = tid; i < tn * nb; i += kGemvThreads) {
+                sd[i] = __ldcg(a.xd + (size_t)t0 * nb + i);
+                ss[i] = __ldcg(a.xs + (size_t)t0 * nb + i);
+            }
+        }
+        __syncthreads();
+        for (int g = gw; g < ngroups; g += nwg) {
+            const bool more = g + nwg < ngroups;
+            if (more) load_row<WT, NU>(a, row_of(g + nwg), li, LPR, nxt);
+            const int r = g * RPW + seg;
+            for (int t = 0; t < tn; t++) {
+                float acc = lane_dot<WT, NU>(cur, sq + (size_t)t * ncol, sd + t * nb, ss + t * nb, ncol, li, LPR);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+                    if (o < LPR) acc = __fadd_rn(acc, __shfl_xor_sync(kFull, acc, o));
+                if (li == 0 && r < a.rows) {
+                    const size_t at = (size_t)(t0 + t) * a.ldy + r;
+                    const float v = a.resid ? __fadd_rn(a.resid[at], acc) : acc;
+                    a.y[at] = v;
+                    if (argmax) {
+                        const unsigned long long k = argmax_key(v, r);
+                        best = k > best ? k : best;
+                    }
+                }
+            }
+            if (more) cur = nxt;
+        }
+    }
+    if (!argmax) return;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k = __shfl_xor_sync(kFull, best, o);
+        best = k > best ? k : best;
+    }
+    if (lane == 0) atomicMax(&s_best, best);
+    __syncthreads();
+    if (tid == 0) {
+        atomicMax(a.amax, s_best);
+        __threadfence();
+        s_last = atomicAdd(a.ticket, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (tid == 0 && s_last) {
+        __threadfence();
+        const unsigned long long k = atomicExch(a.amax, 0ull);
+        *a.tok = (int)(0xffffffffu - (uint32_t)k);
+        if (a.pos) *a.pos += 1;
+        *a.ticket = 0;
+    }
+}
+
+constexpr int kGemvMaxCol = 8192;     // 256 Q4 blocks per row (the largest NU * 32)
+constexpr size_t kGemvMaxSmem = (size_t)kGemvTile * (kGemvMaxCol + kGemvMaxCol / 32 * 8);
+
+// Once per process and device: the variants' shared-memory limit and the SM count.
+static int gemv_setup(int *nsm) {
+    static int s_dev_nsm[64];
+    static bool s_attr[64];
+    int dev = 0;
+    QMS_CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!s_dev_nsm[dev]) {
+        int n = 148;
+        QMS_CK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        s_dev_nsm[dev] = n;
+    }
+    if (!s_attr[dev]) {
+#define QMS_GEMV_ATTR(WT, NU)                                                                                    \
+    QMS_CK(cudaFuncSetAttribute(k_gemv<WT, NU, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvMaxSmem)); \
+    QMS_CK(cudaFuncSetAttribute(k_gemv<WT, NU, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvMaxSmem));
+        QMS_GEMV_ATTR(0, 1) QMS_GEMV_ATTR(0, 2) QMS_GEMV_ATTR(0, 4) QMS_GEMV_ATTR(0, 8)
+        QMS_GEMV_ATTR(1, 1) QMS_GEMV_ATTR(1, 2) QMS_GEMV_ATTR(1, 4) QMS_GEMV_ATTR(1, 8)
+        QMS_GEMV_ATTR(2, 1)
+#undef QMS_GEMV_ATTR
+        s_attr[dev] = true;
+    }
+    *nsm = s_dev_nsm[dev];
+    return QMS_CUDA_OK;
+}
+
+template <int WT, int NU>
+static int launch_gemv_t(const GemvArgs &a, cudaStream_t s) {
+    const int ncol = a.ncol, nb = ncol / 32;
+    const size_t smem = (size_t)kGemvTile * (ncol + (size_t)nb * 8);
+    auto kern = a.x != nullptr ? k_gemv<WT, NU, true> : k_gemv<WT, NU, false>;
+    int nsm = 148;
+    int rc = gemv_setup(&nsm);
+    if (rc) return rc;
+    const int units = WT == 2 ? ncol / 128 : nb;
+    const int LPR = units >= 32 ? 32 : units;
+    const int ngroups = (a.rows + 32 / LPR - 1) / (32 / LPR);
+    int grid = (ngroups + kGemvWarps - 1) / kGemvWarps;
+    grid = std::min(grid, 2 * nsm);
+    QMS_CK(launch_pdl(kern, dim3(grid), dim3(kGemvThreads), smem, s, a));
+    return QMS_CUDA_OK;
+}
+
+int launch_gemv(int type, const GemvArgs &a, cudaStream_t s) {
+    QMS_REQUIRE(a.x == nullptr || a.T <= kGemvTile, QMS_CUDA_EINVAL, "gemv: fp32 input limited to %d tokens", kGemvTile);
+    QMS_REQUIRE(a.amax == nullptr || a.T == 1, QMS_CUDA_EINVAL, "gemv: fused argmax needs T == 1");
+    if (type == QMS_T_Q6_K) {
+        const int units = a.ncol / 128;
+        QMS_REQUIRE(a.ncol % 256 == 0 && units <= 32 && (units & (units - 1)) == 0, QMS_CUDA_EUNSUPPORTED,
+                    "gemv: Q6_K rows of %d values not supported", a.ncol);
+        return launch_gemv_t<2, 1>(a, s);
+    }
+    const int nb = a.ncol / 32;
+    QMS_REQUIRE(a.ncol % 32 == 0 && (nb < 32 ? (nb & (nb - 1)) == 0 : nb % 32 == 0 && nb <= 256),
+                QMS_CUDA_EUNSUPPORTED, "gemv: Q4 rows of %d values not supported", a.ncol);
+    const int nu = nb < 32 ? 1 : nb / 32;
+    QMS_REQUIRE(nu == 1 || nu == 2 || nu == 4 || nu == 8, QMS_CUDA_EUNSUPPORTED, "gemv: %d blocks per row", nb);
+    if (type == QMS_T_Q4_0) {
+        switch (nu) {
+        case 1: return launch_gemv_t<0, 1>(a, s);
+        case 2: return launch_gemv_t<0, 2>(a, s);
+        case 4: return launch_gemv_t<0, 4>(a, s);
+        default: return launch_gemv_t<0, 8>(a, s);
+        }
+    }
+    QMS_REQUIRE(type == QMS_T_Q4_1, QMS_CUDA_EUNSUPPORTED, "gemv: type %d", type);
+    switch (nu) {
+    case 1: return launch_gemv_t<1, 1>(a, s);
+    case 2: return launch_gemv_t<1, 2>(a, s);
+    case 4: return launch_gemv_t<1, 4>(a, s);
+    default: return launch_gemv_t<1, 8>(a, s);
+    }
+}
+
+// ---- QK-norm, RoPE, KV append ------------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(256) k_qk_rope(const AttnArgs a) {
+    constexpr int J = D / 32, JH = J / 2;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hh = blockIdx.x * 8 + warp, t = blockIdx.y;
+    pdl_trigger();
+    pdl_wait();
+    if (hh >= a.H + 2 * a.Hk) return;
+    const int p = *a.pos + t;
+    if (p < 0 || p >= a.ctx) {
+        if (lane == 0) atomicOr(a.err, 1);
+        return;
+    }
+    const int KD = a.Hk * D;
+    float *row = a.qkv + (size_t)t * a.ldq + (size_t)hh * D;
+    float x[J];
+#pragma unroll
+    for (int j = 0; j < J; j++) x[j] = row[lane + 32 * j];
+    if (hh >= a.H + a.Hk) {                                    // v head: append as is
+        float *dst = a.vc + (size_t)p * KD + (size_t)(hh - a.H - a.Hk) * D;
+#pragma unroll
+        for (int j = 0; j < J; j++) dst[lane + 32 * j] = x[j];
+        return;
+    }
+    const float *nw = hh < a.H ? a.q_norm : a.k_norm;
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < J; j++) ss = fma((double)x[j], (double)x[j], ss);
+    ss = warp_sum_d(ss);
+    const double inv = 1.0 / sqrt(ss / D + (double)a.eps);
+#pragma unroll
+    for (int j = 0; j < J; j++) x[j] = norm_elem(x[j], inv, nw, lane + 32 * j);
+    const float *cs = a.rope_cos + (size_t)p * (D / 2), *sn = a.rope_sin + (size_t)p * (D / 2);
+#pragma unroll
+    for (int j = 0; j < JH; j++) {                             // element i pairs with i + D/2
+        const int i = lane + 32 * j;
+        const float c = cs[i], s = sn[i], x1 = x[j], x2 = x[j + JH];
+        x[j] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+        x[j + JH] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+    }
+    float *dst = hh < a.H ? row : a.kc + (size_t)p * KD + (size_t)(hh - a.H) * D;
+#pragma unroll
+    for (int j = 0; j < J; j++) dst[lane + 32 * j] = x[j];
+}
+
+int launch_qk_rope(const AttnArgs &a, cudaStream_t s) {
+    const dim3 grid((a.H + 2 * a.Hk + 7) / 8, a.T);
+    if (a.D == 128) QMS_CK(launch_pdl(k_qk_rope<128>, grid, dim3(256), 0, s, a));
+    else QMS_CK(launch_pdl(k_qk_rope<64>, grid, dim3(256), 0, s, a));
+    return QMS_CUDA_OK;
+}
+
+// ---- attention -------------------------------------------------------------------------------------------------
+int attention_heads_per_cta(int group) { return group < 4 ? group : 4; }
+
+template <int D>
+__global__ void __launch_bounds__(128) k_attention(const AttnArgs a) {
+    constexpr int NQ = D / 16;                   // elements of q per lane (lane k of 16: 16i + k)
+    constexpr int DPL = D / 32;                  // output dims per lane
+    const int HB = blockDim.x >> 5;
+    const int group = a.H / a.Hk, nhb = group / HB;
+    const int g = blockIdx.x / nhb, hb = blockIdx.x % nhb;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = g * group + hb * HB + warp;
+    const int t = blockIdx.z, s = blockIdx.y;
+    __shared__ int s_last;
+    pdl_trigger();
+    pdl_wait();
+    const int pt = *a.pos + t;
+    if (pt < 0 || pt >= a.ctx) return;           // k_qk_rope has flagged it
+    const int npos = pt + 1;
+    int p0 = 0, p1 = npos, S = 1;
+    if (a.split > 0) {
+        S = (npos + a.split - 1) / a.split;
+        if (s >= S) return;
+        p0 = s * a.split;
+        p1 = min(npos, p0 + a.split);
+    }
+    const int KD = a.Hk * D;
+    const float *qh = a.qkv + (size_t)t * a.ldq + (size_t)h * D;
+    const int k16 = lane & 15, half = lane >> 4;
+    float qr[NQ];
+#pragma unroll
+    for (int i = 0; i < NQ; i++) qr[i] = qh[16 * i + k16];
+    const float *kb = a.kc + (size_t)g * D, *vb = a.vc + (size_t)g * D;
+    float o[DPL];
+#pragma unroll
+    for (int d = 0; d < DPL; d++) o[d] = 0.0f;
+    double m = -INFINITY, l = 0.0;
+    for (int pc = p0; pc < p1; pc += 32) {
+        float mydot = 0.0f;
+#pragma unroll 4
+        for (int j = 0; j < 16; j++) {
+            const int p = pc + 2 * j + half;
+            float acc = 0.0f;
+            if (p < p1) {
+                const float *kp = kb + (size_t)p * KD;
+#pragma unroll
+                for (int i = 0; i < NQ; i++) acc = __fmaf_rn(qr[i], __ldcg(kp + 16 * i + k16), acc);
+            }
+            acc = __fadd_rn(acc, __shfl_down_sync(kFull, acc, 8, 16));
+            acc = __fadd_rn(acc, __shfl_down_sync(kFull, acc, 4, 16));
+            acc = __fadd_rn(acc, __shfl_down_sync(kFull, acc, 2, 16));
+            acc = __fadd_rn(acc, __shfl_down_sync(kFull, acc, 1, 16));
+            const float d0 = __shfl_sync(kFull, acc, 0), d1 = __shfl_sync(kFull, acc, 16);
+            if (lane == 2 * j) mydot = d0;
+            if (lane == 2 * j + 1) mydot = d1;
+        }
+        const bool valid = pc + lane < p1;
+        const double sc = valid ? (double)mydot * a.scale : -INFINITY;
+        const double mn = fmax(m, warp_max_d(sc));
+        const double alpha = m == -INFINITY ? 0.0 : exp(m - mn);
+        const double e = valid ? exp(sc - mn) : 0.0;
+        l = fma(l, alpha, warp_sum_d(e));
+        m = mn;
+        const float fa = (float)alpha, fe = (float)e;
+#pragma unroll
+        for (int d = 0; d < DPL; d++) o[d] = __fmul_rn(o[d], fa);
+        const int np = min(32, p1 - pc);
+        for (int q = 0; q < np; q++) {
+            const float w = __shfl_sync(kFull, fe, q);
+            const float *vp = vb + (size_t)(pc + q) * KD + lane * DPL;
+            if constexpr (DPL == 4) {
+                const float4 v = __ldcg(reinterpret_cast<const float4 *>(vp));
+                o[0] = __fmaf_rn(w, v.x, o[0]);
+                o[1] = __fmaf_rn(w, v.y, o[1]);
+                o[2] = __fmaf_rn(w, v.z, o[2]);
+                o[3] = __fmaf_rn(w, v.w, o[3]);
+            } else {
+                const float2 v = __ldcg(reinterpret_cast<const float2 *>(vp));
+                o[0] = __fmaf_rn(w, v.x, o[0]);
+                o[1] = __fmaf_rn(w, v.y, o[1]);
+            }
+        }
+    }
+    float *out = a.out + (size_t)t * a.H * D + (size_t)h * D + lane * DPL;
+    if (S == 1) {
+#pragma unroll
+        for (int d = 0; d < DPL; d++) out[d] = (float)((double)o[d] / l);
+        return;
+    }
+    // split: publish this split's (m, l, o); the last CTA of the head group merges them
+    const size_t slot = (size_t)h * a.max_splits + s;
+#pragma unroll
+    for (int d = 0; d < DPL; d++) a.part_o[slot * D + lane * DPL + d] = o[d];
+    if (lane == 0) {
+        a.part_ml[slot * 2] = m;
+        a.part_ml[slot * 2 + 1] = l;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(a.ticket + blockIdx.x, 1) == S - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const size_t base = (size_t)h * a.max_splits;
+    double M = -INFINITY;
+    for (int q = lane; q < S; q += 32) M = fmax(M, __ldcg(a.part_ml + (base + q) * 2));
+    M = warp_max_d(M);
+    double Z = 0.0;
+    for (int q = lane; q < S; q += 32) Z += __ldcg(a.part_ml + (base + q) * 2 + 1) * exp(__ldcg(a.part_ml + (base + q) * 2) - M);
+    Z = warp_sum_d(Z);
+    float acc[DPL];
+#pragma unroll
+    for (int d = 0; d < DPL; d++) acc[d] = 0.0f;
+    for (int q0 = 0; q0 < S; q0 += 32) {
+        const float f = q0 + lane < S ? (float)exp(__ldcg(a.part_ml + (base + q0 + lane) * 2) - M) : 0.0f;
+        const int nq = min(32, S - q0);
+        for (int q = 0; q < nq; q++) {
+            const float w = __shfl_sync(kFull, f, q);
+            const float *po = a.part_o + (base + q0 + q) * D + lane * DPL;
+#pragma unroll
+            for (int d = 0; d < DPL; d++) acc[d] = __fmaf_rn(w, __ldcg(po + d), acc[d]);
+        }
+    }
+#pragma unroll
+    for (int d = 0; d < DPL; d++) out[d] = (float)((double)acc[d] / Z);
+    __syncthreads();
+    if (threadIdx.x == 0) a.ticket[blockIdx.x] = 0;
+}
+
+int launch_attention(const AttnArgs &a, cudaStream_t s) {
+    const int group = a.H / a.Hk, HB = attention_heads_per_cta(group);
+    const dim3 grid(a.Hk * (group / HB), a.split > 0 ? a.max_splits : 1, a.T);
+    if (a.D == 128) QMS_CK(launch_pdl(k_attention<128>, grid, dim3(32 * HB), 0, s, a));
+    else QMS_CK(launch_pdl(k_attention<64>, grid, dim3(32 * HB), 0, s, a));
+    return QMS_CUDA_OK;
+}
+
+}  // namespace qms

@@ -97,3 +97,162 @@ def zipf_router(layer: MoeLayer, s: float = 1.1, seed: int = 7, scale: float = 2
     return MoeLayer(layer.n_embd, layer.n_expert, layer.n_used, layer.n_ff,
                     np.ascontiguousarray(router, np.float32), layer.gate, layer.up, layer.down,
                     layer.gate_type, layer.up_type, layer.down_type)
+
+
+# ---- whole models (configs 1, 3 and 4) ------------------------------------------------------------
+# Architecture hyper-parameters of BASELINE.json's full-model configs. Every tensor is drawn from
+# its own generator, default_rng([seed, tensor index]), so any tensor can be produced on its own
+# (streamed into a GGUF file, or uploaded layer by layer) and always has the same bytes.
+
+@dataclass(frozen=True)
+class ModelCfg:
+    n_layer: int
+    n_embd: int
+    n_head: int
+    n_head_kv: int
+    head_dim: int
+    n_expert: int
+    n_used: int
+    n_ff: int
+    vocab: int
+    eps: float = 1e-6
+    rope_base: float = 1e6
+    output_type: int = T_Q6_K      # T_Q6_K, or -1 for tied embeddings (no output.weight)
+
+
+MODEL_CONFIGS = {
+    "tiny": ModelCfg(2, 512, 8, 2, 64, 32, 4, 256, 4096),                 # config 1
+    "tiny-tied": ModelCfg(2, 512, 8, 2, 64, 32, 4, 256, 4096, output_type=-1),
+    "30b": ModelCfg(48, 2048, 32, 4, 128, 128, 8, 768, 151936),           # config 3 (Qwen3-30B-A3B)
+    "235b": ModelCfg(94, 4096, 64, 4, 128, 128, 8, 1536, 151936),         # config 4 (Qwen3-235B-A22B)
+}
+
+
+def _raw_bytes(rng: np.random.Generator, n: int) -> np.ndarray:
+    """n uniform random bytes from full-range 64-bit integer draws (an order of magnitude faster
+    than Generator.bytes, which matters for the 16-124 GiB full models)."""
+    w = rng.integers(0, np.iinfo(np.uint64).max, (n + 7) // 8, dtype=np.uint64, endpoint=True)
+    return w.view(np.uint8)[:n]
+
+
+def q4_0_blocks_model(rng: np.random.Generator, nblocks: int) -> np.ndarray:
+    """Q4_0 blocks for the full-model configs: the distributions of q4_0_blocks, nibble bytes
+    from 64-bit integer draws."""
+    blk = np.empty((nblocks, 18), np.uint8)
+    blk[:, 0:2] = rng.uniform(0.002, 0.006, nblocks).astype(np.float16).view(np.uint8).reshape(nblocks, 2)
+    blk[:, 2:] = _raw_bytes(rng, nblocks * 16).reshape(nblocks, 16)
+    return blk.reshape(-1)
+
+
+def q6_k_blocks(rng: np.random.Generator, nblocks: int) -> np.ndarray:
+    """nblocks ggml Q6_K super-blocks {u8 ql[128]; u8 qh[64]; i8 scales[16]; f16 d} (210 bytes):
+    6-bit values uniform 0..63, sub-scales uniform 2..8, d U(1.5e-4, 3e-4), so the weights have
+    about the magnitude of the Q4_0 tensors (gguf-py cannot quantise Q6_K; these are raw blocks)."""
+    blk = np.empty((nblocks, 210), np.uint8)
+    blk[:, :192] = _raw_bytes(rng, nblocks * 192).reshape(nblocks, 192)
+    blk[:, 192:208] = rng.integers(2, 9, (nblocks, 16), dtype=np.int8).view(np.uint8)
+    blk[:, 208:210] = rng.uniform(1.5e-4, 3e-4, nblocks).astype(np.float16).view(np.uint8).reshape(nblocks, 2)
+    return blk.reshape(-1)
+
+
+_ROW_BYTES = {T_F32: (1, 4), T_F16: (1, 2), T_Q4_0: (32, 18), T_Q4_1: (32, 20), T_Q8_0: (32, 34), T_Q6_K: (256, 210)}
+
+
+def tensor_nbytes(typ: int, ne: tuple) -> int:
+    per, nbytes = _ROW_BYTES[typ]
+    n = int(np.prod(ne))
+    return n // per * nbytes
+
+
+def model_tensors(cfg: ModelCfg) -> list[tuple[str, int, tuple]]:
+    """(name, ggml type, ne) of every tensor, in file order; ne[0] is the contiguous dimension
+    (the layout qms_model_load expects, src/model.c:314-387)."""
+    E, D, H, Hk, X, F, V = cfg.n_embd, cfg.head_dim, cfg.n_head, cfg.n_head_kv, cfg.n_expert, cfg.n_ff, cfg.vocab
+    t = [("token_embd.weight", T_Q4_0, (E, V)), ("output_norm.weight", T_F32, (E,))]
+    if cfg.output_type >= 0:
+        t.append(("output.weight", cfg.output_type, (E, V)))
+    for l in range(cfg.n_layer):
+        b = f"blk.{l}."
+        t += [(b + "attn_norm.weight", T_F32, (E,)), (b + "attn_q_norm.weight", T_F32, (D,)),
+              (b + "attn_k_norm.weight", T_F32, (D,)), (b + "attn_q.weight", T_Q4_0, (E, H * D)),
+              (b + "attn_k.weight", T_Q4_0, (E, Hk * D)), (b + "attn_v.weight", T_Q4_0, (E, Hk * D)),
+              (b + "attn_output.weight", T_Q4_0, (H * D, E)), (b + "ffn_norm.weight", T_F32, (E,)),
+              (b + "ffn_gate_inp.weight", T_F32, (E, X)), (b + "ffn_gate_exps.weight", T_Q4_0, (E, F, X)),
+              (b + "ffn_up_exps.weight", T_Q4_0, (E, F, X)), (b + "ffn_down_exps.weight", T_Q4_0, (F, E, X))]
+    return t
+
+
+def tensor_data(cfg: ModelCfg, seed: int, index: int) -> np.ndarray:
+    """Bytes (uint8) or values (float32) of tensor `index` of model_tensors(cfg)."""
+    name, typ, ne = model_tensors(cfg)[index]
+    rng = np.random.default_rng([seed, index])
+    n = int(np.prod(ne))
+    if typ == T_F32:
+        if "ffn_gate_inp" in name:                       # router ~N(0, 0.02)
+            return (rng.standard_normal(n, dtype=np.float32) * np.float32(0.02)).reshape(ne[::-1])
+        return (1.0 + rng.standard_normal(n, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+    if typ == T_Q4_0:
+        return q4_0_blocks_model(rng, n // 32)
+    if typ == T_Q6_K:
+        return q6_k_blocks(rng, n // 256)
+    raise ValueError(f"no generator for type {typ}")
+
+
+def iter_model(cfg: ModelCfg, seed: int):
+    """Yield (name, type, ne, data) in file order."""
+    for i, (name, typ, ne) in enumerate(model_tensors(cfg)):
+        yield name, typ, ne, tensor_data(cfg, seed, i)
+
+
+def write_gguf(path, cfg: ModelCfg, seed: int, alignment: int = 32) -> int:
+    """Write a GGUF v3 qwen3moe file with the seeded tensors (the keys read_cfg requires,
+    src/model.c:279-312). Tensors are generated one at a time, so memory stays at one tensor.
+    Returns the file size."""
+    import struct
+
+    def s_str(b: str) -> bytes:
+        e = b.encode()
+        return struct.pack("<Q", len(e)) + e
+
+    U32, F32, STR = 4, 6, 8
+    kv = [("general.architecture", STR, "qwen3moe"), ("general.alignment", U32, alignment),
+          ("qwen3moe.block_count", U32, cfg.n_layer), ("qwen3moe.embedding_length", U32, cfg.n_embd),
+          ("qwen3moe.attention.head_count", U32, cfg.n_head),
+          ("qwen3moe.attention.head_count_kv", U32, cfg.n_head_kv),
+          ("qwen3moe.attention.key_length", U32, cfg.head_dim),
+          ("qwen3moe.attention.value_length", U32, cfg.head_dim),
+          ("qwen3moe.expert_count", U32, cfg.n_expert), ("qwen3moe.expert_used_count", U32, cfg.n_used),
+          ("qwen3moe.expert_feed_forward_length", U32, cfg.n_ff),
+          ("qwen3moe.attention.layer_norm_rms_epsilon", F32, cfg.eps),
+          ("qwen3moe.rope.freq_base", F32, cfg.rope_base)]
+    tensors = model_tensors(cfg)
+    head = bytearray(b"GGUF" + struct.pack("<IQQ", 3, len(tensors), len(kv)))
+    for key, vt, val in kv:
+        head += s_str(key) + struct.pack("<I", vt)
+        head += s_str(val) if vt == STR else struct.pack("<I" if vt == U32 else "<f", val)
+    off = 0
+    offsets = []
+    for name, typ, ne in tensors:
+        offsets.append(off)
+        head += s_str(name) + struct.pack("<I", len(ne)) + struct.pack(f"<{len(ne)}Q", *ne)
+        head += struct.pack("<IQ", typ, off)
+        off += (tensor_nbytes(typ, ne) + alignment - 1) // alignment * alignment
+    head += b"\0" * ((-len(head)) % alignment)
+    with open(path, "wb") as f:
+        f.write(head)
+        for i, (name, typ, ne) in enumerate(tensors):
+            data = tensor_data(cfg, seed, i)
+            raw = data.tobytes()
+            assert len(raw) == tensor_nbytes(typ, ne), name
+            f.write(raw)
+            f.write(b"\0" * ((-len(raw)) % alignment))
+        return f.tell()
+
+
+def model_bytes(cfg: ModelCfg) -> int:
+    return sum(tensor_nbytes(t, ne) for _, t, ne in model_tensors(cfg))
+
+
+def random_ids(vocab: int, n: int, seed: int) -> list[int]:
+    """Uniform random prompt ids (the configs' random-id prompts)."""
+    return [int(v) for v in np.random.default_rng(seed).integers(0, vocab, n)]

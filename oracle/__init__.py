@@ -202,6 +202,18 @@ class Reference:
         L.qms_dequant_row.argtypes = [i32, vp, vp, i64]
         L.qms_dequant_row.restype = i32
         L.qms_matmul.argtypes = [vp, vp, i32, vp]
+        L.ref_model_new.argtypes = [i32] * 9 + [C.c_float, C.c_double, i32]
+        L.ref_model_new.restype = vp
+        L.ref_model_set_trunk.argtypes = [vp, i32, vp, vp, i32, vp]
+        L.ref_model_set_layer.argtypes = [vp, i32, vp, vp, vp, vp, i32, vp, vp, vp, i32, vp, vp, i32, vp, vp, i32, vp]
+        L.ref_forward.argtypes = [vp, vp, i32, i32, vp, i32]
+        L.ref_forward.restype = i32
+        L.ref_model_free.argtypes = [vp]
+
+    def model(self, cfg, tensors: dict, ctx: int) -> "RefModel":
+        """The reference's own qms_forward on a model held in host arrays (GGUF names and layouts,
+        as large_model_b200.synth.model_tensors lists them)."""
+        return RefModel(self, cfg, tensors, ctx)
 
     def set_threads(self, n: int):
         self.lib.ref_set_threads(int(n))
@@ -244,6 +256,46 @@ class Reference:
         if rc != 0:
             raise RuntimeError(f"reference moe() returned {rc}")
         return (out, tr[: ntr.value].copy()) if trace else out
+
+
+class RefModel:
+    """A QmsModel built from host arrays by oracle/ref_harness.c; forward() is the reference's
+    qms_forward (src/model.c:1252-1296). The arrays are referenced, not copied: keep them alive."""
+
+    def __init__(self, ref: Reference, cfg, tensors: dict, ctx: int):
+        self.ref, self.cfg, self.keep = ref, cfg, tensors
+        L = ref.lib
+        c = cfg
+        self.h = L.ref_model_new(c.n_layer, c.n_embd, c.n_head, c.n_head_kv, c.head_dim, c.n_expert, c.n_used,
+                                 c.n_ff, c.vocab, float(c.eps), float(c.rope_base), int(ctx))
+        if not self.h:
+            raise MemoryError("ref_model_new failed")
+        t = tensors
+        out = t.get("output.weight")
+        L.ref_model_set_trunk(self.h, T_Q4_0, _p(t["token_embd.weight"]), _p(t["output_norm.weight"]),
+                              getattr(c, "output_type", T_Q6_K), None if out is None else _p(out))
+        for l in range(c.n_layer):
+            b = lambda n: _p(t[f"blk.{l}.{n}.weight"])
+            L.ref_model_set_layer(self.h, l, b("attn_norm"), b("attn_q_norm"), b("attn_k_norm"), b("ffn_norm"),
+                                  T_Q4_0, b("attn_q"), b("attn_k"), b("attn_v"), T_Q4_0, b("attn_output"),
+                                  b("ffn_gate_inp"), T_Q4_0, b("ffn_gate_exps"), b("ffn_up_exps"), T_Q4_0,
+                                  b("ffn_down_exps"))
+
+    def forward(self, ids, pos0: int, all_logits: bool = False) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.int32)
+        T = ids.shape[0]
+        logits = np.empty((T, self.cfg.vocab) if all_logits else (self.cfg.vocab,), np.float32)
+        if self.ref.lib.ref_forward(self.h, _p(ids), T, int(pos0), _p(logits), int(all_logits)) != 0:
+            raise RuntimeError("reference qms_forward failed")
+        return logits
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.ref.lib.ref_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
 
 
 def host_threads() -> int:

@@ -67,3 +67,75 @@ int ref_moe(int E, int X, int K, int F, int gate_type, int up_type, int down_typ
     free((void *)m.eptr);
     return rc;
 }
+
+/* ---- the reference's whole forward pass on a model built from host arrays ----------------------
+ * qms_model_load (src/model.c:314-387) without the file: the caller passes each tensor's host
+ * buffer (GGUF layout), which the model points at (not copied); KV cache and expert pointers are
+ * allocated as load does. ref_forward is the reference's own qms_forward (src/model.c:1252). */
+QmsModel *ref_model_new(int n_layer, int n_embd, int n_head, int n_head_kv, int head_dim, int n_expert,
+                        int n_used, int n_ff, int vocab, float eps, double rope_base, int ctx)
+{
+    QmsModel *m = (QmsModel *)calloc(1, sizeof *m);
+    if (!m) return NULL;
+    QmsCfg *c = &m->c;
+    c->n_layer = n_layer; c->n_embd = n_embd; c->n_head = n_head; c->n_head_kv = n_head_kv;
+    c->head_dim = head_dim; c->n_expert = n_expert; c->n_used = n_used; c->n_ff_exp = n_ff;
+    c->vocab = vocab; c->eps = eps; c->rope_base = rope_base;
+    m->ctx = ctx;
+    m->tr.n_pin = n_layer;
+    m->tr.slot_layer[0] = m->tr.slot_layer[1] = -1;
+    m->L = (QmsLayer *)calloc((size_t)n_layer, sizeof(QmsLayer));
+    m->eptr = (const unsigned char **)calloc(3 * (size_t)n_expert, sizeof(*m->eptr));
+    const size_t kv = (size_t)n_layer * ctx * n_head_kv * head_dim;
+    m->kc = (float *)calloc(kv, sizeof(float));
+    m->vc = (float *)calloc(kv, sizeof(float));
+    if (!m->L || !m->eptr || !m->kc || !m->vc) return NULL;
+    return m;
+}
+
+void ref_model_set_trunk(QmsModel *m, int embd_type, const void *embd, const float *out_norm, int out_type,
+                         const void *output)
+{
+    const QmsCfg *c = &m->c;
+    m->embd = mat(embd_type, c->vocab, c->n_embd, embd);
+    m->out_norm = (float *)out_norm;
+    m->output = output ? mat(out_type, c->vocab, c->n_embd, output) : m->embd;   /* tied (src/model.c:335) */
+}
+
+void ref_model_set_layer(QmsModel *m, int l, const float *attn_norm, const float *q_norm, const float *k_norm,
+                         const float *ffn_norm, int att_type, const void *q, const void *k, const void *v,
+                         int o_type, const void *o, const float *router, int gate_type, const void *gate,
+                         const void *up, int down_type, const void *down)
+{
+    const QmsCfg *c = &m->c;
+    QmsLayer *L = &m->L[l];
+    const int E = c->n_embd, QD = c->n_head * c->head_dim, KD = c->n_head_kv * c->head_dim, F = c->n_ff_exp;
+    L->attn_norm = (float *)attn_norm; L->q_norm = (float *)q_norm; L->k_norm = (float *)k_norm;
+    L->ffn_norm = (float *)ffn_norm;
+    L->q = mat(att_type, QD, E, q);
+    L->k = mat(att_type, KD, E, k);
+    L->v = mat(att_type, KD, E, v);
+    L->o = mat(o_type, E, QD, o);
+    L->router = mat(QMS_T_F32, c->n_expert, E, router);
+    L->gate.m = mat(gate_type, F, E, gate);
+    L->gate.expert_bytes = L->gate.m.row_bytes * (uint64_t)F;
+    L->up.m = mat(gate_type, F, E, up);
+    L->up.expert_bytes = L->up.m.row_bytes * (uint64_t)F;
+    L->down.m = mat(down_type, E, F, down);
+    L->down.expert_bytes = L->down.m.row_bytes * (uint64_t)E;
+}
+
+int ref_forward(QmsModel *m, const int *ids, int T, int pos0, float *logits, int all_logits)
+{
+    return qms_forward(m, ids, T, pos0, logits, all_logits);
+}
+
+void ref_model_free(QmsModel *m)
+{
+    if (!m) return;
+    free(m->L);
+    free((void *)m->eptr);
+    free(m->kc);
+    free(m->vc);
+    free(m);
+}

@@ -77,3 +77,63 @@ def test_declared_functions_cite_reference():
     text = (q.HEADER).read_text()
     for cite in ("src/kernels.h:15", "src/kernels.h:19", "src/kernels.h:21", "src/model.c:1032"):
         assert cite in text
+
+
+def _model_desc(**kw):
+    base = dict(n_layer=2, n_embd=512, n_head=8, n_head_kv=2, head_dim=64, n_expert=32, n_used=4, n_ff=256,
+                vocab=4096, eps=1e-6, rope_base=1e6, ctx=64, embd_type=q.T_Q4_0, embd=16, out_norm=16,
+                output_type=q.T_Q6_K, output=16, src_on_device=0)
+    base.update(kw)
+    return q.ModelDesc(**base)
+
+
+def _model_create(d):
+    h = C.c_void_p()
+    rc = q.lib().qms_cuda_model_create(C.byref(d), C.byref(h))
+    return rc, q.lib().qms_cuda_last_error().decode()
+
+
+def test_model_create_validates_config_before_any_device_call():
+    rc, msg = _model_create(_model_desc(head_dim=96))
+    assert rc == q.EUNSUPPORTED and "head_dim" in msg
+    rc, msg = _model_create(_model_desc(n_head=6, n_head_kv=4))      # n_head % n_head_kv (read_cfg's check)
+    assert rc == q.EINVAL and "inconsistent" in msg
+    rc, msg = _model_create(_model_desc(n_embd=288))
+    assert rc == q.EUNSUPPORTED and "256" in msg
+    rc, msg = _model_create(_model_desc(output_type=q.T_Q8_0))
+    assert rc == q.EUNSUPPORTED and "output type" in msg
+    rc, msg = _model_create(_model_desc(embd_type=7))
+    assert rc == q.EUNSUPPORTED and "token_embd" in msg
+    rc, msg = _model_create(_model_desc(embd=None))
+    assert rc == q.EINVAL
+    rc, msg = _model_create(_model_desc(ctx=0))
+    assert rc == q.EINVAL
+
+
+def test_model_calls_validate_arguments():
+    L = q.lib()
+    p = C.c_void_p(16)
+    assert L.qms_cuda_forward(None, p, 1, 0, p, 0, None) == q.EINVAL
+    assert L.qms_cuda_forward_dev(None, p, 1, p, p, 0, None) == q.EINVAL
+    assert L.qms_cuda_decode_step(None, p, p, None, None) == q.EINVAL
+    assert L.qms_cuda_model_set_layer(None, 0, None) == q.EINVAL
+    assert L.qms_cuda_model_reserve(None, 4) == q.EINVAL
+    assert L.qms_cuda_model_status(None) == q.EINVAL
+    assert L.qms_cuda_model_profile(None, 1, None) == q.EINVAL
+    assert L.qms_cuda_model_device_bytes(None) == 0
+    L.qms_cuda_model_free(None)                                     # no-op
+
+
+def test_noalloc_route_validates_before_any_device_call():
+    """qms_cuda_moe_route_noalloc refuses sizes beyond its fixed scratch before any CUDA call."""
+    L = q.lib()
+    p = C.c_void_p(256)
+    assert L.qms_cuda_moe_route_noalloc(p, 128, 4096, 8, p, 65, p, p, None, None) == q.EINVAL   # T > 64
+    assert "64" in L.qms_cuda_last_error().decode()
+    assert L.qms_cuda_moe_route_noalloc(p, 128, 8192, 8, p, 1, p, p, None, None) == q.EINVAL    # n_embd > 4096
+    assert L.qms_cuda_moe_route_noalloc(p, 128, 4000, 8, p, 1, p, p, None, None) == q.EINVAL    # n_embd % 256
+    assert L.qms_cuda_moe_route_noalloc(p, 300, 4096, 8, p, 1, p, p, None, None) == q.EINVAL    # n_expert > 256
+    assert L.qms_cuda_moe_route_noalloc(p, 128, 128, 8, p, 1, p, p, None, None) == q.EINVAL     # 2 X > E
+    assert L.qms_cuda_moe_route_noalloc(None, 128, 4096, 8, p, 1, p, p, None, None) == q.EINVAL
+    assert L.qms_cuda_moe_route_noalloc(p, 128, 4096, 8, p, 1, None, p, None, None) == q.EINVAL
+    assert L.qms_cuda_moe_route_noalloc(C.c_void_p(260), 128, 4096, 8, p, 1, p, p, None, None) == q.EINVAL  # router alignment

@@ -1,6 +1,15 @@
-"""Benchmark of the Qwen3-MoE feed-forward hot path on B200 (libqms_cuda through its C ABI).
+"""Benchmarks of the Qwen3-MoE path on B200 (libqms_cuda through its C ABI).
 
-Workload: the Qwen3-235B-A22B MoE layer operator at decode batch 1 —
+Default (--mode model, BASELINE.json config 4 at batch 1): Qwen3-235B-A22B, the whole model on one
+GPU - 94 layers, hidden 4096, 64 Q / 4 KV heads x 128, 128 experts top-8, moe_intermediate 1536,
+Q4_0 weights and a Q6_K head drawn on the device with the configs' distributions (124 GiB resident),
+fp32 KV cache of 4096 positions. A 1024-id random prompt is prefilled, then a step is 32 greedy
+decode tokens: qms_cuda_decode_step captured once in a CUDA graph (argmax, position and next
+embedding stay on the device). The metric is decode tokens/s; the roofline compares the bytes one
+token must read (weights of the 8 selected experts in every layer, attention weights, the head, the
+KV cache) with the measured HBM bandwidth.
+
+--mode moe: the Qwen3-235B-A22B MoE layer operator at decode batch 1 —
 hidden 4096, 128 experts, top-8, moe_intermediate 1536, Q4_0 experts, F32 router — on 1000
 seeded tokens, each an independent T=1 call. Calls cycle through 8 resident layers with
 independent seeded weights (8 x 1.36 GB), so consecutive calls share no weights and every
@@ -8,7 +17,7 @@ step's inputs are far larger than L2. A step is the 1000 calls; the metric is th
 algorithmic HBM bytes (8 experts x 10,616,832 B + 2,097,152 B router = 87,031,808 B per
 token-layer) divided by time.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--mode model|moe|bs64|prefill]
 
 N > 1 runs N independent replicas (one per GPU, launched by torch.distributed.run): batch-1
 decode does not shard, so there is no collective on the data path (scaling "weak").
@@ -415,6 +424,295 @@ def run_batched(a):
     return 0
 
 
+# ---- the whole model (config 4, batch 1) ------------------------------------------------------------
+
+MODEL_METRIC = "Qwen3-235B-A22B Q4_0 decode tok/s (bs1, whole model on one B200)"
+MODEL_PROMPT = 1024
+MODEL_CTX = 4096
+TOKENS_PER_STEP = 32
+
+
+def model_cfg():
+    from large_model_b200 import synth
+    return synth.MODEL_CONFIGS["235b"]
+
+
+def model_bytes_per_token(cfg, pos: float) -> dict:
+    """Algorithmic bytes one decode token at position `pos` must read, by part (GGUF sizes):
+    per layer the router and 8 experts, the q/k/v/o projections, the fp32 K and V rows of every
+    earlier position, the norms; plus the embedding row and the Q6_K head."""
+    E, X, K, F, L = cfg.n_embd, cfg.n_expert, cfg.n_used, cfg.n_ff, cfg.n_layer
+    QD, KD = cfg.n_head * cfg.head_dim, cfg.n_head_kv * cfg.head_dim
+    moe = K * 3 * F * (E // 32) * 18 + X * E * 4
+    attn = (QD + 2 * KD) * (E // 32) * 18 + E * (QD // 32) * 18
+    kv = 2 * KD * 4 * (pos + 1)
+    norms = (2 * E + 2 * cfg.head_dim) * 4
+    head = cfg.vocab * (E // 256) * 210
+    parts = {"moe": L * moe, "attention_weights": L * attn, "kv_cache": L * kv, "norms": L * norms + E * 4,
+             "head": head, "embedding_row": (E // 32) * 18}
+    parts["total"] = sum(parts.values())
+    return parts
+
+
+def device_model(q, torch, cfg, seed: int, dev, ctx: int):
+    """The 235B architecture drawn on the device with the configs' distributions (Q4_0 nibbles
+    uniform 0..15 with fp16 scales U(0.002, 0.006), router N(0, 0.02), norms 1 + N(0, 0.01), a Q6_K
+    head of uniform 6-bit values) and uploaded layer by layer from device memory (qms_cuda_model_*)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    E, D, H, Hk, X, F, V = cfg.n_embd, cfg.head_dim, cfg.n_head, cfg.n_head_kv, cfg.n_expert, cfg.n_ff, cfg.vocab
+
+    def q4_0(n):
+        nb = n // 32
+        blk = torch.empty((nb, 18), dtype=torch.uint8, device=dev)
+        blk[:, 0:2] = (torch.rand(nb, generator=g, device=dev) * 0.004 + 0.002).to(torch.float16).view(torch.uint8).view(nb, 2)
+        blk[:, 2:] = torch.randint(-2 ** 31, 2 ** 31 - 1, (nb, 4), generator=g, device=dev, dtype=torch.int32).view(torch.uint8).view(nb, 16)
+        return blk.view(-1)
+
+    def q6_k(n):
+        nb = n // 256
+        blk = torch.empty((nb, 210), dtype=torch.uint8, device=dev)
+        blk[:, :192] = torch.randint(-2 ** 31, 2 ** 31 - 1, (nb, 48), generator=g, device=dev, dtype=torch.int32).view(torch.uint8).view(nb, 192)
+        blk[:, 192:208] = torch.randint(2, 9, (nb, 16), generator=g, device=dev, dtype=torch.uint8)
+        blk[:, 208:210] = (torch.rand(nb, generator=g, device=dev) * 1.5e-4 + 1.5e-4).to(torch.float16).view(torch.uint8).view(nb, 2)
+        return blk.view(-1)
+
+    def norm(n):
+        return 1.0 + 0.01 * torch.randn(n, generator=g, device=dev, dtype=torch.float32)
+
+    trunk = {"token_embd.weight": q4_0(V * E), "output_norm.weight": norm(E), "output.weight": q6_k(V * E)}
+    m = q.Model(cfg, trunk, ctx)
+    del trunk
+    QD, KD = H * D, Hk * D
+    for l in range(cfg.n_layer):
+        t = {"attn_norm": norm(E), "attn_q_norm": norm(D), "attn_k_norm": norm(D), "ffn_norm": norm(E),
+             "attn_q": q4_0(QD * E), "attn_k": q4_0(KD * E), "attn_v": q4_0(KD * E), "attn_output": q4_0(E * QD),
+             "ffn_gate_inp": torch.randn((X, E), generator=g, device=dev, dtype=torch.float32) * 0.02,
+             "ffn_gate_exps": q4_0(X * F * E), "ffn_up_exps": q4_0(X * F * E), "ffn_down_exps": q4_0(X * E * F)}
+        m.set_layer(l, t)
+        del t
+    torch.cuda.synchronize()
+    return m
+
+
+def host_model_tensors(cfg, seed: int) -> dict:
+    """The same architecture as host arrays (numpy, seeded) for the reference's CPU forward."""
+    from large_model_b200 import synth
+    out = {}
+    for i, (name, typ, ne) in enumerate(synth.model_tensors(cfg)):
+        out[name] = np.ascontiguousarray(synth.tensor_data(cfg, seed, i))
+    return out
+
+
+def cpu_model_sample(layers=(2, 8), decode_tokens: int = 8, prompt: int = 256, seed: int = 77):
+    """The reference's own qms_forward (oracle/_ref, compiled from its sources) on 235B-shape models
+    of `layers` layers in host RAM (the full 94-layer model needs ~135 GB of host memory): each
+    model prefills a random prompt, then decodes `decode_tokens` tokens one call at a time. The time
+    per token is linear in the layer count (t = fixed + L * per_layer: embedding and head, then
+    identical layers), so two sizes give the 94-layer time. Returns (seconds per 94-layer token,
+    description, threads)."""
+    import dataclasses
+    from oracle import Reference, host_threads
+    ref = Reference()
+    threads = host_threads()
+    ref.set_threads(threads)
+    base = model_cfg()
+    per_tok = {}
+    for L in layers:
+        cfg = dataclasses.replace(base, n_layer=L)
+        t = host_model_tensors(cfg, seed)
+        m = ref.model(cfg, t, prompt + decode_tokens + 4)
+        ids = [int(v) for v in np.random.default_rng(seed).integers(0, cfg.vocab, prompt)]
+        logits = m.forward(ids, 0)
+        nxt = int(np.argmax(logits))
+        m.forward([nxt], prompt)                                   # warm-up (thread pool, page-in)
+        ts = []
+        for k in range(decode_tokens):
+            t0 = time.perf_counter()
+            logits = m.forward([int(np.argmax(logits))], prompt + 1 + k)
+            ts.append(time.perf_counter() - t0)
+        per_tok[L] = statistics.median(ts)
+        m.close()
+        del t
+    (l0, l1) = layers
+    per_layer = (per_tok[l1] - per_tok[l0]) / (l1 - l0)
+    fixed = per_tok[l0] - l0 * per_layer
+    t94 = fixed + base.n_layer * per_layer
+    desc = (f"reference qms_forward ({ref.variant} build, {threads} OpenMP threads) on 235B-shape models of "
+            f"{l0} and {l1} layers in host RAM, {prompt}-id prompt then {decode_tokens} decode tokens each (median): "
+            f"{per_tok[l0] * 1e3:.1f} / {per_tok[l1] * 1e3:.1f} ms per token -> {per_layer * 1e3:.2f} ms per layer, "
+            f"{fixed * 1e3:.1f} ms head + embedding; 94 layers: {t94 * 1e3:.1f} ms per token "
+            f"(attention at position ~{prompt}, the device run decodes at ~{MODEL_PROMPT})")
+    return t94, desc, threads
+
+
+def run_model_reference_arm(a):
+    """--impl reference for the model metric: the reference's qms_forward on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    t0 = time.perf_counter()
+    t94, desc, threads = cpu_model_sample(decode_tokens=max(8, a.steps))
+    value = 1.0 / t94
+    line = {"impl": "reference", "metric": MODEL_METRIC, "value": round(value, 4), "unit": "tok/s",
+            "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t94 * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp32",
+            "data": "synthetic",
+            "config": {"workload": "Qwen3-235B-A22B decode, batch 1 (config 4); reference arm: each step one "
+                                   "decode token on each sampled model", "sample": desc,
+                       "wall_s": round(time.perf_counter() - t0, 1)},
+            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "reference",
+                             "sample": desc},
+            "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_model(a):
+    import torch
+    import large_model_b200 as q
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    q.init(local)
+    dev = torch.device("cuda", local)
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:            # before the GPU model takes host time
+        t94, desc, threads = cpu_model_sample()
+        cpu = {"value": round(1.0 / t94, 4), "unit": "tok/s", "cores": threads, "kind": "reference", "sample": desc}
+    cfg = model_cfg()
+    t_build = time.perf_counter()
+    m = device_model(q, torch, cfg, 4242 + rank, dev, MODEL_CTX)
+    t_build = time.perf_counter() - t_build
+    rng = np.random.default_rng(99 + rank)
+    prompt = [int(v) for v in rng.integers(0, cfg.vocab, MODEL_PROMPT)]
+    t_pre = time.perf_counter()
+    logits = m.forward(prompt, 0)
+    t_pre = time.perf_counter() - t_pre
+    room = MODEL_CTX - MODEL_PROMPT - 64                     # positions left for decode (the last 64 for the
+    per_step = max(1, min(TOKENS_PER_STEP, room // (a.steps + a.warmup + 1)))   # section timers and e2e)
+    stream = torch.cuda.Stream(device=dev)
+    tok = torch.tensor([int(np.argmax(logits))], dtype=torch.int32, device=dev)
+    pos = torch.tensor([MODEL_PROMPT], dtype=torch.int32, device=dev)
+    lg = torch.empty(cfg.vocab, dtype=torch.float32, device=dev)
+    with torch.cuda.stream(stream):
+        m.decode_step(tok, pos, lg, stream=stream)            # outside capture: first-use setup
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(per_step):
+                m.decode_step(tok, pos, lg, stream=stream)
+        for _ in range(a.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    pos0 = int(pos.item())
+    sampler = ClockSampler(local)
+    time.sleep(0.5)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(a.steps):
+            graph.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    pos1 = int(pos.item())
+    m.status()
+    ntok = a.steps * per_step
+    tok_s = ntok * world / (ms / 1e3)
+    bt = model_bytes_per_token(cfg, (pos0 + pos1) / 2)
+    step_gbs = bt["total"] * ntok / (ms / 1e3) / 1e9
+    # section times per token (CUDA events around each section of a token step; they serialise the
+    # programmatic overlap between kernels, so their sum is a little above the graph's time per token)
+    m.profile(True)
+    nprof = 8 if int(pos.item()) + 40 < MODEL_CTX else 1
+    for k in range(nprof):
+        lp = m.forward([int(tok.item())], int(pos.item()))
+        tok.fill_(int(np.argmax(lp)))
+        pos.add_(1)
+    sec = [v / nprof for v in m.profile(False)]
+    names = ["qkv", "attn", "o_proj", "router", "fetch", "moe", "output"]
+    moe_us_layer = sec[5] * 1e3 / cfg.n_layer
+    moe_gbs = bytes_per_token_layer() / (moe_us_layer / 1e6) / 1e9
+    # end to end through the host-buffer entry point: ids in, every token's logits out (as
+    # main.c's decode loop does: it reads the logits on the host, src/main.c:198-207)
+    e2e_n = max(1, min(24, MODEL_CTX - int(pos.item()) - 2))
+    lp = m.forward([int(tok.item())], int(pos.item()))
+    p_e = int(pos.item()) + 1
+    nxt = int(np.argmax(lp))
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for k in range(e2e_n):
+        lp = m.forward([nxt], p_e + k)
+        nxt = int(np.argmax(lp))
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    peak, peak_kind = peaks()
+    if rank == 0:
+        line = {
+            "metric": MODEL_METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
+            "config": {"workload": "Qwen3-235B-A22B (config 4) decode batch 1: 94 layers, 128 experts top-8, Q4_0 "
+                                   "weights + Q6_K head drawn on the device (seeded torch RNG), fp32 KV ctx 4096, "
+                                   f"{MODEL_PROMPT}-id random prompt prefilled; a step = {per_step} greedy "
+                                   f"decode tokens (qms_cuda_decode_step x{per_step} in one CUDA graph)",
+                       "tokens_per_step": per_step, "positions": [pos0, pos1],
+                       "ms_per_token": round(ms / ntok, 4), "device_gb": round(m.device_bytes / 1e9, 2),
+                       "build_s": round(t_build, 1), "prefill_s": round(t_pre, 2),
+                       "bytes_per_token": {k: int(v) for k, v in bt.items()},
+                       "section_ms_per_token": {n: round(v, 4) for n, v in zip(names, sec)},
+                       "moe_layer": {"us": round(moe_us_layer, 2), "gbs": round(moe_gbs, 1),
+                                     "note": "ffn RMSNorm + k_decode_bs1 per layer, from the section timers"},
+                       "l2": "inputs far larger than L2 (124 GiB of weights)",
+                       "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "kernel": "whole decode step (embedding, per layer QKV / RoPE+KV / attention "
+                                                   "/ O / RMSNorm / MoE, head + argmax)",
+                         "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(step_gbs / peak, 4),
+                         "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                         "traffic": None,
+                         "dominant_kernel": {"name": "k_decode_bs1 (MoE block)", "us_per_launch": round(moe_us_layer, 2),
+                                             "achieved": round(moe_gbs, 1), "frac": round(moe_gbs / peak, 4),
+                                             "bytes_per_launch": bytes_per_token_layer(),
+                                             "share_of_step": round(sec[5] / max(1e-9, sum(sec)), 3)}},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_n * world / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": cfg.vocab * 4,
+                    "note": "qms_cuda_forward per token (host id in, the token's 151936 logits to host memory, "
+                            "argmax on the host), per token; h2d/d2h bytes are per token"},
+            "gpu_launches": ntok * (2 + 6 * cfg.n_layer),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    m.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -425,13 +723,15 @@ def main():
     ap.add_argument("--tokens", type=int, default=TOKENS)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--mode", default="decode", choices=["decode", "bs64", "prefill"])
+    ap.add_argument("--mode", default="model", choices=["model", "moe", "bs64", "prefill"])
     ap.add_argument("--ep", action="store_true", help="batched modes under torchrun: shard the experts over the ranks")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":
-        return run_reference_arm(a)
-    if a.mode != "decode":
+        return run_model_reference_arm(a) if a.mode == "model" else run_reference_arm(a)
+    if a.mode == "model":
+        return run_model(a)
+    if a.mode != "moe":
         return run_batched(a)
 
     import torch

@@ -229,9 +229,8 @@ int qms_cuda_forward(QmsCudaModel *m, const int *ids, int T, int pos0, float *lo
 
 /* The same on device buffers, asynchronously on `stream`: ids (device int [T]); *pos (device int)
  * is the position of ids[0] and is read by the kernels, so a captured graph can be replayed as
- * the position advances. logits: device fp32 [all_logits ? T : 1][vocab]. T must not exceed the
- * scratch reserved with qms_cuda_model_reserve (default 1); positions beyond ctx or invalid ids
- * are not written and set the error reported by qms_cuda_model_status. */
+ * the position advances. logits: device fp32 [all_logits ? T : 1][vocab]. 1 <= T <= 256; positions
+ * beyond ctx or invalid ids are not written and set the error reported by qms_cuda_model_status. */
 int qms_cuda_forward_dev(QmsCudaModel *m, const int *ids, int T, const int *pos, float *logits,
                          int all_logits, void *stream);
 /* One greedy decode step entirely on the device (src/main.c:198-207, inc mode): the token *tok at
@@ -240,7 +239,9 @@ int qms_cuda_forward_dev(QmsCudaModel *m, const int *ids, int T, const int *pos,
  * and logits (device fp32 [vocab], optional) receive the step's logits. Graph-capturable: a graph
  * of N steps generates N tokens with no host round trip. */
 int qms_cuda_decode_step(QmsCudaModel *m, int *tok, int *pos, float *logits, void *stream);
-/* Make sure the forward's scratch covers T tokens (capture-safe afterwards). */
+/* The forward's scratch covers up to 256 tokens per pass from creation on (longer calls run in
+ * passes of 256), so device pointers never move and captured graphs stay valid; T > 256 is
+ * QMS_CUDA_EINVAL. */
 int qms_cuda_model_reserve(QmsCudaModel *m, int T);
 /* Waits for the device; QMS_CUDA_EINVAL if a device-side check (position beyond ctx, bad id)
  * refused work since the last call, QMS_CUDA_ETIMEOUT if a MoE kernel's bounded wait gave up. */

@@ -32,7 +32,7 @@ using namespace qms;
 
 namespace qms {
 constexpr int kChunk = 256;          // tokens per forward pass over the layers (prefill)
-constexpr int kSplit = 64;           // positions per attention CTA in one-token steps
+constexpr int kSplit = kAttnBlock;   // positions per attention CTA in one-token steps
 
 struct DevLayer {
     float *norms = nullptr;          // attn_norm [E], ffn_norm [E], q_norm [D], k_norm [D]
@@ -239,7 +239,7 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
     at.Hk = m->Hk;
     at.D = m->D;
     at.scale = 1.0 / sqrt((double)m->D);
-    at.split = T == 1 ? kSplit : 0;
+    at.split = 0;                    // several tokens: one CTA per head group and token
     at.max_splits = m->max_splits;
     at.part_o = m->part_o;
     at.part_ml = m->part_ml;
@@ -248,9 +248,52 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
     at.err = m->err;
     for (int l = 0; l < m->L; l++) {
         const DevLayer &L = m->layers[l];
-        // attention block input: RMSNorm(attn_norm) -> QKV
+        at.q_norm = L.q_norm;
+        at.k_norm = L.k_norm;
+        at.kc = m->kc + (size_t)l * m->ctx * m->KD;
+        at.vc = m->vc + (size_t)l * m->ctx * m->KD;
+        int *sel_l = sel ? sel + (size_t)l * T * m->K : nullptr;
         GemvArgs g;
         memset(&g, 0, sizeof g);
+        if (T == 1) {
+            // one token: streaming projections, fused attention, RMSNorm inside the MoE kernel
+            g.w = L.wqkv;
+            g.stride = rows_stride(L.qkv_type, E);
+            g.rows = m->NQKV;
+            g.ncol = E;
+            g.T = 1;
+            g.x = m->h;
+            g.nw = L.attn_norm;
+            g.eps = m->eps;
+            g.y = m->qkv;
+            if ((rc = launch_gemv1(L.qkv_type, g, m->err, s))) return rc;
+            if ((rc = prof_mark(m, ei++, s))) return rc;
+            if ((rc = launch_attn_decode(at, m->xq, m->xd, m->xs, s))) return rc;
+            if ((rc = prof_mark(m, ei++, s))) return rc;
+            memset(&g, 0, sizeof g);
+            g.w = L.wo;
+            g.stride = rows_stride(L.o_type, m->QD);
+            g.rows = E;
+            g.ncol = m->QD;
+            g.T = 1;
+            g.xq = m->xq;
+            g.xd = m->xd;
+            g.xs = m->xs;
+            g.y = m->h;
+            g.resid = m->h;
+            if ((rc = launch_gemv1(L.o_type, g, m->err, s))) return rc;
+            if ((rc = prof_mark(m, ei++, s))) return rc;
+            rc = moe_forward_normed_bs1(L.moe, m->h, L.ffn_norm, m->eps, m->h, m->h, sel_l, s);
+            if (rc == QMS_CUDA_EUNSUPPORTED) {
+                clear_error();
+                if ((rc = launch_rmsnorm(m->h, L.ffn_norm, m->eps, 1, E, m->xn, nullptr, nullptr, nullptr, s))) return rc;
+                rc = qms_cuda_moe_forward(L.moe, m->xn, 1, m->h, sel_l, nullptr, nullptr, m->h, s);
+            }
+            if (rc) return rc;
+            if ((rc = prof_mark(m, ei++, s))) return rc;
+            continue;
+        }
+        // several tokens: RMSNorm(attn_norm) -> Q8 rows -> QKV
         g.w = L.wqkv;
         g.stride = rows_stride(L.qkv_type, E);
         g.rows = m->NQKV;
@@ -259,22 +302,12 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
         g.eps = m->eps;
         g.y = m->qkv;
         g.ldy = m->NQKV;
-        if (T == 1) {
-            g.x = m->h;
-            g.ldx = E;
-            g.nw = L.attn_norm;
-        } else {
-            if ((rc = launch_rmsnorm(m->h, L.attn_norm, m->eps, T, E, nullptr, m->xq, m->xd, m->xs, s))) return rc;
-            g.xq = m->xq;
-            g.xd = m->xd;
-            g.xs = m->xs;
-        }
+        if ((rc = launch_rmsnorm(m->h, L.attn_norm, m->eps, T, E, nullptr, m->xq, m->xd, m->xs, s))) return rc;
+        g.xq = m->xq;
+        g.xd = m->xd;
+        g.xs = m->xs;
         if ((rc = launch_gemv(L.qkv_type, g, s))) return rc;
         if ((rc = prof_mark(m, ei++, s))) return rc;
-        at.q_norm = L.q_norm;
-        at.k_norm = L.k_norm;
-        at.kc = m->kc + (size_t)l * m->ctx * m->KD;
-        at.vc = m->vc + (size_t)l * m->ctx * m->KD;
         if ((rc = launch_qk_rope(at, s))) return rc;
         if ((rc = launch_attention(at, s))) return rc;
         if ((rc = prof_mark(m, ei++, s))) return rc;
@@ -288,22 +321,15 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
         g.y = m->h;
         g.ldy = E;
         g.resid = m->h;
-        if (T == 1) {
-            g.x = m->att;
-            g.ldx = m->QD;
-        } else {
-            if ((rc = launch_rmsnorm(m->att, nullptr, 0.0f, T, m->QD, nullptr, m->xq, m->xd, m->xs, s))) return rc;
-            g.xq = m->xq;
-            g.xd = m->xd;
-            g.xs = m->xs;
-        }
+        if ((rc = launch_rmsnorm(m->att, nullptr, 0.0f, T, m->QD, nullptr, m->xq, m->xd, m->xs, s))) return rc;
+        g.xq = m->xq;
+        g.xd = m->xd;
+        g.xs = m->xs;
         if ((rc = launch_gemv(L.o_type, g, s))) return rc;
         if ((rc = prof_mark(m, ei++, s))) return rc;
         // MoE block + residual
         if ((rc = launch_rmsnorm(m->h, L.ffn_norm, m->eps, T, E, m->xn, nullptr, nullptr, nullptr, s))) return rc;
-        if ((rc = qms_cuda_moe_forward(L.moe, m->xn, T, m->h, sel ? sel + (size_t)l * T * m->K : nullptr, nullptr,
-                                       nullptr, m->h, s)))
-            return rc;
+        if ((rc = qms_cuda_moe_forward(L.moe, m->xn, T, m->h, sel_l, nullptr, nullptr, m->h, s))) return rc;
         if ((rc = prof_mark(m, ei++, s))) return rc;
     }
     // final norm + head: the last token, or all of them
@@ -318,23 +344,24 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
     g.ldy = m->V;
     const int nT = all ? T : 1;
     g.T = nT;
-    if (nT == 1) {
-        g.x = m->h + (size_t)(T - 1) * E;
-        g.ldx = E;
-        g.nw = m->out_norm;
-    } else {
-        if ((rc = launch_rmsnorm(m->h, m->out_norm, m->eps, nT, E, nullptr, m->xq, m->xd, m->xs, s))) return rc;
-        g.xq = m->xq;
-        g.xd = m->xd;
-        g.xs = m->xs;
-    }
     if (tok) {
         g.amax = m->amax;
         g.ticket = m->amax_ticket;
         g.tok = tok;
         g.pos = pos_adv;
     }
-    if ((rc = launch_gemv(m->head_type, g, s))) return rc;
+    if (nT == 1) {
+        g.x = m->h + (size_t)(T - 1) * E;
+        g.ldx = E;
+        g.nw = m->out_norm;
+        if ((rc = launch_gemv1(m->head_type, g, m->err, s))) return rc;
+    } else {
+        if ((rc = launch_rmsnorm(m->h, m->out_norm, m->eps, nT, E, nullptr, m->xq, m->xd, m->xs, s))) return rc;
+        g.xq = m->xq;
+        g.xd = m->xd;
+        g.xs = m->xs;
+        if ((rc = launch_gemv(m->head_type, g, s))) return rc;
+    }
     if ((rc = prof_mark(m, ei++, s))) return rc;
     return QMS_CUDA_OK;
 }
@@ -397,6 +424,8 @@ int qms_cuda_model_create(const QmsCudaModelDesc *d, QmsCudaModel **out) {
                 QMS_CUDA_EINVAL, "model_create: bad dimensions");
     QMS_REQUIRE(d->n_head % d->n_head_kv == 0 && d->n_used <= d->n_expert, QMS_CUDA_EINVAL,
                 "model_create: inconsistent config (n_head %% n_head_kv, n_used <= n_expert)");
+    QMS_REQUIRE(d->ctx <= kAttnMaxCtx, QMS_CUDA_EUNSUPPORTED, "model_create: ctx %d > %d", d->ctx, kAttnMaxCtx);
+    QMS_REQUIRE(d->n_head / d->n_head_kv <= 16, QMS_CUDA_EUNSUPPORTED, "model_create: more than 16 q heads per kv head");
     QMS_REQUIRE(d->head_dim == 64 || d->head_dim == 128, QMS_CUDA_EUNSUPPORTED,
                 "model_create: head_dim %d (64 or 128 supported)", d->head_dim);
     const int group = d->n_head / d->n_head_kv, HB = attention_heads_per_cta(group);
@@ -482,7 +511,9 @@ int qms_cuda_model_create(const QmsCudaModelDesc *d, QmsCudaModel **out) {
         rc = QMS_CUDA_ECUDA;
     }
     m->weight_bytes = (size_t)m->V * (erb + rows_stride(ht, m->E)) + (size_t)m->E * 4;
-    if (!rc) rc = model_reserve(m, 1);
+    // the whole prefill chunk at once: the scratch never moves afterwards, so decode steps captured
+    // in a CUDA graph stay valid whatever the caller runs next
+    if (!rc) rc = model_reserve(m, kChunk);
     if (rc) {
         qms_cuda_model_free(m);
         return rc;

@@ -764,6 +764,22 @@ int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int 
     return QMS_CUDA_OK;
 }
 
+}  // extern "C"
+
+namespace qms {
+int moe_forward_normed_bs1(QmsCudaMoe *m, const float *h, const float *nw, float eps, float *out,
+                           const float *resid, int *sel, cudaStream_t s) {
+    if (!m->stream_ok || m->n_local != m->X || m->E % 512 || ((uintptr_t)h & 15) || m->cap_T < 1)
+        return QMS_CUDA_EUNSUPPORTED;
+    int rc = stream_forward_bs1(m, h, out, resid, s, nw, eps);
+    if (rc) return rc;
+    if (sel) QMS_CK(cudaMemcpyAsync(sel, m->sel, (size_t)m->K * 4, cudaMemcpyDeviceToDevice, s));
+    return QMS_CUDA_OK;
+}
+}  // namespace qms
+
+extern "C" {
+
 int qms_cuda_moe_route(QmsCudaMoe *m, const float *xn, int T, int *sel, float *wts, float *logits, void *stream) {
     QMS_REQUIRE(m && T >= 0, QMS_CUDA_EINVAL, "moe_route: bad arguments");
     if (T == 0) return QMS_CUDA_OK;

@@ -225,7 +225,13 @@ static cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t 
 
 // batch-1 decode kernels (qms_moe_stream.cu)
 int stream_prepare(QmsCudaMoe *m);     // shape check + kernel attributes; sets m->stream_ok
-int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *resid, cudaStream_t s);
+int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *resid, cudaStream_t s,
+                       const float *nw = nullptr, float eps = 0.0f);
+// One token through the layer with its input RMS-normed inside the batch-1 kernel:
+// out = resid + moe(RMSNorm(h) * nw). Returns QMS_CUDA_EUNSUPPORTED when the batch-1 kernel does
+// not serve this layer (the caller then normalises separately).
+int moe_forward_normed_bs1(QmsCudaMoe *m, const float *h, const float *nw, float eps, float *out,
+                           const float *resid, int *sel, cudaStream_t s);
 struct StreamScratch {                 // bytes of the batch-1 kernel's exchange buffers
     size_t lg_flagged, stamps, aq_flagged, part_gu, fin;
 };

@@ -287,6 +287,8 @@ __device__ void route_weights(const float *lg, int X, int K, const int *s_sel, d
 struct DecodeArgs {
     const float *router_lm;               // [X][16][E/16]: element 16*i + k of a row at [k][i]
     const float *xn, *resid;
+    const float *nw;                      // optional: xn = RMSNorm(xn) * nw first (ffn_norm, src/model.c:1283)
+    float eps;
     float *out;
     const uint8_t *gu, *dn;               // staged experts: gate/up chunks, down column stages
     size_t gu_expert, dn_expert;
@@ -377,6 +379,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
     float *srow = reinterpret_cast<float *>(ring);                  // [16][PS] router row, lane-major
     float *sx = srow + 16 * PS;                                     // [16][PS] xn, lane-major
     __shared__ int s_abort;
+    __shared__ double s_nrm[kConsumerWarps];
     __shared__ const uint8_t *s_gu_base[8], *s_dn_base[8];   // producer: streamed experts' weights
     __shared__ int s_spec[8];                                  // producer: the experts being streamed
     __shared__ int s_sel[64];
@@ -589,6 +592,30 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
         reinterpret_cast<float4 *>(sacc)[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
     consumer_sync();
+    if (a.nw) {
+        // the block's input is RMSNorm(h) * ffn_norm: the sum of squares in one fixed order, the
+        // same in every CTA (each CTA routes and quantises its own copy, so all copies must agree)
+        const int per = E / (kConsumerWarps * 32);          // E % 512 == 0 when nw is passed
+        double s2 = 0.0;
+        for (int k = 0; k < per; k++) {
+            const int j = tid * per + k;
+            const double v = (double)sx[(j & 15) * PS + (j >> 4)];
+            s2 = fma(v, v, s2);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        if ((tid & 31) == 0) s_nrm[tid >> 5] = s2;
+        consumer_sync();
+        double tot = 0.0;
+        for (int i = 0; i < kConsumerWarps; i++) tot += s_nrm[i];
+        const double inv = 1.0 / sqrt(tot / E + (double)a.eps);
+        for (int k = 0; k < per; k++) {
+            const int j = tid * per + k;
+            float *px = sx + (j & 15) * PS + (j >> 4);
+            *px = __fmul_rn((float)((double)*px * inv), __ldg(a.nw + j));
+        }
+        consumer_sync();
+    }
     const uint32_t stamp = s_stamp;
     bool ok = true;
     if (warp == 0) {
@@ -931,10 +958,13 @@ int stream_scratch_sizes(const QmsCudaMoe *m, StreamScratch *sz) {
     return QMS_CUDA_OK;
 }
 
-int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *resid, cudaStream_t s) {
+int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *resid, cudaStream_t s,
+                       const float *nw, float eps) {
     DecodeArgs a;
     a.router_lm = m->router_lm;
     a.xn = xn;
+    a.nw = nw;
+    a.eps = eps;
     a.resid = resid;
     a.out = out;
     a.gu = m->gu;

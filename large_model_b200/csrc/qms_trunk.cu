@@ -685,3 +685,539 @@ int launch_attention(const AttnArgs &a, cudaStream_t s) {
 }
 
 }  // namespace qms
+
+// ---- one-token projections: persistent CTAs streaming their rows through a bulk-copy ring ---------
+#include "qms_async.cuh"
+
+namespace qms {
+
+constexpr int kG1Warps = 8;                          // consumer warps (+ one producer warp)
+constexpr int kG1Threads = (kG1Warps + 1) * 32;
+constexpr uint32_t kG1Stage = 32 * 1024;             // bytes per ring slot (whole rows)
+constexpr int kG1MaxRing = 8;
+constexpr size_t kG1SmemBudget = 160 * 1024;         // leaves room for a co-resident attention CTA
+constexpr uint32_t kG1Spin = 1u << 22;               // polls before a wait gives up (>= 0.1 s)
+enum { G1_ERR_WAIT = 64 };
+
+struct G1Layout {
+    int rps;          // rows per stage (a multiple of the rows one warp pass covers)
+    int nst;          // ring slots
+    uint32_t act;     // bytes of the activation area
+};
+
+__host__ __device__ inline int g1_lpr(int type, int ncol) {
+    const int units = type == QMS_T_Q6_K ? ncol / 128 : ncol / 32;
+    return units >= 32 ? 32 : units;
+}
+
+// Wait for `parity` of `bar` with a bound; on timeout raise *abort and the error bit.
+__device__ __forceinline__ bool g1_wait(uint64_t *bar, uint32_t parity, volatile int *abort, int *err) {
+    uint32_t n = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort) return false;
+        if (++n == kG1Spin) {
+            *abort = 1;
+            atomicOr(err, G1_ERR_WAIT);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
+}
+
+// Activations in shared memory: q[0..15] and q[16..31] of block b at sqa + 16 b and sqb + 16 b
+// (lanes reading consecutive blocks read consecutive 16-byte words), d and packed sums per block.
+template <int WT, int NU>
+__device__ __forceinline__ float g1_row_dot(const uint8_t *row, int ncol, const uint8_t *sqa, const uint8_t *sqb,
+                                            const float *sd, const int *ss, int li, int LPR) {
+    float acc = 0.0f;
+    const int nb = ncol / 32;
+    if constexpr (WT == 2) {
+        const int nsb = ncol / 256, sb = li >> 1, h = li & 1;
+        const uint8_t *body = row + (size_t)sb * 208;
+        uint32_t qlw[16], qhw[8];
+#pragma unroll
+        for (int k = 0; k < 4; k++) *reinterpret_cast<uint4 *>(&qlw[4 * k]) = *reinterpret_cast<const uint4 *>(body + h * 64 + 16 * k);
+#pragma unroll
+        for (int k = 0; k < 2; k++) *reinterpret_cast<uint4 *>(&qhw[4 * k]) = *reinterpret_cast<const uint4 *>(body + 128 + h * 32 + 16 * k);
+        const uint2 scw = *reinterpret_cast<const uint2 *>(body + 192 + h * 8);
+        const float d6 = h2f(*reinterpret_cast<const uint16_t *>(row + (size_t)nsb * 208 + 2 * sb));
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            const int b = sb * 8 + h * 4 + g;
+            const int4 xa0 = *reinterpret_cast<const int4 *>(sqa + 16 * b), xa1 = *reinterpret_cast<const int4 *>(sqb + 16 * b);
+            const int xw[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
+            int dlo = 0, dhi = 0;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint32_t q6 = ((qlw[(g & 1) * 8 + k] >> (4 * (g >> 1))) & 0x0F0F0F0Fu) |
+                                    (((qhw[k] >> (2 * g)) & 0x03030303u) << 4);
+                if (k < 4) dlo = __dp4a((int)q6, xw[k], dlo);
+                else dhi = __dp4a((int)q6, xw[k], dhi);
+            }
+            const uint32_t w = (g >> 1) ? scw.y : scw.x;
+            const int sa = (int)(int8_t)(w >> (16 * (g & 1))), sbv = (int)(int8_t)(w >> (16 * (g & 1) + 8));
+            const int s = ss[b];
+            const int isum = sa * (dlo - 32 * sum_lo(s)) + sbv * (dhi - 32 * sum_hi(s));
+            acc = __fmaf_rn((float)isum, __fmul_rn(d6, sd[b]), acc);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < NU; j++) {
+            const int b = li + LPR * j;
+            const uint4 nib = *reinterpret_cast<const uint4 *>(row + (size_t)b * 16);
+            const float dw = h2f(*reinterpret_cast<const uint16_t *>(row + (size_t)nb * 16 + 2 * b));
+            const int isum = q4_block_isum(nib, *reinterpret_cast<const int4 *>(sqa + 16 * b),
+                                           *reinterpret_cast<const int4 *>(sqb + 16 * b));
+            const float dx = sd[b];
+            const int s = ss[b], sum = sum_lo(s) + sum_hi(s);
+            if constexpr (WT == 0) {
+                acc = __fmaf_rn((float)(isum - 8 * sum), __fmul_rn(dw, dx), acc);
+            } else {
+                const float mw = h2f(*reinterpret_cast<const uint16_t *>(row + (size_t)nb * 16 + pad16((size_t)nb * 2) + 2 * b));
+                acc = __fmaf_rn((float)isum, __fmul_rn(dw, dx), acc);
+                acc = __fmaf_rn(mw, __fmul_rn(dx, (float)sum), acc);
+            }
+        }
+    }
+    return acc;
+}
+
+__device__ __forceinline__ void g1_consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kG1Warps * 32) : "memory"); }
+
+template <int WT, int NU>
+__global__ void __launch_bounds__(kG1Threads, 1) k_gemv1(const GemvArgs a, const G1Layout lay, int *err) {
+    extern __shared__ __align__(128) uint8_t g1sm[];
+    __shared__ __align__(8) uint64_t full[kG1MaxRing], empty[kG1MaxRing];
+    __shared__ double red[kG1Warps];
+    __shared__ unsigned long long s_best;
+    __shared__ int s_abort, s_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int r0 = (int)((int64_t)c * a.rows / G), r1 = (int)((int64_t)(c + 1) * a.rows / G), nr = r1 - r0;
+    const int ncol = a.ncol, nb = ncol / 32;
+    const int LPR = g1_lpr(WT == 2 ? QMS_T_Q6_K : QMS_T_Q4_0, ncol), RPW = 32 / LPR;
+    const int nstage = (nr + lay.rps - 1) / lay.rps;
+    uint8_t *ring = g1sm + lay.act;
+    uint8_t *sqa = g1sm, *sqb = g1sm + (size_t)nb * 16;
+    float *sd = reinterpret_cast<float *>(g1sm + (size_t)nb * 32);
+    int *ss = reinterpret_cast<int *>(g1sm + (size_t)nb * 36);
+    if (tid == 0) {
+        for (int i = 0; i < lay.nst; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], lay.rps / RPW);
+        }
+        fence_mbar_init();
+        s_abort = 0;
+        s_best = 0ull;
+    }
+    __syncthreads();
+    volatile int *abort = &s_abort;
+    if (warp == kG1Warps) {                                   // producer: the weights never depend on
+        if (lane == 0) {                                      // earlier kernels, so they stream at once
+            const uint64_t pol = evict_first_policy();
+            int issued = 0;
+            for (int k = 0; k < nstage; k++) {
+                const int slot = k % lay.nst;
+                if (k >= lay.nst && !g1_wait(&empty[slot], ((k / lay.nst) - 1) & 1, abort, err)) break;
+                const int rows = min(lay.rps, nr - k * lay.rps);
+                const uint32_t bytes = (uint32_t)((size_t)rows * a.stride);
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                bulk_load(ring + (size_t)slot * kG1Stage, a.w + (size_t)(r0 + k * lay.rps) * a.stride, bytes, &full[slot], pol);
+                issued = k + 1;
+            }
+            // every copy this CTA issued must land before the CTA may exit
+            for (int k = issued > lay.nst ? issued - lay.nst : 0; k < issued; k++) {
+                uint32_t n = 0;
+                while (!mbar_try_wait(&full[k % lay.nst], (k / lay.nst) & 1))
+                    if (++n == kG1Spin) {
+                        atomicOr(err, G1_ERR_WAIT);
+                        break;
+                    }
+            }
+        }
+        pdl_trigger();
+        pdl_wait();
+        return;
+    }
+    pdl_trigger();
+    pdl_wait();
+    // ---- activations: Q8 blocks of x (RMS-normed first with nw) or copied Q8 rows
+    if (a.x) {
+        const int per = (ncol + kG1Warps * 32 - 1) / (kG1Warps * 32);   // elements per thread (<= 32)
+        double inv = 1.0;
+        if (a.nw) {
+            double s2 = 0.0;
+            for (int k = 0; k < per; k++) {
+                const int i = tid * per + k;
+                if (i < ncol) {
+                    const double v = (double)__ldcg(a.x + i);
+                    s2 = fma(v, v, s2);
+                }
+            }
+            s2 = warp_sum_d(s2);
+            if (lane == 0) red[warp] = s2;
+            g1_consumer_sync();
+            double tot = 0.0;
+            for (int i = 0; i < kG1Warps; i++) tot += red[i];
+            inv = 1.0 / sqrt(tot / ncol + (double)a.eps);
+        }
+        // four threads per 32-block, eight values each
+        for (int v = tid; v < nb * 4; v += kG1Warps * 32) {
+            const int b = v >> 2, p = v & 3, i0 = 32 * b + 8 * p;
+            const float4 x0 = __ldcg(reinterpret_cast<const float4 *>(a.x + i0));
+            const float4 x1 = __ldcg(reinterpret_cast<const float4 *>(a.x + i0 + 4));
+            float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            if (a.nw) {
+                const float4 w0 = __ldg(reinterpret_cast<const float4 *>(a.nw + i0));
+                const float4 w1 = __ldg(reinterpret_cast<const float4 *>(a.nw + i0 + 4));
+                const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int m = 0; m < 8; m++) x[m] = __fmul_rn((float)((double)x[m] * inv), w[m]);
+            }
+            float amax = 0.0f;
+#pragma unroll
+            for (int m = 0; m < 8; m++) amax = fmaxf(amax, fabsf(x[m]));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            uint32_t w0 = 0, w1 = 0;
+            int sum = 0;
+#pragma unroll
+            for (int m = 0; m < 8; m++) {
+                const int q = __float2int_rn(__fmul_rn(x[m], id));
+                sum += q;
+                if (m < 4) w0 |= (uint32_t)(q & 0xff) << (8 * m);
+                else w1 |= (uint32_t)(q & 0xff) << (8 * (m - 4));
+            }
+            const int s_pair = sum + __shfl_xor_sync(0xffffffffu, sum, 1);   // p 0+1: elements 0..15
+            const int s_all = s_pair + __shfl_xor_sync(0xffffffffu, s_pair, 2);
+            uint8_t *dst = (p < 2 ? sqa : sqb) + 16 * b + 8 * (p & 1);
+            *reinterpret_cast<uint2 *>(dst) = make_uint2(w0, w1);
+            if (p == 0) {
+                sd[b] = d;
+                ss[b] = (s_pair & 0xffff) | ((s_all - s_pair) << 16);
+            }
+        }
+    } else {
+        for (int b = tid; b < nb; b += kG1Warps * 32) {
+            const int4 *src = reinterpret_cast<const int4 *>(a.xq + 32 * (size_t)b);
+            *reinterpret_cast<int4 *>(sqa + 16 * b) = __ldcg(src);
+            *reinterpret_cast<int4 *>(sqb + 16 * b) = __ldcg(src + 1);
+            sd[b] = __ldcg(a.xd + b);
+            ss[b] = __ldcg(a.xs + b);
+        }
+    }
+    g1_consumer_sync();
+    // ---- rows: warp pass g covers local rows [g*RPW, g*RPW + RPW), all inside one stage
+    const int seg = lane / LPR, li = lane % LPR;
+    const int npass = (nr + RPW - 1) / RPW, ppst = lay.rps / RPW;
+    unsigned long long best = 0ull;
+    for (int g = warp; g < npass; g += kG1Warps) {
+        const int k = g / ppst, slot = k % lay.nst;
+        if (!g1_wait(&full[slot], (k / lay.nst) & 1, abort, err)) break;
+        const int lr = g * RPW + seg;
+        const uint8_t *row = ring + (size_t)slot * kG1Stage + (size_t)(lr - k * lay.rps) * a.stride;
+        float acc = lr < nr ? g1_row_dot<WT, NU>(row, ncol, sqa, sqb, sd, ss, li, LPR) : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            if (o < LPR) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);             // this pass no longer reads the slot
+        if (li == 0 && lr < nr) {
+            const int r = r0 + lr;
+            const float v = a.resid ? __fadd_rn(a.resid[r], acc) : acc;
+            a.y[r] = v;
+            if (a.amax) {
+                const unsigned long long key = argmax_key(v, r);
+                best = key > best ? key : best;
+            }
+        }
+    }
+    if (!a.amax) return;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long key = __shfl_xor_sync(0xffffffffu, best, o);
+        best = key > best ? key : best;
+    }
+    if (lane == 0) atomicMax(&s_best, best);
+    g1_consumer_sync();
+    if (tid == 0) {
+        atomicMax(a.amax, s_best);
+        __threadfence();
+        s_last = atomicAdd(a.ticket, 1) == G - 1;
+    }
+    g1_consumer_sync();
+    if (tid == 0 && s_last) {
+        __threadfence();
+        const unsigned long long key = atomicExch(a.amax, 0ull);
+        *a.tok = (int)(0xffffffffu - (uint32_t)key);
+        if (a.pos) *a.pos += 1;
+        *a.ticket = 0;
+    }
+}
+
+template <int WT, int NU>
+static int launch_gemv1_t(const GemvArgs &a, int *err, cudaStream_t s) {
+    int nsm = 148;
+    int rc = gemv_setup(&nsm);
+    if (rc) return rc;
+    const int type = WT == 2 ? QMS_T_Q6_K : WT == 1 ? QMS_T_Q4_1 : QMS_T_Q4_0;
+    const int RPW = 32 / g1_lpr(type, a.ncol);
+    G1Layout lay;
+    lay.act = (uint32_t)(((size_t)(a.ncol / 32) * 40 + 127) & ~(size_t)127);
+    lay.rps = (int)(kG1Stage / a.stride) / RPW * RPW;
+    QMS_REQUIRE(lay.rps >= RPW, QMS_CUDA_EUNSUPPORTED, "gemv1: rows of %zu bytes", a.stride);
+    const int G = std::min(nsm, a.rows);
+    const int per_cta = (a.rows + G - 1) / G;
+    const int stages = (per_cta + lay.rps - 1) / lay.rps;
+    lay.nst = (int)std::min<size_t>(std::min(kG1MaxRing, stages), (kG1SmemBudget - lay.act) / kG1Stage);
+    if (lay.nst < 1) lay.nst = 1;
+    const size_t smem = lay.act + (size_t)lay.nst * kG1Stage;
+    auto kern = k_gemv1<WT, NU>;
+    static bool s_attr[64];
+    int dev = 0;
+    QMS_CK(cudaGetDevice(&dev));
+    if (dev >= 0 && dev < 64 && !s_attr[dev]) {
+        QMS_CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kG1SmemBudget + 16384)));
+        s_attr[dev] = true;
+    }
+    QMS_CK(launch_pdl(kern, dim3(G), dim3(kG1Threads), smem, s, a, lay, err));
+    return QMS_CUDA_OK;
+}
+
+int launch_gemv1(int type, const GemvArgs &a, int *err, cudaStream_t s) {
+    QMS_REQUIRE(a.T == 1 && a.stride % 16 == 0 && ((uintptr_t)a.w & 15) == 0, QMS_CUDA_EINVAL,
+                "gemv1: one token, 16-byte aligned rows");
+    QMS_REQUIRE(a.ncol / 32 * 40 + 128 < 64 * 1024, QMS_CUDA_EUNSUPPORTED, "gemv1: rows of %d values", a.ncol);
+    if (type == QMS_T_Q6_K) {
+        const int units = a.ncol / 128;
+        QMS_REQUIRE(a.ncol % 256 == 0 && units <= 32 && (units & (units - 1)) == 0, QMS_CUDA_EUNSUPPORTED,
+                    "gemv1: Q6_K rows of %d values", a.ncol);
+        return launch_gemv1_t<2, 1>(a, err, s);
+    }
+    const int nb = a.ncol / 32;
+    QMS_REQUIRE(a.ncol % 32 == 0 && (nb < 32 ? (nb & (nb - 1)) == 0 : nb % 32 == 0 && nb <= 256),
+                QMS_CUDA_EUNSUPPORTED, "gemv1: Q4 rows of %d values", a.ncol);
+    const int nu = nb < 32 ? 1 : nb / 32;
+    if (type == QMS_T_Q4_0) {
+        switch (nu) {
+        case 1: return launch_gemv1_t<0, 1>(a, err, s);
+        case 2: return launch_gemv1_t<0, 2>(a, err, s);
+        case 4: return launch_gemv1_t<0, 4>(a, err, s);
+        case 8: return launch_gemv1_t<0, 8>(a, err, s);
+        default: break;
+        }
+    } else if (type == QMS_T_Q4_1) {
+        switch (nu) {
+        case 1: return launch_gemv1_t<1, 1>(a, err, s);
+        case 2: return launch_gemv1_t<1, 2>(a, err, s);
+        case 4: return launch_gemv1_t<1, 4>(a, err, s);
+        case 8: return launch_gemv1_t<1, 8>(a, err, s);
+        default: break;
+        }
+    }
+    set_error("gemv1: type %d with %d blocks per row not supported", type, nb);
+    return QMS_CUDA_EUNSUPPORTED;
+}
+
+}  // namespace qms
+
+// ---- one-token attention: QK-norm + RoPE + KV append fused, K/V staged in shared memory ------------
+namespace qms {
+
+// RMSNorm over one head row (D values, D/32 per lane at lane + 32 j) and the NEOX rotation at
+// position p (src/model.c:403-422, 441-447); the warp returns the row in x.
+template <int D>
+__device__ __forceinline__ void norm_rope_row(float (&x)[D / 32], const float *nw, float eps, const float *cs,
+                                              const float *sn, int lane) {
+    constexpr int J = D / 32, JH = J / 2;
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < J; j++) ss = fma((double)x[j], (double)x[j], ss);
+    ss = warp_sum_d(ss);
+    const double inv = 1.0 / sqrt(ss / D + (double)eps);
+#pragma unroll
+    for (int j = 0; j < J; j++) x[j] = norm_elem(x[j], inv, nw, lane + 32 * j);
+#pragma unroll
+    for (int j = 0; j < JH; j++) {
+        const int i = lane + 32 * j;
+        const float c = cs[i], s = sn[i], x1 = x[j], x2 = x[j + JH];
+        x[j] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+        x[j + JH] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+    }
+}
+
+// CTA (kv head g, block s of kAttnBlock positions), one warp per q head of the group, lane =
+// position. Scores in qms_vec_dot_f32's order: sixteen 8-long FMA chains, then the hsum tree.
+template <int D>
+__global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
+    constexpr int PB = kAttnBlock, KP = D + 1;           // padded K rows: lanes read distinct banks
+    __shared__ float sk[PB * KP];
+    __shared__ __align__(16) float sv[PB * D];
+    __shared__ float sq[16 * D];
+    const int group = a.H / a.Hk, g = blockIdx.x, s = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x, nthr = blockDim.x;
+    pdl_trigger();
+    pdl_wait();
+    const int pos = *a.pos;
+    if (pos < 0 || pos >= a.ctx) {
+        if (tid == 0 && s == 0 && g == 0) atomicOr(a.err, 1);
+        return;
+    }
+    const int npos = pos + 1, S = (npos + PB - 1) / PB;
+    if (s >= S) return;
+    const int p0 = s * PB, p1 = min(npos, p0 + PB), np = p1 - p0;
+    const int KD = a.Hk * D;
+    const float *cs = a.rope_cos + (size_t)pos * (D / 2), *sn = a.rope_sin + (size_t)pos * (D / 2);
+    // cached K/V rows of positions [p0, min(p1, pos)) of head g
+    const int nc = min(p1, pos) - p0;
+    for (int i = tid; i < nc * D; i += nthr) {
+        const int p = i / D, d = i % D;
+        const size_t at = (size_t)(p0 + p) * KD + (size_t)g * D + d;
+        sk[p * KP + d] = __ldcg(a.kc + at);
+        sv[p * D + d] = __ldcg(a.vc + at);
+    }
+    // this warp's q head, normalised and rotated (every CTA of the group does it for itself)
+    {
+        const int h = g * group + warp;
+        float x[D / 32];
+#pragma unroll
+        for (int j = 0; j < D / 32; j++) x[j] = a.qkv[(size_t)h * D + lane + 32 * j];
+        norm_rope_row<D>(x, a.q_norm, a.eps, cs, sn, lane);
+#pragma unroll
+        for (int j = 0; j < D / 32; j++) sq[warp * D + lane + 32 * j] = x[j];
+    }
+    if (p1 == npos) {                                    // the new position: K / V rows, appended
+        if (warp == 0) {
+            float x[D / 32];
+#pragma unroll
+            for (int j = 0; j < D / 32; j++) x[j] = a.qkv[(size_t)a.H * D + (size_t)g * D + lane + 32 * j];
+            norm_rope_row<D>(x, a.k_norm, a.eps, cs, sn, lane);
+#pragma unroll
+            for (int j = 0; j < D / 32; j++) {
+                sk[(pos - p0) * KP + lane + 32 * j] = x[j];
+                a.kc[(size_t)pos * KD + (size_t)g * D + lane + 32 * j] = x[j];
+            }
+        }
+        if (warp == (group > 1 ? 1 : 0)) {
+            for (int j = 0; j < D / 32; j++) {
+                const float v = a.qkv[(size_t)(a.H + a.Hk) * D + (size_t)g * D + lane + 32 * j];
+                sv[(pos - p0) * D + lane + 32 * j] = v;
+                a.vc[(size_t)pos * KD + (size_t)g * D + lane + 32 * j] = v;
+            }
+        }
+    }
+    __syncthreads();
+    const int h = g * group + warp;
+    const bool valid = lane < np;
+    float dot = 0.0f;
+    if (valid) {
+        float acc[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) acc[k] = 0.0f;
+        const float *kr = sk + lane * KP, *qr = sq + warp * D;
+#pragma unroll
+        for (int i = 0; i < D / 16; i++)
+#pragma unroll
+            for (int k = 0; k < 16; k++) acc[k] = __fmaf_rn(qr[16 * i + k], kr[16 * i + k], acc[k]);
+        float t[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) t[k] = __fadd_rn(acc[k], acc[k + 8]);
+#pragma unroll
+        for (int k = 0; k < 4; k++) t[k] = __fadd_rn(t[k], t[k + 4]);
+        t[0] = __fadd_rn(t[0], t[2]);
+        t[1] = __fadd_rn(t[1], t[3]);
+        dot = __fadd_rn(t[0], t[1]);
+    }
+    const double sc = valid ? (double)dot * a.scale : -INFINITY;
+    const double m = warp_max_d(sc);
+    const double e = valid ? exp(sc - m) : 0.0;
+    const double l = warp_sum_d(e);
+    const float fe = (float)e;
+    constexpr int DPL = D / 32;
+    float o[DPL];
+#pragma unroll
+    for (int d = 0; d < DPL; d++) o[d] = 0.0f;
+    for (int q = 0; q < np; q++) {
+        const float w = __shfl_sync(0xffffffffu, fe, q);
+        const float *vp = sv + q * D + lane * DPL;
+#pragma unroll
+        for (int d = 0; d < DPL; d++) o[d] = __fmaf_rn(w, vp[d], o[d]);
+    }
+    const size_t slot = (size_t)h * a.max_splits + s;
+#pragma unroll
+    for (int d = 0; d < DPL; d++) a.part_o[slot * D + lane * DPL + d] = o[d];
+    if (lane == 0) {
+        a.part_ml[slot * 2] = m;
+        a.part_ml[slot * 2 + 1] = l;
+    }
+}
+
+// One CTA per q head: merge the S position blocks (flash-decoding), divide by the softmax sum and
+// write the head's Q8 blocks (the O projection's input, src/kernels.c:34-53).
+template <int D>
+__global__ void __launch_bounds__(D) k_attn_merge(const AttnArgs a, int8_t *xq, float *xd, int *xs) {
+    __shared__ float f[kAttnMaxCtx / kAttnBlock];
+    __shared__ double red[D / 32];
+    __shared__ double s_m;
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_trigger();
+    pdl_wait();
+    const int pos = *a.pos;
+    if (pos < 0 || pos >= a.ctx) return;
+    const int S = (pos + kAttnBlock) / kAttnBlock;
+    const size_t base = (size_t)h * a.max_splits;
+    double mx = -INFINITY;
+    for (int q = tid; q < S; q += D) mx = fmax(mx, __ldcg(a.part_ml + (base + q) * 2));
+    mx = warp_max_d(mx);
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        double v = red[0];
+        for (int i = 1; i < D / 32; i++) v = fmax(v, red[i]);
+        s_m = v;
+    }
+    __syncthreads();
+    const double M = s_m;
+    double z = 0.0;
+    for (int q = tid; q < S; q += D) {
+        const double fq = exp(__ldcg(a.part_ml + (base + q) * 2) - M);
+        f[q] = (float)fq;
+        z += __ldcg(a.part_ml + (base + q) * 2 + 1) * fq;
+    }
+    z = warp_sum_d(z);
+    __syncthreads();
+    if (lane == 0) red[warp] = z;
+    __syncthreads();
+    double Z = 0.0;
+    for (int i = 0; i < D / 32; i++) Z += red[i];
+    float acc = 0.0f;
+    for (int q = 0; q < S; q++) acc = __fmaf_rn(f[q], __ldcg(a.part_o + (base + q) * D + tid), acc);
+    const float v = (float)((double)acc / Z);
+    const Q8Lane r = quantize_lane(v);
+    const size_t e = (size_t)h * D + tid;
+    xq[e] = (int8_t)r.q;
+    if (lane == 0) {
+        xd[e / 32] = r.d;
+        xs[e / 32] = pack_sums(r);
+    }
+}
+
+int launch_attn_decode(const AttnArgs &a, int8_t *xq, float *xd, int *xs, cudaStream_t s) {
+    const int group = a.H / a.Hk;
+    QMS_REQUIRE(group <= 16 && a.T == 1 && a.max_splits <= kAttnMaxCtx / kAttnBlock && a.max_splits * kAttnBlock >= a.ctx,
+                QMS_CUDA_EUNSUPPORTED, "attn_decode: %d q heads per kv head, ctx %d", group, a.ctx);
+    const dim3 grid(a.Hk, a.max_splits);
+    if (a.D == 128) {
+        QMS_CK(launch_pdl(k_attn_decode<128>, grid, dim3(32 * group), 0, s, a));
+        QMS_CK(launch_pdl(k_attn_merge<128>, dim3(a.H), dim3(128), 0, s, a, xq, xd, xs));
+    } else {
+        QMS_CK(launch_pdl(k_attn_decode<64>, grid, dim3(32 * group), 0, s, a));
+        QMS_CK(launch_pdl(k_attn_merge<64>, dim3(a.H), dim3(64), 0, s, a, xq, xd, xs));
+    }
+    return QMS_CUDA_OK;
+}
+
+}  // namespace qms

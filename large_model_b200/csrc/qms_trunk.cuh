@@ -59,6 +59,12 @@ struct GemvArgs {
 };
 int launch_gemv(int type, const GemvArgs &a, cudaStream_t s);
 
+// One-token projection (decode): a persistent CTA per SM owns a contiguous range of rows and
+// streams it through a ring of TMA bulk copies issued before griddepcontrol.wait. Input: fp32 x
+// (RMS-normed with nw first when nw != NULL) quantised in the prologue, or Q8 rows (xq/xd/xs).
+// y[r] = (resid ? resid[r] : 0) + dot; optional fused greedy argmax as in GemvArgs.
+int launch_gemv1(int type, const GemvArgs &a, int *err, cudaStream_t s);
+
 // ---- norms, embedding, attention ----------------------------------------------------------------
 // y = RMSNorm(x) * w per row (src/model.c:403-409), optionally also as Q8 rows (xq / xd / xs as in
 // GemvArgs); w == NULL quantises x unchanged.
@@ -86,6 +92,13 @@ struct AttnArgs {
     float *out;                       // [T][H*D]
     int *err;
 };
+// One-token attention (decode): CTA (kv head, 32 positions) with QK-norm, RoPE and the K/V append
+// of the new position fused in; partials merged by k_attn_merge, which writes the Q8 rows of the
+// attention output for the O projection (xq / xd / xs as in GemvArgs).
+int launch_attn_decode(const AttnArgs &a, int8_t *xq, float *xd, int *xs, cudaStream_t s);
+constexpr int kAttnBlock = 32;        // positions per decode-attention CTA
+constexpr int kAttnMaxCtx = 16384;    // longest context the one-token attention merges
+
 // QK-norm + NEOX RoPE of every q / k head and the fp32 K/V append (src/model.c:441-462).
 int launch_qk_rope(const AttnArgs &a, cudaStream_t s);
 // Causal GQA attention with the reference's score order (src/model.c:465-492).

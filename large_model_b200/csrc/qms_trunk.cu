@@ -691,8 +691,8 @@ int launch_attention(const AttnArgs &a, cudaStream_t s) {
 
 namespace qms {
 
-constexpr int kG1Warps = 8;                          // consumer warps (+ one producer warp)
-constexpr int kG1Threads = (kG1Warps + 1) * 32;
+constexpr int kG1Warps = 8;                          // consumer warps (+ one producer warp); 16 for the head
+constexpr int kG1WarpsHead = 16;
 constexpr uint32_t kG1Stage = 32 * 1024;             // bytes per ring slot (whole rows)
 constexpr int kG1MaxRing = 8;
 constexpr size_t kG1SmemBudget = 160 * 1024;         // leaves room for a co-resident attention CTA
@@ -744,7 +744,7 @@ __device__ __forceinline__ float g1_row_dot(const uint8_t *row, int ncol, const 
         const float d6 = h2f(*reinterpret_cast<const uint16_t *>(row + (size_t)nsb * 208 + 2 * sb));
 #pragma unroll
         for (int g = 0; g < 4; g++) {
-            const int b = sb * 8 + h * 4 + g;
+            const int b = g * (nb >> 2) + sb * 2 + h;               // g1_act_pos of block 8 sb + 4 h + g
             const int4 xa0 = *reinterpret_cast<const int4 *>(sqa + 16 * b), xa1 = *reinterpret_cast<const int4 *>(sqb + 16 * b);
             const int xw[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
             int dlo = 0, dhi = 0;
@@ -783,13 +783,21 @@ __device__ __forceinline__ float g1_row_dot(const uint8_t *row, int ncol, const 
     return acc;
 }
 
-__device__ __forceinline__ void g1_consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kG1Warps * 32) : "memory"); }
+// Where activation block b sits in shared memory. A Q6_K unit (lane li) reads blocks 4 li .. 4 li + 3,
+// so for Q6_K rows block b goes to (b % 4) * nb / 4 + b / 4: for each of the four groups the lanes
+// then read consecutive 16-byte words (no bank conflicts). Q4 lanes read consecutive blocks as is.
+template <int WT>
+__device__ __forceinline__ int g1_act_pos(int b, int nb) { return WT == 2 ? (b & 3) * (nb >> 2) + (b >> 2) : b; }
 
-template <int WT, int NU>
-__global__ void __launch_bounds__(kG1Threads, 1) k_gemv1(const GemvArgs a, const G1Layout lay, int *err) {
+template <int NWC>
+__device__ __forceinline__ void g1_consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NWC * 32) : "memory"); }
+
+template <int WT, int NU, int NWC>
+__global__ void __launch_bounds__((NWC + 1) * 32, NWC > 8 ? 1 : 2) k_gemv1(const GemvArgs a, const G1Layout lay, int *err) {
+    constexpr int kG1Warps = NWC;
     extern __shared__ __align__(128) uint8_t g1sm[];
     __shared__ __align__(8) uint64_t full[kG1MaxRing], empty[kG1MaxRing];
-    __shared__ double red[kG1Warps];
+    __shared__ double red[NWC];
     __shared__ unsigned long long s_best;
     __shared__ int s_abort, s_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -844,40 +852,59 @@ __global__ void __launch_bounds__(kG1Threads, 1) k_gemv1(const GemvArgs a, const
     pdl_wait();
     // ---- activations: Q8 blocks of x (RMS-normed first with nw) or copied Q8 rows
     if (a.x) {
-        const int per = (ncol + kG1Warps * 32 - 1) / (kG1Warps * 32);   // elements per thread (<= 32)
-        double inv = 1.0;
+        // item v = (block v / 4, quarter v % 4): eight consecutive values; a thread takes items
+        // tid + 256 k, all loaded before any is used (one round trip), and the four threads of a
+        // block are consecutive lanes. The sum of squares has one fixed order in every CTA.
+        constexpr int kItems = 4;                       // nb * 4 <= 4 * 256: ncol <= 8192
+        const int nitems = nb * 4;
+        float xv[kItems][8];
+#pragma unroll
+        for (int k = 0; k < kItems; k++) {
+            const int v = tid + kG1Warps * 32 * k;
+            if (v < nitems) {
+                const float4 x0 = __ldcg(reinterpret_cast<const float4 *>(a.x + 8 * v));
+                const float4 x1 = __ldcg(reinterpret_cast<const float4 *>(a.x + 8 * v + 4));
+                xv[k][0] = x0.x; xv[k][1] = x0.y; xv[k][2] = x0.z; xv[k][3] = x0.w;
+                xv[k][4] = x1.x; xv[k][5] = x1.y; xv[k][6] = x1.z; xv[k][7] = x1.w;
+            }
+        }
         if (a.nw) {
-            double s2 = 0.0;
-            for (int k = 0; k < per; k++) {
-                const int i = tid * per + k;
-                if (i < ncol) {
-                    const double v = (double)__ldcg(a.x + i);
-                    s2 = fma(v, v, s2);
+            float wv[kItems][8];
+#pragma unroll
+            for (int k = 0; k < kItems; k++) {
+                const int v = tid + kG1Warps * 32 * k;
+                if (v < nitems) {
+                    const float4 w0 = __ldg(reinterpret_cast<const float4 *>(a.nw + 8 * v));
+                    const float4 w1 = __ldg(reinterpret_cast<const float4 *>(a.nw + 8 * v + 4));
+                    wv[k][0] = w0.x; wv[k][1] = w0.y; wv[k][2] = w0.z; wv[k][3] = w0.w;
+                    wv[k][4] = w1.x; wv[k][5] = w1.y; wv[k][6] = w1.z; wv[k][7] = w1.w;
                 }
             }
+            double s2 = 0.0;
+#pragma unroll
+            for (int k = 0; k < kItems; k++)
+                if (tid + kG1Warps * 32 * k < nitems)
+#pragma unroll
+                    for (int m = 0; m < 8; m++) s2 = fma((double)xv[k][m], (double)xv[k][m], s2);
             s2 = warp_sum_d(s2);
             if (lane == 0) red[warp] = s2;
-            g1_consumer_sync();
+            g1_consumer_sync<NWC>();
             double tot = 0.0;
             for (int i = 0; i < kG1Warps; i++) tot += red[i];
-            inv = 1.0 / sqrt(tot / ncol + (double)a.eps);
-        }
-        // four threads per 32-block, eight values each
-        for (int v = tid; v < nb * 4; v += kG1Warps * 32) {
-            const int b = v >> 2, p = v & 3, i0 = 32 * b + 8 * p;
-            const float4 x0 = __ldcg(reinterpret_cast<const float4 *>(a.x + i0));
-            const float4 x1 = __ldcg(reinterpret_cast<const float4 *>(a.x + i0 + 4));
-            float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-            if (a.nw) {
-                const float4 w0 = __ldg(reinterpret_cast<const float4 *>(a.nw + i0));
-                const float4 w1 = __ldg(reinterpret_cast<const float4 *>(a.nw + i0 + 4));
-                const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            const double inv = 1.0 / sqrt(tot / ncol + (double)a.eps);
 #pragma unroll
-                for (int m = 0; m < 8; m++) x[m] = __fmul_rn((float)((double)x[m] * inv), w[m]);
-            }
+            for (int k = 0; k < kItems; k++)
+#pragma unroll
+                for (int m = 0; m < 8; m++) xv[k][m] = __fmul_rn((float)((double)xv[k][m] * inv), wv[k][m]);
+        }
+#pragma unroll
+        for (int k = 0; k < kItems; k++) {
+            const int v = tid + kG1Warps * 32 * k;
+            if (k * kG1Warps * 32 >= nitems) break;           // uniform: nitems is a multiple of 32
+            const int b = v >> 2, p = v & 3;
             float amax = 0.0f;
 #pragma unroll
-            for (int m = 0; m < 8; m++) amax = fmaxf(amax, fabsf(x[m]));
+            for (int m = 0; m < 8; m++) amax = fmaxf(amax, fabsf(xv[k][m]));
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
             const float d = __fdiv_rn(amax, 127.0f);
@@ -886,45 +913,46 @@ __global__ void __launch_bounds__(kG1Threads, 1) k_gemv1(const GemvArgs a, const
             int sum = 0;
 #pragma unroll
             for (int m = 0; m < 8; m++) {
-                const int q = __float2int_rn(__fmul_rn(x[m], id));
+                const int q = __float2int_rn(__fmul_rn(xv[k][m], id));
                 sum += q;
                 if (m < 4) w0 |= (uint32_t)(q & 0xff) << (8 * m);
                 else w1 |= (uint32_t)(q & 0xff) << (8 * (m - 4));
             }
-            const int s_pair = sum + __shfl_xor_sync(0xffffffffu, sum, 1);   // p 0+1: elements 0..15
+            const int s_pair = sum + __shfl_xor_sync(0xffffffffu, sum, 1);   // quarters 0+1: elements 0..15
             const int s_all = s_pair + __shfl_xor_sync(0xffffffffu, s_pair, 2);
-            uint8_t *dst = (p < 2 ? sqa : sqb) + 16 * b + 8 * (p & 1);
-            *reinterpret_cast<uint2 *>(dst) = make_uint2(w0, w1);
-            if (p == 0) {
-                sd[b] = d;
-                ss[b] = (s_pair & 0xffff) | ((s_all - s_pair) << 16);
+            if (v < nitems) {
+                const int bp = g1_act_pos<WT>(b, nb);
+                uint8_t *dst = (p < 2 ? sqa : sqb) + 16 * bp + 8 * (p & 1);
+                *reinterpret_cast<uint2 *>(dst) = make_uint2(w0, w1);
+                if (p == 0) {
+                    sd[bp] = d;
+                    ss[bp] = (s_pair & 0xffff) | ((s_all - s_pair) << 16);
+                }
             }
         }
     } else {
         for (int b = tid; b < nb; b += kG1Warps * 32) {
             const int4 *src = reinterpret_cast<const int4 *>(a.xq + 32 * (size_t)b);
-            *reinterpret_cast<int4 *>(sqa + 16 * b) = __ldcg(src);
-            *reinterpret_cast<int4 *>(sqb + 16 * b) = __ldcg(src + 1);
-            sd[b] = __ldcg(a.xd + b);
-            ss[b] = __ldcg(a.xs + b);
+            const int bp = g1_act_pos<WT>(b, nb);
+            *reinterpret_cast<int4 *>(sqa + 16 * bp) = __ldcg(src);
+            *reinterpret_cast<int4 *>(sqb + 16 * bp) = __ldcg(src + 1);
+            sd[bp] = __ldcg(a.xd + b);
+            ss[bp] = __ldcg(a.xs + b);
         }
     }
-    g1_consumer_sync();
-    // ---- rows: warp pass g covers local rows [g*RPW, g*RPW + RPW), all inside one stage
+    g1_consumer_sync<NWC>();
+    // ---- rows: warp pass g covers local rows [g*RPW, g*RPW + RPW), all inside one stage; a warp
+    // takes passes g and g + NWC together so two rows' shared-memory loads are in flight at once
     const int seg = lane / LPR, li = lane % LPR;
     const int npass = (nr + RPW - 1) / RPW, ppst = lay.rps / RPW;
     unsigned long long best = 0ull;
-    for (int g = warp; g < npass; g += kG1Warps) {
-        const int k = g / ppst, slot = k % lay.nst;
-        if (!g1_wait(&full[slot], (k / lay.nst) & 1, abort, err)) break;
-        const int lr = g * RPW + seg;
-        const uint8_t *row = ring + (size_t)slot * kG1Stage + (size_t)(lr - k * lay.rps) * a.stride;
-        float acc = lr < nr ? g1_row_dot<WT, NU>(row, ncol, sqa, sqb, sd, ss, li, LPR) : 0.0f;
+    auto finish = [&](int g, int slot, float acc) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1)
             if (o < LPR) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);             // this pass no longer reads the slot
+        const int lr = g * RPW + seg;
         if (li == 0 && lr < nr) {
             const int r = r0 + lr;
             const float v = a.resid ? __fadd_rn(a.resid[r], acc) : acc;
@@ -934,6 +962,20 @@ __global__ void __launch_bounds__(kG1Threads, 1) k_gemv1(const GemvArgs a, const
                 best = key > best ? key : best;
             }
         }
+    };
+    for (int g = warp; g < npass; g += 2 * NWC) {
+        const int g2 = g + NWC;
+        const bool two = g2 < npass;
+        const int k1 = g / ppst, s1 = k1 % lay.nst, k2 = g2 / ppst, s2 = k2 % lay.nst;
+        if (!g1_wait(&full[s1], (k1 / lay.nst) & 1, abort, err)) break;
+        if (two && !g1_wait(&full[s2], (k2 / lay.nst) & 1, abort, err)) break;
+        const int lr1 = g * RPW + seg, lr2 = g2 * RPW + seg;
+        const uint8_t *row1 = ring + (size_t)s1 * kG1Stage + (size_t)(lr1 - k1 * lay.rps) * a.stride;
+        const uint8_t *row2 = ring + (size_t)s2 * kG1Stage + (size_t)(lr2 - k2 * lay.rps) * a.stride;
+        const float acc1 = lr1 < nr ? g1_row_dot<WT, NU>(row1, ncol, sqa, sqb, sd, ss, li, LPR) : 0.0f;
+        const float acc2 = two && lr2 < nr ? g1_row_dot<WT, NU>(row2, ncol, sqa, sqb, sd, ss, li, LPR) : 0.0f;
+        finish(g, s1, acc1);
+        if (two) finish(g2, s2, acc2);
     }
     if (!a.amax) return;
 #pragma unroll
@@ -942,13 +984,13 @@ __global__ void __launch_bounds__(kG1Threads, 1) k_gemv1(const GemvArgs a, const
         best = key > best ? key : best;
     }
     if (lane == 0) atomicMax(&s_best, best);
-    g1_consumer_sync();
+    g1_consumer_sync<NWC>();
     if (tid == 0) {
         atomicMax(a.amax, s_best);
         __threadfence();
         s_last = atomicAdd(a.ticket, 1) == G - 1;
     }
-    g1_consumer_sync();
+    g1_consumer_sync<NWC>();
     if (tid == 0 && s_last) {
         __threadfence();
         const unsigned long long key = atomicExch(a.amax, 0ull);
@@ -958,7 +1000,7 @@ __global__ void __launch_bounds__(kG1Threads, 1) k_gemv1(const GemvArgs a, const
     }
 }
 
-template <int WT, int NU>
+template <int WT, int NU, int NWC = (WT == 2 ? kG1WarpsHead : kG1Warps)>
 static int launch_gemv1_t(const GemvArgs &a, int *err, cudaStream_t s) {
     int nsm = 148;
     int rc = gemv_setup(&nsm);
@@ -975,7 +1017,7 @@ static int launch_gemv1_t(const GemvArgs &a, int *err, cudaStream_t s) {
     lay.nst = (int)std::min<size_t>(std::min(kG1MaxRing, stages), (kG1SmemBudget - lay.act) / kG1Stage);
     if (lay.nst < 1) lay.nst = 1;
     const size_t smem = lay.act + (size_t)lay.nst * kG1Stage;
-    auto kern = k_gemv1<WT, NU>;
+    auto kern = k_gemv1<WT, NU, NWC>;
     static bool s_attr[64];
     int dev = 0;
     QMS_CK(cudaGetDevice(&dev));
@@ -983,7 +1025,7 @@ static int launch_gemv1_t(const GemvArgs &a, int *err, cudaStream_t s) {
         QMS_CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kG1SmemBudget + 16384)));
         s_attr[dev] = true;
     }
-    QMS_CK(launch_pdl(kern, dim3(G), dim3(kG1Threads), smem, s, a, lay, err));
+    QMS_CK(launch_pdl(kern, dim3(G), dim3((NWC + 1) * 32), smem, s, a, lay, err));
     return QMS_CUDA_OK;
 }
 
@@ -1052,7 +1094,7 @@ __device__ __forceinline__ void norm_rope_row(float (&x)[D / 32], const float *n
 // CTA (kv head g, block s of kAttnBlock positions), one warp per q head of the group, lane =
 // position. Scores in qms_vec_dot_f32's order: sixteen 8-long FMA chains, then the hsum tree.
 template <int D>
-__global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
+__global__ void __launch_bounds__(512, 2) k_attn_decode(const AttnArgs a) {
     constexpr int PB = kAttnBlock, KP = D + 1;           // padded K rows: lanes read distinct banks
     __shared__ float sk[PB * KP];
     __shared__ __align__(16) float sv[PB * D];
@@ -1073,11 +1115,33 @@ __global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
     const float *cs = a.rope_cos + (size_t)pos * (D / 2), *sn = a.rope_sin + (size_t)pos * (D / 2);
     // cached K/V rows of positions [p0, min(p1, pos)) of head g
     const int nc = min(p1, pos) - p0;
-    for (int i = tid; i < nc * D; i += nthr) {
-        const int p = i / D, d = i % D;
-        const size_t at = (size_t)(p0 + p) * KD + (size_t)g * D + d;
-        sk[p * KP + d] = __ldcg(a.kc + at);
-        sv[p * D + d] = __ldcg(a.vc + at);
+    {
+        // every float4 of the block's cached rows, loaded before any is stored (one round trip)
+        constexpr int kMaxIt = 4;                        // one round for groups of >= 8 q heads
+        const int n4 = nc * (D / 4);
+        float4 kv[kMaxIt], vv[kMaxIt];
+        for (int i0 = 0; i0 < n4; i0 += kMaxIt * nthr) {
+#pragma unroll
+        for (int it = 0; it < kMaxIt; it++) {
+            const int i = i0 + tid + it * nthr;
+            if (i < n4) {
+                const int p = i / (D / 4), d4 = i % (D / 4);
+                const size_t at = (size_t)(p0 + p) * KD + (size_t)g * D + 4 * d4;
+                kv[it] = __ldcg(reinterpret_cast<const float4 *>(a.kc + at));
+                vv[it] = __ldcg(reinterpret_cast<const float4 *>(a.vc + at));
+            }
+        }
+#pragma unroll
+        for (int it = 0; it < kMaxIt; it++) {
+            const int i = i0 + tid + it * nthr;
+            if (i < n4) {
+                const int p = i / (D / 4), d = 4 * (i % (D / 4));
+                float *kr = sk + p * KP + d;
+                kr[0] = kv[it].x; kr[1] = kv[it].y; kr[2] = kv[it].z; kr[3] = kv[it].w;
+                *reinterpret_cast<float4 *>(sv + p * D + d) = vv[it];
+            }
+        }
+        }
     }
     // this warp's q head, normalised and rotated (every CTA of the group does it for itself)
     {
@@ -1158,45 +1222,54 @@ __global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
 // One CTA per q head: merge the S position blocks (flash-decoding), divide by the softmax sum and
 // write the head's Q8 blocks (the O projection's input, src/kernels.c:34-53).
 template <int D>
-__global__ void __launch_bounds__(D) k_attn_merge(const AttnArgs a, int8_t *xq, float *xd, int *xs) {
+__global__ void __launch_bounds__(4 * D) k_attn_merge(const AttnArgs a, int8_t *xq, float *xd, int *xs) {
+    constexpr int NT = 4 * D, NW = NT / 32;
     __shared__ float f[kAttnMaxCtx / kAttnBlock];
-    __shared__ double red[D / 32];
-    __shared__ double s_m;
+    __shared__ double red[NW];
+    __shared__ float part[4][D];
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_trigger();
     pdl_wait();
     const int pos = *a.pos;
     if (pos < 0 || pos >= a.ctx) return;
-    const int S = (pos + kAttnBlock) / kAttnBlock;
+    const int S = (pos + kAttnBlock) / kAttnBlock;      // <= NT (the launch checks ctx)
     const size_t base = (size_t)h * a.max_splits;
-    double mx = -INFINITY;
-    for (int q = tid; q < S; q += D) mx = fmax(mx, __ldcg(a.part_ml + (base + q) * 2));
-    mx = warp_max_d(mx);
+    const bool own = tid < S;
+    const double mq = own ? __ldcg(a.part_ml + (base + tid) * 2) : -INFINITY;
+    const double lq = own ? __ldcg(a.part_ml + (base + tid) * 2 + 1) : 0.0;
+    double mx = warp_max_d(mq);
     if (lane == 0) red[warp] = mx;
     __syncthreads();
-    if (tid == 0) {
-        double v = red[0];
-        for (int i = 1; i < D / 32; i++) v = fmax(v, red[i]);
-        s_m = v;
-    }
-    __syncthreads();
-    const double M = s_m;
-    double z = 0.0;
-    for (int q = tid; q < S; q += D) {
-        const double fq = exp(__ldcg(a.part_ml + (base + q) * 2) - M);
-        f[q] = (float)fq;
-        z += __ldcg(a.part_ml + (base + q) * 2 + 1) * fq;
-    }
-    z = warp_sum_d(z);
+    double M = red[0];
+    for (int i = 1; i < NW; i++) M = fmax(M, red[i]);
+    const double fq = own ? exp(mq - M) : 0.0;
+    if (own) f[tid] = (float)fq;
+    double z = warp_sum_d(lq * fq);
     __syncthreads();
     if (lane == 0) red[warp] = z;
     __syncthreads();
     double Z = 0.0;
-    for (int i = 0; i < D / 32; i++) Z += red[i];
+    for (int i = 0; i < NW; i++) Z += red[i];
+    // quarter pt of the splits for dimension d, loads issued eight at a time
+    const int pt = tid / D, d = tid % D;
     float acc = 0.0f;
-    for (int q = 0; q < S; q++) acc = __fmaf_rn(f[q], __ldcg(a.part_o + (base + q) * D + tid), acc);
-    const float v = (float)((double)acc / Z);
-    const Q8Lane r = quantize_lane(v);
+    for (int q0 = pt; q0 < S; q0 += 32) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int q = q0 + 4 * u;
+            v[u] = q < S ? __ldcg(a.part_o + (base + q) * D + d) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+            if (q0 + 4 * u < S) acc = __fmaf_rn(f[q0 + 4 * u], v[u], acc);
+    }
+    part[pt][d] = acc;
+    __syncthreads();
+    if (tid >= D) return;
+    const float o = __fadd_rn(__fadd_rn(part[0][tid], part[1][tid]), __fadd_rn(part[2][tid], part[3][tid]));
+    const float val = (float)((double)o / Z);
+    const Q8Lane r = quantize_lane(val);
     const size_t e = (size_t)h * D + tid;
     xq[e] = (int8_t)r.q;
     if (lane == 0) {
@@ -1207,15 +1280,16 @@ __global__ void __launch_bounds__(D) k_attn_merge(const AttnArgs a, int8_t *xq, 
 
 int launch_attn_decode(const AttnArgs &a, int8_t *xq, float *xd, int *xs, cudaStream_t s) {
     const int group = a.H / a.Hk;
-    QMS_REQUIRE(group <= 16 && a.T == 1 && a.max_splits <= kAttnMaxCtx / kAttnBlock && a.max_splits * kAttnBlock >= a.ctx,
+    QMS_REQUIRE(group <= 16 && a.T == 1 && a.max_splits <= kAttnMaxCtx / kAttnBlock && a.max_splits * kAttnBlock >= a.ctx &&
+                    a.max_splits <= 4 * a.D,
                 QMS_CUDA_EUNSUPPORTED, "attn_decode: %d q heads per kv head, ctx %d", group, a.ctx);
     const dim3 grid(a.Hk, a.max_splits);
     if (a.D == 128) {
         QMS_CK(launch_pdl(k_attn_decode<128>, grid, dim3(32 * group), 0, s, a));
-        QMS_CK(launch_pdl(k_attn_merge<128>, dim3(a.H), dim3(128), 0, s, a, xq, xd, xs));
+        QMS_CK(launch_pdl(k_attn_merge<128>, dim3(a.H), dim3(512), 0, s, a, xq, xd, xs));
     } else {
         QMS_CK(launch_pdl(k_attn_decode<64>, grid, dim3(32 * group), 0, s, a));
-        QMS_CK(launch_pdl(k_attn_merge<64>, dim3(a.H), dim3(64), 0, s, a, xq, xd, xs));
+        QMS_CK(launch_pdl(k_attn_merge<64>, dim3(a.H), dim3(256), 0, s, a, xq, xd, xs));
     }
     return QMS_CUDA_OK;
 }

@@ -263,8 +263,11 @@ int qms_cuda_model_profile(QmsCudaModel *m, int on, double *ms);
  * Its scratch lives in one fixed device array inside the library (384.25 KiB on every GPU that
  * loads it, kept until exit): T <= 64, n_embd <= 4096 (multiple of 256), n_expert <= 256 and
  * <= n_embd / 2, n_used <= min(n_expert, 64); larger sizes return QMS_CUDA_EINVAL with a message.
- * The first call on each device looks up that array's device address, so make it before any
- * stream capture. All calls share the one array: calls that overlap on the GPU (other streams,
+ * qms_cuda_init(device) loads the library's device code (and so the array) and looks up the
+ * array's address for that device, so a caller that reserves the rest of HBM afterwards still has
+ * it; without qms_cuda_init, the first call on each device does that (make it before any stream
+ * capture). Every call looks the address up in the current context (a host-side query), so a
+ * device reset or a new context never leaves a stale address. All calls share the one array: calls that overlap on the GPU (other streams,
  * other host threads) race and must be serialised by the caller. */
 int qms_cuda_moe_route_noalloc(const float *router, int n_expert, int n_embd, int n_used,
                                const float *xn, int T, int *sel, float *wts, float *logits,

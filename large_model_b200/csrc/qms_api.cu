@@ -7,6 +7,8 @@
 
 namespace qms {
 
+int route_scratch_ptr(int dev, unsigned char **out);   // qms_moe.cu
+
 static thread_local char g_err[512];
 
 void set_error(const char *fmt, ...) {
@@ -127,7 +129,10 @@ int qms_cuda_init(int device) {
     QMS_CK(cudaGetDeviceProperties(&p, device));
     QMS_REQUIRE(p.major == 10 && p.minor == 0, QMS_CUDA_ENODEV,
                 "device %d is sm_%d%d; libqms_cuda is built for sm_100a only", device, p.major, p.minor);
-    return QMS_CUDA_OK;
+    // load the module holding the fixed routing scratch now (lazy module loading would otherwise
+    // allocate it at the first qms_cuda_moe_route_noalloc call) and cache its address
+    unsigned char *scratch = nullptr;
+    return route_scratch_ptr(device, &scratch);
 }
 
 int qms_cuda_stream_sync(void *stream) {

@@ -939,20 +939,19 @@ constexpr size_t kNoAllocScratchBytes = kNaXqQ + kNaXqD + kNaXqS + kNaLogits + k
 
 static __device__ __align__(256) unsigned char g_route_scratch[kNoAllocScratchBytes];
 
-// Device address of g_route_scratch per device ordinal, looked up once with that device current.
+// Device address of g_route_scratch in the current context, looked up on every call: the lookup
+// is a host-side query once the module is loaded (no allocation, no device work), and a cached
+// address would go stale after a device reset or a new primary context. qms_cuda_init makes the
+// first lookup, which loads the module and so places the array.
 constexpr int kNoAllocMaxDevices = 64;
-static unsigned char *g_route_scratch_ptr[kNoAllocMaxDevices];
 
-static int route_scratch_ptr(int dev, unsigned char **out) {
+int route_scratch_ptr(int dev, unsigned char **out) {
     QMS_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, QMS_CUDA_EINVAL, "moe_route_noalloc: device %d unsupported", dev);
-    unsigned char *p = __atomic_load_n(&g_route_scratch_ptr[dev], __ATOMIC_ACQUIRE);
-    if (!p) {
-        const cudaError_t e = cudaGetSymbolAddress((void **)&p, g_route_scratch);
-        if (e != cudaSuccess || !p) {
-            set_error("moe_route_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev, cudaGetErrorString(e));
-            return QMS_CUDA_ECUDA;
-        }
-        __atomic_store_n(&g_route_scratch_ptr[dev], p, __ATOMIC_RELEASE);
+    unsigned char *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress((void **)&p, g_route_scratch);
+    if (e != cudaSuccess || !p) {
+        set_error("moe_route_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev, cudaGetErrorString(e));
+        return QMS_CUDA_ECUDA;
     }
     *out = p;
     return QMS_CUDA_OK;

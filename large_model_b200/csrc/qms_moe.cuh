@@ -223,6 +223,12 @@ static cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t 
     return cudaLaunchKernelEx(&cfg, kern, ((P)args)...);
 }
 
+// A grid whose CTAs wait for one another is safe only if all of it is resident at once: `grid`
+// CTAs against `per_sm` resident CTAs per SM on `nsm` SMs.
+inline bool persistent_grid_fits(int per_sm, int nsm, int grid) {
+    return per_sm >= 1 && nsm >= 1 && (long long)per_sm * nsm >= grid;
+}
+
 // batch-1 decode kernels (qms_moe_stream.cu)
 int stream_prepare(QmsCudaMoe *m);     // shape check + kernel attributes; sets m->stream_ok
 // Read-only regions (16-byte aligned) the batch-1 kernel pulls into L2 at its start, before its

@@ -957,6 +957,14 @@ int stream_prepare(QmsCudaMoe *m) {
     const DecodeKernel dk = dec_kernel(m);
     QMS_CK(cudaFuncSetAttribute(dk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dec_smem(m)));
     QMS_CK(cudaFuncSetAttribute(dk, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    // CTAs of this kernel wait for one another, so the whole grid (one CTA per SM) must be
+    // resident at once: if an SM cannot hold a CTA, batch-1 calls take the per-slot kernels
+    // instead (they never wait across CTAs). QMS_PERSISTENT=0 forces that choice.
+    int per_sm = 0;
+    QMS_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dk, kStreamThreads, dec_smem(m)));
+    if (!persistent_grid_fits(per_sm, m->nsm, m->nsm)) return QMS_CUDA_OK;
+    if (const char *env = getenv("QMS_PERSISTENT"))
+        if (atoi(env) == 0) return QMS_CUDA_OK;
     m->stream_ok = 1;
     return QMS_CUDA_OK;
 }

@@ -84,19 +84,26 @@ def make_hidden(n_embd: int, T: int, seed: int = 1) -> np.ndarray:
     return rng.standard_normal((T, n_embd), dtype=np.float32)
 
 
-def zipf_router(layer: MoeLayer, s: float = 1.1, seed: int = 7, scale: float = 2.0) -> MoeLayer:
-    """Bias the router rows so expert popularity follows Zipf(s) (config 5): adding a mean
-    direction with per-expert strength log(1/rank^s) makes popular experts win more often."""
+def zipf_layer_and_hidden(layer: MoeLayer, T: int, s: float = 1.1, seed: int = 7, mu: float = 4.0):
+    """Config 5's skewed routing: expert popularity follows Zipf(s) over the experts. The router is
+    bias-free (a plain matmul, src/model.c:1043), so the popularity comes from a component shared by
+    every token: hidden x_t = z_t + mu * u with z_t ~ N(0, 1) and u a random unit vector, and router
+    rows w_e + (b_e / mu) u with b_e = sigma * s * log(1 / rank_e) (sigma = the logits' own spread,
+    0.02 * sqrt(n_embd)), so logit_e = w_e.z_t + b_e + small terms: the noise of the top-k plays the
+    Gumbel noise of Plackett-Luce sampling and expert e is picked with probability ~ rank_e^-s.
+    Returns (layer with the biased router, hidden [T][n_embd])."""
     rng = np.random.default_rng(seed)
     X, E = layer.router.shape
     rank = rng.permutation(X) + 1
-    bias = (-s * np.log(rank)).astype(np.float32)
-    direction = rng.standard_normal(E, dtype=np.float32)
-    direction /= np.linalg.norm(direction)
-    router = layer.router + (scale * bias[:, None] * direction[None, :] / 8.0).astype(np.float32)
-    return MoeLayer(layer.n_embd, layer.n_expert, layer.n_used, layer.n_ff,
-                    np.ascontiguousarray(router, np.float32), layer.gate, layer.up, layer.down,
-                    layer.gate_type, layer.up_type, layer.down_type)
+    sigma = 0.02 * np.sqrt(E)
+    b = (sigma * s * -np.log(rank)).astype(np.float64)
+    u = rng.standard_normal(E)
+    u /= np.linalg.norm(u)
+    router = (layer.router.astype(np.float64) + (b / mu)[:, None] * u[None, :]).astype(np.float32)
+    z = rng.standard_normal((T, E), dtype=np.float32)
+    x = (z + np.float32(mu) * u.astype(np.float32)[None, :]).astype(np.float32)
+    return (MoeLayer(layer.n_embd, layer.n_expert, layer.n_used, layer.n_ff, np.ascontiguousarray(router),
+                     layer.gate, layer.up, layer.down, layer.gate_type, layer.up_type, layer.down_type), x)
 
 
 # ---- whole models (configs 1, 3 and 4) ------------------------------------------------------------

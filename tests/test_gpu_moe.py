@@ -281,3 +281,43 @@ def test_moe_device_source_matches_host_source(cuda):
     assert torch.equal(md.forward(xn), mh.forward(xn))
     md.close()
     mh.close()
+
+
+@pytest.mark.parametrize("skew,T", [(None, 4096), (1.1, 4096), (4.0, 1024)])
+def test_moe_prefill_sizes_and_skewed_routing(cuda, oracle, skew, T):
+    """The grouped tensor-core path at config 5's call size (T = 4096 tokens, 32768 slots) and under
+    skewed routing: Zipf(1.1) expert popularity (config 5: thousands of slots and dozens of 64-slot
+    tiles on the top experts) and a sharper Zipf(4) where a few experts take almost every slot and
+    most get fewer than 8. Same bars as the other block tests."""
+    layer = synth.make_moe_layer("235b", seed=61)
+    if skew is None:
+        xn = synth.make_hidden(layer.n_embd, T, seed=62)
+    else:
+        layer, xn = synth.zipf_layer_and_hidden(layer, T, s=skew, seed=63)
+    m, out, sel, w, logits = _run(cuda, layer, xn)
+    counts = np.bincount(sel.reshape(-1), minlength=layer.n_expert)
+    if skew is not None:
+        assert counts.max() >= 512, counts.max()               # the skew this case exists for
+    o_out, o_sel, o_w, o_logits = oracle.moe(layer, xn)
+    assert np.array_equal(logits.view(np.uint32), o_logits.view(np.uint32)), "router logits differ"
+    assert np.array_equal(sel, o_sel), "selected experts differ"
+    assert _ulps(w, o_w) <= ULP_TOL
+    err = rel_l2(out, o_out)
+    assert err < OUT_TOL, f"rel L2 {err:.3e}"
+    # per token, not only over the whole block: the worst token is within the bar as well
+    tok = np.linalg.norm(out - o_out, axis=1) / np.maximum(np.linalg.norm(o_out, axis=1), 1e-30)
+    assert tok.max() < 10 * OUT_TOL, f"worst token rel L2 {tok.max():.2e} (block {err:.2e})"
+    m.close()
+
+
+@pytest.mark.parametrize("shape", ["tiny", "235b"])
+def test_batch1_without_the_persistent_kernel_matches_oracle(cuda, oracle, shape, monkeypatch):
+    """The batch-1 kernel needs its whole grid resident (its CTAs wait for one another); where an
+    SM cannot hold one of its CTAs the layer runs the per-slot kernels instead. QMS_PERSISTENT=0
+    forces that choice at creation: same results."""
+    monkeypatch.setenv("QMS_PERSISTENT", "0")
+    layer = synth.make_moe_layer(shape, seed=81)
+    xn = synth.make_hidden(layer.n_embd, 1, seed=82)
+    m, out, sel, w, logits = _run(cuda, layer, xn)
+    _check(oracle, layer, xn, out, sel, w, logits, f"{shape} fallback")
+    m.close()

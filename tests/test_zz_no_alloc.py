@@ -66,6 +66,48 @@ def test_route_noalloc_matches_forward_on_consecutive_calls(cuda):
     m.close()
 
 
+def _route_call(route, router, X, E, K, xn, T, stream):
+    import torch
+    sel = torch.full((T, K), -1, dtype=torch.int32, device="cuda")
+    wts = torch.full((T, K), -1.0, dtype=torch.float32, device="cuda")
+    logits = torch.empty((T, X), dtype=torch.float32, device="cuda")
+    return sel, wts, logits
+
+
+def test_route_noalloc_matches_oracle_and_allocates_nothing(cuda, oracle):
+    """Against the CPU restatement of the reference's routing (src/model.c:1043-1064): bit-identical
+    logits and ids, weights within 2 ulps; two calls in a row (T = 5 and an xn that is not 16-byte
+    aligned with T = 20, the tiled-router path); device free memory is the same before and after."""
+    import torch
+    L = cuda.lib()
+    route = _bind(L)
+    layer = synth.make_moe_layer("235b", seed=91)
+    X, E, K = layer.n_expert, layer.n_embd, layer.n_used
+    router = torch.from_numpy(layer.router).cuda()
+    stream = torch.cuda.current_stream()
+    cases = []
+    for call, (T, offset) in enumerate(((5, 0), (20, 1))):
+        x = synth.make_hidden(E, T, seed=700 + call)
+        flat = torch.empty(T * E + 4, dtype=torch.float32, device="cuda")
+        xn = flat[offset:offset + T * E].view(T, E)          # offset 1 float: 4-byte aligned only
+        xn.copy_(torch.from_numpy(x))
+        cases.append((T, x, xn) + _route_call(route, router, X, E, K, xn, T, stream))
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for T, x, xn, sel, wts, logits in cases:
+        rc = route(router.data_ptr(), X, E, K, xn.data_ptr(), T, sel.data_ptr(), wts.data_ptr(), logits.data_ptr(),
+                   C.c_void_p(stream.cuda_stream))
+        assert rc == 0, L.qms_cuda_last_error().decode()
+    torch.cuda.synchronize()
+    free1 = torch.cuda.mem_get_info()[0]
+    assert free1 == free0, f"device free memory changed by {free0 - free1} bytes"
+    for T, x, xn, sel, wts, logits in cases:
+        o_logits, o_sel, o_w = oracle.route(layer.router, K, x)
+        assert np.array_equal(logits.cpu().numpy().view(np.uint32), o_logits.view(np.uint32)), f"T={T}: logits"
+        assert np.array_equal(sel.cpu().numpy(), o_sel), f"T={T}: selected experts"
+        assert _ulps(wts.cpu().numpy(), o_w) <= ULP_TOL, f"T={T}: weights"
+
+
 def test_route_noalloc_rejects_sizes_beyond_its_scratch(cuda):
     import torch
     L = cuda.lib()

@@ -154,8 +154,9 @@ def cpu_reference_rate(seconds: float = 8.0, max_calls: int = 2000, layers: int 
                       f"({dt:.1f} s, reference build {ref.variant}, {threads} OpenMP threads)"}, n, dt
 
 
-def cpu_reference_batched(T: int, seconds: float = 10.0, layers: int = 2):
-    """The reference's moe() on T-token calls (moe() is sequence-agnostic), all host threads."""
+def cpu_reference_batched(T: int, seconds: float = 10.0, layers: int = 2, zipf: float = 0.0):
+    """The reference's moe() on T-token calls (moe() is sequence-agnostic), all host threads; with
+    zipf > 0 the layers and tokens carry config 5's Zipf(zipf) skew."""
     from oracle import Reference, host_threads
     from large_model_b200 import synth
     ref = Reference()
@@ -163,6 +164,9 @@ def cpu_reference_batched(T: int, seconds: float = 10.0, layers: int = 2):
     ref.set_threads(threads)
     ls = [synth.make_moe_layer(SHAPE, seed=1000 + i) for i in range(layers)]
     xn = synth.make_hidden(ls[0].n_embd, T, seed=2001)
+    if zipf > 0:
+        skewed = [synth.zipf_layer_and_hidden(l, T, s=zipf, seed=2002) for l in ls]
+        ls, xn = [l for l, _ in skewed], skewed[0][1]
     ref.moe(ls[0], xn[: min(T, 8)])                       # warm-up (page in, thread pool)
     n, t0 = 0, time.perf_counter()
     while n < 1 or (time.perf_counter() - t0 < seconds and n < 64):
@@ -213,16 +217,33 @@ def run_reference_arm(a):
 
 # ---- GPU ---------------------------------------------------------------------------------------
 
-def device_layer(q, torch, seed: int, device, shard=None):
+def zipf_direction(torch, E: int, X: int, s: float, seed: int, device, mu: float = 4.0):
+    """Config 5's skew (large_model_b200.synth.zipf_layer_and_hidden, on the device): a unit vector u
+    shared by every token's hidden state (x = z + mu u) and per-expert router offsets
+    (b_e / mu) u with b_e = 0.02 sqrt(E) s log(1 / rank_e), so expert e is picked ~ rank_e^-s."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    u = torch.randn(E, generator=g, device=device, dtype=torch.float64)
+    u /= u.norm()
+    rank = torch.randperm(X, generator=g, device=device).to(torch.float64) + 1
+    b = 0.02 * E ** 0.5 * s * -torch.log(rank)
+    return u, b, mu
+
+
+def device_layer(q, torch, seed: int, device, shard=None, zipf=None):
     """A 235B-shape layer drawn on the device with the config's distributions, then uploaded
     through qms_cuda_moe_create from device memory (GGUF layout, repacked by the library).
-    shard = (expert_base, n_local): only those experts (an expert-parallel shard)."""
+    shard = (expert_base, n_local): only those experts (an expert-parallel shard); zipf = the
+    (u, b, mu) of zipf_direction: the router rows get config 5's skew."""
     from large_model_b200 import synth
     E, X, K, F = synth.MOE_SHAPES[SHAPE]
     XL = X if shard is None else shard[1]
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     router = torch.randn((X, E), generator=g, device=device, dtype=torch.float32) * 0.02
+    if zipf is not None:
+        u, b, mu = zipf
+        router = (router.double() + (b / mu)[:, None] * u[None, :]).float().contiguous()
 
     def q4_0(nblocks):
         blk = torch.empty((nblocks, 18), dtype=torch.uint8, device=device)
@@ -262,22 +283,25 @@ def run_batched(a):
     E, X, K, F = 4096, 128, 8, 1536
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:
-        cpu = cpu_reference_batched(T, seconds=10.0 if T <= 256 else 20.0)
+        cpu = cpu_reference_batched(T, seconds=10.0 if T <= 256 else 20.0, zipf=a.zipf)
     ep = a.ep and world > 1
+    zipf = zipf_direction(torch, E, X, a.zipf, 31, dev) if a.zipf > 0 else None
     if ep:                                            # expert parallelism: X / world experts per rank
         from large_model_b200.ep import CudaBackend, ExpertParallelMoe
         per = X // world
-        layers = [device_layer(q, torch, 500 + 17 * i, dev, shard=(rank * per, per)) for i in range(2)]
+        layers = [device_layer(q, torch, 500 + 17 * i, dev, shard=(rank * per, per), zipf=zipf) for i in range(2)]
         eps = [ExpertParallelMoe(CudaBackend(m), X, K, E) for m in layers]
     else:
-        layers = [device_layer(q, torch, 500 + 17 * i, dev) for i in range(2)]
+        layers = [device_layer(q, torch, 500 + 17 * i, dev, zipf=zipf) for i in range(2)]
     g = torch.Generator(device=dev)
     g.manual_seed(11 + rank)                          # every rank its own tokens
     xs = [torch.randn((T, E), generator=g, device=dev, dtype=torch.float32) for _ in range(2)]
+    if zipf is not None:                              # the component every token shares
+        xs = [(x + (zipf[2] * zipf[0]).float()[None, :]).contiguous() for x in xs]
     out = torch.empty((T, E), device=dev, dtype=torch.float32)
     for m in layers:
         m.reserve(T)
-    calls = 8 if T <= 256 else 2
+    calls = 8 if T <= 256 or a.zipf > 0 else 2      # config 5: 8 sequences x 4096 tokens per step
     stream = torch.cuda.Stream(device=dev)
 
     def step():
@@ -301,6 +325,7 @@ def run_batched(a):
             dist.all_gather(sels, sel)
             sel = torch.cat(sels)
         distinct.append(len(torch.unique(sel)))
+        max_expert = int(torch.bincount(sel.reshape(-1).long(), minlength=X).max().item())
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     time.sleep(0.3)
@@ -410,7 +435,11 @@ def run_batched(a):
                            "stage_ms": {"router": round(ksum[0], 4), "gate_up_swiglu": round(ksum[1], 4),
                                         "down_combine": round(ksum[2], 4)},
                            "l2": "inputs larger than L2 (2 layers x 1.36 GB resident)",
-                           "routing": "seeded N(0,1) hidden states, N(0,0.02) router (near-uniform expert load)",
+                           "routing": (f"Zipf({a.zipf}) expert popularity (config 5): a shared hidden-state "
+                                       f"component and per-expert router offsets; per call the busiest expert "
+                                       f"takes {max_expert} of {T * K} slots"
+                                       if a.zipf > 0 else
+                                       "seeded N(0,1) hidden states, N(0,0.02) router (near-uniform expert load)"),
                            "parallelism": f"expert-parallel x{world} (NCCL all-to-all)" if ep else f"replicas x{world}"},
                 "roofline": roof, "cpu_baseline": cpu,
                 "e2e": e2e,
@@ -725,6 +754,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--mode", default="model", choices=["model", "moe", "bs64", "prefill"])
     ap.add_argument("--ep", action="store_true", help="batched modes under torchrun: shard the experts over the ranks")
+    ap.add_argument("--zipf", type=float, default=0.0,
+                    help="batched modes: Zipf(s) expert popularity (config 5: --mode prefill --zipf 1.1)")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":

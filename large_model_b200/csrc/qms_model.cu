@@ -75,7 +75,6 @@ struct QmsCudaModel {
     int *h_pinned;                   // host mirror of ids + pos for the host entry point
     cudaStream_t stream;
     size_t weight_bytes;
-    int l2_prefetch;                 // MoE kernels pull the next layer's projections into L2
     // QMS_PROF sections
     int prof;
     double prof_ms[7];
@@ -284,25 +283,9 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
             g.resid = m->h;
             if ((rc = launch_gemv1(L.o_type, g, m->err, s))) return rc;
             if ((rc = prof_mark(m, ei++, s))) return rc;
-            // while its routing leaves HBM idle, the MoE kernel pulls the next layer's projections
-            // (or the head's first rows) into L2
-            L2Prefetch pf;
-            memset(&pf, 0, sizeof pf);
-            if (m->l2_prefetch) {
-                if (l + 1 < m->L) {
-                    const DevLayer &N = m->layers[l + 1];
-                    pf.ptr[0] = N.wqkv;
-                    pf.bytes[0] = (size_t)m->NQKV * rows_stride(N.qkv_type, E);
-                    pf.ptr[1] = N.wo;
-                    pf.bytes[1] = (size_t)E * rows_stride(N.o_type, m->QD);
-                    pf.n = 2;
-                } else {
-                    pf.ptr[0] = m->head;
-                    pf.bytes[0] = std::min<size_t>((size_t)m->V * rows_stride(m->head_type, E), (size_t)40 << 20);
-                    pf.n = 1;
-                }
-            }
-            rc = moe_forward_normed_bs1(L.moe, m->h, L.ffn_norm, m->eps, m->h, m->h, sel_l, s, &pf);
+        }
+        if (T == 1) {
+            rc = moe_forward_normed_bs1(L.moe, m->h, L.ffn_norm, m->eps, m->h, m->h, sel_l, s);
             if (rc == QMS_CUDA_EUNSUPPORTED) {
                 clear_error();
                 if ((rc = launch_rmsnorm(m->h, L.ffn_norm, m->eps, 1, E, m->xn, nullptr, nullptr, nullptr, s))) return rc;
@@ -489,8 +472,6 @@ int qms_cuda_model_create(const QmsCudaModelDesc *d, QmsCudaModel **out) {
     m->embd_type = et;
     m->head_type = ht;
     m->max_splits = (d->ctx + kSplit - 1) / kSplit;
-    m->l2_prefetch = 1;
-    if (const char *env = getenv("QMS_L2_PREFETCH")) m->l2_prefetch = atoi(env) != 0;   // 0: off (measurements)
     m->layers.resize(d->n_layer);
     int rc = QMS_CUDA_OK;
     const size_t erb = ggml_row_bytes(et, m->E);
@@ -701,6 +682,11 @@ int qms_cuda_model_status(QmsCudaModel *m) {
     QMS_CK(cudaMemcpy(&flags, m->err, 4, cudaMemcpyDeviceToHost));
     if (flags) {
         QMS_CK(cudaMemset(m->err, 0, 4));
+        if (flags & ~3) {
+            set_error("forward: a bounded wait inside the decode kernels gave up (flags 0x%x: 64 = a weight stream, "
+                      "); outputs of that call are invalid", flags);
+            return QMS_CUDA_ETIMEOUT;
+        }
         set_error("forward: a device-side check refused work (flags 0x%x: 1 = position beyond ctx %d, 2 = bad token id)",
                   flags, m->ctx);
         return QMS_CUDA_EINVAL;

@@ -768,10 +768,10 @@ int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int 
 
 namespace qms {
 int moe_forward_normed_bs1(QmsCudaMoe *m, const float *h, const float *nw, float eps, float *out,
-                           const float *resid, int *sel, cudaStream_t s, const L2Prefetch *pf) {
+                           const float *resid, int *sel, cudaStream_t s) {
     if (!m->stream_ok || m->n_local != m->X || m->E % 512 || ((uintptr_t)h & 15) || m->cap_T < 1)
         return QMS_CUDA_EUNSUPPORTED;
-    int rc = stream_forward_bs1(m, h, out, resid, s, nw, eps, pf);
+    int rc = stream_forward_bs1(m, h, out, resid, s, nw, eps);
     if (rc) return rc;
     if (sel) QMS_CK(cudaMemcpyAsync(sel, m->sel, (size_t)m->K * 4, cudaMemcpyDeviceToDevice, s));
     return QMS_CUDA_OK;

@@ -231,20 +231,13 @@ inline bool persistent_grid_fits(int per_sm, int nsm, int grid) {
 
 // batch-1 decode kernels (qms_moe_stream.cu)
 int stream_prepare(QmsCudaMoe *m);     // shape check + kernel attributes; sets m->stream_ok
-// Read-only regions (16-byte aligned) the batch-1 kernel pulls into L2 at its start, before its
-// routing has anything for HBM to do: the weights of the kernels that follow it.
-struct L2Prefetch {
-    int n;
-    const void *ptr[4];
-    size_t bytes[4];
-};
 int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *resid, cudaStream_t s,
-                       const float *nw = nullptr, float eps = 0.0f, const L2Prefetch *pf = nullptr);
+                       const float *nw = nullptr, float eps = 0.0f);
 // One token through the layer with its input RMS-normed inside the batch-1 kernel:
 // out = resid + moe(RMSNorm(h) * nw). Returns QMS_CUDA_EUNSUPPORTED when the batch-1 kernel does
 // not serve this layer (the caller then normalises separately).
 int moe_forward_normed_bs1(QmsCudaMoe *m, const float *h, const float *nw, float eps, float *out,
-                           const float *resid, int *sel, cudaStream_t s, const L2Prefetch *pf = nullptr);
+                           const float *resid, int *sel, cudaStream_t s);
 struct StreamScratch {                 // bytes of the batch-1 kernel's exchange buffers
     size_t lg_flagged, stamps, aq_flagged, part_gu, fin;
 };

@@ -284,17 +284,11 @@ __device__ void route_weights(const float *lg, int X, int K, const int *s_sel, d
 }
 
 // ---- gate/up + SwiGLU + Q8, down, combine in one stream (batch 1) ------------------------------
-constexpr int kPrefetchRegions = 4;
-
 struct DecodeArgs {
     const float *router_lm;               // [X][16][E/16]: element 16*i + k of a row at [k][i]
     const float *xn, *resid;
     const float *nw;                      // optional: xn = RMSNorm(xn) * nw first (ffn_norm, src/model.c:1283)
     float eps;
-    // optional read-only regions (weights of the kernels that follow) pulled into L2 while this
-    // kernel's routing leaves HBM idle; every CTA prefetches its 1/G share of each region
-    const uint8_t *pf[kPrefetchRegions];
-    size_t pf_bytes[kPrefetchRegions];
     float *out;
     const uint8_t *gu, *dn;               // staged experts: gate/up chunks, down column stages
     size_t gu_expert, dn_expert;
@@ -422,13 +416,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_decode_bs1(const DecodeAr
             const uint64_t pol = evict_first_policy();
             for (int k = 0; k < 16; k++)
                 bulk_load(srow + k * PS, a.router_lm + (size_t)c * E + (size_t)k * L, (uint32_t)L * 4, rbar, pol);
-        }
-        for (int r = 0; r < kPrefetchRegions; r++) {  // weights of the next kernels, into L2
-            if (!a.pf[r]) continue;
-            const size_t n = a.pf_bytes[r];
-            const size_t lo = (size_t)c * n / G & ~(size_t)15, hi = (size_t)(c + 1) * n / G & ~(size_t)15;
-            for (size_t o = lo; o < hi; o += 32768)
-                prefetch_l2(a.pf[r] + o, (uint32_t)(hi - o < 32768 ? hi - o : 32768));
         }
     }
     for (int i = threadIdx.x; i <= G; i += blockDim.x) s_rb[i] = part_lo(i, E, G);
@@ -980,12 +967,8 @@ int stream_scratch_sizes(const QmsCudaMoe *m, StreamScratch *sz) {
 }
 
 int stream_forward_bs1(QmsCudaMoe *m, const float *xn, float *out, const float *resid, cudaStream_t s,
-                       const float *nw, float eps, const L2Prefetch *pf) {
+                       const float *nw, float eps) {
     DecodeArgs a;
-    for (int r = 0; r < kPrefetchRegions; r++) {
-        a.pf[r] = pf && r < pf->n ? (const uint8_t *)pf->ptr[r] : nullptr;
-        a.pf_bytes[r] = pf && r < pf->n ? pf->bytes[r] & ~(size_t)15 : 0;
-    }
     a.router_lm = m->router_lm;
     a.xn = xn;
     a.nw = nw;

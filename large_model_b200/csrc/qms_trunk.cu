@@ -1091,6 +1091,27 @@ __device__ __forceinline__ void norm_rope_row(float (&x)[D / 32], const float *n
     }
 }
 
+// RMSNorm + NEOX rotation of one head row from preloaded values: x (the row), w (norm weights) and
+// c / s (cos / sin of the position) as lane + 32 j (src/model.c:403-422, 441-447).
+template <int D>
+__device__ __forceinline__ void norm_rope_pre(float (&x)[D / 32], const float (&w)[D / 32], const float (&c)[D / 64],
+                                              const float (&sn)[D / 64], float eps) {
+    constexpr int J = D / 32, JH = J / 2;
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < J; j++) ss = fma((double)x[j], (double)x[j], ss);
+    ss = warp_sum_d(ss);
+    const double inv = 1.0 / sqrt(ss / D + (double)eps);
+#pragma unroll
+    for (int j = 0; j < J; j++) x[j] = __fmul_rn((float)((double)x[j] * inv), w[j]);
+#pragma unroll
+    for (int j = 0; j < JH; j++) {
+        const float x1 = x[j], x2 = x[j + JH];
+        x[j] = __fsub_rn(__fmul_rn(x1, c[j]), __fmul_rn(x2, sn[j]));
+        x[j + JH] = __fadd_rn(__fmul_rn(x2, c[j]), __fmul_rn(x1, sn[j]));
+    }
+}
+
 // CTA (kv head g, block s of kAttnBlock positions), one warp per q head of the group, lane =
 // position. Scores in qms_vec_dot_f32's order: sixteen 8-long FMA chains, then the hsum tree.
 template <int D>
@@ -1112,11 +1133,28 @@ __global__ void __launch_bounds__(512, 2) k_attn_decode(const AttnArgs a) {
     if (s >= S) return;
     const int p0 = s * PB, p1 = min(npos, p0 + PB), np = p1 - p0;
     const int KD = a.Hk * D;
-    const float *cs = a.rope_cos + (size_t)pos * (D / 2), *sn = a.rope_sin + (size_t)pos * (D / 2);
-    // cached K/V rows of positions [p0, min(p1, pos)) of head g
+    constexpr int J = D / 32, JH = J / 2;
+    const bool has_new = p1 == npos;
     const int nc = min(p1, pos) - p0;
+    // every input in one round trip: this warp's q row, the norm weights, the position's cos / sin,
+    // the new position's raw K / V rows, then the block's cached K / V rows
+    const float *cs = a.rope_cos + (size_t)pos * (D / 2), *snp = a.rope_sin + (size_t)pos * (D / 2);
+    float qx[J], qw[J], kw[J], kx[J], vx[J], c[JH], sn[JH];
+#pragma unroll
+    for (int j = 0; j < J; j++) {
+        qx[j] = __ldcg(a.qkv + (size_t)(g * group + warp) * D + lane + 32 * j);
+        qw[j] = __ldg(a.q_norm + lane + 32 * j);
+        kw[j] = __ldg(a.k_norm + lane + 32 * j);
+        kx[j] = has_new && warp == 0 ? __ldcg(a.qkv + (size_t)a.H * D + (size_t)g * D + lane + 32 * j) : 0.0f;
+        vx[j] = has_new && warp == (group > 1 ? 1 : 0)
+                    ? __ldcg(a.qkv + (size_t)(a.H + a.Hk) * D + (size_t)g * D + lane + 32 * j) : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < JH; j++) {
+        c[j] = __ldg(cs + lane + 32 * j);
+        sn[j] = __ldg(snp + lane + 32 * j);
+    }
     {
-        // every float4 of the block's cached rows, loaded before any is stored (one round trip)
         constexpr int kMaxIt = 4;                        // one round for groups of >= 8 q heads
         const int n4 = nc * (D / 4);
         float4 kv[kMaxIt], vv[kMaxIt];
@@ -1143,34 +1181,22 @@ __global__ void __launch_bounds__(512, 2) k_attn_decode(const AttnArgs a) {
         }
         }
     }
-    // this warp's q head, normalised and rotated (every CTA of the group does it for itself)
-    {
-        const int h = g * group + warp;
-        float x[D / 32];
+    norm_rope_pre<D>(qx, qw, c, sn, a.eps);                   // this warp's q head
 #pragma unroll
-        for (int j = 0; j < D / 32; j++) x[j] = a.qkv[(size_t)h * D + lane + 32 * j];
-        norm_rope_row<D>(x, a.q_norm, a.eps, cs, sn, lane);
+    for (int j = 0; j < J; j++) sq[warp * D + lane + 32 * j] = qx[j];
+    if (has_new && warp == 0) {                               // the new position's K row, appended
+        norm_rope_pre<D>(kx, kw, c, sn, a.eps);
 #pragma unroll
-        for (int j = 0; j < D / 32; j++) sq[warp * D + lane + 32 * j] = x[j];
-    }
-    if (p1 == npos) {                                    // the new position: K / V rows, appended
-        if (warp == 0) {
-            float x[D / 32];
-#pragma unroll
-            for (int j = 0; j < D / 32; j++) x[j] = a.qkv[(size_t)a.H * D + (size_t)g * D + lane + 32 * j];
-            norm_rope_row<D>(x, a.k_norm, a.eps, cs, sn, lane);
-#pragma unroll
-            for (int j = 0; j < D / 32; j++) {
-                sk[(pos - p0) * KP + lane + 32 * j] = x[j];
-                a.kc[(size_t)pos * KD + (size_t)g * D + lane + 32 * j] = x[j];
-            }
+        for (int j = 0; j < J; j++) {
+            sk[(pos - p0) * KP + lane + 32 * j] = kx[j];
+            a.kc[(size_t)pos * KD + (size_t)g * D + lane + 32 * j] = kx[j];
         }
-        if (warp == (group > 1 ? 1 : 0)) {
-            for (int j = 0; j < D / 32; j++) {
-                const float v = a.qkv[(size_t)(a.H + a.Hk) * D + (size_t)g * D + lane + 32 * j];
-                sv[(pos - p0) * D + lane + 32 * j] = v;
-                a.vc[(size_t)pos * KD + (size_t)g * D + lane + 32 * j] = v;
-            }
+    }
+    if (has_new && warp == (group > 1 ? 1 : 0)) {             // and its V row
+#pragma unroll
+        for (int j = 0; j < J; j++) {
+            sv[(pos - p0) * D + lane + 32 * j] = vx[j];
+            a.vc[(size_t)pos * KD + (size_t)g * D + lane + 32 * j] = vx[j];
         }
     }
     __syncthreads();
@@ -1295,3 +1321,4 @@ int launch_attn_decode(const AttnArgs &a, int8_t *xq, float *xd, int *xs, cudaSt
 }
 
 }  // namespace qms
+

@@ -649,12 +649,17 @@ def run_model(a):
         dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    profile_region = os.environ.get("QMS_PROFILE_REGION") == "1"   # ncu --profile-from-start off: the timed steps only
+    if profile_region:
+        torch.cuda.profiler.start()
     with torch.cuda.stream(stream):
         ev0.record(stream)
         for _ in range(a.steps):
             graph.replay()
         ev1.record(stream)
     torch.cuda.synchronize()
+    if profile_region:
+        torch.cuda.profiler.stop()
     clocks = sampler.stop()
     ms = ev0.elapsed_time(ev1)
     if dist:
@@ -730,7 +735,8 @@ def run_model(a):
                     "d2h_bytes_per_step": cfg.vocab * 4,
                     "note": "qms_cuda_forward per token (host id in, the token's 151936 logits to host memory, "
                             "argmax on the host), per token; h2d/d2h bytes are per token"},
-            "gpu_launches": ntok * (2 + 6 * cfg.n_layer),
+            # per token: the embedding gather, per layer QKV / attention / merge / O / MoE, the head
+            "gpu_launches": ntok * (2 + 5 * cfg.n_layer),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

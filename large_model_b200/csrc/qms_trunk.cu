@@ -691,7 +691,7 @@ int launch_attention(const AttnArgs &a, cudaStream_t s) {
 
 namespace qms {
 
-constexpr int kG1Warps = 8;                          // consumer warps (+ one producer warp); 16 for the head
+constexpr int kG1Warps = 16;                         // consumer warps (+ one producer warp), also for the head
 constexpr int kG1WarpsHead = 16;
 constexpr uint32_t kG1Stage = 32 * 1024;             // bytes per ring slot (whole rows)
 constexpr int kG1MaxRing = 8;

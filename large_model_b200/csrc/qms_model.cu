@@ -73,6 +73,8 @@ struct QmsCudaModel {
     unsigned long long *amax;
     int max_splits;
     int *h_pinned;                   // host mirror of ids + pos for the host entry point
+    int *flags;                      // device [1 + L]: the trunk's error word, then each MoE layer's
+    int *h_flags;                    // pinned host mirror of flags, read once per host call
     cudaStream_t stream;
     size_t weight_bytes;
     // QMS_PROF sections
@@ -156,7 +158,7 @@ static int model_reserve(QmsCudaModel *m, int T) {
     const size_t o_ids = take((size_t)T * 4), o_pos = take(4);
     const size_t o_sel = take((size_t)m->L * T * m->K * 4);
     const size_t o_po = take((size_t)m->H * m->max_splits * m->D * 4), o_pml = take((size_t)m->H * m->max_splits * 16);
-    const size_t o_tk = take((size_t)m->Hk * m->nhb * 4), o_at = take(4), o_err = take(4), o_amax = take(8);
+    const size_t o_tk = take((size_t)m->Hk * m->nhb * 4), o_at = take(4), o_amax = take(8);
     void *p = nullptr;
     int rc = dmalloc(&p, off, "forward scratch");
     if (rc) return rc;
@@ -196,7 +198,7 @@ static int model_reserve(QmsCudaModel *m, int T) {
     m->part_ml = (double *)(b + o_pml);
     m->ticket = (int *)(b + o_tk);
     m->amax_ticket = (int *)(b + o_at);
-    m->err = (int *)(b + o_err);
+    m->err = m->flags;
     m->amax = (unsigned long long *)(b + o_amax);
     m->cap_T = T;
     for (auto &L : m->layers)
@@ -410,6 +412,8 @@ void qms_cuda_model_free(QmsCudaModel *m) {
     cudaFree(m->vc);
     cudaFree(m->scratch);
     if (m->h_pinned) cudaFreeHost(m->h_pinned);
+    cudaFree(m->flags);
+    if (m->h_flags) cudaFreeHost(m->h_flags);
     for (cudaEvent_t e : m->ev) cudaEventDestroy(e);
     if (m->stream) cudaStreamDestroy(m->stream);
     if (cur >= 0) cudaSetDevice(cur);
@@ -482,6 +486,13 @@ int qms_cuda_model_create(const QmsCudaModelDesc *d, QmsCudaModel **out) {
     if (!rc) rc = dmalloc((void **)&m->head, (size_t)m->V * rows_stride(ht, m->E), "the output head");
     if (!rc) rc = dmalloc((void **)&m->rope_cos, rope, "RoPE tables");
     if (!rc) rc = dmalloc((void **)&m->rope_sin, rope, "RoPE tables");
+    if (!rc) rc = dmalloc((void **)&m->flags, (size_t)(1 + m->L) * 4, "error flags");
+    if (!rc && (cudaMemset(m->flags, 0, (size_t)(1 + m->L) * 4) != cudaSuccess ||
+                cudaMallocHost(&m->h_flags, (size_t)(1 + m->L) * 4) != cudaSuccess)) {
+        cudaGetLastError();
+        set_error("model_create: cannot set up the error flags");
+        rc = QMS_CUDA_ENOMEM;
+    }
     if (!rc) rc = dmalloc((void **)&m->kc, kv, "the K cache");
     if (!rc) rc = dmalloc((void **)&m->vc, kv, "the V cache");
     if (!rc) rc = to_device(m->embd, d->embd, (size_t)m->V * erb, d->src_on_device);
@@ -578,7 +589,12 @@ int qms_cuda_model_set_layer(QmsCudaModel *m, int l, const QmsCudaLayerDesc *ld)
         rc = upload_rows(ld->o_type, &src, &rows, 1, m->QD, on_dev, L.wo);
     }
     if (!rc) rc = qms_cuda_moe_create(&md, &L.moe);
-    if (!rc) rc = qms_cuda_moe_reserve(L.moe, m->cap_T);
+    if (!rc) {
+        L.moe->err_ext = m->flags + 1 + l;    // one read of the model's flags covers every layer
+        L.moe->err = L.moe->err_ext;
+        QMS_CK(cudaMemset(L.moe->err, 0, 4));
+        rc = qms_cuda_moe_reserve(L.moe, m->cap_T);
+    }
     if (rc) {
         cudaFree(L.norms);
         cudaFree(L.wqkv);
@@ -629,6 +645,8 @@ int qms_cuda_decode_step(QmsCudaModel *m, int *tok, int *pos, float *logits, voi
     return forward_core(m, tok, 1, pos, logits ? logits : m->logits, 0, nullptr, tok, pos, (cudaStream_t)stream);
 }
 
+static int flags_check(QmsCudaModel *m);
+
 int qms_cuda_forward(QmsCudaModel *m, const int *ids, int T, int pos0, float *logits, int all_logits, int *sel_trace) {
     clear_error();
     QMS_REQUIRE(m && ids && logits && T >= 0 && pos0 >= 0, QMS_CUDA_EINVAL, "forward: bad arguments");
@@ -667,10 +685,38 @@ int qms_cuda_forward(QmsCudaModel *m, const int *ids, int T, int pos0, float *lo
             for (int l = 0; l < m->L; l++)
                 QMS_CK(cudaMemcpyAsync(sel_trace + ((size_t)l * T + c0) * m->K, m->sel + (size_t)l * Tc * m->K,
                                        (size_t)Tc * m->K * 4, cudaMemcpyDeviceToHost, s));
+        if (last) QMS_CK(cudaMemcpyAsync(m->h_flags, m->flags, (size_t)(1 + m->L) * 4, cudaMemcpyDeviceToHost, s));
         QMS_CK(cudaStreamSynchronize(s));
         if ((rc = prof_collect(m))) return rc;
     }
-    return qms_cuda_model_status(m);
+    return flags_check(m);
+}
+
+// The flags in h_flags (copied after the stream's last kernel): the trunk's word, then each MoE
+// layer's. A raised flag is reported once and cleared.
+static int flags_check(QmsCudaModel *m) {
+    int trunk = m->h_flags[0], moe = 0, layer = -1;
+    for (int l = 0; l < m->L; l++)
+        if (m->h_flags[1 + l] && layer < 0) {
+            moe = m->h_flags[1 + l];
+            layer = l;
+        }
+    if (!trunk && layer < 0) return QMS_CUDA_OK;
+    QMS_CK(cudaMemset(m->flags, 0, (size_t)(1 + m->L) * 4));
+    memset(m->h_flags, 0, (size_t)(1 + m->L) * 4);
+    if (trunk & ~3) {
+        set_error("forward: a bounded wait inside the decode kernels gave up (flags 0x%x: 64 = a weight stream, "
+                  "128 = attention); outputs of that call are invalid", trunk);
+        return QMS_CUDA_ETIMEOUT;
+    }
+    if (trunk) {
+        set_error("forward: a device-side check refused work (flags 0x%x: 1 = position beyond ctx %d, 2 = bad token id)",
+                  trunk, m->ctx);
+        return QMS_CUDA_EINVAL;
+    }
+    set_error("moe: layer %d: a bounded wait inside the decode kernels gave up (flags 0x%x); outputs of that call "
+              "are invalid", layer, moe);
+    return QMS_CUDA_ETIMEOUT;
 }
 
 int qms_cuda_model_status(QmsCudaModel *m) {
@@ -678,22 +724,8 @@ int qms_cuda_model_status(QmsCudaModel *m) {
     int rc = ensure_dev(m->device);
     if (rc) return rc;
     QMS_CK(cudaDeviceSynchronize());
-    int flags = 0;
-    QMS_CK(cudaMemcpy(&flags, m->err, 4, cudaMemcpyDeviceToHost));
-    if (flags) {
-        QMS_CK(cudaMemset(m->err, 0, 4));
-        if (flags & ~3) {
-            set_error("forward: a bounded wait inside the decode kernels gave up (flags 0x%x: 64 = a weight stream, "
-                      "); outputs of that call are invalid", flags);
-            return QMS_CUDA_ETIMEOUT;
-        }
-        set_error("forward: a device-side check refused work (flags 0x%x: 1 = position beyond ctx %d, 2 = bad token id)",
-                  flags, m->ctx);
-        return QMS_CUDA_EINVAL;
-    }
-    for (auto &L : m->layers)
-        if (L.moe && (rc = qms_cuda_moe_status(L.moe))) return rc;
-    return QMS_CUDA_OK;
+    QMS_CK(cudaMemcpy(m->h_flags, m->flags, (size_t)(1 + m->L) * 4, cudaMemcpyDeviceToHost));
+    return flags_check(m);
 }
 
 int qms_cuda_model_profile(QmsCudaModel *m, int on, double *ms) {

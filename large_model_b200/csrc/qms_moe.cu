@@ -697,7 +697,7 @@ int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
     m->aq_d = (float *)(b + o_aq_d);
     m->aq_s = (int *)(b + o_aq_s);
     m->cnt = (int *)(b + o_cnt);
-    m->err = (int *)(b + o_err);
+    m->err = m->err_ext ? m->err_ext : (int *)(b + o_err);
     m->lg_flagged = (unsigned long long *)(b + o_lgf);
     m->stamps = (unsigned *)(b + o_stamps);
     m->aq_flagged = (unsigned long long *)(b + o_aqf);

@@ -189,6 +189,7 @@ struct QmsCudaMoe {
     int *aq_s;
     int *cnt;            // [0]: router arrivals; [1 + slot*nbF + g]: gate/up group arrivals
     int *err;            // device error flags (bounded waits that gave up)
+    int *err_ext;        // when set (a model owns the layer): the flag word to use instead of the scratch one
     // batch-1 kernel exchange buffers, in flagged words (data | call stamp << 32)
     unsigned long long *lg_flagged;          // [copies][X] router logits
     unsigned long long *aq_flagged;          // [K*F/32 groups][10]: 8 words of q, d, sum

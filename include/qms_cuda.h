@@ -239,6 +239,27 @@ int qms_cuda_forward_dev(QmsCudaModel *m, const int *ids, int T, const int *pos,
  * and logits (device fp32 [vocab], optional) receive the step's logits. Graph-capturable: a graph
  * of N steps generates N tokens with no host round trip. */
 int qms_cuda_decode_step(QmsCudaModel *m, int *tok, int *pos, float *logits, void *stream);
+
+/* Several sequences. The reference serves one sequence per model (src/model.h:116-118,
+ * qms_forward's KV cache); the device model can hold n_seq KV caches of ctx positions each.
+ * set_sequences reallocates them (all positions cleared; sequence 0 is the one qms_cuda_forward
+ * uses); n_seq * n_layer * ctx * 4 KB of device memory for 235B-shape layers. No other call may
+ * be running, and CUDA graphs captured before no longer apply. */
+int qms_cuda_model_set_sequences(QmsCudaModel *m, int n_seq);
+/* Copy positions [0, npos) of sequence src's cache to sequence dst (a shared prompt prefix). */
+int qms_cuda_model_copy_sequence(QmsCudaModel *m, int src, int dst, int npos);
+/* qms_cuda_forward on sequence seq's cache (qms_cuda_forward is seq 0). */
+int qms_cuda_forward_seq(QmsCudaModel *m, int seq, const int *ids, int T, int pos0, float *logits,
+                         int all_logits, int *sel_trace);
+/* One token for each of B sequences in one pass (batched decode): sequence b (0 <= b < B) takes
+ * ids[b] at position pos[b]; logits: host fp32 [B][vocab]. Host buffers, synchronous; each row is
+ * what qms_cuda_forward_seq(m, b, &ids[b], 1, pos[b], ...) would return, up to the float
+ * summation order of the multi-token kernels. B <= n_seq and B <= 256. */
+int qms_cuda_forward_batch(QmsCudaModel *m, int B, const int *ids, const int *pos, float *logits);
+/* The same on the device, greedy: tok[B], pos[B] device ints; each row's argmax (first index among
+ * equal maxima) is written back to tok[b] and pos[b] is incremented; logits (device fp32 [B][vocab])
+ * optional. Graph-capturable. */
+int qms_cuda_decode_batch(QmsCudaModel *m, int B, int *tok, int *pos, float *logits, void *stream);
 /* The forward's scratch covers up to 256 tokens per pass from creation on (longer calls run in
  * passes of 256), so device pointers never move and captured graphs stay valid; T > 256 is
  * QMS_CUDA_EINVAL. */

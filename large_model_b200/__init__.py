@@ -101,6 +101,11 @@ def lib() -> C.CDLL:
     L.qms_cuda_forward.argtypes = [vp, vp, i32, i32, vp, i32, vp]
     L.qms_cuda_forward_dev.argtypes = [vp, vp, i32, vp, vp, i32, vp]
     L.qms_cuda_decode_step.argtypes = [vp, vp, vp, vp, vp]
+    L.qms_cuda_model_set_sequences.argtypes = [vp, i32]
+    L.qms_cuda_model_copy_sequence.argtypes = [vp, i32, i32, i32]
+    L.qms_cuda_forward_seq.argtypes = [vp, i32, vp, i32, i32, vp, i32, vp]
+    L.qms_cuda_forward_batch.argtypes = [vp, i32, vp, vp, vp]
+    L.qms_cuda_decode_batch.argtypes = [vp, i32, vp, vp, vp, vp]
     L.qms_cuda_model_reserve.argtypes = [vp, i32]
     L.qms_cuda_model_status.argtypes = [vp]
     L.qms_cuda_model_profile.argtypes = [vp, i32, vp]
@@ -424,18 +429,41 @@ class Model:
         check(lib().qms_cuda_model_profile(self.h, int(on), ms))
         return list(ms)
 
-    def forward(self, ids, pos0: int, all_logits: bool = False, trace: bool = False):
-        """qms_forward on host buffers: returns logits (numpy [vocab] or [T][vocab]) and, with
-        trace, the selected experts [n_layer][T][n_used]."""
+    def forward(self, ids, pos0: int, all_logits: bool = False, trace: bool = False, seq: int = 0):
+        """qms_forward on host buffers (sequence seq's KV cache): returns logits (numpy [vocab] or
+        [T][vocab]) and, with trace, the selected experts [n_layer][T][n_used]."""
         ids = np.ascontiguousarray(ids, np.int32)
         T = ids.shape[0]
         V = self.cfg.vocab
         logits = np.empty((T, V) if all_logits else (V,), np.float32)
         sel = np.empty((self.cfg.n_layer, T, self.cfg.n_used), np.int32) if trace else None
-        check(lib().qms_cuda_forward(self.h, C.c_void_p(ids.ctypes.data), T, int(pos0),
-                                     C.c_void_p(logits.ctypes.data), int(all_logits),
-                                     None if sel is None else C.c_void_p(sel.ctypes.data)))
+        check(lib().qms_cuda_forward_seq(self.h, int(seq), C.c_void_p(ids.ctypes.data), T, int(pos0),
+                                         C.c_void_p(logits.ctypes.data), int(all_logits),
+                                         None if sel is None else C.c_void_p(sel.ctypes.data)))
         return (logits, sel) if trace else logits
+
+    def set_sequences(self, n_seq: int):
+        """KV caches for n_seq sequences (qms_cuda_model_set_sequences; caches cleared)."""
+        check(lib().qms_cuda_model_set_sequences(self.h, int(n_seq)))
+
+    def copy_sequence(self, src: int, dst: int, npos: int):
+        check(lib().qms_cuda_model_copy_sequence(self.h, int(src), int(dst), int(npos)))
+
+    def forward_batch(self, ids, pos):
+        """One token for each of B sequences (host ids[B], pos[B]): returns logits [B][vocab]."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        pos = np.ascontiguousarray(pos, np.int32)
+        B = ids.shape[0]
+        assert pos.shape == (B,)
+        logits = np.empty((B, self.cfg.vocab), np.float32)
+        check(lib().qms_cuda_forward_batch(self.h, B, C.c_void_p(ids.ctypes.data), C.c_void_p(pos.ctypes.data),
+                                           C.c_void_p(logits.ctypes.data)))
+        return logits
+
+    def decode_batch(self, tok, pos, logits=None, stream=None):
+        """One greedy step for B sequences on the device: tok / pos torch CUDA int32 [B], updated
+        in place (qms_cuda_decode_batch)."""
+        check(lib().qms_cuda_decode_batch(self.h, tok.numel(), _ptr(tok), _ptr(pos), _ptr(logits), _stream(stream)))
 
     def forward_dev(self, ids, pos, logits, all_logits: bool = False, stream=None):
         """Device buffers (torch CUDA int32 ids [T], int32 pos [1], float32 logits)."""

@@ -56,7 +56,9 @@ struct QmsCudaModel {
     int head_type;
     uint8_t *head;                   // repacked rows
     float *rope_cos, *rope_sin;      // [ctx][D/2]
-    float *kc, *vc;                  // [L][ctx][KD]
+    float *kc, *vc;                  // [n_seq][L][ctx][KD]
+    int n_seq;                       // sequences with a KV cache of ctx positions each
+    size_t seq_stride;               // floats between two sequences' caches (L * ctx * KD)
     std::vector<DevLayer> layers;
     // forward scratch for cap_T tokens
     int cap_T;
@@ -67,6 +69,7 @@ struct QmsCudaModel {
     float *xd;
     int *xs;
     int *ids, *pos, *sel;
+    int *pos_vec;                    // [cap_T] positions of a batched host call
     float *part_o;
     double *part_ml;
     int *ticket, *amax_ticket, *err;
@@ -155,7 +158,7 @@ static int model_reserve(QmsCudaModel *m, int T) {
     const size_t o_qkv = take((size_t)T * m->NQKV * 4), o_att = take((size_t)T * m->QD * 4);
     const size_t o_lg = take((size_t)T * m->V * 4);
     const size_t o_xq = take((size_t)T * wq), o_xd = take((size_t)T * wq / 32 * 4), o_xs = take((size_t)T * wq / 32 * 4);
-    const size_t o_ids = take((size_t)T * 4), o_pos = take(4);
+    const size_t o_ids = take((size_t)T * 4), o_pos = take(4), o_posv = take((size_t)T * 4);
     const size_t o_sel = take((size_t)m->L * T * m->K * 4);
     const size_t o_po = take((size_t)m->H * m->max_splits * m->D * 4), o_pml = take((size_t)m->H * m->max_splits * 16);
     const size_t o_tk = take((size_t)m->Hk * m->nhb * 4), o_at = take(4), o_amax = take(8);
@@ -168,7 +171,7 @@ static int model_reserve(QmsCudaModel *m, int T) {
         return QMS_CUDA_ECUDA;
     }
     int *hp = nullptr;
-    if (cudaMallocHost(&hp, (size_t)(T + 1) * 4) != cudaSuccess) {
+    if (cudaMallocHost(&hp, (size_t)(2 * T + 1) * 4) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(p);
         set_error("model: cannot allocate pinned host memory");
@@ -193,6 +196,7 @@ static int model_reserve(QmsCudaModel *m, int T) {
     m->xs = (int *)(b + o_xs);
     m->ids = (int *)(b + o_ids);
     m->pos = (int *)(b + o_pos);
+    m->pos_vec = (int *)(b + o_posv);
     m->sel = (int *)(b + o_sel);
     m->part_o = (float *)(b + o_po);
     m->part_ml = (double *)(b + o_pml);
@@ -220,8 +224,11 @@ static int prof_mark(QmsCudaModel *m, size_t i, cudaStream_t s) {
 
 // One pass over the layers for T <= cap_T tokens. ids, pos: device. logits: device
 // [all ? T : 1][V]. tok != NULL: fused greedy argmax (T == 1) into *tok, and *pos advances.
+// One pass over the layers for T tokens. Single sequence `seq`: tokens at *pos + t. Batch
+// (pos_vec != NULL): token t is sequence t at position pos_vec[t]. tok != NULL: greedy argmax of
+// the head into tok (T == 1 fused into the head; batch per row) and pos_adv += 1.
 static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, float *logits, int all, int *sel,
-                        int *tok, int *pos_adv, cudaStream_t s) {
+                        int *tok, int *pos_adv, cudaStream_t s, int seq = 0, const int *pos_vec = nullptr) {
     int rc;
     const int E = m->E;
     size_t ei = 0;
@@ -235,6 +242,8 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
     at.rope_cos = m->rope_cos;
     at.rope_sin = m->rope_sin;
     at.pos = pos;
+    at.pos_vec = pos_vec;
+    at.seq_stride = m->seq_stride;
     at.T = T;
     at.ctx = m->ctx;
     at.H = m->H;
@@ -252,12 +261,13 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
         const DevLayer &L = m->layers[l];
         at.q_norm = L.q_norm;
         at.k_norm = L.k_norm;
-        at.kc = m->kc + (size_t)l * m->ctx * m->KD;
-        at.vc = m->vc + (size_t)l * m->ctx * m->KD;
+        at.kc = m->kc + (size_t)seq * m->seq_stride + (size_t)l * m->ctx * m->KD;
+        at.vc = m->vc + (size_t)seq * m->seq_stride + (size_t)l * m->ctx * m->KD;
         int *sel_l = sel ? sel + (size_t)l * T * m->K : nullptr;
         GemvArgs g;
         memset(&g, 0, sizeof g);
-        if (T == 1) {
+        const bool one = T == 1 && !pos_vec;
+        if (one) {
             // one token: streaming projections, fused attention, RMSNorm inside the MoE kernel
             g.w = L.wqkv;
             g.stride = rows_stride(L.qkv_type, E);
@@ -286,7 +296,7 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
             if ((rc = launch_gemv1(L.o_type, g, m->err, s))) return rc;
             if ((rc = prof_mark(m, ei++, s))) return rc;
         }
-        if (T == 1) {
+        if (one) {
             rc = moe_forward_normed_bs1(L.moe, m->h, L.ffn_norm, m->eps, m->h, m->h, sel_l, s);
             if (rc == QMS_CUDA_EUNSUPPORTED) {
                 clear_error();
@@ -346,15 +356,15 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
     g.eps = m->eps;
     g.y = logits;
     g.ldy = m->V;
-    const int nT = all ? T : 1;
+    const int nT = all || pos_vec ? T : 1;
     g.T = nT;
-    if (tok) {
+    if (tok && !pos_vec) {
         g.amax = m->amax;
         g.ticket = m->amax_ticket;
         g.tok = tok;
         g.pos = pos_adv;
     }
-    if (nT == 1) {
+    if (nT == 1 && !pos_vec) {
         g.x = m->h + (size_t)(T - 1) * E;
         g.ldx = E;
         g.nw = m->out_norm;
@@ -365,6 +375,7 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
         g.xd = m->xd;
         g.xs = m->xs;
         if ((rc = launch_gemv(m->head_type, g, s))) return rc;
+        if (tok && pos_vec && (rc = launch_argmax_rows(logits, m->V, T, m->V, tok, pos_adv, s))) return rc;
     }
     if ((rc = prof_mark(m, ei++, s))) return rc;
     return QMS_CUDA_OK;
@@ -479,6 +490,8 @@ int qms_cuda_model_create(const QmsCudaModelDesc *d, QmsCudaModel **out) {
     m->layers.resize(d->n_layer);
     int rc = QMS_CUDA_OK;
     const size_t erb = ggml_row_bytes(et, m->E);
+    m->n_seq = 1;
+    m->seq_stride = (size_t)m->L * m->ctx * m->KD;
     const size_t kv = (size_t)m->L * m->ctx * m->KD * 4;
     const size_t rope = (size_t)m->ctx * (m->D / 2) * 4;
     if (!rc) rc = dmalloc((void **)&m->embd, (size_t)m->V * erb, "token_embd");
@@ -612,7 +625,7 @@ int qms_cuda_model_set_layer(QmsCudaModel *m, int l, const QmsCudaLayerDesc *ld)
 int64_t qms_cuda_model_device_bytes(const QmsCudaModel *m) {
     if (!m) return 0;
     int64_t b = (int64_t)m->weight_bytes + (int64_t)m->scratch_bytes;
-    b += (int64_t)2 * m->L * m->ctx * m->KD * 4 + (int64_t)2 * m->ctx * (m->D / 2) * 4;
+    b += (int64_t)2 * m->n_seq * m->L * m->ctx * m->KD * 4 + (int64_t)2 * m->ctx * (m->D / 2) * 4;
     for (const auto &L : m->layers) {
         if (!L.set) continue;
         b += (int64_t)((2 * m->E + 2 * m->D) * 4) + (int64_t)m->NQKV * rows_stride(L.qkv_type, m->E) +
@@ -648,8 +661,14 @@ int qms_cuda_decode_step(QmsCudaModel *m, int *tok, int *pos, float *logits, voi
 static int flags_check(QmsCudaModel *m);
 
 int qms_cuda_forward(QmsCudaModel *m, const int *ids, int T, int pos0, float *logits, int all_logits, int *sel_trace) {
+    return qms_cuda_forward_seq(m, 0, ids, T, pos0, logits, all_logits, sel_trace);
+}
+
+int qms_cuda_forward_seq(QmsCudaModel *m, int seq, const int *ids, int T, int pos0, float *logits, int all_logits,
+                         int *sel_trace) {
     clear_error();
     QMS_REQUIRE(m && ids && logits && T >= 0 && pos0 >= 0, QMS_CUDA_EINVAL, "forward: bad arguments");
+    QMS_REQUIRE(seq >= 0 && seq < m->n_seq, QMS_CUDA_EINVAL, "forward: sequence %d of %d", seq, m->n_seq);
     if (T == 0) return QMS_CUDA_OK;
     QMS_REQUIRE((int64_t)pos0 + T <= m->ctx, QMS_CUDA_EINVAL, "forward: context %d exceeded", m->ctx);
     for (int t = 0; t < T; t++) QMS_REQUIRE(ids[t] >= 0 && ids[t] < m->V, QMS_CUDA_EINVAL, "forward: bad id %d", ids[t]);
@@ -674,7 +693,7 @@ int qms_cuda_forward(QmsCudaModel *m, const int *ids, int T, int pos0, float *lo
         QMS_CK(cudaMemcpyAsync(m->pos, m->h_pinned + Tc, 4, cudaMemcpyHostToDevice, s));
         const int want = all_logits || last;
         if ((rc = forward_core(m, m->ids, Tc, m->pos, m->logits, all_logits, sel_trace ? m->sel : nullptr, nullptr,
-                               nullptr, s)))
+                               nullptr, s, seq)))
             return rc;
         if (want) {
             const size_t n = (size_t)(all_logits ? Tc : 1) * m->V;
@@ -717,6 +736,85 @@ static int flags_check(QmsCudaModel *m) {
     set_error("moe: layer %d: a bounded wait inside the decode kernels gave up (flags 0x%x); outputs of that call "
               "are invalid", layer, moe);
     return QMS_CUDA_ETIMEOUT;
+}
+
+int qms_cuda_model_set_sequences(QmsCudaModel *m, int n_seq) {
+    clear_error();
+    QMS_REQUIRE(m && n_seq >= 1, QMS_CUDA_EINVAL, "set_sequences: bad arguments");
+    int rc = ensure_dev(m->device);
+    if (rc) return rc;
+    if (n_seq == m->n_seq) return QMS_CUDA_OK;
+    const size_t kv = (size_t)n_seq * m->seq_stride * 4;
+    float *kc = nullptr, *vc = nullptr;
+    rc = dmalloc((void **)&kc, kv, "the K caches");
+    if (!rc) rc = dmalloc((void **)&vc, kv, "the V caches");
+    if (!rc && (cudaMemset(kc, 0, kv) != cudaSuccess || cudaMemset(vc, 0, kv) != cudaSuccess)) {
+        set_error("set_sequences: memset failed");
+        rc = QMS_CUDA_ECUDA;
+    }
+    if (rc) {
+        cudaFree(kc);
+        cudaFree(vc);
+        return rc;
+    }
+    QMS_CK(cudaDeviceSynchronize());
+    cudaFree(m->kc);
+    cudaFree(m->vc);
+    m->kc = kc;
+    m->vc = vc;
+    m->n_seq = n_seq;
+    return QMS_CUDA_OK;
+}
+
+int qms_cuda_model_copy_sequence(QmsCudaModel *m, int src, int dst, int npos) {
+    clear_error();
+    QMS_REQUIRE(m && src >= 0 && dst >= 0 && src < m->n_seq && dst < m->n_seq && src != dst && npos >= 0 &&
+                    npos <= m->ctx,
+                QMS_CUDA_EINVAL, "copy_sequence: bad arguments");
+    int rc = ensure_dev(m->device);
+    if (rc) return rc;
+    const size_t layer = (size_t)m->ctx * m->KD, n = (size_t)npos * m->KD * 4;
+    for (int l = 0; l < m->L && n; l++) {
+        const size_t so = (size_t)src * m->seq_stride + l * layer, d = (size_t)dst * m->seq_stride + l * layer;
+        QMS_CK(cudaMemcpyAsync(m->kc + d, m->kc + so, n, cudaMemcpyDeviceToDevice, m->stream));
+        QMS_CK(cudaMemcpyAsync(m->vc + d, m->vc + so, n, cudaMemcpyDeviceToDevice, m->stream));
+    }
+    QMS_CK(cudaStreamSynchronize(m->stream));
+    return QMS_CUDA_OK;
+}
+
+int qms_cuda_forward_batch(QmsCudaModel *m, int B, const int *ids, const int *pos, float *logits) {
+    clear_error();
+    QMS_REQUIRE(m && ids && pos && logits && B >= 1, QMS_CUDA_EINVAL, "forward_batch: bad arguments");
+    QMS_REQUIRE(B <= m->n_seq && B <= m->cap_T, QMS_CUDA_EINVAL, "forward_batch: %d sequences (%d with caches, %d per pass)",
+                B, m->n_seq, m->cap_T);
+    for (int b = 0; b < B; b++) {
+        QMS_REQUIRE(ids[b] >= 0 && ids[b] < m->V, QMS_CUDA_EINVAL, "forward_batch: bad id %d", ids[b]);
+        QMS_REQUIRE(pos[b] >= 0 && pos[b] < m->ctx, QMS_CUDA_EINVAL, "forward_batch: context %d exceeded", m->ctx);
+    }
+    int rc = ensure_dev(m->device);
+    if (rc || (rc = layers_ready(m))) return rc;
+    const cudaStream_t s = m->stream;
+    QMS_CK(cudaStreamSynchronize(s));
+    memcpy(m->h_pinned, ids, (size_t)B * 4);
+    memcpy(m->h_pinned + B, pos, (size_t)B * 4);
+    QMS_CK(cudaMemcpyAsync(m->ids, m->h_pinned, (size_t)B * 4, cudaMemcpyHostToDevice, s));
+    QMS_CK(cudaMemcpyAsync(m->pos_vec, m->h_pinned + B, (size_t)B * 4, cudaMemcpyHostToDevice, s));
+    if ((rc = forward_core(m, m->ids, B, nullptr, m->logits, 1, nullptr, nullptr, nullptr, s, 0, m->pos_vec))) return rc;
+    QMS_CK(cudaMemcpyAsync(logits, m->logits, (size_t)B * m->V * 4, cudaMemcpyDeviceToHost, s));
+    QMS_CK(cudaMemcpyAsync(m->h_flags, m->flags, (size_t)(1 + m->L) * 4, cudaMemcpyDeviceToHost, s));
+    QMS_CK(cudaStreamSynchronize(s));
+    return flags_check(m);
+}
+
+int qms_cuda_decode_batch(QmsCudaModel *m, int B, int *tok, int *pos, float *logits, void *stream) {
+    QMS_REQUIRE(m && tok && pos && B >= 1, QMS_CUDA_EINVAL, "decode_batch: bad arguments");
+    QMS_REQUIRE(B <= m->n_seq && B <= m->cap_T, QMS_CUDA_EINVAL, "decode_batch: %d sequences (%d with caches, %d per pass)",
+                B, m->n_seq, m->cap_T);
+    int rc = ensure_dev(m->device);
+    if (rc || (rc = layers_ready(m))) return rc;
+    return forward_core(m, tok, B, nullptr, logits ? logits : m->logits, 1, nullptr, tok, pos, (cudaStream_t)stream, 0,
+                        pos);
 }
 
 int qms_cuda_model_status(QmsCudaModel *m) {

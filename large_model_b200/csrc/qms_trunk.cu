@@ -501,18 +501,19 @@ __global__ void __launch_bounds__(256) k_qk_rope(const AttnArgs a) {
     pdl_trigger();
     pdl_wait();
     if (hh >= a.H + 2 * a.Hk) return;
-    const int p = *a.pos + t;
+    const int p = a.pos_vec ? a.pos_vec[t] : *a.pos + t;
     if (p < 0 || p >= a.ctx) {
         if (lane == 0) atomicOr(a.err, 1);
         return;
     }
     const int KD = a.Hk * D;
+    const size_t cb = a.pos_vec ? (size_t)t * a.seq_stride : 0;   // this token's sequence
     float *row = a.qkv + (size_t)t * a.ldq + (size_t)hh * D;
     float x[J];
 #pragma unroll
     for (int j = 0; j < J; j++) x[j] = row[lane + 32 * j];
     if (hh >= a.H + a.Hk) {                                    // v head: append as is
-        float *dst = a.vc + (size_t)p * KD + (size_t)(hh - a.H - a.Hk) * D;
+        float *dst = a.vc + cb + (size_t)p * KD + (size_t)(hh - a.H - a.Hk) * D;
 #pragma unroll
         for (int j = 0; j < J; j++) dst[lane + 32 * j] = x[j];
         return;
@@ -533,7 +534,7 @@ __global__ void __launch_bounds__(256) k_qk_rope(const AttnArgs a) {
         x[j] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
         x[j + JH] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
     }
-    float *dst = hh < a.H ? row : a.kc + (size_t)p * KD + (size_t)(hh - a.H) * D;
+    float *dst = hh < a.H ? row : a.kc + cb + (size_t)p * KD + (size_t)(hh - a.H) * D;
 #pragma unroll
     for (int j = 0; j < J; j++) dst[lane + 32 * j] = x[j];
 }
@@ -561,8 +562,9 @@ __global__ void __launch_bounds__(128) k_attention(const AttnArgs a) {
     __shared__ int s_last;
     pdl_trigger();
     pdl_wait();
-    const int pt = *a.pos + t;
+    const int pt = a.pos_vec ? a.pos_vec[t] : *a.pos + t;
     if (pt < 0 || pt >= a.ctx) return;           // k_qk_rope has flagged it
+    const size_t cb = a.pos_vec ? (size_t)t * a.seq_stride : 0;
     const int npos = pt + 1;
     int p0 = 0, p1 = npos, S = 1;
     if (a.split > 0) {
@@ -577,7 +579,7 @@ __global__ void __launch_bounds__(128) k_attention(const AttnArgs a) {
     float qr[NQ];
 #pragma unroll
     for (int i = 0; i < NQ; i++) qr[i] = qh[16 * i + k16];
-    const float *kb = a.kc + (size_t)g * D, *vb = a.vc + (size_t)g * D;
+    const float *kb = a.kc + cb + (size_t)g * D, *vb = a.vc + cb + (size_t)g * D;
     float o[DPL];
 #pragma unroll
     for (int d = 0; d < DPL; d++) o[d] = 0.0f;
@@ -674,6 +676,39 @@ __global__ void __launch_bounds__(128) k_attention(const AttnArgs a) {
     for (int d = 0; d < DPL; d++) out[d] = (float)((double)acc[d] / Z);
     __syncthreads();
     if (threadIdx.x == 0) a.ticket[blockIdx.x] = 0;
+}
+
+// One CTA per row: the largest argmax_key (NaN never wins, ties to the lower index).
+__global__ void __launch_bounds__(256) k_argmax_rows(const float *__restrict__ logits, int ld, int V, int *tok,
+                                                     int *pos) {
+    __shared__ unsigned long long s_best[8];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    pdl_trigger();
+    pdl_wait();
+    const float *row = logits + (size_t)b * ld;
+    unsigned long long best = 0ull;
+    for (int i = tid; i < V; i += 256) {
+        const unsigned long long k = argmax_key(__ldcg(row + i), i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k = __shfl_xor_sync(kFull, best, o);
+        best = k > best ? k : best;
+    }
+    if ((tid & 31) == 0) s_best[tid >> 5] = best;
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < 8; w++) best = s_best[w] > best ? s_best[w] : best;
+        tok[b] = (int)(0xffffffffu - (uint32_t)best);
+        if (pos) pos[b] += 1;
+    }
+}
+
+int launch_argmax_rows(const float *logits, int ld, int B, int V, int *tok, int *pos, cudaStream_t s) {
+    QMS_REQUIRE(B >= 1 && V >= 1 && ld >= V, QMS_CUDA_EINVAL, "argmax_rows: %d rows of %d", B, V);
+    QMS_CK(launch_pdl(k_argmax_rows, dim3(B), dim3(256), 0, s, logits, ld, V, tok, pos));
+    return QMS_CUDA_OK;
 }
 
 int launch_attention(const AttnArgs &a, cudaStream_t s) {

@@ -82,6 +82,10 @@ struct AttnArgs {
     const float *rope_cos, *rope_sin; // [ctx][D/2]
     float *kc, *vc;                   // this layer's cache [ctx][Hk*D]
     const int *pos;                   // device: position of token 0
+    // several sequences (batched decode): token t belongs to sequence t, sits at position pos_vec[t]
+    // and uses the caches at kc / vc + t * seq_stride; NULL: every token of one sequence
+    const int *pos_vec;
+    size_t seq_stride;
     int T, ctx, H, Hk, D;
     double scale;                     // 1/sqrt(D)
     int split;                        // positions per CTA when T == 1 (0: one CTA per head group)
@@ -103,6 +107,9 @@ constexpr int kAttnMaxCtx = 16384;    // longest context the one-token attention
 int launch_qk_rope(const AttnArgs &a, cudaStream_t s);
 // Causal GQA attention with the reference's score order (src/model.c:465-492).
 int launch_attention(const AttnArgs &a, cudaStream_t s);
+// Greedy argmax of each of B rows of logits [B][ld] over V columns (ties: the lower index, as the
+// reference's '>' scan): tok[b] = the winner, pos[b] += 1 when pos is not NULL.
+int launch_argmax_rows(const float *logits, int ld, int B, int V, int *tok, int *pos, cudaStream_t s);
 int attention_heads_per_cta(int group);
 
 }  // namespace qms

@@ -116,6 +116,11 @@ def test_model_calls_validate_arguments():
     assert L.qms_cuda_forward(None, p, 1, 0, p, 0, None) == q.EINVAL
     assert L.qms_cuda_forward_dev(None, p, 1, p, p, 0, None) == q.EINVAL
     assert L.qms_cuda_decode_step(None, p, p, None, None) == q.EINVAL
+    assert L.qms_cuda_forward_seq(None, 0, p, 1, 0, p, 0, None) == q.EINVAL
+    assert L.qms_cuda_forward_batch(None, 1, p, p, p) == q.EINVAL
+    assert L.qms_cuda_decode_batch(None, 1, p, p, None, None) == q.EINVAL
+    assert L.qms_cuda_model_set_sequences(None, 2) == q.EINVAL
+    assert L.qms_cuda_model_copy_sequence(None, 0, 1, 4) == q.EINVAL
     assert L.qms_cuda_model_set_layer(None, 0, None) == q.EINVAL
     assert L.qms_cuda_model_reserve(None, 4) == q.EINVAL
     assert L.qms_cuda_model_status(None) == q.EINVAL

@@ -225,3 +225,95 @@ def test_forward_before_layers_are_set_fails(cuda):
         m.forward([1], 0)
     assert "never set" in str(e.value)
     m.close()
+
+
+def _teacher_forced(m_batch, m_single, prompts, steps):
+    """Sequence b of m_batch and a single-sequence run on m_single see the same tokens (the single
+    run's greedy ids); returns the worst relative L2 between their logits rows and the number of
+    steps whose argmax differs where the single run's top-2 margin is not a near tie."""
+    B = len(prompts)
+    singles = []
+    for p in prompts:                                 # greedy single-sequence runs, host path
+        lg = m_single.forward(p, 0)
+        ids, rows = [int(np.argmax(lg))], [lg]
+        for s in range(steps):
+            lg = m_single.forward([ids[-1]], len(p) + s)
+            rows.append(lg)
+            ids.append(int(np.argmax(lg)))
+        singles.append((ids, rows))
+    worst, flips = 0.0, 0
+    for b, p in enumerate(prompts):
+        lg = m_batch.forward(p, 0, seq=b)
+        worst = max(worst, rel_l2(lg, singles[b][1][0]))
+    for s in range(steps):
+        ids = [singles[b][0][s] for b in range(B)]
+        pos = [len(prompts[b]) + s for b in range(B)]
+        rows = m_batch.forward_batch(ids, pos)
+        for b in range(B):
+            ref = singles[b][1][s + 1]
+            worst = max(worst, rel_l2(rows[b], ref))
+            top = np.sort(_log_softmax(ref))[-2:]
+            if top[1] - top[0] >= NEAR_TIE and int(np.argmax(rows[b])) != int(np.argmax(ref)):
+                flips += 1
+    return worst, flips
+
+
+def test_forward_batch_matches_single_sequences(cuda):
+    """qms_cuda_forward_batch: B sequences at different positions in one pass give, row by row, the
+    logits of qms_cuda_forward_seq on each sequence alone (teacher forcing, config 1 and config 3)."""
+    rng = np.random.default_rng(5)
+    for name, B, steps in (("tiny", 5, 12), ("30b", 3, 6)):
+        cfg = synth.MODEL_CONFIGS[name]
+        prompts = [[int(v) for v in rng.integers(0, cfg.vocab, n)] for n in (7, 19, 3, 40, 11)[:B]]
+        mb = cuda.Model.from_synth(cfg, 1, 128)
+        mb.set_sequences(B)
+        ms = cuda.Model.from_synth(cfg, 1, 128)
+        worst, flips = _teacher_forced(mb, ms, prompts, steps)
+        mb.status()
+        ms.status()
+        mb.close()
+        ms.close()
+        assert worst < LOGIT_TOL, f"{name}: batch rows differ from single-sequence logits by {worst:.2e}"
+        assert flips == 0, f"{name}: {flips} argmax differences outside near ties"
+
+
+def test_decode_batch_graph_matches_reference_ids(cuda):
+    """qms_cuda_decode_batch in a CUDA graph: sequences 0 and 2 hold the golden prompt (sequence 2
+    through qms_cuda_model_copy_sequence), sequence 1 another prompt; 0 and 2 must produce the
+    reference CLI's greedy ids, and sequence 1 must not disturb them."""
+    import torch
+    import make_model_golden as mg
+    g = GOLDEN["tiny"]
+    m = cuda.Model.from_synth(synth.MODEL_CONFIGS["tiny"], g["seed"], g["ctx"])
+    m.set_sequences(3)
+    prompt = mg.prompt_of("tiny")
+    other = [int(v) for v in np.random.default_rng(9).integers(0, 4096, 23)]
+    l0 = m.forward(prompt, 0, seq=0)
+    l1 = m.forward(other, 0, seq=1)
+    m.copy_sequence(0, 2, len(prompt))
+    first = int(np.argmax(l0))
+    tok = torch.tensor([first, int(np.argmax(l1)), first], dtype=torch.int32, device="cuda")
+    pos = torch.tensor([len(prompt), len(other), len(prompt)], dtype=torch.int32, device="cuda")
+    out = [[first], [], [first]]
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        m.decode_batch(tok, pos, stream=s)            # warm-up step outside capture
+        s.synchronize()
+        t = tok.tolist()
+        out[0].append(t[0])
+        out[2].append(t[2])
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            m.decode_batch(tok, pos, stream=s)
+        for _ in range(g["gen"] - 2):
+            graph.replay()
+            s.synchronize()
+            t = tok.tolist()
+            out[0].append(t[0])
+            out[2].append(t[2])
+    m.status()
+    assert prompt + out[0] == g["ids"], "sequence 0 differs from the reference's greedy ids"
+    assert out[2] == out[0], "the copied sequence differs"
+    assert pos.tolist() == [len(prompt) + g["gen"] - 1, len(other) + g["gen"] - 1, len(prompt) + g["gen"] - 1]
+    del graph
+    m.close()

@@ -459,6 +459,10 @@ MODEL_METRIC = "Qwen3-235B-A22B Q4_0 decode tok/s (bs1, whole model on one B200)
 MODEL_PROMPT = 1024
 MODEL_CTX = 4096
 TOKENS_PER_STEP = 32
+BATCH_METRIC = "Qwen3-235B-A22B Q4_0 decode tok/s (bs64: 64 sequences, whole model on one B200)"
+BATCH_SEQS = 64
+BATCH_CTX = MODEL_PROMPT + 128                  # positions per sequence's KV cache
+BATCH_OWN = 128                                 # prompt ids of each sequence's own (after a shared prefix)
 
 
 def model_cfg():
@@ -748,6 +752,167 @@ def run_model(a):
     return 0
 
 
+def batch_bytes_per_step(cfg, B: int, pos: float) -> dict:
+    """Algorithmic bytes of one batched decode step: each expert the step selects once (its expected
+    count for B tokens x top-8 of 128 under uniform routing), router, attention weights, each
+    sequence's KV rows, norms, the head and B embedding rows."""
+    ex = cfg.n_expert * (1.0 - (1.0 - cfg.n_used / cfg.n_expert) ** B)
+    per = model_bytes_per_token(cfg, pos)
+    moe = cfg.n_layer * (ex * 3 * cfg.n_ff * cfg.n_embd * 18 // 32 + cfg.n_expert * cfg.n_embd * 4)
+    d = {"moe": moe, "attention_weights": per["attention_weights"], "kv_cache": B * per["kv_cache"],
+         "norms": per["norms"], "head": per["head"], "embedding_rows": B * per["embedding_row"]}
+    d["total"] = sum(d.values())
+    d["distinct_experts_per_layer"] = ex
+    return d
+
+
+def run_model_batch(a):
+    """--mode model-bs64: B sequences decoded together, one token each per step (qms_cuda_decode_batch
+    in a CUDA graph). Each sequence's 1024-id prompt is a shared 896-id prefix (prefilled once and
+    copied into every sequence's cache) followed by 128 ids of its own (prefilled per sequence), so
+    the sequences' hidden states, and their experts, differ as independent prompts' do."""
+    import torch
+    import large_model_b200 as q
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    q.init(local)
+    dev = torch.device("cuda", local)
+    B = a.batch
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        t94, desc, threads = cpu_model_sample()
+        cpu = {"value": round(1.0 / t94, 4), "unit": "tok/s", "cores": threads, "kind": "reference",
+               "sample": desc + "; the reference serves one sequence at a time (src/model.h:116-118), so B "
+                                "sequences take B x its bs1 time: the same tok/s"}
+    cfg = model_cfg()
+    assert a.steps + a.warmup + 8 < BATCH_CTX - MODEL_PROMPT, "steps beyond the sequences' context"
+    t_build = time.perf_counter()
+    m = device_model(q, torch, cfg, 4242 + rank, dev, BATCH_CTX)
+    m.set_sequences(B)
+    t_build = time.perf_counter() - t_build
+    rng = np.random.default_rng(99 + rank)
+    shared = MODEL_PROMPT - BATCH_OWN
+    prefix = [int(v) for v in rng.integers(0, cfg.vocab, shared)]
+    t_pre = time.perf_counter()
+    m.forward(prefix, 0, seq=0)
+    first = []
+    for b in range(B):
+        if b:
+            m.copy_sequence(0, b, shared)
+        own = [int(v) for v in rng.integers(0, cfg.vocab, BATCH_OWN)]
+        first.append(int(np.argmax(m.forward(own, shared, seq=b))))
+    t_pre = time.perf_counter() - t_pre
+    stream = torch.cuda.Stream(device=dev)
+    tok = torch.tensor(first, dtype=torch.int32, device=dev)
+    pos = torch.full((B,), MODEL_PROMPT, dtype=torch.int32, device=dev)
+    with torch.cuda.stream(stream):
+        m.decode_batch(tok, pos, stream=stream)              # outside capture: first-use setup
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            m.decode_batch(tok, pos, stream=stream)
+        for _ in range(a.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    pos0 = int(pos[0].item())
+    sampler = ClockSampler(local)
+    time.sleep(0.5)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(a.steps):
+            graph.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    pos1 = int(pos[0].item())
+    m.status()
+    distinct = len(set(tok.tolist()))
+    tok_s = B * a.steps * world / (ms / 1e3)
+    # section times of one step (CUDA events between sections, which serialise the overlap)
+    m.profile(True)
+    m.forward_batch(tok.cpu().numpy(), pos.cpu().numpy())
+    sec = m.profile(False)
+    names = ["qkv", "attn", "o_proj", "router", "fetch", "moe", "output"]
+    bt = batch_bytes_per_step(cfg, B, (pos0 + pos1) / 2)
+    step_gbs = bt["total"] * a.steps / (ms / 1e3) / 1e9
+    # end to end through the host-buffer entry point: B ids and positions in, B rows of logits out,
+    # the argmax of each row on the host
+    e2e_n = 3
+    ids = tok.cpu().numpy()
+    p_e = pos.cpu().numpy()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for k in range(e2e_n):
+        lg = m.forward_batch(ids, p_e)
+        ids = lg.argmax(axis=1).astype(np.int32)
+        p_e = p_e + 1
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    peak, peak_kind = peaks()
+    if rank == 0:
+        line = {
+            "metric": BATCH_METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
+            "config": {"workload": f"Qwen3-235B-A22B (config 4) decode, {B} sequences: 94 layers, Q4_0 weights + "
+                                   "Q6_K head drawn on the device (seeded torch RNG), fp32 KV caches of "
+                                   f"{BATCH_CTX} positions each; a {MODEL_PROMPT}-id random prompt prefilled "
+                                   f"once and copied to every sequence, {B} random next tokens; a step = one "
+                                   f"token for each sequence (qms_cuda_decode_batch in one CUDA graph)",
+                       "sequences": B, "positions": [pos0, pos1], "distinct_tokens_last_step": distinct,
+                       "ms_per_token_per_sequence": round(ms / a.steps, 3), "device_gb": round(m.device_bytes / 1e9, 2),
+                       "build_s": round(t_build, 1), "prefill_and_copy_s": round(t_pre, 2),
+                       "section_ms_per_step": {n: round(v, 3) for n, v in zip(names, sec)},
+                       "bytes_per_step": {k: (round(v, 1) if isinstance(v, float) else int(v)) for k, v in bt.items()},
+                       "l2": "inputs far larger than L2 (124 GiB of weights)",
+                       "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "kernel": "whole batched decode step (per layer RMSNorm / QKV / RoPE+KV / "
+                                                   "attention / O / MoE grouped GEMV, head + per-row argmax)",
+                         "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(step_gbs / peak, 4),
+                         "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(B * e2e_n * world / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8 * B,
+                    "d2h_bytes_per_step": B * cfg.vocab * 4,
+                    "note": "qms_cuda_forward_batch per step (host ids and positions in, every sequence's 151936 "
+                            "logits to host memory, argmax per row on the host)"},
+            # per step: embedding; per layer RMSNorm, QKV, RoPE + KV append, attention, Q8 of the
+            # attention output, O, RMSNorm and the 7 kernels of the batched MoE block; head RMSNorm,
+            # head, per-row argmax
+            "gpu_launches": a.steps * (1 + 14 * cfg.n_layer + 3),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    m.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -758,16 +923,19 @@ def main():
     ap.add_argument("--tokens", type=int, default=TOKENS)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--mode", default="model", choices=["model", "moe", "bs64", "prefill"])
+    ap.add_argument("--mode", default="model", choices=["model", "model-bs64", "moe", "bs64", "prefill"])
+    ap.add_argument("--batch", type=int, default=BATCH_SEQS, help="sequences in --mode model-bs64")
     ap.add_argument("--ep", action="store_true", help="batched modes under torchrun: shard the experts over the ranks")
     ap.add_argument("--zipf", type=float, default=0.0,
                     help="batched modes: Zipf(s) expert popularity (config 5: --mode prefill --zipf 1.1)")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":
-        return run_model_reference_arm(a) if a.mode == "model" else run_reference_arm(a)
+        return run_model_reference_arm(a) if a.mode in ("model", "model-bs64") else run_reference_arm(a)
     if a.mode == "model":
         return run_model(a)
+    if a.mode == "model-bs64":
+        return run_model_batch(a)
     if a.mode != "moe":
         return run_batched(a)
 

@@ -58,6 +58,8 @@ struct QmsCudaModel {
     float *rope_cos, *rope_sin;      // [ctx][D/2]
     float *kc, *vc;                  // [n_seq][L][ctx][KD]
     int n_seq;                       // sequences with a KV cache of ctx positions each
+    float *bpart_o;                  // batched one-token attention partials (set_sequences)
+    double *bpart_ml;
     size_t seq_stride;               // floats between two sequences' caches (L * ctx * KD)
     std::vector<DevLayer> layers;
     // forward scratch for cap_T tokens
@@ -224,6 +226,13 @@ static int prof_mark(QmsCudaModel *m, size_t i, cudaStream_t s) {
 
 // One pass over the layers for T <= cap_T tokens. ids, pos: device. logits: device
 // [all ? T : 1][V]. tok != NULL: fused greedy argmax (T == 1) into *tok, and *pos advances.
+// A projection of several tokens' Q8 rows: Q4 weights on the mma.sync kernel, others on the GEMV.
+static int launch_proj(int type, const GemvArgs &g, cudaStream_t s) {
+    if ((type == QMS_T_Q4_0 || type == QMS_T_Q4_1) && g.rows % 16 == 0 && g.x == nullptr)
+        return launch_gemm_q4(type, g, s);
+    return launch_gemv(type, g, s);
+}
+
 // One pass over the layers for T tokens. Single sequence `seq`: tokens at *pos + t. Batch
 // (pos_vec != NULL): token t is sequence t at position pos_vec[t]. tok != NULL: greedy argmax of
 // the head into tok (T == 1 fused into the head; batch per row) and pos_adv += 1.
@@ -320,10 +329,19 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
         g.xq = m->xq;
         g.xd = m->xd;
         g.xs = m->xs;
-        if ((rc = launch_gemv(L.qkv_type, g, s))) return rc;
+        if ((rc = launch_proj(L.qkv_type, g, s))) return rc;
         if ((rc = prof_mark(m, ei++, s))) return rc;
-        if ((rc = launch_qk_rope(at, s))) return rc;
-        if ((rc = launch_attention(at, s))) return rc;
+        if (pos_vec) {                  // one token per sequence: the decode kernels, Q8 rows out
+            AttnArgs ab = at;
+            if (m->bpart_o) {           // else one sequence: the scratch's partials cover it
+                ab.part_o = m->bpart_o;
+                ab.part_ml = m->bpart_ml;
+            }
+            if ((rc = launch_attn_decode(ab, m->xq, m->xd, m->xs, s))) return rc;
+        } else {
+            if ((rc = launch_qk_rope(at, s))) return rc;
+            if ((rc = launch_attention(at, s))) return rc;
+        }
         if ((rc = prof_mark(m, ei++, s))) return rc;
         // O projection + residual (h += O att)
         memset(&g, 0, sizeof g);
@@ -335,11 +353,12 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
         g.y = m->h;
         g.ldy = E;
         g.resid = m->h;
-        if ((rc = launch_rmsnorm(m->att, nullptr, 0.0f, T, m->QD, nullptr, m->xq, m->xd, m->xs, s))) return rc;
+        if (!pos_vec && (rc = launch_rmsnorm(m->att, nullptr, 0.0f, T, m->QD, nullptr, m->xq, m->xd, m->xs, s)))
+            return rc;
         g.xq = m->xq;
         g.xd = m->xd;
         g.xs = m->xs;
-        if ((rc = launch_gemv(L.o_type, g, s))) return rc;
+        if ((rc = launch_proj(L.o_type, g, s))) return rc;
         if ((rc = prof_mark(m, ei++, s))) return rc;
         // MoE block + residual
         if ((rc = launch_rmsnorm(m->h, L.ffn_norm, m->eps, T, E, m->xn, nullptr, nullptr, nullptr, s))) return rc;
@@ -378,6 +397,18 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
         if (tok && pos_vec && (rc = launch_argmax_rows(logits, m->V, T, m->V, tok, pos_adv, s))) return rc;
     }
     if ((rc = prof_mark(m, ei++, s))) return rc;
+    return QMS_CUDA_OK;
+}
+
+// The section timers' events, created when profiling is switched on.
+static int prof_events(QmsCudaModel *m) {
+    if (m->prof && m->ev.size() < (size_t)4 * m->L + 2) {
+        for (size_t i = m->ev.size(); i < (size_t)4 * m->L + 2; i++) {
+            cudaEvent_t e;
+            QMS_CK(cudaEventCreate(&e));
+            m->ev.push_back(e);
+        }
+    }
     return QMS_CUDA_OK;
 }
 
@@ -424,6 +455,8 @@ void qms_cuda_model_free(QmsCudaModel *m) {
     cudaFree(m->scratch);
     if (m->h_pinned) cudaFreeHost(m->h_pinned);
     cudaFree(m->flags);
+    cudaFree(m->bpart_o);
+    cudaFree(m->bpart_ml);
     if (m->h_flags) cudaFreeHost(m->h_flags);
     for (cudaEvent_t e : m->ev) cudaEventDestroy(e);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -676,13 +709,7 @@ int qms_cuda_forward_seq(QmsCudaModel *m, int seq, const int *ids, int T, int po
     if (rc || (rc = layers_ready(m))) return rc;
     if ((rc = model_reserve(m, std::min(T, kChunk)))) return rc;
     const cudaStream_t s = m->stream;
-    if (m->prof && m->ev.size() < (size_t)4 * m->L + 2) {
-        for (size_t i = m->ev.size(); i < (size_t)4 * m->L + 2; i++) {
-            cudaEvent_t e;
-            QMS_CK(cudaEventCreate(&e));
-            m->ev.push_back(e);
-        }
-    }
+    if ((rc = prof_events(m))) return rc;
     for (int c0 = 0; c0 < T; c0 += m->cap_T) {
         const int Tc = std::min(m->cap_T, T - c0);
         const bool last = c0 + Tc == T;
@@ -757,11 +784,30 @@ int qms_cuda_model_set_sequences(QmsCudaModel *m, int n_seq) {
         cudaFree(vc);
         return rc;
     }
+    // the batched attention's partials for up to min(n_seq, 256) sequences, allocated here so
+    // that no batched call allocates (they may be captured in a CUDA graph)
+    const int nb = std::min(n_seq, kChunk), ms = (m->ctx + kAttnBlock - 1) / kAttnBlock;
+    float *po = nullptr;
+    double *pml = nullptr;
+    if (n_seq > 1) {
+        rc = dmalloc((void **)&po, (size_t)nb * m->H * ms * m->D * 4, "batched attention partials");
+        if (!rc) rc = dmalloc((void **)&pml, (size_t)nb * m->H * ms * 16, "batched attention partials");
+        if (rc) {
+            cudaFree(kc);
+            cudaFree(vc);
+            cudaFree(po);
+            return rc;
+        }
+    }
     QMS_CK(cudaDeviceSynchronize());
     cudaFree(m->kc);
     cudaFree(m->vc);
+    cudaFree(m->bpart_o);
+    cudaFree(m->bpart_ml);
     m->kc = kc;
     m->vc = vc;
+    m->bpart_o = po;
+    m->bpart_ml = pml;
     m->n_seq = n_seq;
     return QMS_CUDA_OK;
 }
@@ -795,6 +841,7 @@ int qms_cuda_forward_batch(QmsCudaModel *m, int B, const int *ids, const int *po
     int rc = ensure_dev(m->device);
     if (rc || (rc = layers_ready(m))) return rc;
     const cudaStream_t s = m->stream;
+    if ((rc = prof_events(m))) return rc;
     QMS_CK(cudaStreamSynchronize(s));
     memcpy(m->h_pinned, ids, (size_t)B * 4);
     memcpy(m->h_pinned + B, pos, (size_t)B * 4);
@@ -804,6 +851,7 @@ int qms_cuda_forward_batch(QmsCudaModel *m, int B, const int *ids, const int *po
     QMS_CK(cudaMemcpyAsync(logits, m->logits, (size_t)B * m->V * 4, cudaMemcpyDeviceToHost, s));
     QMS_CK(cudaMemcpyAsync(m->h_flags, m->flags, (size_t)(1 + m->L) * 4, cudaMemcpyDeviceToHost, s));
     QMS_CK(cudaStreamSynchronize(s));
+    if ((rc = prof_collect(m))) return rc;
     return flags_check(m);
 }
 

@@ -492,6 +492,110 @@ int launch_gemv(int type, const GemvArgs &a, cudaStream_t s) {
     }
 }
 
+// ---- multi-token projections on int8 mma.sync ------------------------------------------------------
+// y[t][r] = (resid) + sum_b d_w[r][b] * d_x[t][b] * (sum_k w[r][b][k] * x[t][b][k]) (+ the Q4_1 min
+// term), each 32-block's integer dot exact and scaled in fp32 block by block, as in the one-token
+// kernels (src/kernels.c:82-134). A warp owns 16 rows x 32 tokens: per block one
+// mma.m16n8k32.s8 per 8 tokens (A = the rows' nibbles - 8 for Q4_0, B = the tokens' Q8 bytes),
+// then the int32 results are scaled into fp32 registers. Weights and activations are read straight
+// from global memory (each weight byte once per token tile; activations through L1 / L2).
+template <int Q1>
+__global__ void __launch_bounds__(128) k_gemm_q4(const GemvArgs a) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tg = lane & 3;
+    const int r0 = (blockIdx.x * (blockDim.x >> 5) + warp) * 16, t0 = blockIdx.y * 32;
+    const int nb = a.ncol / 32;
+    pdl_trigger();
+    pdl_wait();
+    if (r0 >= a.rows) return;
+    const uint8_t *wr0 = a.w + (size_t)(r0 + g) * a.stride, *wr1 = wr0 + (size_t)8 * a.stride;
+    const size_t dpl = (size_t)nb * 16, mpl = dpl + pad16((size_t)nb * 2);
+    const int8_t *xr[4];
+    const float *dr[4][2];
+    const int *sr[4][2];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int tb = min(t0 + 8 * j + g, a.T - 1);              // B operand: token tb (clamped rows are not stored)
+        xr[j] = a.xq + (size_t)tb * a.ncol + 4 * tg;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int tt = min(t0 + 8 * j + 2 * tg + h, a.T - 1);  // accumulator column: token tt
+            dr[j][h] = a.xd + (size_t)tt * nb;
+            sr[j][h] = a.xs + (size_t)tt * nb;
+        }
+    }
+    float acc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[j][i] = 0.0f;
+    for (int b = 0; b < nb; b++) {
+        const uint32_t w0 = __ldg(reinterpret_cast<const uint32_t *>(wr0 + (size_t)b * 16 + 4 * tg));
+        const uint32_t w1 = __ldg(reinterpret_cast<const uint32_t *>(wr1 + (size_t)b * 16 + 4 * tg));
+        uint32_t a0 = w0 & 0x0F0F0F0Fu, a2 = (w0 >> 4) & 0x0F0F0F0Fu, a1 = w1 & 0x0F0F0F0Fu, a3 = (w1 >> 4) & 0x0F0F0F0Fu;
+        if (!Q1) {                                                  // q - 8 in [-8, 7], bytewise
+            a0 = __vsub4(a0, 0x08080808u);
+            a1 = __vsub4(a1, 0x08080808u);
+            a2 = __vsub4(a2, 0x08080808u);
+            a3 = __vsub4(a3, 0x08080808u);
+        }
+        const float dw0 = h2f(__ldg(reinterpret_cast<const uint16_t *>(wr0 + dpl) + b));
+        const float dw1 = h2f(__ldg(reinterpret_cast<const uint16_t *>(wr1 + dpl) + b));
+        float mw0 = 0.0f, mw1 = 0.0f;
+        if (Q1) {
+            mw0 = h2f(__ldg(reinterpret_cast<const uint16_t *>(wr0 + mpl) + b));
+            mw1 = h2f(__ldg(reinterpret_cast<const uint16_t *>(wr1 + mpl) + b));
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint32_t b0 = __ldg(reinterpret_cast<const uint32_t *>(xr[j] + (size_t)b * 32));
+            const uint32_t b1 = __ldg(reinterpret_cast<const uint32_t *>(xr[j] + (size_t)b * 32 + 16));
+            int c0, c1, c2, c3;
+            asm volatile(
+                "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%10,%10,%10,%10};"
+                : "=r"(c0), "=r"(c1), "=r"(c2), "=r"(c3)
+                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+            const float dx0 = __ldg(dr[j][0] + b), dx1 = __ldg(dr[j][1] + b);
+            acc[j][0] = __fmaf_rn((float)c0, __fmul_rn(dw0, dx0), acc[j][0]);
+            acc[j][1] = __fmaf_rn((float)c1, __fmul_rn(dw0, dx1), acc[j][1]);
+            acc[j][2] = __fmaf_rn((float)c2, __fmul_rn(dw1, dx0), acc[j][2]);
+            acc[j][3] = __fmaf_rn((float)c3, __fmul_rn(dw1, dx1), acc[j][3]);
+            if (Q1) {
+                const int s0 = __ldg(sr[j][0] + b), s1 = __ldg(sr[j][1] + b);
+                const float f0 = __fmul_rn(dx0, (float)(sum_lo(s0) + sum_hi(s0)));
+                const float f1 = __fmul_rn(dx1, (float)(sum_lo(s1) + sum_hi(s1)));
+                acc[j][0] = __fmaf_rn(mw0, f0, acc[j][0]);
+                acc[j][1] = __fmaf_rn(mw0, f1, acc[j][1]);
+                acc[j][2] = __fmaf_rn(mw1, f0, acc[j][2]);
+                acc[j][3] = __fmaf_rn(mw1, f1, acc[j][3]);
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int t = t0 + 8 * j + 2 * tg + (i & 1), r = r0 + g + 8 * (i >> 1);
+            if (t < a.T) {
+                const size_t at = (size_t)t * a.ldy + r;
+                a.y[at] = a.resid ? __fadd_rn(a.resid[at], acc[j][i]) : acc[j][i];
+            }
+        }
+}
+
+// Multi-token Q4_0 / Q4_1 projection of Q8 rows (xq / xd / xs) on mma.sync; rows a multiple of 16.
+int launch_gemm_q4(int type, const GemvArgs &a, cudaStream_t s) {
+    QMS_REQUIRE((type == QMS_T_Q4_0 || type == QMS_T_Q4_1) && a.x == nullptr && a.xq && a.rows % 16 == 0 &&
+                    a.ncol % 32 == 0 && a.T >= 1 && a.amax == nullptr && a.stride % 4 == 0,
+                QMS_CUDA_EINVAL, "gemm_q4: type %d, %d rows", type, a.rows);
+    const int wpc = a.rows % 64 == 0 ? 4 : 1;                      // warps (16 rows each) per CTA
+    const dim3 grid(a.rows / (16 * wpc), (a.T + 31) / 32);
+    if (type == QMS_T_Q4_0) QMS_CK(launch_pdl(k_gemm_q4<0>, grid, dim3(32 * wpc), 0, s, a));
+    else QMS_CK(launch_pdl(k_gemm_q4<1>, grid, dim3(32 * wpc), 0, s, a));
+    return QMS_CUDA_OK;
+}
+
 // ---- QK-norm, RoPE, KV append ------------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(256) k_qk_rope(const AttnArgs a) {
@@ -1155,15 +1259,17 @@ __global__ void __launch_bounds__(512, 2) k_attn_decode(const AttnArgs a) {
     __shared__ float sk[PB * KP];
     __shared__ __align__(16) float sv[PB * D];
     __shared__ float sq[16 * D];
-    const int group = a.H / a.Hk, g = blockIdx.x, s = blockIdx.y;
+    const int group = a.H / a.Hk, g = blockIdx.x, s = blockIdx.y, z = blockIdx.z;   // z: sequence (batch)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x, nthr = blockDim.x;
     pdl_trigger();
     pdl_wait();
-    const int pos = *a.pos;
+    const int pos = a.pos_vec ? a.pos_vec[z] : *a.pos;
     if (pos < 0 || pos >= a.ctx) {
         if (tid == 0 && s == 0 && g == 0) atomicOr(a.err, 1);
         return;
     }
+    const size_t cb = (size_t)z * a.seq_stride;          // this sequence's caches (0 for one sequence)
+    const float *qkv = a.qkv + (size_t)z * a.ldq;
     const int npos = pos + 1, S = (npos + PB - 1) / PB;
     if (s >= S) return;
     const int p0 = s * PB, p1 = min(npos, p0 + PB), np = p1 - p0;
@@ -1177,12 +1283,12 @@ __global__ void __launch_bounds__(512, 2) k_attn_decode(const AttnArgs a) {
     float qx[J], qw[J], kw[J], kx[J], vx[J], c[JH], sn[JH];
 #pragma unroll
     for (int j = 0; j < J; j++) {
-        qx[j] = __ldcg(a.qkv + (size_t)(g * group + warp) * D + lane + 32 * j);
+        qx[j] = __ldcg(qkv + (size_t)(g * group + warp) * D + lane + 32 * j);
         qw[j] = __ldg(a.q_norm + lane + 32 * j);
         kw[j] = __ldg(a.k_norm + lane + 32 * j);
-        kx[j] = has_new && warp == 0 ? __ldcg(a.qkv + (size_t)a.H * D + (size_t)g * D + lane + 32 * j) : 0.0f;
+        kx[j] = has_new && warp == 0 ? __ldcg(qkv + (size_t)a.H * D + (size_t)g * D + lane + 32 * j) : 0.0f;
         vx[j] = has_new && warp == (group > 1 ? 1 : 0)
-                    ? __ldcg(a.qkv + (size_t)(a.H + a.Hk) * D + (size_t)g * D + lane + 32 * j) : 0.0f;
+                    ? __ldcg(qkv + (size_t)(a.H + a.Hk) * D + (size_t)g * D + lane + 32 * j) : 0.0f;
     }
 #pragma unroll
     for (int j = 0; j < JH; j++) {
@@ -1199,7 +1305,7 @@ __global__ void __launch_bounds__(512, 2) k_attn_decode(const AttnArgs a) {
             const int i = i0 + tid + it * nthr;
             if (i < n4) {
                 const int p = i / (D / 4), d4 = i % (D / 4);
-                const size_t at = (size_t)(p0 + p) * KD + (size_t)g * D + 4 * d4;
+                const size_t at = cb + (size_t)(p0 + p) * KD + (size_t)g * D + 4 * d4;
                 kv[it] = __ldcg(reinterpret_cast<const float4 *>(a.kc + at));
                 vv[it] = __ldcg(reinterpret_cast<const float4 *>(a.vc + at));
             }
@@ -1224,14 +1330,14 @@ __global__ void __launch_bounds__(512, 2) k_attn_decode(const AttnArgs a) {
 #pragma unroll
         for (int j = 0; j < J; j++) {
             sk[(pos - p0) * KP + lane + 32 * j] = kx[j];
-            a.kc[(size_t)pos * KD + (size_t)g * D + lane + 32 * j] = kx[j];
+            a.kc[cb + (size_t)pos * KD + (size_t)g * D + lane + 32 * j] = kx[j];
         }
     }
     if (has_new && warp == (group > 1 ? 1 : 0)) {             // and its V row
 #pragma unroll
         for (int j = 0; j < J; j++) {
             sv[(pos - p0) * D + lane + 32 * j] = vx[j];
-            a.vc[(size_t)pos * KD + (size_t)g * D + lane + 32 * j] = vx[j];
+            a.vc[cb + (size_t)pos * KD + (size_t)g * D + lane + 32 * j] = vx[j];
         }
     }
     __syncthreads();
@@ -1271,7 +1377,7 @@ __global__ void __launch_bounds__(512, 2) k_attn_decode(const AttnArgs a) {
 #pragma unroll
         for (int d = 0; d < DPL; d++) o[d] = __fmaf_rn(w, vp[d], o[d]);
     }
-    const size_t slot = (size_t)h * a.max_splits + s;
+    const size_t slot = ((size_t)z * a.H + h) * a.max_splits + s;
 #pragma unroll
     for (int d = 0; d < DPL; d++) a.part_o[slot * D + lane * DPL + d] = o[d];
     if (lane == 0) {
@@ -1288,13 +1394,13 @@ __global__ void __launch_bounds__(4 * D) k_attn_merge(const AttnArgs a, int8_t *
     __shared__ float f[kAttnMaxCtx / kAttnBlock];
     __shared__ double red[NW];
     __shared__ float part[4][D];
-    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int h = blockIdx.x, z = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_trigger();
     pdl_wait();
-    const int pos = *a.pos;
+    const int pos = a.pos_vec ? a.pos_vec[z] : *a.pos;
     if (pos < 0 || pos >= a.ctx) return;
     const int S = (pos + kAttnBlock) / kAttnBlock;      // <= NT (the launch checks ctx)
-    const size_t base = (size_t)h * a.max_splits;
+    const size_t base = ((size_t)z * a.H + h) * a.max_splits;
     const bool own = tid < S;
     const double mq = own ? __ldcg(a.part_ml + (base + tid) * 2) : -INFINITY;
     const double lq = own ? __ldcg(a.part_ml + (base + tid) * 2 + 1) : 0.0;
@@ -1305,9 +1411,9 @@ __global__ void __launch_bounds__(4 * D) k_attn_merge(const AttnArgs a, int8_t *
     for (int i = 1; i < NW; i++) M = fmax(M, red[i]);
     const double fq = own ? exp(mq - M) : 0.0;
     if (own) f[tid] = (float)fq;
-    double z = warp_sum_d(lq * fq);
+    const double zw = warp_sum_d(lq * fq);
     __syncthreads();
-    if (lane == 0) red[warp] = z;
+    if (lane == 0) red[warp] = zw;
     __syncthreads();
     double Z = 0.0;
     for (int i = 0; i < NW; i++) Z += red[i];
@@ -1331,7 +1437,7 @@ __global__ void __launch_bounds__(4 * D) k_attn_merge(const AttnArgs a, int8_t *
     const float o = __fadd_rn(__fadd_rn(part[0][tid], part[1][tid]), __fadd_rn(part[2][tid], part[3][tid]));
     const float val = (float)((double)o / Z);
     const Q8Lane r = quantize_lane(val);
-    const size_t e = (size_t)h * D + tid;
+    const size_t e = (size_t)z * a.H * D + (size_t)h * D + tid;
     xq[e] = (int8_t)r.q;
     if (lane == 0) {
         xd[e / 32] = r.d;
@@ -1341,16 +1447,16 @@ __global__ void __launch_bounds__(4 * D) k_attn_merge(const AttnArgs a, int8_t *
 
 int launch_attn_decode(const AttnArgs &a, int8_t *xq, float *xd, int *xs, cudaStream_t s) {
     const int group = a.H / a.Hk;
-    QMS_REQUIRE(group <= 16 && a.T == 1 && a.max_splits <= kAttnMaxCtx / kAttnBlock && a.max_splits * kAttnBlock >= a.ctx &&
-                    a.max_splits <= 4 * a.D,
+    QMS_REQUIRE(group <= 16 && (a.T == 1 || a.pos_vec) && a.T <= 65535 && a.max_splits <= kAttnMaxCtx / kAttnBlock &&
+                    a.max_splits * kAttnBlock >= a.ctx && a.max_splits <= 4 * a.D,
                 QMS_CUDA_EUNSUPPORTED, "attn_decode: %d q heads per kv head, ctx %d", group, a.ctx);
-    const dim3 grid(a.Hk, a.max_splits);
+    const dim3 grid(a.Hk, a.max_splits, a.T);
     if (a.D == 128) {
         QMS_CK(launch_pdl(k_attn_decode<128>, grid, dim3(32 * group), 0, s, a));
-        QMS_CK(launch_pdl(k_attn_merge<128>, dim3(a.H), dim3(512), 0, s, a, xq, xd, xs));
+        QMS_CK(launch_pdl(k_attn_merge<128>, dim3(a.H, a.T), dim3(512), 0, s, a, xq, xd, xs));
     } else {
         QMS_CK(launch_pdl(k_attn_decode<64>, grid, dim3(32 * group), 0, s, a));
-        QMS_CK(launch_pdl(k_attn_merge<64>, dim3(a.H), dim3(256), 0, s, a, xq, xd, xs));
+        QMS_CK(launch_pdl(k_attn_merge<64>, dim3(a.H, a.T), dim3(256), 0, s, a, xq, xd, xs));
     }
     return QMS_CUDA_OK;
 }

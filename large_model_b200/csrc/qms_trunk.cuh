@@ -58,6 +58,8 @@ struct GemvArgs {
     int *pos;
 };
 int launch_gemv(int type, const GemvArgs &a, cudaStream_t s);
+// Several tokens (Q8 rows in xq / xd / xs) through Q4_0 / Q4_1 rows on int8 mma.sync; rows % 16 == 0.
+int launch_gemm_q4(int type, const GemvArgs &a, cudaStream_t s);
 
 // One-token projection (decode): a persistent CTA per SM owns a contiguous range of rows and
 // streams it through a ring of TMA bulk copies issued before griddepcontrol.wait. Input: fp32 x
@@ -90,15 +92,16 @@ struct AttnArgs {
     double scale;                     // 1/sqrt(D)
     int split;                        // positions per CTA when T == 1 (0: one CTA per head group)
     int max_splits;
-    float *part_o;                    // [H][max_splits][D]
-    double *part_ml;                  // [H][max_splits][2]
+    float *part_o;                    // one-token attention partials [T][H][max_splits][D]
+    double *part_ml;                  // [T][H][max_splits][2]
     int *ticket;                      // [Hk * head blocks]
     float *out;                       // [T][H*D]
     int *err;
 };
-// One-token attention (decode): CTA (kv head, 32 positions) with QK-norm, RoPE and the K/V append
-// of the new position fused in; partials merged by k_attn_merge, which writes the Q8 rows of the
-// attention output for the O projection (xq / xd / xs as in GemvArgs).
+// One-token attention (decode): CTA (kv head, 32 positions, sequence) with QK-norm, RoPE and the
+// K/V append of the new position fused in; partials merged by k_attn_merge, which writes the Q8
+// rows of the attention output for the O projection (xq / xd / xs as in GemvArgs). T == 1, or a
+// batch (pos_vec): one token for each of T sequences.
 int launch_attn_decode(const AttnArgs &a, int8_t *xq, float *xd, int *xs, cudaStream_t s);
 constexpr int kAttnBlock = 32;        // positions per decode-attention CTA
 constexpr int kAttnMaxCtx = 16384;    // longest context the one-token attention merges

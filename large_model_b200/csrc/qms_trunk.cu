@@ -1251,16 +1251,26 @@ __device__ __forceinline__ void norm_rope_pre(float (&x)[D / 32], const float (&
     }
 }
 
-// CTA (kv head g, block s of kAttnBlock positions), one warp per q head of the group, lane =
-// position. Scores in qms_vec_dot_f32's order: sixteen 8-long FMA chains, then the hsum tree.
-template <int D>
-__global__ void __launch_bounds__(512, 2) k_attn_decode(const AttnArgs a) {
-    constexpr int PB = kAttnBlock, KP = D + 1;           // padded K rows: lanes read distinct banks
-    __shared__ float sk[PB * KP];
-    __shared__ __align__(16) float sv[PB * D];
-    __shared__ float sq[16 * D];
+// 16-byte asynchronous copy global -> shared (L2 only; no register staging).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// CTA (kv head g, block s of kAttnBlock positions, sequence z) with group / HB warps; warp w owns q
+// heads g * group + w * HB .. + HB. Scores: lane = position, each of the block's K rows read once
+// from shared memory (rows padded to D + 4 floats: 16-byte aligned for cp.async, conflict-free
+// float4 reads) for the warp's HB heads, each dot in qms_vec_dot_f32's order (sixteen FMA chains,
+// then the hsum tree). P.V: lane = output dims, each V row read once for the HB heads. Every head's
+// arithmetic is the same as with one warp per head; only the loads are shared.
+template <int D, int HB>
+__global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
+    constexpr int PB = kAttnBlock, KP = D + 4, J = D / 32, JH = J / 2, DPL = D / 32;
+    __shared__ __align__(16) float sk[PB * KP];
+    __shared__ __align__(16) float sv[PB * KP];
+    __shared__ __align__(16) float sq[16 * D];
     const int group = a.H / a.Hk, g = blockIdx.x, s = blockIdx.y, z = blockIdx.z;   // z: sequence (batch)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x, nthr = blockDim.x;
+    const int nwarps = nthr >> 5;
     pdl_trigger();
     pdl_wait();
     const int pos = a.pos_vec ? a.pos_vec[z] : *a.pos;
@@ -1268,64 +1278,46 @@ __global__ void __launch_bounds__(512, 2) k_attn_decode(const AttnArgs a) {
         if (tid == 0 && s == 0 && g == 0) atomicOr(a.err, 1);
         return;
     }
-    const size_t cb = (size_t)z * a.seq_stride;          // this sequence's caches (0 for one sequence)
-    const float *qkv = a.qkv + (size_t)z * a.ldq;
     const int npos = pos + 1, S = (npos + PB - 1) / PB;
     if (s >= S) return;
     const int p0 = s * PB, p1 = min(npos, p0 + PB), np = p1 - p0;
     const int KD = a.Hk * D;
-    constexpr int J = D / 32, JH = J / 2;
+    const size_t cb = (size_t)z * a.seq_stride;          // this sequence's caches (0 for one sequence)
+    const float *qkv = a.qkv + (size_t)z * a.ldq;
     const bool has_new = p1 == npos;
-    const int nc = min(p1, pos) - p0;
-    // every input in one round trip: this warp's q row, the norm weights, the position's cos / sin,
-    // the new position's raw K / V rows, then the block's cached K / V rows
+    const int nc = min(p1, pos) - p0;                    // cached rows (the new one comes from qkv)
+    for (int i = tid; i < nc * (D / 4); i += nthr) {
+        const int p = i / (D / 4), d = 4 * (i % (D / 4));
+        const size_t at = cb + (size_t)(p0 + p) * KD + (size_t)g * D + d;
+        cp_async16(sk + p * KP + d, a.kc + at);
+        cp_async16(sv + p * KP + d, a.vc + at);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    // while the rows land: the group's q heads (QK-norm + NEOX RoPE) and the new position's rows
     const float *cs = a.rope_cos + (size_t)pos * (D / 2), *snp = a.rope_sin + (size_t)pos * (D / 2);
-    float qx[J], qw[J], kw[J], kx[J], vx[J], c[JH], sn[JH];
+    float qw[J], kw[J], c[JH], sn[JH];
 #pragma unroll
     for (int j = 0; j < J; j++) {
-        qx[j] = __ldcg(qkv + (size_t)(g * group + warp) * D + lane + 32 * j);
         qw[j] = __ldg(a.q_norm + lane + 32 * j);
         kw[j] = __ldg(a.k_norm + lane + 32 * j);
-        kx[j] = has_new && warp == 0 ? __ldcg(qkv + (size_t)a.H * D + (size_t)g * D + lane + 32 * j) : 0.0f;
-        vx[j] = has_new && warp == (group > 1 ? 1 : 0)
-                    ? __ldcg(qkv + (size_t)(a.H + a.Hk) * D + (size_t)g * D + lane + 32 * j) : 0.0f;
     }
 #pragma unroll
     for (int j = 0; j < JH; j++) {
         c[j] = __ldg(cs + lane + 32 * j);
         sn[j] = __ldg(snp + lane + 32 * j);
     }
-    {
-        constexpr int kMaxIt = 4;                        // one round for groups of >= 8 q heads
-        const int n4 = nc * (D / 4);
-        float4 kv[kMaxIt], vv[kMaxIt];
-        for (int i0 = 0; i0 < n4; i0 += kMaxIt * nthr) {
+    for (int hh = warp; hh < group; hh += nwarps) {
+        float qx[J];
 #pragma unroll
-        for (int it = 0; it < kMaxIt; it++) {
-            const int i = i0 + tid + it * nthr;
-            if (i < n4) {
-                const int p = i / (D / 4), d4 = i % (D / 4);
-                const size_t at = cb + (size_t)(p0 + p) * KD + (size_t)g * D + 4 * d4;
-                kv[it] = __ldcg(reinterpret_cast<const float4 *>(a.kc + at));
-                vv[it] = __ldcg(reinterpret_cast<const float4 *>(a.vc + at));
-            }
-        }
+        for (int j = 0; j < J; j++) qx[j] = __ldcg(qkv + (size_t)(g * group + hh) * D + lane + 32 * j);
+        norm_rope_pre<D>(qx, qw, c, sn, a.eps);
 #pragma unroll
-        for (int it = 0; it < kMaxIt; it++) {
-            const int i = i0 + tid + it * nthr;
-            if (i < n4) {
-                const int p = i / (D / 4), d = 4 * (i % (D / 4));
-                float *kr = sk + p * KP + d;
-                kr[0] = kv[it].x; kr[1] = kv[it].y; kr[2] = kv[it].z; kr[3] = kv[it].w;
-                *reinterpret_cast<float4 *>(sv + p * D + d) = vv[it];
-            }
-        }
-        }
+        for (int j = 0; j < J; j++) sq[hh * D + lane + 32 * j] = qx[j];
     }
-    norm_rope_pre<D>(qx, qw, c, sn, a.eps);                   // this warp's q head
-#pragma unroll
-    for (int j = 0; j < J; j++) sq[warp * D + lane + 32 * j] = qx[j];
     if (has_new && warp == 0) {                               // the new position's K row, appended
+        float kx[J];
+#pragma unroll
+        for (int j = 0; j < J; j++) kx[j] = __ldcg(qkv + (size_t)a.H * D + (size_t)g * D + lane + 32 * j);
         norm_rope_pre<D>(kx, kw, c, sn, a.eps);
 #pragma unroll
         for (int j = 0; j < J; j++) {
@@ -1333,56 +1325,91 @@ __global__ void __launch_bounds__(512, 2) k_attn_decode(const AttnArgs a) {
             a.kc[cb + (size_t)pos * KD + (size_t)g * D + lane + 32 * j] = kx[j];
         }
     }
-    if (has_new && warp == (group > 1 ? 1 : 0)) {             // and its V row
+    if (has_new && warp == (nwarps > 1 ? 1 : 0)) {            // and its V row
 #pragma unroll
         for (int j = 0; j < J; j++) {
-            sv[(pos - p0) * D + lane + 32 * j] = vx[j];
-            a.vc[cb + (size_t)pos * KD + (size_t)g * D + lane + 32 * j] = vx[j];
+            const float v = __ldcg(qkv + (size_t)(a.H + a.Hk) * D + (size_t)g * D + lane + 32 * j);
+            sv[(pos - p0) * KP + lane + 32 * j] = v;
+            a.vc[cb + (size_t)pos * KD + (size_t)g * D + lane + 32 * j] = v;
         }
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
-    const int h = g * group + warp;
+    const int h0 = warp * HB;                                 // this warp's first head within the group
     const bool valid = lane < np;
-    float dot = 0.0f;
-    if (valid) {
-        float acc[16];
+    double m[HB], l[HB];
+    float fe[HB];
+    {
+        float acc[HB][16];
 #pragma unroll
-        for (int k = 0; k < 16; k++) acc[k] = 0.0f;
-        const float *kr = sk + lane * KP, *qr = sq + warp * D;
+        for (int k = 0; k < HB; k++)
 #pragma unroll
-        for (int i = 0; i < D / 16; i++)
+            for (int c2 = 0; c2 < 16; c2++) acc[k][c2] = 0.0f;
+        if (valid) {
+            const float4 *k4 = reinterpret_cast<const float4 *>(sk + lane * KP);
 #pragma unroll
-            for (int k = 0; k < 16; k++) acc[k] = __fmaf_rn(qr[16 * i + k], kr[16 * i + k], acc[k]);
-        float t[8];
+            for (int i = 0; i < D / 16; i++)
 #pragma unroll
-        for (int k = 0; k < 8; k++) t[k] = __fadd_rn(acc[k], acc[k + 8]);
+                for (int j = 0; j < 4; j++) {
+                    const float4 kv = k4[4 * i + j];
 #pragma unroll
-        for (int k = 0; k < 4; k++) t[k] = __fadd_rn(t[k], t[k + 4]);
-        t[0] = __fadd_rn(t[0], t[2]);
-        t[1] = __fadd_rn(t[1], t[3]);
-        dot = __fadd_rn(t[0], t[1]);
+                    for (int k = 0; k < HB; k++) {
+                        const float4 qv = reinterpret_cast<const float4 *>(sq + (h0 + k) * D)[4 * i + j];
+                        acc[k][4 * j + 0] = __fmaf_rn(qv.x, kv.x, acc[k][4 * j + 0]);
+                        acc[k][4 * j + 1] = __fmaf_rn(qv.y, kv.y, acc[k][4 * j + 1]);
+                        acc[k][4 * j + 2] = __fmaf_rn(qv.z, kv.z, acc[k][4 * j + 2]);
+                        acc[k][4 * j + 3] = __fmaf_rn(qv.w, kv.w, acc[k][4 * j + 3]);
+                    }
+                }
+        }
+#pragma unroll
+        for (int k = 0; k < HB; k++) {
+            float t[8];
+#pragma unroll
+            for (int c2 = 0; c2 < 8; c2++) t[c2] = __fadd_rn(acc[k][c2], acc[k][c2 + 8]);
+#pragma unroll
+            for (int c2 = 0; c2 < 4; c2++) t[c2] = __fadd_rn(t[c2], t[c2 + 4]);
+            t[0] = __fadd_rn(t[0], t[2]);
+            t[1] = __fadd_rn(t[1], t[3]);
+            const double sc = valid ? (double)__fadd_rn(t[0], t[1]) * a.scale : -INFINITY;
+            m[k] = warp_max_d(sc);
+            const double e = valid ? exp(sc - m[k]) : 0.0;
+            l[k] = warp_sum_d(e);
+            fe[k] = (float)e;
+        }
     }
-    const double sc = valid ? (double)dot * a.scale : -INFINITY;
-    const double m = warp_max_d(sc);
-    const double e = valid ? exp(sc - m) : 0.0;
-    const double l = warp_sum_d(e);
-    const float fe = (float)e;
-    constexpr int DPL = D / 32;
-    float o[DPL];
+    float o[HB][DPL];
 #pragma unroll
-    for (int d = 0; d < DPL; d++) o[d] = 0.0f;
+    for (int k = 0; k < HB; k++)
+#pragma unroll
+        for (int d = 0; d < DPL; d++) o[k][d] = 0.0f;
     for (int q = 0; q < np; q++) {
-        const float w = __shfl_sync(0xffffffffu, fe, q);
-        const float *vp = sv + q * D + lane * DPL;
+        const float *vp = sv + q * KP + lane * DPL;
+        float v[DPL];
+        if constexpr (DPL == 4) {
+            const float4 t4 = *reinterpret_cast<const float4 *>(vp);
+            v[0] = t4.x; v[1] = t4.y; v[2] = t4.z; v[3] = t4.w;
+        } else {
+            const float2 t2 = *reinterpret_cast<const float2 *>(vp);
+            v[0] = t2.x; v[1] = t2.y;
+        }
 #pragma unroll
-        for (int d = 0; d < DPL; d++) o[d] = __fmaf_rn(w, vp[d], o[d]);
+        for (int k = 0; k < HB; k++) {
+            const float w = __shfl_sync(0xffffffffu, fe[k], q);
+#pragma unroll
+            for (int d = 0; d < DPL; d++) o[k][d] = __fmaf_rn(w, v[d], o[k][d]);
+        }
     }
-    const size_t slot = ((size_t)z * a.H + h) * a.max_splits + s;
 #pragma unroll
-    for (int d = 0; d < DPL; d++) a.part_o[slot * D + lane * DPL + d] = o[d];
-    if (lane == 0) {
-        a.part_ml[slot * 2] = m;
-        a.part_ml[slot * 2 + 1] = l;
+    for (int k = 0; k < HB; k++) {
+        const int h = g * group + h0 + k;
+        const size_t slot = ((size_t)z * a.H + h) * a.max_splits + s;
+#pragma unroll
+        for (int d = 0; d < DPL; d++) a.part_o[slot * D + lane * DPL + d] = o[k][d];
+        if (lane == 0) {
+            a.part_ml[slot * 2] = m[k];
+            a.part_ml[slot * 2 + 1] = l[k];
+        }
     }
 }
 
@@ -1450,12 +1477,21 @@ int launch_attn_decode(const AttnArgs &a, int8_t *xq, float *xd, int *xs, cudaSt
     QMS_REQUIRE(group <= 16 && (a.T == 1 || a.pos_vec) && a.T <= 65535 && a.max_splits <= kAttnMaxCtx / kAttnBlock &&
                     a.max_splits * kAttnBlock >= a.ctx && a.max_splits <= 4 * a.D,
                 QMS_CUDA_EUNSUPPORTED, "attn_decode: %d q heads per kv head, ctx %d", group, a.ctx);
-    const dim3 grid(a.Hk, a.max_splits, a.T);
+    // heads per warp: 2 for one sequence (more warps shorten the latency-bound chain: 13.8 / 16.7 us
+    // per 235B layer at positions 1024 / 2900 against 16.1 / 18.2 with 4), 4 for a batch (shared-
+    // memory traffic bounds the throughput)
+    const int hmax = a.pos_vec ? 4 : 2, hb = group < hmax ? group : hmax;
+    QMS_REQUIRE(group % hb == 0, QMS_CUDA_EUNSUPPORTED, "attn_decode: %d q heads per kv head", group);
+    const dim3 grid(a.Hk, a.max_splits, a.T), block(32 * (group / hb));
     if (a.D == 128) {
-        QMS_CK(launch_pdl(k_attn_decode<128>, grid, dim3(32 * group), 0, s, a));
+        if (hb == 4) QMS_CK(launch_pdl(k_attn_decode<128, 4>, grid, block, 0, s, a));
+        else if (hb == 2) QMS_CK(launch_pdl(k_attn_decode<128, 2>, grid, block, 0, s, a));
+        else QMS_CK(launch_pdl(k_attn_decode<128, 1>, grid, block, 0, s, a));
         QMS_CK(launch_pdl(k_attn_merge<128>, dim3(a.H, a.T), dim3(512), 0, s, a, xq, xd, xs));
     } else {
-        QMS_CK(launch_pdl(k_attn_decode<64>, grid, dim3(32 * group), 0, s, a));
+        if (hb == 4) QMS_CK(launch_pdl(k_attn_decode<64, 4>, grid, block, 0, s, a));
+        else if (hb == 2) QMS_CK(launch_pdl(k_attn_decode<64, 2>, grid, block, 0, s, a));
+        else QMS_CK(launch_pdl(k_attn_decode<64, 1>, grid, block, 0, s, a));
         QMS_CK(launch_pdl(k_attn_merge<64>, dim3(a.H, a.T), dim3(256), 0, s, a, xq, xd, xs));
     }
     return QMS_CUDA_OK;

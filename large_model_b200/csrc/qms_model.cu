@@ -226,10 +226,10 @@ static int prof_mark(QmsCudaModel *m, size_t i, cudaStream_t s) {
 
 // One pass over the layers for T <= cap_T tokens. ids, pos: device. logits: device
 // [all ? T : 1][V]. tok != NULL: fused greedy argmax (T == 1) into *tok, and *pos advances.
-// A projection of several tokens' Q8 rows: Q4 weights on the mma.sync kernel, others on the GEMV.
+// A projection of several tokens' Q8 rows: Q4 / Q6_K weights on the mma.sync kernels, others on the GEMV.
 static int launch_proj(int type, const GemvArgs &g, cudaStream_t s) {
-    if ((type == QMS_T_Q4_0 || type == QMS_T_Q4_1) && g.rows % 16 == 0 && g.x == nullptr)
-        return launch_gemm_q4(type, g, s);
+    const bool q4 = type == QMS_T_Q4_0 || type == QMS_T_Q4_1, q6 = type == QMS_T_Q6_K && g.ncol % 256 == 0;
+    if ((q4 || q6) && g.rows % 16 == 0 && g.x == nullptr && g.amax == nullptr) return launch_gemm_q(type, g, s);
     return launch_gemv(type, g, s);
 }
 
@@ -393,7 +393,7 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
         g.xq = m->xq;
         g.xd = m->xd;
         g.xs = m->xs;
-        if ((rc = launch_gemv(m->head_type, g, s))) return rc;
+        if ((rc = launch_proj(m->head_type, g, s))) return rc;
         if (tok && pos_vec && (rc = launch_argmax_rows(logits, m->V, T, m->V, tok, pos_adv, s))) return rc;
     }
     if ((rc = prof_mark(m, ei++, s))) return rc;

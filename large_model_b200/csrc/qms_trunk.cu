@@ -584,15 +584,115 @@ __global__ void __launch_bounds__(128) k_gemm_q4(const GemvArgs a) {
         }
 }
 
-// Multi-token Q4_0 / Q4_1 projection of Q8 rows (xq / xd / xs) on mma.sync; rows a multiple of 16.
-int launch_gemm_q4(int type, const GemvArgs &a, cudaStream_t s) {
-    QMS_REQUIRE((type == QMS_T_Q4_0 || type == QMS_T_Q4_1) && a.x == nullptr && a.xq && a.rows % 16 == 0 &&
-                    a.ncol % 32 == 0 && a.T >= 1 && a.amax == nullptr && a.stride % 4 == 0,
-                QMS_CUDA_EINVAL, "gemm_q4: type %d, %d rows", type, a.rows);
+// Q6_K rows (the head) on int8 mma.sync, several tokens. A 256-value super-block holds 16
+// sub-blocks of 16 with int8 scales; a 32-value Q8 activation block covers two of them, so each
+// block takes two m16n8k16 products (A = q6 - 32, exact int32), combined as sa * c_lo + sb * c_hi in
+// integers and scaled by d6 * d_x in fp32: the arithmetic of the one-token head kernel
+// (src/kernels.c:139-195). Element layout of a super-block (ggml): half n = e / 128; within it
+// quarter qq = (e % 128) / 32 and l = e % 32; low 4 bits in ql[64 n + 32 (qq & 1) + l] at shift
+// 4 (qq >> 1), high 2 bits in qh[32 n + l] at shift 2 qq; scale sc[8 n + 2 qq + l / 16].
+__global__ void __launch_bounds__(128) k_gemm_q6k(const GemvArgs a) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tg = lane & 3;
+    const int r0 = (blockIdx.x * (blockDim.x >> 5) + warp) * 16, t0 = blockIdx.y * 32;
+    const int nsb = a.ncol / 256, nb = a.ncol / 32;
+    pdl_trigger();
+    pdl_wait();
+    if (r0 >= a.rows) return;
+    const uint8_t *wr[2] = {a.w + (size_t)(r0 + g) * a.stride, a.w + (size_t)(r0 + g + 8) * a.stride};
+    const int8_t *xr[4];
+    const float *dr[4][2];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        xr[j] = a.xq + (size_t)min(t0 + 8 * j + g, a.T - 1) * a.ncol + 4 * tg;
+#pragma unroll
+        for (int h = 0; h < 2; h++) dr[j][h] = a.xd + (size_t)min(t0 + 8 * j + 2 * tg + h, a.T - 1) * nb;
+    }
+    float acc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[j][i] = 0.0f;
+    for (int sb = 0; sb < nsb; sb++) {
+        uint32_t ql[2][2][2][2], qh[2][2][2];     // [row][half n][ql: qq & 1 / -][k0 / 16]
+        int8_t sc[2][16];
+        float d6[2];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const uint8_t *body = wr[r] + (size_t)sb * 208;
+#pragma unroll
+            for (int n = 0; n < 2; n++)
+#pragma unroll
+                for (int k = 0; k < 2; k++) {
+                    ql[r][n][0][k] = __ldg(reinterpret_cast<const uint32_t *>(body + 64 * n + 16 * k + 4 * tg));
+                    ql[r][n][1][k] = __ldg(reinterpret_cast<const uint32_t *>(body + 64 * n + 32 + 16 * k + 4 * tg));
+                    qh[r][n][k] = __ldg(reinterpret_cast<const uint32_t *>(body + 128 + 32 * n + 16 * k + 4 * tg));
+                }
+            const uint4 s4 = __ldg(reinterpret_cast<const uint4 *>(body + 192));
+            const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int i = 0; i < 16; i++) sc[r][i] = (int8_t)(sw[i >> 2] >> (8 * (i & 3)));
+            d6[r] = h2f(__ldg(reinterpret_cast<const uint16_t *>(wr[r] + (size_t)nsb * 208) + sb));
+        }
+#pragma unroll
+        for (int n = 0; n < 2; n++)
+#pragma unroll
+            for (int qq = 0; qq < 4; qq++) {
+                const int bq = sb * 8 + 4 * n + qq;          // the Q8 block of these 32 values
+                uint32_t A[2][2];                            // [k0 / 16][row]
+#pragma unroll
+                for (int k = 0; k < 2; k++)
+#pragma unroll
+                    for (int r = 0; r < 2; r++) {
+                        const uint32_t lw = ql[r][n][qq & 1][k];
+                        const uint32_t q6 = ((lw >> (4 * (qq >> 1))) & 0x0F0F0F0Fu) | (((qh[r][n][k] >> (2 * qq)) & 0x03030303u) << 4);
+                        A[k][r] = __vsub4(q6, 0x20202020u);
+                    }
+                const int sa0 = sc[0][8 * n + 2 * qq], sb0 = sc[0][8 * n + 2 * qq + 1];
+                const int sa1 = sc[1][8 * n + 2 * qq], sb1 = sc[1][8 * n + 2 * qq + 1];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    int c[2][4];
+#pragma unroll
+                    for (int k = 0; k < 2; k++) {
+                        const uint32_t b0 = __ldg(reinterpret_cast<const uint32_t *>(xr[j] + (size_t)bq * 32 + 16 * k));
+                        asm volatile(
+                            "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
+                            "{%7,%7,%7,%7};"
+                            : "=r"(c[k][0]), "=r"(c[k][1]), "=r"(c[k][2]), "=r"(c[k][3])
+                            : "r"(A[k][0]), "r"(A[k][1]), "r"(b0), "r"(0));
+                    }
+                    const float dx0 = __ldg(dr[j][0] + bq), dx1 = __ldg(dr[j][1] + bq);
+                    acc[j][0] = __fmaf_rn((float)(sa0 * c[0][0] + sb0 * c[1][0]), __fmul_rn(d6[0], dx0), acc[j][0]);
+                    acc[j][1] = __fmaf_rn((float)(sa0 * c[0][1] + sb0 * c[1][1]), __fmul_rn(d6[0], dx1), acc[j][1]);
+                    acc[j][2] = __fmaf_rn((float)(sa1 * c[0][2] + sb1 * c[1][2]), __fmul_rn(d6[1], dx0), acc[j][2]);
+                    acc[j][3] = __fmaf_rn((float)(sa1 * c[0][3] + sb1 * c[1][3]), __fmul_rn(d6[1], dx1), acc[j][3]);
+                }
+            }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int t = t0 + 8 * j + 2 * tg + (i & 1), r = r0 + g + 8 * (i >> 1);
+            if (t < a.T) {
+                const size_t at = (size_t)t * a.ldy + r;
+                a.y[at] = a.resid ? __fadd_rn(a.resid[at], acc[j][i]) : acc[j][i];
+            }
+        }
+}
+
+// Multi-token projection of Q8 rows (xq / xd / xs) on mma.sync: Q4_0 / Q4_1 / Q6_K rows, a multiple of 16.
+int launch_gemm_q(int type, const GemvArgs &a, cudaStream_t s) {
+    QMS_REQUIRE((type == QMS_T_Q4_0 || type == QMS_T_Q4_1 || type == QMS_T_Q6_K) && a.x == nullptr && a.xq &&
+                    a.rows % 16 == 0 && a.ncol % (type == QMS_T_Q6_K ? 256 : 32) == 0 && a.T >= 1 &&
+                    a.amax == nullptr && a.stride % 16 == 0,
+                QMS_CUDA_EINVAL, "gemm_q: type %d, %d rows of %d", type, a.rows, a.ncol);
     const int wpc = a.rows % 64 == 0 ? 4 : 1;                      // warps (16 rows each) per CTA
     const dim3 grid(a.rows / (16 * wpc), (a.T + 31) / 32);
     if (type == QMS_T_Q4_0) QMS_CK(launch_pdl(k_gemm_q4<0>, grid, dim3(32 * wpc), 0, s, a));
-    else QMS_CK(launch_pdl(k_gemm_q4<1>, grid, dim3(32 * wpc), 0, s, a));
+    else if (type == QMS_T_Q4_1) QMS_CK(launch_pdl(k_gemm_q4<1>, grid, dim3(32 * wpc), 0, s, a));
+    else QMS_CK(launch_pdl(k_gemm_q6k, grid, dim3(32 * wpc), 0, s, a));
     return QMS_CUDA_OK;
 }
 

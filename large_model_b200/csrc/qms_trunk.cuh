@@ -58,8 +58,9 @@ struct GemvArgs {
     int *pos;
 };
 int launch_gemv(int type, const GemvArgs &a, cudaStream_t s);
-// Several tokens (Q8 rows in xq / xd / xs) through Q4_0 / Q4_1 rows on int8 mma.sync; rows % 16 == 0.
-int launch_gemm_q4(int type, const GemvArgs &a, cudaStream_t s);
+// Several tokens (Q8 rows in xq / xd / xs) through Q4_0 / Q4_1 / Q6_K rows on int8 mma.sync;
+// rows % 16 == 0.
+int launch_gemm_q(int type, const GemvArgs &a, cudaStream_t s);
 
 // One-token projection (decode): a persistent CTA per SM owns a contiguous range of rows and
 // streams it through a ring of TMA bulk copies issued before griddepcontrol.wait. Input: fp32 x

@@ -470,7 +470,7 @@ def model_cfg():
     return synth.MODEL_CONFIGS["235b"]
 
 
-def model_bytes_per_token(cfg, pos: float) -> dict:
+def model_bytes_per_token(cfg, pos: float, kv_es: int = 4) -> dict:
     """Algorithmic bytes one decode token at position `pos` must read, by part (GGUF sizes):
     per layer the router and 8 experts, the q/k/v/o projections, the fp32 K and V rows of every
     earlier position, the norms; plus the embedding row and the Q6_K head."""
@@ -478,7 +478,7 @@ def model_bytes_per_token(cfg, pos: float) -> dict:
     QD, KD = cfg.n_head * cfg.head_dim, cfg.n_head_kv * cfg.head_dim
     moe = K * 3 * F * (E // 32) * 18 + X * E * 4
     attn = (QD + 2 * KD) * (E // 32) * 18 + E * (QD // 32) * 18
-    kv = 2 * KD * 4 * (pos + 1)
+    kv = 2 * KD * kv_es * (pos + 1)
     norms = (2 * E + 2 * cfg.head_dim) * 4
     head = cfg.vocab * (E // 256) * 210
     parts = {"moe": L * moe, "attention_weights": L * attn, "kv_cache": L * kv, "norms": L * norms + E * 4,
@@ -624,6 +624,8 @@ def run_model(a):
     cfg = model_cfg()
     t_build = time.perf_counter()
     m = device_model(q, torch, cfg, 4242 + rank, dev, MODEL_CTX)
+    if a.kv == "f16":
+        m.set_kv_type(q.T_F16)
     t_build = time.perf_counter() - t_build
     rng = np.random.default_rng(99 + rank)
     prompt = [int(v) for v in rng.integers(0, cfg.vocab, MODEL_PROMPT)]
@@ -674,7 +676,7 @@ def run_model(a):
     m.status()
     ntok = a.steps * per_step
     tok_s = ntok * world / (ms / 1e3)
-    bt = model_bytes_per_token(cfg, (pos0 + pos1) / 2)
+    bt = model_bytes_per_token(cfg, (pos0 + pos1) / 2, 2 if a.kv == "f16" else 4)
     step_gbs = bt["total"] * ntok / (ms / 1e3) / 1e9
     # section times per token (CUDA events around each section of a token step; they serialise the
     # programmatic overlap between kernels, so their sum is a little above the graph's time per token)
@@ -716,6 +718,7 @@ def run_model(a):
                                    f"{MODEL_PROMPT}-id random prompt prefilled; a step = {per_step} greedy "
                                    f"decode tokens (qms_cuda_decode_step x{per_step} in one CUDA graph)",
                        "tokens_per_step": per_step, "positions": [pos0, pos1],
+                       "kv_cache": "fp16 (compacted)" if a.kv == "f16" else "fp32 (the reference's)",
                        "ms_per_token": round(ms / ntok, 4), "device_gb": round(m.device_bytes / 1e9, 2),
                        "build_s": round(t_build, 1), "prefill_s": round(t_pre, 2),
                        "bytes_per_token": {k: int(v) for k, v in bt.items()},
@@ -752,12 +755,12 @@ def run_model(a):
     return 0
 
 
-def batch_bytes_per_step(cfg, B: int, pos: float) -> dict:
+def batch_bytes_per_step(cfg, B: int, pos: float, kv_es: int = 4) -> dict:
     """Algorithmic bytes of one batched decode step: each expert the step selects once (its expected
     count for B tokens x top-8 of 128 under uniform routing), router, attention weights, each
     sequence's KV rows, norms, the head and B embedding rows."""
     ex = cfg.n_expert * (1.0 - (1.0 - cfg.n_used / cfg.n_expert) ** B)
-    per = model_bytes_per_token(cfg, pos)
+    per = model_bytes_per_token(cfg, pos, kv_es)
     moe = cfg.n_layer * (ex * 3 * cfg.n_ff * cfg.n_embd * 18 // 32 + cfg.n_expert * cfg.n_embd * 4)
     d = {"moe": moe, "attention_weights": per["attention_weights"], "kv_cache": B * per["kv_cache"],
          "norms": per["norms"], "head": per["head"], "embedding_rows": B * per["embedding_row"]}
@@ -797,6 +800,8 @@ def run_model_batch(a):
     assert a.steps + a.warmup + 8 < BATCH_CTX - MODEL_PROMPT, "steps beyond the sequences' context"
     t_build = time.perf_counter()
     m = device_model(q, torch, cfg, 4242 + rank, dev, BATCH_CTX)
+    if a.kv == "f16":
+        m.set_kv_type(q.T_F16)
     m.set_sequences(B)
     t_build = time.perf_counter() - t_build
     rng = np.random.default_rng(99 + rank)
@@ -851,7 +856,7 @@ def run_model_batch(a):
     m.forward_batch(tok.cpu().numpy(), pos.cpu().numpy())
     sec = m.profile(False)
     names = ["qkv", "attn", "o_proj", "router", "fetch", "moe", "output"]
-    bt = batch_bytes_per_step(cfg, B, (pos0 + pos1) / 2)
+    bt = batch_bytes_per_step(cfg, B, (pos0 + pos1) / 2, 2 if a.kv == "f16" else 4)
     step_gbs = bt["total"] * a.steps / (ms / 1e3) / 1e9
     # end to end through the host-buffer entry point: B ids and positions in, B rows of logits out,
     # the argmax of each row on the host
@@ -882,6 +887,7 @@ def run_model_batch(a):
                                    f"once and copied to every sequence, {B} random next tokens; a step = one "
                                    f"token for each sequence (qms_cuda_decode_batch in one CUDA graph)",
                        "sequences": B, "positions": [pos0, pos1], "distinct_tokens_last_step": distinct,
+                       "kv_cache": "fp16 (compacted)" if a.kv == "f16" else "fp32 (the reference's)",
                        "ms_per_token_per_sequence": round(ms / a.steps, 3), "device_gb": round(m.device_bytes / 1e9, 2),
                        "build_s": round(t_build, 1), "prefill_and_copy_s": round(t_pre, 2),
                        "section_ms_per_step": {n: round(v, 3) for n, v in zip(names, sec)},
@@ -925,6 +931,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--mode", default="model", choices=["model", "model-bs64", "moe", "bs64", "prefill"])
     ap.add_argument("--batch", type=int, default=BATCH_SEQS, help="sequences in --mode model-bs64")
+    ap.add_argument("--kv", default="f32", choices=["f32", "f16"],
+                    help="model modes: KV cache elements (f16: the compacted cache, not the reference's arithmetic)")
     ap.add_argument("--ep", action="store_true", help="batched modes under torchrun: shard the experts over the ranks")
     ap.add_argument("--zipf", type=float, default=0.0,
                     help="batched modes: Zipf(s) expert popularity (config 5: --mode prefill --zipf 1.1)")

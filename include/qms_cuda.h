@@ -246,6 +246,11 @@ int qms_cuda_decode_step(QmsCudaModel *m, int *tok, int *pos, float *logits, voi
  * uses); n_seq * n_layer * ctx * 4 KB of device memory for 235B-shape layers. No other call may
  * be running, and CUDA graphs captured before no longer apply. */
 int qms_cuda_model_set_sequences(QmsCudaModel *m, int n_seq);
+/* The KV caches' element type: QMS_T_F32 (default: the reference's fp32 cache, src/model.c:459-460)
+ * or QMS_T_F16 (compacted: half the memory and the attention's cache traffic; each K / V value is
+ * rounded to fp16 once when appended, so results depart from the reference's by that rounding).
+ * Reallocates and clears every sequence's cache, like set_sequences. */
+int qms_cuda_model_set_kv_type(QmsCudaModel *m, int kv_type);
 /* Copy positions [0, npos) of sequence src's cache to sequence dst (a shared prompt prefix). */
 int qms_cuda_model_copy_sequence(QmsCudaModel *m, int src, int dst, int npos);
 /* qms_cuda_forward on sequence seq's cache (qms_cuda_forward is seq 0). */

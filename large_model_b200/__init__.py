@@ -103,6 +103,7 @@ def lib() -> C.CDLL:
     L.qms_cuda_decode_step.argtypes = [vp, vp, vp, vp, vp]
     L.qms_cuda_model_set_sequences.argtypes = [vp, i32]
     L.qms_cuda_model_copy_sequence.argtypes = [vp, i32, i32, i32]
+    L.qms_cuda_model_set_kv_type.argtypes = [vp, i32]
     L.qms_cuda_forward_seq.argtypes = [vp, i32, vp, i32, i32, vp, i32, vp]
     L.qms_cuda_forward_batch.argtypes = [vp, i32, vp, vp, vp]
     L.qms_cuda_decode_batch.argtypes = [vp, i32, vp, vp, vp, vp]
@@ -445,6 +446,10 @@ class Model:
     def set_sequences(self, n_seq: int):
         """KV caches for n_seq sequences (qms_cuda_model_set_sequences; caches cleared)."""
         check(lib().qms_cuda_model_set_sequences(self.h, int(n_seq)))
+
+    def set_kv_type(self, kv_type: int):
+        """KV cache elements: T_F32 (the reference's) or T_F16 (compacted); caches cleared."""
+        check(lib().qms_cuda_model_set_kv_type(self.h, int(kv_type)))
 
     def copy_sequence(self, src: int, dst: int, npos: int):
         check(lib().qms_cuda_model_copy_sequence(self.h, int(src), int(dst), int(npos)))

@@ -56,7 +56,9 @@ struct QmsCudaModel {
     int head_type;
     uint8_t *head;                   // repacked rows
     float *rope_cos, *rope_sin;      // [ctx][D/2]
-    float *kc, *vc;                  // [n_seq][L][ctx][KD]
+    void *kc, *vc;                   // [n_seq][L][ctx][KD] elements of kv_es bytes
+    int kv_type;                     // QMS_T_F32 (the reference's cache) or QMS_T_F16 (compacted)
+    size_t kv_es;
     int n_seq;                       // sequences with a KV cache of ctx positions each
     float *bpart_o;                  // batched one-token attention partials (set_sequences)
     double *bpart_ml;
@@ -270,8 +272,10 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
         const DevLayer &L = m->layers[l];
         at.q_norm = L.q_norm;
         at.k_norm = L.k_norm;
-        at.kc = m->kc + (size_t)seq * m->seq_stride + (size_t)l * m->ctx * m->KD;
-        at.vc = m->vc + (size_t)seq * m->seq_stride + (size_t)l * m->ctx * m->KD;
+        const size_t kvo = m->kv_es * ((size_t)seq * m->seq_stride + (size_t)l * m->ctx * m->KD);
+        at.kc = static_cast<char *>(m->kc) + kvo;
+        at.vc = static_cast<char *>(m->vc) + kvo;
+        at.kv16 = m->kv_type == QMS_T_F16;
         int *sel_l = sel ? sel + (size_t)l * T * m->K : nullptr;
         GemvArgs g;
         memset(&g, 0, sizeof g);
@@ -524,6 +528,8 @@ int qms_cuda_model_create(const QmsCudaModelDesc *d, QmsCudaModel **out) {
     int rc = QMS_CUDA_OK;
     const size_t erb = ggml_row_bytes(et, m->E);
     m->n_seq = 1;
+    m->kv_type = QMS_T_F32;
+    m->kv_es = 4;
     m->seq_stride = (size_t)m->L * m->ctx * m->KD;
     const size_t kv = (size_t)m->L * m->ctx * m->KD * 4;
     const size_t rope = (size_t)m->ctx * (m->D / 2) * 4;
@@ -658,7 +664,7 @@ int qms_cuda_model_set_layer(QmsCudaModel *m, int l, const QmsCudaLayerDesc *ld)
 int64_t qms_cuda_model_device_bytes(const QmsCudaModel *m) {
     if (!m) return 0;
     int64_t b = (int64_t)m->weight_bytes + (int64_t)m->scratch_bytes;
-    b += (int64_t)2 * m->n_seq * m->L * m->ctx * m->KD * 4 + (int64_t)2 * m->ctx * (m->D / 2) * 4;
+    b += (int64_t)2 * m->n_seq * m->seq_stride * m->kv_es + (int64_t)2 * m->ctx * (m->D / 2) * 4;
     for (const auto &L : m->layers) {
         if (!L.set) continue;
         b += (int64_t)((2 * m->E + 2 * m->D) * 4) + (int64_t)m->NQKV * rows_stride(L.qkv_type, m->E) +
@@ -765,39 +771,31 @@ static int flags_check(QmsCudaModel *m) {
     return QMS_CUDA_ETIMEOUT;
 }
 
-int qms_cuda_model_set_sequences(QmsCudaModel *m, int n_seq) {
-    clear_error();
-    QMS_REQUIRE(m && n_seq >= 1, QMS_CUDA_EINVAL, "set_sequences: bad arguments");
-    int rc = ensure_dev(m->device);
-    if (rc) return rc;
-    if (n_seq == m->n_seq) return QMS_CUDA_OK;
-    const size_t kv = (size_t)n_seq * m->seq_stride * 4;
-    float *kc = nullptr, *vc = nullptr;
-    rc = dmalloc((void **)&kc, kv, "the K caches");
-    if (!rc) rc = dmalloc((void **)&vc, kv, "the V caches");
+// (Re)allocate the KV caches of n_seq sequences with elements of kv_type (cleared), and the batched
+// attention's partials for up to min(n_seq, 256) sequences (here, so that no batched call
+// allocates: they may be captured in a CUDA graph).
+static int realloc_caches(QmsCudaModel *m, int n_seq, int kv_type) {
+    const size_t es = kv_type == QMS_T_F16 ? 2 : 4, kv = (size_t)n_seq * m->seq_stride * es;
+    void *kc = nullptr, *vc = nullptr;
+    int rc = dmalloc(&kc, kv, "the K caches");
+    if (!rc) rc = dmalloc(&vc, kv, "the V caches");
     if (!rc && (cudaMemset(kc, 0, kv) != cudaSuccess || cudaMemset(vc, 0, kv) != cudaSuccess)) {
-        set_error("set_sequences: memset failed");
+        set_error("KV caches: memset failed");
         rc = QMS_CUDA_ECUDA;
+    }
+    const int nb = std::min(n_seq, kChunk), ms = (m->ctx + kAttnBlock - 1) / kAttnBlock;
+    float *po = nullptr;
+    double *pml = nullptr;
+    if (!rc && n_seq > 1) {
+        rc = dmalloc((void **)&po, (size_t)nb * m->H * ms * m->D * 4, "batched attention partials");
+        if (!rc) rc = dmalloc((void **)&pml, (size_t)nb * m->H * ms * 16, "batched attention partials");
     }
     if (rc) {
         cudaFree(kc);
         cudaFree(vc);
+        cudaFree(po);
+        cudaFree(pml);
         return rc;
-    }
-    // the batched attention's partials for up to min(n_seq, 256) sequences, allocated here so
-    // that no batched call allocates (they may be captured in a CUDA graph)
-    const int nb = std::min(n_seq, kChunk), ms = (m->ctx + kAttnBlock - 1) / kAttnBlock;
-    float *po = nullptr;
-    double *pml = nullptr;
-    if (n_seq > 1) {
-        rc = dmalloc((void **)&po, (size_t)nb * m->H * ms * m->D * 4, "batched attention partials");
-        if (!rc) rc = dmalloc((void **)&pml, (size_t)nb * m->H * ms * 16, "batched attention partials");
-        if (rc) {
-            cudaFree(kc);
-            cudaFree(vc);
-            cudaFree(po);
-            return rc;
-        }
     }
     QMS_CK(cudaDeviceSynchronize());
     cudaFree(m->kc);
@@ -809,7 +807,29 @@ int qms_cuda_model_set_sequences(QmsCudaModel *m, int n_seq) {
     m->bpart_o = po;
     m->bpart_ml = pml;
     m->n_seq = n_seq;
+    m->kv_type = kv_type;
+    m->kv_es = es;
     return QMS_CUDA_OK;
+}
+
+int qms_cuda_model_set_sequences(QmsCudaModel *m, int n_seq) {
+    clear_error();
+    QMS_REQUIRE(m && n_seq >= 1, QMS_CUDA_EINVAL, "set_sequences: bad arguments");
+    int rc = ensure_dev(m->device);
+    if (rc) return rc;
+    if (n_seq == m->n_seq) return QMS_CUDA_OK;
+    return realloc_caches(m, n_seq, m->kv_type);
+}
+
+int qms_cuda_model_set_kv_type(QmsCudaModel *m, int kv_type) {
+    clear_error();
+    QMS_REQUIRE(m, QMS_CUDA_EINVAL, "set_kv_type: NULL model");
+    QMS_REQUIRE(kv_type == QMS_T_F32 || kv_type == QMS_T_F16, QMS_CUDA_EUNSUPPORTED,
+                "set_kv_type: type %d (F32 or F16)", kv_type);
+    int rc = ensure_dev(m->device);
+    if (rc) return rc;
+    if (kv_type == m->kv_type) return QMS_CUDA_OK;
+    return realloc_caches(m, m->n_seq, kv_type);
 }
 
 int qms_cuda_model_copy_sequence(QmsCudaModel *m, int src, int dst, int npos) {
@@ -819,11 +839,12 @@ int qms_cuda_model_copy_sequence(QmsCudaModel *m, int src, int dst, int npos) {
                 QMS_CUDA_EINVAL, "copy_sequence: bad arguments");
     int rc = ensure_dev(m->device);
     if (rc) return rc;
-    const size_t layer = (size_t)m->ctx * m->KD, n = (size_t)npos * m->KD * 4;
+    const size_t es = m->kv_es, layer = (size_t)m->ctx * m->KD, n = (size_t)npos * m->KD * es;
+    char *kc = static_cast<char *>(m->kc), *vc = static_cast<char *>(m->vc);
     for (int l = 0; l < m->L && n; l++) {
-        const size_t so = (size_t)src * m->seq_stride + l * layer, d = (size_t)dst * m->seq_stride + l * layer;
-        QMS_CK(cudaMemcpyAsync(m->kc + d, m->kc + so, n, cudaMemcpyDeviceToDevice, m->stream));
-        QMS_CK(cudaMemcpyAsync(m->vc + d, m->vc + so, n, cudaMemcpyDeviceToDevice, m->stream));
+        const size_t so = es * ((size_t)src * m->seq_stride + l * layer), d = es * ((size_t)dst * m->seq_stride + l * layer);
+        QMS_CK(cudaMemcpyAsync(kc + d, kc + so, n, cudaMemcpyDeviceToDevice, m->stream));
+        QMS_CK(cudaMemcpyAsync(vc + d, vc + so, n, cudaMemcpyDeviceToDevice, m->stream));
     }
     QMS_CK(cudaStreamSynchronize(m->stream));
     return QMS_CUDA_OK;

@@ -125,6 +125,35 @@ __device__ __forceinline__ int pack_sums(const Q8Lane &r) { return (r.sum_lo & 0
 __device__ __forceinline__ int sum_lo(int s) { return (int)(int16_t)(s & 0xffff); }
 __device__ __forceinline__ int sum_hi(int s) { return s >> 16; }
 
+// KV cache elements: fp32 (the reference's cache, src/model.c:459-460) or fp16 (compacted: each K / V
+// value rounded once when appended, read back as fp32).
+__device__ __forceinline__ void kv_st(float *p, float v) { *p = v; }
+__device__ __forceinline__ void kv_st(__half *p, float v) { *p = __float2half_rn(v); }
+__device__ __forceinline__ float kv_ld(const float *p) { return __ldcg(p); }
+__device__ __forceinline__ float kv_ld(const __half *p) { return __half2float(__ldcg(p)); }
+__device__ __forceinline__ float4 kv_ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ float4 kv_ld4(const __half *p) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+__device__ __forceinline__ float2 kv_ld2(const float *p) { return *reinterpret_cast<const float2 *>(p); }
+__device__ __forceinline__ float2 kv_ld2(const __half *p) { return __half22float2(*reinterpret_cast<const __half2 *>(p)); }
+// the same from global memory through L2 only
+__device__ __forceinline__ float4 kv_ldg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
+__device__ __forceinline__ float4 kv_ldg4(const __half *p) {
+    const uint2 u = __ldcg(reinterpret_cast<const uint2 *>(p));
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+__device__ __forceinline__ float2 kv_ldg2(const float *p) { return __ldcg(reinterpret_cast<const float2 *>(p)); }
+__device__ __forceinline__ float2 kv_ldg2(const __half *p) {
+    const uint32_t u = __ldcg(reinterpret_cast<const unsigned int *>(p));
+    return __half22float2(*reinterpret_cast<const __half2 *>(&u));
+}
+
 // ---- embedding ---------------------------------------------------------------------------------------
 __device__ __forceinline__ float dequant_elem(int type, const uint8_t *row, int i) {
     switch (type) {
@@ -697,7 +726,7 @@ int launch_gemm_q(int type, const GemvArgs &a, cudaStream_t s) {
 }
 
 // ---- QK-norm, RoPE, KV append ------------------------------------------------------------------------------
-template <int D>
+template <int D, typename KT>
 __global__ void __launch_bounds__(256) k_qk_rope(const AttnArgs a) {
     constexpr int J = D / 32, JH = J / 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -717,9 +746,9 @@ __global__ void __launch_bounds__(256) k_qk_rope(const AttnArgs a) {
 #pragma unroll
     for (int j = 0; j < J; j++) x[j] = row[lane + 32 * j];
     if (hh >= a.H + a.Hk) {                                    // v head: append as is
-        float *dst = a.vc + cb + (size_t)p * KD + (size_t)(hh - a.H - a.Hk) * D;
+        KT *dst = static_cast<KT *>(a.vc) + cb + (size_t)p * KD + (size_t)(hh - a.H - a.Hk) * D;
 #pragma unroll
-        for (int j = 0; j < J; j++) dst[lane + 32 * j] = x[j];
+        for (int j = 0; j < J; j++) kv_st(dst + lane + 32 * j, x[j]);
         return;
     }
     const float *nw = hh < a.H ? a.q_norm : a.k_norm;
@@ -738,22 +767,32 @@ __global__ void __launch_bounds__(256) k_qk_rope(const AttnArgs a) {
         x[j] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
         x[j + JH] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
     }
-    float *dst = hh < a.H ? row : a.kc + cb + (size_t)p * KD + (size_t)(hh - a.H) * D;
+    if (hh < a.H) {
 #pragma unroll
-    for (int j = 0; j < J; j++) dst[lane + 32 * j] = x[j];
+        for (int j = 0; j < J; j++) row[lane + 32 * j] = x[j];
+        return;
+    }
+    KT *dst = static_cast<KT *>(a.kc) + cb + (size_t)p * KD + (size_t)(hh - a.H) * D;
+#pragma unroll
+    for (int j = 0; j < J; j++) kv_st(dst + lane + 32 * j, x[j]);
 }
 
 int launch_qk_rope(const AttnArgs &a, cudaStream_t s) {
     const dim3 grid((a.H + 2 * a.Hk + 7) / 8, a.T);
-    if (a.D == 128) QMS_CK(launch_pdl(k_qk_rope<128>, grid, dim3(256), 0, s, a));
-    else QMS_CK(launch_pdl(k_qk_rope<64>, grid, dim3(256), 0, s, a));
+    if (a.D == 128) {
+        if (a.kv16) QMS_CK(launch_pdl(k_qk_rope<128, __half>, grid, dim3(256), 0, s, a));
+        else QMS_CK(launch_pdl(k_qk_rope<128, float>, grid, dim3(256), 0, s, a));
+    } else {
+        if (a.kv16) QMS_CK(launch_pdl(k_qk_rope<64, __half>, grid, dim3(256), 0, s, a));
+        else QMS_CK(launch_pdl(k_qk_rope<64, float>, grid, dim3(256), 0, s, a));
+    }
     return QMS_CUDA_OK;
 }
 
 // ---- attention -------------------------------------------------------------------------------------------------
 int attention_heads_per_cta(int group) { return group < 4 ? group : 4; }
 
-template <int D>
+template <int D, typename KT>
 __global__ void __launch_bounds__(128) k_attention(const AttnArgs a) {
     constexpr int NQ = D / 16;                   // elements of q per lane (lane k of 16: 16i + k)
     constexpr int DPL = D / 32;                  // output dims per lane
@@ -783,7 +822,7 @@ __global__ void __launch_bounds__(128) k_attention(const AttnArgs a) {
     float qr[NQ];
 #pragma unroll
     for (int i = 0; i < NQ; i++) qr[i] = qh[16 * i + k16];
-    const float *kb = a.kc + cb + (size_t)g * D, *vb = a.vc + cb + (size_t)g * D;
+    const KT *kb = static_cast<const KT *>(a.kc) + cb + (size_t)g * D, *vb = static_cast<const KT *>(a.vc) + cb + (size_t)g * D;
     float o[DPL];
 #pragma unroll
     for (int d = 0; d < DPL; d++) o[d] = 0.0f;
@@ -795,9 +834,9 @@ __global__ void __launch_bounds__(128) k_attention(const AttnArgs a) {
             const int p = pc + 2 * j + half;
             float acc = 0.0f;
             if (p < p1) {
-                const float *kp = kb + (size_t)p * KD;
+                const KT *kp = kb + (size_t)p * KD;
 #pragma unroll
-                for (int i = 0; i < NQ; i++) acc = __fmaf_rn(qr[i], __ldcg(kp + 16 * i + k16), acc);
+                for (int i = 0; i < NQ; i++) acc = __fmaf_rn(qr[i], kv_ld(kp + 16 * i + k16), acc);
             }
             acc = __fadd_rn(acc, __shfl_down_sync(kFull, acc, 8, 16));
             acc = __fadd_rn(acc, __shfl_down_sync(kFull, acc, 4, 16));
@@ -820,15 +859,15 @@ __global__ void __launch_bounds__(128) k_attention(const AttnArgs a) {
         const int np = min(32, p1 - pc);
         for (int q = 0; q < np; q++) {
             const float w = __shfl_sync(kFull, fe, q);
-            const float *vp = vb + (size_t)(pc + q) * KD + lane * DPL;
+            const KT *vp = vb + (size_t)(pc + q) * KD + lane * DPL;
             if constexpr (DPL == 4) {
-                const float4 v = __ldcg(reinterpret_cast<const float4 *>(vp));
+                const float4 v = kv_ldg4(vp);
                 o[0] = __fmaf_rn(w, v.x, o[0]);
                 o[1] = __fmaf_rn(w, v.y, o[1]);
                 o[2] = __fmaf_rn(w, v.z, o[2]);
                 o[3] = __fmaf_rn(w, v.w, o[3]);
             } else {
-                const float2 v = __ldcg(reinterpret_cast<const float2 *>(vp));
+                const float2 v = kv_ldg2(vp);
                 o[0] = __fmaf_rn(w, v.x, o[0]);
                 o[1] = __fmaf_rn(w, v.y, o[1]);
             }
@@ -918,8 +957,13 @@ int launch_argmax_rows(const float *logits, int ld, int B, int V, int *tok, int 
 int launch_attention(const AttnArgs &a, cudaStream_t s) {
     const int group = a.H / a.Hk, HB = attention_heads_per_cta(group);
     const dim3 grid(a.Hk * (group / HB), a.split > 0 ? a.max_splits : 1, a.T);
-    if (a.D == 128) QMS_CK(launch_pdl(k_attention<128>, grid, dim3(32 * HB), 0, s, a));
-    else QMS_CK(launch_pdl(k_attention<64>, grid, dim3(32 * HB), 0, s, a));
+    if (a.D == 128) {
+        if (a.kv16) QMS_CK(launch_pdl(k_attention<128, __half>, grid, dim3(32 * HB), 0, s, a));
+        else QMS_CK(launch_pdl(k_attention<128, float>, grid, dim3(32 * HB), 0, s, a));
+    } else {
+        if (a.kv16) QMS_CK(launch_pdl(k_attention<64, __half>, grid, dim3(32 * HB), 0, s, a));
+        else QMS_CK(launch_pdl(k_attention<64, float>, grid, dim3(32 * HB), 0, s, a));
+    }
     return QMS_CUDA_OK;
 }
 
@@ -1355,18 +1399,26 @@ __device__ __forceinline__ void norm_rope_pre(float (&x)[D / 32], const float (&
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+// 8-byte asynchronous copy (through L1: the 16-byte form is the only L2-only one).
+__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// Four cache elements: 16 bytes of fp32 or 8 bytes of fp16.
+__device__ __forceinline__ void cp_async_kv4(float *dst, const float *src) { cp_async16(dst, src); }
+__device__ __forceinline__ void cp_async_kv4(__half *dst, const __half *src) { cp_async8(dst, src); }
 
 // CTA (kv head g, block s of kAttnBlock positions, sequence z) with group / HB warps; warp w owns q
 // heads g * group + w * HB .. + HB. Scores: lane = position, each of the block's K rows read once
 // from shared memory (rows padded to D + 4 floats: 16-byte aligned for cp.async, conflict-free
 // float4 reads) for the warp's HB heads, each dot in qms_vec_dot_f32's order (sixteen FMA chains,
 // then the hsum tree). P.V: lane = output dims, each V row read once for the HB heads. Every head's
-// arithmetic is the same as with one warp per head; only the loads are shared.
-template <int D, int HB>
+// arithmetic is the same as with one warp per head; only the loads are shared. KT: the cache's
+// element (fp32, or fp16 converted on each read); rows padded to D + 4 elements either way.
+template <int D, int HB, typename KT>
 __global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
     constexpr int PB = kAttnBlock, KP = D + 4, J = D / 32, JH = J / 2, DPL = D / 32;
-    __shared__ __align__(16) float sk[PB * KP];
-    __shared__ __align__(16) float sv[PB * KP];
+    __shared__ __align__(16) KT sk[PB * KP];
+    __shared__ __align__(16) KT sv[PB * KP];
     __shared__ __align__(16) float sq[16 * D];
     const int group = a.H / a.Hk, g = blockIdx.x, s = blockIdx.y, z = blockIdx.z;   // z: sequence (batch)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x, nthr = blockDim.x;
@@ -1389,8 +1441,8 @@ __global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
     for (int i = tid; i < nc * (D / 4); i += nthr) {
         const int p = i / (D / 4), d = 4 * (i % (D / 4));
         const size_t at = cb + (size_t)(p0 + p) * KD + (size_t)g * D + d;
-        cp_async16(sk + p * KP + d, a.kc + at);
-        cp_async16(sv + p * KP + d, a.vc + at);
+        cp_async_kv4(sk + p * KP + d, static_cast<const KT *>(a.kc) + at);
+        cp_async_kv4(sv + p * KP + d, static_cast<const KT *>(a.vc) + at);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
     // while the rows land: the group's q heads (QK-norm + NEOX RoPE) and the new position's rows
@@ -1421,16 +1473,16 @@ __global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
         norm_rope_pre<D>(kx, kw, c, sn, a.eps);
 #pragma unroll
         for (int j = 0; j < J; j++) {
-            sk[(pos - p0) * KP + lane + 32 * j] = kx[j];
-            a.kc[cb + (size_t)pos * KD + (size_t)g * D + lane + 32 * j] = kx[j];
+            kv_st(sk + (pos - p0) * KP + lane + 32 * j, kx[j]);
+            kv_st(static_cast<KT *>(a.kc) + cb + (size_t)pos * KD + (size_t)g * D + lane + 32 * j, kx[j]);
         }
     }
     if (has_new && warp == (nwarps > 1 ? 1 : 0)) {            // and its V row
 #pragma unroll
         for (int j = 0; j < J; j++) {
             const float v = __ldcg(qkv + (size_t)(a.H + a.Hk) * D + (size_t)g * D + lane + 32 * j);
-            sv[(pos - p0) * KP + lane + 32 * j] = v;
-            a.vc[cb + (size_t)pos * KD + (size_t)g * D + lane + 32 * j] = v;
+            kv_st(sv + (pos - p0) * KP + lane + 32 * j, v);
+            kv_st(static_cast<KT *>(a.vc) + cb + (size_t)pos * KD + (size_t)g * D + lane + 32 * j, v);
         }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
@@ -1446,12 +1498,12 @@ __global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
 #pragma unroll
             for (int c2 = 0; c2 < 16; c2++) acc[k][c2] = 0.0f;
         if (valid) {
-            const float4 *k4 = reinterpret_cast<const float4 *>(sk + lane * KP);
+            const KT *kr = sk + lane * KP;
 #pragma unroll
             for (int i = 0; i < D / 16; i++)
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    const float4 kv = k4[4 * i + j];
+                    const float4 kv = kv_ld4(kr + 4 * (4 * i + j));
 #pragma unroll
                     for (int k = 0; k < HB; k++) {
                         const float4 qv = reinterpret_cast<const float4 *>(sq + (h0 + k) * D)[4 * i + j];
@@ -1484,13 +1536,13 @@ __global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
 #pragma unroll
         for (int d = 0; d < DPL; d++) o[k][d] = 0.0f;
     for (int q = 0; q < np; q++) {
-        const float *vp = sv + q * KP + lane * DPL;
+        const KT *vp = sv + q * KP + lane * DPL;
         float v[DPL];
         if constexpr (DPL == 4) {
-            const float4 t4 = *reinterpret_cast<const float4 *>(vp);
+            const float4 t4 = kv_ld4(vp);
             v[0] = t4.x; v[1] = t4.y; v[2] = t4.z; v[3] = t4.w;
         } else {
-            const float2 t2 = *reinterpret_cast<const float2 *>(vp);
+            const float2 t2 = kv_ld2(vp);
             v[0] = t2.x; v[1] = t2.y;
         }
 #pragma unroll
@@ -1572,6 +1624,18 @@ __global__ void __launch_bounds__(4 * D) k_attn_merge(const AttnArgs a, int8_t *
     }
 }
 
+template <int D>
+static cudaError_t launch_attn_decode_d(const AttnArgs &a, int hb, dim3 grid, dim3 block, cudaStream_t s) {
+    if (a.kv16) {
+        if (hb == 4) return launch_pdl(k_attn_decode<D, 4, __half>, grid, block, 0, s, a);
+        if (hb == 2) return launch_pdl(k_attn_decode<D, 2, __half>, grid, block, 0, s, a);
+        return launch_pdl(k_attn_decode<D, 1, __half>, grid, block, 0, s, a);
+    }
+    if (hb == 4) return launch_pdl(k_attn_decode<D, 4, float>, grid, block, 0, s, a);
+    if (hb == 2) return launch_pdl(k_attn_decode<D, 2, float>, grid, block, 0, s, a);
+    return launch_pdl(k_attn_decode<D, 1, float>, grid, block, 0, s, a);
+}
+
 int launch_attn_decode(const AttnArgs &a, int8_t *xq, float *xd, int *xs, cudaStream_t s) {
     const int group = a.H / a.Hk;
     QMS_REQUIRE(group <= 16 && (a.T == 1 || a.pos_vec) && a.T <= 65535 && a.max_splits <= kAttnMaxCtx / kAttnBlock &&
@@ -1583,17 +1647,10 @@ int launch_attn_decode(const AttnArgs &a, int8_t *xq, float *xd, int *xs, cudaSt
     const int hmax = a.pos_vec ? 4 : 2, hb = group < hmax ? group : hmax;
     QMS_REQUIRE(group % hb == 0, QMS_CUDA_EUNSUPPORTED, "attn_decode: %d q heads per kv head", group);
     const dim3 grid(a.Hk, a.max_splits, a.T), block(32 * (group / hb));
-    if (a.D == 128) {
-        if (hb == 4) QMS_CK(launch_pdl(k_attn_decode<128, 4>, grid, block, 0, s, a));
-        else if (hb == 2) QMS_CK(launch_pdl(k_attn_decode<128, 2>, grid, block, 0, s, a));
-        else QMS_CK(launch_pdl(k_attn_decode<128, 1>, grid, block, 0, s, a));
-        QMS_CK(launch_pdl(k_attn_merge<128>, dim3(a.H, a.T), dim3(512), 0, s, a, xq, xd, xs));
-    } else {
-        if (hb == 4) QMS_CK(launch_pdl(k_attn_decode<64, 4>, grid, block, 0, s, a));
-        else if (hb == 2) QMS_CK(launch_pdl(k_attn_decode<64, 2>, grid, block, 0, s, a));
-        else QMS_CK(launch_pdl(k_attn_decode<64, 1>, grid, block, 0, s, a));
-        QMS_CK(launch_pdl(k_attn_merge<64>, dim3(a.H, a.T), dim3(256), 0, s, a, xq, xd, xs));
-    }
+    if (a.D == 128) QMS_CK(launch_attn_decode_d<128>(a, hb, grid, block, s));
+    else QMS_CK(launch_attn_decode_d<64>(a, hb, grid, block, s));
+    if (a.D == 128) QMS_CK(launch_pdl(k_attn_merge<128>, dim3(a.H, a.T), dim3(512), 0, s, a, xq, xd, xs));
+    else QMS_CK(launch_pdl(k_attn_merge<64>, dim3(a.H, a.T), dim3(256), 0, s, a, xq, xd, xs));
     return QMS_CUDA_OK;
 }
 

@@ -83,7 +83,8 @@ struct AttnArgs {
     const float *q_norm, *k_norm;
     float eps;
     const float *rope_cos, *rope_sin; // [ctx][D/2]
-    float *kc, *vc;                   // this layer's cache [ctx][Hk*D]
+    void *kc, *vc;                    // this layer's cache [ctx][Hk*D]: fp32, or fp16 when kv16
+    int kv16;
     const int *pos;                   // device: position of token 0
     // several sequences (batched decode): token t belongs to sequence t, sits at position pos_vec[t]
     // and uses the caches at kc / vc + t * seq_stride; NULL: every token of one sequence

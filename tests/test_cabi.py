@@ -121,6 +121,7 @@ def test_model_calls_validate_arguments():
     assert L.qms_cuda_decode_batch(None, 1, p, p, None, None) == q.EINVAL
     assert L.qms_cuda_model_set_sequences(None, 2) == q.EINVAL
     assert L.qms_cuda_model_copy_sequence(None, 0, 1, 4) == q.EINVAL
+    assert L.qms_cuda_model_set_kv_type(None, q.T_F16) == q.EINVAL
     assert L.qms_cuda_model_set_layer(None, 0, None) == q.EINVAL
     assert L.qms_cuda_model_reserve(None, 4) == q.EINVAL
     assert L.qms_cuda_model_status(None) == q.EINVAL

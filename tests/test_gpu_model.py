@@ -324,3 +324,43 @@ def test_decode_batch_graph_matches_reference_ids(cuda):
     assert pos.tolist() == [len(prompt) + g["gen"] - 1, len(other) + g["gen"] - 1, len(prompt) + g["gen"] - 1]
     del graph
     m.close()
+
+
+def test_fp16_kv_cache_close_to_fp32(cuda):
+    """KV compaction (qms_cuda_model_set_kv_type F16): the prompt and 8 teacher-forced decode steps
+    with an fp16 cache against the fp32 cache (the reference's). Each K / V value is rounded once
+    to fp16, so the logits move by about that rounding through the softmax; the argmax must agree
+    wherever the fp32 run's top-2 margin is above 0.05 (logprob). A batched step over fp16 caches
+    must match single sequences on fp16 caches as the fp32 batch test does."""
+    rng = np.random.default_rng(17)
+    for name in ("tiny", "30b"):
+        cfg = synth.MODEL_CONFIGS[name]
+        prompt = [int(v) for v in rng.integers(0, cfg.vocab, 40)]
+        m32 = cuda.Model.from_synth(cfg, 3, 96)
+        m16 = cuda.Model.from_synth(cfg, 3, 96)
+        m16.set_kv_type(cuda.T_F16)
+        l32, l16 = m32.forward(prompt, 0, all_logits=True), m16.forward(prompt, 0, all_logits=True)
+        errs = [rel_l2(l16[t], l32[t]) for t in range(len(prompt))]
+        flips = 0
+        tok = int(np.argmax(l32[-1]))
+        for s in range(8):
+            a32, a16 = m32.forward([tok], len(prompt) + s), m16.forward([tok], len(prompt) + s)
+            errs.append(rel_l2(a16, a32))
+            top = np.sort(_log_softmax(a32))[-2:]
+            if top[1] - top[0] > 0.05 and int(np.argmax(a16)) != int(np.argmax(a32)):
+                flips += 1
+            tok = int(np.argmax(a32))
+        m32.status()
+        m16.status()
+        m32.close()
+        errs = np.array(errs)
+        assert errs.mean() < 1e-2 and errs.max() < 5e-2, f"{name}: fp16 cache moves logits by {errs.mean():.2e} (mean), {errs.max():.2e} (worst)"
+        assert flips == 0, f"{name}: {flips} argmax changes outside near ties"
+        # batched decode over fp16 caches against single sequences on fp16 caches
+        m16.set_sequences(2)
+        ms = cuda.Model.from_synth(cfg, 3, 96)
+        ms.set_kv_type(cuda.T_F16)
+        berrs, bflips = _teacher_forced(m16, ms, [prompt[:13], prompt[13:]], 4)
+        m16.close()
+        ms.close()
+        assert berrs.mean() < 3e-3 and bflips == 0, f"{name}: fp16 batch rows differ by {berrs.mean():.2e}"

@@ -835,12 +835,17 @@ def run_model_batch(a):
         dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    profile_region = os.environ.get("QMS_PROFILE_REGION") == "1"   # ncu --profile-from-start off: the timed steps only
+    if profile_region:
+        torch.cuda.profiler.start()
     with torch.cuda.stream(stream):
         ev0.record(stream)
         for _ in range(a.steps):
             graph.replay()
         ev1.record(stream)
     torch.cuda.synchronize()
+    if profile_region:
+        torch.cuda.profiler.stop()
     clocks = sampler.stop()
     ms = ev0.elapsed_time(ev1)
     if dist:

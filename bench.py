@@ -909,10 +909,11 @@ def run_model_batch(a):
                     "d2h_bytes_per_step": B * cfg.vocab * 4,
                     "note": "qms_cuda_forward_batch per step (host ids and positions in, every sequence's 151936 "
                             "logits to host memory, argmax per row on the host)"},
-            # per step: embedding; per layer RMSNorm, QKV, RoPE + KV append, attention, Q8 of the
-            # attention output, O, RMSNorm and the 7 kernels of the batched MoE block; head RMSNorm,
-            # head, per-row argmax
-            "gpu_launches": a.steps * (1 + 14 * cfg.n_layer + 3),
+            # per step: the embedding; per layer RMSNorm, QKV, attention, merge (Q8 out), O, RMSNorm
+            # and the 7 kernels of the batched MoE block (router, top-k, Q8 rows, grouping, gate/up,
+            # down, combine); the head's RMSNorm, the head and the per-row argmax (the launch list in
+            # profiles/launches_decode_step_235b_bs64.md counts the same 1226)
+            "gpu_launches": a.steps * (1 + 13 * cfg.n_layer + 3),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

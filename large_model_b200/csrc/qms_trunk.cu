@@ -26,6 +26,7 @@
 
 #include <algorithm>
 
+#include "qms_async.cuh"
 #include "qms_moe.cuh"
 #include "qms_trunk.cuh"
 
@@ -153,6 +154,22 @@ __device__ __forceinline__ float2 kv_ldg2(const __half *p) {
     const uint32_t u = __ldcg(reinterpret_cast<const unsigned int *>(p));
     return __half22float2(*reinterpret_cast<const __half2 *>(&u));
 }
+
+// 16-byte asynchronous copy global -> shared (L2 only; no register staging).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// 8-byte asynchronous copy (through L1: the 16-byte form is the only L2-only one).
+__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// Four cache elements: 16 bytes of fp32 or 8 bytes of fp16.
+__device__ __forceinline__ void cp_async_kv4(float *dst, const float *src) { cp_async16(dst, src); }
+__device__ __forceinline__ void cp_async_kv4(__half *dst, const __half *src) { cp_async8(dst, src); }
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
 
 // ---- embedding ---------------------------------------------------------------------------------------
 __device__ __forceinline__ float dequant_elem(int type, const uint8_t *row, int i) {
@@ -526,80 +543,112 @@ int launch_gemv(int type, const GemvArgs &a, cudaStream_t s) {
 // term), each 32-block's integer dot exact and scaled in fp32 block by block, as in the one-token
 // kernels (src/kernels.c:82-134). A warp owns 16 rows x 32 tokens: per block one
 // mma.m16n8k32.s8 per 8 tokens (A = the rows' nibbles - 8 for Q4_0, B = the tokens' Q8 bytes),
-// then the int32 results are scaled into fp32 registers. Weights and activations are read straight
-// from global memory (each weight byte once per token tile; activations through L1 / L2).
+// then the int32 results are scaled into fp32 registers. A CTA's warps share one 32-token tile:
+// its Q8 bytes and block scales are staged in shared memory by cp.async, chunks of kGqKB blocks in
+// two buffers (the next chunk loads while this one is used); token rows padded to kGqXS bytes and
+// scale rows to kGqKB + 1 floats, so the fragment reads are conflict-free. Weights come straight
+// from global memory (four lanes read a row's 16 bytes of a block: each weight byte once per tile).
+constexpr int kGqKB = 8;                          // blocks per staged chunk
+constexpr int kGqXS = kGqKB * 32 + 16;            // bytes of one token's chunk (+ pad)
+constexpr int kGqDS = kGqKB + 1;                  // floats of one token's chunk scales (+ pad)
+
 template <int Q1>
 __global__ void __launch_bounds__(128) k_gemm_q4(const GemvArgs a) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __shared__ __align__(16) int8_t sxq[2][32 * kGqXS];
+    __shared__ float sdx[2][32 * kGqDS];
+    __shared__ int ssx[2][Q1 ? 32 * kGqDS : 1];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
     const int g = lane >> 2, tg = lane & 3;
-    const int r0 = (blockIdx.x * (blockDim.x >> 5) + warp) * 16, t0 = blockIdx.y * 32;
-    const int nb = a.ncol / 32;
+    const int r0 = (blockIdx.x * (nthr >> 5) + warp) * 16, t0 = blockIdx.y * 32;
+    const int nb = a.ncol / 32, nch = (nb + kGqKB - 1) / kGqKB;
     pdl_trigger();
     pdl_wait();
-    if (r0 >= a.rows) return;
+    auto stage = [&](int c, int buf) {                         // chunk c of the tile into buffer buf
+        const int c0 = c * kGqKB, kn = min(kGqKB, nb - c0);
+        for (int i = tid; i < 32 * kn * 2; i += nthr) {
+            const int t = i / (kn * 2), kb = (i >> 1) % kn, h = i & 1;
+            const int tt = min(t0 + t, a.T - 1);               // rows past T are copies of the last (not stored)
+            cp_async16(&sxq[buf][t * kGqXS + kb * 32 + 16 * h], a.xq + (size_t)tt * a.ncol + (size_t)(c0 + kb) * 32 + 16 * h);
+        }
+        for (int i = tid; i < 32 * kn; i += nthr) {
+            const int t = i / kn, kb = i % kn, tt = min(t0 + t, a.T - 1);
+            cp_async4(&sdx[buf][t * kGqDS + kb], a.xd + (size_t)tt * nb + c0 + kb);
+            if (Q1) cp_async4(&ssx[buf][t * kGqDS + kb], a.xs + (size_t)tt * nb + c0 + kb);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
     const uint8_t *wr0 = a.w + (size_t)(r0 + g) * a.stride, *wr1 = wr0 + (size_t)8 * a.stride;
     const size_t dpl = (size_t)nb * 16, mpl = dpl + pad16((size_t)nb * 2);
-    const int8_t *xr[4];
-    const float *dr[4][2];
-    const int *sr[4][2];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int tb = min(t0 + 8 * j + g, a.T - 1);              // B operand: token tb (clamped rows are not stored)
-        xr[j] = a.xq + (size_t)tb * a.ncol + 4 * tg;
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int tt = min(t0 + 8 * j + 2 * tg + h, a.T - 1);  // accumulator column: token tt
-            dr[j][h] = a.xd + (size_t)tt * nb;
-            sr[j][h] = a.xs + (size_t)tt * nb;
-        }
-    }
     float acc[4][4];
 #pragma unroll
     for (int j = 0; j < 4; j++)
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[j][i] = 0.0f;
-    for (int b = 0; b < nb; b++) {
-        const uint32_t w0 = __ldg(reinterpret_cast<const uint32_t *>(wr0 + (size_t)b * 16 + 4 * tg));
-        const uint32_t w1 = __ldg(reinterpret_cast<const uint32_t *>(wr1 + (size_t)b * 16 + 4 * tg));
-        uint32_t a0 = w0 & 0x0F0F0F0Fu, a2 = (w0 >> 4) & 0x0F0F0F0Fu, a1 = w1 & 0x0F0F0F0Fu, a3 = (w1 >> 4) & 0x0F0F0F0Fu;
-        if (!Q1) {                                                  // q - 8 in [-8, 7], bytewise
-            a0 = __vsub4(a0, 0x08080808u);
-            a1 = __vsub4(a1, 0x08080808u);
-            a2 = __vsub4(a2, 0x08080808u);
-            a3 = __vsub4(a3, 0x08080808u);
-        }
-        const float dw0 = h2f(__ldg(reinterpret_cast<const uint16_t *>(wr0 + dpl) + b));
-        const float dw1 = h2f(__ldg(reinterpret_cast<const uint16_t *>(wr1 + dpl) + b));
-        float mw0 = 0.0f, mw1 = 0.0f;
-        if (Q1) {
-            mw0 = h2f(__ldg(reinterpret_cast<const uint16_t *>(wr0 + mpl) + b));
-            mw1 = h2f(__ldg(reinterpret_cast<const uint16_t *>(wr1 + mpl) + b));
-        }
+    stage(0, 0);
+    for (int c = 0; c < nch; c++) {
+        const int buf = c & 1;
+        // the chunk's weights into registers first: their round trip overlaps the activations' wait
+        const int c0 = c * kGqKB, kn = min(kGqKB, nb - c0);
+        uint32_t wq0[kGqKB], wq1[kGqKB];
+        float dq0[kGqKB], dq1[kGqKB], mq0[kGqKB], mq1[kGqKB];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const uint32_t b0 = __ldg(reinterpret_cast<const uint32_t *>(xr[j] + (size_t)b * 32));
-            const uint32_t b1 = __ldg(reinterpret_cast<const uint32_t *>(xr[j] + (size_t)b * 32 + 16));
-            int c0, c1, c2, c3;
-            asm volatile(
-                "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                "{%10,%10,%10,%10};"
-                : "=r"(c0), "=r"(c1), "=r"(c2), "=r"(c3)
-                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
-            const float dx0 = __ldg(dr[j][0] + b), dx1 = __ldg(dr[j][1] + b);
-            acc[j][0] = __fmaf_rn((float)c0, __fmul_rn(dw0, dx0), acc[j][0]);
-            acc[j][1] = __fmaf_rn((float)c1, __fmul_rn(dw0, dx1), acc[j][1]);
-            acc[j][2] = __fmaf_rn((float)c2, __fmul_rn(dw1, dx0), acc[j][2]);
-            acc[j][3] = __fmaf_rn((float)c3, __fmul_rn(dw1, dx1), acc[j][3]);
-            if (Q1) {
-                const int s0 = __ldg(sr[j][0] + b), s1 = __ldg(sr[j][1] + b);
-                const float f0 = __fmul_rn(dx0, (float)(sum_lo(s0) + sum_hi(s0)));
-                const float f1 = __fmul_rn(dx1, (float)(sum_lo(s1) + sum_hi(s1)));
-                acc[j][0] = __fmaf_rn(mw0, f0, acc[j][0]);
-                acc[j][1] = __fmaf_rn(mw0, f1, acc[j][1]);
-                acc[j][2] = __fmaf_rn(mw1, f0, acc[j][2]);
-                acc[j][3] = __fmaf_rn(mw1, f1, acc[j][3]);
+        for (int kb = 0; kb < kGqKB; kb++) {
+            const int b = c0 + (kb < kn ? kb : 0);
+            wq0[kb] = __ldg(reinterpret_cast<const uint32_t *>(wr0 + (size_t)b * 16 + 4 * tg));
+            wq1[kb] = __ldg(reinterpret_cast<const uint32_t *>(wr1 + (size_t)b * 16 + 4 * tg));
+            dq0[kb] = h2f(__ldg(reinterpret_cast<const uint16_t *>(wr0 + dpl) + b));
+            dq1[kb] = h2f(__ldg(reinterpret_cast<const uint16_t *>(wr1 + dpl) + b));
+            mq0[kb] = Q1 ? h2f(__ldg(reinterpret_cast<const uint16_t *>(wr0 + mpl) + b)) : 0.0f;
+            mq1[kb] = Q1 ? h2f(__ldg(reinterpret_cast<const uint16_t *>(wr1 + mpl) + b)) : 0.0f;
+        }
+        if (c + 1 < nch) {
+            stage(c + 1, buf ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kb = 0; kb < kGqKB; kb++) {
+            if (kb >= kn) break;
+            const uint32_t w0 = wq0[kb], w1 = wq1[kb];
+            uint32_t a0 = w0 & 0x0F0F0F0Fu, a2 = (w0 >> 4) & 0x0F0F0F0Fu, a1 = w1 & 0x0F0F0F0Fu, a3 = (w1 >> 4) & 0x0F0F0F0Fu;
+            if (!Q1) {                                              // q - 8 in [-8, 7], bytewise
+                a0 = __vsub4(a0, 0x08080808u);
+                a1 = __vsub4(a1, 0x08080808u);
+                a2 = __vsub4(a2, 0x08080808u);
+                a3 = __vsub4(a3, 0x08080808u);
+            }
+            const float dw0 = dq0[kb], dw1 = dq1[kb], mw0 = mq0[kb], mw1 = mq1[kb];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int8_t *xb = &sxq[buf][(8 * j + g) * kGqXS + kb * 32 + 4 * tg];
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xb);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xb + 16);
+                int c0r, c1r, c2r, c3r;
+                asm volatile(
+                    "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                    "{%10,%10,%10,%10};"
+                    : "=r"(c0r), "=r"(c1r), "=r"(c2r), "=r"(c3r)
+                    : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+                const int ta = 8 * j + 2 * tg;
+                const float dx0 = sdx[buf][ta * kGqDS + kb], dx1 = sdx[buf][(ta + 1) * kGqDS + kb];
+                acc[j][0] = __fmaf_rn((float)c0r, __fmul_rn(dw0, dx0), acc[j][0]);
+                acc[j][1] = __fmaf_rn((float)c1r, __fmul_rn(dw0, dx1), acc[j][1]);
+                acc[j][2] = __fmaf_rn((float)c2r, __fmul_rn(dw1, dx0), acc[j][2]);
+                acc[j][3] = __fmaf_rn((float)c3r, __fmul_rn(dw1, dx1), acc[j][3]);
+                if (Q1) {
+                    const int s0 = ssx[buf][ta * kGqDS + kb], s1 = ssx[buf][(ta + 1) * kGqDS + kb];
+                    const float f0 = __fmul_rn(dx0, (float)(sum_lo(s0) + sum_hi(s0)));
+                    const float f1 = __fmul_rn(dx1, (float)(sum_lo(s1) + sum_hi(s1)));
+                    acc[j][0] = __fmaf_rn(mw0, f0, acc[j][0]);
+                    acc[j][1] = __fmaf_rn(mw0, f1, acc[j][1]);
+                    acc[j][2] = __fmaf_rn(mw1, f0, acc[j][2]);
+                    acc[j][3] = __fmaf_rn(mw1, f1, acc[j][3]);
+                }
             }
         }
+        __syncthreads();                                       // buffer buf is refilled next iteration
     }
 #pragma unroll
     for (int j = 0; j < 4; j++)
@@ -1394,18 +1443,6 @@ __device__ __forceinline__ void norm_rope_pre(float (&x)[D / 32], const float (&
         x[j + JH] = __fadd_rn(__fmul_rn(x2, c[j]), __fmul_rn(x1, sn[j]));
     }
 }
-
-// 16-byte asynchronous copy global -> shared (L2 only; no register staging).
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-// 8-byte asynchronous copy (through L1: the 16-byte form is the only L2-only one).
-__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-// Four cache elements: 16 bytes of fp32 or 8 bytes of fp16.
-__device__ __forceinline__ void cp_async_kv4(float *dst, const float *src) { cp_async16(dst, src); }
-__device__ __forceinline__ void cp_async_kv4(__half *dst, const __half *src) { cp_async8(dst, src); }
 
 // CTA (kv head g, block s of kAttnBlock positions, sequence z) with group / HB warps; warp w owns q
 // heads g * group + w * HB .. + HB. Scores: lane = position, each of the block's K rows read once

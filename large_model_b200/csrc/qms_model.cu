@@ -341,6 +341,9 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
                 ab.part_o = m->bpart_o;
                 ab.part_ml = m->bpart_ml;
             }
+            // QK-norm, RoPE and the K / V appends once per head row, not in every position block
+            if ((rc = launch_qk_rope(at, s))) return rc;
+            ab.q_ready = 1;
             if ((rc = launch_attn_decode(ab, m->xq, m->xd, m->xs, s))) return rc;
         } else {
             if ((rc = launch_qk_rope(at, s))) return rc;

@@ -1473,8 +1473,8 @@ __global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
     const int KD = a.Hk * D;
     const size_t cb = (size_t)z * a.seq_stride;          // this sequence's caches (0 for one sequence)
     const float *qkv = a.qkv + (size_t)z * a.ldq;
-    const bool has_new = p1 == npos;
-    const int nc = min(p1, pos) - p0;                    // cached rows (the new one comes from qkv)
+    const bool has_new = p1 == npos && !a.q_ready;
+    const int nc = a.q_ready ? np : min(p1, pos) - p0;   // cached rows (else the new one comes from qkv)
     for (int i = tid; i < nc * (D / 4); i += nthr) {
         const int p = i / (D / 4), d = 4 * (i % (D / 4));
         const size_t at = cb + (size_t)(p0 + p) * KD + (size_t)g * D + d;
@@ -1499,7 +1499,7 @@ __global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
         float qx[J];
 #pragma unroll
         for (int j = 0; j < J; j++) qx[j] = __ldcg(qkv + (size_t)(g * group + hh) * D + lane + 32 * j);
-        norm_rope_pre<D>(qx, qw, c, sn, a.eps);
+        if (!a.q_ready) norm_rope_pre<D>(qx, qw, c, sn, a.eps);
 #pragma unroll
         for (int j = 0; j < J; j++) sq[hh * D + lane + 32 * j] = qx[j];
     }

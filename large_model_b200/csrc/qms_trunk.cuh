@@ -90,6 +90,8 @@ struct AttnArgs {
     // and uses the caches at kc / vc + t * seq_stride; NULL: every token of one sequence
     const int *pos_vec;
     size_t seq_stride;
+    int q_ready;                      // one-token attention: q rows already QK-normed and rotated and
+                                      // the new K / V rows already in the cache (k_qk_rope ran)
     int T, ctx, H, Hk, D;
     double scale;                     // 1/sqrt(D)
     int split;                        // positions per CTA when T == 1 (0: one CTA per head group)

@@ -587,12 +587,16 @@ def run_model_reference_arm(a):
     t0 = time.perf_counter()
     t94, desc, threads = cpu_model_sample(decode_tokens=max(8, a.steps))
     value = 1.0 / t94
-    line = {"impl": "reference", "metric": MODEL_METRIC, "value": round(value, 4), "unit": "tok/s",
+    batch = a.mode == "model-bs64"
+    if batch:     # one sequence at a time (src/model.h:116-118): B sequences take B x the bs1 time
+        desc += f"; {a.batch} sequences served one after another: the same tok/s"
+    line = {"impl": "reference", "metric": BATCH_METRIC if batch else MODEL_METRIC, "value": round(value, 4), "unit": "tok/s",
             "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t94 * 1e3, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp32",
             "data": "synthetic",
-            "config": {"workload": "Qwen3-235B-A22B decode, batch 1 (config 4); reference arm: each step one "
-                                   "decode token on each sampled model", "sample": desc,
+            "config": {"workload": f"Qwen3-235B-A22B decode, {'%d sequences' % a.batch if batch else 'batch 1'} "
+                                   "(config 4); reference arm: each step one decode token on each sampled model",
+                       "sample": desc,
                        "wall_s": round(time.perf_counter() - t0, 1)},
             "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "reference",
                              "sample": desc},

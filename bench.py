@@ -420,11 +420,23 @@ def run_batched(a):
             metric, unit, value = "Qwen3-235B Q4_0 MoE-layer decode bs64 tokens/s (operator)", "tok/s", tok_s
         else:
             tops = world * ops / (call_ms / 1e3) / 1e12
+            # The real bound: every 32-value block product's int32 sum is scaled in fp32 on the CUDA
+            # cores (the reference's per-block arithmetic): at least ~2.5 instructions per block
+            # product (int -> float, d_w * d_x, the FMA; profiles/k_mma_gemm_235b_bs64_prefill.md),
+            # issued at 4 warp instructions per clock per SM.
+            products = T * K * (2 * F * (E // 32) + E * (F // 32))
+            sm_hz = (clocks.get("sm_mhz") or 1965.0) * 1e6
+            floor_ms = products * 2.5 / (torch.cuda.get_device_properties(dev).multi_processor_count * 4 * 32 * sm_hz) * 1e3
             roof = {"bound": "tensor", "kernel": "whole block (router, k_mma_group, gathers, k_mma_gemm x2, combine)",
                     "achieved": round(tops, 1), "peak": 4500.0 * world, "unit": "TOP/s",
                     "frac": round(tops / (4500.0 * world), 4),
                     "peak_kind": "nominal dense int8 (no measured int8 peak on this pool)", "traffic": None,
-                    "ops_per_call": ops}
+                    "ops_per_call": ops,
+                    "epilogue_bound": {"block_products_per_call": products, "instructions_per_product": 2.5,
+                                       "floor_ms_per_call": round(floor_ms, 3),
+                                       "frac": round(floor_ms / call_ms, 4),
+                                       "note": "per-block fp32 scaling on the CUDA cores; the frac is that floor "
+                                               "over the measured call time"}}
             metric, unit, value = "Qwen3-235B Q4_0 MoE-layer prefill tokens/s (operator, 4096-token calls)", "tok/s", tok_s
         line = {"metric": metric, "value": round(value, 1), "unit": unit, "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True,

@@ -364,3 +364,43 @@ def test_fp16_kv_cache_close_to_fp32(cuda):
         m16.close()
         ms.close()
         assert berrs.mean() < 3e-3 and bflips == 0, f"{name}: fp16 batch rows differ by {berrs.mean():.2e}"
+
+
+def test_batch_calls_edge_cases(cuda):
+    """Batch of one through the batched path; a sequence stepping past its context raises the
+    device flag (EINVAL) while the others' rows stay valid; the model stays usable; host checks."""
+    import torch
+    cfg = synth.MODEL_CONFIGS["tiny"]
+    ctx = 24
+    m = cuda.Model.from_synth(cfg, 5, ctx)
+    m.set_sequences(3)
+    single = cuda.Model.from_synth(cfg, 5, ctx)
+    p0, p1 = [7, 8, 9, 10], [11] * (ctx - 1)
+    m.forward(p0, 0, seq=0)
+    m.forward(p1, 0, seq=1)
+    lb = m.forward_batch([3], [len(p0)])                       # B = 1
+    single.forward(p0, 0)
+    ls = single.forward([3], len(p0))
+    assert rel_l2(lb[0], ls) < 1e-2                           # the multi-token vs one-token kernels (config 1 noise)
+    # sequence 1 is at its last position: one step fits, the next one is refused
+    tok = torch.tensor([4, 5], dtype=torch.int32, device="cuda")
+    pos = torch.tensor([len(p0) + 1, ctx - 1], dtype=torch.int32, device="cuda")
+    m.decode_batch(tok, pos)
+    m.status()
+    with pytest.raises(cuda.QmsCudaError) as e:               # host entry: checked before launch
+        m.forward_batch([1, 2], [len(p0) + 2, ctx])
+    assert e.value.code == cuda.EINVAL and "context" in str(e.value)
+    m.decode_batch(tok, pos)                                  # device entry: pos[1] == ctx
+    with pytest.raises(cuda.QmsCudaError) as e:
+        m.status()
+    assert e.value.code == cuda.EINVAL and "position" in str(e.value)
+    rows = m.forward_batch([1], [len(p0) + 3])                # still usable after the flag
+    assert np.isfinite(rows).all()
+    m.status()
+    for bad in (lambda: m.forward([1], 0, seq=3), lambda: m.copy_sequence(0, 0, 4),
+                lambda: m.copy_sequence(0, 1, ctx + 1), lambda: m.forward_batch([1] * 4, [0] * 4),
+                lambda: m.set_kv_type(cuda.T_Q4_0)):
+        with pytest.raises(cuda.QmsCudaError):
+            bad()
+    m.close()
+    single.close()

@@ -477,9 +477,13 @@ BATCH_CTX = MODEL_PROMPT + 128                  # positions per sequence's KV ca
 BATCH_OWN = 128                                 # prompt ids of each sequence's own (after a shared prefix)
 
 
-def model_cfg():
+def model_cfg(layers: int = 0):
+    """Config 4 (Qwen3-235B-A22B); layers > 0 keeps that many layers (small cases for ncu captures;
+    a bench line with fewer layers says so in its config)."""
+    import dataclasses
     from large_model_b200 import synth
-    return synth.MODEL_CONFIGS["235b"]
+    cfg = synth.MODEL_CONFIGS["235b"]
+    return dataclasses.replace(cfg, n_layer=layers) if layers > 0 else cfg
 
 
 def model_bytes_per_token(cfg, pos: float, kv_es: int = 4) -> dict:
@@ -637,7 +641,7 @@ def run_model(a):
     if rank == 0 and world == 1 and not a.no_cpu:            # before the GPU model takes host time
         t94, desc, threads = cpu_model_sample()
         cpu = {"value": round(1.0 / t94, 4), "unit": "tok/s", "cores": threads, "kind": "reference", "sample": desc}
-    cfg = model_cfg()
+    cfg = model_cfg(a.model_layers)
     t_build = time.perf_counter()
     m = device_model(q, torch, cfg, 4242 + rank, dev, MODEL_CTX)
     if a.kv == "f16":
@@ -729,7 +733,7 @@ def run_model(a):
             "metric": MODEL_METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
-            "config": {"workload": "Qwen3-235B-A22B (config 4) decode batch 1: 94 layers, 128 experts top-8, Q4_0 "
+            "config": {"workload": f"Qwen3-235B-A22B (config 4) decode batch 1: {cfg.n_layer} layers, 128 experts top-8, Q4_0 "
                                    "weights + Q6_K head drawn on the device (seeded torch RNG), fp32 KV ctx 4096, "
                                    f"{MODEL_PROMPT}-id random prompt prefilled; a step = {per_step} greedy "
                                    f"decode tokens (qms_cuda_decode_step x{per_step} in one CUDA graph)",
@@ -812,7 +816,7 @@ def run_model_batch(a):
         cpu = {"value": round(1.0 / t94, 4), "unit": "tok/s", "cores": threads, "kind": "reference",
                "sample": desc + "; the reference serves one sequence at a time (src/model.h:116-118), so B "
                                 "sequences take B x its bs1 time: the same tok/s"}
-    cfg = model_cfg()
+    cfg = model_cfg(a.model_layers)
     assert a.steps + a.warmup + 8 < BATCH_CTX - MODEL_PROMPT, "steps beyond the sequences' context"
     t_build = time.perf_counter()
     m = device_model(q, torch, cfg, 4242 + rank, dev, BATCH_CTX)
@@ -902,7 +906,7 @@ def run_model_batch(a):
             "metric": BATCH_METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
-            "config": {"workload": f"Qwen3-235B-A22B (config 4) decode, {B} sequences: 94 layers, Q4_0 weights + "
+            "config": {"workload": f"Qwen3-235B-A22B (config 4) decode, {B} sequences: {cfg.n_layer} layers, Q4_0 weights + "
                                    "Q6_K head drawn on the device (seeded torch RNG), fp32 KV caches of "
                                    f"{BATCH_CTX} positions each; a {MODEL_PROMPT}-id random prompt prefilled "
                                    f"once and copied to every sequence, {B} random next tokens; a step = one "
@@ -953,6 +957,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--mode", default="model", choices=["model", "model-bs64", "moe", "bs64", "prefill"])
     ap.add_argument("--batch", type=int, default=BATCH_SEQS, help="sequences in --mode model-bs64")
+    ap.add_argument("--model-layers", type=int, default=0,
+                    help="model modes: keep only this many layers (small cases for profiling; not a bench line)")
     ap.add_argument("--kv", default="f32", choices=["f32", "f16"],
                     help="model modes: KV cache elements (f16: the compacted cache, not the reference's arithmetic)")
     ap.add_argument("--ep", action="store_true", help="batched modes under torchrun: shard the experts over the ranks")

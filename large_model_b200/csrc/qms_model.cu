@@ -74,6 +74,8 @@ struct QmsCudaModel {
     int *xs;
     int *ids, *pos, *sel;
     int *pos_vec;                    // [cap_T] positions of a batched host call
+    float *kpart;                    // partial sums of split multi-token projections
+    size_t kpart_n;
     float *part_o;
     double *part_ml;
     int *ticket, *amax_ticket, *err;
@@ -166,6 +168,7 @@ static int model_reserve(QmsCudaModel *m, int T) {
     const size_t o_sel = take((size_t)m->L * T * m->K * 4);
     const size_t o_po = take((size_t)m->H * m->max_splits * m->D * 4), o_pml = take((size_t)m->H * m->max_splits * 16);
     const size_t o_tk = take((size_t)m->Hk * m->nhb * 4), o_at = take(4), o_amax = take(8);
+    const size_t kpart_n = (size_t)4 * 64 * std::max(m->NQKV, m->E), o_kp = take(kpart_n * 4);
     void *p = nullptr;
     int rc = dmalloc(&p, off, "forward scratch");
     if (rc) return rc;
@@ -201,6 +204,8 @@ static int model_reserve(QmsCudaModel *m, int T) {
     m->ids = (int *)(b + o_ids);
     m->pos = (int *)(b + o_pos);
     m->pos_vec = (int *)(b + o_posv);
+    m->kpart = (float *)(b + o_kp);
+    m->kpart_n = kpart_n;
     m->sel = (int *)(b + o_sel);
     m->part_o = (float *)(b + o_po);
     m->part_ml = (double *)(b + o_pml);
@@ -333,6 +338,8 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
         g.xq = m->xq;
         g.xd = m->xd;
         g.xs = m->xs;
+        g.kpart = m->kpart;
+        g.kpart_n = m->kpart_n;
         if ((rc = launch_proj(L.qkv_type, g, s))) return rc;
         if ((rc = prof_mark(m, ei++, s))) return rc;
         if (pos_vec) {                  // one token per sequence: the decode kernels, Q8 rows out
@@ -365,6 +372,8 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
         g.xq = m->xq;
         g.xd = m->xd;
         g.xs = m->xs;
+        g.kpart = m->kpart;
+        g.kpart_n = m->kpart_n;
         if ((rc = launch_proj(L.o_type, g, s))) return rc;
         if ((rc = prof_mark(m, ei++, s))) return rc;
         // MoE block + residual

@@ -554,16 +554,20 @@ constexpr int kGqDS = kGqKB + 1;                  // floats of one token's chunk
 
 template <int Q1>
 __global__ void __launch_bounds__(128) k_gemm_q4(const GemvArgs a) {
+    // blockIdx.z: this CTA's share of the blocks when they are split over gridDim.z CTAs (each
+    // writes its partial sums to kpart[z][t][r]; k_sum_parts adds them in order)
     __shared__ __align__(16) int8_t sxq[2][32 * kGqXS];
     __shared__ float sdx[2][32 * kGqDS];
     __shared__ int ssx[2][Q1 ? 32 * kGqDS : 1];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
     const int g = lane >> 2, tg = lane & 3;
     const int r0 = (blockIdx.x * (nthr >> 5) + warp) * 16, t0 = blockIdx.y * 32;
-    const int nb = a.ncol / 32, nch = (nb + kGqKB - 1) / kGqKB;
+    const int nb = a.ncol / 32, nchall = (nb + kGqKB - 1) / kGqKB, KS = gridDim.z, z = blockIdx.z;
+    const int cb0 = z * nchall / KS, nch = (z + 1) * nchall / KS - cb0;   // this CTA's chunks [cb0, cb0 + nch)
     pdl_trigger();
     pdl_wait();
-    auto stage = [&](int c, int buf) {                         // chunk c of the tile into buffer buf
+    auto stage = [&](int cl, int buf) {                        // chunk cb0 + cl of the tile into buffer buf
+        const int c = cb0 + cl;
         const int c0 = c * kGqKB, kn = min(kGqKB, nb - c0);
         for (int i = tid; i < 32 * kn * 2; i += nthr) {
             const int t = i / (kn * 2), kb = (i >> 1) % kn, h = i & 1;
@@ -585,8 +589,8 @@ __global__ void __launch_bounds__(128) k_gemm_q4(const GemvArgs a) {
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[j][i] = 0.0f;
     stage(0, 0);
-    for (int c = 0; c < nch; c++) {
-        const int buf = c & 1;
+    for (int cl = 0; cl < nch; cl++) {
+        const int buf = cl & 1, c = cb0 + cl;
         // the chunk's weights into registers first: their round trip overlaps the activations' wait
         const int c0 = c * kGqKB, kn = min(kGqKB, nb - c0);
         uint32_t wq0[kGqKB], wq1[kGqKB];
@@ -601,8 +605,8 @@ __global__ void __launch_bounds__(128) k_gemm_q4(const GemvArgs a) {
             mq0[kb] = Q1 ? h2f(__ldg(reinterpret_cast<const uint16_t *>(wr0 + mpl) + b)) : 0.0f;
             mq1[kb] = Q1 ? h2f(__ldg(reinterpret_cast<const uint16_t *>(wr1 + mpl) + b)) : 0.0f;
         }
-        if (c + 1 < nch) {
-            stage(c + 1, buf ^ 1);
+        if (cl + 1 < nch) {
+            stage(cl + 1, buf ^ 1);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -656,10 +660,29 @@ __global__ void __launch_bounds__(128) k_gemm_q4(const GemvArgs a) {
         for (int i = 0; i < 4; i++) {
             const int t = t0 + 8 * j + 2 * tg + (i & 1), r = r0 + g + 8 * (i >> 1);
             if (t < a.T) {
-                const size_t at = (size_t)t * a.ldy + r;
-                a.y[at] = a.resid ? __fadd_rn(a.resid[at], acc[j][i]) : acc[j][i];
+                if (KS > 1) {
+                    a.kpart[((size_t)z * a.T + t) * a.rows + r] = acc[j][i];
+                } else {
+                    const size_t at = (size_t)t * a.ldy + r;
+                    a.y[at] = a.resid ? __fadd_rn(a.resid[at], acc[j][i]) : acc[j][i];
+                }
             }
         }
+}
+
+// y[t][r] = (resid) + sum over z in order of part[z][t][r]: the split projections' partial sums.
+__global__ void __launch_bounds__(256) k_sum_parts(const float *__restrict__ part, int KS, int T, int rows, float *y,
+                                                  int ldy, const float *resid) {
+    pdl_trigger();
+    pdl_wait();
+    const size_t n = (size_t)T * rows;
+    for (size_t i = (size_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (size_t)gridDim.x * 256) {
+        float v = part[i];
+        for (int z = 1; z < KS; z++) v = __fadd_rn(v, part[(size_t)z * n + i]);
+        const int t = (int)(i / rows), r = (int)(i % rows);
+        const size_t at = (size_t)t * ldy + r;
+        y[at] = resid ? __fadd_rn(resid[at], v) : v;
+    }
 }
 
 // Q6_K rows (the head) on int8 mma.sync, several tokens. A 256-value super-block holds 16
@@ -767,10 +790,30 @@ int launch_gemm_q(int type, const GemvArgs &a, cudaStream_t s) {
                     a.amax == nullptr && a.stride % 16 == 0,
                 QMS_CUDA_EINVAL, "gemm_q: type %d, %d rows of %d", type, a.rows, a.ncol);
     const int wpc = a.rows % 64 == 0 ? 4 : 1;                      // warps (16 rows each) per CTA
-    const dim3 grid(a.rows / (16 * wpc), (a.T + 31) / 32);
+    dim3 grid(a.rows / (16 * wpc), (a.T + 31) / 32);
+    if (type == QMS_T_Q6_K) {
+        QMS_CK(launch_pdl(k_gemm_q6k, grid, dim3(32 * wpc), 0, s, a));
+        return QMS_CUDA_OK;
+    }
+    // Few tiles (a few dozen tokens): split the blocks over up to 4 CTAs per tile so that ~4 CTAs
+    // per SM hide the load latency; the partial sums are added in order by k_sum_parts.
+    int nsm = 148;
+    const int rc = gemv_setup(&nsm);
+    if (rc) return rc;
+    const int tiles = (int)(grid.x * grid.y), nch = (a.ncol / 32 + kGqKB - 1) / kGqKB;
+    int ks = 1;
+    while (ks < 4 && tiles * ks * 2 <= 4 * nsm && ks * 2 <= nch && a.kpart &&
+           (size_t)ks * 2 * a.T * a.rows <= a.kpart_n)
+        ks *= 2;
+    grid.z = ks;
     if (type == QMS_T_Q4_0) QMS_CK(launch_pdl(k_gemm_q4<0>, grid, dim3(32 * wpc), 0, s, a));
-    else if (type == QMS_T_Q4_1) QMS_CK(launch_pdl(k_gemm_q4<1>, grid, dim3(32 * wpc), 0, s, a));
-    else QMS_CK(launch_pdl(k_gemm_q6k, grid, dim3(32 * wpc), 0, s, a));
+    else QMS_CK(launch_pdl(k_gemm_q4<1>, grid, dim3(32 * wpc), 0, s, a));
+    if (ks > 1) {
+        const size_t n = (size_t)a.T * a.rows;
+        const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)4 * nsm);
+        QMS_CK(launch_pdl(k_sum_parts, dim3(blocks), dim3(256), 0, s, (const float *)a.kpart, ks, a.T, a.rows, a.y,
+                          a.ldy, a.resid));
+    }
     return QMS_CUDA_OK;
 }
 

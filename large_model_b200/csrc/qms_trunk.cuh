@@ -56,6 +56,10 @@ struct GemvArgs {
     int *ticket;
     int *tok;
     int *pos;
+    // multi-token projections: scratch for the partial sums when the blocks are split over CTAs
+    // (kpart_n floats; NULL: no split)
+    float *kpart;
+    size_t kpart_n;
 };
 int launch_gemv(int type, const GemvArgs &a, cudaStream_t s);
 // Several tokens (Q8 rows in xq / xd / xs) through Q4_0 / Q4_1 / Q6_K rows on int8 mma.sync;

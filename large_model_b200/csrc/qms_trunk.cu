@@ -1511,7 +1511,15 @@ __global__ void __launch_bounds__(512) k_attn_decode(const AttnArgs a) {
         return;
     }
     const int npos = pos + 1, S = (npos + PB - 1) / PB;
-    if (s >= S) return;
+    if (s >= S) {                                        // no positions here: an empty block for the merge
+        if (lane == 0)
+            for (int k = 0; k < HB; k++) {
+                const size_t slot = ((size_t)z * a.H + g * group + warp * HB + k) * a.max_splits + s;
+                a.part_ml[slot * 2] = -INFINITY;
+                a.part_ml[slot * 2 + 1] = 0.0;
+            }
+        return;
+    }
     const int p0 = s * PB, p1 = min(npos, p0 + PB), np = p1 - p0;
     const int KD = a.Hk * D;
     const size_t cb = (size_t)z * a.seq_stride;          // this sequence's caches (0 for one sequence)
@@ -1656,9 +1664,9 @@ __global__ void __launch_bounds__(4 * D) k_attn_merge(const AttnArgs a, int8_t *
     const int h = blockIdx.x, z = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_trigger();
     pdl_wait();
-    const int pos = a.pos_vec ? a.pos_vec[z] : *a.pos;
-    if (pos < 0 || pos >= a.ctx) return;
-    const int S = (pos + kAttnBlock) / kAttnBlock;      // <= NT (the launch checks ctx)
+    // every block slot: the ones past the position hold an empty block (m = -inf, l = 0), so the
+    // position need not be read first (one dependent round trip less); their weights are zero
+    const int S = a.max_splits;                         // <= NT (the launch checks ctx)
     const size_t base = ((size_t)z * a.H + h) * a.max_splits;
     const bool own = tid < S;
     const double mq = own ? __ldcg(a.part_ml + (base + tid) * 2) : -INFINITY;
@@ -1684,7 +1692,7 @@ __global__ void __launch_bounds__(4 * D) k_attn_merge(const AttnArgs a, int8_t *
 #pragma unroll
         for (int u = 0; u < 8; u++) {
             const int q = q0 + 4 * u;
-            v[u] = q < S ? __ldcg(a.part_o + (base + q) * D + d) : 0.0f;
+            v[u] = q < S && f[q] != 0.0f ? __ldcg(a.part_o + (base + q) * D + d) : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < 8; u++)

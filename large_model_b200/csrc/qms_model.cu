@@ -49,7 +49,7 @@ struct QmsCudaModel {
     int L, E, H, Hk, D, X, K, F, V, ctx;
     float eps;
     double rope_base;
-    int QD, KD, NQKV, group, nhb;
+    int QD, KD, NQKV, group;
     int embd_type;
     uint8_t *embd;                   // GGUF rows
     float *out_norm;
@@ -78,7 +78,7 @@ struct QmsCudaModel {
     size_t kpart_n;
     float *part_o;
     double *part_ml;
-    int *ticket, *amax_ticket, *err;
+    int *amax_ticket, *err;
     unsigned long long *amax;
     int max_splits;
     int *h_pinned;                   // host mirror of ids + pos for the host entry point
@@ -167,7 +167,7 @@ static int model_reserve(QmsCudaModel *m, int T) {
     const size_t o_ids = take((size_t)T * 4), o_pos = take(4), o_posv = take((size_t)T * 4);
     const size_t o_sel = take((size_t)m->L * T * m->K * 4);
     const size_t o_po = take((size_t)m->H * m->max_splits * m->D * 4), o_pml = take((size_t)m->H * m->max_splits * 16);
-    const size_t o_tk = take((size_t)m->Hk * m->nhb * 4), o_at = take(4), o_amax = take(8);
+    const size_t o_at = take(4), o_amax = take(8);
     const size_t kpart_n = (size_t)4 * 64 * std::max(m->NQKV, m->E), o_kp = take(kpart_n * 4);
     void *p = nullptr;
     int rc = dmalloc(&p, off, "forward scratch");
@@ -209,7 +209,6 @@ static int model_reserve(QmsCudaModel *m, int T) {
     m->sel = (int *)(b + o_sel);
     m->part_o = (float *)(b + o_po);
     m->part_ml = (double *)(b + o_pml);
-    m->ticket = (int *)(b + o_tk);
     m->amax_ticket = (int *)(b + o_at);
     m->err = m->flags;
     m->amax = (unsigned long long *)(b + o_amax);
@@ -266,11 +265,9 @@ static int forward_core(QmsCudaModel *m, const int *ids, int T, const int *pos, 
     at.Hk = m->Hk;
     at.D = m->D;
     at.scale = 1.0 / sqrt((double)m->D);
-    at.split = 0;                    // several tokens: one CTA per head group and token
     at.max_splits = m->max_splits;
     at.part_o = m->part_o;
     at.part_ml = m->part_ml;
-    at.ticket = m->ticket;
     at.out = m->att;
     at.err = m->err;
     for (int l = 0; l < m->L; l++) {
@@ -532,7 +529,6 @@ int qms_cuda_model_create(const QmsCudaModelDesc *d, QmsCudaModel **out) {
     m->KD = d->n_head_kv * d->head_dim;
     m->NQKV = QD + 2 * m->KD;
     m->group = group;
-    m->nhb = group / HB;
     m->embd_type = et;
     m->head_type = ht;
     m->max_splits = (d->ctx + kSplit - 1) / kSplit;

@@ -893,21 +893,13 @@ __global__ void __launch_bounds__(128) k_attention(const AttnArgs a) {
     const int g = blockIdx.x / nhb, hb = blockIdx.x % nhb;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = g * group + hb * HB + warp;
-    const int t = blockIdx.z, s = blockIdx.y;
-    __shared__ int s_last;
+    const int t = blockIdx.z;
     pdl_trigger();
     pdl_wait();
     const int pt = a.pos_vec ? a.pos_vec[t] : *a.pos + t;
     if (pt < 0 || pt >= a.ctx) return;           // k_qk_rope has flagged it
     const size_t cb = a.pos_vec ? (size_t)t * a.seq_stride : 0;
-    const int npos = pt + 1;
-    int p0 = 0, p1 = npos, S = 1;
-    if (a.split > 0) {
-        S = (npos + a.split - 1) / a.split;
-        if (s >= S) return;
-        p0 = s * a.split;
-        p1 = min(npos, p0 + a.split);
-    }
+    const int p1 = pt + 1;                       // positions 0 .. pt (causal)
     const int KD = a.Hk * D;
     const float *qh = a.qkv + (size_t)t * a.ldq + (size_t)h * D;
     const int k16 = lane & 15, half = lane >> 4;
@@ -919,7 +911,7 @@ __global__ void __launch_bounds__(128) k_attention(const AttnArgs a) {
 #pragma unroll
     for (int d = 0; d < DPL; d++) o[d] = 0.0f;
     double m = -INFINITY, l = 0.0;
-    for (int pc = p0; pc < p1; pc += 32) {
+    for (int pc = 0; pc < p1; pc += 32) {
         float mydot = 0.0f;
 #pragma unroll 4
         for (int j = 0; j < 16; j++) {
@@ -966,51 +958,8 @@ __global__ void __launch_bounds__(128) k_attention(const AttnArgs a) {
         }
     }
     float *out = a.out + (size_t)t * a.H * D + (size_t)h * D + lane * DPL;
-    if (S == 1) {
 #pragma unroll
-        for (int d = 0; d < DPL; d++) out[d] = (float)((double)o[d] / l);
-        return;
-    }
-    // split: publish this split's (m, l, o); the last CTA of the head group merges them
-    const size_t slot = (size_t)h * a.max_splits + s;
-#pragma unroll
-    for (int d = 0; d < DPL; d++) a.part_o[slot * D + lane * DPL + d] = o[d];
-    if (lane == 0) {
-        a.part_ml[slot * 2] = m;
-        a.part_ml[slot * 2 + 1] = l;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        s_last = atomicAdd(a.ticket + blockIdx.x, 1) == S - 1;
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    const size_t base = (size_t)h * a.max_splits;
-    double M = -INFINITY;
-    for (int q = lane; q < S; q += 32) M = fmax(M, __ldcg(a.part_ml + (base + q) * 2));
-    M = warp_max_d(M);
-    double Z = 0.0;
-    for (int q = lane; q < S; q += 32) Z += __ldcg(a.part_ml + (base + q) * 2 + 1) * exp(__ldcg(a.part_ml + (base + q) * 2) - M);
-    Z = warp_sum_d(Z);
-    float acc[DPL];
-#pragma unroll
-    for (int d = 0; d < DPL; d++) acc[d] = 0.0f;
-    for (int q0 = 0; q0 < S; q0 += 32) {
-        const float f = q0 + lane < S ? (float)exp(__ldcg(a.part_ml + (base + q0 + lane) * 2) - M) : 0.0f;
-        const int nq = min(32, S - q0);
-        for (int q = 0; q < nq; q++) {
-            const float w = __shfl_sync(kFull, f, q);
-            const float *po = a.part_o + (base + q0 + q) * D + lane * DPL;
-#pragma unroll
-            for (int d = 0; d < DPL; d++) acc[d] = __fmaf_rn(w, __ldcg(po + d), acc[d]);
-        }
-    }
-#pragma unroll
-    for (int d = 0; d < DPL; d++) out[d] = (float)((double)acc[d] / Z);
-    __syncthreads();
-    if (threadIdx.x == 0) a.ticket[blockIdx.x] = 0;
+    for (int d = 0; d < DPL; d++) out[d] = (float)((double)o[d] / l);
 }
 
 // One CTA per row: the largest argmax_key (NaN never wins, ties to the lower index).
@@ -1048,7 +997,7 @@ int launch_argmax_rows(const float *logits, int ld, int B, int V, int *tok, int 
 
 int launch_attention(const AttnArgs &a, cudaStream_t s) {
     const int group = a.H / a.Hk, HB = attention_heads_per_cta(group);
-    const dim3 grid(a.Hk * (group / HB), a.split > 0 ? a.max_splits : 1, a.T);
+    const dim3 grid(a.Hk * (group / HB), 1, a.T);
     if (a.D == 128) {
         if (a.kv16) QMS_CK(launch_pdl(k_attention<128, __half>, grid, dim3(32 * HB), 0, s, a));
         else QMS_CK(launch_pdl(k_attention<128, float>, grid, dim3(32 * HB), 0, s, a));

@@ -98,11 +98,9 @@ struct AttnArgs {
                                       // the new K / V rows already in the cache (k_qk_rope ran)
     int T, ctx, H, Hk, D;
     double scale;                     // 1/sqrt(D)
-    int split;                        // positions per CTA when T == 1 (0: one CTA per head group)
     int max_splits;
     float *part_o;                    // one-token attention partials [T][H][max_splits][D]
     double *part_ml;                  // [T][H][max_splits][2]
-    int *ticket;                      // [Hk * head blocks]
     float *out;                       // [T][H*D]
     int *err;
 };

@@ -290,7 +290,7 @@ def run_batched(a):
         from large_model_b200.ep import CudaBackend, ExpertParallelMoe
         per = X // world
         layers = [device_layer(q, torch, 500 + 17 * i, dev, shard=(rank * per, per), zipf=zipf) for i in range(2)]
-        eps = [ExpertParallelMoe(CudaBackend(m), X, K, E) for m in layers]
+        eps = [ExpertParallelMoe(CudaBackend(m), X, K, E, max_tokens=T) for m in layers]
     else:
         layers = [device_layer(q, torch, 500 + 17 * i, dev, zipf=zipf) for i in range(2)]
     g = torch.Generator(device=dev)
@@ -402,8 +402,9 @@ def run_batched(a):
                        "pinned host memory; max over ranks"}
     # kernels of this library per call (the routing, grouping, expert and combine kernels of the path
     # the call takes; torch's own copies and all-to-alls under EP not counted)
-    gemv = T * K <= 24 * (X // world if ep else X)
-    per_call = (10 if gemv else 11) if ep else (7 if gemv else 9)
+    # (under EP the expert kernels see every segment entry: world * T * K slots over X / world experts)
+    gemv = world * T * K <= 24 * (X // world) if ep else T * K <= 24 * X
+    per_call = (11 if gemv else 12) if ep else (7 if gemv else 9)
     launches = per_call * calls * a.steps
     if rank == 0:
         if a.mode == "bs64":

@@ -140,6 +140,38 @@ int qms_cuda_moe_experts_q8(QmsCudaMoe *m, const QmsQ8 *xq, const int *expert, i
 int qms_cuda_moe_combine(const float *dn, const float *wts, int T, int n_used, int n_embd, const float *resid,
                          float *out, void *stream);
 
+/* ---- expert parallelism with fixed-capacity buffers (no counterpart in the CPU-only reference;
+ * each slot's arithmetic is moe_group_fast's, src/model.c:979-1005, and the combine order is
+ * src/model.c:1152-1162) -------------------------------------------------------------------------
+ * Rank r of n_rank holds experts [r * n_expert / n_rank, (r + 1) * n_expert / n_rank) as a shard
+ * layer. One layer call on every rank, with nothing read back to the host:
+ *   1. qms_cuda_moe_route                      sel, wts for its T tokens;
+ *   2. qms_cuda_ep_pack                        send_x / send_e: n_rank segments of cap entries;
+ *   3. all-to-all of segment o to rank o       send_x (cap * n_embd/32 QmsQ8 blocks per segment)
+ *                                              and send_e (cap ints per segment) -> recv_x, recv_e;
+ *   4. qms_cuda_moe_experts_q8(shard, recv_x, recv_e, n_rank * cap, dn_recv): unused entries
+ *      carry id -1 and are skipped;
+ *   5. all-to-all of dn_recv (cap * n_embd floats per segment) back -> ret;
+ *   6. qms_cuda_ep_combine(ret, slot, wts, ...).
+ * Every segment has the same size on every rank, so the exchange needs no counts: NCCL
+ * send/recv pairs in one group from C, or all_to_all_single. cap = (largest T of any rank) *
+ * n_used never overflows; a smaller cap moves fewer bytes, and a slot past its segment's capacity
+ * is dropped, sets *err (when err is not NULL) and makes its token's output NaN.
+ *
+ * Pack: sel [T][n_used] global expert ids (selection order), xn [T][n_embd] fp32; writes the
+ * owner's local expert id of every used entry and -1 of every unused one into send_e
+ * [n_rank][cap], each token's Q8 row (the reference's quantiser) into send_x [n_rank][cap][n_embd/32]
+ * at every entry one of its slots was given, and slot [T][n_used] = o * cap + (index of the slot
+ * among the slots owned by o, in slot order), or -1 when dropped. T may be 0 (send_e is still
+ * cleared). n_rank <= 64 and n_expert % n_rank == 0. Device buffers; no host synchronisation. */
+int qms_cuda_ep_pack(const float *xn, const int *sel, int T, int n_used, int n_embd, int n_expert, int n_rank,
+                     int cap, QmsQ8 *send_x, int *send_e, int *slot, int *err, void *stream);
+/* out[t] = resid[t] + sum_j wts[t][j] * ret[slot[t][j]] in selection order, the arithmetic of
+ * qms_cuda_moe_combine: ret [n_rank * cap][n_embd] holds the down rows returned by step 5;
+ * resid may be NULL. T <= 65535. Device buffers. */
+int qms_cuda_ep_combine(const float *ret, const int *slot, const float *wts, int T, int n_used, int n_embd,
+                        const float *resid, float *out, void *stream);
+
 /* ---- chat path: token sampling on the device (src/chat.c:27-69) -------------------------------- */
 
 /* One draw of the reference's sampler, sample() (src/chat.c:36-69), on device memory: logits

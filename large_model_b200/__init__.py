@@ -92,6 +92,8 @@ def lib() -> C.CDLL:
     L.qms_cuda_moe_experts_q8.argtypes = [vp, vp, vp, i32, vp, vp]
     L.qms_cuda_sample.argtypes = [vp, i32, C.c_float, C.c_float, i32, vp, vp, vp]
     L.qms_cuda_moe_combine.argtypes = [vp, vp, i32, i32, i32, vp, vp, vp]
+    L.qms_cuda_ep_pack.argtypes = [vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]
+    L.qms_cuda_ep_combine.argtypes = [vp, vp, vp, i32, i32, i32, vp, vp, vp]
     L.qms_cuda_model_create.argtypes = [C.POINTER(ModelDesc), C.POINTER(vp)]
     L.qms_cuda_model_set_layer.argtypes = [vp, i32, C.POINTER(LayerDesc)]
     L.qms_cuda_model_free.argtypes = [vp]
@@ -338,6 +340,35 @@ def combine(dn, wts, resid=None, out=None, stream=None):
     if out is None:
         out = torch.empty((T, E), dtype=torch.float32, device=dn.device)
     check(lib().qms_cuda_moe_combine(_ptr(dn), _ptr(wts), T, K, E, _ptr(resid), _ptr(out), _stream(stream)))
+    return out
+
+
+def ep_pack(xn, sel, n_expert: int, n_rank: int, cap: int, err=None, stream=None):
+    """Expert-parallel dispatch buffers on the device (qms_cuda_ep_pack): xn CUDA float32 [T][E],
+    sel CUDA int32 [T][K]. Returns (send_x uint8 [n_rank * cap][E/32 * 44] of QmsQ8 rows,
+    send_e int32 [n_rank * cap] local expert ids or -1, slot int32 [T][K] entry of each slot or -1);
+    err (CUDA int32 [1] or None) gets bit 0 set when a slot does not fit its segment."""
+    torch = _torch()
+    xn, sel = xn.contiguous(), sel.contiguous()
+    T, K = sel.shape
+    E = xn.shape[-1]
+    send_x = torch.empty((n_rank * cap, E // 32 * 44), dtype=torch.uint8, device=xn.device)
+    send_e = torch.empty((n_rank * cap,), dtype=torch.int32, device=xn.device)
+    slot = torch.empty((T, K), dtype=torch.int32, device=xn.device)
+    check(lib().qms_cuda_ep_pack(_ptr(xn), _ptr(sel), T, K, E, n_expert, n_rank, cap, _ptr(send_x), _ptr(send_e),
+                                 _ptr(slot), _ptr(err), _stream(stream)))
+    return send_x, send_e, slot
+
+
+def ep_combine(ret, slot, wts, resid=None, out=None, stream=None):
+    """out[t] = resid[t] + sum_j wts[t][j] * ret[slot[t][j]] in selection order (qms_cuda_ep_combine)."""
+    torch = _torch()
+    T, K = wts.shape
+    E = ret.shape[-1]
+    if out is None:
+        out = torch.empty((T, E), dtype=torch.float32, device=ret.device)
+    check(lib().qms_cuda_ep_combine(_ptr(ret), _ptr(slot), _ptr(wts), T, K, E, _ptr(resid), _ptr(out),
+                                    _stream(stream)))
     return out
 
 

@@ -143,3 +143,23 @@ def test_noalloc_route_validates_before_any_device_call():
     assert L.qms_cuda_moe_route_noalloc(None, 128, 4096, 8, p, 1, p, p, None, None) == q.EINVAL
     assert L.qms_cuda_moe_route_noalloc(p, 128, 4096, 8, p, 1, None, p, None, None) == q.EINVAL
     assert L.qms_cuda_moe_route_noalloc(C.c_void_p(260), 128, 4096, 8, p, 1, p, p, None, None) == q.EINVAL  # router alignment
+
+
+def test_ep_calls_validate_before_any_device_call():
+    """qms_cuda_ep_pack / qms_cuda_ep_combine refuse bad shapes, splits and pointers on the host."""
+    L = q.lib()
+    p = C.c_void_p(256)
+    #                      xn sel T  K  E    X    N   cap send_x send_e slot err stream
+    assert L.qms_cuda_ep_pack(p, p, 4, 4, 500, 32, 2, 16, p, p, p, None, None) == q.EINVAL       # n_embd % 32
+    assert L.qms_cuda_ep_pack(p, p, 4, 4, 512, 32, 3, 16, p, p, p, None, None) == q.EUNSUPPORTED  # 32 experts over 3
+    assert L.qms_cuda_ep_pack(p, p, 4, 4, 512, 130, 65, 16, p, p, p, None, None) == q.EUNSUPPORTED  # > 64 ranks
+    assert L.qms_cuda_ep_pack(p, p, 4, 4, 512, 32, 2, 0, p, p, p, None, None) == q.EINVAL        # cap 0
+    assert L.qms_cuda_ep_pack(p, p, -1, 4, 512, 32, 2, 16, p, p, p, None, None) == q.EINVAL      # T < 0
+    assert L.qms_cuda_ep_pack(p, p, 1 << 29, 8, 512, 32, 2, 16, p, p, p, None, None) == q.EINVAL  # slots overflow
+    assert L.qms_cuda_ep_pack(p, None, 4, 4, 512, 32, 2, 16, p, p, p, None, None) == q.EINVAL    # no sel
+    assert L.qms_cuda_ep_pack(None, None, 0, 4, 512, 32, 2, 16, None, p, None, None, None) == q.EINVAL  # no send_x
+    assert L.qms_cuda_ep_pack(p, p, 4, 4, 512, 32, 2, 16, C.c_void_p(258), p, p, None, None) == q.EINVAL  # alignment
+    assert "aligned" in L.qms_cuda_last_error().decode()
+    assert L.qms_cuda_ep_combine(None, p, p, 4, 4, 512, None, p, None) == q.EINVAL
+    assert L.qms_cuda_ep_combine(p, p, p, 70000, 4, 512, None, p, None) == q.EINVAL              # T > 65535
+    assert L.qms_cuda_ep_combine(p, p, p, 0, 4, 512, None, p, None) == q.OK                      # nothing to do

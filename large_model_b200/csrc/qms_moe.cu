@@ -643,26 +643,27 @@ int64_t qms_cuda_moe_device_bytes(const QmsCudaMoe *m) {
     return (int64_t)(m->weight_bytes + m->scratch_bytes) + (int64_t)m->io_cap_T * m->E * 8;
 }
 
-int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
-    QMS_REQUIRE(m && T >= 0, QMS_CUDA_EINVAL, "moe_reserve: bad arguments");
-    QMS_REQUIRE((int64_t)T * m->K <= 65535, QMS_CUDA_EINVAL, "moe: T * n_used must be <= 65535");
-    int rc = ensure_device(m->device);
-    if (rc) return rc;
-    if (m->mma_min_t > 0 && T >= m->mma_min_t && (rc = mma_reserve(m, T))) return rc;
-    if (T <= m->cap_T) return QMS_CUDA_OK;
+// Scratch for calls of up to T tokens (forward, route: T Q8 rows, T * K slots) and expert calls of
+// up to `rows` slots (qms_cuda_moe_experts*: one Q8 row and one SwiGLU row per slot). Both only grow.
+static int reserve_scratch(QmsCudaMoe *m, int T, int rows) {
+    T = std::max(T, m->cap_T);
+    rows = std::max(rows, m->cap_rows);
+    if (m->scratch && T == m->cap_T && rows == m->cap_rows) return QMS_CUDA_OK;
     const size_t TK = (size_t)T * m->K;
+    const size_t R = std::max((size_t)T, (size_t)rows);        // Q8 activation rows
+    const size_t RS = std::max(TK, (size_t)rows);               // slot rows (SwiGLU, Q8 groups, arrivals)
     size_t off = 0;
-    const size_t o_xq_q = off; off += al256((size_t)T * m->E);
-    const size_t o_xq_d = off; off += al256((size_t)T * m->nbE * 4);
-    const size_t o_xq_s = off; off += al256((size_t)T * m->nbE * 4);
+    const size_t o_xq_q = off; off += al256(R * m->E);
+    const size_t o_xq_d = off; off += al256(R * m->nbE * 4);
+    const size_t o_xq_s = off; off += al256(R * m->nbE * 4);
     const size_t o_log = off; off += al256((size_t)T * m->X * 4);
     const size_t o_sel = off; off += al256(TK * 4);
     const size_t o_wts = off; off += al256(TK * 4);
-    const size_t o_act = off; off += al256(TK * m->F * 4);
-    const size_t o_aq_q = off; off += al256(TK * m->F);
-    const size_t o_aq_d = off; off += al256(TK * m->nbF * 4);
-    const size_t o_aq_s = off; off += al256(TK * m->nbF * 4);
-    const size_t o_cnt = off; off += al256((1 + TK * m->nbF) * 4);
+    const size_t o_act = off; off += al256(RS * m->F * 4);
+    const size_t o_aq_q = off; off += al256(RS * m->F);
+    const size_t o_aq_d = off; off += al256(RS * m->nbF * 4);
+    const size_t o_aq_s = off; off += al256(RS * m->nbF * 4);
+    const size_t o_cnt = off; off += al256((1 + RS * m->nbF) * 4);
     const size_t o_err = off; off += 256;
     StreamScratch ss;
     stream_scratch_sizes(m, &ss);
@@ -704,7 +705,32 @@ int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
     m->part_gu = (unsigned long long *)(b + o_pgu);
     m->fin = (unsigned long long *)(b + o_fin);
     m->cap_T = T;
+    m->cap_rows = rows;
     return QMS_CUDA_OK;
+}
+
+int qms_cuda_moe_reserve(QmsCudaMoe *m, int T) {
+    QMS_REQUIRE(m && T >= 0, QMS_CUDA_EINVAL, "moe_reserve: bad arguments");
+    QMS_REQUIRE((int64_t)T * m->K <= 65535, QMS_CUDA_EINVAL, "moe: T * n_used must be <= 65535");
+    int rc = ensure_device(m->device);
+    if (rc) return rc;
+    if (m->mma_min_t > 0 && T >= m->mma_min_t && (rc = mma_reserve(m, T))) return rc;
+    if (T <= m->cap_T) return QMS_CUDA_OK;
+    return reserve_scratch(m, T, 0);
+}
+
+// Rows of one expert call: the grouped kernels' tile grids (S / 64 + X tiles) stay within 65535.
+constexpr int kMaxExpertRows = 1 << 21;
+
+// Expert calls of S slots: S Q8 rows and S SwiGLU rows in the scratch (the grouped kernels'
+// workspace is sized by mma_core itself). Outside graph capture only.
+static int reserve_expert_rows(QmsCudaMoe *m, int S, cudaStream_t s, const char *who) {
+    if (S <= std::max(m->cap_T, m->cap_rows)) return QMS_CUDA_OK;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    QMS_CK(cudaStreamIsCapturing(s, &cs));
+    QMS_REQUIRE(cs == cudaStreamCaptureStatusNone, QMS_CUDA_EINVAL,
+                "%s: scratch for %d slots must be reserved before graph capture", who, S);
+    return reserve_scratch(m, 0, S);           // (cudaFree of the old scratch waits for the device)
 }
 
 int qms_cuda_moe_forward(QmsCudaMoe *m, const float *xn, int T, float *out, int *sel, float *wts, float *logits,
@@ -809,16 +835,10 @@ int qms_cuda_moe_experts(QmsCudaMoe *m, const float *x, const int *expert, int S
     if (S == 0) return QMS_CUDA_OK;
     QMS_REQUIRE(x && expert && dn, QMS_CUDA_EINVAL, "moe_experts: NULL x, expert or dn");
     QMS_REQUIRE(m->mma_min_t > 0, QMS_CUDA_EUNSUPPORTED, "moe_experts: the grouped tensor-core path is off for this layer");
+    QMS_REQUIRE(S <= kMaxExpertRows, QMS_CUDA_EINVAL, "moe_experts: %d rows (at most %d per call)", S, kMaxExpertRows);
     int rc = ensure_device(m->device);
     if (rc) return rc;
-    const int T = (S + m->K - 1) / m->K;                 // scratch holds S rows of x and S SwiGLU rows
-    if (S > m->cap_T || T > m->cap_T) {
-        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        QMS_CK(cudaStreamIsCapturing((cudaStream_t)stream, &cs));
-        QMS_REQUIRE(cs == cudaStreamCaptureStatusNone, QMS_CUDA_EINVAL,
-                    "moe_experts: scratch for %d slots must be reserved before graph capture", S);
-        if ((rc = qms_cuda_moe_reserve(m, S))) return rc;
-    }
+    if ((rc = reserve_expert_rows(m, S, (cudaStream_t)stream, "moe_experts"))) return rc;
     const cudaStream_t s = (cudaStream_t)stream;
     const int64_t nblocks = (int64_t)S * m->nbE;
     k_quantize_rows<<<(unsigned)std::min<int64_t>((nblocks + 7) / 8, 4096), 256, 0, s>>>(x, nblocks, m->xq_q, m->xq_d,
@@ -832,16 +852,10 @@ int qms_cuda_moe_experts_q8(QmsCudaMoe *m, const QmsQ8 *xq, const int *expert, i
     if (S == 0) return QMS_CUDA_OK;
     QMS_REQUIRE(xq && expert && dn, QMS_CUDA_EINVAL, "moe_experts_q8: NULL xq, expert or dn");
     QMS_REQUIRE(m->mma_min_t > 0, QMS_CUDA_EUNSUPPORTED, "moe_experts_q8: the grouped path is off for this layer");
+    QMS_REQUIRE(S <= kMaxExpertRows, QMS_CUDA_EINVAL, "moe_experts_q8: %d rows (at most %d per call)", S, kMaxExpertRows);
     int rc = ensure_device(m->device);
     if (rc) return rc;
-    const int T = (S + m->K - 1) / m->K;
-    if (S > m->cap_T || T > m->cap_T) {
-        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        QMS_CK(cudaStreamIsCapturing((cudaStream_t)stream, &cs));
-        QMS_REQUIRE(cs == cudaStreamCaptureStatusNone, QMS_CUDA_EINVAL,
-                    "moe_experts_q8: scratch for %d slots must be reserved before graph capture", S);
-        if ((rc = qms_cuda_moe_reserve(m, S))) return rc;
-    }
+    if ((rc = reserve_expert_rows(m, S, (cudaStream_t)stream, "moe_experts_q8"))) return rc;
     const cudaStream_t s = (cudaStream_t)stream;
     const int64_t nblocks = (int64_t)S * m->nbE;
     k_unpack_q8<<<(unsigned)std::min<int64_t>((nblocks + 255) / 256, 4096), 256, 0, s>>>(xq, nblocks, m->xq_q, m->xq_d,

@@ -173,8 +173,9 @@ struct QmsCudaMoe {
     int stream_ok;       // batch-1 streaming kernels usable for this shape
     int mma_min_t;       // T from which the grouped kernels run (0: never)
     int gemv;            // grouped GEMV (CUDA cores) for calls of few slots per expert
-    // scratch, sized for cap_T tokens
+    // scratch, sized for cap_T tokens and for expert calls of cap_rows slots
     int cap_T;
+    int cap_rows;
     void *scratch;
     size_t scratch_bytes;
     int8_t *xq_q;

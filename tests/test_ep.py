@@ -412,3 +412,30 @@ def test_ep_pack_overflow_is_flagged_on_one_gpu():
     assert torch.isnan(out[lost]).all(dim=1).all()
     assert torch.equal(out[~lost], full_out[~lost])
     sh.close()
+
+
+@pytest.mark.gpu
+def test_expert_calls_beyond_the_token_scratch():
+    """An expert call of 20000 rows (a rank's segments at prefill sizes; more than the 65535 / K
+    tokens a forward call may reserve) runs, and each row equals the same rows run in 5000-row
+    calls bit for bit (both sizes take the 64-slot tensor-core tiles)."""
+    import large_model_b200 as lmb
+    lmb.init(0)
+    layer = synth.make_moe_layer("tiny", seed=52)
+    per = layer.n_expert // 2
+    sh = lmb.MoeLayer.shard_from_synth(layer, per, per)
+    S = 20000
+    g = torch.Generator().manual_seed(5)
+    x = torch.from_numpy(synth.make_hidden(layer.n_embd, S, seed=53)).cuda()
+    ids = torch.randint(-1, per, (S,), generator=g).to(torch.int32).cuda()    # -1: unused entries
+    xq = lmb.quantize_q8(x)
+    whole = sh.experts_q8(xq, ids, dn=torch.zeros((S, layer.n_embd), device="cuda"))
+    parts = torch.zeros_like(whole)
+    for c in range(0, S, 5000):
+        sh.experts_q8(xq[c:c + 5000], ids[c:c + 5000], dn=parts[c:c + 5000])
+    torch.cuda.synchronize()
+    sh.status()
+    assert torch.equal(whole, parts)
+    used = ids >= 0
+    assert bool(torch.isfinite(whole[used]).all()) and bool((whole[used] != 0).any())
+    sh.close()

@@ -450,10 +450,12 @@ def run_batched(a):
                            "l2": "inputs larger than L2 (2 layers x 1.36 GB resident)",
                            "routing": (f"Zipf({a.zipf}) expert popularity (config 5): a shared hidden-state "
                                        f"component and per-expert router offsets; per call the busiest expert "
-                                       f"takes {max_expert} of {T * K} slots"
+                                       f"takes {max_expert} of {T * K * (world if ep else 1)} slots"
+                                       f"{' (all ranks: each rank its own T tokens)' if ep else ''}"
                                        if a.zipf > 0 else
                                        "seeded N(0,1) hidden states, N(0,0.02) router (near-uniform expert load)"),
-                           "parallelism": f"expert-parallel x{world} (NCCL all-to-all)" if ep else f"replicas x{world}"},
+                           "parallelism": (f"expert-parallel x{world} (device dispatch into fixed-capacity segments, "
+                                           f"NCCL all-to-all)" if ep else f"replicas x{world}")},
                 "roofline": roof, "cpu_baseline": cpu,
                 "e2e": e2e,
                 "gpu_launches": launches, "clocks": clocks}

@@ -439,3 +439,29 @@ def test_expert_calls_beyond_the_token_scratch():
     used = ids >= 0
     assert bool(torch.isfinite(whole[used]).all()) and bool((whole[used] != 0).any())
     sh.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cap", [5600, 700])
+def test_ep_pack_many_chunks_matches_restatement(cap):
+    """qms_cuda_ep_pack over 5600 slots (the index kernel's 1024-slot chunks carry each owner's
+    running count from chunk to chunk) with skewed expert ids over 4 ranks: slot map, ids, rows
+    and overflow flag equal the host restatement; cap 700 drops slots in later chunks."""
+    import large_model_b200 as lmb
+    lmb.init(0)
+    T, K, E, X, N = 700, 8, 512, 128, 4
+    g = torch.Generator().manual_seed(9)
+    w = torch.arange(1, X + 1, dtype=torch.float64).pow(-1.1)                   # Zipf-like popularity
+    sel = torch.multinomial(w.expand(T, X), K, replacement=False, generator=g).to(torch.int32)
+    x = torch.from_numpy(synth.make_hidden(E, T, seed=54)).cuda()
+    err = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    sx, se, slot = lmb.ep_pack(x, sel.cuda(), X, N, cap, err=err)
+    ref_slot, ref_ids, dropped = pack_index(sel, X, N, cap)
+    torch.cuda.synchronize()
+    assert torch.equal(slot.cpu(), ref_slot)
+    assert torch.equal(se.cpu(), ref_ids)
+    assert int(err.item()) == int(dropped) and dropped == (cap == 700)     # owner 0 gets 4138 slots
+    s = slot.reshape(-1).long()
+    kept = s >= 0
+    rows = lmb.quantize_q8(x).repeat_interleave(K, dim=0)
+    assert torch.equal(sx[s[kept]], rows[kept])

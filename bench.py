@@ -559,8 +559,8 @@ def host_model_tensors(cfg, seed: int) -> dict:
 def cpu_model_sample(layers=(2, 8), decode_tokens: int = 8, prompt: int = 256, seed: int = 77):
     """The reference's own qms_forward (oracle/_ref, compiled from its sources) on 235B-shape models
     of `layers` layers in host RAM (the full 94-layer model needs ~135 GB of host memory): each
-    model prefills a random prompt, then decodes `decode_tokens` tokens one call at a time. The time
-    per token is linear in the layer count (t = fixed + L * per_layer: embedding and head, then
+    model prefills a random prompt, then the sizes decode `decode_tokens` tokens each, one call at a
+    time and interleaved (both see the same host load). The time per token is linear in the layer count (t = fixed + L * per_layer: embedding and head, then
     identical layers), so two sizes give the 94-layer time. Returns (seconds per 94-layer token,
     description, threads)."""
     import dataclasses
@@ -569,32 +569,48 @@ def cpu_model_sample(layers=(2, 8), decode_tokens: int = 8, prompt: int = 256, s
     threads = host_threads()
     ref.set_threads(threads)
     base = model_cfg()
-    per_tok = {}
-    for L in layers:
-        cfg = dataclasses.replace(base, n_layer=L)
-        t = host_model_tensors(cfg, seed)
-        m = ref.model(cfg, t, prompt + decode_tokens + 4)
-        ids = [int(v) for v in np.random.default_rng(seed).integers(0, cfg.vocab, prompt)]
-        logits = m.forward(ids, 0)
-        nxt = int(np.argmax(logits))
-        m.forward([nxt], prompt)                                   # warm-up (thread pool, page-in)
-        ts = []
-        for k in range(decode_tokens):
-            t0 = time.perf_counter()
-            logits = m.forward([int(np.argmax(logits))], prompt + 1 + k)
-            ts.append(time.perf_counter() - t0)
-        per_tok[L] = statistics.median(ts)
-        m.close()
-        del t
+    attempts = 3
+    models = {}
+    try:
+        for L in layers:
+            cfg = dataclasses.replace(base, n_layer=L)
+            t = host_model_tensors(cfg, seed)
+            m = ref.model(cfg, t, prompt + 1 + attempts * decode_tokens + 4)
+            ids = [int(v) for v in np.random.default_rng(seed).integers(0, cfg.vocab, prompt)]
+            logits = m.forward(ids, 0)
+            logits = m.forward([int(np.argmax(logits))], prompt)      # warm-up (thread pool, page-in)
+            models[L] = [m, t, logits, prompt + 1]
+        # the sizes' tokens interleaved, so both medians see the same host load; a slope that is
+        # not positive (load that changed between the sizes anyway) is measured again
+        for attempt in range(attempts):
+            ts = {L: [] for L in layers}
+            for _ in range(decode_tokens):
+                for L in layers:
+                    m, _, logits, pos = models[L]
+                    t0 = time.perf_counter()
+                    logits = m.forward([int(np.argmax(logits))], pos)
+                    ts[L].append(time.perf_counter() - t0)
+                    models[L][2], models[L][3] = logits, pos + 1
+            per_tok = {L: statistics.median(ts[L]) for L in layers}
+            if per_tok[layers[1]] > per_tok[layers[0]]:
+                break
+    finally:
+        for m, *_ in models.values():
+            m.close()
+        models.clear()
     (l0, l1) = layers
     per_layer = (per_tok[l1] - per_tok[l0]) / (l1 - l0)
-    fixed = per_tok[l0] - l0 * per_layer
+    note = ""
+    if per_layer <= 0:             # unresolved: the larger model's time, all of it counted per layer
+        per_layer = per_tok[l1] / l1
+        note = f" (per-layer slope not resolved in {attempts} tries under host load: proportional estimate)"
+    fixed = per_tok[l0] - l0 * per_layer if not note else 0.0
     t94 = fixed + base.n_layer * per_layer
     desc = (f"reference qms_forward ({ref.variant} build, {threads} OpenMP threads) on 235B-shape models of "
             f"{l0} and {l1} layers in host RAM, {prompt}-id prompt then {decode_tokens} decode tokens each (median): "
             f"{per_tok[l0] * 1e3:.1f} / {per_tok[l1] * 1e3:.1f} ms per token -> {per_layer * 1e3:.2f} ms per layer, "
             f"{fixed * 1e3:.1f} ms head + embedding; 94 layers: {t94 * 1e3:.1f} ms per token "
-            f"(attention at position ~{prompt}, the device run decodes at ~{MODEL_PROMPT})")
+            f"(attention at position ~{prompt}, the device run decodes at ~{MODEL_PROMPT}){note}")
     return t94, desc, threads
 
 

@@ -102,8 +102,10 @@ int qms_cuda_moe_create(const QmsCudaMoeDesc *desc, QmsCudaMoe **out);
 void qms_cuda_moe_destroy(QmsCudaMoe *m);
 /* Bytes of device memory held by the layer (weights + scratch). */
 int64_t qms_cuda_moe_device_bytes(const QmsCudaMoe *m);
-/* Make sure scratch for T tokens exists. Forward calls do this themselves; call it before
- * capturing forward calls into a CUDA graph (no allocation may happen during capture). */
+/* Make sure scratch for T tokens exists (T * n_used <= 65535). Forward calls do this themselves;
+ * call it before capturing forward calls into a CUDA graph (no allocation may happen during
+ * capture). Growing the scratch moves it, so graphs captured on this layer before any call that
+ * grows it (a larger T, or an expert call with more rows) no longer apply. */
 int qms_cuda_moe_reserve(QmsCudaMoe *m, int T);
 
 /* out[t] = sum_j w[t][j] * FFN_{sel[t][j]}(xn[t]) for T tokens: moe(m, l, xn, h, T, out)
@@ -128,7 +130,8 @@ int qms_cuda_moe_route(QmsCudaMoe *m, const float *xn, int T, int *sel, float *w
 /* Expert FFNs of S rows (moe_group_fast's phases 1-3 for one slot each, src/model.c:979-1005):
  * x [S][n_embd] fp32, expert[S] local ids (0 .. n_local - 1), dn [S][n_embd] receives each row's
  * down projection before weighting. Rows with an out-of-range id are skipped (dn left as is).
- * Runs the grouped tensor-core kernels; device buffers. */
+ * S <= 2^21; the layer's scratch grows to S rows on the first call that needs it (outside graph
+ * capture). Runs the grouped tensor-core kernels; device buffers. */
 int qms_cuda_moe_experts(QmsCudaMoe *m, const float *x, const int *expert, int S, float *dn, void *stream);
 /* The same from rows already quantised: xq [S][n_embd/32] QmsQ8 blocks (e.g. from
  * qms_cuda_quantize_q8, bit-identical to the reference's quantiser), so a dispatch sends 44 bytes
